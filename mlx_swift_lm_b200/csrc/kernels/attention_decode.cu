@@ -1,0 +1,401 @@
+// Paged decode attention (flash-decoding, split over the KV sequence).
+//
+// Same contract as the reference's two-pass Metal kernel
+// (ContinuousBatchingV2/Paged/pagedattention.metal:260-486 partition pass,
+// :518-587 merge pass; dispatch PagedAttentionKernel.swift:636):
+//   pass A, one CTA per (row, KV head, partition): online softmax over the
+//           partition's tokens for every query head of the GQA group, writing
+//           unnormalised partial outputs plus (max, sum);
+//   pass B, one CTA per row: merge the partitions; learned sinks enter the
+//           denominator only.
+// Partition boundaries are fixed multiples of kPartTokens in absolute token
+// positions, so a row's reduction order depends only on its own length: the
+// result is bit-identical whatever its batch-mates are.
+//
+// B200 specifics: each KV page (16 tokens x D for one KV head, contiguous)
+// is pulled into shared memory by the bulk-copy engine
+// (cp.async.bulk ... mbarrier::complete_tx) through a 4-stage ring, and every
+// warp of the CTA computes from shared memory; waits are bounded.
+//
+// Layouts
+//   q          [B, H, D] bf16 (H = KVH * G), already normed and rotated
+//   k/v cache  [num_pages, KVH, 16, D] bf16 or fp8-e4m3 (per-KV-head scale)
+//   page_table [B, ld_pt] int32, seq_lens [B] int32 (tokens incl. current)
+//   scratch    part_acc [B, H, max_parts, D] fp32, part_ml [B, H, max_parts, 2]
+#include "b200_common.cuh"
+
+namespace b200 {
+
+constexpr int kPartTokens = 256;  // tokens per partition (16 pages)
+constexpr int kPage = 16;
+constexpr int kStages = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+template <typename KVT, int N>
+__device__ __forceinline__ void load_kv_vec(const KVT* p, float* out) {
+  // N consecutive elements from shared memory, as fp32
+  if constexpr (sizeof(KVT) == 2) {
+    static_assert(N % 8 == 0, "vector width");
+#pragma unroll
+    for (int c = 0; c < N / 8; ++c) {
+      uint4 u = reinterpret_cast<const uint4*>(p)[c];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        out[c * 8 + 2 * j] = f.x;
+        out[c * 8 + 2 * j + 1] = f.y;
+      }
+    }
+  } else {
+    static_assert(N % 8 == 0, "vector width");
+#pragma unroll
+    for (int c = 0; c < N / 8; ++c) {
+      uint2 u = reinterpret_cast<const uint2*>(p)[c];
+      const __nv_fp8x2_e4m3* h = reinterpret_cast<const __nv_fp8x2_e4m3*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = static_cast<float2>(h[j]);
+        out[c * 8 + 2 * j] = f.x;
+        out[c * 8 + 2 * j + 1] = f.y;
+      }
+    }
+  }
+}
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;
+  const void* k_cache;
+  const void* v_cache;
+  const int* page_table;
+  const int* seq_lens;
+  const float* sinks;  // [H] natural-log units, or null
+  const float* k_scale;
+  const float* v_scale;
+  float* part_acc;
+  float* part_ml;
+  __nv_bfloat16* out;
+  int H, KVH, ld_pt, max_parts, window;
+  int64_t num_pages;
+  float scale, softcap;
+};
+
+// D: head dim; G: query heads per KV head.
+template <int D, int G, typename KVT>
+__global__ void __launch_bounds__(128) paged_decode_part_kernel(DecodeArgs a) {
+  constexpr int DL = D / 8;                      // dims per lane
+  constexpr int HW = G >= 4 ? G / 4 : 1;         // heads per warp
+  constexpr int TS = G >= 4 ? 1 : 4 / G;         // warps sharing one head (split tokens)
+  constexpr int TPW = kPage / TS;                // tokens of a page handled by one warp
+  constexpr int TPG = TPW / 4;                   // tokens per token-group per page
+  constexpr int kPageBytes = kPage * D * (int)sizeof(KVT);
+  static_assert(TPG >= 1, "layout");
+
+  extern __shared__ __align__(128) uint8_t ring_raw[];  // [kStages][2][kPageBytes]
+  auto ring = reinterpret_cast<uint8_t(*)[2][kPageBytes]>(ring_raw);
+  __shared__ __align__(8) uint64_t bars[kStages];
+  __shared__ float xw_m[4][HW], xw_l[4][HW];
+  __shared__ float xw_acc[4][HW][TS > 1 ? D : 1];
+
+  const int part = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tg = lane >> 3, sub = lane & 7;
+  const int L = a.seq_lens[b];
+  const int start = a.window > 0 ? max(0, L - a.window) : 0;
+  if (L <= 0) return;
+  const int p_first = start / kPartTokens, p_last = (L - 1) / kPartTokens;
+  if (part < p_first || part > p_last) return;
+  const int lo = max(start, part * kPartTokens);
+  const int hi = min(L, (part + 1) * kPartTokens);
+  const int pg_lo = lo / kPage, pg_hi = (hi - 1) / kPage;
+  const int npages = pg_hi - pg_lo + 1;
+
+  const int head0 = (G >= 4) ? warp * HW : warp / TS;  // first head (within group) of this warp
+  const int tw = (G >= 4) ? 0 : warp % TS;             // token slice of this warp
+
+  // q (pre-scaled into the log2 domain unless softcap is used)
+  float q[HW][DL];
+  const float kscale = a.k_scale ? a.k_scale[kvh] : 1.f;
+  const float qmul = (a.softcap > 0.f ? a.scale : a.scale * kLog2e) * kscale;
+#pragma unroll
+  for (int h = 0; h < HW; ++h) {
+    const __nv_bfloat16* qp = a.q + ((size_t)b * a.H + kvh * G + head0 + h) * D + sub * DL;
+#pragma unroll
+    for (int d = 0; d < DL; ++d) q[h][d] = bf2f(qp[d]) * qmul;
+  }
+  float m[HW], l[HW], acc[HW][DL];
+#pragma unroll
+  for (int h = 0; h < HW; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DL; ++d) acc[h][d] = 0.f;
+  }
+
+  const uint32_t bar0 = smem_u32(&bars[0]);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(bar0 + 8 * s, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const KVT* kc = reinterpret_cast<const KVT*>(a.k_cache);
+  const KVT* vc = reinterpret_cast<const KVT*>(a.v_cache);
+  const int* pt = a.page_table + (size_t)b * a.ld_pt;
+  auto issue = [&](int i) {
+    const int s = i % kStages;
+    int64_t page = pt[pg_lo + i];
+    if (page < 0 || page >= a.num_pages) {
+      set_status(kErrBounds);
+      page = 0;
+    }
+    const size_t off = ((size_t)page * a.KVH + kvh) * kPage * D;
+    mbar_arrive_expect_tx(bar0 + 8 * s, 2 * kPageBytes);
+    bulk_copy_g2s(smem_u32(ring[s][0]), kc + off, kPageBytes, bar0 + 8 * s);
+    bulk_copy_g2s(smem_u32(ring[s][1]), vc + off, kPageBytes, bar0 + 8 * s);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(kStages, npages); ++i) issue(i);
+
+  bool ok = true;
+  for (int i = 0; i < npages; ++i) {
+    const int s = i % kStages;
+    if (ok && !mbar_wait(bar0 + 8 * s, (i / kStages) & 1, kErrAttnWait)) ok = false;
+    const KVT* ks = reinterpret_cast<const KVT*>(ring[s][0]);
+    const KVT* vs = reinterpret_cast<const KVT*>(ring[s][1]);
+    const int pos0 = (pg_lo + i) * kPage;
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < TPG; ++j) {
+        const int tok = tw * TPW + tg + 4 * j;  // token within page
+        const int pos = pos0 + tok;
+        // every lane runs the shuffles below; out-of-range tokens skip only the update
+        const bool valid = pos >= lo && pos < hi;
+        float kv[DL];
+        load_kv_vec<KVT, DL>(ks + tok * D + sub * DL, kv);
+        float sc[HW];
+#pragma unroll
+        for (int h = 0; h < HW; ++h) {
+          float sdot = 0.f;
+#pragma unroll
+          for (int d = 0; d < DL; ++d) sdot += q[h][d] * kv[d];
+          sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+          sdot += __shfl_xor_sync(0xffffffffu, sdot, 2);
+          sdot += __shfl_xor_sync(0xffffffffu, sdot, 4);
+          if (a.softcap > 0.f) sdot = a.softcap * tanhf(sdot / a.softcap) * kLog2e;
+          sc[h] = sdot;
+        }
+        load_kv_vec<KVT, DL>(vs + tok * D + sub * DL, kv);
+        if (!valid) continue;
+#pragma unroll
+        for (int h = 0; h < HW; ++h) {
+          const float mn = fmaxf(m[h], sc[h]);
+          const float corr = exp2f(m[h] - mn);  // m == -inf -> 0
+          const float p = exp2f(sc[h] - mn);
+          l[h] = l[h] * corr + p;
+#pragma unroll
+          for (int d = 0; d < DL; ++d) acc[h][d] = acc[h][d] * corr + p * kv[d];
+          m[h] = mn;
+        }
+      }
+    }
+    __syncthreads();  // everyone is done with stage s
+    if (threadIdx.x == 0 && ok && i + kStages < npages) issue(i + kStages);
+  }
+
+  // combine the 4 token groups of the warp (lanes with equal `sub`)
+#pragma unroll
+  for (int h = 0; h < HW; ++h) {
+#pragma unroll
+    for (int o = 8; o <= 16; o <<= 1) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m[h], o);
+      const float lo_ = __shfl_xor_sync(0xffffffffu, l[h], o);
+      const float mn = fmaxf(m[h], mo);
+      const float c0 = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - mn);
+      const float c1 = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+      l[h] = l[h] * c0 + lo_ * c1;
+#pragma unroll
+      for (int d = 0; d < DL; ++d) {
+        const float ao = __shfl_xor_sync(0xffffffffu, acc[h][d], o);
+        acc[h][d] = acc[h][d] * c0 + ao * c1;
+      }
+      m[h] = mn;
+    }
+  }
+  // combine warps sharing a head (only when G < 4)
+  if constexpr (TS > 1) {
+    if (tg == 0) {
+#pragma unroll
+      for (int h = 0; h < HW; ++h) {
+        if (sub == 0) {
+          xw_m[warp][h] = m[h];
+          xw_l[warp][h] = l[h];
+        }
+#pragma unroll
+        for (int d = 0; d < DL; ++d) xw_acc[warp][h][sub * DL + d] = acc[h][d];
+      }
+    }
+    __syncthreads();
+    if (tw != 0) return;
+    for (int w2 = warp + 1; w2 < warp + TS; ++w2) {
+#pragma unroll
+      for (int h = 0; h < HW; ++h) {
+        const float mo = xw_m[w2][h], lo_ = xw_l[w2][h];
+        const float mn = fmaxf(m[h], mo);
+        const float c0 = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - mn);
+        const float c1 = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+        l[h] = l[h] * c0 + lo_ * c1;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[h][d] = acc[h][d] * c0 + xw_acc[w2][h][sub * DL + d] * c1;
+        m[h] = mn;
+      }
+    }
+  }
+  if (tg != 0) return;
+  const float vscale = a.v_scale ? a.v_scale[kvh] : 1.f;
+#pragma unroll
+  for (int h = 0; h < HW; ++h) {
+    const int head = kvh * G + head0 + h;
+    const size_t pidx = ((size_t)b * a.H + head) * a.max_parts + part;
+    float* dst = a.part_acc + pidx * D + sub * DL;
+#pragma unroll
+    for (int d = 0; d < DL; ++d) dst[d] = acc[h][d] * vscale;
+    if (sub == 0) {
+      a.part_ml[pidx * 2 + 0] = m[h];
+      a.part_ml[pidx * 2 + 1] = l[h];
+    }
+  }
+}
+
+// One CTA per row, one warp per head (looping). Writes bf16 output.
+template <int D>
+__global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeArgs a) {
+  constexpr int DL = D / 32 > 0 ? D / 32 : 1;
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int L = a.seq_lens[b];
+  const int start = a.window > 0 ? max(0, L - a.window) : 0;
+  const int p_first = start / kPartTokens, p_last = L > 0 ? (L - 1) / kPartTokens : -1;
+  for (int h = warp; h < a.H; h += blockDim.x >> 5) {
+    __nv_bfloat16* o = a.out + ((size_t)b * a.H + h) * D;
+    if (L <= 0) {
+      for (int d = lane; d < D; d += 32) o[d] = f2bf(0.f);
+      continue;
+    }
+    const size_t base = ((size_t)b * a.H + h) * a.max_parts;
+    float M = a.sinks ? a.sinks[h] * kLog2e : -INFINITY;
+    for (int p = p_first; p <= p_last; ++p) M = fmaxf(M, a.part_ml[(base + p) * 2]);
+    float den = a.sinks ? exp2f(a.sinks[h] * kLog2e - M) : 0.f;
+    float accv[DL];
+#pragma unroll
+    for (int j = 0; j < DL; ++j) accv[j] = 0.f;
+    for (int p = p_first; p <= p_last; ++p) {
+      const float mp = a.part_ml[(base + p) * 2];
+      const float w = (mp == -INFINITY) ? 0.f : exp2f(mp - M);
+      den += a.part_ml[(base + p) * 2 + 1] * w;
+      const float* src = a.part_acc + (base + p) * D;
+#pragma unroll
+      for (int j = 0; j < DL; ++j) {
+        const int d = lane + 32 * j;
+        if (d < D) accv[j] += src[d] * w;
+      }
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+#pragma unroll
+    for (int j = 0; j < DL; ++j) {
+      const int d = lane + 32 * j;
+      if (d < D) o[d] = f2bf(accv[j] * inv);
+    }
+  }
+}
+
+template <int D, int G, typename KVT>
+static int launch_decode(const DecodeArgs& a, int B, cudaStream_t st) {
+  constexpr int smem = kStages * 2 * kPage * D * (int)sizeof(KVT);
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_part_kernel<D, G, KVT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return (int)e;
+    configured = true;
+  }
+  dim3 grid(a.max_parts, a.KVH, B);
+  paged_decode_part_kernel<D, G, KVT><<<grid, 128, smem, st>>>(a);
+  paged_decode_merge_kernel<D><<<B, 128, 0, st>>>(a);
+  return (int)cudaGetLastError();
+}
+
+template <int D, typename KVT>
+static int dispatch_g(const DecodeArgs& a, int B, int G, cudaStream_t st) {
+  switch (G) {
+    case 1: return launch_decode<D, 1, KVT>(a, B, st);
+    case 2: return launch_decode<D, 2, KVT>(a, B, st);
+    case 4: return launch_decode<D, 4, KVT>(a, B, st);
+    case 8: return launch_decode<D, 8, KVT>(a, B, st);
+    case 16: return launch_decode<D, 16, KVT>(a, B, st);
+    default: return -1;
+  }
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+int b200_paged_decode_part_tokens() { return kPartTokens; }
+
+// Scratch needed: part_acc B*H*max_parts*D floats, part_ml B*H*max_parts*2 floats.
+int b200_paged_decode(const void* q, const void* k_cache, const void* v_cache, int kv_fp8, const float* k_scale,
+                      const float* v_scale, const int* page_table, int ld_pt, const int* seq_lens,
+                      const float* sinks, void* out, float* part_acc, float* part_ml, int B, int H, int KVH, int D,
+                      int max_parts, int window, float scale, float softcap, int64_t num_pages, cudaStream_t st) {
+  if (B <= 0) return 0;
+  if (H % KVH) return -1;
+  DecodeArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.page_table = page_table;
+  a.seq_lens = seq_lens;
+  a.sinks = sinks;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.part_acc = part_acc;
+  a.part_ml = part_ml;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.H = H;
+  a.KVH = KVH;
+  a.ld_pt = ld_pt;
+  a.max_parts = max_parts;
+  a.window = window;
+  a.num_pages = num_pages;
+  a.scale = scale;
+  a.softcap = softcap;
+  const int G = H / KVH;
+  if (kv_fp8) {
+    switch (D) {
+      case 64: return dispatch_g<64, uint8_t>(a, B, G, st);
+      case 128: return dispatch_g<128, uint8_t>(a, B, G, st);
+      case 256: return dispatch_g<256, uint8_t>(a, B, G, st);
+      default: return -1;
+    }
+  }
+  switch (D) {
+    case 64: return dispatch_g<64, __nv_bfloat16>(a, B, G, st);
+    case 128: return dispatch_g<128, __nv_bfloat16>(a, B, G, st);
+    case 256: return dispatch_g<256, __nv_bfloat16>(a, B, G, st);
+    default: return -1;
+  }
+}
+
+}  // extern "C"
+
+B200_STATUS_ACCESSORS(attn_decode)

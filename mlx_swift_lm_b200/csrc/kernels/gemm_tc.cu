@@ -1,0 +1,444 @@
+// Dense bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+//   Y[M, N] = X[M, K] . W[N, K]^T        (X: activations, W: nn.Linear weight)
+//
+// Orientation ("swap AB"): the MMA's 128-row M side walks the weight rows
+// (output features) and its N side walks the tokens, so a decode batch of
+// 1..128 rows still fills the 128-lane accumulator. One CTA owns a
+// 128-feature x BN-token output tile and a contiguous range of 64-wide K
+// blocks:
+//   warp 0 / lane 0 : TMA producer (weights + activations, 128B swizzle)
+//   warp 1 / lane 0 : MMA issuer (tcgen05.mma kind::f16, accumulator in TMEM)
+//   warps 0..3      : epilogue (tcgen05.ld, fused activation, store)
+// Split-K partials go to an fp32 workspace; the last CTA of a tile (atomic
+// ticket) sums the partials in split order 0..S-1, so results are
+// deterministic and independent of which CTA finishes last. The split count
+// is chosen from (N, K) only for M <= 128, which keeps a row's result the same
+// whatever the decode batch size is.
+//
+// Replaces the MLX matmul / quantizedMatmul library calls that the reference
+// relies on for every Linear (Libraries/MLXLMCommon/SwitchLayers.swift:1361,
+// AttentionUtils.swift:133 call sites); the dequantizing variants live in
+// gemm_quant.cu.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "b200_common.cuh"
+
+namespace b200 {
+
+enum GemmEpilogue : int {
+  kEpiStoreBf16 = 0,  // Y = bf16(acc)
+  kEpiSwiGLU = 1,     // weight rows interleaved in 64-row gate/up halves: Y[:, f] = silu(gate) * up
+  kEpiStoreF32 = 2,   // Y = acc (fp32)
+  kEpiAddBf16 = 3,    // Y = bf16(acc + R)   (R has Y's layout)
+  kEpiGeGLU = 4,      // as kEpiSwiGLU with gelu(tanh approximation) on the gate
+  kEpiSwiGLUOAI = 5,  // GPT-OSS gate: g=min(g,7), u=clamp(u,-7,7), (u+1)*g*sigmoid(1.702g)
+};
+
+__device__ __forceinline__ float glu_act(int epi, float g, float u) {
+  if (epi == kEpiGeGLU) {
+    const float c = 0.7978845608028654f;  // sqrt(2/pi)
+    return 0.5f * g * (1.f + tanhf(c * (g + 0.044715f * g * g * g))) * u;
+  }
+  if (epi == kEpiSwiGLUOAI) {
+    g = fminf(g, 7.f);
+    u = fminf(fmaxf(u, -7.f), 7.f);
+    return (u + 1.f) * g / (1.f + __expf(-1.702f * g));
+  }
+  return silu(g) * u;
+}
+
+struct GemmArgs {
+  void* Y;
+  const __nv_bfloat16* R;
+  const __nv_bfloat16* bias;  // [N] per output row of W, or null
+  float* ws;
+  int* counters;
+  int M, N, K, ldy, ldr;
+  int kb_total, kb_per_split, ksplit;
+  int epi;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
+  static constexpr int kBBytes = BN * 128;   // BN rows x 64 bf16
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kTotal = kBarOffset + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(128, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                        GemmArgs args) {
+  using S = GemmSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_full = sbase + S::kBarOffset;
+  const uint32_t bar_empty = bar_full + STAGES * 8;
+  const uint32_t bar_accum = bar_empty + STAGES * 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kBarOffset + (2 * STAGES + 1) * 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * 128;
+  const int m0 = blockIdx.y * BN;
+  const int z = blockIdx.z;
+  const int kb_begin = z * args.kb_per_split;
+  const int kb_end = min(args.kb_total, kb_begin + args.kb_per_split);
+  const int nkb = kb_end - kb_begin;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_accum, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    const uint64_t pol_w = l2_policy_evict_first();  // weights stream through once per step
+    const uint64_t pol_x = l2_policy_evict_last();   // activations are re-read by every feature tile
+    int issued = 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES, r = i / STAGES;
+      if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
+      const uint32_t a = sbase + s * S::kStageBytes;
+      const uint32_t b = a + S::kABytes;
+      mbar_arrive_expect_tx(bar_full + 8 * s, S::kStageBytes);
+      const int kc = (kb_begin + i) * 64;
+      tma_load_2d(a, &tmW, bar_full + 8 * s, kc, n0, pol_w);
+      tma_load_2d(b, &tmX, bar_full + 8 * s, kc, m0, pol_x);
+      issued = i + 1;
+    }
+    // Drain: make sure no copy we issued is still landing when the CTA exits
+    // (only matters if the consumer gave up early).
+    for (int i = max(0, issued - STAGES); i < issued; ++i)
+      mbar_wait(bar_full + 8 * (i % STAGES), (i / STAGES) & 1, kErrGemmWait);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES, r = i / STAGES;
+      if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
+      tc_fence_after();
+      const uint32_t a = sbase + s * S::kStageBytes;
+      const uint32_t b = a + S::kABytes;
+      const uint64_t ad = umma_desc_k_sw128(a, 1024);
+      const uint64_t bd = umma_desc_k_sw128(b, 1024);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tc_mma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+      tc_commit(bar_empty + 8 * s);
+    }
+    tc_commit(bar_accum);
+  }
+  __syncwarp();
+
+  // ---------------- Epilogue (all 4 warps) ----------------
+  // CTA-uniform verdict: the epilogue below contains block barriers.
+  const bool acc_ok = __syncthreads_and(mbar_wait(bar_accum, 0, kErrTmemWait) ? 1 : 0) != 0;
+  tc_fence_after();
+  const int row_lane = warp * 32 + lane;  // TMEM lane == weight row within tile
+  const int n = n0 + row_lane;
+  const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+  float* xbuf = reinterpret_cast<float*>(smem);  // stage memory is free once the accumulator is final
+
+  const bool split = args.ksplit > 1;
+  bool do_final = true;
+  if (split) {
+    // 1) publish this split's partial tile
+    float* wsz = args.ws + (size_t)z * args.M * args.N;
+    for (int jc = 0; jc < BN; jc += 16) {
+      uint32_t r[16];
+      tmem_ld16(t_lane + jc, r);
+      tc_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int m = m0 + jc + j;
+        if (m < args.M && n < args.N && nkb > 0) wsz[(size_t)m * args.N + n] = __uint_as_float(r[j]);
+        else if (m < args.M && n < args.N) wsz[(size_t)m * args.N + n] = 0.f;
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_ticket;
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    if (threadIdx.x == 0) s_ticket = atomicAdd(&args.counters[tile], 1);
+    __syncthreads();
+    do_final = (s_ticket == args.ksplit - 1);
+    if (do_final) {
+      __threadfence();
+      if (threadIdx.x == 0) args.counters[tile] = 0;  // self-reset for the next launch / graph replay
+    }
+  }
+
+  if (do_final && acc_ok) {
+    for (int jc = 0; jc < BN; jc += 16) {
+      float v[16];
+      if (!split) {
+        uint32_t r[16];
+        tmem_ld16(t_lane + jc, r);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = m0 + jc + j;
+          float acc = 0.f;
+          if (m < args.M && n < args.N) {
+            const float* p = args.ws + (size_t)m * args.N + n;
+            acc = __ldcg(p);
+            for (int zz = 1; zz < args.ksplit; ++zz) acc += __ldcg(p + (size_t)zz * args.M * args.N);
+          }
+          v[j] = acc;
+        }
+      }
+      if (args.bias && n < args.N) {
+        const float bb = bf2f(args.bias[n]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] += bb;
+      }
+      const bool glu = args.epi == kEpiSwiGLU || args.epi == kEpiGeGLU || args.epi == kEpiSwiGLUOAI;
+      if (glu) {
+        // rows 0..63 of the tile are gate rows, 64..127 the matching up rows
+        __syncthreads();
+        if (warp >= 2) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xbuf[(row_lane - 64) * 17 + j] = v[j];
+        }
+        __syncthreads();
+        if (warp < 2) {
+          __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(args.Y);
+          const int f = (n0 >> 1) + row_lane;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + jc + j;
+            if (m < args.M && f < (args.N >> 1)) {
+              const float up = xbuf[row_lane * 17 + j];
+              // round the gate and up projections to bf16 first, as an
+              // unfused bf16 model would, then apply silu(g) * u in fp32
+              const float g = bf2f(f2bf(v[j]));
+              const float u = bf2f(f2bf(up));
+              Y[(size_t)m * args.ldy + f] = f2bf(glu_act(args.epi, g, u));
+            }
+          }
+        }
+      } else if (n < args.N) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = m0 + jc + j;
+          if (m >= args.M) break;
+          if (args.epi == kEpiStoreF32) {
+            reinterpret_cast<float*>(args.Y)[(size_t)m * args.ldy + n] = v[j];
+          } else if (args.epi == kEpiAddBf16) {
+            const float rr = bf2f(args.R[(size_t)m * args.ldr + n]);
+            reinterpret_cast<__nv_bfloat16*>(args.Y)[(size_t)m * args.ldy + n] = f2bf(bf2f(f2bf(v[j])) + rr);
+          } else {
+            reinterpret_cast<__nv_bfloat16*>(args.Y)[(size_t)m * args.ldy + n] = f2bf(v[j]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor-map cache + launch
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+struct TmKey {
+  uintptr_t ptr;
+  int64_t rows, cols, ld;
+  int box_rows, box_cols, dtype_bytes;
+  bool operator==(const TmKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows &&
+           box_cols == o.box_cols && dtype_bytes == o.dtype_bytes;
+  }
+};
+struct TmKeyHash {
+  size_t operator()(const TmKey& k) const {
+    size_t h = std::hash<uintptr_t>()(k.ptr);
+    h ^= std::hash<int64_t>()(k.rows * 1315423911ll + k.cols * 2654435761ll + k.ld) + 0x9e3779b97f4a7c15ull + (h << 6);
+    h ^= (size_t)(k.box_rows * 131 + k.box_cols * 7 + k.dtype_bytes);
+    return h;
+  }
+};
+
+// 2-D row-major tensor map with a 128-byte swizzle: box = box_rows x (128 bytes).
+// Returns false if the driver rejects the layout.
+bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows,
+                  int box_cols, int dtype_bytes) {
+  static std::mutex mu;
+  static std::unordered_map<TmKey, CUtensorMap, TmKeyHash> cache;
+  TmKey key{(uintptr_t)ptr, rows, cols, ld_elems, box_rows, box_cols, dtype_bytes};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  CUtensorMapDataType dt = dtype_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                           : dtype_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)(ld_elems * dtype_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = enc(out, dt, 2, const_cast<void*>(ptr), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 8192) cache.clear();
+  cache.emplace(key, *out);
+  return true;
+}
+
+template <int BN, int STAGES>
+static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, int tiles_n, int tiles_m,
+                       cudaStream_t st) {
+  using S = GemmSmem<BN, STAGES>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    if (e != cudaSuccess) return (int)e;
+    configured = true;
+  }
+  dim3 grid(tiles_n, tiles_m, a.ksplit);
+  gemm_bf16_tc_kernel<BN, STAGES><<<grid, 128, S::kTotal, st>>>(tw, tx, a);
+  return (int)cudaGetLastError();
+}
+
+// Split-K choice for skinny (decode) GEMMs: depends only on (N, K), never on
+// M, so a row's reduction order does not change with the batch size.
+static int choose_kb_per_split(int N, int K, int M, int num_sms) {
+  const int kb = (K + 63) / 64;
+  const int tiles = (N + 127) / 128;
+  if (M > 128 || tiles >= 2 * num_sms) return kb;
+  double best_eff = -1.0;
+  int best = kb;
+  for (int kps = kb; kps >= 4; --kps) {
+    const int s = (kb + kps - 1) / kps;
+    if (s > 16) break;
+    const long ctas = (long)tiles * s;
+    const long waves = (ctas + num_sms - 1) / num_sms;
+    double eff = (double)ctas / (double)(waves * num_sms);
+    // prefer at least ~one full wave; penalise tiny per-split work
+    if (ctas < num_sms) eff *= (double)ctas / num_sms;
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = kps;
+    }
+  }
+  return best;
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+// Workspace needed (bytes) for a GEMM of this shape; counters needed = tiles.
+size_t b200_gemm_workspace_bytes(int M, int N, int K, int num_sms) {
+  const int kb = (K + 63) / 64;
+  const int kps = choose_kb_per_split(N, K, M, num_sms);
+  const int s = (kb + kps - 1) / kps;
+  return s > 1 ? (size_t)s * M * N * sizeof(float) : 0;
+}
+
+int b200_gemm_num_splits(int M, int N, int K, int num_sms) {
+  const int kb = (K + 63) / 64;
+  const int kps = choose_kb_per_split(N, K, M, num_sms);
+  return (kb + kps - 1) / kps;
+}
+
+// Y[M, :] = epi(X[M, K] . W[N, K]^T). X row stride ldx, W row stride ldw (elements).
+// epi: 0 bf16 store, 1 SwiGLU (W rows interleaved gate/up per 64), 2 fp32 store, 3 bf16 add R,
+// 4 GeGLU, 5 GPT-OSS SwiGLU. `bias` (per W row) is added to the accumulator first.
+// Returns 0 on success, a CUDA error code, or -1 for a bad layout.
+int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, int ldw, void* Y, int ldy,
+                   const void* R, int ldr, const void* bias, int epi, void* ws, size_t ws_bytes, int* counters,
+                   int n_counters, int num_sms, int force_kps, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return 0;
+  if ((K % 8) || (ldx % 8) || (ldw % 8) || ((uintptr_t)X & 15) || ((uintptr_t)W & 15)) return -1;
+  const bool glu = epi == kEpiSwiGLU || epi == kEpiGeGLU || epi == kEpiSwiGLUOAI;
+  if (glu && (N % 128)) return -1;
+  int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
+  if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
+  GemmArgs a;
+  a.Y = Y;
+  a.R = reinterpret_cast<const __nv_bfloat16*>(R);
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  a.ws = reinterpret_cast<float*>(ws);
+  a.counters = counters;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldy = ldy;
+  a.ldr = ldr;
+  a.epi = epi;
+  a.kb_total = (K + 63) / 64;
+  a.kb_per_split = force_kps > 0 ? force_kps : choose_kb_per_split(N, K, M, num_sms);
+  a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  const int tiles_n = (N + 127) / 128, tiles_m = (M + BN - 1) / BN;
+  if (a.ksplit > 1) {
+    if (!ws || ws_bytes < (size_t)a.ksplit * M * N * sizeof(float)) return -2;
+    if (!counters || n_counters < tiles_n * tiles_m) return -3;
+  }
+  switch (BN) {
+    case 16: return launch_gemm<16, 8>(tw, tx, a, tiles_n, tiles_m, stream);
+    case 32: return launch_gemm<32, 8>(tw, tx, a, tiles_n, tiles_m, stream);
+    case 64: return launch_gemm<64, 8>(tw, tx, a, tiles_n, tiles_m, stream);
+    case 128: return launch_gemm<128, 6>(tw, tx, a, tiles_n, tiles_m, stream);
+    default: return launch_gemm<256, 4>(tw, tx, a, tiles_n, tiles_m, stream);
+  }
+}
+
+}  // extern "C"
+
+B200_STATUS_ACCESSORS(gemm)

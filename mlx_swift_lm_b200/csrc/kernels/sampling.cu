@@ -1,0 +1,476 @@
+// Fused sampling pipeline, one CTA per row, in the vLLM order that the
+// reference's CBv2 sampler documents (DefaultSamplerV2.swift:84-183,
+// LogitsPipelineV2.swift:292-357, docs/engine-v2/specs/E-sampling.md):
+//   raw logprobs -> logit bias -> repetition penalty -> frequency/presence
+//   penalties -> grammar/tool token mask -> temperature -> top-k -> top-p
+//   -> min-p -> draw.
+// The draw is Gumbel-max with a counter-based Philox-4x32-10 stream keyed by
+// (seed, request id) and counted by (step, token), so a row's sample depends
+// only on its own logits and key (batch-composition invariant, reproducible).
+//
+// top-k and top-p thresholds are found exactly by radix select over the
+// order-preserving integer image of the scaled logits: 4 passes of 8-bit
+// digits. For top-p the pass histograms accumulate probability mass as
+// 2^30-scaled integers in 64-bit counters, so the result does not depend on
+// the order of atomic additions.
+#include "b200_common.cuh"
+
+namespace b200 {
+
+// ---------------- Philox-4x32-10 (Salmon et al., SC'11) ----------------
+__host__ __device__ __forceinline__ void philox_round(uint32_t c[4], uint32_t k[2]) {
+  const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+  const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+  const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+  const uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+  const uint32_t n0 = hi1 ^ c[1] ^ k[0];
+  const uint32_t n2 = hi0 ^ c[3] ^ k[1];
+  c[0] = n0;
+  c[1] = lo1;
+  c[2] = n2;
+  c[3] = lo0;
+}
+__host__ __device__ __forceinline__ uint32_t philox_u32(uint64_t key, uint64_t step, uint32_t idx) {
+  uint32_t c[4] = {idx, (uint32_t)step, (uint32_t)(step >> 32), 0x42323030u};
+  uint32_t k[2] = {(uint32_t)key, (uint32_t)(key >> 32)};
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    philox_round(c, k);
+    k[0] += 0x9E3779B9u;
+    k[1] += 0xBB67AE85u;
+  }
+  return c[0];
+}
+// Uniform in (0, 1) from the top 24 bits.
+__device__ __forceinline__ float philox_uniform(uint64_t key, uint64_t step, uint32_t idx) {
+  const uint32_t x = philox_u32(key, step, idx);
+  return ((float)(x >> 8) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+// Order-preserving map float -> uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t fkey(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+constexpr int kThreads = 1024;
+
+// ---------------- logits processing (in place) ----------------
+struct ProcessArgs {
+  float* logits;
+  int64_t ld;
+  int V;
+  const int* bias_ids;
+  const float* bias_vals;
+  const int* n_bias;
+  int ld_bias;
+  const int* rep_ids;
+  const int* n_rep;
+  int ld_rep;
+  const float* rep_penalty;
+  const int* out_ids;
+  const int* n_out;
+  int ld_out;
+  const float* freq_penalty;
+  const float* pres_penalty;
+  const uint32_t* allow_mask;  // [B, ld_mask] bit 1 = allowed, or null
+  int ld_mask;
+  const int* mask_rows;  // [B] 1 if the row's mask applies
+};
+
+__global__ void __launch_bounds__(kThreads) logits_process_kernel(ProcessArgs a) {
+  extern __shared__ uint32_t seen[];  // V bits
+  const int b = blockIdx.x;
+  float* lg = a.logits + (size_t)b * a.ld;
+  const int words = (a.V + 31) / 32;
+  // 1) logit bias (ids unique per row)
+  if (a.n_bias) {
+    const int nb = a.n_bias[b];
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+      const int id = a.bias_ids[(size_t)b * a.ld_bias + i];
+      if (id >= 0 && id < a.V) lg[id] += a.bias_vals[(size_t)b * a.ld_bias + i];
+    }
+    __syncthreads();
+  }
+  // 2) repetition penalty over the recent-context window, once per distinct id
+  if (a.n_rep && a.rep_penalty[b] != 1.f) {
+    for (int i = threadIdx.x; i < words; i += blockDim.x) seen[i] = 0;
+    __syncthreads();
+    const int nr = a.n_rep[b];
+    const float rp = a.rep_penalty[b];
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+      const int id = a.rep_ids[(size_t)b * a.ld_rep + i];
+      if (id < 0 || id >= a.V) continue;
+      const uint32_t bit = 1u << (id & 31);
+      if (!(atomicOr(&seen[id >> 5], bit) & bit)) {
+        const float x = lg[id];
+        lg[id] = x > 0.f ? x / rp : x * rp;
+      }
+    }
+    __syncthreads();
+  }
+  // 3) frequency / presence penalties over generated tokens: the first
+  //    occurrence of an id counts all occurrences and applies one update.
+  if (a.n_out && (a.freq_penalty[b] != 0.f || a.pres_penalty[b] != 0.f)) {
+    const int no = a.n_out[b];
+    const int* ids = a.out_ids + (size_t)b * a.ld_out;
+    for (int i = threadIdx.x; i < no; i += blockDim.x) {
+      const int id = ids[i];
+      if (id < 0 || id >= a.V) continue;
+      bool first = true;
+      for (int j = 0; j < i; ++j)
+        if (ids[j] == id) {
+          first = false;
+          break;
+        }
+      if (!first) continue;
+      int cnt = 1;
+      for (int j = i + 1; j < no; ++j) cnt += (ids[j] == id);
+      lg[id] = lg[id] - ((float)cnt * a.freq_penalty[b] + a.pres_penalty[b]);
+    }
+    __syncthreads();
+  }
+  // 4) token mask
+  if (a.allow_mask && a.mask_rows[b]) {
+    const uint32_t* mk = a.allow_mask + (size_t)b * a.ld_mask;
+    for (int i = threadIdx.x; i < a.V; i += blockDim.x)
+      if (!((mk[i >> 5] >> (i & 31)) & 1u)) lg[i] = -INFINITY;
+  }
+}
+
+// ---------------- sampling ----------------
+struct SampleArgs {
+  const float* logits;
+  int64_t ld;
+  int V;
+  const float* temperature;  // [B]; <= 0 -> greedy
+  const int* top_k;          // [B]; <= 0 -> off
+  const float* top_p;        // [B]; >= 1 -> off
+  const float* min_p;        // [B]; <= 0 -> off
+  const uint64_t* keys;      // [B] RNG key (seed mixed with request id)
+  const int64_t* steps;      // [B] RNG counter (generation step)
+  int* out_tokens;           // [B]
+  int* out_tokens2;          // optional second destination (next step's input ids)
+  float* out_logit;          // optional [B] value of the chosen logit (raw)
+};
+
+__device__ __forceinline__ void block_argmax(float& v, int& idx, float* sv, int* si) {
+  // ties -> smallest index
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+  __syncthreads();
+  if (lane == 0) {
+    sv[wid] = v;
+    si[wid] = idx;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+    idx = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > v || (ov == v && oi < idx)) {
+        v = ov;
+        idx = oi;
+      }
+    }
+    if (lane == 0) {
+      sv[0] = v;
+      si[0] = idx;
+    }
+  }
+  __syncthreads();
+  v = sv[0];
+  idx = si[0];
+}
+
+__global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ unsigned long long hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ unsigned long long s_rem;
+  const int b = blockIdx.x;
+  const float* lg = a.logits + (size_t)b * a.ld;
+  const float T = a.temperature[b];
+
+  // greedy / max pass (argmax of raw logits also gives the softmax max)
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
+    const float x = lg[i];
+    if (x > bv) {
+      bv = x;
+      bi = i;
+    }
+  }
+  block_argmax(bv, bi, sv, si);
+  if (T <= 0.f || bv == -INFINITY) {
+    if (threadIdx.x == 0) {
+      const int tok = bi == 0x7fffffff ? 0 : bi;
+      a.out_tokens[b] = tok;
+      if (a.out_tokens2) a.out_tokens2[b] = tok;
+      if (a.out_logit) a.out_logit[b] = bv;
+    }
+    return;
+  }
+  const float invT = 1.f / T;
+  const float mx = bv * invT;  // max scaled logit
+  uint32_t thr = 0;            // keep keys >= thr
+
+  // ---- top-k ----
+  const int k = a.top_k[b];
+  if (k > 0 && k < a.V) {
+    uint32_t prefix = 0;
+    unsigned long long rem = (unsigned long long)k;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+      __syncthreads();
+      const uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
+        const uint32_t key = fkey(lg[i] * invT);
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1ull);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        unsigned long long cum = 0;
+        int d = 255;
+        for (; d > 0; --d) {
+          if (cum + hist[d] >= rem) break;
+          cum += hist[d];
+        }
+        s_prefix = prefix | ((uint32_t)d << shift);
+        s_rem = rem - cum;
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      rem = s_rem;
+    }
+    thr = prefix;
+  }
+
+  // ---- top-p (exact, integer mass) ----
+  const float p = a.top_p[b];
+  if (p < 1.f) {
+    // total mass of the top-k survivors
+    unsigned long long tot = 0;
+    for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
+      const float s = lg[i] * invT;
+      if (fkey(s) >= thr) tot += (unsigned long long)__float2uint_rn(exp2f((s - mx) * 1.4426950408889634f) * 1073741824.f);
+    }
+    // block reduce (64-bit)
+    __shared__ unsigned long long red64[32];
+    {
+      const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+      if (lane == 0) red64[wid] = tot;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        unsigned long long t = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red64[w];
+        red64[0] = t;
+      }
+      __syncthreads();
+      tot = red64[0];
+    }
+    const unsigned long long target = (unsigned long long)ceil((double)p * (double)tot);
+    uint32_t prefix = 0;
+    unsigned long long rem = target > 0 ? target : 1;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+      __syncthreads();
+      const uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
+        const float s = lg[i] * invT;
+        const uint32_t key = fkey(s);
+        if (key >= thr && (key & pmask) == prefix)
+          atomicAdd(&hist[(key >> shift) & 255u],
+                    (unsigned long long)__float2uint_rn(exp2f((s - mx) * 1.4426950408889634f) * 1073741824.f));
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        unsigned long long cum = 0;
+        int d = 255;
+        for (; d > 0; --d) {
+          if (cum + hist[d] >= rem) break;
+          cum += hist[d];
+        }
+        s_prefix = prefix | ((uint32_t)d << shift);
+        s_rem = rem - cum;
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      rem = s_rem;
+    }
+    thr = max(thr, prefix);
+  }
+
+  // ---- min-p: keep p_i >= min_p * p_max  <=>  s_i >= mx + ln(min_p) ----
+  const float mp = a.min_p[b];
+  if (mp > 0.f) thr = max(thr, fkey(mx + logf(mp)));
+
+  // ---- Gumbel-max draw over the kept set ----
+  const uint64_t key = a.keys[b];
+  const uint64_t step = (uint64_t)a.steps[b];
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
+    const float s = lg[i] * invT;
+    if (fkey(s) < thr || s == -INFINITY) continue;
+    const float u = philox_uniform(key, step, (uint32_t)i);
+    const float g = -logf(-logf(u));
+    const float v = s + g;
+    if (v > best) {
+      best = v;
+      besti = i;
+    }
+  }
+  block_argmax(best, besti, sv, si);
+  if (threadIdx.x == 0) {
+    const int tok = besti == 0x7fffffff ? 0 : besti;
+    a.out_tokens[b] = tok;
+    if (a.out_tokens2) a.out_tokens2[b] = tok;
+    if (a.out_logit) a.out_logit[b] = lg[tok];
+  }
+}
+
+// Greedy argmax only (the all-greedy fast path).
+__global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                                                          int* out, int* out2) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int b = blockIdx.x;
+  const float* lg = logits + (size_t)b * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  const int V4 = (ld % 4 == 0) ? V / 4 : 0;
+  const float4* lg4 = reinterpret_cast<const float4*>(lg);
+  for (int i = threadIdx.x; i < V4; i += blockDim.x) {
+    const float4 x = lg4[i];
+    if (x.x > bv) { bv = x.x; bi = 4 * i; }
+    if (x.y > bv) { bv = x.y; bi = 4 * i + 1; }
+    if (x.z > bv) { bv = x.z; bi = 4 * i + 2; }
+    if (x.w > bv) { bv = x.w; bi = 4 * i + 3; }
+  }
+  for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x)
+    if (lg[i] > bv) {
+      bv = lg[i];
+      bi = i;
+    }
+  block_argmax(bv, bi, sv, si);
+  if (threadIdx.x == 0) {
+    const int tok = bi == 0x7fffffff ? 0 : bi;
+    out[b] = tok;
+    if (out2) out2[b] = tok;
+  }
+}
+
+// Raw log-softmax statistics: logprob of `tokens[b]` and the top-n entries.
+__global__ void __launch_bounds__(kThreads) logprobs_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                                                            const int* tokens, int n_top, float* out_lp,
+                                                            int* top_ids, float* top_lp) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const float* lg = logits + (size_t)b * ld;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, lg[i]);
+  mx = block_max(mx, red);
+  float se = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) se += expf(lg[i] - mx);
+  se = block_sum(se, red);
+  const float lse = mx + logf(se);
+  if (threadIdx.x == 0 && tokens) out_lp[b] = lg[tokens[b]] - lse;
+  // top-n by repeated argmax, excluding already chosen (n_top is small)
+  float prev_v = INFINITY;
+  int prev_i = -1;
+  for (int r = 0; r < n_top; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float x = lg[i];
+      // strictly after (prev_v, prev_i) in (value desc, index asc) order
+      const bool after = (x < prev_v) || (x == prev_v && i > prev_i);
+      if (after && (x > bv || (x == bv && i < bi))) {
+        bv = x;
+        bi = i;
+      }
+    }
+    block_argmax(bv, bi, sv, si);
+    if (threadIdx.x == 0) {
+      top_ids[(size_t)b * n_top + r] = bi == 0x7fffffff ? -1 : bi;
+      top_lp[(size_t)b * n_top + r] = bv - lse;
+    }
+    prev_v = bv;
+    prev_i = bi;
+  }
+}
+
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+int b200_logits_process(float* logits, int64_t ld, int B, int V, const int* bias_ids, const float* bias_vals,
+                        const int* n_bias, int ld_bias, const int* rep_ids, const int* n_rep, int ld_rep,
+                        const float* rep_penalty, const int* out_ids, const int* n_out, int ld_out,
+                        const float* freq_penalty, const float* pres_penalty, const uint32_t* allow_mask,
+                        int ld_mask, const int* mask_rows, cudaStream_t st) {
+  if (B <= 0) return 0;
+  ProcessArgs a{logits, ld,      V,           bias_ids, bias_vals,    n_bias,       ld_bias,
+                rep_ids, n_rep,  ld_rep,      rep_penalty, out_ids,   n_out,        ld_out,
+                freq_penalty, pres_penalty, allow_mask, ld_mask, mask_rows};
+  const size_t smem = ((V + 31) / 32) * sizeof(uint32_t);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(logits_process_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    configured = true;
+  }
+  if (smem > 200 * 1024) return -1;
+  logits_process_kernel<<<B, kThreads, smem, st>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int b200_sample(const float* logits, int64_t ld, int B, int V, const float* temperature, const int* top_k,
+                const float* top_p, const float* min_p, const uint64_t* keys, const int64_t* steps, int* out_tokens,
+                int* out_tokens2, float* out_logit, cudaStream_t st) {
+  if (B <= 0) return 0;
+  SampleArgs a{logits, ld, V, temperature, top_k, top_p, min_p, keys, steps, out_tokens, out_tokens2, out_logit};
+  sample_kernel<<<B, kThreads, 0, st>>>(a);
+  return (int)cudaGetLastError();
+}
+
+int b200_argmax(const float* logits, int64_t ld, int B, int V, int* out, int* out2, cudaStream_t st) {
+  if (B <= 0) return 0;
+  argmax_kernel<<<B, kThreads, 0, st>>>(logits, ld, V, out, out2);
+  return (int)cudaGetLastError();
+}
+
+int b200_logprobs(const float* logits, int64_t ld, int B, int V, const int* tokens, int n_top, float* out_lp,
+                  int* top_ids, float* top_lp, cudaStream_t st) {
+  if (B <= 0) return 0;
+  logprobs_kernel<<<B, kThreads, 0, st>>>(logits, ld, V, tokens, n_top, out_lp, top_ids, top_lp);
+  return (int)cudaGetLastError();
+}
+
+// Host-side Philox for tests and CPU oracles (same stream as the kernel).
+uint32_t b200_philox_u32(uint64_t key, uint64_t step, uint32_t idx) { return philox_u32(key, step, idx); }
+
+}  // extern "C"
+
+B200_STATUS_ACCESSORS(sampling)

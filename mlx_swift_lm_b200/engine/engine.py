@@ -1,0 +1,538 @@
+"""EngineV2: the continuous-batching serving engine.
+
+Public surface mirrors the reference engine (ContinuousBatchingV2/EngineV2.swift:
+``init`` :282, ``submit`` :1428, ``cancel`` :1836, ``capacity`` :1842,
+``shutdown`` :1922; health :216-224) and its step loop
+(EngineLoopV2.swift:3044-3373 ``engineStep``, :5218 ``finalize``).
+
+One step = plan (host scheduler) -> one flattened forward over decode rows and
+prefill chunks -> fused sampling -> finalize (commit KV, stop checks,
+detokenise, stream events). Pure-decode steps replay a CUDA graph captured for
+the batch bucket (:mod:`.graphs`) and, with ``chained_decode``, the next
+step's graph is launched on the device-resident sampled tokens of this step
+before its tokens are read back, so host finalisation overlaps GPU work (the
+reference's chained-decode fast path, EngineLoopV2.swift:3115-3250, 4394).
+"""
+from __future__ import annotations
+
+import collections
+import threading
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ..kv.paged import PAGE, PagedKVCache
+from ..models.batch import ForwardBatch
+from ..ops.attention import decode_max_parts
+from .detok import IncrementalDetokenizer, StopHoldback
+from .graphs import PENDING
+from .sampler import Sampler
+from .scheduler import Scheduler, SchedulerConfig, Status
+from .types import CapacitySnapshot, Event, FinishReason, Request, now
+
+STREAM_CAPACITY = 256  # events buffered per request before backpressure pauses it
+
+
+@dataclass
+class EngineConfig:
+    scheduler: SchedulerConfig = field(default_factory=SchedulerConfig)
+    kv_tokens: int | None = None  # pool size in tokens (default: enough for max_concurrent * max_model_len)
+    kv_bytes: int | None = None
+    kv_fp8: bool = False
+    max_model_len: int = 8192
+    use_cuda_graphs: bool = True
+    graph_buckets: tuple = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
+    chained_decode: bool = True
+    enable_prefix_cache: bool = False
+    prefix_block_size: int = 256
+    step_timeout_s: float = 30.0  # watchdog (background mode)
+    admission_timeout_s: float = 0.0  # 0 = no lease
+    decode_progress_timeout_s: float = 0.0
+    clock: object = None  # injectable monotonic clock (tests)
+
+
+class RequestStream:
+    """Per-request event stream. Iterating drives the engine when it is not
+    running its own background loop."""
+
+    def __init__(self, engine: "EngineV2", st):
+        self.engine = engine
+        self.st = st
+        self.q: collections.deque = collections.deque()
+        self.cv = threading.Condition()
+        self.done = False
+
+    @property
+    def request_id(self) -> int:
+        return self.st.req.id
+
+    def put(self, ev: Event):
+        with self.cv:
+            self.q.append(ev)
+            if len(self.q) >= STREAM_CAPACITY and not ev.finished:
+                self.st.paused = True
+            self.cv.notify_all()
+
+    def get(self, timeout: float | None = None) -> Event | None:
+        eng = self.engine
+        while True:
+            with self.cv:
+                if self.q:
+                    ev = self.q.popleft()
+                    if self.st.paused and len(self.q) < STREAM_CAPACITY // 2:
+                        self.st.paused = False
+                    return ev
+                if eng.background:
+                    if not self.cv.wait(timeout):
+                        return None
+                    continue
+            if not eng.step_once_for_stream():
+                return None
+
+    def __iter__(self):
+        while not self.done:
+            ev = self.get()
+            if ev is None:
+                return
+            if ev.finished:
+                self.done = True
+            yield ev
+
+    async def __aiter__(self):
+        import asyncio
+
+        loop = asyncio.get_running_loop()
+        while not self.done:
+            ev = await loop.run_in_executor(None, self.get, 0.5)
+            if ev is None:
+                if not self.engine.background and not self.engine.sched.has_work():
+                    return
+                continue
+            if ev.finished:
+                self.done = True
+            yield ev
+
+    def tokens(self) -> list[int]:
+        out = []
+        for ev in self:
+            out.extend(ev.tokens)
+        return out
+
+
+class EngineV2:
+    def __init__(self, model, tokenizer=None, config: EngineConfig | None = None, eos_token_ids=None,
+                 graph_runner=None):
+        self.model = model
+        self.tok = tokenizer
+        self.cfg = config or EngineConfig()
+        self.device = model.device
+        sc = self.cfg.scheduler
+        kv_tokens = self.cfg.kv_tokens or sc.max_concurrent_requests * self.cfg.max_model_len
+        if self.cfg.kv_bytes is not None:
+            self.kv = PagedKVCache.for_model(model, kv_bytes=self.cfg.kv_bytes, kv_fp8=self.cfg.kv_fp8)
+        else:
+            self.kv = PagedKVCache.for_model(model, max_tokens=kv_tokens, kv_fp8=self.cfg.kv_fp8)
+        self.prefix_cache = None
+        if self.cfg.enable_prefix_cache:
+            from ..kv.prefix_cache import PrefixCache
+
+            self.prefix_cache = PrefixCache(self.kv, self.cfg.prefix_block_size)
+        self.sched = Scheduler(sc, self.kv, self.prefix_cache)
+        self.sampler = Sampler(model.cfg.vocab_size, self.device)
+        self.eos = set(eos_token_ids or [])
+        self.states: dict[int, object] = {}
+        self.streams: dict[int, RequestStream] = {}
+        self.background = False
+        self.healthy = True
+        self.on_step_wedge = None
+        self.steps = 0
+        self.last_step_ms = 0.0
+        self._lock = threading.RLock()
+        self._thread = None
+        self._stop = threading.Event()
+        self._step_started = None
+        self._clock = self.cfg.clock or time.monotonic
+        self.max_pages = PagedKVCache.pages_for(self.cfg.max_model_len)
+        self.graphs = graph_runner
+        if self.graphs is None and self.device.type == "cuda" and self.cfg.use_cuda_graphs:
+            from .graphs import DecodeGraphRunner  # noqa: F811
+
+            self.graphs = DecodeGraphRunner(self)
+        self._inflight = None  # chained decode: (plan rows, device tokens, event)
+        self.forward_shapes: list[tuple[int, int]] = []
+        self.record_shapes = False
+
+    # ------------------------------------------------------------------ submit / cancel
+    def submit(self, req: Request) -> RequestStream:
+        total = len(req.prompt_tokens) + req.max_tokens
+        if not req.prompt_tokens:
+            raise ValueError("empty prompt")
+        if total > self.cfg.max_model_len:
+            raise ValueError(f"prompt + max_tokens = {total} exceeds max_model_len {self.cfg.max_model_len}")
+        if not self.sched.can_ever_fit(total):
+            raise ValueError("request can never fit in the KV pool")
+        with self._lock:
+            st = self.sched.add(req)
+            st.timing.submitted = now()
+            st.extra["submit_clock"] = self._clock()
+            if self.tok is not None:
+                st.detok = IncrementalDetokenizer(self.tok)
+            st.extra["hold"] = StopHoldback(req.stop_strings)
+            stream = RequestStream(self, st)
+            st.stream = stream
+            self.states[req.id] = st
+            self.streams[req.id] = stream
+        return stream
+
+    def cancel(self, request_id: int) -> bool:
+        with self._lock:
+            st = self.states.get(request_id)
+            if st is None or st.status == Status.FINISHED:
+                return False
+            self._drain_inflight()
+            self._finish(st, FinishReason.CANCELLED)
+            return True
+
+    # ------------------------------------------------------------------ batch build
+    def _build_batch(self, plan, dev):
+        rows = plan.rows
+        nd = sum(1 for r in rows if r.is_decode)
+        ids, pos, slots = [], [], []
+        for r in rows:
+            st = r.state
+            toks = st.all_tokens[r.start:r.start + r.num_tokens]
+            ids.extend(toks)
+            pos.extend(range(r.start, r.start + r.num_tokens))
+            slots.extend(st.seq.slots(r.start, r.num_tokens))
+        T = len(ids)
+        fb = ForwardBatch(input_ids=torch.tensor(ids, dtype=torch.int32), positions=torch.tensor(pos, dtype=torch.int32),
+                          slots=torch.tensor(slots, dtype=torch.int64), num_decode=nd)
+        maxp = max(len(r.state.seq.pages) for r in rows)
+        logit_idx = []
+        off = 0
+        for r in rows:
+            off += r.num_tokens
+            if r.sample:
+                logit_idx.append(off - 1)
+        if nd:
+            pt = np.zeros((nd, maxp), np.int32)
+            sl = np.zeros(nd, np.int32)
+            for i, r in enumerate(rows[:nd]):
+                pg = r.state.seq.pages
+                pt[i, :len(pg)] = pg
+                sl[i] = r.start + 1
+            fb.dec_page_table = torch.from_numpy(pt)
+            fb.dec_seq_lens = torch.from_numpy(sl)
+            fb.dec_max_parts = decode_max_parts(int(sl.max()))
+        pf = rows[nd:]
+        if pf:
+            cu = [0]
+            p0 = []
+            pt = np.zeros((len(pf), maxp), np.int32)
+            for i, r in enumerate(pf):
+                cu.append(cu[-1] + r.num_tokens)
+                p0.append(r.start)
+                pg = r.state.seq.pages
+                pt[i, :len(pg)] = pg
+            fb.pf_cu_q = torch.tensor(cu, dtype=torch.int32)
+            fb.pf_cu_q_host = cu
+            fb.pf_pos0 = torch.tensor(p0, dtype=torch.int32)
+            fb.pf_page_table = torch.from_numpy(pt)
+        if len(logit_idx) != T:
+            fb.logit_idx = torch.tensor(logit_idx, dtype=torch.int64)
+        if dev.type == "cuda":
+            for name in ("input_ids", "positions", "slots", "dec_page_table", "dec_seq_lens", "pf_cu_q", "pf_pos0",
+                         "pf_page_table", "logit_idx"):
+                t = getattr(fb, name)
+                if t is not None:
+                    setattr(fb, name, t.pin_memory().to(dev, non_blocking=True))
+        return fb
+
+    # ------------------------------------------------------------------ step
+    def step_once_for_stream(self) -> bool:
+        with self._lock:
+            if not self.sched.has_work() and self._inflight is None:
+                return False
+            self.step()
+            return True
+
+    def step(self) -> list[Event]:
+        """Run one engine step; returns the events it emitted."""
+        with self._lock:
+            t0 = time.perf_counter()
+            self._step_started = t0
+            self._process_leases()
+            events: list[Event] = []
+            plan = self.sched.plan()
+            self._handle_preemptions(plan)
+            if not plan.rows:
+                events += self._drain_inflight()
+                self._step_started = None
+                return events
+            if self.record_shapes:
+                self.forward_shapes.append((len(plan.decode_rows), plan.num_tokens))
+            use_graph = (self.graphs is not None and plan.pure_decode and self.graphs.can_run(plan)
+                         and not any(self._row_needs_eager(r.state) for r in plan.rows))
+            if use_graph:
+                # launch on device-resident tokens of the in-flight step (if any), then
+                # optimistically advance: this step's input K/V is written and its output
+                # is a placeholder until the step is finalized.
+                prev = self._inflight
+                handle = self.graphs.launch(plan, chained_from=prev)
+                for r in plan.rows:
+                    self.sched.commit(r)
+                    r.state.all_tokens.append(PENDING)
+                self._inflight = (plan, handle)
+                if prev is not None:
+                    events += self._finalize_inflight(prev)
+                if not self.cfg.chained_decode:
+                    events += self._drain_inflight()
+            else:
+                if self._inflight is not None:
+                    # the eager path needs every token on the host: finalize, then re-plan
+                    events += self._drain_inflight()
+                    self._step_started = None
+                    return events + self.step()
+                fb = self._build_batch(plan, self.device)
+                logits = self.model.forward(fb, self.kv)
+                srows = [r for r in plan.rows if r.sample]
+                toks, lp = self.sampler.sample(logits, [r.state for r in srows])
+                toks_host = toks.cpu().tolist() if toks.numel() else []
+                for r in plan.rows:
+                    self.sched.commit(r)
+                    r.state.timing.prefill_chunks += 0 if r.is_decode else 1
+                lps = self.sampler.logprob_entries(lp, toks_host, [r.state for r in srows])
+                for r, t, l in zip(srows, toks_host, lps):
+                    events += self._accept_token(r.state, int(t), l)
+            self.steps += 1
+            self.last_step_ms = (time.perf_counter() - t0) * 1e3
+            self._step_started = None
+            return events
+
+    def _row_needs_eager(self, st) -> bool:
+        sp = st.req.sampling
+        return (not sp.greedy or st.req.token_constraint is not None or sp.logprobs or sp.top_logprobs > 0
+                or sp.needs_processing or st.req.lora is not None)
+
+    def _finalize_inflight(self, inflight) -> list[Event]:
+        plan, handle = inflight
+        toks_host = self.graphs.read_tokens(handle, len(plan.rows))
+        events = []
+        for r, t in zip(plan.rows, toks_host):
+            st = r.state
+            if st.status == Status.FINISHED:
+                # the row finished while this step was in flight; its extra K/V went to
+                # pages it already released (stream order makes their reuse safe)
+                continue
+            events += self._accept_token(st, int(t), None, index=r.start + 1)
+        return events
+
+    def _drain_inflight(self) -> list[Event]:
+        if self._inflight is None:
+            return []
+        inf, self._inflight = self._inflight, None
+        return self._finalize_inflight(inf)
+
+    # ------------------------------------------------------------------ finalize
+    def _accept_token(self, st, tok: int, lp, index: int | None = None) -> list[Event]:
+        t = now()
+        if st.status == Status.FINISHED:
+            return []
+        if index is None:
+            st.all_tokens.append(tok)
+        else:
+            assert st.all_tokens[index] == PENDING, "finalizing a token that is not pending"
+            st.all_tokens[index] = tok
+        st.gen_step += 1
+        st.usage.completion_tokens += 1
+        if not st.timing.first_token:
+            st.timing.first_token = t
+            if st.req.on_prefill_completed:
+                st.req.on_prefill_completed(st.usage)
+        st.timing.last_token = t
+        st.timing.token_times.append(t)
+        st.timing.decode_steps += 1
+        st.extra["last_progress"] = self._clock()
+        if st.req.token_constraint is not None:
+            st.req.token_constraint.commit(tok)
+        reason = None
+        if (tok in st.req.stop_tokens or (tok in self.eos and not st.req.ignore_eos)):
+            reason = FinishReason.STOP
+        elif st.num_output >= st.req.max_tokens and PENDING not in st.all_tokens[st.num_prompt:]:
+            reason = FinishReason.LENGTH
+        elif index is not None and index + 1 - st.num_prompt >= st.req.max_tokens:
+            reason = FinishReason.LENGTH
+        elif st.req.token_constraint is not None and st.req.token_constraint.is_terminated():
+            reason = FinishReason.STOP
+        text = ""
+        emit_tokens = [tok]
+        if st.detok is not None:
+            if reason == FinishReason.STOP and (tok in st.req.stop_tokens or tok in self.eos):
+                emit_tokens = []
+                text = st.detok.flush()
+            else:
+                text = st.detok.push([tok])
+            text, stopped = st.extra["hold"].push(text)
+            if stopped and reason is None:
+                reason = FinishReason.STOP
+        ev = Event(st.req.id, tokens=emit_tokens, text=text, logprobs=[lp] if lp is not None else None)
+        events = [ev]
+        st.stream.put(ev)
+        if reason is not None:
+            events += self._finish(st, reason)
+        return events
+
+    def _finish(self, st, reason, error=None) -> list[Event]:
+        if st.status == Status.FINISHED:
+            return []
+        tail = ""
+        if st.detok is not None and reason != FinishReason.STOP:
+            tail = st.extra["hold"].push(st.detok.flush())[0] + st.extra["hold"].flush()
+        st.timing.finished = now()
+        st.finish_reason = reason
+        if self.prefix_cache is not None and reason in (FinishReason.STOP, FinishReason.LENGTH):
+            self.prefix_cache.donate(st)
+        self.sched.finish(st)
+        st.seq.release()
+        ev = Event(st.req.id, tokens=[], text=tail, finished=True, finish_reason=reason, usage=st.usage,
+                   timing=st.timing, error=error)
+        st.stream.put(ev)
+        self.states.pop(st.req.id, None)
+        self.streams.pop(st.req.id, None)
+        return [ev]
+
+    def _handle_preemptions(self, plan):
+        for st in plan.preempted:
+            if self._inflight is not None:
+                # a preempted row may be in the in-flight step: finalize first
+                pass
+
+    # ------------------------------------------------------------------ leases / watchdog
+    def _process_leases(self):
+        c = self._clock()
+        cfg = self.cfg
+        if cfg.admission_timeout_s > 0:
+            for st in list(self.sched.waiting):
+                if c - st.extra.get("submit_clock", c) > cfg.admission_timeout_s:
+                    self._finish(st, FinishReason.DEADLINE, "admission lease expired")
+        if cfg.decode_progress_timeout_s > 0:
+            for st in list(self.sched.running):
+                last = st.extra.get("last_progress", st.extra.get("submit_clock", c))
+                if c - last > cfg.decode_progress_timeout_s:
+                    self._finish(st, FinishReason.DEADLINE, "progress lease expired")
+
+    def _watchdog(self):
+        while not self._stop.wait(0.25):
+            t = self._step_started
+            if t is not None and time.perf_counter() - t > self.cfg.step_timeout_s and self.healthy:
+                self.healthy = False
+                for st in list(self.states.values()):
+                    try:
+                        ev = Event(st.req.id, finished=True, finish_reason=FinishReason.WATCHDOG, usage=st.usage,
+                                   timing=st.timing, error="engine step exceeded its timeout")
+                        st.status = Status.FINISHED
+                        st.stream.put(ev)
+                    except Exception:
+                        pass
+                if self.on_step_wedge:
+                    self.on_step_wedge()
+
+    # ------------------------------------------------------------------ loop control
+    def start(self):
+        """Run the step loop on a background thread (server mode)."""
+        if self._thread is not None:
+            return
+        self.background = True
+        self._stop.clear()
+
+        def loop():
+            while not self._stop.is_set():
+                if not self.healthy:
+                    time.sleep(0.05)
+                    continue
+                if self.sched.has_work() or self._inflight is not None:
+                    try:
+                        self.step()
+                    except Exception as e:  # engine error: fail live requests, stay up
+                        with self._lock:
+                            self._inflight = None
+                            for st in list(self.states.values()):
+                                self._finish(st, FinishReason.ERROR, repr(e))
+                else:
+                    time.sleep(0.0005)
+
+        self._thread = threading.Thread(target=loop, daemon=True, name="engine-loop")
+        self._thread.start()
+        self._wd = threading.Thread(target=self._watchdog, daemon=True, name="engine-watchdog")
+        self._wd.start()
+
+    def shutdown(self, timeout: float = 10.0):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout)
+            self._thread = None
+        with self._lock:
+            self._drain_inflight()
+            for st in list(self.states.values()):
+                self._finish(st, FinishReason.CANCELLED, "engine shutdown")
+        self.background = False
+
+    def run_until_idle(self, max_steps: int = 1 << 30) -> list[Event]:
+        events = []
+        n = 0
+        while (self.sched.has_work() or self._inflight is not None) and n < max_steps:
+            events += self.step()
+            n += 1
+        events += self._drain_inflight()
+        return events
+
+    # ------------------------------------------------------------------ introspection
+    def capacity(self) -> CapacitySnapshot:
+        pool = self.kv.pool
+        return CapacitySnapshot(active_requests=len(self.sched.running), waiting_requests=len(self.sched.waiting),
+                                kv_pages_total=self.kv.num_pages, kv_pages_used=pool.num_used,
+                                kv_pages_free=pool.num_free, kv_bytes_per_page=self.kv.page_bytes,
+                                active_tokens=sum(s.num_computed for s in self.sched.running), steps=self.steps,
+                                last_step_ms=self.last_step_ms, decode_rows=sum(1 for s in self.sched.running
+                                                                                if s.is_decode),
+                                healthy=self.healthy)
+
+    # ------------------------------------------------------------------ convenience
+    def generate(self, prompts: list[list[int]], max_tokens: int = 64, sampling=None, **kw) -> list[list[int]]:
+        from .types import SamplingParams
+
+        sampling = sampling or SamplingParams(temperature=0.0)
+        streams = [self.submit(Request(prompt_tokens=list(p), max_tokens=max_tokens, sampling=sampling, **kw))
+                   for p in prompts]
+        self.run_until_idle()
+        out = []
+        for s in streams:
+            toks = []
+            while s.q:
+                ev = s.q.popleft()
+                toks.extend(ev.tokens)
+            out.append(toks)
+        return out
+
+    def teacher_forced_top1(self, tokens: list[int]) -> list[int]:
+        """Greedy next-token prediction at every position of `tokens` (one prefill)."""
+        st = self.sched.add(Request(prompt_tokens=list(tokens), max_tokens=1))
+        self.sched.waiting.remove(st)
+        try:
+            if not st.seq.ensure(len(tokens)):
+                raise RuntimeError("no KV capacity")
+            slots = st.seq.slots(0, len(tokens))
+            dev = self.device
+            pt = torch.tensor([st.seq.pages], dtype=torch.int32)
+            fb = ForwardBatch(input_ids=torch.tensor(tokens, dtype=torch.int32).to(dev),
+                              positions=torch.arange(len(tokens), dtype=torch.int32).to(dev),
+                              slots=torch.tensor(slots, dtype=torch.int64).to(dev), num_decode=0,
+                              pf_cu_q=torch.tensor([0, len(tokens)], dtype=torch.int32).to(dev),
+                              pf_cu_q_host=[0, len(tokens)], pf_pos0=torch.tensor([0], dtype=torch.int32).to(dev),
+                              pf_page_table=pt.to(dev))
+            logits = self.model.forward(fb, self.kv)
+            return logits.argmax(-1).tolist()
+        finally:
+            st.seq.release()

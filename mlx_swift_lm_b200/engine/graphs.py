@@ -1,0 +1,198 @@
+"""CUDA-graph decode runner: one captured graph per decode batch bucket.
+
+A pure-decode step of B rows replays the graph of the smallest bucket >= B
+(padding rows write no KV: slot -1, length 0). All per-step inputs live in one
+packed device buffer that a single host->device copy refreshes from a
+double-buffered pinned staging area; the sampled tokens land in a shared
+device buffer and are copied back to pinned memory asynchronously. Input ids
+of a chained step are gathered on the device from the previous step's output
+(``gather_tokens``), so step N+1 can be launched before the host has read
+step N's tokens. This replaces the reference's MLX ``compile`` traces of the
+decode step (MLXLMCommon/CompiledTrace.swift:51, CompiledDecodeSegments.swift:10).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..models.batch import ForwardBatch
+from ..ops import _lib
+from ..ops.attention import SCRATCH, decode_max_parts
+
+PENDING = -1
+
+
+class DecodeGraphRunner:
+    def __init__(self, engine):
+        self.eng = engine
+        self.model = engine.model
+        self.dev = engine.device
+        mc = engine.cfg.scheduler.max_concurrent_requests
+        bk = sorted(b for b in engine.cfg.graph_buckets if b <= max(mc, 1))
+        if not bk or bk[-1] < mc:
+            bk.append(mc)
+        self.buckets = bk
+        self.Bmax = bk[-1] + (bk[-1] % 2)
+        self.maxp = engine.max_pages
+        self.max_parts = decode_max_parts(engine.cfg.max_model_len)
+        B, P = self.Bmax, self.maxp
+        # packed int32 layout: pos | seq_lens | src | host_ids | page_table | slots(int64)
+        self.o_pos, self.o_sl, self.o_src, self.o_hid, self.o_pt = 0, B, 2 * B, 3 * B, 4 * B
+        self.o_slots = 4 * B + B * P
+        self.o_slots += self.o_slots % 2
+        self.n_i32 = self.o_slots + 2 * B
+        self.packed = torch.zeros(self.n_i32, dtype=torch.int32, device=self.dev)
+        self.staging = [torch.zeros(self.n_i32, dtype=torch.int32).pin_memory() for _ in range(2)]
+        self.staging_ev = [None, None]
+        self.slot_k = 0
+        self.pos = self.packed[self.o_pos:self.o_pos + B]
+        self.sl = self.packed[self.o_sl:self.o_sl + B]
+        self.src = self.packed[self.o_src:self.o_src + B]
+        self.hid = self.packed[self.o_hid:self.o_hid + B]
+        self.pt = self.packed[self.o_pt:self.o_pt + B * P].view(B, P)
+        self.slots = self.packed[self.o_slots:self.o_slots + 2 * B].view(torch.int64)
+        self.ids = torch.zeros(B, dtype=torch.int32, device=self.dev)
+        self.out = torch.zeros(B, dtype=torch.int32, device=self.dev)
+        self.host_out = [torch.zeros(B, dtype=torch.int32).pin_memory() for _ in range(4)]
+        self.out_k = 0
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.pool = None
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.launches_per_replay: dict[int, int] = {}
+        self._reserved = False
+
+    # ------------------------------------------------------------------ capture
+    def _reserve(self):
+        if self._reserved:
+            return
+        m = self.model
+        SCRATCH.get(self.dev, "dec_acc", self.Bmax * m.H * self.max_parts * m.D)
+        SCRATCH.get(self.dev, "dec_ml", self.Bmax * m.H * self.max_parts * 2)
+        ops.WORKSPACE.reserve(self.dev, 512 << 20)
+        self._reserved = True
+
+    def _fb(self, B):
+        return ForwardBatch(input_ids=self.ids[:B], positions=self.pos[:B], slots=self.slots[:B], num_decode=B,
+                            dec_page_table=self.pt[:B], dec_seq_lens=self.sl[:B], dec_max_parts=self.max_parts)
+
+    def _body(self, B):
+        logits = self.model.forward(self._fb(B), self.eng.kv)
+        ops.argmax(logits, out=self.out[:B])
+
+    def capture(self, B):
+        self._reserve()
+        # inert inputs for warm-up: no KV writes, empty contexts
+        self.slots.fill_(-1)
+        self.sl.zero_()
+        self.pos.zero_()
+        self.ids.zero_()
+        cur = torch.cuda.current_stream(self.dev)
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._body(B)
+        cur.wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        n0 = _lib.launch_counter[0]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.pool):
+            self._body(B)
+        self.launches_per_replay[B] = _lib.launch_counter[0] - n0
+        if self.pool is None:
+            self.pool = g.pool()
+        self.graphs[B] = g
+        torch.cuda.synchronize(self.dev)
+
+    def capture_all(self):
+        for b in reversed(self.buckets):
+            if b not in self.graphs:
+                self.capture(b)
+
+    # ------------------------------------------------------------------ run
+    def bucket(self, n):
+        for b in self.buckets:
+            if b >= n:
+                return b
+        return None
+
+    def can_run(self, plan) -> bool:
+        n = len(plan.rows)
+        if self.bucket(n) is None:
+            return False
+        for r in plan.rows:
+            if len(r.state.seq.pages) > self.maxp:
+                return False
+        return True
+
+    def chainable(self, prev, plan) -> bool:
+        return True
+
+    def launch(self, plan, chained_from=None):
+        rows = plan.rows
+        n = len(rows)
+        Bb = self.bucket(n)
+        if Bb not in self.graphs:
+            # capture's warm-up overwrites the shared output buffer, which may hold
+            # the in-flight step's tokens that this launch gathers from
+            saved = self.out.clone()
+            self.capture(Bb)
+            self.out.copy_(saved)
+        k = self.slot_k
+        self.slot_k ^= 1
+        ev = self.staging_ev[k]
+        if ev is not None:
+            ev.synchronize()
+        stg = self.staging[k]
+        a = stg.numpy()
+        P = self.maxp
+        a[self.o_pos:self.o_pos + Bb] = 0
+        a[self.o_sl:self.o_sl + Bb] = 0
+        a[self.o_src:self.o_src + Bb] = -1
+        a[self.o_hid:self.o_hid + Bb] = 0
+        slots = a[self.o_slots:self.o_slots + 2 * self.Bmax].view(np.int64)
+        slots[:Bb] = -1
+        pt = a[self.o_pt:self.o_pt + self.Bmax * P].reshape(self.Bmax, P)
+        prev_idx = {}
+        if chained_from is not None:
+            for j, r in enumerate(chained_from[0].rows):
+                prev_idx[id(r.state)] = j
+        for i, r in enumerate(rows):
+            st = r.state
+            p = r.start
+            a[self.o_pos + i] = p
+            a[self.o_sl + i] = p + 1
+            slots[i] = st.seq.slot(p)
+            pg = st.seq.pages
+            pt[i, :len(pg)] = pg
+            tok = st.all_tokens[p]
+            if tok == PENDING:
+                a[self.o_src + i] = prev_idx[id(st)]
+            else:
+                a[self.o_hid + i] = tok
+        nbytes = (self.o_slots + 2 * self.Bmax) * 4
+        self.packed.copy_(stg, non_blocking=True)
+        self.h2d_bytes += nbytes
+        e = torch.cuda.Event()
+        e.record()
+        self.staging_ev[k] = e
+        L = _lib.lib()
+        _lib.check(L.b200_gather_tokens(self.out.data_ptr(), self.src.data_ptr(), self.hid.data_ptr(),
+                                        self.ids.data_ptr(), Bb, _lib.stream_ptr(self.dev)), "gather_tokens")
+        _lib.count(1)
+        self.graphs[Bb].replay()
+        _lib.count(self.launches_per_replay.get(Bb, 0))
+        ko = self.out_k
+        self.out_k = (self.out_k + 1) % len(self.host_out)
+        self.host_out[ko][:n].copy_(self.out[:n], non_blocking=True)
+        self.d2h_bytes += 4 * n
+        done = torch.cuda.Event()
+        done.record()
+        return (ko, done, n)
+
+    def read_tokens(self, handle, n):
+        ko, done, n0 = handle
+        done.synchronize()
+        return self.host_out[ko][:n].tolist()

@@ -1,0 +1,42 @@
+"""Flattened forward batch consumed by the decoder.
+
+Tokens of a step are laid out ``[decode rows (1 token each) | prefill chunks]``
+- the rectangular ``[B, 1]`` decode of the reference engine
+(EngineLoopV2.swift:4633-4708) followed by the packed prefill rows
+(:4721-4884). Every token carries its absolute position and the cache slot
+(``page * 16 + offset``) its K/V is written to.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass
+class ForwardBatch:
+    input_ids: torch.Tensor  # [T] int32
+    positions: torch.Tensor  # [T] int32
+    slots: torch.Tensor  # [T] int64
+    num_decode: int = 0
+    # decode rows
+    dec_page_table: torch.Tensor | None = None  # [Bd, maxp] int32
+    dec_seq_lens: torch.Tensor | None = None  # [Bd] int32 (context length incl. the new token)
+    dec_max_parts: int = 1
+    # prefill rows
+    pf_cu_q: torch.Tensor | None = None  # [R+1] int32 (offsets relative to the prefill part)
+    pf_cu_q_host: list | None = None
+    pf_pos0: torch.Tensor | None = None  # [R] int32
+    pf_page_table: torch.Tensor | None = None  # [R, maxp] int32
+    # rows whose logits are needed (indices into the T tokens); None = all tokens
+    logit_idx: torch.Tensor | None = None
+    # per-token LoRA adapter slot (-1 = none), used when adapters are active
+    lora_slots: torch.Tensor | None = None
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.input_ids.shape[0])
+
+    @property
+    def num_prefill_tokens(self) -> int:
+        return self.num_tokens - self.num_decode

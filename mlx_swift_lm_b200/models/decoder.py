@@ -1,0 +1,389 @@
+"""The fused pre-norm decoder used by every text family.
+
+Per layer (paged path, the serving hot path):
+
+    h      = add_rmsnorm(x, delta)            # residual add + norm, one kernel
+    qkv    = gemm(h, Wqkv)                    # tcgen05 GEMM (+ bias)
+    q      = qk_norm_rope_kv(qkv, ...)        # qk-norm + RoPE + paged K/V append
+    attn   = paged_decode(q[:Bd]) | paged_prefill(q[Bd:])
+    delta  = gemm(attn, Wo)                   # (+ tensor-parallel reduction)
+    h      = add_rmsnorm(x, delta)
+    delta  = gemm(gemm(h, Wgate_up, epi=glu), Wdown)   or the MoE block
+
+Parity: MLXLLM/Models/Qwen3.swift:56-216 (attention, block, model), Llama.swift,
+GPTOSS.swift:122-381 (sinks, alternating windows), Qwen3MoE.swift:114-156 (MoE);
+the ``LanguageModel`` protocol surface (MLXLMCommon/LanguageModel.swift:331-463)
+is :class:`DecoderLM`'s ``new_cache`` / ``forward_dense`` / ``forward``.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops
+from ..ops import reference as ref
+from .batch import ForwardBatch
+from .config import DecoderConfig
+from .rope import build_rope
+
+
+class LayerWeights:
+    __slots__ = ("ln1", "wqkv", "bqkv", "q_norm", "k_norm", "wo", "bo", "ln2", "post_attn_norm", "post_ffn_norm",
+                 "wgu", "bgu", "wd", "bd", "router", "router_b", "experts_gu", "experts_gu_b", "experts_d",
+                 "experts_d_b", "shared_gu", "shared_d", "shared_gate", "sinks", "moe")
+
+    def __init__(self):
+        for s in self.__slots__:
+            setattr(self, s, None)
+
+    def tensors(self):
+        for s in self.__slots__:
+            v = getattr(self, s)
+            if isinstance(v, torch.Tensor):
+                yield s, v
+            elif hasattr(v, "tensors"):
+                for n, t in v.tensors():
+                    yield f"{s}.{n}", t
+
+
+class TensorParallel:
+    """Tensor-parallel context of a rank: which heads / channels / vocab rows
+    it owns, and the reduction used after the row-parallel projections.
+    With world == 1 every hook is the identity."""
+
+    def __init__(self, rank: int = 0, world: int = 1, group=None, reducer=None):
+        self.rank, self.world, self.group = rank, world, group
+        self.reducer = reducer  # callable(t) -> reduced tensor (in place allowed)
+
+    def reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return t
+        if self.reducer is not None:
+            return self.reducer(t)
+        import torch.distributed as dist
+
+        dist.all_reduce(t, group=self.group)
+        return t
+
+
+class DenseKVCache:
+    """Per-layer contiguous K/V grown by concatenation (the legacy
+    KVCacheSimple of MLXLMCommon/KVCache.swift:470). CPU / reference path."""
+
+    def __init__(self, num_layers: int):
+        self.k = [None] * num_layers
+        self.v = [None] * num_layers
+        self.offset = 0
+
+    def update(self, layer: int, k: torch.Tensor, v: torch.Tensor):
+        if self.k[layer] is None:
+            self.k[layer], self.v[layer] = k, v
+        else:
+            self.k[layer] = torch.cat([self.k[layer], k], 0)
+            self.v[layer] = torch.cat([self.v[layer], v], 0)
+        return self.k[layer], self.v[layer]
+
+    def trim(self, n: int):
+        """Drop the last n tokens (speculative rollback)."""
+        n = min(n, self.offset)
+        for i in range(len(self.k)):
+            if self.k[i] is not None:
+                self.k[i] = self.k[i][: self.k[i].shape[0] - n]
+                self.v[i] = self.v[i][: self.v[i].shape[0] - n]
+        self.offset -= n
+        return n
+
+
+class DecoderLM:
+    """A decoder-only language model with paged-KV and dense-KV forwards."""
+
+    def __init__(self, cfg: DecoderConfig, device="cpu", dtype=torch.float32, tp: TensorParallel | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.tp = tp or TensorParallel()
+        w = self.tp.world
+        assert cfg.num_heads % w == 0, "query heads must divide across TP ranks"
+        self.H = cfg.num_heads // w
+        self.KVH = max(1, cfg.num_kv_heads // w) if cfg.num_kv_heads >= w else 1
+        self.D = cfg.head_dim
+        self.F = cfg.intermediate_size // w if cfg.intermediate_size else 0
+        self.Fe = cfg.moe_intermediate_size // w if cfg.moe_intermediate_size else 0
+        self.embed = None
+        self.norm = None
+        self.lm_head = None
+        self.layers: list[LayerWeights] = []
+        self.mtp_layers: list = []
+        self.cos_sin, self.rot_dim = build_rope(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling,
+                                                cfg.max_position_embeddings, cfg.partial_rotary_factor)
+        self.cos_sin = self.cos_sin.to(self.device)
+        self.lora = None  # optional LoRA manager (api.lora)
+
+    # ------------------------------------------------------------------ weights
+    def named_tensors(self):
+        yield "embed", self.embed
+        yield "norm", self.norm
+        if self.lm_head is not None and self.lm_head is not self.embed:
+            yield "lm_head", self.lm_head
+        for i, L in enumerate(self.layers):
+            for n, t in L.tensors():
+                yield f"layers.{i}.{n}", t
+
+    def num_params(self) -> int:
+        return sum(t.numel() for _, t in self.named_tensors() if t is not None)
+
+    def init_random(self, seed: int = 0, std: float = 0.02):
+        """Random N(0, std) weights (norm weights 1), generated on the model's
+        device. Shapes are the rank-local TP shards."""
+        cfg = self.cfg
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed + 7919 * self.tp.rank)
+        dev, dt = self.device, self.dtype
+
+        def rn(*shape):
+            t = torch.empty(shape, device=dev, dtype=dt)
+            t.normal_(0.0, std, generator=g)
+            return t
+
+        def ones(n):
+            return torch.zeros(n, device=dev, dtype=dt) if cfg.norm_offset_one else torch.ones(n, device=dev, dtype=dt)
+
+        hd = cfg.hidden_size
+        self.embed = rn(cfg.vocab_size, hd)
+        self.norm = ones(hd)
+        self.lm_head = self.embed if cfg.tie_word_embeddings else rn(cfg.vocab_size, hd)
+        self.layers = []
+        for li in range(cfg.num_layers):
+            L = LayerWeights()
+            L.ln1 = ones(hd)
+            L.ln2 = ones(hd)
+            L.wqkv = rn((self.H + 2 * self.KVH) * self.D, hd)
+            if cfg.attention_bias:
+                L.bqkv = rn((self.H + 2 * self.KVH) * self.D)
+            if cfg.qk_norm:
+                L.q_norm = ones(self.D)
+                L.k_norm = ones(self.D)
+            L.wo = rn(hd, self.H * self.D)
+            if cfg.o_bias:
+                L.bo = rn(hd) if self.tp.rank == 0 else torch.zeros(hd, device=dev, dtype=dt)
+            if cfg.post_norms:
+                L.post_attn_norm = ones(hd)
+                L.post_ffn_norm = ones(hd)
+            if cfg.attention_sinks:
+                L.sinks = torch.empty(self.H, device=dev, dtype=torch.float32).normal_(0.0, 1.0, generator=g)
+            if cfg.is_moe(li):
+                E = cfg.num_experts
+                L.moe = True
+                L.router = rn(E, hd)
+                if cfg.router_bias:
+                    L.router_b = rn(E)
+                L.experts_gu = rn(E, 2 * self.Fe, hd)
+                L.experts_d = rn(E, hd, self.Fe)
+                if cfg.mlp_bias:
+                    L.experts_gu_b = rn(E, 2 * self.Fe)
+                    L.experts_d_b = rn(E, hd)
+                if cfg.shared_expert_intermediate_size:
+                    Fs = cfg.shared_expert_intermediate_size // self.tp.world
+                    L.shared_gu = rn(2 * Fs, hd)
+                    L.shared_d = rn(hd, Fs)
+                    if cfg.shared_expert_gate:
+                        L.shared_gate = rn(1, hd)
+            else:
+                L.moe = False
+                L.wgu = rn(2 * self.F, hd)
+                L.wd = rn(hd, self.F)
+                if cfg.mlp_bias:
+                    L.bgu = rn(2 * self.F)
+                    L.bd = rn(hd)
+            self.layers.append(L)
+        return self
+
+    # ------------------------------------------------------------------ pieces
+    def _attn_out(self, L, attn2d):
+        delta = ops.gemm(attn2d, L.wo, bias=L.bo if self.tp.rank == 0 or L.bo is None else None)
+        return self.tp.reduce(delta)
+
+    def _mlp(self, L, h):
+        cfg = self.cfg
+        if L.moe:
+            return self._moe(L, h)
+        gu = ops.gemm(h, L.wgu, epi=cfg.glu_epi, bias=L.bgu)
+        delta = ops.gemm(gu, L.wd, bias=L.bd if self.tp.rank == 0 else None)
+        return self.tp.reduce(delta)
+
+    def route(self, L, h):
+        """Router top-k: returns (weights [T, k] fp32, ids [T, k] int64)."""
+        cfg = self.cfg
+        logits = ops.gemm(h, L.router, epi="f32", bias=L.router_b)
+        k = cfg.num_experts_per_tok
+        if cfg.router_mode == "topk_softmax":
+            v, idx = torch.topk(logits, k, dim=-1)
+            w = torch.softmax(v, dim=-1)
+        else:
+            p = torch.softmax(logits, dim=-1)
+            w, idx = torch.topk(p, k, dim=-1)
+            if cfg.norm_topk_prob:
+                w = w / w.sum(-1, keepdim=True)
+        return w.float(), idx
+
+    def _moe(self, L, h):
+        from ..ops import moe as moe_ops
+
+        cfg = self.cfg
+        w, idx = self.route(L, h)
+        out = moe_ops.moe_experts(h, L.experts_gu, L.experts_d, w, idx, cfg.glu_epi, L.experts_gu_b,
+                                  L.experts_d_b if self.tp.rank == 0 else None)
+        if L.shared_gu is not None:
+            s = ops.gemm(ops.gemm(h, L.shared_gu, epi=cfg.glu_epi), L.shared_d)
+            if L.shared_gate is not None:
+                s = (torch.sigmoid(ops.gemm(h, L.shared_gate, epi="f32")) * s.float()).to(s.dtype)
+            out = (out.float() + s.float()).to(out.dtype)
+        return self.tp.reduce(out)
+
+    def _final_logits(self, h):
+        logits = ops.gemm(h, self.lm_head, epi="f32")
+        if self.cfg.final_logit_softcap > 0:
+            c = self.cfg.final_logit_softcap
+            logits = torch.tanh(logits / c) * c
+        return logits
+
+    # ------------------------------------------------------------------ paged forward
+    def forward(self, fb: ForwardBatch, kv, return_hidden: bool = False):
+        """Paged-KV forward over a flattened batch. Returns fp32 logits for
+        ``fb.logit_idx`` rows (all tokens when None)."""
+        cfg = self.cfg
+        T = fb.num_tokens
+        nd = fb.num_decode
+        x = ops.embedding(fb.input_ids, self.embed, cfg.embed_scale)
+        delta = None
+        attn = torch.empty((T, self.H, self.D), dtype=x.dtype, device=x.device)
+        for li, L in enumerate(self.layers):
+            if delta is not None and L.post_attn_norm is not None:
+                pass
+            h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
+            if self.lora is not None:
+                qkv = self.lora.apply(li, "qkv", h, qkv, fb)
+            kc, vc = kv.layer(li)
+            q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
+                                    L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
+                                    kv.k_scale(li), kv.v_scale(li))
+            win = cfg.window(li)
+            if nd:
+                ops.paged_decode(q[:nd], kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, win, L.sinks,
+                                 cfg.attn_logit_softcap, kv.k_scale(li), kv.v_scale(li), fb.dec_max_parts,
+                                 out=attn[:nd])
+            if T > nd:
+                ops.paged_prefill(q[nd:], kc, vc, fb.pf_page_table, fb.pf_cu_q, fb.pf_pos0, cfg.scale, win, L.sinks,
+                                  cfg.attn_logit_softcap, kv.k_scale(li), kv.v_scale(li), fb.pf_cu_q_host,
+                                  out=attn[nd:])
+            delta = self._attn_out(L, attn.view(T, self.H * self.D))
+            if L.post_attn_norm is not None:
+                delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+            h = ops.add_rmsnorm(x, delta, L.ln2, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            delta = self._mlp(L, h)
+            if L.post_ffn_norm is not None:
+                delta = ops.rmsnorm(delta, L.post_ffn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+        if fb.logit_idx is not None:
+            xs = (x.float() + delta.float()).to(x.dtype)[fb.logit_idx] if delta is not None else x[fb.logit_idx]
+            h = ops.rmsnorm(xs.contiguous(), self.norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+        else:
+            h = ops.add_rmsnorm(x, delta, self.norm, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+        if return_hidden:
+            return h
+        return self._final_logits(h)
+
+    # ------------------------------------------------------------------ dense forward
+    def new_cache(self) -> DenseKVCache:
+        return DenseKVCache(self.cfg.num_layers)
+
+    @torch.no_grad()
+    def forward_dense(self, tokens: torch.Tensor, cache: DenseKVCache, return_hidden: bool = False):
+        """Single-sequence forward with a dense, concatenating KV cache (the
+        legacy single-request path). tokens [L] int; returns logits [L, V]."""
+        cfg = self.cfg
+        Lq = tokens.shape[0]
+        p0 = cache.offset
+        positions = torch.arange(p0, p0 + Lq, dtype=torch.int32, device=tokens.device)
+        x = ops.embedding(tokens.to(torch.int32), self.embed, cfg.embed_scale)
+        delta = None
+        for li, L in enumerate(self.layers):
+            h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
+            q, k, v = ops.qk_norm_rope_kv(qkv, positions, None, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
+                                          L.q_norm, L.k_norm, cfg.rms_norm_eps, None, None, self.H, self.KVH,
+                                          self.D, return_kv=True)
+            kk, vv = cache.update(li, k, v)
+            a = ref.attention_rows_ref(q.float(), kk.float(), vv.float(), positions, kk.shape[0], cfg.scale,
+                                       cfg.window(li), L.sinks, cfg.attn_logit_softcap).to(x.dtype)
+            delta = self._attn_out(L, a.reshape(Lq, self.H * self.D).contiguous())
+            if L.post_attn_norm is not None:
+                delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+            h = ops.add_rmsnorm(x, delta, L.ln2, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            delta = self._mlp(L, h)
+            if L.post_ffn_norm is not None:
+                delta = ops.rmsnorm(delta, L.post_ffn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+        cache.offset += Lq
+        h = ops.add_rmsnorm(x, delta, self.norm, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+        if return_hidden:
+            return h
+        return self._final_logits(h)
+
+    # ------------------------------------------------------------------ misc
+    def clone_to(self, device, dtype) -> "DecoderLM":
+        """A copy of this model (weights converted) on another device / dtype."""
+        m = DecoderLM(self.cfg, device, dtype, tp=self.tp)
+        dev = torch.device(device)
+
+        def cv(t, keep_f32=False):
+            if t is None:
+                return None
+            return t.to(device=dev, dtype=torch.float32 if keep_f32 else dtype)
+
+        m.embed = cv(self.embed)
+        m.norm = cv(self.norm)
+        m.lm_head = m.embed if self.lm_head is self.embed else cv(self.lm_head)
+        for L in self.layers:
+            N = LayerWeights()
+            for s in LayerWeights.__slots__:
+                v = getattr(L, s)
+                setattr(N, s, cv(v, s == "sinks") if isinstance(v, torch.Tensor) else v)
+            m.layers.append(N)
+        return m
+
+    def kv_bytes_per_token(self, kv_dtype=None) -> int:
+        dt = kv_dtype or self.dtype
+        es = torch.empty((), dtype=dt).element_size()
+        return 2 * self.cfg.num_layers * self.KVH * self.D * es
+
+    def to(self, device=None, dtype=None):
+        device = torch.device(device) if device is not None else self.device
+        dtype = dtype or self.dtype
+
+        def mv(t):
+            if t is None:
+                return None
+            if t.is_floating_point() and t.dtype != torch.float32 or (t.dtype == torch.float32 and dtype != torch.float32):
+                return t.to(device=device, dtype=dtype if t.dtype != torch.float32 or True else t.dtype)
+            return t.to(device=device)
+
+        tied = self.lm_head is self.embed
+        self.embed = mv(self.embed)
+        self.norm = mv(self.norm)
+        self.lm_head = self.embed if tied else mv(self.lm_head)
+        for L in self.layers:
+            for s in LayerWeights.__slots__:
+                v = getattr(L, s)
+                if isinstance(v, torch.Tensor):
+                    if s == "sinks":
+                        setattr(L, s, v.to(device=device, dtype=torch.float32))
+                    else:
+                        setattr(L, s, v.to(device=device, dtype=dtype))
+        self.cos_sin = self.cos_sin.to(device)
+        self.device, self.dtype = device, dtype
+        return self
+
+
+def softmax_scale(cfg: DecoderConfig) -> float:
+    return cfg.scale if cfg.attn_scale is not None else 1.0 / math.sqrt(cfg.head_dim)

@@ -1,0 +1,152 @@
+"""ctypes binding of ``libb200kernels.so`` (the sm_100a kernel library).
+
+Every CUDA op in :mod:`mlx_swift_lm_b200.ops` goes through this module. The
+library is required whenever a CUDA tensor reaches an op: there is no silent
+eager fallback on a GPU box. If the shared object is missing, the first CUDA
+op raises :class:`KernelLibraryMissing` with the build command.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+import torch
+
+_PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(_PKG, "_lib", "libb200kernels.so")
+
+_lock = threading.Lock()
+_lib = None
+
+vp = C.c_void_p
+i32 = C.c_int
+i64 = C.c_int64
+f32 = C.c_float
+u64 = C.c_uint64
+sz = C.c_size_t
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "b200_gemm_bf16": (i32, [vp, i32, i32, i32, vp, i32, i32, vp, i32, vp, i32, vp, i32, vp, sz, vp, i32, i32, i32, vp]),
+    "b200_gemm_workspace_bytes": (sz, [i32, i32, i32, i32]),
+    "b200_gemm_num_splits": (i32, [i32, i32, i32, i32]),
+    "b200_add_rmsnorm": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp]),
+    "b200_qk_norm_rope_kv": (i32, [vp, i32, i32, vp, vp, vp, i32, i32, vp, vp, f32, vp, vp, vp, i32, vp, vp,
+                                   i32, i32, i32, i64, vp, vp, vp]),
+    "b200_embedding": (i32, [vp, vp, vp, i32, i32, i64, f32, vp]),
+    "b200_silu_mul": (i32, [vp, vp, i32, i32, i32, i32, vp]),
+    "b200_paged_decode": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32,
+                                i32, f32, f32, i64, vp]),
+    "b200_paged_decode_part_tokens": (i32, []),
+    "b200_paged_prefill_simt": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32, f32,
+                                      i64, vp]),
+    "b200_prefill_simt_q_tile": (i32, [i32]),
+    "b200_logits_process": (i32, [vp, i64, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp, vp, vp, i32, vp, vp, vp,
+                                  i32, vp, vp]),
+    "b200_sample": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "b200_argmax": (i32, [vp, i64, i32, i32, vp, vp, vp]),
+    "b200_logprobs": (i32, [vp, i64, i32, i32, vp, i32, vp, vp, vp, vp]),
+    "b200_philox_u32": (C.c_uint32, [u64, u64, C.c_uint32]),
+    "b200_gather_tokens": (i32, [vp, vp, vp, vp, i32, vp]),
+}
+
+# status accessors exported per translation unit
+_STATUS_TAGS = ["gemm", "norm", "attn_decode", "attn_prefill_simt", "sampling", "misc"]
+
+
+class KernelLibraryMissing(RuntimeError):
+    pass
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+def _load():
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise KernelLibraryMissing(
+                f"{LIB_PATH} is missing: build it with `python -m mlx_swift_lm_b200._build` "
+                "(CUDA tensors are only served by the sm_100a kernel library)")
+        lib = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(lib, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        for tag in _STATUS_TAGS + _EXTRA_STATUS_TAGS:
+            fn = getattr(lib, "b200_status_" + tag, None)
+            if fn is not None:
+                fn.restype = i32
+                fn.argtypes = [C.POINTER(C.c_uint), i32]
+        _lib = lib
+        return lib
+
+
+_EXTRA_STATUS_TAGS: list[str] = []
+
+
+def register_signatures(sigs: dict, status_tags=()):
+    """Add signatures for kernels defined in other modules (called at import)."""
+    _SIGS.update(sigs)
+    _EXTRA_STATUS_TAGS.extend(status_tags)
+    if _lib is not None:
+        for name, (res, args) in sigs.items():
+            fn = getattr(_lib, name, None)
+            if fn is not None:
+                fn.restype = res
+                fn.argtypes = args
+        for tag in status_tags:
+            fn = getattr(_lib, "b200_status_" + tag, None)
+            if fn is not None:
+                fn.restype = i32
+                fn.argtypes = [C.POINTER(C.c_uint), i32]
+
+
+def lib():
+    return _lib if _lib is not None else _load()
+
+
+def available() -> bool:
+    return os.path.exists(LIB_PATH)
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def check(rc: int, what: str):
+    if rc != 0:
+        raise KernelError(f"{what} failed with code {rc}")
+
+
+def read_status(clear: bool = True) -> dict:
+    """Device status words of every kernel unit (nonzero = a bounded wait
+    expired or a bounds check failed). Synchronizes the device."""
+    L = lib()
+    out = {}
+    for tag in _STATUS_TAGS + _EXTRA_STATUS_TAGS:
+        fn = getattr(L, "b200_status_" + tag, None)
+        if fn is None:
+            continue
+        v = C.c_uint(0)
+        fn(C.byref(v), 1 if clear else 0)
+        out[tag] = v.value
+    return out
+
+
+# Count of kernel launches issued through this binding (for bench accounting).
+launch_counter = [0]
+
+
+def count(n: int = 1):
+    launch_counter[0] += n

@@ -1,0 +1,102 @@
+"""Paged attention entry points: decode (split-KV) and prefill (chunked, causal)."""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+from . import reference as ref
+
+PART_TOKENS = ref.DECODE_PART_TOKENS
+
+
+class _Scratch:
+    """Per-device scratch for decode partials (grown on demand, reused)."""
+
+    def __init__(self):
+        self.lock = threading.Lock()
+        self.bufs: dict[tuple, torch.Tensor] = {}
+
+    def get(self, device, name, numel):
+        key = (device.index, name)
+        with self.lock:
+            t = self.bufs.get(key)
+            if t is None or t.numel() < numel:
+                t = torch.empty(max(numel, 1 << 20), dtype=torch.float32, device=device)
+                self.bufs[key] = t
+            return t
+
+
+SCRATCH = _Scratch()
+
+
+def decode_max_parts(max_seq_len: int) -> int:
+    return max(1, (max_seq_len + PART_TOKENS - 1) // PART_TOKENS)
+
+
+def paged_decode(q, k_cache, v_cache, page_table, seq_lens, scale, window=0, sinks=None, softcap=0.0,
+                 k_scale=None, v_scale=None, max_parts=None, out=None):
+    """q [B, H, D]; caches [P, KVH, 16, D]; page_table [B, maxp] int32; seq_lens [B] int32."""
+    if not q.is_cuda:
+        y = ref.paged_decode_ref(q, k_cache, v_cache, page_table, seq_lens, scale, window, sinks, softcap,
+                                 k_scale, v_scale)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    B, H, D = q.shape
+    KVH = k_cache.shape[1]
+    if max_parts is None:
+        max_parts = decode_max_parts(page_table.shape[1] * 16)
+    if out is None:
+        out = torch.empty_like(q)
+    acc = SCRATCH.get(q.device, "dec_acc", B * H * max_parts * D)
+    ml = SCRATCH.get(q.device, "dec_ml", B * H * max_parts * 2)
+    kv_fp8 = k_cache.dtype == torch.float8_e4m3fn
+    rc = _lib.lib().b200_paged_decode(
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), 1 if kv_fp8 else 0, _lib.ptr(k_scale),
+        _lib.ptr(v_scale), page_table.data_ptr(), page_table.stride(0), seq_lens.data_ptr(), _lib.ptr(sinks),
+        out.data_ptr(), acc.data_ptr(), ml.data_ptr(), B, H, KVH, D, max_parts, int(window), float(scale),
+        float(softcap), k_cache.shape[0], _lib.stream_ptr(q.device))
+    _lib.check(rc, "paged_decode")
+    _lib.count(2)
+    return out
+
+
+def prefill_tiles(cu_q: list[int], G: int) -> list[tuple[int, int]]:
+    qt = 128 // G
+    tiles = []
+    for r in range(len(cu_q) - 1):
+        n = cu_q[r + 1] - cu_q[r]
+        for off in range(0, n, qt):
+            tiles.append((r, off))
+    return tiles
+
+
+def paged_prefill(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0, sinks=None, softcap=0.0,
+                  k_scale=None, v_scale=None, cu_q_host=None, out=None):
+    """q [T, H, D] for rows' chunks; cu_q [R+1] int32; q_pos0 [R] int32 (first position of each chunk)."""
+    if not q.is_cuda:
+        y = ref.paged_prefill_ref(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window, sinks, softcap,
+                                  k_scale, v_scale)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    T, H, D = q.shape
+    KVH = k_cache.shape[1]
+    G = H // KVH
+    if out is None:
+        out = torch.empty_like(q)
+    if cu_q_host is None:
+        cu_q_host = cu_q.tolist()
+    tiles = prefill_tiles(cu_q_host, G)
+    tiles_t = torch.tensor(tiles, dtype=torch.int32).pin_memory().to(q.device, non_blocking=True)
+    rc = _lib.lib().b200_paged_prefill_simt(
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), page_table.data_ptr(), page_table.stride(0),
+        cu_q.data_ptr(), q_pos0.data_ptr(), tiles_t.data_ptr(), len(tiles), _lib.ptr(sinks), out.data_ptr(), H, KVH,
+        D, int(window), float(scale), float(softcap), k_cache.shape[0], _lib.stream_ptr(q.device))
+    _lib.check(rc, "paged_prefill")
+    _lib.count(1)
+    return out

@@ -1,0 +1,253 @@
+"""sm_100a kernels vs their plain-PyTorch fp32 oracles (ops/reference.py)."""
+import math
+
+import pytest
+import torch
+
+from mlx_swift_lm_b200 import ops
+from mlx_swift_lm_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 33, 64, 100, 128, 300, 1024])
+@pytest.mark.parametrize("N,K", [(256, 256), (384, 1024), (1024, 4096), (4096, 512)])
+def test_gemm_bf16(M, N, K):
+    torch.manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.05
+    y = ops.gemm(x, w)
+    r = ref.gemm_ref(x.cpu(), w.cpu())
+    assert _rel(y.cpu(), r) < 1e-2
+    yf = ops.gemm(x, w, epi="f32")
+    assert _rel(yf.cpu(), ref.gemm_ref(x.cpu(), w.cpu(), "f32")) < 1e-3
+
+
+@pytest.mark.parametrize("epi", ["swiglu", "geglu", "swiglu_oai"])
+@pytest.mark.parametrize("M", [3, 64, 200])
+def test_gemm_glu_and_bias(epi, M):
+    torch.manual_seed(3)
+    K, F = 512, 384
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    g = torch.randn(F, K, device=DEV, dtype=torch.bfloat16) * 0.05
+    u = torch.randn(F, K, device=DEV, dtype=torch.bfloat16) * 0.05
+    w = ref.interleave_gate_up(g, u)
+    b = torch.randn(2 * F, device=DEV, dtype=torch.bfloat16) * 0.1
+    y = ops.gemm(x, w, epi=epi, bias=b)
+    r = ref.gemm_ref(x.cpu(), w.cpu(), epi, bias=b.cpu())
+    assert y.shape == (M, F)
+    assert _rel(y.cpu(), r) < 1.5e-2
+
+
+def test_gemm_residual_add():
+    torch.manual_seed(4)
+    x = torch.randn(40, 256, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(512, 256, device=DEV, dtype=torch.bfloat16) * 0.05
+    res = torch.randn(40, 512, device=DEV, dtype=torch.bfloat16)
+    y = ops.gemm(x, w, epi="add", residual=res)
+    assert _rel(y.cpu(), ref.gemm_ref(x.cpu(), w.cpu(), "add", res.cpu())) < 1e-2
+
+
+def test_gemm_batch_invariance():
+    """A row's output does not depend on how many other rows share the GEMM."""
+    torch.manual_seed(5)
+    K, N = 4096, 6144
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.02
+    x = torch.randn(64, K, device=DEV, dtype=torch.bfloat16)
+    full = ops.gemm(x, w)
+    for m in (1, 5, 16, 33):
+        part = ops.gemm(x[:m].contiguous(), w)
+        assert torch.equal(part, full[:m]), m
+
+
+def test_add_rmsnorm():
+    torch.manual_seed(6)
+    x = torch.randn(17, 4096, device=DEV, dtype=torch.bfloat16)
+    d = torch.randn(17, 4096, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(4096, device=DEV, dtype=torch.bfloat16)
+    xr, yr = ref.add_rmsnorm_ref(x.cpu(), d.cpu(), w.cpu(), 1e-6)
+    y = ops.add_rmsnorm(x, d, w, 1e-6)
+    assert torch.equal(x.cpu(), xr)
+    assert _rel(y.cpu(), yr) < 5e-3
+
+
+@pytest.mark.parametrize("H,KVH,D", [(32, 8, 128), (4, 2, 64), (64, 8, 64)])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_qk_norm_rope_kv(H, KVH, D, fp8):
+    from mlx_swift_lm_b200.models.rope import build_rope
+
+    torch.manual_seed(7)
+    T, P = 37, 8
+    qkv = torch.randn(T, (H + 2 * KVH) * D, device=DEV, dtype=torch.bfloat16)
+    pos = torch.randint(0, 1000, (T,), device=DEV, dtype=torch.int32)
+    slots = torch.randperm(P * 16, device=DEV)[:T].to(torch.int64)
+    cs, rot = build_rope(D, 1e6, None, 1024)
+    cs = cs.to(DEV)
+    qn = torch.randn(D, device=DEV, dtype=torch.bfloat16)
+    kn = torch.randn(D, device=DEV, dtype=torch.bfloat16)
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    kc = torch.zeros(P, KVH, 16, D, device=DEV, dtype=dt)
+    vc = torch.zeros_like(kc)
+    ks = torch.rand(KVH, device=DEV) + 0.5 if fp8 else None
+    vs = torch.rand(KVH, device=DEV) + 0.5 if fp8 else None
+    q = ops.qk_norm_rope_kv(qkv, pos, slots, cs, rot, False, qn, kn, 1e-6, kc, vc, H, KVH, D, ks, vs)
+    kc_r = torch.zeros(P, KVH, 16, D, dtype=dt)
+    vc_r = torch.zeros_like(kc_r)
+    qr, _, _ = ref.qk_norm_rope_kv_ref(qkv.cpu(), pos.cpu(), slots.cpu(), cs.cpu(), rot, False, qn.cpu(), kn.cpu(),
+                                       1e-6, kc_r, vc_r, H, KVH, D, None if ks is None else ks.cpu(),
+                                       None if vs is None else vs.cpu())
+    assert _rel(q.cpu(), qr) < 1e-2
+    tol = 0.07 if fp8 else 1e-2
+    assert _rel(kc.cpu().float(), kc_r.float()) < tol
+    assert _rel(vc.cpu().float(), vc_r.float()) < tol
+
+
+def _make_paged(B, lens, KVH, D, P, dt=torch.bfloat16):
+    maxp = max((l + 15) // 16 for l in lens)
+    perm = torch.randperm(P)
+    pt = torch.zeros(B, maxp, dtype=torch.int32)
+    k = 0
+    for b, l in enumerate(lens):
+        n = (l + 15) // 16
+        pt[b, :n] = perm[k:k + n].to(torch.int32)
+        k += n
+    kc = (torch.randn(P, KVH, 16, D) * 1.0).to(dt)
+    vc = torch.randn(P, KVH, 16, D).to(dt)
+    return kc, vc, pt
+
+
+@pytest.mark.parametrize("H,KVH,D", [(32, 8, 128), (4, 2, 64), (64, 8, 64), (8, 8, 128), (16, 1, 128),
+                                     (8, 2, 256)])
+@pytest.mark.parametrize("window,sinks", [(0, False), (100, False), (0, True), (128, True)])
+def test_paged_decode(H, KVH, D, window, sinks):
+    torch.manual_seed(8)
+    lens = [1, 15, 16, 17, 255, 256, 257, 700, 1500]
+    B = len(lens)
+    P = sum((l + 15) // 16 for l in lens) + 5
+    kc, vc, pt = _make_paged(B, lens, KVH, D, P)
+    q = torch.randn(B, H, D, dtype=torch.bfloat16)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    sk = torch.randn(H) if sinks else None
+    scale = D ** -0.5
+    r = ref.paged_decode_ref(q, kc, vc, pt, sl, scale, window, sk)
+    y = ops.paged_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), pt.to(DEV), sl.to(DEV), scale, window,
+                         None if sk is None else sk.to(DEV))
+    assert _rel(y.cpu(), r) < 1e-2
+
+
+def test_paged_decode_fp8():
+    torch.manual_seed(9)
+    H, KVH, D = 32, 8, 128
+    lens = [33, 400, 1025]
+    P = 200
+    kc, vc, pt = _make_paged(3, lens, KVH, D, P, torch.float32)
+    ks = torch.rand(KVH) + 0.5
+    vs = torch.rand(KVH) + 0.5
+    kq = (kc / ks[None, :, None, None]).to(torch.float8_e4m3fn)
+    vq = (vc / vs[None, :, None, None]).to(torch.float8_e4m3fn)
+    q = torch.randn(3, H, D, dtype=torch.bfloat16)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    r = ref.paged_decode_ref(q, kq, vq, pt, sl, D ** -0.5, k_scale=ks, v_scale=vs)
+    y = ops.paged_decode(q.to(DEV), kq.to(DEV), vq.to(DEV), pt.to(DEV), sl.to(DEV), D ** -0.5,
+                         k_scale=ks.to(DEV), v_scale=vs.to(DEV))
+    assert _rel(y.cpu(), r) < 1e-2
+
+
+def test_paged_decode_batch_invariance():
+    torch.manual_seed(10)
+    H, KVH, D = 32, 8, 128
+    lens = [300, 1200, 77, 2000]
+    P = 300
+    kc, vc, pt = _make_paged(4, lens, KVH, D, P)
+    q = torch.randn(4, H, D, dtype=torch.bfloat16, device=DEV)
+    kc, vc, pt = kc.to(DEV), vc.to(DEV), pt.to(DEV)
+    sl = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    full = ops.paged_decode(q, kc, vc, pt, sl, D ** -0.5)
+    for b in range(4):
+        one = ops.paged_decode(q[b:b + 1].contiguous(), kc, vc, pt[b:b + 1].contiguous(), sl[b:b + 1], D ** -0.5)
+        assert torch.equal(one[0], full[b])
+
+
+@pytest.mark.parametrize("H,KVH,D", [(32, 8, 128), (4, 2, 64), (64, 8, 64)])
+@pytest.mark.parametrize("window,sinks", [(0, False), (64, True)])
+def test_paged_prefill(H, KVH, D, window, sinks):
+    torch.manual_seed(11)
+    # rows: (history before the chunk, chunk length)
+    rows = [(0, 37), (100, 64), (16, 1), (250, 130)]
+    lens = [h + c for h, c in rows]
+    P = sum((l + 15) // 16 for l in lens) + 3
+    kc, vc, pt = _make_paged(len(rows), lens, KVH, D, P)
+    cu = [0]
+    for h, c in rows:
+        cu.append(cu[-1] + c)
+    T = cu[-1]
+    q = torch.randn(T, H, D, dtype=torch.bfloat16)
+    cu_t = torch.tensor(cu, dtype=torch.int32)
+    p0 = torch.tensor([h for h, _ in rows], dtype=torch.int32)
+    sk = torch.randn(H) if sinks else None
+    r = ref.paged_prefill_ref(q, kc, vc, pt, cu_t, p0, D ** -0.5, window, sk)
+    y = ops.paged_prefill(q.to(DEV), kc.to(DEV), vc.to(DEV), pt.to(DEV), cu_t.to(DEV), p0.to(DEV), D ** -0.5, window,
+                          None if sk is None else sk.to(DEV), cu_q_host=cu)
+    assert _rel(y.cpu(), r) < 1e-2
+
+
+def test_argmax_and_sample_match_oracle():
+    torch.manual_seed(12)
+    B, V = 6, 151936
+    logits = torch.randn(B, V) * 3
+    a = ops.argmax(logits.to(DEV))
+    assert torch.equal(a.cpu(), logits.argmax(-1).to(torch.int32))
+    params = [dict(temperature=0.7, top_k=0, top_p=1.0, min_p=0.0, key=11, step=3),
+              dict(temperature=1.0, top_k=40, top_p=1.0, min_p=0.0, key=12, step=0),
+              dict(temperature=0.9, top_k=0, top_p=0.8, min_p=0.0, key=13, step=9),
+              dict(temperature=1.3, top_k=100, top_p=0.5, min_p=0.05, key=14, step=2),
+              dict(temperature=0.0, top_k=0, top_p=1.0, min_p=0.0, key=15, step=1),
+              dict(temperature=1.0, top_k=0, top_p=1.0, min_p=0.2, key=16, step=7)]
+    f = lambda k, dt: torch.tensor([p[k] for p in params], dtype=dt, device=DEV)
+    keys = torch.tensor([p["key"] for p in params], dtype=torch.int64, device=DEV)
+    toks = ops.sample(logits.to(DEV), f("temperature", torch.float32), f("top_k", torch.int32),
+                      f("top_p", torch.float32), f("min_p", torch.float32), keys, f("step", torch.int64))
+    exp = [ref.sample_ref(logits[b], **{k: v for k, v in params[b].items()}) for b in range(B)]
+    assert toks.cpu().tolist() == exp
+
+
+def test_process_logits_matches_oracle():
+    torch.manual_seed(13)
+    B, V = 3, 5000
+    logits = torch.randn(B, V)
+    bias = {5: 2.0, 17: -1.5}
+    rep = [3, 3, 9, 100, 5]
+    outs = [3, 9, 9, 9, 42]
+    exp = torch.stack([ref.process_logits_ref(logits[b], bias, rep, 1.3, outs, 0.4, 0.7) for b in range(B)])
+    t = lambda a, dt: torch.tensor(a, dtype=dt, device=DEV)
+    lg = logits.to(DEV)
+    ops.process_logits(lg, t([[5, 17]] * B, torch.int32), t([[2.0, -1.5]] * B, torch.float32),
+                       t([2] * B, torch.int32), t([rep] * B, torch.int32), t([5] * B, torch.int32),
+                       t([1.3] * B, torch.float32), t([outs] * B, torch.int32), t([5] * B, torch.int32),
+                       t([0.4] * B, torch.float32), t([0.7] * B, torch.float32))
+    assert torch.allclose(lg.cpu(), exp, atol=1e-5)
+
+
+def test_philox_host_matches_numpy():
+    import ctypes
+
+    from mlx_swift_lm_b200.ops import _lib
+    import numpy as np
+
+    L = _lib.lib()
+    idx = np.arange(64)
+    host = [L.b200_philox_u32(ctypes.c_uint64(123456789), ctypes.c_uint64(77), int(i)) for i in idx]
+    assert host == ref.philox_u32(123456789, 77, idx).tolist()
+
+
+def test_status_words_clean():
+    from mlx_swift_lm_b200.ops import _lib
+
+    st = _lib.read_status()
+    assert all(v == 0 for v in st.values()), st
