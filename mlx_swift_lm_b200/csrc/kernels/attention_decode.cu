@@ -274,20 +274,23 @@ __global__ void __launch_bounds__(128) paged_decode_part_kernel(DecodeArgs a) {
   }
 }
 
-// One CTA per row, one warp per head (looping). Writes bf16 output.
+// One warp per (row, head); 4 warps per CTA. Writes bf16 output.
 template <int D>
-__global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeArgs a, int B) {
   constexpr int DL = D / 32 > 0 ? D / 32 : 1;
-  const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gi = blockIdx.x * 4 + warp;
+  if (gi >= B * a.H) return;
+  const int b = gi / a.H;
   const int L = a.seq_lens[b];
   const int start = a.window > 0 ? max(0, L - a.window) : 0;
   const int p_first = start / kPartTokens, p_last = L > 0 ? (L - 1) / kPartTokens : -1;
-  for (int h = warp; h < a.H; h += blockDim.x >> 5) {
+  {
+    const int h = gi % a.H;
     __nv_bfloat16* o = a.out + ((size_t)b * a.H + h) * D;
     if (L <= 0) {
       for (int d = lane; d < D; d += 32) o[d] = f2bf(0.f);
-      continue;
+      return;
     }
     const size_t base = ((size_t)b * a.H + h) * a.max_parts;
     float M = a.sinks ? a.sinks[h] * kLog2e : -INFINITY;
@@ -328,7 +331,7 @@ static int launch_decode(const DecodeArgs& a, int B, cudaStream_t st) {
   }
   dim3 grid(a.max_parts, a.KVH, B);
   paged_decode_part_kernel<D, G, KVT><<<grid, 128, smem, st>>>(a);
-  paged_decode_merge_kernel<D><<<B, 128, 0, st>>>(a);
+  paged_decode_merge_kernel<D><<<(B * a.H + 3) / 4, 128, 0, st>>>(a, B);
   return (int)cudaGetLastError();
 }
 

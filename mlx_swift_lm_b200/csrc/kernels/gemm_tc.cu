@@ -1,25 +1,28 @@
-// Dense bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// Dense bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA),
+// with split-K reduced inside a thread-block cluster over distributed shared
+// memory.
 //
-//   Y[M, N] = X[M, K] . W[N, K]^T        (X: activations, W: nn.Linear weight)
+//   Y[M, N] = epi(X[M, K] . W[N, K]^T + bias)     (X: activations, W: nn.Linear weight)
 //
 // Orientation ("swap AB"): the MMA's 128-row M side walks the weight rows
 // (output features) and its N side walks the tokens, so a decode batch of
-// 1..128 rows still fills the 128-lane accumulator. One CTA owns a
-// 128-feature x BN-token output tile and a contiguous range of 64-wide K
-// blocks:
-//   warp 0 / lane 0 : TMA producer (weights + activations, 128B swizzle)
-//   warp 1 / lane 0 : MMA issuer (tcgen05.mma kind::f16, accumulator in TMEM)
-//   warps 0..3      : epilogue (tcgen05.ld, fused activation, store)
-// Split-K partials go to an fp32 workspace; the last CTA of a tile (atomic
-// ticket) sums the partials in split order 0..S-1, so results are
-// deterministic and independent of which CTA finishes last. The split count
-// is chosen from (N, K) only for M <= 128, which keeps a row's result the same
-// whatever the decode batch size is.
+// 1..128 rows still fills the 128-lane accumulator.
 //
-// Replaces the MLX matmul / quantizedMatmul library calls that the reference
-// relies on for every Linear (Libraries/MLXLMCommon/SwitchLayers.swift:1361,
-// AttentionUtils.swift:133 call sites); the dequantizing variants live in
-// gemm_quant.cu.
+// Grid (N/128, ceil(M/BN), S) with cluster (1, 1, S): the S CTAs of a cluster
+// own the same 128 x BN output tile and disjoint, fixed ranges of 64-wide K
+// blocks. Per CTA:
+//   warp 0 / lane 0 : TMA producer (weights evict-first, activations evict-last)
+//   warp 1 / lane 0 : MMA issuer (tcgen05.mma kind::f16, fp32 accumulator in TMEM)
+//   warps 0..3      : drain TMEM -> this CTA's shared memory as an fp32 partial
+// then, after a cluster barrier, CTA z reduces token columns [z*BN/S, ...) of
+// the tile by reading the S partials through DSMEM (mapa + ld.shared::cluster)
+// in split order 0..S-1, applies the epilogue and stores. S depends only on
+// (N, K) - never on M - so a row's result is bit-identical whatever the batch
+// (decode rows alone, or mixed with prefill chunks): the batch-composition
+// invariance the reference engine guarantees (docs/engine-v2/TESTPLAN.md).
+//
+// Replaces the MLX matmul the reference uses for every Linear
+// (Libraries/MLXLMCommon/SwitchLayers.swift:1361 and the model files).
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -31,9 +34,9 @@ namespace b200 {
 
 enum GemmEpilogue : int {
   kEpiStoreBf16 = 0,  // Y = bf16(acc)
-  kEpiSwiGLU = 1,     // weight rows interleaved in 64-row gate/up halves: Y[:, f] = silu(gate) * up
+  kEpiSwiGLU = 1,     // W rows interleaved in 64-row gate/up halves: Y[:, f] = silu(gate) * up
   kEpiStoreF32 = 2,   // Y = acc (fp32)
-  kEpiAddBf16 = 3,    // Y = bf16(acc + R)   (R has Y's layout)
+  kEpiAddBf16 = 3,    // Y = bf16(bf16(acc) + R)   (R has Y's layout)
   kEpiGeGLU = 4,      // as kEpiSwiGLU with gelu(tanh approximation) on the gate
   kEpiSwiGLUOAI = 5,  // GPT-OSS gate: g=min(g,7), u=clamp(u,-7,7), (u+1)*g*sigmoid(1.702g)
 };
@@ -54,9 +57,7 @@ __device__ __forceinline__ float glu_act(int epi, float g, float u) {
 struct GemmArgs {
   void* Y;
   const __nv_bfloat16* R;
-  const __nv_bfloat16* bias;  // [N] per output row of W, or null
-  float* ws;
-  int* counters;
+  const __nv_bfloat16* bias;  // [N] per row of W, or null
   int M, N, K, ldy, ldr;
   int kb_total, kb_per_split, ksplit;
   int epi;
@@ -67,10 +68,27 @@ struct GemmSmem {
   static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
   static constexpr int kBBytes = BN * 128;   // BN rows x 64 bf16
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kPipeBytes = STAGES * kStageBytes;
+  static constexpr int kPartBytes = BN * 128 * 4;  // fp32 partial [BN][128]
+  static constexpr int kMain = kPipeBytes > kPartBytes ? kPipeBytes : kPartBytes;
+  static constexpr int kBarOffset = kMain;
   static constexpr int kTotal = kBarOffset + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
 };
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(128, 1)
@@ -114,8 +132,8 @@ __global__ void __launch_bounds__(128, 1)
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
-    const uint64_t pol_w = l2_policy_evict_first();  // weights stream through once per step
-    const uint64_t pol_x = l2_policy_evict_last();   // activations are re-read by every feature tile
+    const uint64_t pol_w = l2_policy_evict_first();
+    const uint64_t pol_x = l2_policy_evict_last();
     int issued = 0;
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
@@ -128,8 +146,7 @@ __global__ void __launch_bounds__(128, 1)
       tma_load_2d(b, &tmX, bar_full + 8 * s, kc, m0, pol_x);
       issued = i + 1;
     }
-    // Drain: make sure no copy we issued is still landing when the CTA exits
-    // (only matters if the consumer gave up early).
+    // make sure no copy issued here is still landing when the stage memory is reused
     for (int i = max(0, issued - STAGES); i < issued; ++i)
       mbar_wait(bar_full + 8 * (i % STAGES), (i / STAGES) & 1, kErrGemmWait);
   } else if (warp == 1 && lane == 0) {
@@ -151,116 +168,81 @@ __global__ void __launch_bounds__(128, 1)
   }
   __syncwarp();
 
-  // ---------------- Epilogue (all 4 warps) ----------------
-  // CTA-uniform verdict: the epilogue below contains block barriers.
+  // ---------------- drain TMEM into this CTA's fp32 partial [BN][128] ----------------
   const bool acc_ok = __syncthreads_and(mbar_wait(bar_accum, 0, kErrTmemWait) ? 1 : 0) != 0;
   tc_fence_after();
-  const int row_lane = warp * 32 + lane;  // TMEM lane == weight row within tile
-  const int n = n0 + row_lane;
-  const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
-  float* xbuf = reinterpret_cast<float*>(smem);  // stage memory is free once the accumulator is final
-
-  const bool split = args.ksplit > 1;
-  bool do_final = true;
-  if (split) {
-    // 1) publish this split's partial tile
-    float* wsz = args.ws + (size_t)z * args.M * args.N;
+  const int r = warp * 32 + lane;  // TMEM lane == weight row within the tile
+  float* part = reinterpret_cast<float*>(smem);
+  {
+    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
     for (int jc = 0; jc < BN; jc += 16) {
-      uint32_t r[16];
-      tmem_ld16(t_lane + jc, r);
+      uint32_t v[16];
+      tmem_ld16(t_lane + jc, v);
       tc_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = m0 + jc + j;
-        if (m < args.M && n < args.N && nkb > 0) wsz[(size_t)m * args.N + n] = __uint_as_float(r[j]);
-        else if (m < args.M && n < args.N) wsz[(size_t)m * args.N + n] = 0.f;
-      }
-    }
-    __threadfence();
-    __syncthreads();
-    __shared__ int s_ticket;
-    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-    if (threadIdx.x == 0) s_ticket = atomicAdd(&args.counters[tile], 1);
-    __syncthreads();
-    do_final = (s_ticket == args.ksplit - 1);
-    if (do_final) {
-      __threadfence();
-      if (threadIdx.x == 0) args.counters[tile] = 0;  // self-reset for the next launch / graph replay
+      for (int j = 0; j < 16; ++j) part[(jc + j) * 128 + r] = (acc_ok && nkb > 0) ? __uint_as_float(v[j]) : 0.f;
     }
   }
-
-  if (do_final && acc_ok) {
-    for (int jc = 0; jc < BN; jc += 16) {
-      float v[16];
-      if (!split) {
-        uint32_t r[16];
-        tmem_ld16(t_lane + jc, r);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + jc + j;
-          float acc = 0.f;
-          if (m < args.M && n < args.N) {
-            const float* p = args.ws + (size_t)m * args.N + n;
-            acc = __ldcg(p);
-            for (int zz = 1; zz < args.ksplit; ++zz) acc += __ldcg(p + (size_t)zz * args.M * args.N);
-          }
-          v[j] = acc;
-        }
-      }
-      if (args.bias && n < args.N) {
-        const float bb = bf2f(args.bias[n]);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] += bb;
-      }
-      const bool glu = args.epi == kEpiSwiGLU || args.epi == kEpiGeGLU || args.epi == kEpiSwiGLUOAI;
-      if (glu) {
-        // rows 0..63 of the tile are gate rows, 64..127 the matching up rows
-        __syncthreads();
-        if (warp >= 2) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) xbuf[(row_lane - 64) * 17 + j] = v[j];
-        }
-        __syncthreads();
-        if (warp < 2) {
-          __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(args.Y);
-          const int f = (n0 >> 1) + row_lane;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + jc + j;
-            if (m < args.M && f < (args.N >> 1)) {
-              const float up = xbuf[row_lane * 17 + j];
-              // round the gate and up projections to bf16 first, as an
-              // unfused bf16 model would, then apply silu(g) * u in fp32
-              const float g = bf2f(f2bf(v[j]));
-              const float u = bf2f(f2bf(up));
-              Y[(size_t)m * args.ldy + f] = f2bf(glu_act(args.epi, g, u));
-            }
-          }
-        }
-      } else if (n < args.N) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + jc + j;
-          if (m >= args.M) break;
-          if (args.epi == kEpiStoreF32) {
-            reinterpret_cast<float*>(args.Y)[(size_t)m * args.ldy + n] = v[j];
-          } else if (args.epi == kEpiAddBf16) {
-            const float rr = bf2f(args.R[(size_t)m * args.ldr + n]);
-            reinterpret_cast<__nv_bfloat16*>(args.Y)[(size_t)m * args.ldy + n] = f2bf(bf2f(f2bf(v[j])) + rr);
-          } else {
-            reinterpret_cast<__nv_bfloat16*>(args.Y)[(size_t)m * args.ldy + n] = f2bf(v[j]);
-          }
-        }
-      }
-    }
-  }
-
   tc_fence_before();
-  __syncthreads();
+  if (args.ksplit > 1) cluster_sync();
+  else __syncthreads();
+
+  // ---------------- cluster reduction + epilogue ----------------
+  const int ks = args.ksplit;
+  const int js = (BN + ks - 1) / ks;
+  const int j_lo = z * js;
+  const int j_hi = min(BN, min(j_lo + js, args.M - m0));
+  const uint32_t part_addr = smem_u32(part);
+  uint32_t rbase[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) rbase[q] = q < ks ? (ks > 1 ? mapa_shared(part_addr, q) : part_addr) : 0u;
+  auto reduce_at = [&](int j, int row) -> float {
+    if (ks == 1) return part[j * 128 + row];
+    const uint32_t off = (uint32_t)((j * 128 + row) * 4);
+    float acc = ld_dsmem_f32(rbase[0] + off);
+#pragma unroll
+    for (int q = 1; q < 8; ++q)
+      if (q < ks) acc += ld_dsmem_f32(rbase[q] + off);
+    return acc;
+  };
+  const bool glu = args.epi == kEpiSwiGLU || args.epi == kEpiGeGLU || args.epi == kEpiSwiGLUOAI;
+  if (glu) {
+    const int row = r & 63, par = r >> 6;
+    const int f = (n0 >> 1) + row;
+    __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(args.Y);
+    const float bg = args.bias ? bf2f(args.bias[n0 + row]) : 0.f;
+    const float bu = args.bias ? bf2f(args.bias[n0 + 64 + row]) : 0.f;
+    if (f < (args.N >> 1)) {
+      for (int j = j_lo + par; j < j_hi; j += 2) {
+        // round the gate and up projections to bf16 first, as an unfused bf16
+        // model would, then apply the activation in fp32
+        const float g = bf2f(f2bf(reduce_at(j, row) + bg));
+        const float u = bf2f(f2bf(reduce_at(j, row + 64) + bu));
+        Y[(size_t)(m0 + j) * args.ldy + f] = f2bf(glu_act(args.epi, g, u));
+      }
+    }
+  } else {
+    const int n = n0 + r;
+    if (n < args.N) {
+      const float bb = args.bias ? bf2f(args.bias[n]) : 0.f;
+      for (int j = j_lo; j < j_hi; ++j) {
+        const float v = reduce_at(j, r) + bb;
+        const size_t m = (size_t)(m0 + j);
+        if (args.epi == kEpiStoreF32) {
+          reinterpret_cast<float*>(args.Y)[m * args.ldy + n] = v;
+        } else if (args.epi == kEpiAddBf16) {
+          const float rr = bf2f(args.R[m * args.ldr + n]);
+          reinterpret_cast<__nv_bfloat16*>(args.Y)[m * args.ldy + n] = f2bf(bf2f(f2bf(v)) + rr);
+        } else {
+          reinterpret_cast<__nv_bfloat16*>(args.Y)[m * args.ldy + n] = f2bf(v);
+        }
+      }
+    }
+  }
+  // no CTA may leave while a peer still reads its partial
+  if (args.ksplit > 1) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, S::kTmemCols);
@@ -301,7 +283,7 @@ struct TmKeyHash {
   }
 };
 
-// 2-D row-major tensor map with a 128-byte swizzle: box = box_rows x (128 bytes).
+// 2-D row-major tensor map with a 128-byte swizzle: box = box_rows x box_cols.
 // Returns false if the driver rejects the layout.
 bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows,
                   int box_cols, int dtype_bytes) {
@@ -346,33 +328,49 @@ static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmA
     if (e != cudaSuccess) return (int)e;
     configured = true;
   }
-  dim3 grid(tiles_n, tiles_m, a.ksplit);
-  gemm_bf16_tc_kernel<BN, STAGES><<<grid, 128, S::kTotal, st>>>(tw, tx, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles_n, tiles_m, a.ksplit);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = S::kTotal;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = a.ksplit;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<BN, STAGES>, tw, tx, a);
+  if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
 }
 
-// Split-K choice for skinny (decode) GEMMs: depends only on (N, K), never on
-// M, so a row's reduction order does not change with the batch size.
-static int choose_kb_per_split(int N, int K, int M, int num_sms) {
+// Split count S (1..8, the cluster size) for a weight of N rows and K inputs.
+// A function of (N, K) only: every M uses the same K partition and the same
+// reduction order. Chosen so skinny (decode) GEMMs fill the machine with about
+// two CTAs per SM while every split keeps at least 8 K blocks.
+static int choose_splits(int N, int K, int num_sms) {
   const int kb = (K + 63) / 64;
   const int tiles = (N + 127) / 128;
-  if (M > 128 || tiles >= 2 * num_sms) return kb;
-  double best_eff = -1.0;
-  int best = kb;
-  for (int kps = kb; kps >= 4; --kps) {
-    const int s = (kb + kps - 1) / kps;
-    if (s > 16) break;
+  const int slots = 2 * num_sms;
+  if (tiles >= slots) return 1;
+  double best = -1.0;
+  int best_s = 1;
+  for (int s = 1; s <= 8; ++s) {
+    const int kps = (kb + s - 1) / s;
+    if (s > 1 && kps < 8) break;
+    const int s_eff = (kb + kps - 1) / kps;
+    if (s_eff != s) continue;
     const long ctas = (long)tiles * s;
-    const long waves = (ctas + num_sms - 1) / num_sms;
-    double eff = (double)ctas / (double)(waves * num_sms);
-    // prefer at least ~one full wave; penalise tiny per-split work
-    if (ctas < num_sms) eff *= (double)ctas / num_sms;
-    if (eff > best_eff + 1e-9) {
-      best_eff = eff;
-      best = kps;
+    const long waves = (ctas + slots - 1) / slots;
+    double eff = (double)ctas / (double)(waves * slots);
+    eff -= 0.01 * s;  // reduction work grows with s
+    if (eff > best + 1e-9) {
+      best = eff;
+      best_s = s;
     }
   }
-  return best;
+  return best_s;
 }
 
 }  // namespace b200
@@ -381,27 +379,18 @@ using namespace b200;
 
 extern "C" {
 
-// Workspace needed (bytes) for a GEMM of this shape; counters needed = tiles.
-size_t b200_gemm_workspace_bytes(int M, int N, int K, int num_sms) {
-  const int kb = (K + 63) / 64;
-  const int kps = choose_kb_per_split(N, K, M, num_sms);
-  const int s = (kb + kps - 1) / kps;
-  return s > 1 ? (size_t)s * M * N * sizeof(float) : 0;
-}
-
 int b200_gemm_num_splits(int M, int N, int K, int num_sms) {
-  const int kb = (K + 63) / 64;
-  const int kps = choose_kb_per_split(N, K, M, num_sms);
-  return (kb + kps - 1) / kps;
+  (void)M;
+  return choose_splits(N, K, num_sms);
 }
 
-// Y[M, :] = epi(X[M, K] . W[N, K]^T). X row stride ldx, W row stride ldw (elements).
+// Y[M, :] = epi(X[M, K] . W[N, K]^T + bias). X row stride ldx, W row stride ldw (elements).
 // epi: 0 bf16 store, 1 SwiGLU (W rows interleaved gate/up per 64), 2 fp32 store, 3 bf16 add R,
-// 4 GeGLU, 5 GPT-OSS SwiGLU. `bias` (per W row) is added to the accumulator first.
+// 4 GeGLU, 5 GPT-OSS SwiGLU. force_splits > 0 overrides the split count (tests / tuning).
 // Returns 0 on success, a CUDA error code, or -1 for a bad layout.
 int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, int ldw, void* Y, int ldy,
-                   const void* R, int ldr, const void* bias, int epi, void* ws, size_t ws_bytes, int* counters,
-                   int n_counters, int num_sms, int force_kps, cudaStream_t stream) {
+                   const void* R, int ldr, const void* bias, int epi, int num_sms, int force_splits,
+                   cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
   if ((K % 8) || (ldx % 8) || (ldw % 8) || ((uintptr_t)X & 15) || ((uintptr_t)W & 15)) return -1;
   const bool glu = epi == kEpiSwiGLU || epi == kEpiGeGLU || epi == kEpiSwiGLUOAI;
@@ -414,8 +403,6 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   a.Y = Y;
   a.R = reinterpret_cast<const __nv_bfloat16*>(R);
   a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
-  a.ws = reinterpret_cast<float*>(ws);
-  a.counters = counters;
   a.M = M;
   a.N = N;
   a.K = K;
@@ -423,18 +410,16 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   a.ldr = ldr;
   a.epi = epi;
   a.kb_total = (K + 63) / 64;
-  a.kb_per_split = force_kps > 0 ? force_kps : choose_kb_per_split(N, K, M, num_sms);
+  const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms);
+  if (s > 8) return -1;
+  a.kb_per_split = (a.kb_total + s - 1) / s;
   a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
   const int tiles_n = (N + 127) / 128, tiles_m = (M + BN - 1) / BN;
-  if (a.ksplit > 1) {
-    if (!ws || ws_bytes < (size_t)a.ksplit * M * N * sizeof(float)) return -2;
-    if (!counters || n_counters < tiles_n * tiles_m) return -3;
-  }
   switch (BN) {
-    case 16: return launch_gemm<16, 8>(tw, tx, a, tiles_n, tiles_m, stream);
-    case 32: return launch_gemm<32, 8>(tw, tx, a, tiles_n, tiles_m, stream);
-    case 64: return launch_gemm<64, 8>(tw, tx, a, tiles_n, tiles_m, stream);
-    case 128: return launch_gemm<128, 6>(tw, tx, a, tiles_n, tiles_m, stream);
+    case 16: return launch_gemm<16, 6>(tw, tx, a, tiles_n, tiles_m, stream);
+    case 32: return launch_gemm<32, 5>(tw, tx, a, tiles_n, tiles_m, stream);
+    case 64: return launch_gemm<64, 4>(tw, tx, a, tiles_n, tiles_m, stream);
+    case 128: return launch_gemm<128, 3>(tw, tx, a, tiles_n, tiles_m, stream);
     default: return launch_gemm<256, 4>(tw, tx, a, tiles_n, tiles_m, stream);
   }
 }

@@ -1,0 +1,295 @@
+"""Checkpoint loading: HF / MLX directories -> :class:`DecoderLM`.
+
+Parity: ``loadModelContainer`` (MLXLMCommon/ModelFactory.swift:310) resolves a
+directory, reads ``config.json``, dispatches on ``model_type`` and runs
+``loadWeights`` (Load.swift:522): read every shard, per-model ``sanitize``
+(drop ``lm_head`` for tied models, Qwen3.swift:200-207), quantized modules
+from ``scales``/``biases`` (``applyCheckpoint`` :651), convert to bf16 (:733).
+
+Here the per-family sanitize step is the name mapping below; projections are
+fused at load (q|k|v into one weight, gate/up interleaved in 64-row blocks
+for the SwiGLU GEMM epilogue) and sliced for tensor parallelism.
+MLX affine / MXFP4 / NVFP4 / MXFP8 weights are kept in their packed layout
+(:class:`QuantizedWeight`) when a dequantising kernel serves them, and are
+dequantised to bf16 otherwise.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+
+import torch
+
+from ..models.config import DecoderConfig
+from ..models.decoder import DecoderLM, LayerWeights, TensorParallel
+from ..models.families import build_config
+from ..ops import quant
+from ..ops.reference import interleave_gate_up
+from .safetensors import load_safetensors
+
+
+class CheckpointView:
+    """Name lookup over a flat tensor dict with prefix detection and MLX-quantized
+    linear dequantisation."""
+
+    def __init__(self, tensors: dict, qcfg: dict | None, dtype):
+        self.t = tensors
+        self.q = qcfg or {}
+        self.dtype = dtype
+        keys = list(tensors)
+        self.prefix = ""
+        for pre in ("model.language_model.", "language_model.model.", "model.", "transformer.", ""):
+            if any(k.startswith(pre + "layers.0.") or k.startswith(pre + "embed_tokens") for k in keys):
+                self.prefix = pre
+                break
+        self.used = set()
+
+    def has(self, name):
+        return (self.prefix + name) in self.t or name in self.t
+
+    def raw(self, name):
+        key = self.prefix + name if (self.prefix + name) in self.t else name
+        self.used.add(key)
+        return self.t[key]
+
+    def _qparams(self, base):
+        q = self.q
+        per = q.get(base) if isinstance(q.get(base), dict) else None
+        src = per or q
+        return src.get("group_size", 64), src.get("bits", 4), src.get("mode", "affine")
+
+    def linear(self, base, required=True):
+        """Weight of a linear layer `base` (without the .weight suffix), dequantised."""
+        wname = base + ".weight"
+        if not self.has(wname):
+            if self.has(base):  # bare parameter (e.g. gpt-oss experts.gate_up_proj)
+                return self.raw(base).to(self.dtype)
+            if required:
+                raise KeyError(f"missing weight {self.prefix + wname}")
+            return None
+        w = self.raw(wname)
+        if self.has(base + ".scales"):
+            gs, bits, mode = self._qparams(base)
+            s = self.raw(base + ".scales")
+            b = self.raw(base + ".biases") if self.has(base + ".biases") else None
+            return quant.dequantize(w, s, b, mode, gs, bits, torch.float32).to(self.dtype)
+        return w.to(self.dtype)
+
+    def vec(self, name, required=False):
+        if not self.has(name):
+            if required:
+                raise KeyError(name)
+            return None
+        return self.raw(name).to(self.dtype)
+
+
+def _shard_rows(w, rank, world):
+    if w is None or world == 1:
+        return w
+    n = w.shape[0] // world
+    return w[rank * n:(rank + 1) * n]
+
+
+def _shard_cols(w, rank, world):
+    if w is None or world == 1:
+        return w
+    n = w.shape[-1] // world
+    return w[..., rank * n:(rank + 1) * n]
+
+
+def _kv_rows(w, cfg, rank, world):
+    """K or V projection rows for this rank (heads split, or replicated when KVH < world)."""
+    if w is None or world == 1:
+        return w
+    D = cfg.head_dim
+    if cfg.num_kv_heads >= world:
+        return _shard_rows(w, rank, world)
+    h = (rank * cfg.num_kv_heads) // world
+    return w[h * D:(h + 1) * D]
+
+
+def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParallel | None = None,
+               config_overrides: dict | None = None):
+    """Load a model directory (config.json + *.safetensors). Returns (model, hf_config)."""
+    with open(os.path.join(path, "config.json")) as f:
+        hf = json.load(f)
+    cfg = build_config(hf)
+    for k, v in (config_overrides or {}).items():
+        setattr(cfg, k, v)
+    tensors, _ = load_safetensors(path)
+    model = build_from_tensors(cfg, tensors, device, dtype, tp)
+    return model, hf
+
+
+def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=torch.float32, tp=None):
+    tp = tp or TensorParallel()
+    r, w = tp.rank, tp.world
+    q = cfg.quantization if isinstance(cfg.quantization, dict) else None
+    ck = CheckpointView(tensors, q, torch.float32)
+    m = DecoderLM(cfg, "cpu", torch.float32, tp=tp)
+    off = 1.0 if cfg.norm_offset_one else 0.0
+
+    def norm(name):
+        v = ck.vec(name, required=True).float()
+        return v + off
+
+    m.embed = ck.linear("embed_tokens")
+    if cfg.extra.get("embedding_multiplier"):
+        pass
+    m.norm = norm("norm.weight")
+    if cfg.tie_word_embeddings or not (ck.has("lm_head.weight") or "lm_head.weight" in tensors):
+        m.lm_head = m.embed
+    else:
+        m.lm_head = ck.linear("lm_head") if ck.has("lm_head.weight") else ck.linear("lm_head", False)
+        if m.lm_head is None:
+            key = "lm_head.weight"
+            m.lm_head = tensors[key].float()
+    hd = cfg.head_dim
+    for i in range(cfg.num_layers):
+        p = f"layers.{i}."
+        L = LayerWeights()
+        L.ln1 = norm(p + "input_layernorm.weight")
+        if cfg.post_norms:
+            L.post_attn_norm = norm(p + "post_attention_layernorm.weight")
+            L.ln2 = norm(p + "pre_feedforward_layernorm.weight")
+            L.post_ffn_norm = norm(p + "post_feedforward_layernorm.weight")
+        else:
+            L.ln2 = norm(p + "post_attention_layernorm.weight")
+        a = p + "self_attn."
+        if cfg.extra.get("fused_qkv"):
+            qkv = ck.linear(a + "qkv_proj")
+            qw, kw, vw = torch.split(qkv, [cfg.q_size, cfg.kv_size, cfg.kv_size], 0)
+        else:
+            qw, kw, vw = ck.linear(a + "q_proj"), ck.linear(a + "k_proj"), ck.linear(a + "v_proj")
+        L.wqkv = torch.cat([_shard_rows(qw, r, w), _kv_rows(kw, cfg, r, w), _kv_rows(vw, cfg, r, w)], 0)
+        if cfg.attention_bias:
+            qb, kb, vb = ck.vec(a + "q_proj.bias"), ck.vec(a + "k_proj.bias"), ck.vec(a + "v_proj.bias")
+            if qb is not None:
+                L.bqkv = torch.cat([_shard_rows(qb, r, w), _kv_rows(kb, cfg, r, w), _kv_rows(vb, cfg, r, w)], 0)
+        if cfg.qk_norm:
+            L.q_norm = norm(a + "q_norm.weight")
+            L.k_norm = norm(a + "k_norm.weight")
+        L.wo = _shard_cols(ck.linear(a + "o_proj"), r, w)
+        if cfg.o_bias:
+            L.bo = ck.vec(a + "o_proj.bias")
+        if cfg.attention_sinks:
+            s = ck.vec(a + "sinks")
+            L.sinks = _shard_rows(s.float(), r, w) if s is not None else torch.zeros(cfg.num_heads // w)
+        if cfg.is_moe(i):
+            _load_moe(ck, cfg, L, p, r, w)
+        else:
+            mp = p + "mlp."
+            if cfg.extra.get("fused_gate_up"):
+                gu = ck.linear(mp + "gate_up_proj")
+                g, u = gu.chunk(2, 0)
+            else:
+                g, u = ck.linear(mp + "gate_proj"), ck.linear(mp + "up_proj")
+            L.moe = False
+            L.wgu = interleave_gate_up(_shard_rows(g, r, w), _shard_rows(u, r, w))
+            L.wd = _shard_cols(ck.linear(mp + "down_proj"), r, w)
+            if cfg.mlp_bias:
+                gb, ub = ck.vec(mp + "gate_proj.bias"), ck.vec(mp + "up_proj.bias")
+                if gb is not None:
+                    L.bgu = interleave_gate_up(_shard_rows(gb, r, w)[:, None], _shard_rows(ub, r, w)[:, None])[:, 0]
+                L.bd = ck.vec(mp + "down_proj.bias")
+        m.layers.append(L)
+    if cfg.norm_offset_one:
+        cfg.norm_offset_one = False  # folded into the stored weights
+    return m.clone_to(device, dtype)
+
+
+def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
+    L.moe = True
+    E = cfg.num_experts
+    if cfg.model_type == "gpt_oss":
+        mp = p + "mlp."
+        L.router = ck.linear(mp + "router")
+        L.router_b = ck.vec(mp + "router.bias")
+        if ck.has(mp + "experts.gate_up_proj_blocks"):
+            blocks = ck.raw(mp + "experts.gate_up_proj_blocks")  # [E, 2F, K/32, 16] uint8
+            scales = ck.raw(mp + "experts.gate_up_proj_scales")  # [E, 2F, K/32] uint8
+            gu = _mxfp4_blocks(blocks, scales)  # [E, 2F, K]
+            gu = gu.transpose(1, 2)  # -> [E, K, 2F] as the bf16 layout
+            db = ck.raw(mp + "experts.down_proj_blocks")
+            ds = ck.raw(mp + "experts.down_proj_scales")
+            down = _mxfp4_blocks(db, ds).transpose(1, 2)  # [E, F, K]... as bf16 layout [E, F, K]
+        else:
+            gu = ck.raw(mp + "experts.gate_up_proj").float()  # [E, K, 2F] (gate even, up odd columns)
+            down = ck.raw(mp + "experts.down_proj").float()  # [E, F, K]
+        g, u = gu[..., 0::2].transpose(1, 2), gu[..., 1::2].transpose(1, 2)  # [E, F, K]
+        gub = ck.vec(mp + "experts.gate_up_proj_bias")
+        L.experts_gu = torch.stack([interleave_gate_up(_shard_rows(g[e], r, w), _shard_rows(u[e], r, w))
+                                    for e in range(E)])
+        L.experts_d = torch.stack([_shard_cols(down[e].t(), r, w) for e in range(E)])  # [E, K, F]
+        if gub is not None:
+            gb, ub = gub[..., 0::2], gub[..., 1::2]
+            L.experts_gu_b = torch.stack([interleave_gate_up(_shard_rows(gb[e], r, w)[:, None],
+                                                             _shard_rows(ub[e], r, w)[:, None])[:, 0]
+                                          for e in range(E)])
+        L.experts_d_b = ck.vec(mp + "experts.down_proj_bias")
+        return
+    mixtral = cfg.extra.get("mixtral_names")
+    mp = p + ("block_sparse_moe." if mixtral else "mlp.")
+    L.router = ck.linear(mp + "gate")
+    names = ("w1", "w3", "w2") if mixtral else ("gate_proj", "up_proj", "down_proj")
+    if ck.has(mp + "switch_mlp.gate_proj.weight"):
+        g = ck.linear(mp + "switch_mlp.gate_proj")
+        u = ck.linear(mp + "switch_mlp.up_proj")
+        d = ck.linear(mp + "switch_mlp.down_proj")
+    else:
+        g = torch.stack([ck.linear(f"{mp}experts.{e}.{names[0]}") for e in range(E)])
+        u = torch.stack([ck.linear(f"{mp}experts.{e}.{names[1]}") for e in range(E)])
+        d = torch.stack([ck.linear(f"{mp}experts.{e}.{names[2]}") for e in range(E)])
+    L.experts_gu = torch.stack([interleave_gate_up(_shard_rows(g[e], r, w), _shard_rows(u[e], r, w)) for e in range(E)])
+    L.experts_d = torch.stack([_shard_cols(d[e], r, w) for e in range(E)])
+    if cfg.shared_expert_intermediate_size:
+        sp = mp + "shared_expert."
+        L.shared_gu = interleave_gate_up(_shard_rows(ck.linear(sp + "gate_proj"), r, w),
+                                         _shard_rows(ck.linear(sp + "up_proj"), r, w))
+        L.shared_d = _shard_cols(ck.linear(sp + "down_proj"), r, w)
+        if ck.has(mp + "shared_expert_gate.weight"):
+            L.shared_gate = ck.linear(mp + "shared_expert_gate")
+
+
+def _mxfp4_blocks(blocks, scales):
+    """HF MXFP4 (blocks [..., G, 16] uint8 with two e2m1 codes per byte, scales [..., G] e8m0) -> float."""
+    lo = (blocks & 0x0F).to(torch.int64)
+    hi = (blocks >> 4).to(torch.int64)
+    codes = torch.stack([lo, hi], -1).reshape(*blocks.shape[:-1], 32)
+    v = quant.E2M1[codes] * quant.e8m0_to_float(scales.to(torch.int64))[..., None]
+    return v.reshape(*blocks.shape[:-2], -1)
+
+
+def load_tokenizer(path: str):
+    """A local HF tokenizer (no network), or None when the directory has none."""
+    try:
+        from transformers import AutoTokenizer
+
+        return AutoTokenizer.from_pretrained(path, local_files_only=True, trust_remote_code=False)
+    except Exception:
+        return None
+
+
+def eos_token_ids(path: str, hf: dict, tokenizer=None) -> set[int]:
+    ids = set()
+    for src in (hf, _read_json(os.path.join(path, "generation_config.json"))):
+        e = (src or {}).get("eos_token_id")
+        if isinstance(e, int):
+            ids.add(e)
+        elif isinstance(e, list):
+            ids.update(int(x) for x in e)
+    if tokenizer is not None and getattr(tokenizer, "eos_token_id", None) is not None:
+        ids.add(int(tokenizer.eos_token_id))
+    return ids
+
+
+def _read_json(p):
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+_ = math

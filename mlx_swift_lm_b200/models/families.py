@@ -1,0 +1,140 @@
+"""Model-family adapters: HF/MLX ``config.json`` -> :class:`DecoderConfig`, and
+checkpoint tensor names -> the fused decoder's weights.
+
+Registry parity with MLXLLM/LLMModelFactory.swift:71-143 (``model_type`` keys).
+Each adapter states the few switches in which its family differs from the
+Llama baseline; :func:`build_config` handles the shared keys.
+"""
+from __future__ import annotations
+
+import math
+
+from .config import DecoderConfig
+
+FAMILIES: dict[str, dict] = {}
+
+
+def register(*model_types, **traits):
+    for mt in model_types:
+        FAMILIES[mt] = dict(traits)
+
+
+# --- the registry -----------------------------------------------------------------
+register("llama", "mistral", "smollm3", "helium", "apertus", "granite", "hunyuan_v1_dense", "exaone4",
+         "ernie4_5", "internlm2", "minicpm", "olmo2", "olmo3", "nanbeige", "laguna", "acereason", "mellum")
+register("qwen2")  # q/k/v biases
+register("qwen3", qk_norm=True)
+register("qwen3_moe", qk_norm=True, moe=True)
+register("qwen3_next", qk_norm=True, moe=True)
+register("mixtral", moe=True, mixtral_names=True)
+register("phimoe", moe=True, mixtral_names=True)
+register("olmoe", moe=True, qk_norm=True)
+register("gemma", gemma=1)
+register("gemma2", gemma=2)
+register("gemma3", "gemma3_text", gemma=3)
+register("phi3", fused_qkv=True, fused_gate_up=True)
+register("gpt_oss", gpt_oss=True)
+register("glm4", fused_gate_up=True)
+register("cohere")
+register("starcoder2")
+
+
+def supported_model_types() -> list[str]:
+    return sorted(FAMILIES)
+
+
+def build_config(hf: dict) -> DecoderConfig:
+    """Translate a HF / MLX config.json dict."""
+    if "text_config" in hf and "hidden_size" not in hf:
+        hf = {**hf["text_config"], "model_type": hf["text_config"].get("model_type", hf.get("model_type"))}
+    mt = hf.get("model_type", "llama")
+    tr = FAMILIES.get(mt)
+    if tr is None:
+        raise ValueError(f"unsupported model_type {mt!r}; supported: {', '.join(supported_model_types())}")
+    hidden = hf["hidden_size"]
+    heads = hf["num_attention_heads"]
+    kvh = hf.get("num_key_value_heads") or heads
+    hd = hf.get("head_dim") or hidden // heads
+    cfg = DecoderConfig(
+        model_type=mt, vocab_size=hf["vocab_size"], hidden_size=hidden, num_layers=hf["num_hidden_layers"],
+        num_heads=heads, num_kv_heads=kvh, head_dim=hd, intermediate_size=hf.get("intermediate_size", 0),
+        rms_norm_eps=hf.get("rms_norm_eps", hf.get("layer_norm_eps", 1e-6)),
+        rope_theta=hf.get("rope_theta", 10000.0), rope_scaling=hf.get("rope_scaling"),
+        partial_rotary_factor=hf.get("partial_rotary_factor", 1.0),
+        max_position_embeddings=hf.get("max_position_embeddings", 4096),
+        tie_word_embeddings=hf.get("tie_word_embeddings", False), qk_norm=tr.get("qk_norm", False),
+        attention_bias=hf.get("attention_bias", mt == "qwen2"), o_bias=hf.get("o_bias", False),
+        mlp_bias=hf.get("mlp_bias", False), quantization=hf.get("quantization") or hf.get("quantization_config"),
+        hidden_act=_act(hf.get("hidden_activation") or hf.get("hidden_act") or "silu"))
+    if cfg.rope_scaling and cfg.rope_scaling.get("rope_type", cfg.rope_scaling.get("type")) == "default":
+        cfg.rope_scaling = None
+    sw = hf.get("sliding_window")
+    layer_types = hf.get("layer_types")
+    if layer_types:
+        cfg.layer_windows = [int(sw or 0) if t == "sliding_attention" else 0 for t in layer_types]
+    elif sw and hf.get("use_sliding_window", True) and mt in ("mistral", "qwen2") and hf.get("use_sliding_window", False):
+        cfg.layer_windows = [int(sw)] * cfg.num_layers
+    if tr.get("moe"):
+        cfg.num_experts = hf.get("num_experts", hf.get("num_local_experts", 0))
+        cfg.num_experts_per_tok = hf.get("num_experts_per_tok", 2)
+        cfg.moe_intermediate_size = hf.get("moe_intermediate_size", cfg.intermediate_size)
+        cfg.norm_topk_prob = hf.get("norm_topk_prob", mt in ("mixtral", "phimoe"))
+        step = hf.get("decoder_sparse_step", 1)
+        mlp_only = set(hf.get("mlp_only_layers", []) or [])
+        cfg.moe_layers = [(i not in mlp_only) and ((i + 1) % step == 0) for i in range(cfg.num_layers)]
+        cfg.shared_expert_intermediate_size = hf.get("shared_expert_intermediate_size", 0)
+        cfg.shared_expert_gate = bool(cfg.shared_expert_intermediate_size)
+    g = tr.get("gemma")
+    if g:
+        cfg.embed_scale = math.sqrt(hidden)
+        cfg.norm_offset_one = True
+        cfg.hidden_act = "gelu_tanh"
+        qpas = hf.get("query_pre_attn_scalar")
+        if qpas:
+            cfg.attn_scale = qpas ** -0.5
+        if g >= 2:
+            cfg.post_norms = True
+            cfg.attn_logit_softcap = hf.get("attn_logit_softcapping") or 0.0
+            cfg.final_logit_softcap = hf.get("final_logit_softcapping") or 0.0
+            if not layer_types and sw:
+                if g == 2:
+                    cfg.layer_windows = [int(sw) if i % 2 == 0 else 0 for i in range(cfg.num_layers)]
+                else:
+                    pat = hf.get("sliding_window_pattern", 6)
+                    cfg.layer_windows = [0 if (i + 1) % pat == 0 else int(sw) for i in range(cfg.num_layers)]
+        if g == 3:
+            cfg.qk_norm = True
+            cfg.extra["rope_local_theta"] = hf.get("rope_local_base_freq", 10000.0)
+        cfg.tie_word_embeddings = hf.get("tie_word_embeddings", True)
+    if tr.get("gpt_oss"):
+        cfg.num_experts = hf.get("num_local_experts", 128)
+        cfg.num_experts_per_tok = hf.get("num_experts_per_tok", hf.get("experts_per_token", 4))
+        cfg.moe_intermediate_size = hf.get("intermediate_size")
+        cfg.router_mode = "topk_softmax"
+        cfg.router_bias = True
+        cfg.attention_bias = True
+        cfg.o_bias = True
+        cfg.mlp_bias = True
+        cfg.attention_sinks = True
+        cfg.hidden_act = "swiglu_oai"
+        cfg.extra["swiglu_limit"] = hf.get("swiglu_limit", 7.0)
+        if not layer_types:
+            cfg.layer_windows = [int(sw or 128) if i % 2 == 0 else 0 for i in range(cfg.num_layers)]
+    cfg.extra["fused_qkv"] = tr.get("fused_qkv", False)
+    cfg.extra["fused_gate_up"] = tr.get("fused_gate_up", False)
+    cfg.extra["mixtral_names"] = tr.get("mixtral_names", False)
+    if mt == "granite":
+        cfg.extra.update(embedding_multiplier=hf.get("embedding_multiplier", 1.0),
+                         residual_multiplier=hf.get("residual_multiplier", 1.0),
+                         logits_scaling=hf.get("logits_scaling", 1.0))
+        cfg.embed_scale = hf.get("embedding_multiplier", 1.0)
+        if hf.get("attention_multiplier"):
+            cfg.attn_scale = hf["attention_multiplier"]
+    return cfg
+
+
+def _act(a: str) -> str:
+    a = a.lower()
+    if a in ("gelu_pytorch_tanh", "gelu_tanh", "gelu_new", "gelu"):
+        return "gelu_tanh"
+    return "silu"

@@ -28,8 +28,7 @@ sz = C.c_size_t
 
 # name -> (restype, argtypes)
 _SIGS = {
-    "b200_gemm_bf16": (i32, [vp, i32, i32, i32, vp, i32, i32, vp, i32, vp, i32, vp, i32, vp, sz, vp, i32, i32, i32, vp]),
-    "b200_gemm_workspace_bytes": (sz, [i32, i32, i32, i32]),
+    "b200_gemm_bf16": (i32, [vp, i32, i32, i32, vp, i32, i32, vp, i32, vp, i32, vp, i32, i32, i32, vp]),
     "b200_gemm_num_splits": (i32, [i32, i32, i32, i32]),
     "b200_add_rmsnorm": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp]),
     "b200_qk_norm_rope_kv": (i32, [vp, i32, i32, vp, vp, vp, i32, i32, vp, vp, f32, vp, vp, vp, i32, vp, vp,

@@ -66,6 +66,26 @@ def test_gemm_batch_invariance():
         assert torch.equal(part, full[:m]), m
 
 
+def test_gemm_batch_invariance_across_prefill_sizes():
+    """Decode-sized and prefill-sized GEMMs give bit-identical rows (same split order)."""
+    torch.manual_seed(15)
+    K, N = 4096, 4096
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) * 0.02
+    x = torch.randn(700, K, device=DEV, dtype=torch.bfloat16)
+    big = ops.gemm(x, w)
+    for m in (1, 64, 128, 129, 300):
+        assert torch.equal(ops.gemm(x[:m].contiguous(), w), big[:m]), m
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 5, 8])
+def test_gemm_forced_splits(splits):
+    torch.manual_seed(16)
+    x = torch.randn(77, 2048, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(640, 2048, device=DEV, dtype=torch.bfloat16) * 0.05
+    y = ops.gemm(x, w, splits=splits)
+    assert _rel(y.cpu(), ref.gemm_ref(x.cpu(), w.cpu())) < 1e-2
+
+
 def test_add_rmsnorm():
     torch.manual_seed(6)
     x = torch.randn(17, 4096, device=DEV, dtype=torch.bfloat16)
