@@ -1,0 +1,103 @@
+"""ModelContainer: model + tokenizer + engine behind one object.
+
+Parity: MLXLMCommon/ModelContainer.swift:53-262 (``perform``, ``prepare``,
+``generate``, ``encode`` / ``decode``, chat template) and
+``loadModelContainer`` (ModelFactory.swift:310).
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from ..engine.engine import EngineConfig, EngineV2
+from ..engine.scheduler import SchedulerConfig
+from .generate import GenerateParameters, generate, generate_stream
+from .tokenizer import ByteTokenizer, as_tokenizer
+
+
+class ModelContainer:
+    def __init__(self, model, tokenizer=None, engine_config: EngineConfig | None = None, eos_token_ids=None,
+                 model_id: str = "local", hf_config: dict | None = None):
+        self.model = model
+        self.tokenizer = as_tokenizer(tokenizer) or ByteTokenizer(model.cfg.vocab_size)
+        eos = set(eos_token_ids or [])
+        if getattr(self.tokenizer, "eos_token_id", None) is not None:
+            eos.add(int(self.tokenizer.eos_token_id))
+        self.eos = eos
+        self.engine = EngineV2(model, self.tokenizer, engine_config or EngineConfig(), eos_token_ids=eos)
+        self.model_id = model_id
+        self.hf_config = hf_config or {}
+        self.lock = threading.RLock()
+
+    # ------------------------------------------------------------------ loading
+    @classmethod
+    def load(cls, path: str, device=None, dtype=torch.bfloat16, engine_config: EngineConfig | None = None,
+             tp=None):
+        from ..loader.load import eos_token_ids, load_model, load_tokenizer
+
+        device = device or ("cuda" if torch.cuda.is_available() else "cpu")
+        if device == "cpu":
+            dtype = torch.float32
+        model, hf = load_model(path, device, dtype, tp)
+        tok = load_tokenizer(path)
+        return cls(model, tok, engine_config, eos_token_ids(path, hf, tok), model_id=path, hf_config=hf)
+
+    @classmethod
+    def random(cls, cfg, device="cpu", dtype=torch.float32, seed=0, std=0.02, engine_config=None, tokenizer=None):
+        from ..models.decoder import DecoderLM
+
+        m = DecoderLM(cfg, device, dtype).init_random(seed, std=std)
+        return cls(m, tokenizer, engine_config or EngineConfig(scheduler=SchedulerConfig(),
+                                                               use_cuda_graphs=torch.device(device).type == "cuda"))
+
+    # ------------------------------------------------------------------ actor-style access
+    def perform(self, fn):
+        with self.lock:
+            return fn(self)
+
+    # ------------------------------------------------------------------ text <-> tokens
+    def encode(self, text: str) -> list[int]:
+        return self.tokenizer.encode(text)
+
+    def decode(self, ids) -> str:
+        return self.tokenizer.decode(ids)
+
+    def apply_chat_template(self, messages, tools=None, add_generation_prompt=True, **kw) -> list[int]:
+        out = self.tokenizer.apply_chat_template(messages, tools=tools, add_generation_prompt=add_generation_prompt,
+                                                 tokenize=True, **kw)
+        if isinstance(out, dict):
+            out = out["input_ids"]
+        return list(out)
+
+    def prepare(self, prompt=None, messages=None, tools=None) -> list[int]:
+        if messages is not None:
+            return self.apply_chat_template(messages, tools=tools)
+        if isinstance(prompt, str):
+            return self.encode(prompt)
+        return list(prompt)
+
+    # ------------------------------------------------------------------ generation
+    def generate(self, prompt=None, messages=None, params: GenerateParameters | None = None, tools=None):
+        toks = self.prepare(prompt, messages, tools)
+        return generate(self.engine, toks, params)
+
+    def stream(self, prompt=None, messages=None, params: GenerateParameters | None = None, tools=None):
+        toks = self.prepare(prompt, messages, tools)
+        yield from generate_stream(self.engine, toks, params)
+
+    # ------------------------------------------------------------------ embeddings
+    @torch.no_grad()
+    def embed(self, texts, pooling: str = "mean", normalize: bool = True) -> list[list[float]]:
+        """Sentence embeddings from the final hidden states (mean or last-token
+        pooling, L2-normalised), the decoder-embedder path of MLXEmbedders."""
+        out = []
+        for t in texts:
+            toks = self.encode(t) if isinstance(t, str) else list(t)
+            h = self.model.forward_dense(torch.tensor(toks, device=self.model.device), self.model.new_cache(),
+                                         return_hidden=True).float()
+            v = h.mean(0) if pooling == "mean" else h[-1]
+            if normalize:
+                v = v / v.norm().clamp(min=1e-12)
+            out.append(v.cpu().tolist())
+        return out

@@ -1,0 +1,179 @@
+"""Single-request generation API.
+
+Parity: MLXLMCommon/Evaluate.swift -
+``GenerateParameters`` (:127-327), ``TokenIterator`` (:905-1207, ``next`` :1159),
+``SpeculativeTokenIterator`` (:1239-1715), the ``generate`` family (:1927-2720)
+with ``Generation`` chunk / info events and completion info.
+
+``generate`` runs through the continuous-batching engine (one request is a
+batch of one; on a GPU this is the CUDA-graph decode path).
+``TokenIterator`` is the legacy dense-KV iterator of the reference (one
+sequence, concatenating cache), kept for parity and for CPU use; it honours
+``max_kv_size`` by keeping a rotating window of the most recent tokens.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from ..engine.types import FinishReason, Request, SamplingParams
+
+
+@dataclass
+class GenerateParameters:
+    max_tokens: int | None = 256
+    max_kv_size: int | None = None
+    temperature: float = 0.6
+    top_p: float = 1.0
+    top_k: int = 0
+    min_p: float = 0.0
+    repetition_penalty: float | None = None
+    repetition_context_size: int = 20
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
+    seed: int | None = None
+    logit_bias: dict = field(default_factory=dict)
+    top_logprobs: int = 0
+    prefill_step_size: int = 512
+    stop: list[str] = field(default_factory=list)
+    kv_bits: int | None = None  # quantized legacy KV (affine 4/8)
+    kv_group_size: int = 64
+
+    def sampling(self) -> SamplingParams:
+        return SamplingParams(temperature=self.temperature, top_p=self.top_p, top_k=self.top_k, min_p=self.min_p,
+                              repetition_penalty=self.repetition_penalty or 1.0,
+                              repetition_context_size=self.repetition_context_size,
+                              frequency_penalty=self.frequency_penalty, presence_penalty=self.presence_penalty,
+                              seed=self.seed, logit_bias=dict(self.logit_bias), top_logprobs=self.top_logprobs,
+                              logprobs=self.top_logprobs > 0)
+
+
+@dataclass
+class GenerateCompletionInfo:
+    prompt_tokens: int
+    generation_tokens: int
+    prompt_time: float
+    generate_time: float
+    stop_reason: str
+
+    @property
+    def prompt_tokens_per_second(self) -> float:
+        return self.prompt_tokens / self.prompt_time if self.prompt_time > 0 else 0.0
+
+    @property
+    def tokens_per_second(self) -> float:
+        return self.generation_tokens / self.generate_time if self.generate_time > 0 else 0.0
+
+
+@dataclass
+class Generation:
+    """A streamed generation event: a text chunk, a token, or the final info."""
+    chunk: str | None = None
+    token: int | None = None
+    info: GenerateCompletionInfo | None = None
+    tool_call: object = None
+    reasoning: str | None = None
+
+
+def generate_stream(engine, prompt_tokens: list[int], params: GenerateParameters | None = None, stop_tokens=(),
+                    token_constraint=None):
+    """Yield :class:`Generation` events for one request through the engine."""
+    params = params or GenerateParameters()
+    max_tokens = params.max_tokens or (engine.cfg.max_model_len - len(prompt_tokens))
+    req = Request(prompt_tokens=list(prompt_tokens), max_tokens=max_tokens, sampling=params.sampling(),
+                  stop_tokens=set(stop_tokens), stop_strings=list(params.stop), token_constraint=token_constraint)
+    t0 = time.perf_counter()
+    stream = engine.submit(req)
+    n = 0
+    t_first = None
+    reason = FinishReason.STOP
+    for ev in stream:
+        for tok in ev.tokens:
+            if t_first is None:
+                t_first = time.perf_counter()
+            n += 1
+            yield Generation(token=tok)
+        if ev.text:
+            yield Generation(chunk=ev.text)
+        if ev.finished:
+            reason = ev.finish_reason
+    t1 = time.perf_counter()
+    t_first = t_first or t1
+    yield Generation(info=GenerateCompletionInfo(len(prompt_tokens), n, t_first - t0, t1 - t_first,
+                                                 reason.value if reason else "stop"))
+
+
+def generate(engine, prompt_tokens: list[int], params: GenerateParameters | None = None, **kw):
+    """Blocking generation; returns (tokens, text, info)."""
+    toks, text, info = [], [], None
+    for g in generate_stream(engine, prompt_tokens, params, **kw):
+        if g.token is not None:
+            toks.append(g.token)
+        if g.chunk:
+            text.append(g.chunk)
+        if g.info is not None:
+            info = g.info
+    return toks, "".join(text), info
+
+
+class TokenIterator:
+    """Legacy single-sequence iterator over a dense KV cache.
+
+    Each ``next()`` returns the next token id. Prefill runs in
+    ``prefill_step_size`` chunks; with ``max_kv_size`` the cache keeps the
+    most recent ``max_kv_size`` tokens (rotating window, first tokens kept as
+    in the reference's RotatingKVCache)."""
+
+    def __init__(self, model, prompt_tokens, params: GenerateParameters | None = None, cache=None):
+        from ..engine.sampler import row_key
+        from ..ops import reference as ref
+
+        self.model = model
+        self.params = params or GenerateParameters()
+        self.cache = cache or model.new_cache()
+        self.tokens = list(prompt_tokens)
+        self.n_generated = 0
+        self._ref = ref
+        self._row_key = row_key
+        toks = torch.tensor(self.tokens, dtype=torch.int64, device=model.device)
+        step = self.params.prefill_step_size
+        logits = None
+        for i in range(0, len(toks), step):
+            logits = model.forward_dense(toks[i:i + step], self.cache)
+        self._logits = logits[-1]
+
+    def _sample(self, logits):
+        p = self.params
+        sp = p.sampling()
+        rep = self.tokens[-sp.repetition_context_size:] if sp.repetition_penalty != 1.0 else None
+        outs = self.tokens[len(self.tokens) - self.n_generated:] if (sp.frequency_penalty or sp.presence_penalty) else None
+        lg = self._ref.process_logits_ref(logits.float().cpu(), sp.logit_bias, rep, sp.repetition_penalty, outs,
+                                          sp.frequency_penalty, sp.presence_penalty)
+        key = self._ref.mix_key(sp.seed if sp.seed is not None else 0x5EED, 0)
+        return self._ref.sample_ref(lg, sp.temperature, sp.top_k, sp.top_p, sp.min_p, key, self.n_generated)
+
+    def __iter__(self):
+        return self
+
+    def __next__(self) -> int:
+        if self.params.max_tokens is not None and self.n_generated >= self.params.max_tokens:
+            raise StopIteration
+        tok = self._sample(self._logits)
+        self.tokens.append(tok)
+        self.n_generated += 1
+        if self.params.max_kv_size and self.cache.offset >= self.params.max_kv_size:
+            self._rotate()
+        self._logits = self.model.forward_dense(torch.tensor([tok], device=self.model.device), self.cache)[-1]
+        return tok
+
+    def _rotate(self, keep: int = 4):
+        """Drop the oldest tokens past the window, keeping the first `keep`."""
+        c = self.cache
+        limit = self.params.max_kv_size
+        for i in range(len(c.k)):
+            if c.k[i] is not None and c.k[i].shape[0] > limit - 1:
+                drop = c.k[i].shape[0] - (limit - 1)
+                c.k[i] = torch.cat([c.k[i][:keep], c.k[i][keep + drop:]], 0)
+                c.v[i] = torch.cat([c.v[i][:keep], c.v[i][keep + drop:]], 0)

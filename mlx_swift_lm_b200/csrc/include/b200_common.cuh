@@ -15,6 +15,8 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <utility>
+
 namespace b200 {
 
 // ---------------------------------------------------------------------------
@@ -298,6 +300,53 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Kernels are launched with programmatic
+// stream serialization, so the next kernel may start while this one runs.
+// Contract for every kernel of this library:
+//   * pdl_launch_dependents() at entry: lets the next kernel's CTAs be
+//     scheduled once all CTAs of this grid have started;
+//   * pdl_wait() before the first access to memory that an earlier kernel
+//     writes, or that a later kernel may still read (WAR). Work on data no
+//     kernel writes (weights, page tables set before the step) may precede it.
+// pdl_wait() returns once all prerequisite grids have completed and their
+// writes are visible; it is a no-op for launches without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+}  // namespace b200
+
+// Host: launch `kernel` with programmatic stream serialization (PDL) unless
+// disabled by b200_set_pdl(0). Optional cluster dimension along z.
+namespace b200 {
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                   int cluster_z, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_z > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = cluster_z;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 }  // namespace b200
 
 // Host accessor for this translation unit's status word: copies it out and

@@ -90,6 +90,8 @@ struct DecodeArgs {
 // D: head dim; G: query heads per KV head.
 template <int D, int G, typename KVT>
 __global__ void __launch_bounds__(128) paged_decode_part_kernel(DecodeArgs a) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   constexpr int DL = D / 8;                      // dims per lane
   constexpr int HW = G >= 4 ? G / 4 : 1;         // heads per warp
   constexpr int TS = G >= 4 ? 1 : 4 / G;         // warps sharing one head (split tokens)
@@ -274,9 +276,257 @@ __global__ void __launch_bounds__(128) paged_decode_part_kernel(DecodeArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Page-stream variant (the default). The 4 warps of a CTA form HG head groups
+// x PS page streams (HG * PS = 4). Each stream owns a private 2-stage ring of
+// K/V pages filled by the bulk-copy engine and consumes every PS-th page of
+// the partition; a warp holds HW = G / HG query heads, so shared memory is
+// read once per page per head group. Within a warp, 4 token groups of 8
+// lanes take 4 tokens of a page each and apply one online-softmax update per
+// 4 tokens.
+// ---------------------------------------------------------------------------
+template <int D, int G>
+struct StreamCfg {
+  static constexpr int DL = D / 8;
+  static constexpr int HG = (G * DL <= 64) ? 1 : (G * DL <= 128 ? 2 : 4);
+  static constexpr int HW = G / HG;
+  static constexpr int PS = 4 / HG;
+  static constexpr int NST = 2;
+};
+
+template <int D, int G, typename KVT>
+__global__ void __launch_bounds__(128) paged_decode_stream_kernel(DecodeArgs a) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
+  using C = StreamCfg<D, G>;
+  constexpr int DL = C::DL, HG = C::HG, HW = C::HW, PS = C::PS, NST = C::NST;
+  constexpr int kPageBytes = kPage * D * (int)sizeof(KVT);
+  static_assert(HW >= 1 && HG * HW == G, "head split");
+
+  extern __shared__ __align__(128) uint8_t ring_raw[];  // [PS][NST][2][kPageBytes]
+  __shared__ __align__(8) uint64_t full_bar[PS][NST];
+  __shared__ __align__(8) uint64_t empty_bar[PS][NST];
+  __shared__ float xw_m[4][HW], xw_l[4][HW];
+  __shared__ float xw_acc[4][HW][PS > 1 ? D : 1];
+
+  const int part = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tg = lane >> 3, sub = lane & 7;
+  const int hg = warp / PS, ps = warp % PS;
+  const int L = a.seq_lens[b];
+  const int start = a.window > 0 ? max(0, L - a.window) : 0;
+  if (L <= 0) return;
+  const int p_first = start / kPartTokens, p_last = (L - 1) / kPartTokens;
+  if (part < p_first || part > p_last) return;
+  const int lo = max(start, part * kPartTokens);
+  const int hi = min(L, (part + 1) * kPartTokens);
+  const int pg_lo = lo / kPage, pg_hi = (hi - 1) / kPage;
+  const int npages = pg_hi - pg_lo + 1;
+  const int my_pages = npages > ps ? (npages - ps + PS - 1) / PS : 0;  // pages ps, ps+PS, ...
+
+  float q[HW][DL];
+  const float kscale = a.k_scale ? a.k_scale[kvh] : 1.f;
+  const float qmul = (a.softcap > 0.f ? a.scale : a.scale * kLog2e) * kscale;
+#pragma unroll
+  for (int h = 0; h < HW; ++h) {
+    const __nv_bfloat16* qp = a.q + ((size_t)b * a.H + kvh * G + hg * HW + h) * D + sub * DL;
+#pragma unroll
+    for (int d = 0; d < DL; d += 8) {
+      uint4 u = *reinterpret_cast<const uint4*>(qp + d);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h2[j]);
+        q[h][d + 2 * j] = f.x * qmul;
+        q[h][d + 2 * j + 1] = f.y * qmul;
+      }
+    }
+  }
+  float m[HW], l[HW], acc[HW][DL];
+#pragma unroll
+  for (int h = 0; h < HW; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DL; ++d) acc[h][d] = 0.f;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PS; ++s)
+      for (int t = 0; t < NST; ++t) {
+        mbar_init(smem_u32(&full_bar[s][t]), 1);
+        mbar_init(smem_u32(&empty_bar[s][t]), HG);
+      }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const KVT* kc = reinterpret_cast<const KVT*>(a.k_cache);
+  const KVT* vc = reinterpret_cast<const KVT*>(a.v_cache);
+  const int* pt = a.page_table + (size_t)b * a.ld_pt;
+  uint8_t* my_ring = ring_raw + (size_t)ps * NST * 2 * kPageBytes;
+  const bool producer = (hg == 0 && lane == 0);
+  auto issue = [&](int i) {  // i-th page of this stream
+    const int s = i % NST;
+    int64_t page = pt[pg_lo + ps + i * PS];
+    if (page < 0 || page >= a.num_pages) {
+      set_status(kErrBounds);
+      page = 0;
+    }
+    const size_t off = ((size_t)page * a.KVH + kvh) * kPage * D;
+    const uint32_t fb = smem_u32(&full_bar[ps][s]);
+    mbar_arrive_expect_tx(fb, 2 * kPageBytes);
+    bulk_copy_g2s(smem_u32(my_ring + (s * 2 + 0) * kPageBytes), kc + off, kPageBytes, fb);
+    bulk_copy_g2s(smem_u32(my_ring + (s * 2 + 1) * kPageBytes), vc + off, kPageBytes, fb);
+  };
+  if (producer)
+    for (int i = 0; i < min(NST, my_pages); ++i) issue(i);
+
+  bool ok = true;
+  for (int i = 0; i < my_pages; ++i) {
+    const int s = i % NST;
+    if (ok && !mbar_wait(smem_u32(&full_bar[ps][s]), (i / NST) & 1, kErrAttnWait)) ok = false;
+    if (ok) {
+      const KVT* ks = reinterpret_cast<const KVT*>(my_ring + (s * 2 + 0) * kPageBytes);
+      const KVT* vs = reinterpret_cast<const KVT*>(my_ring + (s * 2 + 1) * kPageBytes);
+      const int pos0 = (pg_lo + ps + i * PS) * kPage;
+      float sc[4][HW];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int tok = tg + 4 * t;
+        const int pos = pos0 + tok;
+        const bool valid = pos >= lo && pos < hi;
+        float kv[DL];
+        load_kv_vec<KVT, DL>(ks + tok * D + sub * DL, kv);
+#pragma unroll
+        for (int h = 0; h < HW; ++h) {
+          float sd = 0.f;
+#pragma unroll
+          for (int d = 0; d < DL; ++d) sd += q[h][d] * kv[d];
+          sd += __shfl_xor_sync(0xffffffffu, sd, 1);
+          sd += __shfl_xor_sync(0xffffffffu, sd, 2);
+          sd += __shfl_xor_sync(0xffffffffu, sd, 4);
+          if (a.softcap > 0.f) sd = a.softcap * tanhf(sd / a.softcap) * kLog2e;
+          sc[t][h] = valid ? sd : -INFINITY;
+        }
+      }
+      float p[4][HW];
+#pragma unroll
+      for (int h = 0; h < HW; ++h) {
+        const float mx = fmaxf(fmaxf(sc[0][h], sc[1][h]), fmaxf(sc[2][h], sc[3][h]));
+        const float mn = fmaxf(m[h], mx);
+        if (mn == -INFINITY) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) p[t][h] = 0.f;
+          continue;
+        }
+        const float corr = exp2f(m[h] - mn);
+        float ps_ = 0.f;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          p[t][h] = exp2f(sc[t][h] - mn);
+          ps_ += p[t][h];
+        }
+        l[h] = l[h] * corr + ps_;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[h][d] *= corr;
+        m[h] = mn;
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float vv[DL];
+        load_kv_vec<KVT, DL>(vs + (tg + 4 * t) * D + sub * DL, vv);
+        const int pos = pos0 + tg + 4 * t;
+        if (pos < lo || pos >= hi) {  // stale slot of a partial page: never let it reach acc
+#pragma unroll
+          for (int d = 0; d < DL; ++d) vv[d] = 0.f;
+        }
+#pragma unroll
+        for (int h = 0; h < HW; ++h)
+#pragma unroll
+          for (int d = 0; d < DL; ++d) acc[h][d] += p[t][h] * vv[d];
+      }
+    }
+    // release the stage; the stream's producer refills it
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty_bar[ps][s]));
+    if (producer && ok && i + NST < my_pages) {
+      if (!mbar_wait(smem_u32(&empty_bar[ps][s]), (i / NST) & 1, kErrAttnWait)) ok = false;
+      else issue(i + NST);
+    }
+  }
+
+  // combine the 4 token groups of the warp (lanes with equal `sub`)
+#pragma unroll
+  for (int h = 0; h < HW; ++h) {
+#pragma unroll
+    for (int o = 8; o <= 16; o <<= 1) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m[h], o);
+      const float lo_ = __shfl_xor_sync(0xffffffffu, l[h], o);
+      const float mn = fmaxf(m[h], mo);
+      const float c0 = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - mn);
+      const float c1 = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+      l[h] = l[h] * c0 + lo_ * c1;
+#pragma unroll
+      for (int d = 0; d < DL; ++d) {
+        const float ao = __shfl_xor_sync(0xffffffffu, acc[h][d], o);
+        acc[h][d] = acc[h][d] * c0 + ao * c1;
+      }
+      m[h] = mn;
+    }
+  }
+  // combine the PS page streams of each head group, in stream order
+  if constexpr (PS > 1) {
+    if (tg == 0) {
+#pragma unroll
+      for (int h = 0; h < HW; ++h) {
+        if (sub == 0) {
+          xw_m[warp][h] = m[h];
+          xw_l[warp][h] = l[h];
+        }
+#pragma unroll
+        for (int d = 0; d < DL; ++d) xw_acc[warp][h][sub * DL + d] = acc[h][d];
+      }
+    }
+    __syncthreads();
+    if (ps != 0) return;
+    for (int w2 = warp + 1; w2 < warp + PS; ++w2) {
+#pragma unroll
+      for (int h = 0; h < HW; ++h) {
+        const float mo = xw_m[w2][h], lo_ = xw_l[w2][h];
+        const float mn = fmaxf(m[h], mo);
+        const float c0 = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - mn);
+        const float c1 = (mo == -INFINITY) ? 0.f : exp2f(mo - mn);
+        l[h] = l[h] * c0 + lo_ * c1;
+#pragma unroll
+        for (int d = 0; d < DL; ++d) acc[h][d] = acc[h][d] * c0 + xw_acc[w2][h][sub * DL + d] * c1;
+        m[h] = mn;
+      }
+    }
+  }
+  if (tg != 0) return;
+  const float vscale = a.v_scale ? a.v_scale[kvh] : 1.f;
+#pragma unroll
+  for (int h = 0; h < HW; ++h) {
+    const int head = kvh * G + hg * HW + h;
+    const size_t pidx = ((size_t)b * a.H + head) * a.max_parts + part;
+    float* dst = a.part_acc + pidx * D + sub * DL;
+#pragma unroll
+    for (int d = 0; d < DL; d += 4)
+      *reinterpret_cast<float4*>(dst + d) =
+          make_float4(acc[h][d] * vscale, acc[h][d + 1] * vscale, acc[h][d + 2] * vscale, acc[h][d + 3] * vscale);
+    if (sub == 0) {
+      a.part_ml[pidx * 2 + 0] = m[h];
+      a.part_ml[pidx * 2 + 1] = l[h];
+    }
+  }
+}
+
 // One warp per (row, head); 4 warps per CTA. Writes bf16 output.
 template <int D>
 __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeArgs a, int B) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   constexpr int DL = D / 32 > 0 ? D / 32 : 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gi = blockIdx.x * 4 + warp;
@@ -321,17 +571,18 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(DecodeArgs a, i
 
 template <int D, int G, typename KVT>
 static int launch_decode(const DecodeArgs& a, int B, cudaStream_t st) {
-  constexpr int smem = kStages * 2 * kPage * D * (int)sizeof(KVT);
+  using C = StreamCfg<D, G>;
+  constexpr int smem = C::PS * C::NST * 2 * kPage * D * (int)sizeof(KVT);
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_part_kernel<D, G, KVT>,
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_stream_kernel<D, G, KVT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     configured = true;
   }
   dim3 grid(a.max_parts, a.KVH, B);
-  paged_decode_part_kernel<D, G, KVT><<<grid, 128, smem, st>>>(a);
-  paged_decode_merge_kernel<D><<<(B * a.H + 3) / 4, 128, 0, st>>>(a, B);
+b200::launch_k(  paged_decode_stream_kernel<D, G, KVT>, dim3(grid), dim3(128), smem, st, 1, a);
+b200::launch_k(  paged_decode_merge_kernel<D>, dim3((B * a.H + 3) / 4), dim3(128), 0, st, 1, a, B);
   return (int)cudaGetLastError();
 }
 
@@ -354,6 +605,30 @@ using namespace b200;
 extern "C" {
 
 int b200_paged_decode_part_tokens() { return kPartTokens; }
+
+// Merge pass alone (used after the tensor-core partition pass).
+int b200_paged_decode_merge(const float* part_acc, const float* part_ml, const int* seq_lens, const float* sinks,
+                            void* out, int B, int H, int D, int max_parts, int window, cudaStream_t st) {
+  if (B <= 0) return 0;
+  DecodeArgs a = {};
+  a.seq_lens = seq_lens;
+  a.sinks = sinks;
+  a.part_acc = const_cast<float*>(part_acc);
+  a.part_ml = const_cast<float*>(part_ml);
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.H = H;
+  a.max_parts = max_parts;
+  a.window = window;
+  cudaError_t e;
+  const dim3 grid((B * H + 3) / 4);
+  switch (D) {
+    case 64: e = launch_k(paged_decode_merge_kernel<64>, grid, dim3(128), 0, st, 1, a, B); break;
+    case 128: e = launch_k(paged_decode_merge_kernel<128>, grid, dim3(128), 0, st, 1, a, B); break;
+    case 256: e = launch_k(paged_decode_merge_kernel<256>, grid, dim3(128), 0, st, 1, a, B); break;
+    default: return -1;
+  }
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
 
 // Scratch needed: part_acc B*H*max_parts*D floats, part_ml B*H*max_parts*2 floats.
 int b200_paged_decode(const void* q, const void* k_cache, const void* v_cache, int kv_fp8, const float* k_scale,

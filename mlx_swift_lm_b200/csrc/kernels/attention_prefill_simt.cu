@@ -33,6 +33,8 @@ struct PrefillArgs {
 
 template <int D, int G>
 __global__ void __launch_bounds__(128) paged_prefill_simt_kernel(PrefillArgs a) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   constexpr int QT = 128 / G;  // queries per tile
   __shared__ __align__(16) __nv_bfloat16 ks[16][D];
   __shared__ __align__(16) __nv_bfloat16 vs[16][D];
@@ -130,11 +132,11 @@ template <int D>
 static int dispatch_prefill(const PrefillArgs& a, int n_tiles, int G, cudaStream_t st) {
   dim3 grid(n_tiles, a.KVH);
   switch (G) {
-    case 1: paged_prefill_simt_kernel<D, 1><<<grid, 128, 0, st>>>(a); break;
-    case 2: paged_prefill_simt_kernel<D, 2><<<grid, 128, 0, st>>>(a); break;
-    case 4: paged_prefill_simt_kernel<D, 4><<<grid, 128, 0, st>>>(a); break;
-    case 8: paged_prefill_simt_kernel<D, 8><<<grid, 128, 0, st>>>(a); break;
-    case 16: paged_prefill_simt_kernel<D, 16><<<grid, 128, 0, st>>>(a); break;
+    case 1: launch_k(paged_prefill_simt_kernel<D, 1>, grid, dim3(128), 0, st, 1, a); break;
+    case 2: launch_k(paged_prefill_simt_kernel<D, 2>, grid, dim3(128), 0, st, 1, a); break;
+    case 4: launch_k(paged_prefill_simt_kernel<D, 4>, grid, dim3(128), 0, st, 1, a); break;
+    case 8: launch_k(paged_prefill_simt_kernel<D, 8>, grid, dim3(128), 0, st, 1, a); break;
+    case 16: launch_k(paged_prefill_simt_kernel<D, 16>, grid, dim3(128), 0, st, 1, a); break;
     default: return -1;
   }
   return (int)cudaGetLastError();

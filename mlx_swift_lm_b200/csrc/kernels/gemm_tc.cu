@@ -79,15 +79,12 @@ struct GemmSmem {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+// Generic address of the same shared-memory variable in cluster CTA `rank`
+// (distributed shared memory); plain loads through it batch and overlap.
+__device__ __forceinline__ const float* map_cluster_rank(const float* p, uint32_t rank) {
+  uint64_t r;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+  return reinterpret_cast<const float*>(r);
 }
 
 template <int BN, int STAGES>
@@ -111,6 +108,7 @@ __global__ void __launch_bounds__(128, 1)
   const int kb_end = min(args.kb_total, kb_begin + args.kb_per_split);
   const int nkb = kb_end - kb_begin;
 
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
@@ -134,8 +132,20 @@ __global__ void __launch_bounds__(128, 1)
     // ---------------- TMA producer ----------------
     const uint64_t pol_w = l2_policy_evict_first();
     const uint64_t pol_x = l2_policy_evict_last();
-    int issued = 0;
-    for (int i = 0; i < nkb; ++i) {
+    // Weights are written by no kernel: the first STAGES weight tiles are
+    // requested before waiting on the previous kernel (PDL), so their HBM
+    // latency overlaps the predecessor's tail.
+    const int pre = min(STAGES, nkb);
+    for (int i = 0; i < pre; ++i) {
+      const uint32_t a = sbase + i * S::kStageBytes;
+      mbar_arrive_expect_tx(bar_full + 8 * i, S::kStageBytes);
+      tma_load_2d(a, &tmW, bar_full + 8 * i, (kb_begin + i) * 64, n0, pol_w);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d(sbase + i * S::kStageBytes + S::kABytes, &tmX, bar_full + 8 * i, (kb_begin + i) * 64, m0, pol_x);
+    int issued = pre;
+    for (int i = pre; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
       const uint32_t a = sbase + s * S::kStageBytes;
@@ -168,6 +178,9 @@ __global__ void __launch_bounds__(128, 1)
   }
   __syncwarp();
 
+  // every thread that touches global memory below orders itself after the
+  // previous kernel (the producer thread already did)
+  if (!(warp == 0 && lane == 0)) pdl_wait();
   // ---------------- drain TMEM into this CTA's fp32 partial [BN][128] ----------------
   const bool acc_ok = __syncthreads_and(mbar_wait(bar_accum, 0, kErrTmemWait) ? 1 : 0) != 0;
   tc_fence_after();
@@ -193,17 +206,20 @@ __global__ void __launch_bounds__(128, 1)
   const int js = (BN + ks - 1) / ks;
   const int j_lo = z * js;
   const int j_hi = min(BN, min(j_lo + js, args.M - m0));
-  const uint32_t part_addr = smem_u32(part);
-  uint32_t rbase[8];
+  const float* rp[8];
 #pragma unroll
-  for (int q = 0; q < 8; ++q) rbase[q] = q < ks ? (ks > 1 ? mapa_shared(part_addr, q) : part_addr) : 0u;
+  for (int q = 0; q < 8; ++q) rp[q] = (q < ks) ? (ks > 1 ? map_cluster_rank(part, q) : part) : part;
+  // Sum of the split partials in split order; all loads of a group are issued
+  // before the adds so their DSMEM latencies overlap.
   auto reduce_at = [&](int j, int row) -> float {
-    if (ks == 1) return part[j * 128 + row];
-    const uint32_t off = (uint32_t)((j * 128 + row) * 4);
-    float acc = ld_dsmem_f32(rbase[0] + off);
+    const int off = j * 128 + row;
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = (q < ks) ? rp[q][off] : 0.f;
+    float acc = v[0];
 #pragma unroll
     for (int q = 1; q < 8; ++q)
-      if (q < ks) acc += ld_dsmem_f32(rbase[q] + off);
+      if (q < ks) acc += v[q];
     return acc;
   };
   const bool glu = args.epi == kEpiSwiGLU || args.epi == kEpiGeGLU || args.epi == kEpiSwiGLUOAI;
@@ -214,6 +230,7 @@ __global__ void __launch_bounds__(128, 1)
     const float bg = args.bias ? bf2f(args.bias[n0 + row]) : 0.f;
     const float bu = args.bias ? bf2f(args.bias[n0 + 64 + row]) : 0.f;
     if (f < (args.N >> 1)) {
+#pragma unroll 2
       for (int j = j_lo + par; j < j_hi; j += 2) {
         // round the gate and up projections to bf16 first, as an unfused bf16
         // model would, then apply the activation in fp32
@@ -226,6 +243,7 @@ __global__ void __launch_bounds__(128, 1)
     const int n = n0 + r;
     if (n < args.N) {
       const float bb = args.bias ? bf2f(args.bias[n]) : 0.f;
+#pragma unroll 4
       for (int j = j_lo; j < j_hi; ++j) {
         const float v = reduce_at(j, r) + bb;
         const size_t m = (size_t)(m0 + j);
@@ -328,19 +346,8 @@ static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmA
     if (e != cudaSuccess) return (int)e;
     configured = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles_n, tiles_m, a.ksplit);
-  cfg.blockDim = dim3(128, 1, 1);
-  cfg.dynamicSmemBytes = S::kTotal;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = a.ksplit;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel<BN, STAGES>, tw, tx, a);
+  cudaError_t e = launch_k(gemm_bf16_tc_kernel<BN, STAGES>, dim3(tiles_n, tiles_m, a.ksplit), dim3(128, 1, 1),
+                           S::kTotal, st, a.ksplit, tw, tx, a);
   if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
 }

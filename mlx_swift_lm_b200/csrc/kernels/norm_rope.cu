@@ -18,6 +18,8 @@ namespace b200 {
 __global__ void add_rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H,
                                    int ldx, int ldd, int ldo, float eps, int w_offset_one) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   extern __shared__ float rbuf[];  // H floats
   __shared__ float red[32];
   const int row = blockIdx.x;
@@ -77,6 +79,8 @@ __global__ void qk_norm_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, in
                                        KVT* __restrict__ v_cache, const float* __restrict__ k_scale,
                                        const float* __restrict__ v_scale, int H, int KVH, int D, int64_t num_slots,
                                        __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int pos = positions[t];
@@ -184,6 +188,8 @@ __global__ void qk_norm_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, in
 
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  __nv_bfloat16* __restrict__ out, int H, int64_t vocab, float scale) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   const int t = blockIdx.x;
   int64_t id = ids[t];
   if (id < 0 || id >= vocab) {
@@ -203,6 +209,8 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
 // out = silu(gate) * up for a [T, 2*F] tensor laid out [gate | up].
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int F,
                                 int ld_in, int ld_out) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   const int t = blockIdx.y;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= F) return;
@@ -223,7 +231,7 @@ int b200_add_rmsnorm(void* x, const void* delta, const void* w, void* out, int T
   if (H % 8) return -1;
   int threads = ((H / 8 + 31) / 32) * 32;
   threads = threads > 1024 ? 1024 : threads;
-  add_rmsnorm_kernel<<<T, threads, H * sizeof(float), st>>>(
+b200::launch_k(  add_rmsnorm_kernel, dim3(T), dim3(threads), H * sizeof(float), st, 1, 
       reinterpret_cast<__nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(delta),
       reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<__nv_bfloat16*>(out), H, ldx, ldd, ldo, eps,
       w_offset_one);
@@ -241,14 +249,14 @@ int b200_qk_norm_rope_kv(const void* qkv, int T, int ld_qkv, const int* position
   const int threads = 256;
   const size_t smem = (threads / 32) * D * sizeof(float);
   if (kv_fp8) {
-    qk_norm_rope_kv_kernel<uint8_t><<<T, threads, smem, st>>>(
+b200::launch_k(    qk_norm_rope_kv_kernel<uint8_t>, dim3(T), dim3(threads), smem, st, 1, 
         reinterpret_cast<const __nv_bfloat16*>(qkv), ld_qkv, positions, slots, cos_sin, rot_dim, interleaved,
         reinterpret_cast<const __nv_bfloat16*>(qw), reinterpret_cast<const __nv_bfloat16*>(kw), eps,
         reinterpret_cast<__nv_bfloat16*>(q_out), reinterpret_cast<uint8_t*>(k_cache),
         reinterpret_cast<uint8_t*>(v_cache), k_scale, v_scale, H, KVH, D, num_slots,
         reinterpret_cast<__nv_bfloat16*>(k_out), reinterpret_cast<__nv_bfloat16*>(v_out));
   } else {
-    qk_norm_rope_kv_kernel<__nv_bfloat16><<<T, threads, smem, st>>>(
+b200::launch_k(    qk_norm_rope_kv_kernel<__nv_bfloat16>, dim3(T), dim3(threads), smem, st, 1, 
         reinterpret_cast<const __nv_bfloat16*>(qkv), ld_qkv, positions, slots, cos_sin, rot_dim, interleaved,
         reinterpret_cast<const __nv_bfloat16*>(qw), reinterpret_cast<const __nv_bfloat16*>(kw), eps,
         reinterpret_cast<__nv_bfloat16*>(q_out), reinterpret_cast<__nv_bfloat16*>(k_cache),
@@ -262,7 +270,7 @@ int b200_embedding(const int* ids, const void* table, void* out, int T, int H, i
                    cudaStream_t st) {
   if (T <= 0) return 0;
   if (H % 8) return -1;
-  embedding_kernel<<<T, 256, 0, st>>>(ids, reinterpret_cast<const __nv_bfloat16*>(table),
+b200::launch_k(  embedding_kernel, dim3(T), dim3(256), 0, st, 1, ids, reinterpret_cast<const __nv_bfloat16*>(table),
                                       reinterpret_cast<__nv_bfloat16*>(out), H, vocab, scale);
   return (int)cudaGetLastError();
 }
@@ -270,7 +278,7 @@ int b200_embedding(const int* ids, const void* table, void* out, int T, int H, i
 int b200_silu_mul(const void* gu, void* out, int T, int F, int ld_in, int ld_out, cudaStream_t st) {
   if (T <= 0) return 0;
   dim3 grid((F + 255) / 256, T);
-  silu_mul_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(gu),
+b200::launch_k(  silu_mul_kernel, dim3(grid), dim3(256), 0, st, 1, reinterpret_cast<const __nv_bfloat16*>(gu),
                                         reinterpret_cast<__nv_bfloat16*>(out), F, ld_in, ld_out);
   return (int)cudaGetLastError();
 }

@@ -79,6 +79,8 @@ struct ProcessArgs {
 };
 
 __global__ void __launch_bounds__(kThreads) logits_process_kernel(ProcessArgs a) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   extern __shared__ uint32_t seen[];  // V bits
   const int b = blockIdx.x;
   float* lg = a.logits + (size_t)b * a.ld;
@@ -195,6 +197,8 @@ __device__ __forceinline__ void block_argmax(float& v, int& idx, float* sv, int*
 }
 
 __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   __shared__ unsigned long long hist[256];
@@ -350,6 +354,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
 // Greedy argmax only (the all-greedy fast path).
 __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restrict__ logits, int64_t ld, int V,
                                                           int* out, int* out2) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int b = blockIdx.x;
@@ -382,6 +388,8 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
 __global__ void __launch_bounds__(kThreads) logprobs_kernel(const float* __restrict__ logits, int64_t ld, int V,
                                                             const int* tokens, int n_top, float* out_lp,
                                                             int* top_ids, float* top_lp) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   __shared__ float red[32];
@@ -442,7 +450,7 @@ int b200_logits_process(float* logits, int64_t ld, int B, int V, const int* bias
     configured = true;
   }
   if (smem > 200 * 1024) return -1;
-  logits_process_kernel<<<B, kThreads, smem, st>>>(a);
+b200::launch_k(  logits_process_kernel, dim3(B), dim3(kThreads), smem, st, 1, a);
   return (int)cudaGetLastError();
 }
 
@@ -451,20 +459,20 @@ int b200_sample(const float* logits, int64_t ld, int B, int V, const float* temp
                 int* out_tokens2, float* out_logit, cudaStream_t st) {
   if (B <= 0) return 0;
   SampleArgs a{logits, ld, V, temperature, top_k, top_p, min_p, keys, steps, out_tokens, out_tokens2, out_logit};
-  sample_kernel<<<B, kThreads, 0, st>>>(a);
+b200::launch_k(  sample_kernel, dim3(B), dim3(kThreads), 0, st, 1, a);
   return (int)cudaGetLastError();
 }
 
 int b200_argmax(const float* logits, int64_t ld, int B, int V, int* out, int* out2, cudaStream_t st) {
   if (B <= 0) return 0;
-  argmax_kernel<<<B, kThreads, 0, st>>>(logits, ld, V, out, out2);
+b200::launch_k(  argmax_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, out, out2);
   return (int)cudaGetLastError();
 }
 
 int b200_logprobs(const float* logits, int64_t ld, int B, int V, const int* tokens, int n_top, float* out_lp,
                   int* top_ids, float* top_lp, cudaStream_t st) {
   if (B <= 0) return 0;
-  logprobs_kernel<<<B, kThreads, 0, st>>>(logits, ld, V, tokens, n_top, out_lp, top_ids, top_lp);
+b200::launch_k(  logprobs_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, tokens, n_top, out_lp, top_ids, top_lp);
   return (int)cudaGetLastError();
 }
 

@@ -162,6 +162,17 @@ class Scheduler:
             self.running.remove(st)
         self.waiting.insert(0, st)
 
+    def _ensure(self, st: RequestState, total_tokens: int) -> bool:
+        """Grow a row's pages; on pool exhaustion first evict unreferenced
+        prefix-cache blocks, then report failure (the caller may preempt)."""
+        if st.seq.ensure(total_tokens):
+            return True
+        if self.prefix_cache is not None:
+            need = st.seq.pages_needed(total_tokens) - self.cache.pool.num_free
+            if need > 0 and self.prefix_cache.evict(need) > 0:
+                return st.seq.ensure(total_tokens)
+        return False
+
     # ------------------------------------------------------------------ plan
     def plan(self) -> StepPlan:
         cfg = self.cfg
@@ -178,8 +189,10 @@ class Scheduler:
                 break
             if st.num_output >= st.req.max_tokens:
                 continue  # its last token is still in flight; finalize ends it
-            while not st.seq.ensure(st.num_computed + 1):
-                victim = self._victim(scheduled | {st})
+            while not self._ensure(st, st.num_computed + 1):
+                # lowest priority, then youngest, among rows not yet scheduled this
+                # step - possibly the row itself
+                victim = self._victim(scheduled)
                 if victim is None:
                     victim = st
                 self.preempt(victim)
@@ -205,7 +218,7 @@ class Scheduler:
             if st.status != Status.RUNNING:
                 continue
             n = min(st.remaining, cfg.prefill_chunk_size, pbudget)
-            if not st.seq.ensure(st.num_computed + n):
+            if not self._ensure(st, st.num_computed + n):
                 continue
             rows.append(ScheduledRow(st, st.num_computed, n, False, st.num_computed + n == len(st.all_tokens)))
             scheduled.add(st)
@@ -223,7 +236,7 @@ class Scheduler:
                 n = min(st.remaining, cfg.prefill_chunk_size, pbudget)
                 if n <= 0:
                     continue
-                if not st.seq.ensure(st.num_computed + n):
+                if not self._ensure(st, st.num_computed + n):
                     if st.seq.num_tokens and st.seq.shared_prefix_pages:
                         st.seq.release()
                     break

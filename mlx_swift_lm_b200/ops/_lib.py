@@ -48,10 +48,15 @@ _SIGS = {
     "b200_logprobs": (i32, [vp, i64, i32, i32, vp, i32, vp, vp, vp, vp]),
     "b200_philox_u32": (C.c_uint32, [u64, u64, C.c_uint32]),
     "b200_gather_tokens": (i32, [vp, vp, vp, vp, i32, vp]),
+    "b200_paged_decode_mma_part": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, f32,
+                                         i64, vp]),
+    "b200_paged_decode_merge": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "b200_set_pdl": (None, [i32]),
+    "b200_get_pdl": (i32, []),
 }
 
 # status accessors exported per translation unit
-_STATUS_TAGS = ["gemm", "norm", "attn_decode", "attn_prefill_simt", "sampling", "misc"]
+_STATUS_TAGS = ["gemm", "norm", "attn_decode", "attn_prefill_simt", "sampling", "misc", "attn_decode_mma"]
 
 
 class KernelLibraryMissing(RuntimeError):

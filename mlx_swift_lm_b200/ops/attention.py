@@ -9,6 +9,8 @@ from . import _lib
 from . import reference as ref
 
 PART_TOKENS = ref.DECODE_PART_TOKENS
+# bf16 pages use the tensor-core partition pass; set [0] = False for the CUDA-core kernel
+USE_MMA_DECODE = [True]
 
 
 class _Scratch:
@@ -54,7 +56,20 @@ def paged_decode(q, k_cache, v_cache, page_table, seq_lens, scale, window=0, sin
     acc = SCRATCH.get(q.device, "dec_acc", B * H * max_parts * D)
     ml = SCRATCH.get(q.device, "dec_ml", B * H * max_parts * 2)
     kv_fp8 = k_cache.dtype == torch.float8_e4m3fn
-    rc = _lib.lib().b200_paged_decode(
+    L = _lib.lib()
+    if not kv_fp8 and D in (64, 128, 256) and H // KVH <= (16 if D < 256 else 8) and USE_MMA_DECODE[0]:
+        st = _lib.stream_ptr(q.device)
+        rc = L.b200_paged_decode_mma_part(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), page_table.data_ptr(),
+                                          page_table.stride(0), seq_lens.data_ptr(), acc.data_ptr(), ml.data_ptr(), B,
+                                          H, KVH, D, max_parts, int(window), float(scale), float(softcap),
+                                          k_cache.shape[0], st)
+        _lib.check(rc, "paged_decode_mma_part")
+        rc = L.b200_paged_decode_merge(acc.data_ptr(), ml.data_ptr(), seq_lens.data_ptr(), _lib.ptr(sinks),
+                                       out.data_ptr(), B, H, D, max_parts, int(window), st)
+        _lib.check(rc, "paged_decode_merge")
+        _lib.count(2)
+        return out
+    rc = L.b200_paged_decode(
         q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), 1 if kv_fp8 else 0, _lib.ptr(k_scale),
         _lib.ptr(v_scale), page_table.data_ptr(), page_table.stride(0), seq_lens.data_ptr(), _lib.ptr(sinks),
         out.data_ptr(), acc.data_ptr(), ml.data_ptr(), B, H, KVH, D, max_parts, int(window), float(scale),

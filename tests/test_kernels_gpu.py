@@ -271,3 +271,23 @@ def test_status_words_clean():
 
     st = _lib.read_status()
     assert all(v == 0 for v in st.values()), st
+
+
+@pytest.mark.parametrize("H,KVH,D", [(32, 8, 128), (64, 8, 64)])
+def test_paged_decode_cuda_core_path(H, KVH, D):
+    """The CUDA-core partition kernel (fp8 pages use it) stays correct for bf16 too."""
+    from mlx_swift_lm_b200.ops import attention as att
+
+    torch.manual_seed(14)
+    lens = [5, 300, 1030]
+    P = sum((l + 15) // 16 for l in lens) + 2
+    kc, vc, pt = _make_paged(3, lens, KVH, D, P)
+    q = torch.randn(3, H, D, dtype=torch.bfloat16)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    r = ref.paged_decode_ref(q, kc, vc, pt, sl, D ** -0.5, 0, None)
+    att.USE_MMA_DECODE[0] = False
+    try:
+        y = ops.paged_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), pt.to(DEV), sl.to(DEV), D ** -0.5)
+    finally:
+        att.USE_MMA_DECODE[0] = True
+    assert _rel(y.cpu(), r) < 1e-2
