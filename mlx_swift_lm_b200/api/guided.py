@@ -1,0 +1,288 @@
+"""Guided (grammar-constrained) generation.
+
+Front ends lower to the native engine's regular-expression dialect
+(csrc/host/grammar.cpp, a byte-level lazily determinised automaton with
+per-state token masks):
+  * :func:`json_schema_to_regex` - objects (properties in declaration order,
+    required / optional), arrays (min/max items), strings (enum, const,
+    pattern, min/max length), integers, numbers, booleans, null, anyOf / oneOf,
+    ``$ref`` to ``$defs``; recursion and free-form JSON are unrolled to a
+    bounded nesting depth;
+  * :func:`ebnf_to_regex` - GBNF-style rules ``name ::= alternatives`` with
+    quoted literals, character classes, grouping and ``* + ?``; recursive rules
+    are unrolled to a bounded depth;
+  * regex directly.
+:class:`GrammarConstraint` is the per-request token constraint the engine's
+sampler consumes (allowed-token mask per step, commit, rollback,
+termination). Parity: MLXGuidedGeneration/GuidedGenerationLoop.swift:21-611,
+XGrammarBridge.swift (``GrammarConstraint`` :184, ``computeMask`` :515,
+``commitToken`` :560, ``rollback`` :698).
+"""
+from __future__ import annotations
+
+import json
+import os
+import re
+import sys
+
+import numpy as np
+
+_LIBDIR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "_lib")
+if _LIBDIR not in sys.path:
+    sys.path.insert(0, _LIBDIR)
+import _b200host  # noqa: E402
+
+WS = r"[ \n]?"  # whitespace policy between JSON tokens
+STRING_CHAR = r'([^"\\\x00-\x1f]|\\["\\/bfnrt])'
+JSON_STRING = '"' + STRING_CHAR + '*"'
+JSON_INT = r"-?(0|[1-9][0-9]{0,15})"
+JSON_NUM = JSON_INT + r"(\.[0-9]{1,16})?([eE][+-]?[0-9]{1,3})?"
+JSON_BOOL = r"(true|false)"
+JSON_NULL = r"null"
+
+
+def _esc(s: str) -> str:
+    out = []
+    for ch in s:
+        if ch in r"\.^$|?*+()[]{}":
+            out.append("\\" + ch)
+        elif ch == "\n":
+            out.append("\\n")
+        else:
+            out.append(ch)
+    return "".join(out)
+
+
+def _json_literal(v) -> str:
+    return _esc(json.dumps(v))
+
+
+def any_json(depth: int = 2) -> str:
+    scalar = f"({JSON_STRING}|{JSON_NUM}|{JSON_BOOL}|{JSON_NULL})"
+    if depth <= 0:
+        return scalar
+    inner = any_json(depth - 1)
+    arr = rf"\[{WS}({inner}({WS},{WS}{inner}){{0,16}})?{WS}\]"
+    obj = rf"\{{{WS}({JSON_STRING}{WS}:{WS}{inner}({WS},{WS}{JSON_STRING}{WS}:{WS}{inner}){{0,16}})?{WS}\}}"
+    return f"({scalar}|{arr}|{obj})"
+
+
+def json_schema_to_regex(schema, defs=None, depth: int = 4) -> str:
+    if isinstance(schema, str):
+        schema = json.loads(schema)
+    defs = defs if defs is not None else schema.get("$defs", schema.get("definitions", {}))
+    if depth < 0:
+        return any_json(0)
+    if "$ref" in schema:
+        name = schema["$ref"].split("/")[-1]
+        return json_schema_to_regex(defs[name], defs, depth - 1)
+    if "const" in schema:
+        return _json_literal(schema["const"])
+    if "enum" in schema:
+        return "(" + "|".join(_json_literal(v) for v in schema["enum"]) + ")"
+    for key in ("anyOf", "oneOf"):
+        if key in schema:
+            return "(" + "|".join(json_schema_to_regex(s, defs, depth) for s in schema[key]) + ")"
+    t = schema.get("type")
+    if isinstance(t, list):
+        return "(" + "|".join(json_schema_to_regex({**schema, "type": x}, defs, depth) for x in t) + ")"
+    if t == "object" or (t is None and "properties" in schema):
+        props = schema.get("properties", {})
+        if not props:
+            return any_json(min(depth, 2)) if t is None else rf"\{{{WS}({JSON_STRING}{WS}:{WS}{any_json(1)}" \
+                rf"({WS},{WS}{JSON_STRING}{WS}:{WS}{any_json(1)}){{0,16}})?{WS}\}}"
+        required = set(schema.get("required", list(props)))
+        parts = []
+        for name, sub in props.items():
+            kv = f'"{_esc(name)}"{WS}:{WS}{json_schema_to_regex(sub, defs, depth - 1)}'
+            parts.append((kv, name in required))
+        # properties in declaration order; a comma precedes every emitted property but the first
+        body = ""
+        first_emitted_possible = True
+        for i, (kv, req) in enumerate(parts):
+            if i == 0:
+                piece = kv
+            else:
+                piece = f"{WS},{WS}{kv}" if not first_emitted_possible else f"({WS},{WS})?{kv}"
+            body += piece if req else f"({piece})?"
+            if req:
+                first_emitted_possible = False
+        return rf"\{{{WS}{body}{WS}\}}"
+    if t == "array":
+        item = json_schema_to_regex(schema.get("items", {}), defs, depth - 1)
+        lo = int(schema.get("minItems", 0))
+        hi = schema.get("maxItems")
+        if hi is None:
+            rest = f"({WS},{WS}{item})*"
+        else:
+            rest = f"({WS},{WS}{item}){{0,{max(0, int(hi) - 1)}}}"
+        if lo > 0:
+            rest_min = "".join(f"{WS},{WS}{item}" for _ in range(lo - 1))
+            tail = f"({WS},{WS}{item})*" if hi is None else f"({WS},{WS}{item}){{0,{max(0, int(hi) - lo)}}}"
+            return rf"\[{WS}{item}{rest_min}{tail}{WS}\]"
+        return rf"\[{WS}({item}{rest})?{WS}\]"
+    if t == "string":
+        if "pattern" in schema:
+            return '"' + schema["pattern"].lstrip("^").rstrip("$") + '"'
+        fmt = schema.get("format")
+        if fmt == "date":
+            return r'"[0-9]{4}-[0-9]{2}-[0-9]{2}"'
+        lo, hi = schema.get("minLength"), schema.get("maxLength")
+        if lo is not None or hi is not None:
+            return '"' + STRING_CHAR + "{" + f"{int(lo or 0)},{'' if hi is None else int(hi)}" + '}"'
+        return JSON_STRING
+    if t == "integer":
+        return JSON_INT
+    if t == "number":
+        return JSON_NUM
+    if t == "boolean":
+        return JSON_BOOL
+    if t == "null":
+        return JSON_NULL
+    return any_json(min(depth, 2))
+
+
+# ----------------------------------------------------------------------------- EBNF
+_TOKEN = re.compile(r'\s*(::=|\||\(|\)|\*|\+|\?|"(?:[^"\\]|\\.)*"|\[(?:[^\]\\]|\\.)*\]|[A-Za-z_][\w-]*)')
+
+
+def ebnf_to_regex(grammar: str, root: str = "root", depth: int = 6) -> str:
+    rules = {}
+    for line in re.split(r"\n(?=\s*[A-Za-z_][\w-]*\s*::=)", grammar.strip()):
+        if "::=" not in line:
+            continue
+        name, body = line.split("::=", 1)
+        rules[name.strip()] = body.strip()
+
+    def expand(name, d):
+        if d < 0:
+            return "(?!)" if False else "[^\\x00-\\xff]"  # unreachable branch: matches nothing
+        toks = [m.group(1) for m in _TOKEN.finditer(rules[name])]
+        out = []
+        for t in toks:
+            if t.startswith('"'):
+                out.append(_esc(json.loads(t)))
+            elif t.startswith("["):
+                out.append(t)
+            elif t in ("|", "(", ")", "*", "+", "?"):
+                out.append(t)
+            else:
+                out.append("(" + expand(t, d - 1) + ")")
+        return "".join(out)
+
+    return expand(root, depth)
+
+
+# ----------------------------------------------------------------------------- vocab
+def token_bytes(tokenizer, vocab_size: int) -> list[bytes]:
+    """Byte string of every token id (empty for special tokens)."""
+    if hasattr(tokenizer, "get_vocab_strings") and type(tokenizer).__name__ == "ByteTokenizer":
+        out = []
+        for i in range(vocab_size):
+            out.append(bytes([i]) if i < 256 else b"")
+        return out
+    tok = getattr(tokenizer, "tok", tokenizer)
+    special = set(getattr(tok, "all_special_ids", []) or [])
+    out = []
+    try:
+        pieces = tok.convert_ids_to_tokens(list(range(min(vocab_size, len(tok)))))
+    except Exception:
+        pieces = None
+    bdec = _gpt2_byte_decoder()
+    for i in range(vocab_size):
+        if i in special or pieces is None or i >= len(pieces) or pieces[i] is None:
+            out.append(b"")
+            continue
+        p = pieces[i]
+        if p.startswith("<0x") and p.endswith(">") and len(p) == 6:  # sentencepiece byte fallback
+            out.append(bytes([int(p[3:5], 16)]))
+        elif "▁" in p:
+            out.append(p.replace("▁", " ").encode("utf-8"))
+        elif all(c in bdec for c in p):
+            out.append(bytes(bdec[c] for c in p))
+        else:
+            out.append(p.encode("utf-8"))
+    return out
+
+
+def _gpt2_byte_decoder():
+    bs = list(range(ord("!"), ord("~") + 1)) + list(range(ord("¡"), ord("¬") + 1)) + list(range(ord("®"), ord("ÿ") + 1))
+    cs = bs[:]
+    n = 0
+    for b in range(256):
+        if b not in bs:
+            bs.append(b)
+            cs.append(256 + n)
+            n += 1
+    return {chr(c): b for b, c in zip(bs, cs)}
+
+
+class GrammarVocabulary:
+    """Shared per-tokenizer trie (build once, reuse for every request)."""
+
+    def __init__(self, tokenizer, vocab_size: int, eos_ids):
+        self.size = vocab_size
+        self.native = _b200host.GrammarVocab(token_bytes(tokenizer, vocab_size), sorted(int(e) for e in eos_ids))
+
+
+class GrammarConstraint:
+    """Per-request constraint consumed by the engine's sampler."""
+
+    def __init__(self, vocab: GrammarVocabulary, regex: str):
+        self.vocab = vocab
+        self.regex = regex
+        self.m = _b200host.GrammarMatcher(vocab.native, regex)
+        self.n_committed = 0
+
+    @classmethod
+    def from_json_schema(cls, vocab, schema):
+        return cls(vocab, json_schema_to_regex(schema))
+
+    @classmethod
+    def from_ebnf(cls, vocab, grammar, root="root"):
+        return cls(vocab, ebnf_to_regex(grammar, root))
+
+    @classmethod
+    def json_object(cls, vocab):
+        return cls(vocab, WS + any_json(3) + WS)
+
+    def allowed_mask(self, V: int) -> np.ndarray:
+        words = self.m.mask()
+        bits = np.unpackbits(words.view(np.uint8), bitorder="little")[:V].astype(bool)
+        if bits.shape[0] < V:
+            bits = np.pad(bits, (0, V - bits.shape[0]))
+        return bits
+
+    def commit(self, tok: int):
+        if not self.m.accept_token(int(tok)):
+            raise ValueError(f"token {tok} violates the grammar")
+        self.n_committed += 1
+
+    def rollback(self, n: int):
+        self.m.rollback(int(n))
+        self.n_committed -= n
+
+    def is_terminated(self) -> bool:
+        return self.m.is_terminated()
+
+    def forced_prefix(self) -> bytes:
+        return self.m.forced_prefix()
+
+
+def constraint_factory(vocab: GrammarVocabulary):
+    """OpenAI ``response_format`` -> constraint (server hook)."""
+
+    def make(rf: dict):
+        t = rf.get("type")
+        if t == "json_object":
+            return GrammarConstraint.json_object(vocab)
+        if t == "json_schema":
+            js = rf.get("json_schema", {})
+            return GrammarConstraint.from_json_schema(vocab, js.get("schema", js))
+        if t == "regex":
+            return GrammarConstraint(vocab, rf["regex"])
+        if t == "grammar":
+            return GrammarConstraint.from_ebnf(vocab, rf["grammar"])
+        return None
+
+    return make

@@ -61,6 +61,7 @@ struct GemmArgs {
   int M, N, K, ldy, ldr;
   int kb_total, kb_per_split, ksplit;
   int epi;
+  unsigned long long* trace;  // optional [ctas][6] %globaltimer stamps (diagnostics), null in production
 };
 
 template <int BN, int STAGES>
@@ -109,6 +110,9 @@ __global__ void __launch_bounds__(128, 1)
   const int nkb = kb_end - kb_begin;
 
   pdl_launch_dependents();
+  unsigned long long* trace =
+      args.trace ? args.trace + 6 * (blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) : nullptr;
+  if (trace && threadIdx.x == 0) trace[0] = globaltimer();
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
@@ -127,6 +131,7 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (trace && threadIdx.x == 0) trace[1] = globaltimer();
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
@@ -165,6 +170,7 @@ __global__ void __launch_bounds__(128, 1)
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
+      if (trace && i == 0) trace[2] = globaltimer();
       tc_fence_after();
       const uint32_t a = sbase + s * S::kStageBytes;
       const uint32_t b = a + S::kABytes;
@@ -184,6 +190,7 @@ __global__ void __launch_bounds__(128, 1)
   // ---------------- drain TMEM into this CTA's fp32 partial [BN][128] ----------------
   const bool acc_ok = __syncthreads_and(mbar_wait(bar_accum, 0, kErrTmemWait) ? 1 : 0) != 0;
   tc_fence_after();
+  if (trace && threadIdx.x == 0) trace[3] = globaltimer();
   const int r = warp * 32 + lane;  // TMEM lane == weight row within the tile
   float* part = reinterpret_cast<float*>(smem);
   {
@@ -200,60 +207,108 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   if (args.ksplit > 1) cluster_sync();
   else __syncthreads();
+  if (trace && threadIdx.x == 0) trace[4] = globaltimer();
 
   // ---------------- cluster reduction + epilogue ----------------
   const int ks = args.ksplit;
   const int js = (BN + ks - 1) / ks;
   const int j_lo = z * js;
   const int j_hi = min(BN, min(j_lo + js, args.M - m0));
-  const float* rp[8];
+  // Partials are [BN][128] fp32 rows = 32 float4 per token column. Each thread
+  // sums whole float4s of the S partials in split order 0..S-1; all S loads of
+  // a float4 are issued before the adds so their DSMEM latencies overlap.
+  const float4* rp[8];
 #pragma unroll
-  for (int q = 0; q < 8; ++q) rp[q] = (q < ks) ? (ks > 1 ? map_cluster_rank(part, q) : part) : part;
-  // Sum of the split partials in split order; all loads of a group are issued
-  // before the adds so their DSMEM latencies overlap.
-  auto reduce_at = [&](int j, int row) -> float {
-    const int off = j * 128 + row;
-    float v[8];
+  for (int q = 0; q < 8; ++q)
+    rp[q] = reinterpret_cast<const float4*>((q < ks) ? (ks > 1 ? map_cluster_rank(part, q) : part) : part);
+  auto red4 = [&](int j, int r4) -> float4 {
+    const int off = j * 32 + r4;
+    float4 v[8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) v[q] = (q < ks) ? rp[q][off] : 0.f;
-    float acc = v[0];
+    for (int q = 0; q < 8; ++q)
+      if (q < ks) v[q] = rp[q][off];
+    float4 acc = v[0];
 #pragma unroll
     for (int q = 1; q < 8; ++q)
-      if (q < ks) acc += v[q];
+      if (q < ks) {
+        acc.x += v[q].x;
+        acc.y += v[q].y;
+        acc.z += v[q].z;
+        acc.w += v[q].w;
+      }
     return acc;
   };
   const bool glu = args.epi == kEpiSwiGLU || args.epi == kEpiGeGLU || args.epi == kEpiSwiGLUOAI;
   if (glu) {
-    const int row = r & 63, par = r >> 6;
-    const int f = (n0 >> 1) + row;
+    // 16 threads per token column (64 gate rows as 16 float4), 8 columns per pass
+    const int jj = threadIdx.x >> 4, f4 = threadIdx.x & 15;
     __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(args.Y);
-    const float bg = args.bias ? bf2f(args.bias[n0 + row]) : 0.f;
-    const float bu = args.bias ? bf2f(args.bias[n0 + 64 + row]) : 0.f;
-    if (f < (args.N >> 1)) {
-#pragma unroll 2
-      for (int j = j_lo + par; j < j_hi; j += 2) {
+    float bg[4], bu[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      bg[e] = args.bias ? bf2f(args.bias[n0 + f4 * 4 + e]) : 0.f;
+      bu[e] = args.bias ? bf2f(args.bias[n0 + 64 + f4 * 4 + e]) : 0.f;
+    }
+    for (int j = j_lo + jj; j < j_hi; j += 8) {
+      const float4 g4 = red4(j, f4), u4 = red4(j, f4 + 16);
+      const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+      __nv_bfloat16 o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
         // round the gate and up projections to bf16 first, as an unfused bf16
         // model would, then apply the activation in fp32
-        const float g = bf2f(f2bf(reduce_at(j, row) + bg));
-        const float u = bf2f(f2bf(reduce_at(j, row + 64) + bu));
-        Y[(size_t)(m0 + j) * args.ldy + f] = f2bf(glu_act(args.epi, g, u));
+        const float g = bf2f(f2bf(gv[e] + bg[e]));
+        const float u = bf2f(f2bf(uv[e] + bu[e]));
+        o[e] = f2bf(glu_act(args.epi, g, u));
+      }
+      const int f = (n0 >> 1) + f4 * 4;
+      __nv_bfloat16* dst = Y + (size_t)(m0 + j) * args.ldy + f;
+      if (f + 3 < (args.N >> 1) && (((uintptr_t)dst) & 7) == 0) {
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (f + e < (args.N >> 1)) dst[e] = o[e];
       }
     }
   } else {
-    const int n = n0 + r;
-    if (n < args.N) {
-      const float bb = args.bias ? bf2f(args.bias[n]) : 0.f;
-#pragma unroll 4
-      for (int j = j_lo; j < j_hi; ++j) {
-        const float v = reduce_at(j, r) + bb;
-        const size_t m = (size_t)(m0 + j);
-        if (args.epi == kEpiStoreF32) {
-          reinterpret_cast<float*>(args.Y)[m * args.ldy + n] = v;
-        } else if (args.epi == kEpiAddBf16) {
-          const float rr = bf2f(args.R[m * args.ldr + n]);
-          reinterpret_cast<__nv_bfloat16*>(args.Y)[m * args.ldy + n] = f2bf(bf2f(f2bf(v)) + rr);
+    // 32 threads per token column (128 rows as 32 float4), 4 columns per pass
+    const int jj = threadIdx.x >> 5, r4 = threadIdx.x & 31;
+    const int n = n0 + r4 * 4;
+    float bb[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) bb[e] = (args.bias && n + e < args.N) ? bf2f(args.bias[n + e]) : 0.f;
+    for (int j = j_lo + jj; j < j_hi; j += 4) {
+      const float4 v4 = red4(j, r4);
+      const float v[4] = {v4.x + bb[0], v4.y + bb[1], v4.z + bb[2], v4.w + bb[3]};
+      const size_t m = (size_t)(m0 + j);
+      if (args.epi == kEpiStoreF32) {
+        float* dst = reinterpret_cast<float*>(args.Y) + m * args.ldy + n;
+        if (n + 3 < args.N && (((uintptr_t)dst) & 15) == 0) {
+          *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
         } else {
-          reinterpret_cast<__nv_bfloat16*>(args.Y)[m * args.ldy + n] = f2bf(v);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (n + e < args.N) dst[e] = v[e];
+        }
+      } else {
+        __nv_bfloat16 o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (args.epi == kEpiAddBf16) {
+            const float rr = (n + e < args.N) ? bf2f(args.R[m * args.ldr + n + e]) : 0.f;
+            o[e] = f2bf(bf2f(f2bf(v[e])) + rr);
+          } else {
+            o[e] = f2bf(v[e]);
+          }
+        }
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.Y) + m * args.ldy + n;
+        if (n + 3 < args.N && (((uintptr_t)dst) & 7) == 0) {
+          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (n + e < args.N) dst[e] = o[e];
         }
       }
     }
@@ -261,6 +316,7 @@ __global__ void __launch_bounds__(128, 1)
   // no CTA may leave while a peer still reads its partial
   if (args.ksplit > 1) cluster_sync();
   else __syncthreads();
+  if (trace && threadIdx.x == 0) trace[5] = globaltimer();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, S::kTmemCols);
@@ -356,28 +412,18 @@ static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmA
 // A function of (N, K) only: every M uses the same K partition and the same
 // reduction order. Chosen so skinny (decode) GEMMs fill the machine with about
 // two CTAs per SM while every split keeps at least 8 K blocks.
+// Powers of two only (clusters of 2/4/8 pack into GPCs without stranding
+// slots), the largest that keeps the grid within one wave of ~90% of the
+// 2-per-SM CTA slots and at least 8 K blocks per split.
 static int choose_splits(int N, int K, int num_sms) {
   const int kb = (K + 63) / 64;
   const int tiles = (N + 127) / 128;
-  const int slots = 2 * num_sms;
-  if (tiles >= slots) return 1;
-  double best = -1.0;
-  int best_s = 1;
-  for (int s = 1; s <= 8; ++s) {
-    const int kps = (kb + s - 1) / s;
-    if (s > 1 && kps < 8) break;
-    const int s_eff = (kb + kps - 1) / kps;
-    if (s_eff != s) continue;
-    const long ctas = (long)tiles * s;
-    const long waves = (ctas + slots - 1) / slots;
-    double eff = (double)ctas / (double)(waves * slots);
-    eff -= 0.01 * s;  // reduction work grows with s
-    if (eff > best + 1e-9) {
-      best = eff;
-      best_s = s;
-    }
-  }
-  return best_s;
+  const long budget = (long)(0.9 * 2 * num_sms);
+  int s = 1;
+  while (s < 8 && (long)tiles * (s * 2) <= budget && (kb + 2 * s - 1) / (2 * s) >= 8) s *= 2;
+  // the last split must own at least one K block
+  while (s > 1 && (long)((kb + s - 1) / s) * (s - 1) >= kb) s /= 2;
+  return s;
 }
 
 }  // namespace b200
@@ -385,6 +431,12 @@ static int choose_splits(int N, int K, int num_sms) {
 using namespace b200;
 
 extern "C" {
+
+// Diagnostics: when set, the next GEMM launches record 6 %globaltimer stamps per
+// CTA (entry, prologue done, first stage landed, accumulator ready, partials
+// published, exit) into this device buffer. Pass null to turn it off.
+static unsigned long long* g_gemm_trace = nullptr;
+void b200_gemm_set_trace(unsigned long long* buf) { g_gemm_trace = buf; }
 
 int b200_gemm_num_splits(int M, int N, int K, int num_sms) {
   (void)M;
@@ -416,6 +468,7 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   a.ldy = ldy;
   a.ldr = ldr;
   a.epi = epi;
+  a.trace = g_gemm_trace;
   a.kb_total = (K + 63) / 64;
   const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms);
   if (s > 8) return -1;

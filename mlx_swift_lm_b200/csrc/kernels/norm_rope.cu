@@ -92,7 +92,8 @@ __global__ void qk_norm_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, in
   const float* cs = cos_sin + (size_t)pos * rot_dim;
   const int half = rot_dim >> 1;
   const __nv_bfloat16* row = qkv + (size_t)t * ld_qkv;
-  for (int hh = warp; hh < H + 2 * KVH; hh += nw) {
+  // one warp per head; blockIdx.y selects the group of nw heads
+  for (int hh = blockIdx.y * nw + warp; hh < min(H + 2 * KVH, (int)(blockIdx.y + 1) * nw); hh += nw) {
     const __nv_bfloat16* src = row + (size_t)hh * D;
     const bool is_q = hh < H, is_k = !is_q && hh < H + KVH;
     if (!is_q && !is_k) {
@@ -246,17 +247,18 @@ int b200_qk_norm_rope_kv(const void* qkv, int T, int ld_qkv, const int* position
                          cudaStream_t st) {
   if (T <= 0) return 0;
   if (D > 512 || (rot_dim & 1) || rot_dim > D) return -1;
-  const int threads = 256;
+  const int threads = 128;
   const size_t smem = (threads / 32) * D * sizeof(float);
+  const dim3 grid(T, (H + 2 * KVH + threads / 32 - 1) / (threads / 32));
   if (kv_fp8) {
-b200::launch_k(    qk_norm_rope_kv_kernel<uint8_t>, dim3(T), dim3(threads), smem, st, 1, 
+    launch_k(qk_norm_rope_kv_kernel<uint8_t>, grid, dim3(threads), smem, st, 1,
         reinterpret_cast<const __nv_bfloat16*>(qkv), ld_qkv, positions, slots, cos_sin, rot_dim, interleaved,
         reinterpret_cast<const __nv_bfloat16*>(qw), reinterpret_cast<const __nv_bfloat16*>(kw), eps,
         reinterpret_cast<__nv_bfloat16*>(q_out), reinterpret_cast<uint8_t*>(k_cache),
         reinterpret_cast<uint8_t*>(v_cache), k_scale, v_scale, H, KVH, D, num_slots,
         reinterpret_cast<__nv_bfloat16*>(k_out), reinterpret_cast<__nv_bfloat16*>(v_out));
   } else {
-b200::launch_k(    qk_norm_rope_kv_kernel<__nv_bfloat16>, dim3(T), dim3(threads), smem, st, 1, 
+    launch_k(qk_norm_rope_kv_kernel<__nv_bfloat16>, grid, dim3(threads), smem, st, 1,
         reinterpret_cast<const __nv_bfloat16*>(qkv), ld_qkv, positions, slots, cos_sin, rot_dim, interleaved,
         reinterpret_cast<const __nv_bfloat16*>(qw), reinterpret_cast<const __nv_bfloat16*>(kw), eps,
         reinterpret_cast<__nv_bfloat16*>(q_out), reinterpret_cast<__nv_bfloat16*>(k_cache),

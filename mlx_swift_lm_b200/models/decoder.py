@@ -134,12 +134,16 @@ class DecoderLM:
         return sum(t.numel() for _, t in self.named_tensors() if t is not None)
 
     def init_random(self, seed: int = 0, std: float = 0.02):
-        """Random N(0, std) weights (norm weights 1), generated on the model's
-        device. Shapes are the rank-local TP shards."""
+        """Random N(0, std) weights (norm weights 1, sinks N(0,1)), generated on
+        the model's device. Every rank draws the full tensors from the same
+        seed and keeps its tensor-parallel shard, so a TP=N model computes the
+        same function as the TP=1 model of that seed."""
         cfg = self.cfg
         g = torch.Generator(device=self.device)
-        g.manual_seed(seed + 7919 * self.tp.rank)
+        g.manual_seed(seed)
         dev, dt = self.device, self.dtype
+        r, w = self.tp.rank, self.tp.world
+        D = self.D
 
         def rn(*shape):
             t = torch.empty(shape, device=dev, dtype=dt)
@@ -148,6 +152,30 @@ class DecoderLM:
 
         def ones(n):
             return torch.zeros(n, device=dev, dtype=dt) if cfg.norm_offset_one else torch.ones(n, device=dev, dtype=dt)
+
+        def rows(t, n_per):  # contiguous row block of this rank
+            return t if w == 1 else t[r * n_per:(r + 1) * n_per].contiguous()
+
+        def cols(t):
+            if w == 1:
+                return t
+            n = t.shape[-1] // w
+            return t[..., r * n:(r + 1) * n].contiguous()
+
+        def kv_rows(t):
+            if w == 1:
+                return t
+            if cfg.num_kv_heads >= w:
+                return rows(t, self.KVH * D)
+            h = (r * cfg.num_kv_heads) // w
+            return t[h * D:(h + 1) * D].contiguous()
+
+        def glu_pair(F_full, F_local, K, lead=()):
+            gate, up = rn(*lead, F_full, K), rn(*lead, F_full, K)
+            if lead:
+                return torch.stack([ref.interleave_gate_up(rows(gate[e], F_local), rows(up[e], F_local))
+                                    for e in range(lead[0])])
+            return ref.interleave_gate_up(rows(gate, F_local), rows(up, F_local))
 
         hd = cfg.hidden_size
         self.embed = rn(cfg.vocab_size, hd)
@@ -158,44 +186,56 @@ class DecoderLM:
             L = LayerWeights()
             L.ln1 = ones(hd)
             L.ln2 = ones(hd)
-            L.wqkv = rn((self.H + 2 * self.KVH) * self.D, hd)
+            wq, wk, wv = rn(cfg.q_size, hd), rn(cfg.kv_size, hd), rn(cfg.kv_size, hd)
+            L.wqkv = torch.cat([rows(wq, self.H * D), kv_rows(wk), kv_rows(wv)], 0)
             if cfg.attention_bias:
-                L.bqkv = rn((self.H + 2 * self.KVH) * self.D)
+                bq, bk, bv = rn(cfg.q_size), rn(cfg.kv_size), rn(cfg.kv_size)
+                L.bqkv = torch.cat([rows(bq, self.H * D), kv_rows(bk), kv_rows(bv)], 0)
             if cfg.qk_norm:
-                L.q_norm = ones(self.D)
-                L.k_norm = ones(self.D)
-            L.wo = rn(hd, self.H * self.D)
+                L.q_norm = ones(D)
+                L.k_norm = ones(D)
+            L.wo = cols(rn(hd, cfg.q_size))
             if cfg.o_bias:
-                L.bo = rn(hd) if self.tp.rank == 0 else torch.zeros(hd, device=dev, dtype=dt)
+                bo = rn(hd)
+                L.bo = bo if r == 0 else torch.zeros_like(bo)
             if cfg.post_norms:
                 L.post_attn_norm = ones(hd)
                 L.post_ffn_norm = ones(hd)
             if cfg.attention_sinks:
-                L.sinks = torch.empty(self.H, device=dev, dtype=torch.float32).normal_(0.0, 1.0, generator=g)
+                s = torch.empty(cfg.num_heads, device=dev, dtype=torch.float32).normal_(0.0, 1.0, generator=g)
+                L.sinks = rows(s, self.H)
             if cfg.is_moe(li):
                 E = cfg.num_experts
+                Fe = cfg.moe_intermediate_size
                 L.moe = True
                 L.router = rn(E, hd)
                 if cfg.router_bias:
                     L.router_b = rn(E)
-                L.experts_gu = rn(E, 2 * self.Fe, hd)
-                L.experts_d = rn(E, hd, self.Fe)
+                L.experts_gu = glu_pair(Fe, self.Fe, hd, (E,))
+                L.experts_d = cols(rn(E, hd, Fe))
                 if cfg.mlp_bias:
-                    L.experts_gu_b = rn(E, 2 * self.Fe)
-                    L.experts_d_b = rn(E, hd)
+                    gb, ub = rn(E, Fe), rn(E, Fe)
+                    L.experts_gu_b = torch.stack([ref.interleave_gate_up(rows(gb[e], self.Fe)[:, None],
+                                                                         rows(ub[e], self.Fe)[:, None])[:, 0]
+                                                  for e in range(E)])
+                    db = rn(E, hd)
+                    L.experts_d_b = db if r == 0 else torch.zeros_like(db)
                 if cfg.shared_expert_intermediate_size:
-                    Fs = cfg.shared_expert_intermediate_size // self.tp.world
-                    L.shared_gu = rn(2 * Fs, hd)
-                    L.shared_d = rn(hd, Fs)
+                    Fs = cfg.shared_expert_intermediate_size
+                    L.shared_gu = glu_pair(Fs, Fs // w, hd)
+                    L.shared_d = cols(rn(hd, Fs))
                     if cfg.shared_expert_gate:
                         L.shared_gate = rn(1, hd)
             else:
                 L.moe = False
-                L.wgu = rn(2 * self.F, hd)
-                L.wd = rn(hd, self.F)
+                F = cfg.intermediate_size
+                L.wgu = glu_pair(F, self.F, hd)
+                L.wd = cols(rn(hd, F))
                 if cfg.mlp_bias:
-                    L.bgu = rn(2 * self.F)
-                    L.bd = rn(hd)
+                    gb, ub = rn(F), rn(F)
+                    L.bgu = ref.interleave_gate_up(rows(gb, self.F)[:, None], rows(ub, self.F)[:, None])[:, 0]
+                    bd = rn(hd)
+                    L.bd = bd if r == 0 else torch.zeros_like(bd)
             self.layers.append(L)
         return self
 
