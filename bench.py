@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--out-tokens", type=int, default=256)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
+                    help="tensor-parallel collectives: fused symmetric-memory kernels or NCCL all-reduce")
     return ap.parse_args()
 
 
@@ -144,6 +146,8 @@ def main():
         cfg.num_layers = args.layers
     tp = TensorParallel(rank, world, group)
     model = DecoderLM(cfg, dev, torch.bfloat16, tp=tp).init_random(args.seed)
+    if world > 1 and args.tp_mode == "fused":
+        model.enable_fused_tp(args.streams)
     max_len = args.max_prompt + args.out_tokens + 16
     ecfg = EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=args.streams,
                                                   max_batched_tokens_per_step=16384, prefill_chunk_size=4096),
@@ -180,6 +184,7 @@ def main():
     B = g.bucket(args.streams)
     graph = g.graphs[B]
     for _ in range(args.warmup):
+        model.begin_step()
         graph.replay()
     barrier()
     clocks = ClockSampler(local)
@@ -187,6 +192,7 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
+        model.begin_step()
         graph.replay()
     e1.record()
     barrier()
@@ -236,7 +242,7 @@ def main():
             "config": {"model": f"{args.model}-shape" + (f" ({cfg.num_layers} layers, DEBUG)" if args.layers else ""),
                        "global_batch": args.streams, "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}] + "
                                                                 f"{args.out_tokens} out",
-                       "parallelism": f"tp{world}", "kv": "paged bf16, page 16",
+                       "parallelism": f"tp{world}" + (f" ({args.tp_mode} collectives)" if world > 1 else ""), "kv": "paged bf16, page 16",
                        "l2": "inputs larger than L2 (weights ~16 GB/world + KV per step)"},
             "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
             "itl_p50_ms": round(itl_p50_ms, 3),

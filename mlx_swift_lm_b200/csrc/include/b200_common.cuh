@@ -135,7 +135,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled, no multicast). Coordinates are element indices, innermost first.
+// TMA tiled loads into this CTA's shared memory. Coordinates are element
+// indices, innermost first.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -29,6 +29,9 @@
 #include <unordered_map>
 
 #include "b200_common.cuh"
+#include "b200_comm.cuh"
+
+#include <memory>
 
 namespace b200 {
 
@@ -88,10 +91,24 @@ __device__ __forceinline__ const float* map_cluster_rank(const float* p, uint32_
   return reinterpret_cast<const float*>(r);
 }
 
-template <int BN, int STAGES>
+// Collective modes of the GEMM (tensor parallelism over symmetric memory).
+enum GemmMode : int {
+  kModeLocal = 0,  // X from local memory, Y stored locally
+  kModeAG = 1,     // all-gather prologue: X rows are fetched from every rank's published rows
+  kModeRS = 2,     // reduce-scatter epilogue: fp32 partial rows stored into the owner rank's inbox
+};
+
+struct CollArgs {
+  CUtensorMap peer_x[2 * kMaxRanks];  // AG: [parity][rank] maps over each rank's published rows
+  CommCtx comm;
+  int phase;   // collective phase index within the step (epoch = step * kPhasesPerStep + phase + 1)
+  int parity;  // buffer slot of this call
+};
+
+template <int BN, int STAGES, int MODE>
 __global__ void __launch_bounds__(128, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                        GemmArgs args) {
+                        GemmArgs args, const __grid_constant__ CollArgs coll) {
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -147,8 +164,25 @@ __global__ void __launch_bounds__(128, 1)
       tma_load_2d(a, &tmW, bar_full + 8 * i, (kb_begin + i) * 64, n0, pol_w);
     }
     pdl_wait();
+    // Activation tile: local TMA, or (all-gather mode) one TMA box per rank,
+    // fetched straight from that rank's published rows over NVLink into this
+    // CTA's own shared memory (plain tiled loads).
+    auto load_x = [&](uint32_t b, uint32_t bar, int kc) {
+      if constexpr (MODE == kModeAG) {
+        const int rpr = coll.comm.rows_per_rank;
+        for (int j = 0; j < coll.comm.world; ++j)
+          tma_load_2d(b + j * rpr * 128, &coll.peer_x[coll.parity * kMaxRanks + j], bar, kc, 0, pol_x);
+      } else {
+        tma_load_2d(b, &tmX, bar, kc, m0, pol_x);
+      }
+    };
+    if constexpr (MODE == kModeAG) {
+      // every rank must have published this phase's rows (bounded wait)
+      const uint32_t ep = coll.comm.epoch(coll.phase);
+      for (int j = 0; j < coll.comm.world; ++j) wait_counter(coll.comm.pad_ptr(coll.comm.rank, kPadAG, j), ep);
+    }
     for (int i = 0; i < pre; ++i)
-      tma_load_2d(sbase + i * S::kStageBytes + S::kABytes, &tmX, bar_full + 8 * i, (kb_begin + i) * 64, m0, pol_x);
+      load_x(sbase + i * S::kStageBytes + S::kABytes, bar_full + 8 * i, (kb_begin + i) * 64);
     int issued = pre;
     for (int i = pre; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
@@ -158,7 +192,7 @@ __global__ void __launch_bounds__(128, 1)
       mbar_arrive_expect_tx(bar_full + 8 * s, S::kStageBytes);
       const int kc = (kb_begin + i) * 64;
       tma_load_2d(a, &tmW, bar_full + 8 * s, kc, n0, pol_w);
-      tma_load_2d(b, &tmX, bar_full + 8 * s, kc, m0, pol_x);
+      load_x(b, bar_full + 8 * s, kc);
       issued = i + 1;
     }
     // make sure no copy issued here is still landing when the stage memory is reused
@@ -282,7 +316,18 @@ __global__ void __launch_bounds__(128, 1)
       const float4 v4 = red4(j, r4);
       const float v[4] = {v4.x + bb[0], v4.y + bb[1], v4.z + bb[2], v4.w + bb[3]};
       const size_t m = (size_t)(m0 + j);
-      if (args.epi == kEpiStoreF32) {
+      if constexpr (MODE == kModeRS) {
+        // fp32 partial row m -> inbox slot [parity][this rank][row] of its owner rank
+        const int rpr = coll.comm.rows_per_rank;
+        float* dst = coll.comm.recv_row((int)m / rpr, coll.parity, coll.comm.rank, (int)m % rpr) + n;
+        if (n + 3 < args.N) {
+          *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (n + e < args.N) dst[e] = v[e];
+        }
+      } else if (args.epi == kEpiStoreF32) {
         float* dst = reinterpret_cast<float*>(args.Y) + m * args.ldy + n;
         if (n + 3 < args.N && (((uintptr_t)dst) & 15) == 0) {
           *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
@@ -316,6 +361,11 @@ __global__ void __launch_bounds__(128, 1)
   // no CTA may leave while a peer still reads its partial
   if (args.ksplit > 1) cluster_sync();
   else __syncthreads();
+  if constexpr (MODE == kModeRS) {
+    // all of this CTA's inbox stores are issued; the last CTA of the grid
+    // publishes the phase to every rank
+    if (threadIdx.x == 0) last_cta_signal(coll.comm, kPadRS, coll.comm.epoch(coll.phase));
+  }
   if (trace && threadIdx.x == 0) trace[5] = globaltimer();
   if (warp == 1) {
     tc_fence_after();
@@ -391,21 +441,39 @@ bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols,
   return true;
 }
 
-template <int BN, int STAGES>
-static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, int tiles_n, int tiles_m,
-                       cudaStream_t st) {
+template <int BN, int STAGES, int MODE>
+static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, const CollArgs& coll,
+                       int tiles_n, int tiles_m, cudaStream_t st) {
   using S = GemmSmem<BN, STAGES>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES, MODE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
     if (e != cudaSuccess) return (int)e;
     configured = true;
   }
-  cudaError_t e = launch_k(gemm_bf16_tc_kernel<BN, STAGES>, dim3(tiles_n, tiles_m, a.ksplit), dim3(128, 1, 1),
-                           S::kTotal, st, a.ksplit, tw, tx, a);
+  cudaError_t e = launch_k(gemm_bf16_tc_kernel<BN, STAGES, MODE>, dim3(tiles_n, tiles_m, a.ksplit),
+                           dim3(128, 1, 1), S::kTotal, st, a.ksplit, tw, tx, a, coll);
   if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
+}
+
+template <int MODE>
+static int launch_bn(int BN, const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, const CollArgs& coll,
+                     int tiles_n, int tiles_m, cudaStream_t st) {
+  switch (BN) {
+    case 16: return launch_gemm<16, 6, MODE>(tw, tx, a, coll, tiles_n, tiles_m, st);
+    case 32: return launch_gemm<32, 5, MODE>(tw, tx, a, coll, tiles_n, tiles_m, st);
+    case 64: return launch_gemm<64, 4, MODE>(tw, tx, a, coll, tiles_n, tiles_m, st);
+    case 128: return launch_gemm<128, 3, MODE>(tw, tx, a, coll, tiles_n, tiles_m, st);
+    case 256: return launch_gemm<256, 4, MODE>(tw, tx, a, coll, tiles_n, tiles_m, st);
+    default: return -1;
+  }
+}
+
+static const CollArgs& local_coll() {
+  static CollArgs c = {};
+  return c;
 }
 
 // Split count S (1..8, the cluster size) for a weight of N rows and K inputs.
@@ -475,13 +543,85 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   a.kb_per_split = (a.kb_total + s - 1) / s;
   a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
   const int tiles_n = (N + 127) / 128, tiles_m = (M + BN - 1) / BN;
-  switch (BN) {
-    case 16: return launch_gemm<16, 6>(tw, tx, a, tiles_n, tiles_m, stream);
-    case 32: return launch_gemm<32, 5>(tw, tx, a, tiles_n, tiles_m, stream);
-    case 64: return launch_gemm<64, 4>(tw, tx, a, tiles_n, tiles_m, stream);
-    case 128: return launch_gemm<128, 3>(tw, tx, a, tiles_n, tiles_m, stream);
-    default: return launch_gemm<256, 4>(tw, tx, a, tiles_n, tiles_m, stream);
-  }
+  return launch_bn<kModeLocal>(BN, tw, tx, a, local_coll(), tiles_n, tiles_m, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Fused collective GEMMs (tensor parallelism). `comm_ctx` is a CommCtx blob
+// (see b200_comm.cuh). Rows: M_pad = world * rows_per_rank, rank j owns rows
+// [j*rpr, (j+1)*rpr); only the first M_real rows are meaningful.
+// ---------------------------------------------------------------------------
+
+// All-gather -> GEMM: X rows come from every rank's published rows of slot
+// `parity`; waits (bounded) for phase `phase` on the AG pad. Y is local.
+int b200_gemm_bf16_ag(const void* comm_ctx, int phase, int parity, int M_real, int K, const void* W, int N, int ldw,
+                      void* Y, int ldy, const void* bias, int epi, int num_sms, int force_splits,
+                      cudaStream_t stream) {
+  CollArgs* coll = new CollArgs();  // heap: ~2 KB, copied into the launch
+  std::unique_ptr<CollArgs> guard(coll);
+  memcpy(&coll->comm, comm_ctx, sizeof(CommCtx));
+  coll->phase = phase;
+  coll->parity = parity;
+  const CommCtx& c = coll->comm;
+  const int M = c.world * c.rows_per_rank;
+  if (M_real > M || (c.rows_per_rank % 8) || c.hidden != K) return -1;
+  if (M != 16 && M != 32 && M != 64 && M != 128 && M != 256) return -1;
+  if ((K % 8) || (ldw % 8)) return -1;
+  const bool glu = epi == kEpiSwiGLU || epi == kEpiGeGLU || epi == kEpiSwiGLUOAI;
+  if (glu && (N % 128)) return -1;
+  CUtensorMap tw;
+  if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
+  for (int p = 0; p < 2; ++p)
+    for (int j = 0; j < c.world; ++j) {
+      const uint8_t* rows = c.base[j] + c.h_off + (size_t)p * c.rows_per_rank * c.hidden * 2;
+      if (!make_tmap_2d(&coll->peer_x[p * kMaxRanks + j], rows, c.rows_per_rank, K, K, c.rows_per_rank, 64, 2))
+        return -1;
+    }
+  GemmArgs a = {};
+  a.Y = Y;
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  a.M = M_real;
+  a.N = N;
+  a.K = K;
+  a.ldy = ldy;
+  a.epi = epi;
+  a.trace = g_gemm_trace;
+  a.kb_total = (K + 63) / 64;
+  const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms);
+  a.kb_per_split = (a.kb_total + s - 1) / s;
+  a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  return launch_bn<kModeAG>(M, tw, tw, a, *coll, (N + 127) / 128, 1, stream);
+}
+
+// GEMM -> reduce-scatter: fp32 partial rows go to their owner rank's inbox
+// slot `parity`; the last CTA publishes phase `phase` on the RS pad.
+int b200_gemm_bf16_rs(const void* comm_ctx, int phase, int parity, const void* X, int M_real, int K, int ldx,
+                      const void* W, int N, int ldw, const void* bias, int num_sms, int force_splits,
+                      cudaStream_t stream) {
+  CollArgs* coll = new CollArgs();
+  std::unique_ptr<CollArgs> guard(coll);
+  memcpy(&coll->comm, comm_ctx, sizeof(CommCtx));
+  coll->phase = phase;
+  coll->parity = parity;
+  const CommCtx& c = coll->comm;
+  const int M = c.world * c.rows_per_rank;
+  if (M_real > M || c.hidden != N || (K % 8) || (ldx % 8) || (ldw % 8)) return -1;
+  int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
+  if (!make_tmap_2d(&tx, X, M_real, K, ldx, BN, 64, 2)) return -1;
+  GemmArgs a = {};
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  a.M = M_real;
+  a.N = N;
+  a.K = K;
+  a.epi = kEpiStoreF32;
+  a.trace = g_gemm_trace;
+  a.kb_total = (K + 63) / 64;
+  const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms);
+  a.kb_per_split = (a.kb_total + s - 1) / s;
+  a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  return launch_bn<kModeRS>(BN, tw, tx, a, *coll, (N + 127) / 128, (M_real + BN - 1) / BN, stream);
 }
 
 }  // extern "C"

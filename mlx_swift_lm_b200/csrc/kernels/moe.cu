@@ -1,0 +1,443 @@
+// Mixture-of-experts kernels: router top-k, expert sort, grouped tcgen05 GEMM,
+// weighted combine.
+//
+// Reference behaviour: router top-k with normalisation in one threadgroup,
+// bit-identical to sort+gather (MLXLMCommon/MoERouterTopK.swift:22-160);
+// SwitchGLU gather -> expert matmuls -> weighted un-sort
+// (SwitchLayers.swift:478, gatherSort :244, scatterUnsort :257,
+// weightedExpertUnsort :149).
+//
+// B200 design:
+//   moe_route_topk   one warp per token: softmax over experts then top-k (and
+//                    optional renormalisation), or top-k logits then softmax;
+//                    ties resolve to the lower expert id.
+//   moe_sort         single-CTA counting sort of the T*k (token, expert) pairs
+//                    by expert (stable in pair index -> deterministic), plus a
+//                    work list of (expert, first row, rows) chunks of <= BN rows.
+//   moe_gather       sorted activation rows.
+//   grouped GEMM     tcgen05 swap-AB tiles: CTA (n tile, chunk) multiplies the
+//                    chunk's rows by its expert's weight tile (TMA row offset
+//                    expert * N); GLU epilogue for gate/up; grid sized for the
+//                    worst case so it can live in a CUDA graph (idle CTAs exit).
+//   moe_combine      out[t] = sum_j w[t, j] * y[pos(t, j)] in slot order j.
+#include <cudaTypedefs.h>
+
+#include "b200_common.cuh"
+
+namespace b200 {
+
+bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows,
+                  int box_cols, int dtype_bytes);
+
+namespace moe {
+
+// ---------------------------------------------------------------- router
+// mode 0: softmax over all experts, take top-k, renormalise if norm_topk.
+// mode 1: top-k over logits, softmax over the k (GPT-OSS).
+__global__ void route_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int mode, int norm_topk,
+                                  int* __restrict__ ids, float* __restrict__ w) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* lg = logits + (size_t)warp * E;
+  constexpr int kMaxPer = 8;  // E <= 256
+  float v[kMaxPer];
+  int per = (E + 31) / 32;
+  float mx = -INFINITY;
+  for (int i = 0; i < per; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? lg[e] : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
+  mx = warp_max(mx);
+  float denom = 1.f;
+  if (mode == 0) {
+    float s = 0.f;
+    for (int i = 0; i < per; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E) {
+        v[i] = __expf(v[i] - mx);
+        s += v[i];
+      }
+    }
+    denom = warp_sum(s);
+  }
+  float sel_v[16];
+  int sel_i[16];
+  for (int j = 0; j < k; ++j) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = 0; i < per; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && (v[i] > bv || (v[i] == bv && e < bi))) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    sel_v[j] = bv;
+    sel_i[j] = bi;
+    // remove the winner
+    for (int i = 0; i < per; ++i)
+      if (lane + 32 * i == bi) v[i] = -INFINITY;
+  }
+  if (lane == 0) {
+    if (mode == 0) {
+      float s = 0.f;
+      for (int j = 0; j < k; ++j) {
+        sel_v[j] /= denom;
+        s += sel_v[j];
+      }
+      for (int j = 0; j < k; ++j) {
+        ids[warp * k + j] = sel_i[j];
+        w[warp * k + j] = norm_topk ? sel_v[j] / s : sel_v[j];
+      }
+    } else {
+      const float m0 = sel_v[0];
+      float s = 0.f;
+      for (int j = 0; j < k; ++j) {
+        sel_v[j] = __expf(sel_v[j] - m0);
+        s += sel_v[j];
+      }
+      for (int j = 0; j < k; ++j) {
+        ids[warp * k + j] = sel_i[j];
+        w[warp * k + j] = sel_v[j] / s;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- sort
+// Outputs: perm [P] (pair index in expert order), pos [P] (sorted position of
+// each pair), chunks [max_chunks][3] (expert, first sorted row, rows), and
+// n_chunks. One CTA of 32 warps; warp w owns the contiguous pair range
+// [w*seg, (w+1)*seg), so ranks come from per-warp per-expert counters
+// (wcnt[32][E] in shared memory) plus __match_any_sync inside each 32-pair
+// slab: the placement is stable in pair index, hence deterministic.
+__global__ void __launch_bounds__(1024) sort_kernel(const int* __restrict__ ids, int P, int E, int BN,
+                                                    int max_chunks, int* __restrict__ perm, int* __restrict__ pos,
+                                                    int* __restrict__ chunks, int* __restrict__ n_chunks) {
+  pdl_launch_dependents();
+  pdl_wait();
+  extern __shared__ int sm[];
+  int* wcnt = sm;             // [32][E] counts, then exclusive bases
+  int* off = sm + 32 * E;     // [E] expert start offsets
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) wcnt[i] = 0;
+  __syncthreads();
+  const int seg = (P + 31) / 32;
+  const int p0 = warp * seg, p1 = min(P, p0 + seg);
+  for (int b = p0; b < p1; b += 32) {
+    const int p = b + lane;
+    const int e = p < p1 ? ids[p] : -1;
+    const bool ok = e >= 0 && e < E;
+    const unsigned grp = __match_any_sync(0xffffffffu, ok ? e : -1);
+    if (ok && (grp & lt) == 0) wcnt[warp * E + e] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int acc = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = wcnt[w * E + e];
+      wcnt[w * E + e] = acc;
+      acc += c;
+    }
+    off[e] = acc;  // total for now
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, nc = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = off[e];
+      off[e] = acc;
+      for (int r = 0; r < c; r += BN) {
+        if (nc < max_chunks) {
+          chunks[3 * nc + 0] = e;
+          chunks[3 * nc + 1] = acc + r;
+          chunks[3 * nc + 2] = min(BN, c - r);
+        }
+        ++nc;
+      }
+      acc += c;
+    }
+    *n_chunks = min(nc, max_chunks);
+    if (nc > max_chunks) set_status(kErrBounds);
+  }
+  __syncthreads();
+  for (int b = p0; b < p1; b += 32) {
+    const int p = b + lane;
+    const int e = p < p1 ? ids[p] : -1;
+    const bool ok = e >= 0 && e < E;
+    const unsigned grp = __match_any_sync(0xffffffffu, ok ? e : -1);
+    if (ok) {
+      const int s = off[e] + wcnt[warp * E + e] + __popc(grp & lt);
+      perm[s] = p;
+      pos[p] = s;
+    }
+    __syncwarp();
+    if (ok && (grp & lt) == 0) wcnt[warp * E + e] += __popc(grp);
+    __syncwarp();
+  }
+}
+
+__global__ void gather_kernel(const __nv_bfloat16* __restrict__ x, int K, const int* __restrict__ perm, int P,
+                              int k, __nv_bfloat16* __restrict__ xs) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int s = blockIdx.x;
+  if (s >= P) return;
+  const int t = perm[s] / k;
+  const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * K);
+  uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)s * K);
+  for (int i = threadIdx.x; i < K / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+__global__ void combine_kernel(const __nv_bfloat16* __restrict__ ys, int N, const int* __restrict__ pos,
+                               const float* __restrict__ w, int k, __nv_bfloat16* __restrict__ out,
+                               const __nv_bfloat16* __restrict__ bias_d, const int* __restrict__ ids) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int s = pos[t * k + j];
+      float y = bf2f(ys[(size_t)s * N + i]);
+      if (bias_d) y = bf2f(f2bf(y + bf2f(bias_d[(size_t)ids[t * k + j] * N + i])));
+      acc += w[t * k + j] * y;
+    }
+    out[(size_t)t * N + i] = f2bf(acc);
+  }
+}
+
+// ---------------------------------------------------------------- grouped GEMM
+struct GArgs {
+  __nv_bfloat16* Y;  // [P, ldy] sorted rows
+  const __nv_bfloat16* bias;  // [E, N] or null
+  const int* chunks;
+  const int* n_chunks;
+  int N, K, ldy, epi;
+};
+
+__device__ __forceinline__ float glu(int epi, float g, float u) {
+  if (epi == 4) {
+    const float c = 0.7978845608028654f;
+    return 0.5f * g * (1.f + tanhf(c * (g + 0.044715f * g * g * g))) * u;
+  }
+  if (epi == 5) {
+    g = fminf(g, 7.f);
+    u = fminf(fmaxf(u, -7.f), 7.f);
+    return (u + 1.f) * g / (1.f + __expf(-1.702f * g));
+  }
+  return silu(g) * u;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(128, 1) grouped_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                         const __grid_constant__ CUtensorMap tmX, GArgs a) {
+  constexpr int kA = 128 * 128, kB = BN * 128, kStage = kA + kB;
+  constexpr int kTmem = BN < 32 ? 32 : BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_full = sbase + STAGES * kStage;
+  const uint32_t bar_empty = bar_full + 8 * STAGES;
+  const uint32_t bar_acc = bar_empty + 8 * STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * kStage + (2 * STAGES + 1) * 8);
+  __shared__ float xbuf[64][17];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int chunk = blockIdx.y;
+  if (chunk >= *a.n_chunks) return;
+  const int e = a.chunks[3 * chunk], r0 = a.chunks[3 * chunk + 1], rc = a.chunks[3 * chunk + 2];
+  const int n0 = blockIdx.x * 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = (a.K + 63) / 64;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_acc, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmem);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0 && lane == 0) {
+    const uint64_t pw = l2_policy_evict_first(), px = l2_policy_evict_last();
+    int issued = 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES, r = i / STAGES;
+      if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
+      mbar_arrive_expect_tx(bar_full + 8 * s, kStage);
+      tma_load_2d(sbase + s * kStage, &tmW, bar_full + 8 * s, i * 64, e * a.N + n0, pw);
+      tma_load_2d(sbase + s * kStage + kA, &tmX, bar_full + 8 * s, i * 64, r0, px);
+      issued = i + 1;
+    }
+    for (int i = max(0, issued - STAGES); i < issued; ++i)
+      mbar_wait(bar_full + 8 * (i % STAGES), (i / STAGES) & 1, kErrGemmWait);
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES, r = i / STAGES;
+      if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
+      tc_fence_after();
+      const uint64_t ad = umma_desc_k_sw128(sbase + s * kStage, 1024);
+      const uint64_t bd = umma_desc_k_sw128(sbase + s * kStage + kA, 1024);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) tc_mma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+      tc_commit(bar_empty + 8 * s);
+    }
+    tc_commit(bar_acc);
+  }
+  __syncwarp();
+  const bool ok = __syncthreads_and(mbar_wait(bar_acc, 0, kErrTmemWait) ? 1 : 0) != 0;
+  tc_fence_after();
+  const int rl = warp * 32 + lane;
+  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+  const bool isglu = a.epi == 1 || a.epi == 4 || a.epi == 5;
+  const float bb = a.bias ? bf2f(a.bias[(size_t)e * a.N + n0 + rl]) : 0.f;
+  for (int jc = 0; jc < BN; jc += 16) {
+    uint32_t v[16];
+    tmem_ld16(tl + jc, v);
+    tc_wait_ld();
+    float f[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = ok ? __uint_as_float(v[j]) + bb : 0.f;
+    if (isglu) {
+      __syncthreads();
+      if (warp >= 2) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xbuf[rl - 64][j] = f[j];
+      }
+      __syncthreads();
+      if (warp < 2) {
+        const int fo = (n0 >> 1) + rl;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int row = jc + j;
+          if (row < rc && fo < (a.N >> 1)) {
+            const float g = bf2f(f2bf(f[j])), u = bf2f(f2bf(xbuf[rl][j]));
+            a.Y[(size_t)(r0 + row) * a.ldy + fo] = f2bf(glu(a.epi, g, u));
+          }
+        }
+      }
+    } else if (n0 + rl < a.N) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int row = jc + j;
+        if (row < rc) a.Y[(size_t)(r0 + row) * a.ldy + n0 + rl] = f2bf(f[j]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmem);
+  }
+}
+
+template <int BN, int STAGES>
+int launch_grouped(const CUtensorMap& tw, const CUtensorMap& tx, const GArgs& a, int max_chunks, cudaStream_t st) {
+  constexpr int smem = STAGES * (128 * 128 + BN * 128) + (2 * STAGES + 1) * 8 + 16 + 1024;
+  static bool cfg = false;
+  if (!cfg) {
+    cudaError_t e = cudaFuncSetAttribute(grouped_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return (int)e;
+    cfg = true;
+  }
+  cudaError_t e = launch_k(grouped_kernel<BN, STAGES>, dim3((a.N + 127) / 128, max_chunks), dim3(128), smem, st, 1, tw,
+                           tx, a);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+}  // namespace moe
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+int b200_moe_route_topk(const float* logits, int T, int E, int k, int mode, int norm_topk, int* ids, float* w,
+                        cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (E > 256 || k > 16) return -1;
+  cudaError_t e = launch_k(moe::route_topk_kernel, dim3((T + 3) / 4), dim3(128), 0, st, 1, logits, T, E, k, mode,
+                           norm_topk, ids, w);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+int b200_moe_sort(const int* ids, int P, int E, int BN, int max_chunks, int* perm, int* pos, int* chunks,
+                  int* n_chunks, cudaStream_t st) {
+  if (E > 1024 || P <= 0) return P < 0 ? -1 : (E > 1024 ? -1 : 0);
+  const int smem = 33 * E * (int)sizeof(int);
+  static bool cfg = false;
+  if (!cfg) {
+    cudaError_t e = cudaFuncSetAttribute(moe::sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 33 * 1024 * 4);
+    if (e != cudaSuccess) return (int)e;
+    cfg = true;
+  }
+  cudaError_t e = launch_k(moe::sort_kernel, dim3(1), dim3(1024), smem, st, 1, ids, P, E, BN, max_chunks, perm, pos,
+                           chunks, n_chunks);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+int b200_moe_gather(const void* x, int K, const int* perm, int P, int k, void* xs, cudaStream_t st) {
+  if (P <= 0) return 0;
+  if (K % 8) return -1;
+  cudaError_t e = launch_k(moe::gather_kernel, dim3(P), dim3(128), 0, st, 1,
+                           reinterpret_cast<const __nv_bfloat16*>(x), K, perm, P, k, reinterpret_cast<__nv_bfloat16*>(xs));
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+int b200_moe_combine(const void* ys, int T, int N, const int* pos, const float* w, int k, void* out,
+                     const void* bias_d, const int* ids, cudaStream_t st) {
+  if (T <= 0) return 0;
+  cudaError_t e = launch_k(moe::combine_kernel, dim3(T), dim3(256), 0, st, 1, reinterpret_cast<const __nv_bfloat16*>(ys),
+                           N, pos, w, k, reinterpret_cast<__nv_bfloat16*>(out),
+                           reinterpret_cast<const __nv_bfloat16*>(bias_d), ids);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+// Grouped GEMM over expert chunks: Y[rows of chunk] = epi(Xs[rows] . W[e]^T (+ bias[e])).
+// W: [E * N, K] (experts stacked), Xs: [P, K] sorted rows. BN is the chunk row cap.
+int b200_moe_grouped_gemm(const void* xs, int P, int K, const void* W, int E, int N, void* Y, int ldy,
+                          const void* bias, int epi, const int* chunks, const int* n_chunks, int max_chunks, int BN,
+                          cudaStream_t st) {
+  if (P <= 0) return 0;
+  if (K % 8) return -1;
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d(&tw, W, (int64_t)E * N, K, K, 128, 64, 2)) return -1;
+  if (!make_tmap_2d(&tx, xs, P, K, K, BN, 64, 2)) return -1;
+  moe::GArgs a{reinterpret_cast<__nv_bfloat16*>(Y), reinterpret_cast<const __nv_bfloat16*>(bias), chunks, n_chunks,
+               N, K, ldy, epi};
+  switch (BN) {
+    case 16: return moe::launch_grouped<16, 6>(tw, tx, a, max_chunks, st);
+    case 32: return moe::launch_grouped<32, 6>(tw, tx, a, max_chunks, st);
+    case 64: return moe::launch_grouped<64, 4>(tw, tx, a, max_chunks, st);
+    case 128: return moe::launch_grouped<128, 4>(tw, tx, a, max_chunks, st);
+    default: return -1;
+  }
+}
+
+}  // extern "C"
+
+B200_STATUS_ACCESSORS(moe)

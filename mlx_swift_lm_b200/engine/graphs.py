@@ -78,8 +78,7 @@ class DecodeGraphRunner:
                             dec_page_table=self.pt[:B], dec_seq_lens=self.sl[:B], dec_max_parts=self.max_parts)
 
     def _body(self, B):
-        logits = self.model.forward(self._fb(B), self.eng.kv)
-        ops.argmax(logits, out=self.out[:B])
+        self.model.forward_decode_tokens(self._fb(B), self.eng.kv, self.out[:B])
 
     def capture(self, B):
         self._reserve()
@@ -93,11 +92,13 @@ class DecodeGraphRunner:
         s.wait_stream(cur)
         with torch.cuda.stream(s):
             for _ in range(2):
+                self.model.begin_step()
                 self._body(B)
         cur.wait_stream(s)
         torch.cuda.synchronize(self.dev)
         n0 = _lib.launch_counter[0]
         g = torch.cuda.CUDAGraph()
+        self.model.begin_step()  # the capture itself does not run; every replay advances the step first
         with torch.cuda.graph(g, pool=self.pool):
             self._body(B)
         self.launches_per_replay[B] = _lib.launch_counter[0] - n0
@@ -182,6 +183,7 @@ class DecodeGraphRunner:
         _lib.check(L.b200_gather_tokens(self.out.data_ptr(), self.src.data_ptr(), self.hid.data_ptr(),
                                         self.ids.data_ptr(), Bb, _lib.stream_ptr(self.dev)), "gather_tokens")
         _lib.count(1)
+        self.model.begin_step()
         self.graphs[Bb].replay()
         _lib.count(self.launches_per_replay.get(Bb, 0))
         ko = self.out_k

@@ -119,6 +119,7 @@ class DecoderLM:
                                                 cfg.max_position_embeddings, cfg.partial_rotary_factor)
         self.cos_sin = self.cos_sin.to(self.device)
         self.lora = None  # optional LoRA manager (api.lora)
+        self.tp_fused = None  # fused symmetric-memory TP decode path (parallel.tp_fused)
 
     # ------------------------------------------------------------------ weights
     def named_tensors(self):
@@ -253,18 +254,12 @@ class DecoderLM:
         return self.tp.reduce(delta)
 
     def route(self, L, h):
-        """Router top-k: returns (weights [T, k] fp32, ids [T, k] int64)."""
+        """Router top-k: returns (weights [T, k] fp32, ids [T, k] expert ids)."""
         cfg = self.cfg
+        from ..ops import moe as moe_ops
+
         logits = ops.gemm(h, L.router, epi="f32", bias=L.router_b)
-        k = cfg.num_experts_per_tok
-        if cfg.router_mode == "topk_softmax":
-            v, idx = torch.topk(logits, k, dim=-1)
-            w = torch.softmax(v, dim=-1)
-        else:
-            p = torch.softmax(logits, dim=-1)
-            w, idx = torch.topk(p, k, dim=-1)
-            if cfg.norm_topk_prob:
-                w = w / w.sum(-1, keepdim=True)
+        w, idx = moe_ops.route_topk(logits, cfg.num_experts_per_tok, cfg.router_mode, cfg.norm_topk_prob)
         return w.float(), idx
 
     def _moe(self, L, h):
@@ -333,6 +328,30 @@ class DecoderLM:
         if return_hidden:
             return h
         return self._final_logits(h)
+
+    # ------------------------------------------------------------------ decode step -> tokens
+    def enable_fused_tp(self, max_rows: int):
+        """Use the fused symmetric-memory collectives for decode steps of up
+        to `max_rows` rows (tensor parallel only)."""
+        if self.tp.world > 1:
+            from ..parallel.tp_fused import FusedTP
+
+            self.tp_fused = FusedTP(self, max_rows)
+        return self
+
+    def begin_step(self):
+        """Advance the collective step counter (every rank, once per decode step)."""
+        if getattr(self, "tp_fused", None) is not None:
+            self.tp_fused.comm.begin_step()
+
+    def forward_decode_tokens(self, fb: ForwardBatch, kv, out: torch.Tensor, out2=None):
+        """Greedy tokens of a pure-decode batch: the fused TP path when
+        enabled, else forward + argmax."""
+        tpf = getattr(self, "tp_fused", None)
+        if tpf is not None and fb.num_decode == fb.num_tokens and fb.num_tokens <= tpf.M_pad:
+            return tpf.decode_tokens(fb, kv, out, out2)
+        logits = self.forward(fb, kv)
+        return ops.argmax(logits, out=out, out2=out2)
 
     # ------------------------------------------------------------------ dense forward
     def new_cache(self) -> DenseKVCache:

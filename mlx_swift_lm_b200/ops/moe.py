@@ -1,10 +1,21 @@
-"""MoE expert computation (sort tokens by expert -> per-expert GLU MLP ->
-weighted un-sort), the SwitchGLU of MLXLMCommon/SwitchLayers.swift:478
-(gatherSort :244, scatterUnsort :257, weightedExpertUnsort :149).
+"""MoE routing and expert computation: router top-k, sort tokens by expert,
+per-expert GLU MLP, weighted un-sort. Parity: MLXLMCommon/MoERouterTopK.swift:22
+(router top-k, ties to the lower expert id) and the SwitchGLU of
+MLXLMCommon/SwitchLayers.swift:478 (gatherSort :244, scatterUnsort :257,
+weightedExpertUnsort :149).
 
-On CUDA the grouped path runs the fused grouped-GEMM kernels of
-``csrc/kernels/moe.cu`` when they are built in; otherwise each expert's rows go
-through the dense tcgen05 GEMM.
+On CUDA every step runs on the kernels of ``csrc/kernels/moe.cu`` with no host
+synchronisation (so the MoE layer captures into the decode CUDA graph):
+
+    route_topk   warp-per-token softmax/top-k
+    sort         stable counting sort of the T*k (token, expert) pairs plus a
+                 device work list of (expert, first row, rows <= BN) chunks
+    gather       activation rows in expert order
+    grouped GEMM tcgen05 tiles over (weight tile, chunk); the gate/up GEMM
+                 applies the GLU in its epilogue, the down GEMM adds the bias
+    combine      out[t] = sum_j w[t, j] * y[pos(t, j)] in slot order j
+
+CPU tensors take the plain PyTorch path (used by the CPU test suite).
 """
 from __future__ import annotations
 
@@ -13,10 +24,38 @@ import torch
 from . import _lib
 from .linear import gemm
 
+_EPI = {"none": 0, "swiglu": 1, "geglu": 4, "swiglu_oai": 5}
+
+_lib.register_signatures({
+    "b200_moe_route_topk": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp,
+                                       _lib.vp]),
+    "b200_moe_sort": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.vp,
+                                 _lib.vp, _lib.vp]),
+    "b200_moe_gather": (_lib.i32, [_lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.vp]),
+    "b200_moe_combine": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.vp,
+                                    _lib.vp, _lib.vp]),
+    "b200_moe_grouped_gemm": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.vp,
+                                         _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.i32, _lib.i32,
+                                         _lib.vp]),
+}, status_tags=("moe",))
+
 
 def route_topk(logits: torch.Tensor, k: int, mode: str = "softmax_topk", norm_topk: bool = True):
-    """Router top-k. softmax_topk: softmax over experts then top-k (optionally
-    renormalised); topk_softmax: top-k logits then softmax over the k."""
+    """Router top-k over fp32 logits [T, E]. softmax_topk: softmax over experts
+    then top-k (optionally renormalised); topk_softmax: top-k logits then
+    softmax over the k. Returns (weights [T, k] fp32, ids [T, k] int32 on CUDA,
+    int64 on CPU)."""
+    T, E = logits.shape
+    if logits.is_cuda:
+        assert E <= 256 and k <= 16, "router kernel supports up to 256 experts and k <= 16"
+        lg = logits.float().contiguous()
+        ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+        w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+        _lib.check(_lib.lib().b200_moe_route_topk(lg.data_ptr(), T, E, k, 1 if mode == "topk_softmax" else 0,
+                                                  1 if norm_topk else 0, ids.data_ptr(), w.data_ptr(),
+                                                  _lib.stream_ptr(logits.device)), "moe_route_topk")
+        _lib.count(1)
+        return w, ids
     if mode == "topk_softmax":
         v, idx = torch.topk(logits.float(), k, dim=-1)
         return torch.softmax(v, dim=-1), idx
@@ -27,12 +66,63 @@ def route_topk(logits: torch.Tensor, k: int, mode: str = "softmax_topk", norm_to
     return w, idx
 
 
+def chunk_rows(P: int, E: int) -> int:
+    """Row cap of one grouped-GEMM chunk: the smallest tile width that holds the
+    average rows per expert (a function of the shape only, so it is fixed per
+    captured graph)."""
+    avg = (P + E - 1) // max(E, 1)
+    for bn in (16, 32, 64):
+        if avg <= bn:
+            return bn
+    return 128
+
+
+def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias):
+    T, K = h.shape
+    k = idx.shape[1]
+    E, N2, _ = experts_gu.shape
+    F = experts_d.shape[2]
+    assert N2 == 2 * F and N2 % 128 == 0, "gate/up rows must be 2*F, a multiple of 128 (64-row interleave)"
+    P = T * k
+    dev = h.device
+    BN = chunk_rows(P, E)
+    max_chunks = (P + BN - 1) // BN + E
+    ids = idx.to(torch.int32).contiguous()
+    w = w.float().contiguous()
+    perm = torch.empty(P, dtype=torch.int32, device=dev)
+    pos = torch.empty(P, dtype=torch.int32, device=dev)
+    chunks = torch.empty(max_chunks * 3, dtype=torch.int32, device=dev)
+    n_chunks = torch.empty(1, dtype=torch.int32, device=dev)
+    xs = torch.empty(P, K, dtype=h.dtype, device=dev)
+    gu = torch.empty(P, F, dtype=h.dtype, device=dev)
+    ys = torch.empty(P, K, dtype=h.dtype, device=dev)
+    out = torch.empty(T, K, dtype=h.dtype, device=dev)
+    L = _lib.lib()
+    st = _lib.stream_ptr(dev)
+    hc = h.contiguous()
+    _lib.check(L.b200_moe_sort(ids.data_ptr(), P, E, BN, max_chunks, perm.data_ptr(), pos.data_ptr(),
+                               chunks.data_ptr(), n_chunks.data_ptr(), st), "moe_sort")
+    _lib.check(L.b200_moe_gather(hc.data_ptr(), K, perm.data_ptr(), P, k, xs.data_ptr(), st), "moe_gather")
+    _lib.check(L.b200_moe_grouped_gemm(xs.data_ptr(), P, K, experts_gu.data_ptr(), E, N2, gu.data_ptr(), F,
+                                       _lib.ptr(gu_bias), _EPI[epi], chunks.data_ptr(), n_chunks.data_ptr(),
+                                       max_chunks, BN, st), "moe_grouped_gemm gate/up")
+    _lib.check(L.b200_moe_grouped_gemm(gu.data_ptr(), P, F, experts_d.data_ptr(), E, K, ys.data_ptr(), K,
+                                       _lib.ptr(d_bias), 0, chunks.data_ptr(), n_chunks.data_ptr(), max_chunks, BN,
+                                       st), "moe_grouped_gemm down")
+    _lib.check(L.b200_moe_combine(ys.data_ptr(), T, K, pos.data_ptr(), w.data_ptr(), k, out.data_ptr(), None, None,
+                                  st), "moe_combine")
+    _lib.count(5)
+    return out
+
+
 def moe_experts(h, experts_gu, experts_d, w, idx, epi="swiglu", gu_bias=None, d_bias=None):
     """h [T, K]; experts_gu [E, 2F, K] (64-row interleaved gate/up); experts_d [E, K, F];
     w [T, k] fp32 weights; idx [T, k] expert ids. Returns [T, K] in h.dtype."""
+    if h.is_cuda:
+        return _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias)
     T, K = h.shape
     k = idx.shape[1]
-    flat = idx.reshape(-1)
+    flat = idx.reshape(-1).long()
     order = torch.argsort(flat, stable=True)
     tok = order // k
     wsorted = w.reshape(-1)[order]
@@ -49,6 +139,3 @@ def moe_experts(h, experts_gu, experts_d, w, idx, epi="swiglu", gu_bias=None, d_
         out.index_add_(0, rows, y.float() * wsorted[start:start + c, None])
         start += c
     return out.to(h.dtype)
-
-
-_ = _lib  # kernels registered by moe.cu bindings when present

@@ -1,0 +1,92 @@
+"""Tensor parallelism on 2 GPUs: the fused symmetric-memory decode path and
+the NCCL path produce the single-GPU tokens. Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.dist]
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, mode, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        from mlx_swift_lm_b200 import DecoderLM, EngineConfig, EngineV2, SchedulerConfig
+        from mlx_swift_lm_b200.models.config import tiny_qwen3
+        from mlx_swift_lm_b200.models.decoder import TensorParallel
+
+        cfg = tiny_qwen3()
+        m = DecoderLM(cfg, dev, torch.bfloat16, tp=TensorParallel(rank, world, dist.group.WORLD)).init_random(
+            5, std=0.2)
+        ok = True
+        if mode == "fused":
+            m.enable_fused_tp(8)
+            ok = m.tp_fused.comm.self_test()
+        eng = EngineV2(m, config=EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=8),
+                                              max_model_len=256, graph_buckets=(1, 2, 4, 8)))
+        g = torch.Generator().manual_seed(1)
+        prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (20, 7, 33)]
+        out = eng.generate(prompts, max_tokens=12)
+        from mlx_swift_lm_b200.ops import _lib
+
+        st = _lib.read_status()
+        if rank == 0:
+            q.put((out, ok, st))
+        if m.tp_fused is not None:
+            eng.graphs.graphs.clear()
+            torch.cuda.synchronize()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = q.get(timeout=600)
+    for p in ps:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in ps)
+    return res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_fused_and_nccl_match_single_gpu():
+    from mlx_swift_lm_b200 import DecoderLM, EngineConfig, EngineV2, SchedulerConfig
+    from mlx_swift_lm_b200.models.config import tiny_qwen3
+
+    cfg = tiny_qwen3()
+    m = DecoderLM(cfg, torch.device("cuda", 0), torch.bfloat16).init_random(5, std=0.2)
+    eng = EngineV2(m, config=EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=8), max_model_len=256,
+                                          graph_buckets=(1, 2, 4, 8)))
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (20, 7, 33)]
+    ref = eng.generate(prompts, max_tokens=12)
+    fused, ok, st = _run("fused")
+    assert ok, "symmetric-memory signal round trip failed"
+    assert all(v == 0 for v in st.values()), st
+    nccl, _, _ = _run("nccl")
+    agree_f = sum(a == b for x, y in zip(fused, ref) for a, b in zip(x, y)) / 36
+    agree_n = sum(a == b for x, y in zip(nccl, ref) for a, b in zip(x, y)) / 36
+    assert agree_f >= 0.75 and agree_n >= 0.75, (fused, nccl, ref)
