@@ -255,8 +255,21 @@ def main():
             "kernel_status": status,
         }
         print(json.dumps(out))
+    # release every CUDA graph (they may hold NCCL work) and the peer mappings
+    # before the process group goes away; otherwise the exit can wait forever
+    del graph
     eng.graphs.graphs.clear()
+    eng.graphs.pool = None
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize(dev)
     if world > 1:
+        dist.barrier()
+        if getattr(model, "tp_fused", None) is not None:
+            model.tp_fused.comm.close()
+            model.tp_fused = None
+        torch.cuda.synchronize(dev)
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -49,9 +49,20 @@ def _worker(rank, world, port, mode, q):
         st = _lib.read_status()
         if rank == 0:
             q.put((out, ok, st))
-        if m.tp_fused is not None:
+        # graphs may hold NCCL work and peer addresses: release them, then the
+        # peer mappings, before the process group goes away
+        if eng.graphs is not None:
             eng.graphs.graphs.clear()
-            torch.cuda.synchronize()
+            eng.graphs.pool = None
+        import gc
+
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.barrier()
+        if m.tp_fused is not None:
+            m.tp_fused.comm.close()
+            m.tp_fused = None
+        torch.cuda.synchronize()
         dist.barrier()
     finally:
         dist.destroy_process_group()
