@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(128, 1) grouped_kernel(const __grid_constant__
   const int rl = warp * 32 + lane;
   const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
   const bool isglu = a.epi == 1 || a.epi == 4 || a.epi == 5;
-  const float bb = a.bias ? bf2f(a.bias[(size_t)e * a.N + n0 + rl]) : 0.f;
+  const float bb = (a.bias && n0 + rl < a.N) ? bf2f(a.bias[(size_t)e * a.N + n0 + rl]) : 0.f;
   for (int jc = 0; jc < BN; jc += 16) {
     uint32_t v[16];
     tmem_ld16(tl + jc, v);
