@@ -677,3 +677,90 @@ int b200_paged_decode(const void* q, const void* k_cache, const void* v_cache, i
 }  // extern "C"
 
 B200_STATUS_ACCESSORS(attn_decode)
+
+// ---------------------------------------------------------------------------
+// Variant of b200_paged_decode whose scratch is compiled into the library; it
+// allocates no device memory. Contract, size limit and concurrency rules are
+// in attention_decode_noalloc.h.
+#include <mutex>
+
+#include "attention_decode_noalloc.h"
+
+namespace {
+
+static __device__ __align__(256) float g_decode_noalloc_scratch[B200_DECODE_NOALLOC_SCRATCH_FLOATS];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of this device's scratch array; looked up once per device,
+// with that device current, by the first call made on it.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return -1;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+    if (e != cudaSuccess) return (int)e;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int b200_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, int kv_fp8,
+                                         const float* k_scale, const float* v_scale, const int* page_table,
+                                         int ld_pt, const int* seq_lens, const float* sinks, void* out, int B, int H,
+                                         int KVH, int D, int max_parts, int window, float scale, float softcap,
+                                         int64_t num_pages, cudaStream_t st) {
+  if (B <= 0) return 0;
+  if (H <= 0 || KVH <= 0 || H % KVH || max_parts <= 0) return -1;
+  if (D != 64 && D != 128 && D != 256) return -1;
+  const int64_t slots = (int64_t)B * H * max_parts;
+  const int64_t acc_floats = (slots * D + 63) / 64 * 64;  // keeps part_ml on a 256-byte boundary
+  if (acc_floats + slots * 2 > (int64_t)B200_DECODE_NOALLOC_SCRATCH_FLOATS) return B200_DECODE_NOALLOC_TOO_LARGE;
+  float* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != 0) return rc;
+  float* part_acc = scratch;
+  float* part_ml = scratch + acc_floats;
+  DecodeArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.page_table = page_table;
+  a.seq_lens = seq_lens;
+  a.sinks = sinks;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.part_acc = part_acc;
+  a.part_ml = part_ml;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.H = H;
+  a.KVH = KVH;
+  a.ld_pt = ld_pt;
+  a.max_parts = max_parts;
+  a.window = window;
+  a.num_pages = num_pages;
+  a.scale = scale;
+  a.softcap = softcap;
+  const int G = H / KVH;
+  if (kv_fp8) {
+    switch (D) {
+      case 64: return dispatch_g<64, uint8_t>(a, B, G, st);
+      case 128: return dispatch_g<128, uint8_t>(a, B, G, st);
+      default: return dispatch_g<256, uint8_t>(a, B, G, st);
+    }
+  }
+  switch (D) {
+    case 64: return dispatch_g<64, __nv_bfloat16>(a, B, G, st);
+    case 128: return dispatch_g<128, __nv_bfloat16>(a, B, G, st);
+    default: return dispatch_g<256, __nv_bfloat16>(a, B, G, st);
+  }
+}
