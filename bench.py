@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--out-tokens", type=int, default=256)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
+    ap.add_argument("--tp-mode", default="nccl", choices=["fused", "nccl"],
                     help="tensor-parallel collectives: fused symmetric-memory kernels or NCCL all-reduce")
     return ap.parse_args()
 

@@ -5,8 +5,10 @@
 //   [pads]   kNumPads x kMaxRanks uint32 flags; flag(pad, src) on the owner's
 //            buffer is written by rank `src` with release semantics
 //   [recv]   2 x world x rows_per_rank x hidden fp32 - reduce-scatter inboxes
-//   [h]      2 x rows_per_rank x hidden bf16 - rows this rank publishes for
-//            the all-gather that feeds the next column-parallel GEMM
+//   [h]      2 x (world * rows_per_rank) x hidden bf16 - the gathered
+//            normalised rows feeding the next column-parallel GEMM; every
+//            rank pushes its own rows into every rank's copy (NVLink stores),
+//            so the GEMM's TMA reads local memory only
 //   [xarg]   2 x world x rows x {float value, int index} - split-argmax inbox
 // Parity (2 slots) alternates by phase so a writer can never overwrite data
 // its reader has not consumed: a rank reaches phase p+2 only after every peer
@@ -54,9 +56,12 @@ struct CommCtx {
     float* r = reinterpret_cast<float*>(base[owner] + recv_off);
     return r + (((size_t)parity * world + src) * rows_per_rank + lrow) * hidden;
   }
-  __device__ __forceinline__ __nv_bfloat16* h_row(int owner, int parity, int lrow) const {
+  // normalised row `grow` (global row index 0..world*rpr-1) in the gathered
+  // buffer [2][world*rpr][hidden] of `owner`; every rank pushes its rows into
+  // every rank's buffer, so the all-gather GEMM reads local memory only
+  __device__ __forceinline__ __nv_bfloat16* h_row(int owner, int parity, int grow) const {
     __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(base[owner] + h_off);
-    return h + ((size_t)parity * rows_per_rank + lrow) * hidden;
+    return h + ((size_t)parity * world * rows_per_rank + grow) * hidden;
   }
   __device__ __forceinline__ float2* xarg(int owner, int parity, int src) const {
     float2* x = reinterpret_cast<float2*>(base[owner] + xarg_off);

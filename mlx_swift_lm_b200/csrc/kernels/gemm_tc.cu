@@ -67,17 +67,26 @@ struct GemmArgs {
   unsigned long long* trace;  // optional [ctas][6] %globaltimer stamps (diagnostics), null in production
 };
 
-template <int BN, int STAGES>
+// Shared-memory plan of one CTA. Per stage: the bf16 weight tile A (TMA, or
+// written by the dequantising warps when WQ > 0), the activation tile B, and
+// for quantised weights the raw tile (codes [128][WQ*8 bytes], then scales and
+// biases [groups][128] bf16).
+template <int BN, int STAGES, int WQ = 0>
 struct GemmSmem {
   static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
   static constexpr int kBBytes = BN * 128;   // BN rows x 64 bf16
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kCodeBytes = WQ * 128 * 64 / 8;
+  static constexpr int kGroupBytes = 2 * 128 * 2;  // up to 2 groups x 128 rows x bf16
+  static constexpr int kRawBytes = WQ ? kCodeBytes + 2 * kGroupBytes : 0;
+  static constexpr int kStageBytes = (kABytes + kBBytes + kRawBytes + 1023) / 1024 * 1024;
   static constexpr int kPipeBytes = STAGES * kStageBytes;
   static constexpr int kPartBytes = BN * 128 * 4;  // fp32 partial [BN][128]
   static constexpr int kMain = kPipeBytes > kPartBytes ? kPipeBytes : kPartBytes;
   static constexpr int kBarOffset = kMain;
-  static constexpr int kTotal = kBarOffset + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int kNumBars = (WQ ? 3 : 2) * STAGES + 1;
+  static constexpr int kTotal = kBarOffset + kNumBars * 8 + 16 + 1024;  // + alignment slack
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kThreads = WQ ? 256 : 128;
 };
 
 __device__ __forceinline__ void cluster_sync() {
@@ -99,24 +108,46 @@ enum GemmMode : int {
 };
 
 struct CollArgs {
-  CUtensorMap peer_x[2 * kMaxRanks];  // AG: [parity][rank] maps over each rank's published rows
+  CUtensorMap peer_x[2 * kMaxRanks];  // AG: [parity] maps over this rank's gathered rows (entries 0, 1)
   CommCtx comm;
   int phase;   // collective phase index within the step (epoch = step * kPhasesPerStep + phase + 1)
   int parity;  // buffer slot of this call
 };
 
-template <int BN, int STAGES, int MODE>
-__global__ void __launch_bounds__(128, 1)
+// Affine-quantised weights (WQ bits per code): w = scale[g] * q + bias[g] per
+// group of `gs` inputs. codes: [N, K*WQ/8] bytes (4-bit words repacked so that
+// nibble j of the low half-word and nibble j of the high half-word hold inputs
+// 2j and 2j+1 of the word's 8); scales / biases: [K/gs, N] bf16.
+struct QArgs {
+  CUtensorMap codes, scales, biases;
+  int gs;
+};
+
+// bf16 pair (q_lo + 128, q_hi + 128) from two 4-bit codes placed at bits 0..3
+// and 16..19 of v (exact: 128..143 are bf16 integers), minus 128, then
+// scale * q + bias with one rounding.
+__device__ __forceinline__ uint32_t dq4_pair(uint32_t v, __nv_bfloat162 s2, __nv_bfloat162 b2) {
+  const uint32_t x = (v & 0x000F000Fu) | 0x43004300u;
+  const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
+  const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&x), c128);
+  const __nv_bfloat162 w = __hfma2(q, s2, b2);
+  return *reinterpret_cast<const uint32_t*>(&w);
+}
+
+template <int BN, int STAGES, int MODE, int WQ>
+__global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                        GemmArgs args, const __grid_constant__ CollArgs coll) {
-  using S = GemmSmem<BN, STAGES>;
+                        GemmArgs args, const __grid_constant__ CollArgs coll, const __grid_constant__ QArgs qa) {
+  using S = GemmSmem<BN, STAGES, WQ>;
+  constexpr int kThreads = S::kThreads;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar_full = sbase + S::kBarOffset;
   const uint32_t bar_empty = bar_full + STAGES * 8;
   const uint32_t bar_accum = bar_empty + STAGES * 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kBarOffset + (2 * STAGES + 1) * 8);
+  const uint32_t bar_aready = bar_accum + 8;  // [STAGES], quantised weights only
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kBarOffset + S::kNumBars * 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * 128;
@@ -131,11 +162,12 @@ __global__ void __launch_bounds__(128, 1)
       args.trace ? args.trace + 6 * (blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)) : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = globaltimer();
   if (threadIdx.x == 0) {
-    tma_prefetch_desc(&tmW);
+    if constexpr (WQ == 0) tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
+      if constexpr (WQ != 0) mbar_init(bar_aready + 8 * s, 4);  // one arrive per dequantising warp
     }
     mbar_init(bar_accum, 1);
     fence_barrier_init();
@@ -154,24 +186,37 @@ __global__ void __launch_bounds__(128, 1)
     // ---------------- TMA producer ----------------
     const uint64_t pol_w = l2_policy_evict_first();
     const uint64_t pol_x = l2_policy_evict_last();
+    // quantised: groups covered by one 64-input K block (1 or 2), and the bytes
+    // one stage receives from TMA
+    const int gpb = WQ ? (qa.gs >= 64 ? 1 : 64 / qa.gs) : 0;
+    const uint32_t stage_tx =
+        WQ ? (uint32_t)(S::kBBytes + S::kCodeBytes + 2 * gpb * 128 * 2) : (uint32_t)(S::kABytes + S::kBBytes);
+    auto load_w = [&](uint32_t a, uint32_t bar, int kb) {
+      if constexpr (WQ == 0) {
+        tma_load_2d(a, &tmW, bar, kb * 64, n0, pol_w);
+      } else {
+        const uint32_t raw = a + S::kABytes + S::kBBytes;
+        tma_load_2d(raw, &qa.codes, bar, kb * WQ * 8, n0, pol_w);
+        const int g0 = qa.gs >= 64 ? (kb * 64) / qa.gs : kb * gpb;
+        tma_load_2d(raw + S::kCodeBytes, &qa.scales, bar, n0, g0, pol_w);
+        tma_load_2d(raw + S::kCodeBytes + S::kGroupBytes, &qa.biases, bar, n0, g0, pol_w);
+      }
+    };
     // Weights are written by no kernel: the first STAGES weight tiles are
     // requested before waiting on the previous kernel (PDL), so their HBM
     // latency overlaps the predecessor's tail.
     const int pre = min(STAGES, nkb);
     for (int i = 0; i < pre; ++i) {
       const uint32_t a = sbase + i * S::kStageBytes;
-      mbar_arrive_expect_tx(bar_full + 8 * i, S::kStageBytes);
-      tma_load_2d(a, &tmW, bar_full + 8 * i, (kb_begin + i) * 64, n0, pol_w);
+      mbar_arrive_expect_tx(bar_full + 8 * i, stage_tx);
+      load_w(a, bar_full + 8 * i, kb_begin + i);
     }
     pdl_wait();
-    // Activation tile: local TMA, or (all-gather mode) one TMA box per rank,
-    // fetched straight from that rank's published rows over NVLink into this
-    // CTA's own shared memory (plain tiled loads).
+    // Activation tile: local TMA; in all-gather mode from the gathered buffer
+    // that every rank's combine kernel has pushed its rows into (local).
     auto load_x = [&](uint32_t b, uint32_t bar, int kc) {
       if constexpr (MODE == kModeAG) {
-        const int rpr = coll.comm.rows_per_rank;
-        for (int j = 0; j < coll.comm.world; ++j)
-          tma_load_2d(b + j * rpr * 128, &coll.peer_x[coll.parity * kMaxRanks + j], bar, kc, 0, pol_x);
+        tma_load_2d(b, &coll.peer_x[coll.parity], bar, kc, 0, pol_x);
       } else {
         tma_load_2d(b, &tmX, bar, kc, m0, pol_x);
       }
@@ -189,9 +234,9 @@ __global__ void __launch_bounds__(128, 1)
       if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
       const uint32_t a = sbase + s * S::kStageBytes;
       const uint32_t b = a + S::kABytes;
-      mbar_arrive_expect_tx(bar_full + 8 * s, S::kStageBytes);
+      mbar_arrive_expect_tx(bar_full + 8 * s, stage_tx);
       const int kc = (kb_begin + i) * 64;
-      tma_load_2d(a, &tmW, bar_full + 8 * s, kc, n0, pol_w);
+      load_w(a, bar_full + 8 * s, kb_begin + i);
       load_x(b, bar_full + 8 * s, kc);
       issued = i + 1;
     }
@@ -204,6 +249,9 @@ __global__ void __launch_bounds__(128, 1)
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
+      if constexpr (WQ != 0) {
+        if (!mbar_wait(bar_aready + 8 * s, r & 1, kErrGemmWait)) break;
+      }
       if (trace && i == 0) trace[2] = globaltimer();
       tc_fence_after();
       const uint32_t a = sbase + s * S::kStageBytes;
@@ -215,6 +263,65 @@ __global__ void __launch_bounds__(128, 1)
       tc_commit(bar_empty + 8 * s);
     }
     tc_commit(bar_accum);
+  } else if (warp >= 4) {
+   if constexpr (WQ != 0) {
+    // ---------------- dequantising warps: raw tile -> bf16 A tile ----------------
+    // thread t owns weight row t; writes its 128-byte row with the 128B swizzle
+    // the MMA descriptor expects (16-byte chunk c lands at c ^ (t & 7)).
+    const int t = threadIdx.x - 128;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES, r = i / STAGES;
+      if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
+      uint8_t* stage = smem + s * S::kStageBytes;
+      const uint8_t* raw = stage + S::kABytes + S::kBBytes;
+      const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(raw + S::kCodeBytes);
+      const __nv_bfloat16* bi = reinterpret_cast<const __nv_bfloat16*>(raw + S::kCodeBytes + S::kGroupBytes);
+      uint8_t* arow = stage + t * 128;
+      if constexpr (WQ == 4) {
+        const uint4* cw = reinterpret_cast<const uint4*>(raw + t * 32);
+        const uint4 c0 = cw[0], c1 = cw[1];
+        const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const int g = qa.gs == 32 ? (w >> 2) : 0;
+          const __nv_bfloat16 sv = sc[g * 128 + t], bv = bi[g * 128 + t];
+          const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv), b2 = __halves2bfloat162(bv, bv);
+          const uint32_t v = words[w];
+          uint4 o;
+          o.x = dq4_pair(v, s2, b2);
+          o.y = dq4_pair(v >> 4, s2, b2);
+          o.z = dq4_pair(v >> 8, s2, b2);
+          o.w = dq4_pair(v >> 12, s2, b2);
+          *reinterpret_cast<uint4*>(arow + ((w ^ (t & 7)) << 4)) = o;
+        }
+      } else {
+        const uint4* cw = reinterpret_cast<const uint4*>(raw + t * 64);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 q4 = cw[c];
+          const uint32_t words[4] = {q4.x, q4.y, q4.z, q4.w};
+          const int g = qa.gs == 32 ? (c >> 1) : 0;
+          const float sv = bf2f(sc[g * 128 + t]), bv = bf2f(bi[g * 128 + t]);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const uint32_t v = words[2 * h + e];
+              o[2 * e] = pack_bf16x2(fmaf((float)(v & 0xFF), sv, bv), fmaf((float)((v >> 8) & 0xFF), sv, bv));
+              o[2 * e + 1] = pack_bf16x2(fmaf((float)((v >> 16) & 0xFF), sv, bv), fmaf((float)(v >> 24), sv, bv));
+            }
+            const int chunk = 2 * c + h;
+            *reinterpret_cast<uint4*>(arow + ((chunk ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+      }
+      // generic-proxy smem writes -> visible to the tensor core (async proxy)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_aready + 8 * s);
+    }
+   }
   }
   __syncwarp();
 
@@ -227,7 +334,7 @@ __global__ void __launch_bounds__(128, 1)
   if (trace && threadIdx.x == 0) trace[3] = globaltimer();
   const int r = warp * 32 + lane;  // TMEM lane == weight row within the tile
   float* part = reinterpret_cast<float*>(smem);
-  {
+  if (warp < 4) {
     const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
     for (int jc = 0; jc < BN; jc += 16) {
@@ -276,6 +383,7 @@ __global__ void __launch_bounds__(128, 1)
   if (glu) {
     // 16 threads per token column (64 gate rows as 16 float4), 8 columns per pass
     const int jj = threadIdx.x >> 4, f4 = threadIdx.x & 15;
+    constexpr int kColsPerPass = kThreads / 16;
     __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(args.Y);
     float bg[4], bu[4];
 #pragma unroll
@@ -283,7 +391,7 @@ __global__ void __launch_bounds__(128, 1)
       bg[e] = args.bias ? bf2f(args.bias[n0 + f4 * 4 + e]) : 0.f;
       bu[e] = args.bias ? bf2f(args.bias[n0 + 64 + f4 * 4 + e]) : 0.f;
     }
-    for (int j = j_lo + jj; j < j_hi; j += 8) {
+    for (int j = j_lo + jj; j < j_hi; j += kColsPerPass) {
       const float4 g4 = red4(j, f4), u4 = red4(j, f4 + 16);
       const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
       __nv_bfloat16 o[4];
@@ -308,11 +416,12 @@ __global__ void __launch_bounds__(128, 1)
   } else {
     // 32 threads per token column (128 rows as 32 float4), 4 columns per pass
     const int jj = threadIdx.x >> 5, r4 = threadIdx.x & 31;
+    constexpr int kColsPerPass = kThreads / 32;
     const int n = n0 + r4 * 4;
     float bb[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) bb[e] = (args.bias && n + e < args.N) ? bf2f(args.bias[n + e]) : 0.f;
-    for (int j = j_lo + jj; j < j_hi; j += 4) {
+    for (int j = j_lo + jj; j < j_hi; j += kColsPerPass) {
       const float4 v4 = red4(j, r4);
       const float v[4] = {v4.x + bb[0], v4.y + bb[1], v4.z + bb[2], v4.w + bb[3]};
       const size_t m = (size_t)(m0 + j);
@@ -407,13 +516,13 @@ struct TmKeyHash {
   }
 };
 
-// 2-D row-major tensor map with a 128-byte swizzle: box = box_rows x box_cols.
-// Returns false if the driver rejects the layout.
-bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows,
-                  int box_cols, int dtype_bytes) {
+// 2-D row-major tensor map, box = box_rows x box_cols, 128-byte swizzle or
+// none. Returns false if the driver rejects the layout.
+bool make_tmap_2d_sw(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows,
+                     int box_cols, int dtype_bytes, bool swizzle128) {
   static std::mutex mu;
   static std::unordered_map<TmKey, CUtensorMap, TmKeyHash> cache;
-  TmKey key{(uintptr_t)ptr, rows, cols, ld_elems, box_rows, box_cols, dtype_bytes};
+  TmKey key{(uintptr_t)ptr, rows, cols, ld_elems, box_rows, box_cols, dtype_bytes * (swizzle128 ? 1 : 16)};
   {
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find(key);
@@ -432,8 +541,8 @@ bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols,
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estride[2] = {1, 1};
   CUresult r = enc(out, dt, 2, const_cast<void*>(ptr), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   std::lock_guard<std::mutex> g(mu);
   if (cache.size() > 8192) cache.clear();
@@ -441,21 +550,51 @@ bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols,
   return true;
 }
 
-template <int BN, int STAGES, int MODE>
+// 2-D row-major tensor map with a 128-byte swizzle: box = box_rows x box_cols.
+bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows,
+                  int box_cols, int dtype_bytes) {
+  return make_tmap_2d_sw(out, ptr, rows, cols, ld_elems, box_rows, box_cols, dtype_bytes, true);
+}
+
+static const QArgs& no_quant() {
+  static QArgs q = {};
+  return q;
+}
+static const CollArgs& local_coll_q() {
+  static CollArgs c = {};
+  return c;
+}
+
+template <int BN, int STAGES, int MODE, int WQ = 0>
 static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, const CollArgs& coll,
-                       int tiles_n, int tiles_m, cudaStream_t st) {
-  using S = GemmSmem<BN, STAGES>;
+                       int tiles_n, int tiles_m, cudaStream_t st, const QArgs& q = no_quant()) {
+  using S = GemmSmem<BN, STAGES, WQ>;
+  static_assert(S::kTotal <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES, MODE>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
     if (e != cudaSuccess) return (int)e;
     configured = true;
   }
-  cudaError_t e = launch_k(gemm_bf16_tc_kernel<BN, STAGES, MODE>, dim3(tiles_n, tiles_m, a.ksplit),
-                           dim3(128, 1, 1), S::kTotal, st, a.ksplit, tw, tx, a, coll);
+  cudaError_t e = launch_k(gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ>, dim3(tiles_n, tiles_m, a.ksplit),
+                           dim3(S::kThreads, 1, 1), S::kTotal, st, a.ksplit, tw, tx, a, coll, q);
   if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
+}
+
+template <int WQ>
+static int launch_bn_q(int BN, const CUtensorMap& tx, const GemmArgs& a, const QArgs& q, int tiles_n, int tiles_m,
+                       cudaStream_t st) {
+  const CollArgs& c = local_coll_q();
+  switch (BN) {
+    case 16: return launch_gemm<16, 8, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 32: return launch_gemm<32, 7, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 64: return launch_gemm<64, 6, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 128: return launch_gemm<128, 5, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 256: return launch_gemm<256, 3, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    default: return -1;
+  }
 }
 
 template <int MODE>
@@ -483,10 +622,10 @@ static const CollArgs& local_coll() {
 // Powers of two only (clusters of 2/4/8 pack into GPCs without stranding
 // slots), the largest that keeps the grid within one wave of ~90% of the
 // 2-per-SM CTA slots and at least 8 K blocks per split.
-static int choose_splits(int N, int K, int num_sms) {
+static int choose_splits(int N, int K, int num_sms, int ctas_per_sm = 2) {
   const int kb = (K + 63) / 64;
   const int tiles = (N + 127) / 128;
-  const long budget = (long)(0.9 * 2 * num_sms);
+  const long budget = (long)(0.9 * ctas_per_sm * num_sms);
   int s = 1;
   while (s < 8 && (long)tiles * (s * 2) <= budget && (kb + 2 * s - 1) / (2 * s) >= 8) s *= 2;
   // the last split must own at least one K block
@@ -546,6 +685,55 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   return launch_bn<kModeLocal>(BN, tw, tx, a, local_coll(), tiles_n, tiles_m, stream);
 }
 
+// Y[M, :] = epi(X[M, K] . dequant(W)^T + bias) with affine-quantised W
+// (bits 4 or 8): codes [N, K*bits/8] bytes (4-bit words in the repacked
+// nibble order of QArgs), scales_t / biases_t [K/gs, N] bf16, gs in {32, 64, 128}.
+// The weight tile is dequantised in shared memory by four extra warps and fed
+// to the same tcgen05 pipeline and epilogues as b200_gemm_bf16 (one CTA per
+// SM, so the split count budgets one CTA slot per SM).
+int b200_gemm_q(const void* X, int M, int K, int ldx, const void* codes, const void* scales_t, const void* biases_t,
+                int N, int bits, int gs, void* Y, int ldy, const void* R, int ldr, const void* bias, int epi,
+                int num_sms, int force_splits, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return 0;
+  if ((bits != 4 && bits != 8) || (gs != 32 && gs != 64 && gs != 128)) return -1;
+  if ((K % 128) || (ldx % 8) || ((uintptr_t)X & 15) || ((uintptr_t)codes & 15)) return -1;
+  if (((uintptr_t)scales_t & 15) || ((uintptr_t)biases_t & 15) || (N % 8)) return -1;
+  const bool glu = epi == kEpiSwiGLU || epi == kEpiGeGLU || epi == kEpiSwiGLUOAI;
+  if (glu && (N % 128)) return -1;
+  const int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  const int G = K / gs;
+  const int gpb = gs >= 64 ? 1 : 64 / gs;
+  QArgs q;
+  q.gs = gs;
+  CUtensorMap tx;
+  if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
+  const int64_t cb = (int64_t)K * bits / 8;
+  if (!make_tmap_2d_sw(&q.codes, codes, N, cb, cb, 128, bits * 8, 1, false)) return -1;
+  if (!make_tmap_2d_sw(&q.scales, scales_t, G, N, N, gpb, 128, 2, false)) return -1;
+  if (!make_tmap_2d_sw(&q.biases, biases_t, G, N, N, gpb, 128, 2, false)) return -1;
+  GemmArgs a = {};
+  a.Y = Y;
+  a.R = reinterpret_cast<const __nv_bfloat16*>(R);
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldy = ldy;
+  a.ldr = ldr;
+  a.epi = epi;
+  a.trace = g_gemm_trace;
+  a.kb_total = K / 64;
+  const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms, 1);
+  if (s > 8) return -1;
+  a.kb_per_split = (a.kb_total + s - 1) / s;
+  a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  const int tiles_n = (N + 127) / 128, tiles_m = (M + BN - 1) / BN;
+  return bits == 4 ? launch_bn_q<4>(BN, tx, a, q, tiles_n, tiles_m, stream)
+                   : launch_bn_q<8>(BN, tx, a, q, tiles_n, tiles_m, stream);
+}
+
+int b200_gemm_q_num_splits(int N, int K, int num_sms) { return choose_splits(N, K, num_sms, 1); }
+
 // ---------------------------------------------------------------------------
 // Fused collective GEMMs (tensor parallelism). `comm_ctx` is a CommCtx blob
 // (see b200_comm.cuh). Rows: M_pad = world * rows_per_rank, rank j owns rows
@@ -571,12 +759,10 @@ int b200_gemm_bf16_ag(const void* comm_ctx, int phase, int parity, int M_real, i
   if (glu && (N % 128)) return -1;
   CUtensorMap tw;
   if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
-  for (int p = 0; p < 2; ++p)
-    for (int j = 0; j < c.world; ++j) {
-      const uint8_t* rows = c.base[j] + c.h_off + (size_t)p * c.rows_per_rank * c.hidden * 2;
-      if (!make_tmap_2d(&coll->peer_x[p * kMaxRanks + j], rows, c.rows_per_rank, K, K, c.rows_per_rank, 64, 2))
-        return -1;
-    }
+  for (int p = 0; p < 2; ++p) {
+    const uint8_t* rows = c.base[c.rank] + c.h_off + (size_t)p * M * c.hidden * 2;
+    if (!make_tmap_2d(&coll->peer_x[p], rows, M, K, K, M, 64, 2)) return -1;
+  }
   GemmArgs a = {};
   a.Y = Y;
   a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);

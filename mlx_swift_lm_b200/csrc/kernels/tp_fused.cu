@@ -6,8 +6,8 @@
 //   gemm AG (gate_up) -> gemm RS (down) -> tp_combine_norm
 // tp_combine_norm sums the world fp32 partial rows of its inbox in rank order
 // (deterministic), rounds the sum to bf16 (the unsharded model's o_proj/down
-// output), adds it to the residual rows, applies RMSNorm and publishes the
-// normalised rows for the next all-gather, then signals every rank.
+// output), adds it to the residual rows, applies RMSNorm, pushes the
+// normalised rows into every rank's gathered buffer, then signals every rank.
 // These replace the reference's injected allSum / reduceScatter / allGather
 // closures (Gemma4TensorParallel.swift:196-236, GLM5NextTextModel.swift:455-498)
 // with one-pass kernels over peer memory.
@@ -61,12 +61,17 @@ __global__ void __launch_bounds__(256) tp_combine_norm_kernel(CommCtx c, int pha
   }
   ss = block_sum(ss, red);
   const float inv = rsqrtf(ss / (float)H + eps);
-  __nv_bfloat16* hrow = c.h_row(c.rank, parity_ag, lrow);
+  // push the normalised row into every rank's gathered buffer (own rank first)
+  const int grow = c.rank * c.rows_per_rank + lrow;
   for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
     __nv_bfloat16 o[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[e] = f2bf(rbuf[i + e] * inv * bf2f(w[i + e]));
-    *reinterpret_cast<uint2*>(hrow + i) = *reinterpret_cast<const uint2*>(o);
+    const uint2 v = *reinterpret_cast<const uint2*>(o);
+    for (int jj = 0; jj < c.world; ++jj) {
+      const int j = (c.rank + jj) % c.world;
+      *reinterpret_cast<uint2*>(c.h_row(j, parity_ag, grow) + i) = v;
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) last_cta_signal(c, kPadAG, c.epoch(phase_ag));

@@ -1,0 +1,214 @@
+"""Model conversion: write a :class:`DecoderLM` (or a converted checkpoint) as
+a Hugging Face / MLX directory, optionally quantising the linear layers in
+MLX's affine format.
+
+Parity: ModelConversion (MLXLMCommon/ModelConversion.swift,
+MLXLLM/ModelConversion.swift): load, optionally quantise
+(``quantization {group_size, bits, mode}`` in config.json with ``weight`` /
+``scales`` / ``biases`` per quantised linear), save shards plus config.
+
+The model's fused layouts are undone on export: q|k|v is split back into
+q_proj / k_proj / v_proj and the 64-row interleaved gate/up into gate_proj /
+up_proj, so any loader that reads HF names (including this one) accepts the
+result. Tensor-parallel shards cannot be exported (world 1 only).
+
+CLI (mlx_lm.convert style):
+    python -m mlx_swift_lm_b200.loader.convert --src DIR --dst DIR [--q-bits 4 --q-group-size 64] [--dtype bf16]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from ..models.families import FAMILIES
+from ..ops import quant
+from ..ops.qlinear import QuantizedWeight
+from ..ops.reference import deinterleave_gate_up
+from .safetensors import save_safetensors
+
+# names of the linears that quantisation covers (MLX quantises every Linear
+# whose input size divides the group size; embeddings too)
+_QUANTISABLE = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "lm_head",
+                "embed_tokens")
+
+
+def to_hf_config(cfg, quantization: dict | None = None) -> dict:
+    d = {"model_type": cfg.model_type, "vocab_size": cfg.vocab_size, "hidden_size": cfg.hidden_size,
+         "num_hidden_layers": cfg.num_layers, "num_attention_heads": cfg.num_heads,
+         "num_key_value_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
+         "intermediate_size": cfg.intermediate_size, "rms_norm_eps": cfg.rms_norm_eps, "rope_theta": cfg.rope_theta,
+         "max_position_embeddings": cfg.max_position_embeddings, "tie_word_embeddings": cfg.tie_word_embeddings,
+         "attention_bias": cfg.attention_bias, "mlp_bias": cfg.mlp_bias, "hidden_act": "silu"}
+    if cfg.rope_scaling:
+        d["rope_scaling"] = cfg.rope_scaling
+    if cfg.partial_rotary_factor != 1.0:
+        d["partial_rotary_factor"] = cfg.partial_rotary_factor
+    if cfg.num_experts:
+        d.update(num_experts=cfg.num_experts, num_experts_per_tok=cfg.num_experts_per_tok,
+                 moe_intermediate_size=cfg.moe_intermediate_size, norm_topk_prob=cfg.norm_topk_prob)
+        if cfg.moe_layers is not None:
+            d["mlp_only_layers"] = [i for i, x in enumerate(cfg.moe_layers) if not x]
+    if quantization:
+        d["quantization"] = dict(quantization)
+    return d
+
+
+def _dense(t) -> torch.Tensor:
+    if isinstance(t, QuantizedWeight):
+        return t.dequantize(torch.float32)
+    return t.detach().float().cpu()
+
+
+def export_tensors(model) -> dict[str, torch.Tensor]:
+    """HF-named fp32 tensors of a world-1 model."""
+    if model.tp.world != 1:
+        raise ValueError("export needs the unsharded model (tensor-parallel world 1)")
+    cfg = model.cfg
+    gemma = bool(FAMILIES.get(cfg.model_type, {}).get("gemma"))
+    off = 1.0 if gemma else 0.0  # the loader folds Gemma's (1 + w) into the stored norm weights
+    out = {"model.embed_tokens.weight": _dense(model.embed), "model.norm.weight": _dense(model.norm) - off}
+    if model.lm_head is not model.embed and not cfg.tie_word_embeddings:
+        out["lm_head.weight"] = _dense(model.lm_head)
+    qn, kn = model.H * model.D, model.KVH * model.D
+    for i, L in enumerate(model.layers):
+        p = f"model.layers.{i}."
+        out[p + "input_layernorm.weight"] = _dense(L.ln1) - off
+        if L.post_attn_norm is not None:
+            out[p + "post_attention_layernorm.weight"] = _dense(L.post_attn_norm) - off
+            out[p + "pre_feedforward_layernorm.weight"] = _dense(L.ln2) - off
+            out[p + "post_feedforward_layernorm.weight"] = _dense(L.post_ffn_norm) - off
+        else:
+            out[p + "post_attention_layernorm.weight"] = _dense(L.ln2) - off
+        a = p + "self_attn."
+        w = _dense(L.wqkv)
+        out[a + "q_proj.weight"], out[a + "k_proj.weight"], out[a + "v_proj.weight"] = (
+            w[:qn], w[qn:qn + kn], w[qn + kn:])
+        if L.bqkv is not None:
+            b = _dense(L.bqkv)
+            out[a + "q_proj.bias"], out[a + "k_proj.bias"], out[a + "v_proj.bias"] = b[:qn], b[qn:qn + kn], b[qn + kn:]
+        if L.q_norm is not None:
+            out[a + "q_norm.weight"] = _dense(L.q_norm) - off
+            out[a + "k_norm.weight"] = _dense(L.k_norm) - off
+        out[a + "o_proj.weight"] = _dense(L.wo)
+        if L.bo is not None:
+            out[a + "o_proj.bias"] = _dense(L.bo)
+        if L.sinks is not None:
+            out[a + "sinks"] = _dense(L.sinks)
+        mp = p + "mlp."
+        if L.moe:
+            if cfg.model_type == "gpt_oss":
+                raise ValueError("export of gpt-oss expert layouts is not supported")
+            out[mp + "gate.weight"] = _dense(L.router)
+            for e in range(L.experts_gu.shape[0]):
+                g, u = deinterleave_gate_up(_dense(L.experts_gu[e]))
+                out[f"{mp}experts.{e}.gate_proj.weight"] = g
+                out[f"{mp}experts.{e}.up_proj.weight"] = u
+                out[f"{mp}experts.{e}.down_proj.weight"] = _dense(L.experts_d[e])
+            if L.shared_gu is not None:
+                g, u = deinterleave_gate_up(_dense(L.shared_gu))
+                out[mp + "shared_expert.gate_proj.weight"] = g
+                out[mp + "shared_expert.up_proj.weight"] = u
+                out[mp + "shared_expert.down_proj.weight"] = _dense(L.shared_d)
+                if L.shared_gate is not None:
+                    out[mp + "shared_expert_gate.weight"] = _dense(L.shared_gate)
+        else:
+            g, u = deinterleave_gate_up(_dense(L.wgu))
+            out[mp + "gate_proj.weight"], out[mp + "up_proj.weight"] = g, u
+            out[mp + "down_proj.weight"] = _dense(L.wd)
+            if L.bgu is not None:
+                gb, ub = deinterleave_gate_up(_dense(L.bgu)[:, None])
+                out[mp + "gate_proj.bias"], out[mp + "up_proj.bias"] = gb[:, 0], ub[:, 0]
+            if L.bd is not None:
+                out[mp + "down_proj.bias"] = _dense(L.bd)
+    return out
+
+
+def quantize_tensors(tensors: dict, bits: int = 4, group_size: int = 64, dtype=torch.bfloat16) -> dict:
+    """MLX affine quantisation of every quantisable 2-D weight whose input
+    size is a multiple of the group size; scales / biases in `dtype`."""
+    out = {}
+    for name, t in tensors.items():
+        base = name[:-len(".weight")] if name.endswith(".weight") else None
+        leaf = base.rsplit(".", 1)[-1] if base else ""
+        if base and t.dim() == 2 and leaf in _QUANTISABLE and t.shape[1] % group_size == 0:
+            packed, s, b = quant.affine_quantize(t.float(), group_size, bits)
+            out[name] = packed
+            out[base + ".scales"] = s.to(dtype)
+            out[base + ".biases"] = b.to(dtype)
+        else:
+            out[name] = t
+    return out
+
+
+def save_model(model, path: str, quantize: dict | None = None, dtype=torch.bfloat16, shard_bytes: int = 5 << 30):
+    """Write config.json + model(-NNNNN-of-NNNNN).safetensors (+ index) for `model`."""
+    os.makedirs(path, exist_ok=True)
+    tensors = export_tensors(model)
+    qcfg = None
+    if quantize:
+        qcfg = {"group_size": int(quantize.get("group_size", 64)), "bits": int(quantize.get("bits", 4)),
+                "mode": "affine"}
+        tensors = quantize_tensors(tensors, qcfg["bits"], qcfg["group_size"], dtype)
+    tensors = {k: (v.to(dtype) if v.is_floating_point() else v) for k, v in tensors.items()}
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(to_hf_config(model.cfg, qcfg), f, indent=2)
+    write_shards(tensors, path, shard_bytes)
+
+
+def write_shards(tensors: dict, path: str, shard_bytes: int = 5 << 30):
+    shards, cur, size = [], {}, 0
+    for k in sorted(tensors):
+        t = tensors[k]
+        nb = t.numel() * t.element_size()
+        if cur and size + nb > shard_bytes:
+            shards.append(cur)
+            cur, size = {}, 0
+        cur[k] = t
+        size += nb
+    if cur:
+        shards.append(cur)
+    if len(shards) == 1:
+        save_safetensors(os.path.join(path, "model.safetensors"), shards[0], {"format": "pt"})
+        return
+    wmap = {}
+    for i, sh in enumerate(shards):
+        fn = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+        save_safetensors(os.path.join(path, fn), sh, {"format": "pt"})
+        wmap.update({k: fn for k in sh})
+    total = sum(t.numel() * t.element_size() for t in tensors.values())
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": total}, "weight_map": wmap}, f, indent=2)
+
+
+def convert(src: str, dst: str, quantize: dict | None = None, dtype=torch.bfloat16):
+    """Load a checkpoint directory (dequantising it) and write it to `dst`."""
+    from .load import load_model
+
+    model, hf = load_model(src, device="cpu", dtype=torch.float32, keep_quantized=False)
+    save_model(model, dst, quantize, dtype)
+    for extra in ("tokenizer.json", "tokenizer_config.json", "generation_config.json", "special_tokens_map.json",
+                  "chat_template.jinja"):
+        sp = os.path.join(src, extra)
+        if os.path.exists(sp):
+            with open(sp, "rb") as fi, open(os.path.join(dst, extra), "wb") as fo:
+                fo.write(fi.read())
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description="convert / quantise a checkpoint directory")
+    ap.add_argument("--src", required=True)
+    ap.add_argument("--dst", required=True)
+    ap.add_argument("--q-bits", type=int, default=0)
+    ap.add_argument("--q-group-size", type=int, default=64)
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp16", "fp32"])
+    a = ap.parse_args(argv)
+    dt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[a.dtype]
+    q = {"bits": a.q_bits, "group_size": a.q_group_size} if a.q_bits else None
+    convert(a.src, a.dst, q, dt)
+
+
+if __name__ == "__main__":
+    main()

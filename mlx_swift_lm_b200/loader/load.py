@@ -25,18 +25,32 @@ from ..models.config import DecoderConfig
 from ..models.decoder import DecoderLM, LayerWeights, TensorParallel
 from ..models.families import build_config
 from ..ops import quant
-from ..ops.reference import interleave_gate_up
+from ..ops.qlinear import SUPPORTED_BITS, SUPPORTED_GROUPS, QuantizedWeight
+from ..ops.reference import interleave_gate_up as _interleave_dense
 from .safetensors import load_safetensors
+
+
+def interleave_gate_up(g, u):
+    if isinstance(g, QuantizedWeight):
+        return QuantizedWeight.interleave_gate_up(g, u)
+    return _interleave_dense(g, u)
+
+
+def _cat_rows(parts):
+    if isinstance(parts[0], QuantizedWeight):
+        return QuantizedWeight.cat_rows(parts)
+    return torch.cat(parts, 0)
 
 
 class CheckpointView:
     """Name lookup over a flat tensor dict with prefix detection and MLX-quantized
     linear dequantisation."""
 
-    def __init__(self, tensors: dict, qcfg: dict | None, dtype):
+    def __init__(self, tensors: dict, qcfg: dict | None, dtype, keep_quantized: bool = False):
         self.t = tensors
         self.q = qcfg or {}
         self.dtype = dtype
+        self.keep_quantized = keep_quantized
         keys = list(tensors)
         self.prefix = ""
         for pre in ("model.language_model.", "language_model.model.", "model.", "transformer.", ""):
@@ -59,8 +73,10 @@ class CheckpointView:
         src = per or q
         return src.get("group_size", 64), src.get("bits", 4), src.get("mode", "affine")
 
-    def linear(self, base, required=True):
-        """Weight of a linear layer `base` (without the .weight suffix), dequantised."""
+    def linear(self, base, required=True, packed=True):
+        """Weight of a linear layer `base` (without the .weight suffix). Affine
+        4/8-bit weights stay packed (QuantizedWeight) when the view keeps
+        quantised weights and `packed`; everything else is dequantised."""
         wname = base + ".weight"
         if not self.has(wname):
             if self.has(base):  # bare parameter (e.g. gpt-oss experts.gate_up_proj)
@@ -73,6 +89,9 @@ class CheckpointView:
             gs, bits, mode = self._qparams(base)
             s = self.raw(base + ".scales")
             b = self.raw(base + ".biases") if self.has(base + ".biases") else None
+            if (self.keep_quantized and packed and mode == "affine" and b is not None and bits in SUPPORTED_BITS
+                    and gs in SUPPORTED_GROUPS):
+                return QuantizedWeight.from_mlx(w, s.to(torch.bfloat16), b.to(torch.bfloat16), bits, gs)
             return quant.dequantize(w, s, b, mode, gs, bits, torch.float32).to(self.dtype)
         return w.to(self.dtype)
 
@@ -88,6 +107,8 @@ def _shard_rows(w, rank, world):
     if w is None or world == 1:
         return w
     n = w.shape[0] // world
+    if isinstance(w, QuantizedWeight):
+        return w.rows(rank * n, (rank + 1) * n)
     return w[rank * n:(rank + 1) * n]
 
 
@@ -95,6 +116,8 @@ def _shard_cols(w, rank, world):
     if w is None or world == 1:
         return w
     n = w.shape[-1] // world
+    if isinstance(w, QuantizedWeight):
+        return w.cols(rank * n, (rank + 1) * n)
     return w[..., rank * n:(rank + 1) * n]
 
 
@@ -106,27 +129,35 @@ def _kv_rows(w, cfg, rank, world):
     if cfg.num_kv_heads >= world:
         return _shard_rows(w, rank, world)
     h = (rank * cfg.num_kv_heads) // world
+    if isinstance(w, QuantizedWeight):
+        return w.rows(h * D, (h + 1) * D)
     return w[h * D:(h + 1) * D]
 
 
 def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParallel | None = None,
-               config_overrides: dict | None = None):
-    """Load a model directory (config.json + *.safetensors). Returns (model, hf_config)."""
+               config_overrides: dict | None = None, keep_quantized: bool = True):
+    """Load a model directory (config.json + *.safetensors). Returns (model, hf_config).
+    MLX affine 4/8-bit projections stay packed unless `keep_quantized` is False."""
     with open(os.path.join(path, "config.json")) as f:
         hf = json.load(f)
     cfg = build_config(hf)
     for k, v in (config_overrides or {}).items():
         setattr(cfg, k, v)
     tensors, _ = load_safetensors(path)
-    model = build_from_tensors(cfg, tensors, device, dtype, tp)
+    model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized)
     return model, hf
 
 
-def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=torch.float32, tp=None):
+def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=torch.float32, tp=None,
+                       keep_quantized: bool = False):
+    """Build a DecoderLM from checkpoint tensors. With `keep_quantized`, MLX
+    affine 4/8-bit projections of dense layers stay packed and run through
+    the dequantising GEMM; embeddings, MoE experts and other formats are
+    dequantised."""
     tp = tp or TensorParallel()
     r, w = tp.rank, tp.world
     q = cfg.quantization if isinstance(cfg.quantization, dict) else None
-    ck = CheckpointView(tensors, q, torch.float32)
+    ck = CheckpointView(tensors, q, torch.float32, keep_quantized=keep_quantized and bool(q))
     m = DecoderLM(cfg, "cpu", torch.float32, tp=tp)
     off = 1.0 if cfg.norm_offset_one else 0.0
 
@@ -134,7 +165,7 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         v = ck.vec(name, required=True).float()
         return v + off
 
-    m.embed = ck.linear("embed_tokens")
+    m.embed = ck.linear("embed_tokens", packed=False)
     if cfg.extra.get("embedding_multiplier"):
         pass
     m.norm = norm("norm.weight")
@@ -142,6 +173,8 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         m.lm_head = m.embed
     else:
         m.lm_head = ck.linear("lm_head") if ck.has("lm_head.weight") else ck.linear("lm_head", False)
+        if isinstance(m.lm_head, QuantizedWeight) and (m.lm_head.shape[0] % 8):
+            m.lm_head = m.lm_head.dequantize(torch.float32)
         if m.lm_head is None:
             key = "lm_head.weight"
             m.lm_head = tensors[key].float()
@@ -158,11 +191,11 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
             L.ln2 = norm(p + "post_attention_layernorm.weight")
         a = p + "self_attn."
         if cfg.extra.get("fused_qkv"):
-            qkv = ck.linear(a + "qkv_proj")
+            qkv = ck.linear(a + "qkv_proj", packed=False)
             qw, kw, vw = torch.split(qkv, [cfg.q_size, cfg.kv_size, cfg.kv_size], 0)
         else:
             qw, kw, vw = ck.linear(a + "q_proj"), ck.linear(a + "k_proj"), ck.linear(a + "v_proj")
-        L.wqkv = torch.cat([_shard_rows(qw, r, w), _kv_rows(kw, cfg, r, w), _kv_rows(vw, cfg, r, w)], 0)
+        L.wqkv = _cat_rows([_shard_rows(qw, r, w), _kv_rows(kw, cfg, r, w), _kv_rows(vw, cfg, r, w)])
         if cfg.attention_bias:
             qb, kb, vb = ck.vec(a + "q_proj.bias"), ck.vec(a + "k_proj.bias"), ck.vec(a + "v_proj.bias")
             if qb is not None:
@@ -181,7 +214,7 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         else:
             mp = p + "mlp."
             if cfg.extra.get("fused_gate_up"):
-                gu = ck.linear(mp + "gate_up_proj")
+                gu = ck.linear(mp + "gate_up_proj", packed=False)
                 g, u = gu.chunk(2, 0)
             else:
                 g, u = ck.linear(mp + "gate_proj"), ck.linear(mp + "up_proj")
@@ -191,7 +224,7 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
             if cfg.mlp_bias:
                 gb, ub = ck.vec(mp + "gate_proj.bias"), ck.vec(mp + "up_proj.bias")
                 if gb is not None:
-                    L.bgu = interleave_gate_up(_shard_rows(gb, r, w)[:, None], _shard_rows(ub, r, w)[:, None])[:, 0]
+                    L.bgu = _interleave_dense(_shard_rows(gb, r, w)[:, None], _shard_rows(ub, r, w)[:, None])[:, 0]
                 L.bd = ck.vec(mp + "down_proj.bias")
         m.layers.append(L)
     if cfg.norm_offset_one:
@@ -204,7 +237,7 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
     E = cfg.num_experts
     if cfg.model_type == "gpt_oss":
         mp = p + "mlp."
-        L.router = ck.linear(mp + "router")
+        L.router = ck.linear(mp + "router", packed=False)
         L.router_b = ck.vec(mp + "router.bias")
         if ck.has(mp + "experts.gate_up_proj_blocks"):
             blocks = ck.raw(mp + "experts.gate_up_proj_blocks")  # [E, 2F, K/32, 16] uint8
@@ -231,16 +264,16 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
         return
     mixtral = cfg.extra.get("mixtral_names")
     mp = p + ("block_sparse_moe." if mixtral else "mlp.")
-    L.router = ck.linear(mp + "gate")
+    L.router = ck.linear(mp + "gate", packed=False)
     names = ("w1", "w3", "w2") if mixtral else ("gate_proj", "up_proj", "down_proj")
     if ck.has(mp + "switch_mlp.gate_proj.weight"):
-        g = ck.linear(mp + "switch_mlp.gate_proj")
-        u = ck.linear(mp + "switch_mlp.up_proj")
-        d = ck.linear(mp + "switch_mlp.down_proj")
+        g = ck.linear(mp + "switch_mlp.gate_proj", packed=False)
+        u = ck.linear(mp + "switch_mlp.up_proj", packed=False)
+        d = ck.linear(mp + "switch_mlp.down_proj", packed=False)
     else:
-        g = torch.stack([ck.linear(f"{mp}experts.{e}.{names[0]}") for e in range(E)])
-        u = torch.stack([ck.linear(f"{mp}experts.{e}.{names[1]}") for e in range(E)])
-        d = torch.stack([ck.linear(f"{mp}experts.{e}.{names[2]}") for e in range(E)])
+        g = torch.stack([ck.linear(f"{mp}experts.{e}.{names[0]}", packed=False) for e in range(E)])
+        u = torch.stack([ck.linear(f"{mp}experts.{e}.{names[1]}", packed=False) for e in range(E)])
+        d = torch.stack([ck.linear(f"{mp}experts.{e}.{names[2]}", packed=False) for e in range(E)])
     L.experts_gu = torch.stack([interleave_gate_up(_shard_rows(g[e], r, w), _shard_rows(u[e], r, w)) for e in range(E)])
     L.experts_d = torch.stack([_shard_cols(d[e], r, w) for e in range(E)])
     if cfg.shared_expert_intermediate_size:
@@ -249,7 +282,7 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
                                          _shard_rows(ck.linear(sp + "up_proj"), r, w))
         L.shared_d = _shard_cols(ck.linear(sp + "down_proj"), r, w)
         if ck.has(mp + "shared_expert_gate.weight"):
-            L.shared_gate = ck.linear(mp + "shared_expert_gate")
+            L.shared_gate = ck.linear(mp + "shared_expert_gate", packed=False)
 
 
 def _mxfp4_blocks(blocks, scales):

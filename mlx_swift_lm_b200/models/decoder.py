@@ -23,6 +23,7 @@ import torch
 
 from .. import ops
 from ..ops import reference as ref
+from ..ops.qlinear import QuantizedWeight
 from .batch import ForwardBatch
 from .config import DecoderConfig
 from .rope import build_rope
@@ -334,6 +335,8 @@ class DecoderLM:
         """Use the fused symmetric-memory collectives for decode steps of up
         to `max_rows` rows (tensor parallel only)."""
         if self.tp.world > 1:
+            if any(isinstance(t, QuantizedWeight) for L in self.layers for t in (L.wqkv, L.wo, L.wgu, L.wd)):
+                raise ValueError("the fused TP decode path serves bf16 weights; quantised models use NCCL TP")
             from ..parallel.tp_fused import FusedTP
 
             self.tp_fused = FusedTP(self, max_rows)
@@ -402,12 +405,21 @@ class DecoderLM:
 
         m.embed = cv(self.embed)
         m.norm = cv(self.norm)
-        m.lm_head = m.embed if self.lm_head is self.embed else cv(self.lm_head)
+        if self.lm_head is self.embed:
+            m.lm_head = m.embed
+        elif isinstance(self.lm_head, QuantizedWeight):
+            m.lm_head = self.lm_head.to(dev)
+        else:
+            m.lm_head = cv(self.lm_head)
         for L in self.layers:
             N = LayerWeights()
             for s in LayerWeights.__slots__:
                 v = getattr(L, s)
-                setattr(N, s, cv(v, s == "sinks") if isinstance(v, torch.Tensor) else v)
+                if isinstance(v, torch.Tensor):
+                    v = cv(v, s == "sinks")
+                elif isinstance(v, QuantizedWeight):
+                    v = v.to(dev)
+                setattr(N, s, v)
             m.layers.append(N)
         return m
 

@@ -1,0 +1,147 @@
+"""Affine-quantised linear weights kept packed on the device.
+
+MLX checkpoints store ``w = scale * q + bias`` per group of ``gs`` inputs with
+unsigned ``bits``-bit codes packed into uint32 words (MLXNN QuantizedLinear;
+layout checked at MLXLMCommon/SwitchLayers.swift:1431-1452). This module keeps
+such weights packed in the layout the dequantising tcgen05 GEMM
+(``b200_gemm_q``) streams:
+
+* codes   uint8 [N, K*bits/8]. 8-bit: one code per byte, in input order.
+  4-bit: each 32-bit word holds 8 consecutive inputs with input 2j in bits
+  4j..4j+3 and input 2j+1 in bits 16+4j..19+4j, so one mask turns a shifted
+  word into a bf16 pair (repacked once from MLX's nibble order at load).
+* scales_t, biases_t  bf16 [K/gs, N] (transposed: rows of N are what a
+  128-row weight tile needs, contiguous for TMA).
+
+Row operations used by the model builder (stacking q|k|v, interleaving
+gate/up, tensor-parallel row / column shards) act on codes, scales and biases
+together; groups run along K, so they commute with quantisation. Column shards
+must start on a group boundary.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import quant
+
+SUPPORTED_BITS = (4, 8)
+SUPPORTED_GROUPS = (32, 64, 128)
+
+
+def _repack4(q: torch.Tensor) -> torch.Tensor:
+    """int codes [N, K] (0..15) -> uint8 [N, K/2] in the kernel's nibble order."""
+    N, K = q.shape
+    w = q.to(torch.int32).reshape(N, K // 8, 8)
+    b0 = w[..., 0] | (w[..., 2] << 4)
+    b1 = w[..., 4] | (w[..., 6] << 4)
+    b2 = w[..., 1] | (w[..., 3] << 4)
+    b3 = w[..., 5] | (w[..., 7] << 4)
+    return torch.stack([b0, b1, b2, b3], -1).reshape(N, K // 2).to(torch.uint8)
+
+
+def _unpack4(c: torch.Tensor) -> torch.Tensor:
+    N, KB = c.shape
+    b = c.to(torch.int32).reshape(N, KB // 4, 4)
+    q = torch.empty(N, KB // 4, 8, dtype=torch.int32, device=c.device)
+    q[..., 0], q[..., 2] = b[..., 0] & 15, b[..., 0] >> 4
+    q[..., 4], q[..., 6] = b[..., 1] & 15, b[..., 1] >> 4
+    q[..., 1], q[..., 3] = b[..., 2] & 15, b[..., 2] >> 4
+    q[..., 5], q[..., 7] = b[..., 3] & 15, b[..., 3] >> 4
+    return q.reshape(N, KB * 2)
+
+
+class QuantizedWeight:
+    """Packed affine weight of logical shape [N, K]."""
+
+    def __init__(self, codes: torch.Tensor, scales_t: torch.Tensor, biases_t: torch.Tensor, bits: int, gs: int):
+        assert bits in SUPPORTED_BITS and gs in SUPPORTED_GROUPS, (bits, gs)
+        self.codes, self.scales_t, self.biases_t = codes, scales_t, biases_t
+        self.bits, self.gs = bits, gs
+        self.shape = (codes.shape[0], codes.shape[1] * 8 // bits)
+
+    # ---------------------------------------------------------------- construction
+    @classmethod
+    def from_codes(cls, q: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, bits: int, gs: int,
+                   dtype=torch.bfloat16):
+        """q int [N, K]; scales / biases [N, K/gs]."""
+        codes = _repack4(q) if bits == 4 else q.to(torch.uint8).contiguous()
+        return cls(codes.contiguous(), scales.t().to(dtype).contiguous(), biases.t().to(dtype).contiguous(), bits, gs)
+
+    @classmethod
+    def from_mlx(cls, packed: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, bits: int, gs: int):
+        """MLX layout: packed uint32 (as int32) [N, K*bits/32], scales / biases [N, K/gs]."""
+        K = scales.shape[-1] * gs
+        q = quant.unpack_codes(packed.cpu(), bits, K)
+        return cls.from_codes(q, scales.cpu(), biases.cpu(), bits, gs)
+
+    @classmethod
+    def quantize(cls, w: torch.Tensor, bits: int = 4, gs: int = 64):
+        """MLX-style affine quantisation of a float weight [N, K]."""
+        packed, s, b = quant.affine_quantize(w.float().cpu(), gs, bits)
+        # round scale / bias to bf16 first: the kernel applies them in bf16
+        return cls.from_mlx(packed, s.to(torch.bfloat16), b.to(torch.bfloat16), bits, gs)
+
+    # ---------------------------------------------------------------- views
+    @property
+    def device(self):
+        return self.codes.device
+
+    @property
+    def dtype(self):
+        return self.scales_t.dtype
+
+    def codes_int(self) -> torch.Tensor:
+        return _unpack4(self.codes) if self.bits == 4 else self.codes.to(torch.int32)
+
+    def dequantize(self, dtype=torch.float32) -> torch.Tensor:
+        """[N, K] weights with one rounding of scale * q + bias (as the kernel)."""
+        q = self.codes_int().float()
+        N, K = q.shape
+        s = self.scales_t.t().float().repeat_interleave(self.gs, dim=1)
+        b = self.biases_t.t().float().repeat_interleave(self.gs, dim=1)
+        return (q * s + b).to(torch.bfloat16).to(dtype)
+
+    def to(self, device=None, dtype=None):
+        dt = dtype if dtype in (torch.bfloat16, torch.float16, torch.float32) else None
+        sc = self.scales_t.to(device=device, dtype=dt or self.scales_t.dtype)
+        bi = self.biases_t.to(device=device, dtype=dt or self.biases_t.dtype)
+        return QuantizedWeight(self.codes.to(device), sc, bi, self.bits, self.gs)
+
+    def numel(self) -> int:
+        return self.shape[0] * self.shape[1]
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.codes, self.scales_t, self.biases_t))
+
+    # ---------------------------------------------------------------- row / column ops
+    def rows(self, lo: int, hi: int) -> "QuantizedWeight":
+        return QuantizedWeight(self.codes[lo:hi].contiguous(), self.scales_t[:, lo:hi].contiguous(),
+                               self.biases_t[:, lo:hi].contiguous(), self.bits, self.gs)
+
+    def cols(self, lo: int, hi: int) -> "QuantizedWeight":
+        assert lo % self.gs == 0 and hi % self.gs == 0, "column shards must align with quantisation groups"
+        c0, c1 = lo * self.bits // 8, hi * self.bits // 8
+        return QuantizedWeight(self.codes[:, c0:c1].contiguous(), self.scales_t[lo // self.gs:hi // self.gs].contiguous(),
+                               self.biases_t[lo // self.gs:hi // self.gs].contiguous(), self.bits, self.gs)
+
+    @staticmethod
+    def cat_rows(parts: list["QuantizedWeight"]) -> "QuantizedWeight":
+        p0 = parts[0]
+        assert all(p.bits == p0.bits and p.gs == p0.gs for p in parts)
+        return QuantizedWeight(torch.cat([p.codes for p in parts], 0), torch.cat([p.scales_t for p in parts], 1),
+                               torch.cat([p.biases_t for p in parts], 1), p0.bits, p0.gs)
+
+    @staticmethod
+    def interleave_gate_up(g: "QuantizedWeight", u: "QuantizedWeight", block: int = 64) -> "QuantizedWeight":
+        F = g.shape[0]
+        assert F % block == 0 and u.shape == g.shape
+        idx = []
+        for b in range(F // block):
+            idx.append(("g", b))
+            idx.append(("u", b))
+        parts = [(g if w == "g" else u).rows(b * block, (b + 1) * block) for w, b in idx]
+        return QuantizedWeight.cat_rows(parts)
+
+
+def is_quantized(w) -> bool:
+    return isinstance(w, QuantizedWeight)

@@ -65,7 +65,7 @@ class SymmetricComm:
         assert L.b200_comm_ctx_size() == C.sizeof(CommCtxStruct), "CommCtx layout mismatch"
         pads = NUM_PADS * MAX_RANKS * 4
         recv = 2 * world * rows_per_rank * hidden * 4
-        hbuf = 2 * rows_per_rank * hidden * 2
+        hbuf = 2 * world * rows_per_rank * hidden * 2
         xarg = 2 * world * max_rows * 8
         self.pads_off = 0
         self.recv_off = _align(pads)

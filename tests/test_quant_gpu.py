@@ -1,0 +1,62 @@
+"""Dequantising tcgen05 GEMM (affine 4/8-bit weights, MLX groups) vs the fp32
+oracle over the same dequantised weights."""
+import pytest
+import torch
+
+from mlx_swift_lm_b200 import ops
+from mlx_swift_lm_b200.ops import reference as ref
+from mlx_swift_lm_b200.ops.qlinear import QuantizedWeight
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+@pytest.mark.parametrize("M", [1, 16, 33, 64, 130, 300])
+def test_gemm_q(bits, gs, M):
+    torch.manual_seed(M + bits + gs)
+    N, K = 384, 1024
+    w = torch.randn(N, K) * 0.05
+    q = QuantizedWeight.quantize(w, bits, gs).to(DEV)
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    y = ops.gemm(x, q)
+    r = ref.gemm_ref(x.cpu(), q.dequantize().to(torch.bfloat16).cpu())
+    assert _rel(y.cpu(), r) < 1e-2
+    yf = ops.gemm(x, q, epi="f32")
+    assert _rel(yf.cpu(), ref.gemm_ref(x.cpu(), q.dequantize().to(torch.bfloat16).cpu(), "f32")) < 1e-3
+
+
+@pytest.mark.parametrize("epi", ["swiglu", "geglu", "swiglu_oai"])
+def test_gemm_q_glu_bias_and_add(epi):
+    torch.manual_seed(7)
+    K, F, M = 512, 256, 48
+    g = QuantizedWeight.quantize(torch.randn(F, K) * 0.05, 4, 64)
+    u = QuantizedWeight.quantize(torch.randn(F, K) * 0.05, 4, 64)
+    gu = QuantizedWeight.interleave_gate_up(g, u).to(DEV)
+    b = torch.randn(2 * F, device=DEV, dtype=torch.bfloat16) * 0.1
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    y = ops.gemm(x, gu, epi=epi, bias=b)
+    r = ref.gemm_ref(x.cpu(), gu.dequantize().to(torch.bfloat16).cpu(), epi, bias=b.cpu())
+    assert _rel(y.cpu(), r) < 1.5e-2
+    res = torch.randn(M, 2 * F, device=DEV, dtype=torch.bfloat16)
+    ya = ops.gemm(x, gu, epi="add", residual=res)
+    ra = ref.gemm_ref(x.cpu(), gu.dequantize().to(torch.bfloat16).cpu(), "add", res.cpu())
+    assert _rel(ya.cpu(), ra) < 1e-2
+
+
+def test_gemm_q_large_shape_and_batch_invariance():
+    torch.manual_seed(9)
+    N, K = 4096, 4096
+    q = QuantizedWeight.quantize(torch.randn(N, K) * 0.02, 4, 64).to(DEV)
+    x = torch.randn(64, K, device=DEV, dtype=torch.bfloat16)
+    full = ops.gemm(x, q)
+    one = ops.gemm(x[5:6].contiguous(), q)
+    assert torch.equal(full[5:6], one)
+    r = ref.gemm_ref(x[:8].cpu(), q.dequantize().to(torch.bfloat16).cpu())
+    assert _rel(full[:8].cpu(), r) < 1e-2
