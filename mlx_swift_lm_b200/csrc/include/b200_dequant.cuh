@@ -1,0 +1,74 @@
+// Affine-quantised weight tiles -> bf16 MMA operand tiles in shared memory.
+//
+// Raw tile of one 64-input K block for 128 weight rows (TMA, no swizzle):
+//   codes   [128][WQ * 8] bytes. 8-bit: one code per byte in input order.
+//           4-bit: 32-bit words of 8 inputs; input 2j in bits 4j..4j+3 and
+//           input 2j+1 in bits 16+4j..19+4j (repacked from MLX at load).
+//   scales  [groups][128] bf16, biases [groups][128] bf16 (groups = 1 or 2).
+// w = scale * q + bias with one rounding to bf16.
+// Output: row t of a K-major bf16 tile [128][64] with the 128-byte swizzle
+// the UMMA descriptor expects (16-byte chunk c of row t at c ^ (t & 7)).
+#pragma once
+
+#include "b200_common.cuh"
+
+namespace b200 {
+
+// bf16 pair (q_lo + 128, q_hi + 128) from two 4-bit codes placed at bits 0..3
+// and 16..19 of v (exact: 128..143 are bf16 integers), minus 128, then
+// scale * q + bias with one rounding.
+__device__ __forceinline__ uint32_t dq4_pair(uint32_t v, __nv_bfloat162 s2, __nv_bfloat162 b2) {
+  const uint32_t x = (v & 0x000F000Fu) | 0x43004300u;
+  const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
+  const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&x), c128);
+  const __nv_bfloat162 w = __hfma2(q, s2, b2);
+  return *reinterpret_cast<const uint32_t*>(&w);
+}
+
+// Thread (t, half) converts inputs [32*half, 32*half + 32) of row t. `g` is
+// the group of that half (0, or `half` when the group size is 32).
+template <int WQ>
+__device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* atile, int t, int half, int g) {
+  constexpr int kCodeBytes = WQ * 128 * 64 / 8;
+  constexpr int kGroupBytes = 2 * 128 * 2;
+  const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes);
+  const __nv_bfloat16* bi = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes + kGroupBytes);
+  const __nv_bfloat16 sv = sc[g * 128 + t], bv = bi[g * 128 + t];
+  uint8_t* arow = atile + t * 128;
+  if constexpr (WQ == 4) {
+    const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
+    const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+    const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv), b2 = __halves2bfloat162(bv, bv);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t v = words[w];
+      uint4 o;
+      o.x = dq4_pair(v, s2, b2);
+      o.y = dq4_pair(v >> 4, s2, b2);
+      o.z = dq4_pair(v >> 8, s2, b2);
+      o.w = dq4_pair(v >> 12, s2, b2);
+      const int chunk = half * 4 + w;
+      *reinterpret_cast<uint4*>(arow + ((chunk ^ (t & 7)) << 4)) = o;
+    }
+  } else {
+    static_assert(WQ == 8, "4- or 8-bit codes");
+    const uint4* cw = reinterpret_cast<const uint4*>(raw + t * 64 + half * 32);
+    const uint4 q0 = cw[0], q1 = cw[1];
+    const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const float sf = bf2f(sv), bf = bf2f(bv);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t v = words[2 * h + e];
+        o[2 * e] = pack_bf16x2(fmaf((float)(v & 0xFF), sf, bf), fmaf((float)((v >> 8) & 0xFF), sf, bf));
+        o[2 * e + 1] = pack_bf16x2(fmaf((float)((v >> 16) & 0xFF), sf, bf), fmaf((float)(v >> 24), sf, bf));
+      }
+      const int chunk = half * 4 + h;
+      *reinterpret_cast<uint4*>(arow + ((chunk ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+}  // namespace b200

@@ -30,6 +30,7 @@
 
 #include "b200_common.cuh"
 #include "b200_comm.cuh"
+#include "b200_dequant.cuh"
 
 #include <memory>
 
@@ -65,12 +66,18 @@ struct GemmArgs {
   int kb_total, kb_per_split, ksplit;
   int epi;
   unsigned long long* trace;  // optional [ctas][6] %globaltimer stamps (diagnostics), null in production
+  unsigned long long* ktrace;  // optional per-K-block stamps of CTA 0 (diagnostics), null in production
 };
 
-// Shared-memory plan of one CTA. Per stage: the bf16 weight tile A (TMA, or
-// written by the dequantising warps when WQ > 0), the activation tile B, and
-// for quantised weights the raw tile (codes [128][WQ*8 bytes], then scales and
-// biases [groups][128] bf16).
+// Shared-memory plan of one CTA.
+// bf16 weights (WQ = 0): STAGES stages of {A weight tile (TMA), B activation
+// tile}, barriers full/empty per stage.
+// Quantised weights (WQ = 4 / 8): two rings. A deep raw ring of kRawStages
+// small stages {codes [128][WQ*8 B], scales, biases [groups][128] bf16} keeps
+// enough weight bytes in flight to cover DRAM latency (a 4-bit stage is only
+// 5 KB); STAGES operand stages {A bf16 tile written by the dequantising warps,
+// B activation tile (TMA)} feed the MMA. Barriers: raw_full/raw_empty per raw
+// stage, x_full/a_ready/a_empty per operand stage.
 template <int BN, int STAGES, int WQ = 0>
 struct GemmSmem {
   static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
@@ -78,15 +85,20 @@ struct GemmSmem {
   static constexpr int kCodeBytes = WQ * 128 * 64 / 8;
   static constexpr int kGroupBytes = 2 * 128 * 2;  // up to 2 groups x 128 rows x bf16
   static constexpr int kRawBytes = WQ ? kCodeBytes + 2 * kGroupBytes : 0;
-  static constexpr int kStageBytes = (kABytes + kBBytes + kRawBytes + 1023) / 1024 * 1024;
+  static constexpr int kStageBytes = (kABytes + kBBytes + 1023) / 1024 * 1024;
   static constexpr int kPipeBytes = STAGES * kStageBytes;
+  static constexpr int kRawBudget = 200 * 1024 - kPipeBytes;
+  static constexpr int kRawStages = WQ ? (kRawBudget / kRawBytes > 24 ? 24 : kRawBudget / kRawBytes) : 0;
+  static constexpr int kRawOffset = kPipeBytes;
+  static constexpr int kAllPipe = kPipeBytes + kRawStages * kRawBytes;
   static constexpr int kPartBytes = BN * 128 * 4;  // fp32 partial [BN][128]
-  static constexpr int kMain = kPipeBytes > kPartBytes ? kPipeBytes : kPartBytes;
-  static constexpr int kBarOffset = kMain;
-  static constexpr int kNumBars = (WQ ? 3 : 2) * STAGES + 1;
+  static constexpr int kMain = kAllPipe > kPartBytes ? kAllPipe : kPartBytes;
+  static constexpr int kBarOffset = (kMain + 7) / 8 * 8;
+  static constexpr int kNumBars = (WQ ? 3 : 2) * STAGES + 2 * kRawStages + 1;
   static constexpr int kTotal = kBarOffset + kNumBars * 8 + 16 + 1024;  // + alignment slack
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  static constexpr int kThreads = WQ ? 256 : 128;
+  static constexpr int kThreads = WQ ? 384 : 128;  // + 8 dequantising warps (two per SM sub-partition)
+  static_assert(!WQ || kRawStages >= 4, "raw ring too shallow");
 };
 
 __device__ __forceinline__ void cluster_sync() {
@@ -123,17 +135,6 @@ struct QArgs {
   int gs;
 };
 
-// bf16 pair (q_lo + 128, q_hi + 128) from two 4-bit codes placed at bits 0..3
-// and 16..19 of v (exact: 128..143 are bf16 integers), minus 128, then
-// scale * q + bias with one rounding.
-__device__ __forceinline__ uint32_t dq4_pair(uint32_t v, __nv_bfloat162 s2, __nv_bfloat162 b2) {
-  const uint32_t x = (v & 0x000F000Fu) | 0x43004300u;
-  const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
-  const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&x), c128);
-  const __nv_bfloat162 w = __hfma2(q, s2, b2);
-  return *reinterpret_cast<const uint32_t*>(&w);
-}
-
 template <int BN, int STAGES, int MODE, int WQ>
 __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
@@ -143,10 +144,13 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar_full = sbase + S::kBarOffset;
-  const uint32_t bar_empty = bar_full + STAGES * 8;
+  constexpr int RS = S::kRawStages;
+  const uint32_t bar_full = sbase + S::kBarOffset;  // bf16: stage full; quantised: activation tile landed
+  const uint32_t bar_empty = bar_full + STAGES * 8;  // operand stage consumed by the MMA
   const uint32_t bar_accum = bar_empty + STAGES * 8;
-  const uint32_t bar_aready = bar_accum + 8;  // [STAGES], quantised weights only
+  const uint32_t bar_aready = bar_accum + 8;               // [STAGES] quantised: bf16 A tile written
+  const uint32_t bar_rfull = bar_aready + STAGES * 8;      // [RS] raw stage landed
+  const uint32_t bar_rempty = bar_rfull + RS * 8;          // [RS] raw stage consumed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kBarOffset + S::kNumBars * 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -167,7 +171,11 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
-      if constexpr (WQ != 0) mbar_init(bar_aready + 8 * s, 4);  // one arrive per dequantising warp
+      if constexpr (WQ != 0) mbar_init(bar_aready + 8 * s, 8);  // one arrive per dequantising warp
+    }
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(bar_rfull + 8 * s, 1);
+      mbar_init(bar_rempty + 8 * s, 8);
     }
     mbar_init(bar_accum, 1);
     fence_barrier_init();
@@ -182,26 +190,12 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   if (trace && threadIdx.x == 0) trace[1] = globaltimer();
 
+  if constexpr (WQ == 0) {
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
     const uint64_t pol_w = l2_policy_evict_first();
     const uint64_t pol_x = l2_policy_evict_last();
-    // quantised: groups covered by one 64-input K block (1 or 2), and the bytes
-    // one stage receives from TMA
-    const int gpb = WQ ? (qa.gs >= 64 ? 1 : 64 / qa.gs) : 0;
-    const uint32_t stage_tx =
-        WQ ? (uint32_t)(S::kBBytes + S::kCodeBytes + 2 * gpb * 128 * 2) : (uint32_t)(S::kABytes + S::kBBytes);
-    auto load_w = [&](uint32_t a, uint32_t bar, int kb) {
-      if constexpr (WQ == 0) {
-        tma_load_2d(a, &tmW, bar, kb * 64, n0, pol_w);
-      } else {
-        const uint32_t raw = a + S::kABytes + S::kBBytes;
-        tma_load_2d(raw, &qa.codes, bar, kb * WQ * 8, n0, pol_w);
-        const int g0 = qa.gs >= 64 ? (kb * 64) / qa.gs : kb * gpb;
-        tma_load_2d(raw + S::kCodeBytes, &qa.scales, bar, n0, g0, pol_w);
-        tma_load_2d(raw + S::kCodeBytes + S::kGroupBytes, &qa.biases, bar, n0, g0, pol_w);
-      }
-    };
+    const uint32_t stage_tx = (uint32_t)(S::kABytes + S::kBBytes);
     // Weights are written by no kernel: the first STAGES weight tiles are
     // requested before waiting on the previous kernel (PDL), so their HBM
     // latency overlaps the predecessor's tail.
@@ -209,7 +203,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     for (int i = 0; i < pre; ++i) {
       const uint32_t a = sbase + i * S::kStageBytes;
       mbar_arrive_expect_tx(bar_full + 8 * i, stage_tx);
-      load_w(a, bar_full + 8 * i, kb_begin + i);
+      tma_load_2d(a, &tmW, bar_full + 8 * i, (kb_begin + i) * 64, n0, pol_w);
     }
     pdl_wait();
     // Activation tile: local TMA; in all-gather mode from the gathered buffer
@@ -236,7 +230,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
       const uint32_t b = a + S::kABytes;
       mbar_arrive_expect_tx(bar_full + 8 * s, stage_tx);
       const int kc = (kb_begin + i) * 64;
-      load_w(a, bar_full + 8 * s, kb_begin + i);
+      tma_load_2d(a, &tmW, bar_full + 8 * s, kc, n0, pol_w);
       load_x(b, bar_full + 8 * s, kc);
       issued = i + 1;
     }
@@ -249,9 +243,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
-      if constexpr (WQ != 0) {
-        if (!mbar_wait(bar_aready + 8 * s, r & 1, kErrGemmWait)) break;
-      }
+      if (args.ktrace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) args.ktrace[2 * nkb + i] = globaltimer();
       if (trace && i == 0) trace[2] = globaltimer();
       tc_fence_after();
       const uint32_t a = sbase + s * S::kStageBytes;
@@ -263,71 +255,94 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
       tc_commit(bar_empty + 8 * s);
     }
     tc_commit(bar_accum);
-  } else if (warp >= 4) {
-   if constexpr (WQ != 0) {
-    // ---------------- dequantising warps: raw tile -> bf16 A tile ----------------
-    // thread t owns weight row t; writes its 128-byte row with the 128B swizzle
-    // the MMA descriptor expects (16-byte chunk c lands at c ^ (t & 7)).
-    const int t = threadIdx.x - 128;
+  }
+  } else {
+  // ---------------- quantised weights ----------------
+  const int gpb = qa.gs >= 64 ? 1 : 64 / qa.gs;  // groups per 64-input K block
+  if (warp == 0 && lane == 0) {
+    // raw producer: codes + scales + biases, RS stages ahead (weights are
+    // written by no kernel, so the whole ring is requested before the PDL wait)
+    const uint64_t pol_w = l2_policy_evict_first();
+    const uint32_t raw_tx = (uint32_t)(S::kCodeBytes + 2 * gpb * 128 * 2);
+    int issued = 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % RS, r = i / RS;
+      if (r > 0 && !mbar_wait(bar_rempty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
+      const uint32_t raw = sbase + S::kRawOffset + s * S::kRawBytes;
+      const int kb = kb_begin + i;
+      mbar_arrive_expect_tx(bar_rfull + 8 * s, raw_tx);
+      tma_load_2d(raw, &qa.codes, bar_rfull + 8 * s, kb * WQ * 8, n0, pol_w);
+      const int g0 = qa.gs >= 64 ? (kb * 64) / qa.gs : kb * gpb;
+      tma_load_2d(raw + S::kCodeBytes, &qa.scales, bar_rfull + 8 * s, n0, g0, pol_w);
+      tma_load_2d(raw + S::kCodeBytes + S::kGroupBytes, &qa.biases, bar_rfull + 8 * s, n0, g0, pol_w);
+      issued = i + 1;
+    }
+    for (int i = max(0, issued - RS); i < issued; ++i)
+      mbar_wait(bar_rfull + 8 * (i % RS), (i / RS) & 1, kErrGemmWait);
+  } else if (warp == 2 && lane == 0) {
+    // activation producer
+    const uint64_t pol_x = l2_policy_evict_last();
+    pdl_wait();
+    int issued = 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES, r = i / STAGES;
+      if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
+      mbar_arrive_expect_tx(bar_full + 8 * s, S::kBBytes);
+      tma_load_2d(sbase + s * S::kStageBytes + S::kABytes, &tmX, bar_full + 8 * s, (kb_begin + i) * 64, m0, pol_x);
+      issued = i + 1;
+    }
+    for (int i = max(0, issued - STAGES); i < issued; ++i)
+      mbar_wait(bar_full + 8 * (i % STAGES), (i / STAGES) & 1, kErrGemmWait);
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
-      uint8_t* stage = smem + s * S::kStageBytes;
-      const uint8_t* raw = stage + S::kABytes + S::kBBytes;
-      const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(raw + S::kCodeBytes);
-      const __nv_bfloat16* bi = reinterpret_cast<const __nv_bfloat16*>(raw + S::kCodeBytes + S::kGroupBytes);
-      uint8_t* arow = stage + t * 128;
-      if constexpr (WQ == 4) {
-        const uint4* cw = reinterpret_cast<const uint4*>(raw + t * 32);
-        const uint4 c0 = cw[0], c1 = cw[1];
-        const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const bool kt = args.ktrace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+      if (kt) args.ktrace[3 * nkb + i] = globaltimer();
+      if (!mbar_wait(bar_aready + 8 * s, r & 1, kErrGemmWait)) break;
+      if (kt) args.ktrace[2 * nkb + i] = globaltimer();
+      if (trace && i == 0) trace[2] = globaltimer();
+      tc_fence_after();
+      const uint32_t a = sbase + s * S::kStageBytes;
+      const uint64_t ad = umma_desc_k_sw128(a, 1024);
+      const uint64_t bd = umma_desc_k_sw128(a + S::kABytes, 1024);
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const int g = qa.gs == 32 ? (w >> 2) : 0;
-          const __nv_bfloat16 sv = sc[g * 128 + t], bv = bi[g * 128 + t];
-          const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv), b2 = __halves2bfloat162(bv, bv);
-          const uint32_t v = words[w];
-          uint4 o;
-          o.x = dq4_pair(v, s2, b2);
-          o.y = dq4_pair(v >> 4, s2, b2);
-          o.z = dq4_pair(v >> 8, s2, b2);
-          o.w = dq4_pair(v >> 12, s2, b2);
-          *reinterpret_cast<uint4*>(arow + ((w ^ (t & 7)) << 4)) = o;
-        }
-      } else {
-        const uint4* cw = reinterpret_cast<const uint4*>(raw + t * 64);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 q4 = cw[c];
-          const uint32_t words[4] = {q4.x, q4.y, q4.z, q4.w};
-          const int g = qa.gs == 32 ? (c >> 1) : 0;
-          const float sv = bf2f(sc[g * 128 + t]), bv = bf2f(bi[g * 128 + t]);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const uint32_t v = words[2 * h + e];
-              o[2 * e] = pack_bf16x2(fmaf((float)(v & 0xFF), sv, bv), fmaf((float)((v >> 8) & 0xFF), sv, bv));
-              o[2 * e + 1] = pack_bf16x2(fmaf((float)((v >> 16) & 0xFF), sv, bv), fmaf((float)(v >> 24), sv, bv));
-            }
-            const int chunk = 2 * c + h;
-            *reinterpret_cast<uint4*>(arow + ((chunk ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        }
-      }
-      // generic-proxy smem writes -> visible to the tensor core (async proxy)
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_aready + 8 * s);
+      for (int k = 0; k < 4; ++k) tc_mma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+      tc_commit(bar_empty + 8 * s);
     }
-   }
+    tc_commit(bar_accum);
+  } else if (warp >= 4) {
+    // Eight dequantising warps: thread (t, half) converts inputs
+    // [32*half, 32*half + 32) of weight row t (one group per half).
+    const int t = (threadIdx.x - 128) & 127;
+    const int half = (threadIdx.x - 128) >> 7;
+    const int g = qa.gs == 32 ? half : 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int rs = i % RS, rr = i / RS;
+      const int s = i % STAGES, r = i / STAGES;
+      if (!mbar_wait(bar_rfull + 8 * rs, rr & 1, kErrGemmWait)) break;
+      const bool kt = args.ktrace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 128;
+      if (kt) args.ktrace[i] = globaltimer();
+      if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
+      uint8_t* stage = smem + s * S::kStageBytes;
+      dequant_half_row<WQ>(smem + S::kRawOffset + rs * S::kRawBytes, stage, t, half, g);
+      if (kt) args.ktrace[nkb + i] = globaltimer();
+      // generic-proxy smem writes -> visible to the tensor core (async proxy)
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(bar_rempty + 8 * rs);
+        mbar_arrive(bar_aready + 8 * s);
+      }
+    }
+  }
   }
   __syncwarp();
 
   // every thread that touches global memory below orders itself after the
   // previous kernel (the producer thread already did)
-  if (!(warp == 0 && lane == 0)) pdl_wait();
+  if (WQ != 0 || !(warp == 0 && lane == 0)) pdl_wait();
   // ---------------- drain TMEM into this CTA's fp32 partial [BN][128] ----------------
   const bool acc_ok = __syncthreads_and(mbar_wait(bar_accum, 0, kErrTmemWait) ? 1 : 0) != 0;
   tc_fence_after();
@@ -588,11 +603,11 @@ static int launch_bn_q(int BN, const CUtensorMap& tx, const GemmArgs& a, const Q
                        cudaStream_t st) {
   const CollArgs& c = local_coll_q();
   switch (BN) {
-    case 16: return launch_gemm<16, 8, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
-    case 32: return launch_gemm<32, 7, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
-    case 64: return launch_gemm<64, 6, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
-    case 128: return launch_gemm<128, 5, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
-    case 256: return launch_gemm<256, 3, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 16: return launch_gemm<16, 4, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 32: return launch_gemm<32, 4, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 64: return launch_gemm<64, 4, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 128: return launch_gemm<128, 3, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 256: return launch_gemm<256, 2, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
     default: return -1;
   }
 }
@@ -644,6 +659,10 @@ extern "C" {
 // published, exit) into this device buffer. Pass null to turn it off.
 static unsigned long long* g_gemm_trace = nullptr;
 void b200_gemm_set_trace(unsigned long long* buf) { g_gemm_trace = buf; }
+// Diagnostics: per-K-block stamps of CTA (0,0,0) of the next launches:
+// [4][nkb] = {raw/weights landed, operand ready (dequantised), MMA issued, activation landed}.
+static unsigned long long* g_gemm_ktrace = nullptr;
+void b200_gemm_set_ktrace(unsigned long long* buf) { g_gemm_ktrace = buf; }
 
 int b200_gemm_num_splits(int M, int N, int K, int num_sms) {
   (void)M;
@@ -676,6 +695,7 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   a.ldr = ldr;
   a.epi = epi;
   a.trace = g_gemm_trace;
+  a.ktrace = g_gemm_ktrace;
   a.kb_total = (K + 63) / 64;
   const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms);
   if (s > 8) return -1;
@@ -722,6 +742,7 @@ int b200_gemm_q(const void* X, int M, int K, int ldx, const void* codes, const v
   a.ldr = ldr;
   a.epi = epi;
   a.trace = g_gemm_trace;
+  a.ktrace = g_gemm_ktrace;
   a.kb_total = K / 64;
   const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms, 1);
   if (s > 8) return -1;
@@ -772,6 +793,7 @@ int b200_gemm_bf16_ag(const void* comm_ctx, int phase, int parity, int M_real, i
   a.ldy = ldy;
   a.epi = epi;
   a.trace = g_gemm_trace;
+  a.ktrace = g_gemm_ktrace;
   a.kb_total = (K + 63) / 64;
   const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms);
   a.kb_per_split = (a.kb_total + s - 1) / s;
@@ -803,6 +825,7 @@ int b200_gemm_bf16_rs(const void* comm_ctx, int phase, int parity, const void* X
   a.K = K;
   a.epi = kEpiStoreF32;
   a.trace = g_gemm_trace;
+  a.ktrace = g_gemm_ktrace;
   a.kb_total = (K + 63) / 64;
   const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms);
   a.kb_per_split = (a.kb_total + s - 1) / s;

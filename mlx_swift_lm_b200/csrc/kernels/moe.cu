@@ -23,11 +23,14 @@
 #include <cudaTypedefs.h>
 
 #include "b200_common.cuh"
+#include "b200_dequant.cuh"
 
 namespace b200 {
 
 bool make_tmap_2d(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows,
                   int box_cols, int dtype_bytes);
+bool make_tmap_2d_sw(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems, int box_rows,
+                     int box_cols, int dtype_bytes, bool swizzle128);
 
 namespace moe {
 
@@ -243,18 +246,48 @@ __device__ __forceinline__ float glu(int epi, float g, float u) {
   return silu(g) * u;
 }
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(128, 1) grouped_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                         const __grid_constant__ CUtensorMap tmX, GArgs a) {
-  constexpr int kA = 128 * 128, kB = BN * 128, kStage = kA + kB;
-  constexpr int kTmem = BN < 32 ? 32 : BN;
+// Quantised expert weights (WQ = 4 or 8): codes [E*N, K*WQ/8] bytes,
+// scales / biases [K/gs, E*N] bf16 (layout of b200_dequant.cuh).
+struct GQuant {
+  CUtensorMap codes, scales, biases;
+  int gs;
+};
+
+// Operand stages {A bf16 weight tile, B activation tile}; with quantised
+// experts also a raw ring of small {codes, scales, biases} stages sized so two
+// CTAs fit on an SM (one CTA's start-up latency overlaps the other's stream).
+template <int BN, int STAGES, int WQ>
+struct GSmem {
+  static constexpr int kA = 128 * 128, kB = BN * 128;
+  static constexpr int kCode = WQ * 128 * 64 / 8, kGroup = 2 * 128 * 2;
+  static constexpr int kRaw = WQ ? kCode + 2 * kGroup : 0;
+  static constexpr int kStage = (kA + kB + 1023) / 1024 * 1024;
+  static constexpr int kRawStages = WQ ? (100 * 1024 - STAGES * kStage) / kRaw : 0;
+  static constexpr int kRawOff = STAGES * kStage;
+  static constexpr int kBars = (WQ ? 3 : 2) * STAGES + 2 * kRawStages + 1;
+  static constexpr int kTotal = kRawOff + kRawStages * kRaw + kBars * 8 + 16 + 1024;
+  static constexpr int kThreads = WQ ? 384 : 128;
+  static constexpr int kMinBlocks = WQ ? 2 : 1;
+  static constexpr int kTmem = BN < 32 ? 32 : BN;
+  static_assert(!WQ || kRawStages >= 4, "raw ring too shallow");
+};
+
+template <int BN, int STAGES, int WQ>
+__global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STAGES, WQ>::kMinBlocks)
+    grouped_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GArgs a,
+                   const __grid_constant__ GQuant q) {
+  using S = GSmem<BN, STAGES, WQ>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar_full = sbase + STAGES * kStage;
+  constexpr int RS = S::kRawStages;
+  const uint32_t bar_full = sbase + S::kRawOff + RS * S::kRaw;
   const uint32_t bar_empty = bar_full + 8 * STAGES;
   const uint32_t bar_acc = bar_empty + 8 * STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * kStage + (2 * STAGES + 1) * 8);
+  const uint32_t bar_aready = bar_acc + 8;
+  const uint32_t bar_rfull = bar_aready + 8 * STAGES;
+  const uint32_t bar_rempty = bar_rfull + 8 * RS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kRawOff + RS * S::kRaw + S::kBars * 8);
   __shared__ float xbuf[64][17];
   pdl_launch_dependents();
   pdl_wait();
@@ -268,62 +301,116 @@ __global__ void __launch_bounds__(128, 1) grouped_kernel(const __grid_constant__
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
+      if constexpr (WQ != 0) mbar_init(bar_aready + 8 * s, 8);
+    }
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(bar_rfull + 8 * s, 1);
+      mbar_init(bar_rempty + 8 * s, 8);
     }
     mbar_init(bar_acc, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kTmem);
+    tmem_alloc(smem_u32(tmem_slot), S::kTmem);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int gpb = WQ ? (q.gs >= 64 ? 1 : 64 / q.gs) : 0;
+  const int wrow = e * a.N + n0;
+  const uint64_t pw = l2_policy_evict_first(), px = l2_policy_evict_last();
   if (warp == 0 && lane == 0) {
-    const uint64_t pw = l2_policy_evict_first(), px = l2_policy_evict_last();
+    // operand producer: weight tile (bf16) + activation tile, or the
+    // activation tile alone (quantised: the dequantising warps write A)
+    const uint32_t tx_bytes = WQ ? (uint32_t)S::kB : (uint32_t)(S::kA + S::kB);
     int issued = 0;
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
-      mbar_arrive_expect_tx(bar_full + 8 * s, kStage);
-      tma_load_2d(sbase + s * kStage, &tmW, bar_full + 8 * s, i * 64, e * a.N + n0, pw);
-      tma_load_2d(sbase + s * kStage + kA, &tmX, bar_full + 8 * s, i * 64, r0, px);
+      const uint32_t st = sbase + s * S::kStage;
+      mbar_arrive_expect_tx(bar_full + 8 * s, tx_bytes);
+      if constexpr (WQ == 0) tma_load_2d(st, &tmW, bar_full + 8 * s, i * 64, wrow, pw);
+      tma_load_2d(st + S::kA, &tmX, bar_full + 8 * s, i * 64, r0, px);
       issued = i + 1;
     }
     for (int i = max(0, issued - STAGES); i < issued; ++i)
       mbar_wait(bar_full + 8 * (i % STAGES), (i / STAGES) & 1, kErrGemmWait);
+  } else if (warp == 2 && lane == 0) {
+    if constexpr (WQ != 0) {
+      // raw producer: codes + scales + biases, RS stages ahead
+      const uint32_t raw_tx = (uint32_t)(S::kCode + 2 * gpb * 256);
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % RS, r = i / RS;
+        if (r > 0 && !mbar_wait(bar_rempty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
+        const uint32_t raw = sbase + S::kRawOff + s * S::kRaw;
+        mbar_arrive_expect_tx(bar_rfull + 8 * s, raw_tx);
+        tma_load_2d(raw, &q.codes, bar_rfull + 8 * s, i * WQ * 8, wrow, pw);
+        const int g0 = q.gs >= 64 ? (i * 64) / q.gs : i * gpb;
+        tma_load_2d(raw + S::kCode, &q.scales, bar_rfull + 8 * s, wrow, g0, pw);
+        tma_load_2d(raw + S::kCode + S::kGroup, &q.biases, bar_rfull + 8 * s, wrow, g0, pw);
+        issued = i + 1;
+      }
+      for (int i = max(0, issued - RS); i < issued; ++i)
+        mbar_wait(bar_rfull + 8 * (i % RS), (i / RS) & 1, kErrGemmWait);
+    }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
+      if constexpr (WQ != 0) {
+        if (!mbar_wait(bar_aready + 8 * s, r & 1, kErrGemmWait)) break;
+      }
       tc_fence_after();
-      const uint64_t ad = umma_desc_k_sw128(sbase + s * kStage, 1024);
-      const uint64_t bd = umma_desc_k_sw128(sbase + s * kStage + kA, 1024);
+      const uint64_t ad = umma_desc_k_sw128(sbase + s * S::kStage, 1024);
+      const uint64_t bd = umma_desc_k_sw128(sbase + s * S::kStage + S::kA, 1024);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) tc_mma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
       tc_commit(bar_empty + 8 * s);
     }
     tc_commit(bar_acc);
+  } else if (warp >= 4) {
+    if constexpr (WQ != 0) {
+      const int t = (threadIdx.x - 128) & 127, half = (threadIdx.x - 128) >> 7;
+      const int g = q.gs == 32 ? half : 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int rs = i % RS, rr = i / RS;
+        const int s = i % STAGES, r = i / STAGES;
+        if (!mbar_wait(bar_rfull + 8 * rs, rr & 1, kErrGemmWait)) break;
+        if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
+        dequant_half_row<WQ>(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, g);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar_rempty + 8 * rs);
+          mbar_arrive(bar_aready + 8 * s);
+        }
+      }
+    }
   }
   __syncwarp();
   const bool ok = __syncthreads_and(mbar_wait(bar_acc, 0, kErrTmemWait) ? 1 : 0) != 0;
   tc_fence_after();
+  const bool ep = warp < 4;  // TMEM lanes 32*warp.. belong to warps 0..3
   const int rl = warp * 32 + lane;
-  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   const bool isglu = a.epi == 1 || a.epi == 4 || a.epi == 5;
-  const float bb = (a.bias && n0 + rl < a.N) ? bf2f(a.bias[(size_t)e * a.N + n0 + rl]) : 0.f;
+  const float bb = (ep && a.bias && n0 + rl < a.N) ? bf2f(a.bias[(size_t)e * a.N + n0 + rl]) : 0.f;
   for (int jc = 0; jc < BN; jc += 16) {
-    uint32_t v[16];
-    tmem_ld16(tl + jc, v);
-    tc_wait_ld();
     float f[16];
+    if (ep) {
+      uint32_t v[16];
+      tmem_ld16(tl + jc, v);
+      tc_wait_ld();
 #pragma unroll
-    for (int j = 0; j < 16; ++j) f[j] = ok ? __uint_as_float(v[j]) + bb : 0.f;
+      for (int j = 0; j < 16; ++j) f[j] = ok ? __uint_as_float(v[j]) + bb : 0.f;
+    }
     if (isglu) {
       __syncthreads();
-      if (warp >= 2) {
+      if (ep && warp >= 2) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) xbuf[rl - 64][j] = f[j];
       }
@@ -334,12 +421,12 @@ __global__ void __launch_bounds__(128, 1) grouped_kernel(const __grid_constant__
         for (int j = 0; j < 16; ++j) {
           const int row = jc + j;
           if (row < rc && fo < (a.N >> 1)) {
-            const float g = bf2f(f2bf(f[j])), u = bf2f(f2bf(xbuf[rl][j]));
-            a.Y[(size_t)(r0 + row) * a.ldy + fo] = f2bf(glu(a.epi, g, u));
+            const float gg = bf2f(f2bf(f[j])), u = bf2f(f2bf(xbuf[rl][j]));
+            a.Y[(size_t)(r0 + row) * a.ldy + fo] = f2bf(glu(a.epi, gg, u));
           }
         }
       }
-    } else if (n0 + rl < a.N) {
+    } else if (ep && n0 + rl < a.N) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int row = jc + j;
@@ -351,22 +438,37 @@ __global__ void __launch_bounds__(128, 1) grouped_kernel(const __grid_constant__
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmem);
+    tmem_dealloc(tmem, S::kTmem);
   }
 }
 
-template <int BN, int STAGES>
-int launch_grouped(const CUtensorMap& tw, const CUtensorMap& tx, const GArgs& a, int max_chunks, cudaStream_t st) {
-  constexpr int smem = STAGES * (128 * 128 + BN * 128) + (2 * STAGES + 1) * 8 + 16 + 1024;
+template <int BN, int STAGES, int WQ>
+int launch_grouped(const CUtensorMap& tw, const CUtensorMap& tx, const GArgs& a, const GQuant& q, int max_chunks,
+                   cudaStream_t st) {
+  using S = GSmem<BN, STAGES, WQ>;
+  static_assert(S::kTotal <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
   static bool cfg = false;
   if (!cfg) {
-    cudaError_t e = cudaFuncSetAttribute(grouped_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(grouped_kernel<BN, STAGES, WQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
     if (e != cudaSuccess) return (int)e;
     cfg = true;
   }
-  cudaError_t e = launch_k(grouped_kernel<BN, STAGES>, dim3((a.N + 127) / 128, max_chunks), dim3(128), smem, st, 1, tw,
-                           tx, a);
+  cudaError_t e = launch_k(grouped_kernel<BN, STAGES, WQ>, dim3((a.N + 127) / 128, max_chunks), dim3(S::kThreads),
+                           S::kTotal, st, 1, tw, tx, a, q);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+template <int WQ>
+int dispatch_grouped(int BN, const CUtensorMap& tw, const CUtensorMap& tx, const GArgs& a, const GQuant& q,
+                     int max_chunks, cudaStream_t st) {
+  switch (BN) {
+    case 16: return launch_grouped<16, WQ ? 3 : 6, WQ>(tw, tx, a, q, max_chunks, st);
+    case 32: return launch_grouped<32, WQ ? 3 : 6, WQ>(tw, tx, a, q, max_chunks, st);
+    case 64: return launch_grouped<64, WQ ? 2 : 4, WQ>(tw, tx, a, q, max_chunks, st);
+    case 128: return launch_grouped<128, WQ ? 2 : 4, WQ>(tw, tx, a, q, max_chunks, st);
+    default: return -1;
+  }
 }
 
 }  // namespace moe
@@ -429,13 +531,32 @@ int b200_moe_grouped_gemm(const void* xs, int P, int K, const void* W, int E, in
   if (!make_tmap_2d(&tx, xs, P, K, K, BN, 64, 2)) return -1;
   moe::GArgs a{reinterpret_cast<__nv_bfloat16*>(Y), reinterpret_cast<const __nv_bfloat16*>(bias), chunks, n_chunks,
                N, K, ldy, epi};
-  switch (BN) {
-    case 16: return moe::launch_grouped<16, 6>(tw, tx, a, max_chunks, st);
-    case 32: return moe::launch_grouped<32, 6>(tw, tx, a, max_chunks, st);
-    case 64: return moe::launch_grouped<64, 4>(tw, tx, a, max_chunks, st);
-    case 128: return moe::launch_grouped<128, 4>(tw, tx, a, max_chunks, st);
-    default: return -1;
-  }
+  moe::GQuant q = {};
+  return moe::dispatch_grouped<0>(BN, tw, tx, a, q, max_chunks, st);
+}
+
+// Same with affine-quantised experts: codes [E*N, K*bits/8], scales_t / biases_t [K/gs, E*N] bf16.
+int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* codes, const void* scales_t,
+                            const void* biases_t, int bits, int gs, int E, int N, void* Y, int ldy, const void* bias,
+                            int epi, const int* chunks, const int* n_chunks, int max_chunks, int BN, cudaStream_t st) {
+  if (P <= 0) return 0;
+  if ((K % 128) || (N % 8) || (bits != 4 && bits != 8) || (gs != 32 && gs != 64 && gs != 128)) return -1;
+  if (((uintptr_t)codes & 15) || ((uintptr_t)scales_t & 15) || ((uintptr_t)biases_t & 15)) return -1;
+  const int64_t rows = (int64_t)E * N;
+  const int64_t cb = (int64_t)K * bits / 8;
+  const int G = K / gs, gpb = gs >= 64 ? 1 : 64 / gs;
+  if ((rows * 2) % 16) return -1;
+  CUtensorMap tx;
+  moe::GQuant q;
+  q.gs = gs;
+  if (!make_tmap_2d(&tx, xs, P, K, K, BN, 64, 2)) return -1;
+  if (!make_tmap_2d_sw(&q.codes, codes, rows, cb, cb, 128, bits * 8, 1, false)) return -1;
+  if (!make_tmap_2d_sw(&q.scales, scales_t, G, rows, rows, gpb, 128, 2, false)) return -1;
+  if (!make_tmap_2d_sw(&q.biases, biases_t, G, rows, rows, gpb, 128, 2, false)) return -1;
+  moe::GArgs a{reinterpret_cast<__nv_bfloat16*>(Y), reinterpret_cast<const __nv_bfloat16*>(bias), chunks, n_chunks,
+               N, K, ldy, epi};
+  return bits == 4 ? moe::dispatch_grouped<4>(BN, tx, tx, a, q, max_chunks, st)
+                   : moe::dispatch_grouped<8>(BN, tx, tx, a, q, max_chunks, st);
 }
 
 }  // extern "C"

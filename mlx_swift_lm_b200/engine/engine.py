@@ -161,8 +161,16 @@ class EngineV2:
 
             self.graphs = DecodeGraphRunner(self)
         self._inflight = None  # chained decode: (plan rows, device tokens, event)
+        self.mtp = None  # MTPDriver when speculative decoding is enabled
         self.forward_shapes: list[tuple[int, int]] = []
         self.record_shapes = False
+
+    def enable_mtp(self, module, config=None):
+        """Speculative decoding with an MTP draft module (greedy rows)."""
+        from .mtp import MTPDriver
+
+        self.mtp = MTPDriver(self, module, config)
+        return self.mtp
 
     # ------------------------------------------------------------------ submit / cancel
     def submit(self, req: Request) -> RequestStream:
@@ -273,6 +281,17 @@ class EngineV2:
                 return events
             if self.record_shapes:
                 self.forward_shapes.append((len(plan.decode_rows), plan.num_tokens))
+            if self.mtp is not None and self.mtp.eligible(plan):
+                if self._inflight is not None:
+                    events += self._drain_inflight()
+                    self._step_started = None
+                    return events + self.step()
+                mev = self.mtp.round(plan)
+                if mev is not None:
+                    self.steps += 1
+                    self.last_step_ms = (time.perf_counter() - t0) * 1e3
+                    self._step_started = None
+                    return events + mev
             use_graph = (self.graphs is not None and plan.pure_decode and self.graphs.can_run(plan)
                          and not any(self._row_needs_eager(r.state) for r in plan.rows))
             if use_graph:
@@ -280,6 +299,9 @@ class EngineV2:
                 # optimistically advance: this step's input K/V is written and its output
                 # is a placeholder until the step is finalized.
                 prev = self._inflight
+                if self.mtp is not None:
+                    for r in plan.rows:
+                        self.mtp.drop(r.state)  # history broken: MTP restarts after an eager step
                 handle = self.graphs.launch(plan, chained_from=prev)
                 for r in plan.rows:
                     self.sched.commit(r)
@@ -296,7 +318,11 @@ class EngineV2:
                     self._step_started = None
                     return events + self.step()
                 fb = self._build_batch(plan, self.device)
-                logits = self.model.forward(fb, self.kv)
+                hid = None
+                if self.mtp is not None:
+                    logits, hid = self.model.forward(fb, self.kv, return_both=True)
+                else:
+                    logits = self.model.forward(fb, self.kv)
                 srows = [r for r in plan.rows if r.sample]
                 toks, lp = self.sampler.sample(logits, [r.state for r in srows])
                 toks_host = toks.cpu().tolist() if toks.numel() else []
@@ -304,8 +330,10 @@ class EngineV2:
                     self.sched.commit(r)
                     r.state.timing.prefill_chunks += 0 if r.is_decode else 1
                 lps = self.sampler.logprob_entries(lp, toks_host, [r.state for r in srows])
-                for r, t, l in zip(srows, toks_host, lps):
+                for i, (r, t, l) in enumerate(zip(srows, toks_host, lps)):
                     events += self._accept_token(r.state, int(t), l)
+                    if hid is not None and r.state.status != Status.FINISHED:
+                        self.mtp.on_first_token(r.state, hid[i])
             self.steps += 1
             self.last_step_ms = (time.perf_counter() - t0) * 1e3
             self._step_started = None
@@ -392,6 +420,8 @@ class EngineV2:
             tail = st.extra["hold"].push(st.detok.flush())[0] + st.extra["hold"].flush()
         st.timing.finished = now()
         st.finish_reason = reason
+        if self.mtp is not None:
+            self.mtp.drop(st)
         if self.prefix_cache is not None and reason in (FinishReason.STOP, FinishReason.LENGTH):
             self.prefix_cache.donate(st)
         self.sched.finish(st)

@@ -119,7 +119,7 @@ class DecoderLM:
         self.cos_sin, self.rot_dim = build_rope(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling,
                                                 cfg.max_position_embeddings, cfg.partial_rotary_factor)
         self.cos_sin = self.cos_sin.to(self.device)
-        self.lora = None  # optional LoRA manager (api.lora)
+        self.lora = None  # adapter whose update is currently added into the weights (adapters.lora)
         self.tp_fused = None  # fused symmetric-memory TP decode path (parallel.tp_fused)
 
     # ------------------------------------------------------------------ weights
@@ -135,7 +135,7 @@ class DecoderLM:
     def num_params(self) -> int:
         return sum(t.numel() for _, t in self.named_tensors() if t is not None)
 
-    def init_random(self, seed: int = 0, std: float = 0.02):
+    def init_random(self, seed: int = 0, std: float = 0.02, with_embeddings: bool = True):
         """Random N(0, std) weights (norm weights 1, sinks N(0,1)), generated on
         the model's device. Every rank draws the full tensors from the same
         seed and keeps its tensor-parallel shard, so a TP=N model computes the
@@ -180,9 +180,10 @@ class DecoderLM:
             return ref.interleave_gate_up(rows(gate, F_local), rows(up, F_local))
 
         hd = cfg.hidden_size
-        self.embed = rn(cfg.vocab_size, hd)
+        if with_embeddings:
+            self.embed = rn(cfg.vocab_size, hd)
+            self.lm_head = self.embed if cfg.tie_word_embeddings else rn(cfg.vocab_size, hd)
         self.norm = ones(hd)
-        self.lm_head = self.embed if cfg.tie_word_embeddings else rn(cfg.vocab_size, hd)
         self.layers = []
         for li in range(cfg.num_layers):
             L = LayerWeights()
@@ -285,13 +286,16 @@ class DecoderLM:
         return logits
 
     # ------------------------------------------------------------------ paged forward
-    def forward(self, fb: ForwardBatch, kv, return_hidden: bool = False):
+    def forward(self, fb: ForwardBatch, kv, return_hidden: bool = False, inputs_embeds: torch.Tensor | None = None,
+                return_both: bool = False):
         """Paged-KV forward over a flattened batch. Returns fp32 logits for
-        ``fb.logit_idx`` rows (all tokens when None)."""
+        ``fb.logit_idx`` rows (all tokens when None); with `return_hidden` the
+        final-normed hidden rows instead, with `return_both` (logits, hidden).
+        `inputs_embeds` [T, H] replaces the token embedding (MTP modules)."""
         cfg = self.cfg
         T = fb.num_tokens
         nd = fb.num_decode
-        x = ops.embedding(fb.input_ids, self.embed, cfg.embed_scale)
+        x = inputs_embeds if inputs_embeds is not None else ops.embedding(fb.input_ids, self.embed, cfg.embed_scale)
         delta = None
         attn = torch.empty((T, self.H, self.D), dtype=x.dtype, device=x.device)
         for li, L in enumerate(self.layers):
@@ -299,8 +303,6 @@ class DecoderLM:
                 pass
             h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
             qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
-            if self.lora is not None:
-                qkv = self.lora.apply(li, "qkv", h, qkv, fb)
             kc, vc = kv.layer(li)
             q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
                                     L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
@@ -328,6 +330,8 @@ class DecoderLM:
             h = ops.add_rmsnorm(x, delta, self.norm, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
         if return_hidden:
             return h
+        if return_both:
+            return self._final_logits(h), h
         return self._final_logits(h)
 
     # ------------------------------------------------------------------ decode step -> tokens

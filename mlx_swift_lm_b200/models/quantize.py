@@ -1,0 +1,38 @@
+"""Quantise a built model's weights in place to MLX-style affine codes kept
+packed on the device (:class:`QuantizedWeight`), e.g. to run a random-init
+model in the quantised serving configuration of a checkpoint.
+
+Parity: MLXLMCommon quantize (``quantize(model:groupSize:bits:)`` with a
+per-layer predicate), applied here to the fused projection layouts: dense
+projections (q|k|v, o, gate/up, down), MoE expert stacks (gate/up, down) and,
+optionally, the LM head. Embedding tables stay bf16 (rows are gathered).
+"""
+from __future__ import annotations
+
+import torch
+
+from ..ops.qlinear import QuantizedWeight
+
+
+def _q(t: torch.Tensor, bits: int, gs: int, device) -> QuantizedWeight:
+    return QuantizedWeight.quantize(t.float().cpu(), bits, gs).to(device)
+
+
+def quantize_model(model, bits: int = 4, group_size: int = 64, dense: bool = True, experts: bool = True,
+                   lm_head: bool = False):
+    dev = model.device
+    for L in model.layers:
+        if dense:
+            for name in ("wqkv", "wo", "wgu", "wd", "shared_gu", "shared_d"):
+                t = getattr(L, name)
+                if isinstance(t, torch.Tensor) and t.shape[1] % group_size == 0 and t.shape[0] % 8 == 0:
+                    setattr(L, name, _q(t, bits, group_size, dev))
+        if experts and L.moe and isinstance(L.experts_gu, torch.Tensor):
+            E = L.experts_gu.shape[0]
+            L.experts_gu = QuantizedWeight.stack_experts([_q(L.experts_gu[e], bits, group_size, "cpu")
+                                                          for e in range(E)]).to(dev)
+            L.experts_d = QuantizedWeight.stack_experts([_q(L.experts_d[e], bits, group_size, "cpu")
+                                                         for e in range(E)]).to(dev)
+    if lm_head and isinstance(model.lm_head, torch.Tensor) and model.lm_head is not model.embed:
+        model.lm_head = _q(model.lm_head, bits, group_size, dev)
+    return model

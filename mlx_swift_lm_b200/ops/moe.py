@@ -23,6 +23,7 @@ import torch
 
 from . import _lib
 from .linear import gemm
+from .qlinear import QuantizedWeight
 
 _EPI = {"none": 0, "swiglu": 1, "geglu": 4, "swiglu_oai": 5}
 
@@ -37,6 +38,9 @@ _lib.register_signatures({
     "b200_moe_grouped_gemm": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.vp,
                                          _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.i32, _lib.i32,
                                          _lib.vp]),
+    "b200_moe_grouped_gemm_q": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.vp, _lib.i32,
+                                           _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.i32,
+                                           _lib.vp, _lib.vp, _lib.i32, _lib.i32, _lib.vp]),
 }, status_tags=("moe",))
 
 
@@ -77,11 +81,27 @@ def chunk_rows(P: int, E: int) -> int:
     return 128
 
 
+def _grouped(L, xs, P, K, W, E, N, Y, ldy, bias, epi, chunks, n_chunks, max_chunks, BN, st, what):
+    if isinstance(W, QuantizedWeight):
+        rc = L.b200_moe_grouped_gemm_q(xs.data_ptr(), P, K, W.codes.data_ptr(), W.scales_t.data_ptr(),
+                                       W.biases_t.data_ptr(), W.bits, W.gs, E, N, Y.data_ptr(), ldy, _lib.ptr(bias),
+                                       epi, chunks.data_ptr(), n_chunks.data_ptr(), max_chunks, BN, st)
+    else:
+        rc = L.b200_moe_grouped_gemm(xs.data_ptr(), P, K, W.data_ptr(), E, N, Y.data_ptr(), ldy, _lib.ptr(bias), epi,
+                                     chunks.data_ptr(), n_chunks.data_ptr(), max_chunks, BN, st)
+    _lib.check(rc, f"moe_grouped_gemm {what}")
+
+
 def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias):
     T, K = h.shape
     k = idx.shape[1]
-    E, N2, _ = experts_gu.shape
-    F = experts_d.shape[2]
+    if isinstance(experts_gu, QuantizedWeight):
+        E = experts_gu.num_experts
+        N2 = experts_gu.shape[0] // E
+        F = experts_d.shape[1]
+    else:
+        E, N2, _ = experts_gu.shape
+        F = experts_d.shape[2]
     assert N2 == 2 * F and N2 % 128 == 0, "gate/up rows must be 2*F, a multiple of 128 (64-row interleave)"
     P = T * k
     dev = h.device
@@ -103,12 +123,9 @@ def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias):
     _lib.check(L.b200_moe_sort(ids.data_ptr(), P, E, BN, max_chunks, perm.data_ptr(), pos.data_ptr(),
                                chunks.data_ptr(), n_chunks.data_ptr(), st), "moe_sort")
     _lib.check(L.b200_moe_gather(hc.data_ptr(), K, perm.data_ptr(), P, k, xs.data_ptr(), st), "moe_gather")
-    _lib.check(L.b200_moe_grouped_gemm(xs.data_ptr(), P, K, experts_gu.data_ptr(), E, N2, gu.data_ptr(), F,
-                                       _lib.ptr(gu_bias), _EPI[epi], chunks.data_ptr(), n_chunks.data_ptr(),
-                                       max_chunks, BN, st), "moe_grouped_gemm gate/up")
-    _lib.check(L.b200_moe_grouped_gemm(gu.data_ptr(), P, F, experts_d.data_ptr(), E, K, ys.data_ptr(), K,
-                                       _lib.ptr(d_bias), 0, chunks.data_ptr(), n_chunks.data_ptr(), max_chunks, BN,
-                                       st), "moe_grouped_gemm down")
+    _grouped(L, xs, P, K, experts_gu, E, N2, gu, F, gu_bias, _EPI[epi], chunks, n_chunks, max_chunks, BN, st,
+             "gate/up")
+    _grouped(L, gu, P, F, experts_d, E, K, ys, K, d_bias, 0, chunks, n_chunks, max_chunks, BN, st, "down")
     _lib.check(L.b200_moe_combine(ys.data_ptr(), T, K, pos.data_ptr(), w.data_ptr(), k, out.data_ptr(), None, None,
                                   st), "moe_combine")
     _lib.count(5)
@@ -120,13 +137,17 @@ def moe_experts(h, experts_gu, experts_d, w, idx, epi="swiglu", gu_bias=None, d_
     w [T, k] fp32 weights; idx [T, k] expert ids. Returns [T, K] in h.dtype."""
     if h.is_cuda:
         return _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias)
+    if isinstance(experts_gu, QuantizedWeight):
+        E = experts_gu.num_experts
+        experts_gu = torch.stack([experts_gu.expert(e).dequantize(torch.float32) for e in range(E)]).to(h.dtype)
+        experts_d = torch.stack([experts_d.expert(e).dequantize(torch.float32) for e in range(E)]).to(h.dtype)
     T, K = h.shape
     k = idx.shape[1]
     flat = idx.reshape(-1).long()
     order = torch.argsort(flat, stable=True)
     tok = order // k
     wsorted = w.reshape(-1)[order]
-    counts = torch.bincount(flat, minlength=experts_gu.shape[0]).tolist()
+    counts = torch.bincount(flat, minlength=experts_gu.shape[0]).tolist()  # experts dim
     out = torch.zeros((T, K), dtype=torch.float32, device=h.device)
     start = 0
     for e, c in enumerate(counts):

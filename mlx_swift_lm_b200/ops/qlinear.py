@@ -53,11 +53,14 @@ def _unpack4(c: torch.Tensor) -> torch.Tensor:
 class QuantizedWeight:
     """Packed affine weight of logical shape [N, K]."""
 
-    def __init__(self, codes: torch.Tensor, scales_t: torch.Tensor, biases_t: torch.Tensor, bits: int, gs: int):
+    def __init__(self, codes: torch.Tensor, scales_t: torch.Tensor, biases_t: torch.Tensor, bits: int, gs: int,
+                 num_experts: int = 0):
         assert bits in SUPPORTED_BITS and gs in SUPPORTED_GROUPS, (bits, gs)
         self.codes, self.scales_t, self.biases_t = codes, scales_t, biases_t
         self.bits, self.gs = bits, gs
         self.shape = (codes.shape[0], codes.shape[1] * 8 // bits)
+        # > 0: MoE experts stacked along rows, expert e owns rows [e*N/E, (e+1)*N/E)
+        self.num_experts = num_experts
 
     # ---------------------------------------------------------------- construction
     @classmethod
@@ -105,7 +108,25 @@ class QuantizedWeight:
         dt = dtype if dtype in (torch.bfloat16, torch.float16, torch.float32) else None
         sc = self.scales_t.to(device=device, dtype=dt or self.scales_t.dtype)
         bi = self.biases_t.to(device=device, dtype=dt or self.biases_t.dtype)
-        return QuantizedWeight(self.codes.to(device), sc, bi, self.bits, self.gs)
+        return QuantizedWeight(self.codes.to(device), sc, bi, self.bits, self.gs, self.num_experts)
+
+    def select_rows(self, idx: torch.Tensor, num_experts: int = 0) -> "QuantizedWeight":
+        """Rows `idx` (any order) as a new weight."""
+        idx = idx.to(self.codes.device)
+        return QuantizedWeight(self.codes.index_select(0, idx).contiguous(),
+                               self.scales_t.index_select(1, idx).contiguous(),
+                               self.biases_t.index_select(1, idx).contiguous(), self.bits, self.gs, num_experts)
+
+    @staticmethod
+    def stack_experts(parts: list["QuantizedWeight"]) -> "QuantizedWeight":
+        """Experts [E] of shape [N, K] -> one weight [E*N, K] with num_experts = E."""
+        w = QuantizedWeight.cat_rows(parts)
+        w.num_experts = len(parts)
+        return w
+
+    def expert(self, e: int) -> "QuantizedWeight":
+        n = self.shape[0] // self.num_experts
+        return self.rows(e * n, (e + 1) * n)
 
     def numel(self) -> int:
         return self.shape[0] * self.shape[1]

@@ -125,3 +125,37 @@ def test_moe_model_logits_close_to_cpu_oracle():
     # bf16 router logits may flip a near-tied expert choice for a few tokens,
     # so the bound is looser than the dense model's
     assert _rel(lg, r) < 0.15
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("T", [1, 64, 300])
+def test_moe_experts_quantized(bits, T):
+    from mlx_swift_lm_b200.ops.qlinear import QuantizedWeight
+
+    torch.manual_seed(T + bits)
+    E, k, K, F = 16, 4, 512, 256
+    h = torch.randn(T, K, device=DEV, dtype=torch.bfloat16)
+    gu_f = [ref.interleave_gate_up(torch.randn(F, K) * 0.05, torch.randn(F, K) * 0.05) for _ in range(E)]
+    d_f = [torch.randn(K, F) * 0.05 for _ in range(E)]
+    gu = QuantizedWeight.stack_experts([QuantizedWeight.quantize(t, bits, 64) for t in gu_f]).to(DEV)
+    d = QuantizedWeight.stack_experts([QuantizedWeight.quantize(t, bits, 64) for t in d_f]).to(DEV)
+    w, idx = moe.route_topk(torch.randn(T, E, device=DEV), k)
+    y = moe.moe_experts(h, gu, d, w, idx)
+    gud = torch.stack([gu.expert(e).dequantize() for e in range(E)])
+    dd = torch.stack([d.expert(e).dequantize() for e in range(E)])
+    r = _moe_ref(h.cpu(), gud.to(torch.bfloat16).cpu(), dd.to(torch.bfloat16).cpu(), w.cpu(), idx.cpu(), "swiglu")
+    assert _rel(y.cpu(), r) < 2e-2
+
+
+def test_quantized_moe_model_graph_matches_eager():
+    from mlx_swift_lm_b200.models.quantize import quantize_model
+
+    m = quantize_model(_moe_model(seed=5), bits=4, group_size=64)
+    g = torch.Generator().manual_seed(2)
+    ps = [torch.randint(0, m.cfg.vocab_size, (n,), generator=g).tolist() for n in (12, 30)]
+
+    def eng(graphs):
+        return EngineV2(m, config=EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=4),
+                                               max_model_len=256, use_cuda_graphs=graphs, graph_buckets=(1, 2, 4)))
+
+    assert eng(True).generate(ps, max_tokens=12) == eng(False).generate(ps, max_tokens=12)

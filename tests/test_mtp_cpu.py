@@ -1,0 +1,78 @@
+"""MTP speculative decoding in the engine (tiny Qwen3, fp32, CPU): exact
+greedy acceptance reproduces plain greedy decoding token for token; the
+Bernoulli acceptance schedule emits a+1 tokens per round with consistent
+target / MTP K/V lengths."""
+import torch
+
+from mlx_swift_lm_b200 import DecoderLM, EngineConfig, EngineV2, SchedulerConfig
+from mlx_swift_lm_b200.engine.mtp import MTPConfig
+from mlx_swift_lm_b200.engine.types import Request, SamplingParams
+from mlx_swift_lm_b200.models.config import tiny_qwen3
+from mlx_swift_lm_b200.models.mtp import MTPModule
+
+
+def _model(seed=0):
+    return DecoderLM(tiny_qwen3(), "cpu", torch.float32).init_random(seed, std=0.2)
+
+
+def _eng(m):
+    return EngineV2(m, config=EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=4, prefill_chunk_size=32),
+                                           max_model_len=256, use_cuda_graphs=False))
+
+
+def _prompts(vocab, lens, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(0, vocab, (n,), generator=g).tolist() for n in lens]
+
+
+def test_mtp_exact_matches_greedy():
+    m = _model()
+    ps = _prompts(m.cfg.vocab_size, (9, 23, 40))
+    ref = _eng(m).generate(ps, max_tokens=24)
+    eng = _eng(m)
+    mod = MTPModule(m).init_random(3, std=0.2)
+    drv = eng.enable_mtp(mod, MTPConfig(k=3))
+    out = eng.generate(ps, max_tokens=24)
+    assert out == ref
+    assert drv.stats.rounds > 0 and drv.stats.drafted > 0
+
+
+def test_mtp_self_draft_accepts_everything():
+    """An MTP 'module' that copies the target's own prediction (its layer is
+    the target's first layer ... replaced by an oracle hook) is not needed:
+    with acceptance forced to 1 the round emits k+1 tokens every time."""
+    m = _model(seed=2)
+    ps = _prompts(m.cfg.vocab_size, (17, 5), seed=4)
+    eng = _eng(m)
+    drv = eng.enable_mtp(MTPModule(m).init_random(5, std=0.2), MTPConfig(k=3, acceptance="bernoulli", p=1.0))
+    streams = [eng.submit(Request(prompt_tokens=p, max_tokens=21, sampling=SamplingParams(temperature=0.0),
+                                  ignore_eos=True)) for p in ps]
+    eng.run_until_idle()
+    for s in streams:
+        assert len(s.tokens()) == 21
+    assert drv.stats.accepted == drv.stats.drafted  # p = 1: every draft accepted
+    # 1 token from prefill + rounds of k+1 = 4: 20 = 5 rounds per row
+    assert drv.stats.rows == 10
+
+
+def test_mtp_bernoulli_kv_consistency():
+    m = _model(seed=3)
+    ps = _prompts(m.cfg.vocab_size, (30, 12, 7, 50), seed=6)
+    eng = _eng(m)
+    drv = eng.enable_mtp(MTPModule(m).init_random(7, std=0.2), MTPConfig(k=3, acceptance="bernoulli", p=0.7, seed=11))
+    streams = [eng.submit(Request(prompt_tokens=p, max_tokens=30, sampling=SamplingParams(temperature=0.0),
+                                  ignore_eos=True)) for p in ps]
+    for _ in range(8):
+        eng.step()
+        for s in streams:
+            st = s.st
+            if st.status.name == "RUNNING" and st.num_output > 0:
+                # every committed token has K/V except the pending last one
+                assert st.seq.num_tokens == len(st.all_tokens) - 1
+                if "mtp_m" in st.extra:
+                    assert st.extra["mtp_seq"].num_tokens == st.extra["mtp_m"] - st.extra["mtp_p0"]
+                    assert st.extra["mtp_h"].shape[0] == len(st.all_tokens) - st.extra["mtp_m"]
+    eng.run_until_idle()
+    assert all(len(s.tokens()) == 30 for s in streams)
+    r = drv.stats.acceptance_rate
+    assert 0.4 < r < 0.95, r
