@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--tp-mode", default="nccl", choices=["fused", "nccl"],
                     help="tensor-parallel collectives: fused symmetric-memory kernels or NCCL all-reduce")
+    ap.add_argument("--quant-experts", type=int, default=0, help="MLX affine bits for MoE experts (0 = bf16)")
+    ap.add_argument("--quant-dense", type=int, default=0, help="MLX affine bits for dense projections (0 = bf16)")
+    ap.add_argument("--mtp", type=int, default=0, help="MTP draft depth k (0 = off); acceptance: seeded Bernoulli(0.7)")
     return ap.parse_args()
 
 
@@ -115,6 +118,77 @@ def reference_arm(args):
     return 0
 
 
+def _mtp_measure(args, eng, mtp, streams, dev, world, rank, ttfts, prefill_s, cfg, barrier, ClockSampler, local, _lib):
+    """MTP rounds are eager (draft steps + one batched verify): value = tokens
+    emitted per second over K engine steps timed with CUDA events on the
+    device; e2e = wall clock over K further steps (inputs host->device, tokens
+    device->host every step)."""
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(args.warmup):
+        eng.step()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    tok0 = sum(s.st.num_output for s in streams)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    n0 = _lib.launch_counter[0]
+    for _ in range(args.steps):
+        eng.step()
+    e1.record()
+    barrier()
+    launches = _lib.launch_counter[0] - n0
+    dev_ms = e0.elapsed_time(e1)
+    dev_tokens = sum(s.st.num_output for s in streams) - tok0
+    tok1 = sum(s.st.num_output for s in streams)
+    h2d0, d2h0 = mtp.h2d_bytes, mtp.d2h_bytes
+    t0 = time.perf_counter()
+    step_times = []
+    for _ in range(args.steps):
+        ts = time.perf_counter()
+        eng.step()
+        step_times.append(time.perf_counter() - ts)
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    e2e_tokens = sum(s.st.num_output for s in streams) - tok1
+    h2d = (mtp.h2d_bytes - h2d0) / args.steps
+    d2h = (mtp.d2h_bytes - d2h0) / args.steps
+    clk = clocks.stop()
+    t = torch.tensor([dev_ms, e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_s = t.tolist()
+    st = mtp.stats
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(dev_tokens / (dev_ms / 1e3), 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random token ids, random-init N(0,0.02) weights; MTP acceptance from a seeded "
+                    "Bernoulli(0.7) schedule)",
+            "config": {"model": f"{args.model}-shape" + (f" ({cfg.num_layers} layers, DEBUG)" if args.layers else ""),
+                       "global_batch": args.streams,
+                       "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}] + {args.out_tokens} out",
+                       "parallelism": f"tp{world}",
+                       "experts": f"q{args.quant_experts} g64" if args.quant_experts else "bf16", "mtp_k": args.mtp,
+                       "kv": "paged bf16, page 16", "l2": "inputs larger than L2 (weights + KV per step)"},
+            "mtp": {"rounds": st.rounds, "acceptance": round(st.acceptance_rate, 3),
+                    "tokens_per_row_round": round(st.emitted / max(st.rows, 1), 3)},
+            "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
+            "itl_p50_ms": round(statistics.median(step_times) * 1e3, 3), "prefill_s": round(prefill_s, 3),
+            "e2e": {"value": round(e2e_tokens / e2e_s, 2), "unit": "tok/s", "api": "EngineV2.step (MTP rounds)",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": int(launches), "clocks": clk, "kernel_status": _lib.read_status(),
+        }
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -146,6 +220,14 @@ def main():
         cfg.num_layers = args.layers
     tp = TensorParallel(rank, world, group)
     model = DecoderLM(cfg, dev, torch.bfloat16, tp=tp).init_random(args.seed)
+    if args.quant_experts or args.quant_dense:
+        from mlx_swift_lm_b200.models.quantize import quantize_model
+
+        if args.quant_experts:
+            quantize_model(model, bits=args.quant_experts, group_size=64, dense=False, experts=True)
+        if args.quant_dense:
+            quantize_model(model, bits=args.quant_dense, group_size=64, dense=True, experts=False)
+        torch.cuda.empty_cache()
     if world > 1 and args.tp_mode == "fused":
         model.enable_fused_tp(args.streams)
     max_len = args.max_prompt + args.out_tokens + 16
@@ -154,6 +236,17 @@ def main():
                         max_model_len=max_len, use_cuda_graphs=True, chained_decode=True,
                         graph_buckets=(args.streams,))
     eng = EngineV2(model, config=ecfg)
+    mtp = None
+    if args.mtp:
+        from mlx_swift_lm_b200.engine.mtp import MTPConfig
+        from mlx_swift_lm_b200.models.mtp import MTPModule
+
+        mod = MTPModule(model).init_random(args.seed + 1)
+        if args.quant_experts:
+            from mlx_swift_lm_b200.models.quantize import quantize_model
+
+            quantize_model(mod.inner, bits=args.quant_experts, group_size=64, dense=False, experts=True)
+        mtp = eng.enable_mtp(mod, MTPConfig(k=args.mtp, acceptance="bernoulli", p=0.7, seed=args.seed))
 
     rng = np.random.default_rng(args.seed)
     lens = rng.integers(args.min_prompt, args.max_prompt + 1, size=args.streams)
@@ -176,6 +269,9 @@ def main():
     prefill_s = time.perf_counter() - t_pf
     ttfts = [s.st.timing.ttft for s in streams]
 
+    if mtp is not None:
+        return _mtp_measure(args, eng, mtp, streams, dev, world, rank, ttfts, prefill_s, cfg, barrier, ClockSampler,
+                            local, _lib)
     # ---- kernel-only value: replays of the captured decode-step graph ----
     g = eng.graphs
     # one real chained decode step captures/launches the 64-row graph with live inputs

@@ -10,6 +10,8 @@ Two shared objects are produced under ``mlx_swift_lm_b200/_lib/``:
   module.
 
 Sources are rebuilt only when they (or a header) are newer than the output.
+Run it as a script (``python mlx_swift_lm_b200/_build.py``): importing the
+package needs the host module that this build produces.
 """
 from __future__ import annotations
 

@@ -134,6 +134,16 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
   }
 }
 
+// Contiguous global -> shared copy by the bulk-copy engine, completing on an
+// mbarrier (transaction bytes). Addresses and size must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // TMA tiled loads into this CTA's shared memory. Coordinates are element
 // indices, innermost first.

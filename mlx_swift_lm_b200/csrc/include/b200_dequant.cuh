@@ -1,10 +1,12 @@
 // Affine-quantised weight tiles -> bf16 MMA operand tiles in shared memory.
 //
-// Raw tile of one 64-input K block for 128 weight rows (TMA, no swizzle):
+// Raw record of one 64-input K block for 128 weight rows (one contiguous
+// bulk copy from the tile-major device layout):
 //   codes   [128][WQ * 8] bytes. 8-bit: one code per byte in input order.
 //           4-bit: 32-bit words of 8 inputs; input 2j in bits 4j..4j+3 and
 //           input 2j+1 in bits 16+4j..19+4j (repacked from MLX at load).
-//   scales  [groups][128] bf16, biases [groups][128] bf16 (groups = 1 or 2).
+//   scales  [gpb][128] bf16, then biases [gpb][128] bf16 (gpb = groups in the
+//           block: 2 for group size 32, else 1).
 // w = scale * q + bias with one rounding to bf16.
 // Output: row t of a K-major bf16 tile [128][64] with the 128-byte swizzle
 // the UMMA descriptor expects (16-byte chunk c of row t at c ^ (t & 7)).
@@ -28,11 +30,11 @@ __device__ __forceinline__ uint32_t dq4_pair(uint32_t v, __nv_bfloat162 s2, __nv
 // Thread (t, half) converts inputs [32*half, 32*half + 32) of row t. `g` is
 // the group of that half (0, or `half` when the group size is 32).
 template <int WQ>
-__device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* atile, int t, int half, int g) {
+__device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* atile, int t, int half, int g,
+                                                 int gpb) {
   constexpr int kCodeBytes = WQ * 128 * 64 / 8;
-  constexpr int kGroupBytes = 2 * 128 * 2;
   const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes);
-  const __nv_bfloat16* bi = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes + kGroupBytes);
+  const __nv_bfloat16* bi = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes + gpb * 256);
   const __nv_bfloat16 sv = sc[g * 128 + t], bv = bi[g * 128 + t];
   uint8_t* arow = atile + t * 128;
   if constexpr (WQ == 4) {
@@ -67,6 +69,43 @@ __device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* at
       }
       const int chunk = half * 4 + h;
       *reinterpret_cast<uint4*>(arow + ((chunk ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// Same conversion into 16 registers of packed bf16 pairs (inputs 32*half +
+// 2c and 2c+1 in register c): 16 consecutive 32-bit tensor-memory columns of
+// lane t, the layout of an MMA A operand read from tensor memory.
+template <int WQ>
+__device__ __forceinline__ void dequant_half_row_regs(const uint8_t* raw, int t, int half, int g, int gpb,
+                                                      uint32_t* v) {
+  constexpr int kCodeBytes = WQ * 128 * 64 / 8;
+  const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes);
+  const __nv_bfloat16* bi = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes + gpb * 256);
+  const __nv_bfloat16 sv = sc[g * 128 + t], bv = bi[g * 128 + t];
+  if constexpr (WQ == 4) {
+    const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
+    const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+    const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv), b2 = __halves2bfloat162(bv, bv);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t x = words[w];
+      v[4 * w + 0] = dq4_pair(x, s2, b2);
+      v[4 * w + 1] = dq4_pair(x >> 4, s2, b2);
+      v[4 * w + 2] = dq4_pair(x >> 8, s2, b2);
+      v[4 * w + 3] = dq4_pair(x >> 12, s2, b2);
+    }
+  } else {
+    static_assert(WQ == 8, "4- or 8-bit codes");
+    const uint4* cw = reinterpret_cast<const uint4*>(raw + t * 64 + half * 32);
+    const uint4 q0 = cw[0], q1 = cw[1];
+    const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const float sf = bf2f(sv), bf = bf2f(bv);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t x = words[w];
+      v[2 * w] = pack_bf16x2(fmaf((float)(x & 0xFF), sf, bf), fmaf((float)((x >> 8) & 0xFF), sf, bf));
+      v[2 * w + 1] = pack_bf16x2(fmaf((float)((x >> 16) & 0xFF), sf, bf), fmaf((float)(x >> 24), sf, bf));
     }
   }
 }

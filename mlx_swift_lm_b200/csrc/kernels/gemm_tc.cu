@@ -72,12 +72,17 @@ struct GemmArgs {
 // Shared-memory plan of one CTA.
 // bf16 weights (WQ = 0): STAGES stages of {A weight tile (TMA), B activation
 // tile}, barriers full/empty per stage.
-// Quantised weights (WQ = 4 / 8): two rings. A deep raw ring of kRawStages
-// small stages {codes [128][WQ*8 B], scales, biases [groups][128] bf16} keeps
-// enough weight bytes in flight to cover DRAM latency (a 4-bit stage is only
-// 5 KB); STAGES operand stages {A bf16 tile written by the dequantising warps,
-// B activation tile (TMA)} feed the MMA. Barriers: raw_full/raw_empty per raw
-// stage, x_full/a_ready/a_empty per operand stage.
+// Quantised weights (WQ = 4 / 8): a deep raw ring of kRawStages records
+// {codes [128][WQ*8 B], scales, biases [gpb][128] bf16}, one contiguous bulk
+// copy each (a 4-bit record is only 4.5-5 KB, so many are in flight to cover
+// DRAM latency). Eight dequantising warps (two groups of four taking
+// alternate K blocks) expand a record into the bf16 A
+// tile and write it straight into tensor memory (tcgen05.st; 32 columns per
+// stage after the accumulator); the MMA reads A from there (tcgen05.mma with
+// an A operand in tensor memory), so shared-memory stages hold only the
+// activation tile. Barriers: full[s] (activation bytes + one arrive per
+// dequantising warp + the producer's arrive), empty[s] (MMA consumed the
+// stage), rfull/rempty per raw record.
 template <int BN, int STAGES, int WQ = 0>
 struct GemmSmem {
   static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
@@ -85,7 +90,7 @@ struct GemmSmem {
   static constexpr int kCodeBytes = WQ * 128 * 64 / 8;
   static constexpr int kGroupBytes = 2 * 128 * 2;  // up to 2 groups x 128 rows x bf16
   static constexpr int kRawBytes = WQ ? kCodeBytes + 2 * kGroupBytes : 0;
-  static constexpr int kStageBytes = (kABytes + kBBytes + 1023) / 1024 * 1024;
+  static constexpr int kStageBytes = ((WQ ? 0 : kABytes) + kBBytes + 1023) / 1024 * 1024;
   static constexpr int kPipeBytes = STAGES * kStageBytes;
   static constexpr int kRawBudget = 200 * 1024 - kPipeBytes;
   static constexpr int kRawStages = WQ ? (kRawBudget / kRawBytes > 24 ? 24 : kRawBudget / kRawBytes) : 0;
@@ -94,9 +99,13 @@ struct GemmSmem {
   static constexpr int kPartBytes = BN * 128 * 4;  // fp32 partial [BN][128]
   static constexpr int kMain = kAllPipe > kPartBytes ? kAllPipe : kPartBytes;
   static constexpr int kBarOffset = (kMain + 7) / 8 * 8;
-  static constexpr int kNumBars = (WQ ? 3 : 2) * STAGES + 2 * kRawStages + 1;
+  static constexpr int kNumBars = 2 * STAGES + 1 + (WQ ? 2 * kRawStages : 0);
   static constexpr int kTotal = kBarOffset + kNumBars * 8 + 16 + 1024;  // + alignment slack
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kNeedCols = kAccCols + (WQ ? STAGES * 32 : 0);
+  static constexpr int kTmemCols = kNeedCols <= 32 ? 32 : kNeedCols <= 64 ? 64 : kNeedCols <= 128 ? 128
+                                   : kNeedCols <= 256 ? 256 : 512;
+  static_assert(kNeedCols <= 512, "tensor memory plan exceeds 512 columns");
   static constexpr int kThreads = WQ ? 384 : 128;  // + 8 dequantising warps (two per SM sub-partition)
   static_assert(!WQ || kRawStages >= 4, "raw ring too shallow");
 };
@@ -131,8 +140,8 @@ struct CollArgs {
 // nibble j of the low half-word and nibble j of the high half-word hold inputs
 // 2j and 2j+1 of the word's 8); scales / biases: [K/gs, N] bf16.
 struct QArgs {
-  CUtensorMap codes, scales, biases;
-  int gs;
+  const uint8_t* tiled;  // tile-major records [N/128][K/64][rec_bytes]
+  int gs, gpb, rec_bytes, kb_total;
 };
 
 template <int BN, int STAGES, int MODE, int WQ>
@@ -145,12 +154,11 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   constexpr int RS = S::kRawStages;
-  const uint32_t bar_full = sbase + S::kBarOffset;  // bf16: stage full; quantised: activation tile landed
-  const uint32_t bar_empty = bar_full + STAGES * 8;  // operand stage consumed by the MMA
+  const uint32_t bar_full = sbase + S::kBarOffset;   // [STAGES] operands of the stage in place
+  const uint32_t bar_empty = bar_full + STAGES * 8;  // [STAGES] stage consumed by the MMA
   const uint32_t bar_accum = bar_empty + STAGES * 8;
-  const uint32_t bar_aready = bar_accum + 8;               // [STAGES] quantised: bf16 A tile written
-  const uint32_t bar_rfull = bar_aready + STAGES * 8;      // [RS] raw stage landed
-  const uint32_t bar_rempty = bar_rfull + RS * 8;          // [RS] raw stage consumed
+  const uint32_t bar_rfull = bar_accum + 8;          // [RS] quantised: raw record landed
+  const uint32_t bar_rempty = bar_rfull + RS * 8;    // [RS] quantised: raw record consumed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kBarOffset + S::kNumBars * 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -169,13 +177,12 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     if constexpr (WQ == 0) tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_full + 8 * s, WQ ? 5 : 1);  // quantised: activation producer + four dequantising warps
       mbar_init(bar_empty + 8 * s, 1);
-      if constexpr (WQ != 0) mbar_init(bar_aready + 8 * s, 8);  // one arrive per dequantising warp
     }
     for (int s = 0; s < RS; ++s) {
       mbar_init(bar_rfull + 8 * s, 1);
-      mbar_init(bar_rempty + 8 * s, 8);
+      mbar_init(bar_rempty + 8 * s, 4);
     }
     mbar_init(bar_accum, 1);
     fence_barrier_init();
@@ -258,23 +265,19 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
   }
   } else {
   // ---------------- quantised weights ----------------
-  const int gpb = qa.gs >= 64 ? 1 : 64 / qa.gs;  // groups per 64-input K block
   if (warp == 0 && lane == 0) {
-    // raw producer: codes + scales + biases, RS stages ahead (weights are
-    // written by no kernel, so the whole ring is requested before the PDL wait)
+    // raw producer: one contiguous record {codes, scales, biases} per K block,
+    // RS records ahead (weights are written by no kernel, so the ring is
+    // requested before the PDL wait)
     const uint64_t pol_w = l2_policy_evict_first();
-    const uint32_t raw_tx = (uint32_t)(S::kCodeBytes + 2 * gpb * 128 * 2);
+    const uint8_t* tile = qa.tiled + (size_t)blockIdx.x * qa.kb_total * qa.rec_bytes;
     int issued = 0;
     for (int i = 0; i < nkb; ++i) {
       const int s = i % RS, r = i / RS;
       if (r > 0 && !mbar_wait(bar_rempty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
       const uint32_t raw = sbase + S::kRawOffset + s * S::kRawBytes;
-      const int kb = kb_begin + i;
-      mbar_arrive_expect_tx(bar_rfull + 8 * s, raw_tx);
-      tma_load_2d(raw, &qa.codes, bar_rfull + 8 * s, kb * WQ * 8, n0, pol_w);
-      const int g0 = qa.gs >= 64 ? (kb * 64) / qa.gs : kb * gpb;
-      tma_load_2d(raw + S::kCodeBytes, &qa.scales, bar_rfull + 8 * s, n0, g0, pol_w);
-      tma_load_2d(raw + S::kCodeBytes + S::kGroupBytes, &qa.biases, bar_rfull + 8 * s, n0, g0, pol_w);
+      mbar_arrive_expect_tx(bar_rfull + 8 * s, (uint32_t)qa.rec_bytes);
+      bulk_g2s(raw, tile + (size_t)(kb_begin + i) * qa.rec_bytes, (uint32_t)qa.rec_bytes, bar_rfull + 8 * s, pol_w);
       issued = i + 1;
     }
     for (int i = max(0, issued - RS); i < issued; ++i)
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
       const int s = i % STAGES, r = i / STAGES;
       if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
       mbar_arrive_expect_tx(bar_full + 8 * s, S::kBBytes);
-      tma_load_2d(sbase + s * S::kStageBytes + S::kABytes, &tmX, bar_full + 8 * s, (kb_begin + i) * 64, m0, pol_x);
+      tma_load_2d(sbase + s * S::kStageBytes, &tmX, bar_full + 8 * s, (kb_begin + i) * 64, m0, pol_x);
       issued = i + 1;
     }
     for (int i = max(0, issued - STAGES); i < issued; ++i)
@@ -298,42 +301,45 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
-      const bool kt = args.ktrace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-      if (kt) args.ktrace[3 * nkb + i] = globaltimer();
-      if (!mbar_wait(bar_aready + 8 * s, r & 1, kErrGemmWait)) break;
-      if (kt) args.ktrace[2 * nkb + i] = globaltimer();
+      if (args.ktrace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) args.ktrace[2 * nkb + i] = globaltimer();
       if (trace && i == 0) trace[2] = globaltimer();
       tc_fence_after();
-      const uint32_t a = sbase + s * S::kStageBytes;
-      const uint64_t ad = umma_desc_k_sw128(a, 1024);
-      const uint64_t bd = umma_desc_k_sw128(a + S::kABytes, 1024);
+      const uint64_t bd = umma_desc_k_sw128(sbase + s * S::kStageBytes, 1024);
+      const uint32_t at = tmem + S::kAccCols + s * 32;  // A stage: 32 columns = 64 bf16 per lane
 #pragma unroll
-      for (int k = 0; k < 4; ++k) tc_mma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+      for (int k = 0; k < 4; ++k) tc_mma_f16_ts(tmem, at + 8 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
       tc_commit(bar_empty + 8 * s);
     }
     tc_commit(bar_accum);
   } else if (warp >= 4) {
-    // Eight dequantising warps: thread (t, half) converts inputs
-    // [32*half, 32*half + 32) of weight row t (one group per half).
+    // Eight dequantising warps in two groups of four; group g converts the
+    // K blocks i with i % 2 == g, so two blocks are in flight at once. Thread
+    // t of a group owns weight row t and stores its 64 inputs as 32
+    // tensor-memory columns of lane t.
     const int t = (threadIdx.x - 128) & 127;
-    const int half = (threadIdx.x - 128) >> 7;
-    const int g = qa.gs == 32 ? half : 0;
-    for (int i = 0; i < nkb; ++i) {
+    const int grp = (threadIdx.x - 128) >> 7;
+    const int g1 = qa.gs == 32 ? 1 : 0;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16) + S::kAccCols;
+    for (int i = grp; i < nkb; i += 2) {
       const int rs = i % RS, rr = i / RS;
       const int s = i % STAGES, r = i / STAGES;
       if (!mbar_wait(bar_rfull + 8 * rs, rr & 1, kErrGemmWait)) break;
       const bool kt = args.ktrace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 128;
       if (kt) args.ktrace[i] = globaltimer();
       if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
-      uint8_t* stage = smem + s * S::kStageBytes;
-      dequant_half_row<WQ>(smem + S::kRawOffset + rs * S::kRawBytes, stage, t, half, g);
+      const uint8_t* raw = smem + S::kRawOffset + rs * S::kRawBytes;
+      uint32_t v0[16], v1[16];
+      dequant_half_row_regs<WQ>(raw, t, 0, 0, qa.gpb, v0);
+      dequant_half_row_regs<WQ>(raw, t, 1, g1, qa.gpb, v1);
+      tmem_st16(lane_base + s * 32, v0);
+      tmem_st16(lane_base + s * 32 + 16, v1);
+      tc_wait_st();
+      tc_fence_before();
       if (kt) args.ktrace[nkb + i] = globaltimer();
-      // generic-proxy smem writes -> visible to the tensor core (async proxy)
-      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(bar_rempty + 8 * rs);
-        mbar_arrive(bar_aready + 8 * s);
+        mbar_arrive(bar_full + 8 * s);
       }
     }
   }
@@ -603,11 +609,13 @@ static int launch_bn_q(int BN, const CUtensorMap& tx, const GemmArgs& a, const Q
                        cudaStream_t st) {
   const CollArgs& c = local_coll_q();
   switch (BN) {
-    case 16: return launch_gemm<16, 4, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
-    case 32: return launch_gemm<32, 4, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
-    case 64: return launch_gemm<64, 4, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
-    case 128: return launch_gemm<128, 3, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
-    case 256: return launch_gemm<256, 2, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    // STAGES = tensor-memory A stages (32 columns each after the accumulator)
+    // and activation stages in shared memory
+    case 16: return launch_gemm<16, 14, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 32: return launch_gemm<32, 14, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 64: return launch_gemm<64, 12, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 128: return launch_gemm<128, 6, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
+    case 256: return launch_gemm<256, 3, kModeLocal, WQ>(tx, tx, a, c, tiles_n, tiles_m, st, q);
     default: return -1;
   }
 }
@@ -646,6 +654,23 @@ static int choose_splits(int N, int K, int num_sms, int ctas_per_sm = 2) {
   // the last split must own at least one K block
   while (s > 1 && (long)((kb + s - 1) / s) * (s - 1) >= kb) s /= 2;
   return s;
+}
+
+// Split count of the quantised GEMM (one CTA per SM): the largest S <= 8
+// (any S: cluster sizes up to 8 are portable) that keeps the grid within one
+// wave with at least 8 K blocks per split; a function of (N, K) only, so
+// results do not depend on M.
+static int choose_splits_q(int N, int K, int num_sms) {
+  const int kb = K / 64;
+  const int tiles = (N + 127) / 128;
+  int best = 1;
+  for (int s = 2; s <= 8; ++s) {
+    if ((long)tiles * s > num_sms) break;
+    if ((kb + s - 1) / s < 8) break;
+    if ((long)((kb + s - 1) / s) * (s - 1) >= kb) continue;  // the last split must own a K block
+    best = s;
+  }
+  return best;
 }
 
 }  // namespace b200
@@ -706,31 +731,28 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
 }
 
 // Y[M, :] = epi(X[M, K] . dequant(W)^T + bias) with affine-quantised W
-// (bits 4 or 8): codes [N, K*bits/8] bytes (4-bit words in the repacked
-// nibble order of QArgs), scales_t / biases_t [K/gs, N] bf16, gs in {32, 64, 128}.
-// The weight tile is dequantised in shared memory by four extra warps and fed
-// to the same tcgen05 pipeline and epilogues as b200_gemm_bf16 (one CTA per
-// SM, so the split count budgets one CTA slot per SM).
-int b200_gemm_q(const void* X, int M, int K, int ldx, const void* codes, const void* scales_t, const void* biases_t,
-                int N, int bits, int gs, void* Y, int ldy, const void* R, int ldr, const void* bias, int epi,
-                int num_sms, int force_splits, cudaStream_t stream) {
+// (bits 4 or 8, group size 32 / 64 / 128) in the tile-major device layout:
+// record (tile, K block) = {codes [128][bits*8 B] (4-bit words in the
+// repacked nibble order), scales [gpb][128] bf16, biases [gpb][128] bf16},
+// records contiguous per 128-row tile; gpb = 2 for group size 32, else 1 (a
+// 128-input group repeats its scale and bias in both of its K blocks).
+// Same epilogues and cluster split-K as b200_gemm_bf16; one CTA per SM.
+int b200_gemm_q(const void* X, int M, int K, int ldx, const void* tiled, int N, int bits, int gs, void* Y, int ldy,
+                const void* R, int ldr, const void* bias, int epi, int num_sms, int force_splits, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
   if ((bits != 4 && bits != 8) || (gs != 32 && gs != 64 && gs != 128)) return -1;
-  if ((K % 128) || (ldx % 8) || ((uintptr_t)X & 15) || ((uintptr_t)codes & 15)) return -1;
-  if (((uintptr_t)scales_t & 15) || ((uintptr_t)biases_t & 15) || (N % 8)) return -1;
+  if ((K % 128) || (ldx % 8) || ((uintptr_t)X & 15) || ((uintptr_t)tiled & 15) || (N % 8)) return -1;
   const bool glu = epi == kEpiSwiGLU || epi == kEpiGeGLU || epi == kEpiSwiGLUOAI;
   if (glu && (N % 128)) return -1;
   const int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  const int G = K / gs;
-  const int gpb = gs >= 64 ? 1 : 64 / gs;
   QArgs q;
+  q.tiled = reinterpret_cast<const uint8_t*>(tiled);
   q.gs = gs;
+  q.gpb = gs == 32 ? 2 : 1;
+  q.rec_bytes = bits * 128 * 8 + q.gpb * 512;
+  q.kb_total = K / 64;
   CUtensorMap tx;
   if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
-  const int64_t cb = (int64_t)K * bits / 8;
-  if (!make_tmap_2d_sw(&q.codes, codes, N, cb, cb, 128, bits * 8, 1, false)) return -1;
-  if (!make_tmap_2d_sw(&q.scales, scales_t, G, N, N, gpb, 128, 2, false)) return -1;
-  if (!make_tmap_2d_sw(&q.biases, biases_t, G, N, N, gpb, 128, 2, false)) return -1;
   GemmArgs a = {};
   a.Y = Y;
   a.R = reinterpret_cast<const __nv_bfloat16*>(R);
@@ -744,7 +766,7 @@ int b200_gemm_q(const void* X, int M, int K, int ldx, const void* codes, const v
   a.trace = g_gemm_trace;
   a.ktrace = g_gemm_ktrace;
   a.kb_total = K / 64;
-  const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms, 1);
+  const int s = force_splits > 0 ? force_splits : choose_splits_q(N, K, num_sms);
   if (s > 8) return -1;
   a.kb_per_split = (a.kb_total + s - 1) / s;
   a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
@@ -753,7 +775,7 @@ int b200_gemm_q(const void* X, int M, int K, int ldx, const void* codes, const v
                    : launch_bn_q<8>(BN, tx, a, q, tiles_n, tiles_m, stream);
 }
 
-int b200_gemm_q_num_splits(int N, int K, int num_sms) { return choose_splits(N, K, num_sms, 1); }
+int b200_gemm_q_num_splits(int N, int K, int num_sms) { return choose_splits_q(N, K, num_sms); }
 
 // ---------------------------------------------------------------------------
 // Fused collective GEMMs (tensor parallelism). `comm_ctx` is a CommCtx blob

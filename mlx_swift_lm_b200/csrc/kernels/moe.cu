@@ -249,8 +249,8 @@ __device__ __forceinline__ float glu(int epi, float g, float u) {
 // Quantised expert weights (WQ = 4 or 8): codes [E*N, K*WQ/8] bytes,
 // scales / biases [K/gs, E*N] bf16 (layout of b200_dequant.cuh).
 struct GQuant {
-  CUtensorMap codes, scales, biases;
-  int gs;
+  const uint8_t* tiled;  // records [E][tiles_per_expert][K/64][rec_bytes] (tile-major, per expert)
+  int gs, gpb, rec_bytes, kb_total, tiles_per_expert;
 };
 
 // Operand stages {A bf16 weight tile, B activation tile}; with quantised
@@ -318,7 +318,6 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int gpb = WQ ? (q.gs >= 64 ? 1 : 64 / q.gs) : 0;
   const int wrow = e * a.N + n0;
   const uint64_t pw = l2_policy_evict_first(), px = l2_policy_evict_last();
   if (warp == 0 && lane == 0) {
@@ -340,17 +339,14 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
   } else if (warp == 2 && lane == 0) {
     if constexpr (WQ != 0) {
       // raw producer: codes + scales + biases, RS stages ahead
-      const uint32_t raw_tx = (uint32_t)(S::kCode + 2 * gpb * 256);
+      const uint8_t* tile = q.tiled + ((size_t)e * q.tiles_per_expert + blockIdx.x) * q.kb_total * q.rec_bytes;
       int issued = 0;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % RS, r = i / RS;
         if (r > 0 && !mbar_wait(bar_rempty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
         const uint32_t raw = sbase + S::kRawOff + s * S::kRaw;
-        mbar_arrive_expect_tx(bar_rfull + 8 * s, raw_tx);
-        tma_load_2d(raw, &q.codes, bar_rfull + 8 * s, i * WQ * 8, wrow, pw);
-        const int g0 = q.gs >= 64 ? (i * 64) / q.gs : i * gpb;
-        tma_load_2d(raw + S::kCode, &q.scales, bar_rfull + 8 * s, wrow, g0, pw);
-        tma_load_2d(raw + S::kCode + S::kGroup, &q.biases, bar_rfull + 8 * s, wrow, g0, pw);
+        mbar_arrive_expect_tx(bar_rfull + 8 * s, (uint32_t)q.rec_bytes);
+        bulk_g2s(raw, tile + (size_t)i * q.rec_bytes, (uint32_t)q.rec_bytes, bar_rfull + 8 * s, pw);
         issued = i + 1;
       }
       for (int i = max(0, issued - RS); i < issued; ++i)
@@ -381,7 +377,7 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
         const int s = i % STAGES, r = i / STAGES;
         if (!mbar_wait(bar_rfull + 8 * rs, rr & 1, kErrGemmWait)) break;
         if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
-        dequant_half_row<WQ>(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, g);
+        dequant_half_row<WQ>(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, g, q.gpb);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -535,24 +531,24 @@ int b200_moe_grouped_gemm(const void* xs, int P, int K, const void* W, int E, in
   return moe::dispatch_grouped<0>(BN, tw, tx, a, q, max_chunks, st);
 }
 
-// Same with affine-quantised experts: codes [E*N, K*bits/8], scales_t / biases_t [K/gs, E*N] bf16.
-int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* codes, const void* scales_t,
-                            const void* biases_t, int bits, int gs, int E, int N, void* Y, int ldy, const void* bias,
-                            int epi, const int* chunks, const int* n_chunks, int max_chunks, int BN, cudaStream_t st) {
+// Same with affine-quantised experts in the tile-major device layout: per
+// expert ceil(N/128) tiles of K/64 records {codes [128][bits*8 B], scales,
+// biases [gpb][128] bf16} (rows past N are zero).
+int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* tiled, int bits, int gs, int E, int N, void* Y,
+                            int ldy, const void* bias, int epi, const int* chunks, const int* n_chunks, int max_chunks,
+                            int BN, cudaStream_t st) {
   if (P <= 0) return 0;
   if ((K % 128) || (N % 8) || (bits != 4 && bits != 8) || (gs != 32 && gs != 64 && gs != 128)) return -1;
-  if (((uintptr_t)codes & 15) || ((uintptr_t)scales_t & 15) || ((uintptr_t)biases_t & 15)) return -1;
-  const int64_t rows = (int64_t)E * N;
-  const int64_t cb = (int64_t)K * bits / 8;
-  const int G = K / gs, gpb = gs >= 64 ? 1 : 64 / gs;
-  if ((rows * 2) % 16) return -1;
+  if ((uintptr_t)tiled & 15) return -1;
   CUtensorMap tx;
   moe::GQuant q;
+  q.tiled = reinterpret_cast<const uint8_t*>(tiled);
   q.gs = gs;
+  q.gpb = gs == 32 ? 2 : 1;
+  q.rec_bytes = bits * 128 * 8 + q.gpb * 512;
+  q.kb_total = K / 64;
+  q.tiles_per_expert = (N + 127) / 128;
   if (!make_tmap_2d(&tx, xs, P, K, K, BN, 64, 2)) return -1;
-  if (!make_tmap_2d_sw(&q.codes, codes, rows, cb, cb, 128, bits * 8, 1, false)) return -1;
-  if (!make_tmap_2d_sw(&q.scales, scales_t, G, rows, rows, gpb, 128, 2, false)) return -1;
-  if (!make_tmap_2d_sw(&q.biases, biases_t, G, rows, rows, gpb, 128, 2, false)) return -1;
   moe::GArgs a{reinterpret_cast<__nv_bfloat16*>(Y), reinterpret_cast<const __nv_bfloat16*>(bias), chunks, n_chunks,
                N, K, ldy, epi};
   return bits == 4 ? moe::dispatch_grouped<4>(BN, tx, tx, a, q, max_chunks, st)

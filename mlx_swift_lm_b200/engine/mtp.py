@@ -68,6 +68,8 @@ class MTPDriver:
         self.kv = module.new_kv(max_tokens=(engine.kv.num_pages - 1) * 16, kv_fp8=engine.cfg.kv_fp8)
         self.rng = np.random.default_rng(self.cfg.seed)
         self.stats = MTPStats()
+        self.h2d_bytes = 0  # step inputs copied host -> device
+        self.d2h_bytes = 0  # drafts + target tokens read back
 
     # ------------------------------------------------------------------ row state
     def on_first_token(self, st, hidden_row: torch.Tensor):
@@ -115,6 +117,7 @@ class MTPDriver:
                          "pf_page_table", "logit_idx"):
                 t = getattr(fb, name)
                 if t is not None and not t.is_cuda:
+                    self.h2d_bytes += t.numel() * t.element_size()
                     setattr(fb, name, t.pin_memory().to(dev, non_blocking=True))
         return fb
 
@@ -197,6 +200,7 @@ class MTPDriver:
         vlog, vh = eng.model.forward(fbv, eng.kv, return_both=True)
         pred = ops.argmax(vlog).view(B, k + 1)
         both = torch.cat([pred, D], 1).cpu().numpy()
+        self.d2h_bytes += both.nbytes
         pred_h, D_h = both[:, :k + 1], both[:, k + 1:]
         vh = vh.view(B, k + 1, -1)
         events = []

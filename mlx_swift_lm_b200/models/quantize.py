@@ -15,7 +15,7 @@ from ..ops.qlinear import QuantizedWeight
 
 
 def _q(t: torch.Tensor, bits: int, gs: int, device) -> QuantizedWeight:
-    return QuantizedWeight.quantize(t.float().cpu(), bits, gs).to(device)
+    return QuantizedWeight.quantize_device(t, bits, gs).to(device)
 
 
 def quantize_model(model, bits: int = 4, group_size: int = 64, dense: bool = True, experts: bool = True,
@@ -28,11 +28,13 @@ def quantize_model(model, bits: int = 4, group_size: int = 64, dense: bool = Tru
                 if isinstance(t, torch.Tensor) and t.shape[1] % group_size == 0 and t.shape[0] % 8 == 0:
                     setattr(L, name, _q(t, bits, group_size, dev))
         if experts and L.moe and isinstance(L.experts_gu, torch.Tensor):
+            # all experts at once: groups run along K, so quantising the
+            # stacked [E*N, K] matrix equals quantising each expert
             E = L.experts_gu.shape[0]
-            L.experts_gu = QuantizedWeight.stack_experts([_q(L.experts_gu[e], bits, group_size, "cpu")
-                                                          for e in range(E)]).to(dev)
-            L.experts_d = QuantizedWeight.stack_experts([_q(L.experts_d[e], bits, group_size, "cpu")
-                                                         for e in range(E)]).to(dev)
+            L.experts_gu = _q(L.experts_gu.reshape(-1, L.experts_gu.shape[-1]), bits, group_size, dev)
+            L.experts_gu.num_experts = E
+            L.experts_d = _q(L.experts_d.reshape(-1, L.experts_d.shape[-1]), bits, group_size, dev)
+            L.experts_d.num_experts = E
     if lm_head and isinstance(model.lm_head, torch.Tensor) and model.lm_head is not model.embed:
         model.lm_head = _q(model.lm_head, bits, group_size, dev)
     return model

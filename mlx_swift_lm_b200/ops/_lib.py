@@ -30,7 +30,7 @@ sz = C.c_size_t
 _SIGS = {
     "b200_gemm_bf16": (i32, [vp, i32, i32, i32, vp, i32, i32, vp, i32, vp, i32, vp, i32, i32, i32, vp]),
     "b200_gemm_num_splits": (i32, [i32, i32, i32, i32]),
-    "b200_gemm_q": (i32, [vp, i32, i32, i32, vp, vp, vp, i32, i32, i32, vp, i32, vp, i32, vp, i32, i32, i32, vp]),
+    "b200_gemm_q": (i32, [vp, i32, i32, i32, vp, i32, i32, i32, vp, i32, vp, i32, vp, i32, i32, i32, vp]),
     "b200_gemm_q_num_splits": (i32, [i32, i32, i32]),
     "b200_gemm_set_ktrace": (None, [vp]),
     "b200_add_rmsnorm": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp]),

@@ -38,9 +38,9 @@ _lib.register_signatures({
     "b200_moe_grouped_gemm": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.vp,
                                          _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.i32, _lib.i32,
                                          _lib.vp]),
-    "b200_moe_grouped_gemm_q": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.vp, _lib.i32,
-                                           _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.i32,
-                                           _lib.vp, _lib.vp, _lib.i32, _lib.i32, _lib.vp]),
+    "b200_moe_grouped_gemm_q": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.i32,
+                                           _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.vp,
+                                           _lib.i32, _lib.i32, _lib.vp]),
 }, status_tags=("moe",))
 
 
@@ -83,9 +83,9 @@ def chunk_rows(P: int, E: int) -> int:
 
 def _grouped(L, xs, P, K, W, E, N, Y, ldy, bias, epi, chunks, n_chunks, max_chunks, BN, st, what):
     if isinstance(W, QuantizedWeight):
-        rc = L.b200_moe_grouped_gemm_q(xs.data_ptr(), P, K, W.codes.data_ptr(), W.scales_t.data_ptr(),
-                                       W.biases_t.data_ptr(), W.bits, W.gs, E, N, Y.data_ptr(), ldy, _lib.ptr(bias),
-                                       epi, chunks.data_ptr(), n_chunks.data_ptr(), max_chunks, BN, st)
+        rc = L.b200_moe_grouped_gemm_q(xs.data_ptr(), P, K, W.tiled().data_ptr(), W.bits, W.gs, E, N, Y.data_ptr(),
+                                       ldy, _lib.ptr(bias), epi, chunks.data_ptr(), n_chunks.data_ptr(), max_chunks,
+                                       BN, st)
     else:
         rc = L.b200_moe_grouped_gemm(xs.data_ptr(), P, K, W.data_ptr(), E, N, Y.data_ptr(), ldy, _lib.ptr(bias), epi,
                                      chunks.data_ptr(), n_chunks.data_ptr(), max_chunks, BN, st)

@@ -84,6 +84,23 @@ class QuantizedWeight:
         # round scale / bias to bf16 first: the kernel applies them in bf16
         return cls.from_mlx(packed, s.to(torch.bfloat16), b.to(torch.bfloat16), bits, gs)
 
+    @classmethod
+    def quantize_device(cls, w: torch.Tensor, bits: int = 4, gs: int = 64):
+        """:meth:`quantize` computed where `w` lives (vectorised; for large
+        random-init models on the GPU). Same rule: scale = (max - min) /
+        levels, bias = min, q = round((w - bias) / scale); scale and bias are
+        then stored in bf16."""
+        N, K = w.shape
+        g = w.float().reshape(N, K // gs, gs)
+        mx = g.amax(-1, keepdim=True)
+        mn = g.amin(-1, keepdim=True)
+        levels = (1 << bits) - 1
+        scale = ((mx - mn) / levels).clamp(min=1e-8)
+        q = torch.round((g - mn) / scale).clamp(0, levels).to(torch.int32).reshape(N, K)
+        codes = _repack4(q) if bits == 4 else q.to(torch.uint8)
+        return cls(codes.contiguous(), scale[..., 0].t().to(torch.bfloat16).contiguous(),
+                   mn[..., 0].t().to(torch.bfloat16).contiguous(), bits, gs)
+
     # ---------------------------------------------------------------- views
     @property
     def device(self):
@@ -127,6 +144,53 @@ class QuantizedWeight:
     def expert(self, e: int) -> "QuantizedWeight":
         n = self.shape[0] // self.num_experts
         return self.rows(e * n, (e + 1) * n)
+
+    # ---------------------------------------------------------------- device layout
+    def record_bytes(self) -> int:
+        gpb = 2 if self.gs == 32 else 1
+        return self.bits * 128 * 8 + gpb * 512
+
+    def tiled(self) -> torch.Tensor:
+        """Tile-major device layout streamed by the dequantising kernels
+        (built once, cached): for each 128-row tile (per expert when experts
+        are stacked; rows past the end are zero) and each 64-input K block one
+        contiguous record {codes [128][bits*8 B], scales [gpb][128] bf16,
+        biases [gpb][128] bf16}; gpb = 2 for group size 32, else 1 (a
+        128-input group repeats its scale and bias in both of its blocks)."""
+        t = getattr(self, "_tiled", None)
+        if t is not None:
+            return t
+        E = self.num_experts or 1
+        N, K = self.shape
+        Ne = N // E
+        tiles = (Ne + 127) // 128
+        KB = K // 64
+        cb = self.bits * 8  # code bytes per row per K block
+        dev = self.codes.device
+        codes = self.codes.view(E, Ne, KB, cb)
+        sc = self.scales_t.t().reshape(E, Ne, -1)  # [E, Ne, G]
+        bi = self.biases_t.t().reshape(E, Ne, -1)
+        pad = tiles * 128 - Ne
+        if pad:
+            codes = torch.cat([codes, torch.zeros(E, pad, KB, cb, dtype=codes.dtype, device=dev)], 1)
+            sc = torch.cat([sc, torch.zeros(E, pad, sc.shape[2], dtype=sc.dtype, device=dev)], 1)
+            bi = torch.cat([bi, torch.zeros(E, pad, bi.shape[2], dtype=bi.dtype, device=dev)], 1)
+        if self.gs == 32:  # groups of each K block: [E, rows, KB, gpb]
+            sc_kb, bi_kb = sc.reshape(E, -1, KB, 2), bi.reshape(E, -1, KB, 2)
+        elif self.gs == 64:
+            sc_kb, bi_kb = sc.reshape(E, -1, KB, 1), bi.reshape(E, -1, KB, 1)
+        else:  # 128: one group per two K blocks
+            sc_kb = sc.repeat_interleave(2, dim=2).reshape(E, -1, KB, 1)
+            bi_kb = bi.repeat_interleave(2, dim=2).reshape(E, -1, KB, 1)
+        c = codes.reshape(E, tiles, 128, KB, cb).permute(0, 1, 3, 2, 4).reshape(E, tiles, KB, 128 * cb)
+        s_ = sc_kb.reshape(E, tiles, 128, KB, -1).permute(0, 1, 3, 4, 2).contiguous()  # [E, t, KB, gpb, 128]
+        b_ = bi_kb.reshape(E, tiles, 128, KB, -1).permute(0, 1, 3, 4, 2).contiguous()
+        s_b = s_.view(torch.uint8).reshape(E, tiles, KB, -1)
+        b_b = b_.view(torch.uint8).reshape(E, tiles, KB, -1)
+        rec = torch.cat([c, s_b, b_b], dim=-1).contiguous()
+        assert rec.shape[-1] == self.record_bytes()
+        self._tiled = rec.reshape(-1)
+        return self._tiled
 
     def numel(self) -> int:
         return self.shape[0] * self.shape[1]
