@@ -5,7 +5,8 @@
 // reference's prefill path (gather pages then MLX SDPA,
 // ContinuousBatchingV2/Paged/PagedLayerCache.swift:584-637) with sliding
 // windows from absolute positions and learned sinks. It is the fallback for
-// shapes the tcgen05 FMHA (attention_prefill_tc.cu) does not take.
+// shapes the tensor-core kernel (attention_prefill_mma.cu) does not take
+// (fp8 KV pages).
 //
 // Work unit: a tile of QT query tokens of one row x one KV head; each thread
 // owns one (query, head-of-group) pair with an exact online softmax. KV pages

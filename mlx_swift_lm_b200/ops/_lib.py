@@ -41,6 +41,8 @@ _SIGS = {
     "b200_paged_decode": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32,
                                 i32, f32, f32, i64, vp]),
     "b200_paged_decode_part_tokens": (i32, []),
+    "b200_paged_prefill_mma": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32, f32,
+                                     i64, vp]),
     "b200_paged_prefill_simt": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32, f32,
                                       i64, vp]),
     "b200_prefill_simt_q_tile": (i32, [i32]),
@@ -59,7 +61,8 @@ _SIGS = {
 }
 
 # status accessors exported per translation unit
-_STATUS_TAGS = ["gemm", "norm", "attn_decode", "attn_prefill_simt", "sampling", "misc", "attn_decode_mma"]
+_STATUS_TAGS = ["gemm", "norm", "attn_decode", "attn_prefill_simt", "sampling", "misc", "attn_decode_mma",
+                "attn_prefill_mma"]
 
 
 class KernelLibraryMissing(RuntimeError):

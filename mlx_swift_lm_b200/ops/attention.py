@@ -79,6 +79,21 @@ def paged_decode(q, k_cache, v_cache, page_table, seq_lens, scale, window=0, sin
     return out
 
 
+USE_MMA_PREFILL = [True]  # tests flip it to cover the CUDA-core kernel
+
+
+def prefill_tiles_mma(cu_q: list[int], qt: int = 64) -> list[tuple[int, int]]:
+    """(row, query offset) work items of the tensor-core prefill kernel, the
+    tiles that see the most keys (last offsets of long rows) first."""
+    tiles = []
+    for r in range(len(cu_q) - 1):
+        n = cu_q[r + 1] - cu_q[r]
+        for off in range(0, n, qt):
+            tiles.append((r, off))
+    tiles.sort(key=lambda t: -t[1])
+    return tiles
+
+
 def prefill_tiles(cu_q: list[int], G: int) -> list[tuple[int, int]]:
     qt = 128 // G
     tiles = []
@@ -106,6 +121,17 @@ def paged_prefill(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0
         out = torch.empty_like(q)
     if cu_q_host is None:
         cu_q_host = cu_q.tolist()
+    if USE_MMA_PREFILL[0] and k_scale is None and k_cache.dtype == torch.bfloat16 and D in (64, 128, 256):
+        # tensor-core kernel: 64-query tiles of one head, longest rows first
+        tiles = prefill_tiles_mma(cu_q_host)
+        tiles_t = torch.tensor(tiles, dtype=torch.int32).pin_memory().to(q.device, non_blocking=True)
+        rc = _lib.lib().b200_paged_prefill_mma(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), page_table.data_ptr(), page_table.stride(0),
+            cu_q.data_ptr(), q_pos0.data_ptr(), tiles_t.data_ptr(), len(tiles), _lib.ptr(sinks), out.data_ptr(), H,
+            KVH, D, int(window), float(scale), float(softcap), k_cache.shape[0], _lib.stream_ptr(q.device))
+        _lib.check(rc, "paged_prefill_mma")
+        _lib.count(1)
+        return out
     tiles = prefill_tiles(cu_q_host, G)
     tiles_t = torch.tensor(tiles, dtype=torch.int32).pin_memory().to(q.device, non_blocking=True)
     rc = _lib.lib().b200_paged_prefill_simt(
