@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--quant-experts", type=int, default=0, help="MLX affine bits for MoE experts (0 = bf16)")
     ap.add_argument("--quant-dense", type=int, default=0, help="MLX affine bits for dense projections (0 = bf16)")
     ap.add_argument("--mtp", type=int, default=0, help="MTP draft depth k (0 = off); acceptance: seeded Bernoulli(0.7)")
+    ap.add_argument("--pp", type=int, default=1, help="pipeline stages (world = pp x tp); stages exchange hidden "
+                                                     "states with NCCL p2p")
+    ap.add_argument("--kv-fp8", action="store_true", help="fp8-e4m3 paged KV with per-head scales")
     return ap.parse_args()
 
 
@@ -143,7 +146,7 @@ def _mtp_measure(args, eng, mtp, streams, dev, world, rank, ttfts, prefill_s, cf
     dev_ms = e0.elapsed_time(e1)
     dev_tokens = sum(s.st.num_output for s in streams) - tok0
     tok1 = sum(s.st.num_output for s in streams)
-    h2d0, d2h0 = mtp.h2d_bytes, mtp.d2h_bytes
+    h2d0, d2h0 = (mtp.h2d_bytes, mtp.d2h_bytes) if mtp is not None else (eng.h2d_bytes, eng.d2h_bytes)
     t0 = time.perf_counter()
     step_times = []
     for _ in range(args.steps):
@@ -153,14 +156,18 @@ def _mtp_measure(args, eng, mtp, streams, dev, world, rank, ttfts, prefill_s, cf
     barrier()
     e2e_s = time.perf_counter() - t0
     e2e_tokens = sum(s.st.num_output for s in streams) - tok1
-    h2d = (mtp.h2d_bytes - h2d0) / args.steps
-    d2h = (mtp.d2h_bytes - d2h0) / args.steps
+    if mtp is not None:
+        h2d = (mtp.h2d_bytes - h2d0) / args.steps
+        d2h = (mtp.d2h_bytes - d2h0) / args.steps
+    else:  # eager engine steps: batch inputs host->device, sampled tokens back
+        h2d = (eng.h2d_bytes - h2d0) / args.steps
+        d2h = (eng.d2h_bytes - d2h0) / args.steps
     clk = clocks.stop()
     t = torch.tensor([dev_ms, e2e_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dev_ms, e2e_s = t.tolist()
-    st = mtp.stats
+    st = mtp.stats if mtp is not None else None
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(dev_tokens / (dev_ms / 1e3), 2), "unit": "tok/s", "n_gpus": world,
@@ -171,15 +178,16 @@ def _mtp_measure(args, eng, mtp, streams, dev, world, rank, ttfts, prefill_s, cf
             "config": {"model": f"{args.model}-shape" + (f" ({cfg.num_layers} layers, DEBUG)" if args.layers else ""),
                        "global_batch": args.streams,
                        "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}] + {args.out_tokens} out",
-                       "parallelism": f"tp{world}",
+                       "parallelism": f"pp{args.pp}xtp{world // args.pp}" if args.pp > 1 else f"tp{world}",
                        "experts": f"q{args.quant_experts} g64" if args.quant_experts else "bf16", "mtp_k": args.mtp,
                        "kv": "paged bf16, page 16", "l2": "inputs larger than L2 (weights + KV per step)"},
-            "mtp": {"rounds": st.rounds, "acceptance": round(st.acceptance_rate, 3),
-                    "tokens_per_row_round": round(st.emitted / max(st.rows, 1), 3)},
+            "mtp": ({"rounds": st.rounds, "acceptance": round(st.acceptance_rate, 3),
+                     "tokens_per_row_round": round(st.emitted / max(st.rows, 1), 3)} if st else None),
             "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
             "itl_p50_ms": round(statistics.median(step_times) * 1e3, 3), "prefill_s": round(prefill_s, 3),
             "e2e": {"value": round(e2e_tokens / e2e_s, 2), "unit": "tok/s", "api": "EngineV2.step (MTP rounds)",
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+                    "h2d_bytes_per_step": int(h2d) if h2d is not None else None,
+                    "d2h_bytes_per_step": int(d2h) if d2h is not None else None},
             "gpu_launches": int(launches), "clocks": clk, "kernel_status": _lib.read_status(),
         }
         print(json.dumps(out))
@@ -218,8 +226,23 @@ def main():
     cfg = getattr(mcfg, args.model)()
     if args.layers:
         cfg.num_layers = args.layers
-    tp = TensorParallel(rank, world, group)
-    model = DecoderLM(cfg, dev, torch.bfloat16, tp=tp).init_random(args.seed)
+    pp_size = args.pp
+    tp_size = world // pp_size
+    tp_group = group
+    ppc = None
+    if pp_size > 1:
+        from mlx_swift_lm_b200.parallel.pipeline import PipelineParallel, PipelinedDecoderLM
+
+        stage, tp_rank = rank // tp_size, rank % tp_size
+        tp_groups = [dist.new_group(list(range(s * tp_size, (s + 1) * tp_size))) for s in range(pp_size)]
+        pp_groups = [dist.new_group([s * tp_size + t for s in range(pp_size)]) for t in range(tp_size)]
+        tp_group = tp_groups[stage]
+        ppc = PipelineParallel(stage, pp_size, [s * tp_size + tp_rank for s in range(pp_size)], pp_groups[tp_rank])
+        tp = TensorParallel(tp_rank, tp_size, tp_group)
+        model = PipelinedDecoderLM(cfg, ppc, dev, torch.bfloat16, tp=tp).init_random(args.seed)
+    else:
+        tp = TensorParallel(rank, world, group)
+        model = DecoderLM(cfg, dev, torch.bfloat16, tp=tp).init_random(args.seed)
     if args.quant_experts or args.quant_dense:
         from mlx_swift_lm_b200.models.quantize import quantize_model
 
@@ -228,12 +251,13 @@ def main():
         if args.quant_dense:
             quantize_model(model, bits=args.quant_dense, group_size=64, dense=True, experts=False)
         torch.cuda.empty_cache()
-    if world > 1 and args.tp_mode == "fused":
+    if tp_size > 1 and args.tp_mode == "fused" and pp_size == 1:
         model.enable_fused_tp(args.streams)
     max_len = args.max_prompt + args.out_tokens + 16
     ecfg = EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=args.streams,
                                                   max_batched_tokens_per_step=16384, prefill_chunk_size=4096),
-                        max_model_len=max_len, use_cuda_graphs=True, chained_decode=True,
+                        max_model_len=max_len, use_cuda_graphs=pp_size == 1, chained_decode=True,
+                        kv_fp8=args.kv_fp8,
                         graph_buckets=(args.streams,))
     eng = EngineV2(model, config=ecfg)
     mtp = None
@@ -269,7 +293,7 @@ def main():
     prefill_s = time.perf_counter() - t_pf
     ttfts = [s.st.timing.ttft for s in streams]
 
-    if mtp is not None:
+    if mtp is not None or pp_size > 1:
         return _mtp_measure(args, eng, mtp, streams, dev, world, rank, ttfts, prefill_s, cfg, barrier, ClockSampler,
                             local, _lib)
     # ---- kernel-only value: replays of the captured decode-step graph ----

@@ -156,12 +156,15 @@ class EngineV2:
         self._clock = self.cfg.clock or time.monotonic
         self.max_pages = PagedKVCache.pages_for(self.cfg.max_model_len)
         self.graphs = graph_runner
-        if self.graphs is None and self.device.type == "cuda" and self.cfg.use_cuda_graphs:
+        if (self.graphs is None and self.device.type == "cuda" and self.cfg.use_cuda_graphs
+                and getattr(model, "pp_stages", 1) == 1):
             from .graphs import DecodeGraphRunner  # noqa: F811
 
             self.graphs = DecodeGraphRunner(self)
         self._inflight = None  # chained decode: (plan rows, device tokens, event)
         self.mtp = None  # MTPDriver when speculative decoding is enabled
+        self.h2d_bytes = 0  # eager-path step inputs copied host -> device
+        self.d2h_bytes = 0  # eager-path sampled tokens read back
         self.forward_shapes: list[tuple[int, int]] = []
         self.record_shapes = False
 
@@ -250,11 +253,13 @@ class EngineV2:
             fb.pf_page_table = torch.from_numpy(pt)
         if len(logit_idx) != T:
             fb.logit_idx = torch.tensor(logit_idx, dtype=torch.int64)
+            fb.logit_idx_host = logit_idx
         if dev.type == "cuda":
             for name in ("input_ids", "positions", "slots", "dec_page_table", "dec_seq_lens", "pf_cu_q", "pf_pos0",
                          "pf_page_table", "logit_idx"):
                 t = getattr(fb, name)
                 if t is not None:
+                    self.h2d_bytes += t.numel() * t.element_size()
                     setattr(fb, name, t.pin_memory().to(dev, non_blocking=True))
         return fb
 
@@ -324,8 +329,12 @@ class EngineV2:
                 else:
                     logits = self.model.forward(fb, self.kv)
                 srows = [r for r in plan.rows if r.sample]
-                toks, lp = self.sampler.sample(logits, [r.state for r in srows])
+                if getattr(self.model, "pp_stages", 1) > 1:
+                    toks, lp = self._pp_tokens(logits, srows)
+                else:
+                    toks, lp = self.sampler.sample(logits, [r.state for r in srows])
                 toks_host = toks.cpu().tolist() if toks.numel() else []
+                self.d2h_bytes += toks.numel() * toks.element_size()
                 for r in plan.rows:
                     self.sched.commit(r)
                     r.state.timing.prefill_chunks += 0 if r.is_decode else 1
@@ -338,6 +347,22 @@ class EngineV2:
             self.last_step_ms = (time.perf_counter() - t0) * 1e3
             self._step_started = None
             return events
+
+    def _pp_tokens(self, logits, srows):
+        """Pipeline parallelism: the last stage samples, every stage receives
+        the tokens (so all schedulers advance identically)."""
+        import torch.distributed as dist
+
+        pp = self.model.pp
+        lp = None
+        if pp.is_last:
+            toks, lp = self.sampler.sample(logits, [r.state for r in srows])
+            toks = toks.to(torch.int32).contiguous()
+        else:
+            toks = torch.empty(len(srows), dtype=torch.int32, device=self.device)
+        if len(srows):
+            dist.broadcast(toks, src=pp.last, group=pp.group)
+        return toks, lp
 
     def _row_needs_eager(self, st) -> bool:
         sp = st.req.sampling

@@ -30,6 +30,7 @@ class ForwardBatch:
     pf_page_table: torch.Tensor | None = None  # [R, maxp] int32
     # rows whose logits are needed (indices into the T tokens); None = all tokens
     logit_idx: torch.Tensor | None = None
+    logit_idx_host: list | None = None  # the same indices on the host (microbatch splitting)
     # per-token LoRA adapter slot (-1 = none), used when adapters are active
     lora_slots: torch.Tensor | None = None
 

@@ -135,11 +135,15 @@ class DecoderLM:
     def num_params(self) -> int:
         return sum(t.numel() for _, t in self.named_tensors() if t is not None)
 
-    def init_random(self, seed: int = 0, std: float = 0.02, with_embeddings: bool = True):
+    def init_random(self, seed: int = 0, std: float = 0.02, with_embeddings: bool = True,
+                    keep_layers: tuple[int, int] | None = None):
         """Random N(0, std) weights (norm weights 1, sinks N(0,1)), generated on
         the model's device. Every rank draws the full tensors from the same
         seed and keeps its tensor-parallel shard, so a TP=N model computes the
-        same function as the TP=1 model of that seed."""
+        same function as the TP=1 model of that seed. With `keep_layers`
+        (lo, hi) every layer is still drawn (the generator advances exactly
+        as for the full model) but only layers lo..hi-1 are kept: a pipeline
+        stage of the same function."""
         cfg = self.cfg
         g = torch.Generator(device=self.device)
         g.manual_seed(seed)
@@ -239,7 +243,8 @@ class DecoderLM:
                     L.bgu = ref.interleave_gate_up(rows(gb, self.F)[:, None], rows(ub, self.F)[:, None])[:, 0]
                     bd = rn(hd)
                     L.bd = bd if r == 0 else torch.zeros_like(bd)
-            self.layers.append(L)
+            if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
+                self.layers.append(L)
         return self
 
     # ------------------------------------------------------------------ pieces
@@ -287,11 +292,14 @@ class DecoderLM:
 
     # ------------------------------------------------------------------ paged forward
     def forward(self, fb: ForwardBatch, kv, return_hidden: bool = False, inputs_embeds: torch.Tensor | None = None,
-                return_both: bool = False):
+                return_both: bool = False, return_residual: bool = False):
         """Paged-KV forward over a flattened batch. Returns fp32 logits for
         ``fb.logit_idx`` rows (all tokens when None); with `return_hidden` the
         final-normed hidden rows instead, with `return_both` (logits, hidden).
-        `inputs_embeds` [T, H] replaces the token embedding (MTP modules)."""
+        `inputs_embeds` [T, H] replaces the token embedding (MTP modules,
+        pipeline stages after the first); `return_residual` returns the
+        residual stream of every token after the last layer instead (pipeline
+        stages before the last)."""
         cfg = self.cfg
         T = fb.num_tokens
         nd = fb.num_decode
@@ -323,6 +331,8 @@ class DecoderLM:
             delta = self._mlp(L, h)
             if L.post_ffn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_ffn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+        if return_residual:
+            return (x.float() + delta.float()).to(x.dtype) if delta is not None else x
         if fb.logit_idx is not None:
             xs = (x.float() + delta.float()).to(x.dtype)[fb.logit_idx] if delta is not None else x[fb.logit_idx]
             h = ops.rmsnorm(xs.contiguous(), self.norm, cfg.rms_norm_eps, cfg.norm_offset_one)
