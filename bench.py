@@ -59,6 +59,10 @@ def parse():
     ap.add_argument("--pp", type=int, default=1, help="pipeline stages (world = pp x tp); stages exchange hidden "
                                                      "states with NCCL p2p")
     ap.add_argument("--kv-fp8", action="store_true", help="fp8-e4m3 paged KV with per-head scales")
+    ap.add_argument("--ep", type=int, default=1, help="expert-parallel ranks (world = ep): MoE experts split whole "
+                                                      "across ranks, attention data-parallel over the rows")
+    ap.add_argument("--ep-mode", default="fused", choices=["fused", "a2a"],
+                    help="fused: dispatch/combine kernels over symmetric memory; a2a: NCCL all_to_all baseline")
     return ap.parse_args()
 
 
@@ -112,6 +116,17 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+EP_MAX_TOKENS = 8192  # tokens per step (all ranks) with expert parallelism; sizes the EP receive buffers
+
+
+def _par(args, world):
+    if args.pp > 1:
+        return f"pp{args.pp}xtp{world // args.pp}"
+    if args.ep > 1:
+        return f"ep{args.ep} ({args.ep_mode} dispatch/combine, data-parallel attention)"
+    return f"tp{world}" + (f" ({args.tp_mode} collectives)" if world > 1 else "")
 
 
 def reference_arm(args):
@@ -178,9 +193,9 @@ def _mtp_measure(args, eng, mtp, streams, dev, world, rank, ttfts, prefill_s, cf
             "config": {"model": f"{args.model}-shape" + (f" ({cfg.num_layers} layers, DEBUG)" if args.layers else ""),
                        "global_batch": args.streams,
                        "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}] + {args.out_tokens} out",
-                       "parallelism": f"pp{args.pp}xtp{world // args.pp}" if args.pp > 1 else f"tp{world}",
+                       "parallelism": _par(args, world),
                        "experts": f"q{args.quant_experts} g64" if args.quant_experts else "bf16", "mtp_k": args.mtp,
-                       "kv": "paged bf16, page 16", "l2": "inputs larger than L2 (weights + KV per step)"},
+                       "kv": ("paged fp8-e4m3 (per-head scales)" if args.kv_fp8 else "paged bf16") + ", page 16", "l2": "inputs larger than L2 (weights + KV per step)"},
             "mtp": ({"rounds": st.rounds, "acceptance": round(st.acceptance_rate, 3),
                      "tokens_per_row_round": round(st.emitted / max(st.rows, 1), 3)} if st else None),
             "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
@@ -193,6 +208,8 @@ def _mtp_measure(args, eng, mtp, streams, dev, world, rank, ttfts, prefill_s, cf
         print(json.dumps(out))
     if world > 1:
         dist.barrier()
+        if getattr(eng.model, "ep", None) is not None:
+            eng.model.ep.close()
         dist.destroy_process_group()
     return 0
 
@@ -240,6 +257,14 @@ def main():
         ppc = PipelineParallel(stage, pp_size, [s * tp_size + tp_rank for s in range(pp_size)], pp_groups[tp_rank])
         tp = TensorParallel(tp_rank, tp_size, tp_group)
         model = PipelinedDecoderLM(cfg, ppc, dev, torch.bfloat16, tp=tp).init_random(args.seed)
+    elif args.ep > 1:
+        from mlx_swift_lm_b200.parallel.expert import ExpertParallel, ExpertParallelDecoderLM
+
+        assert args.ep == world, "--ep must equal the number of ranks"
+        epc = ExpertParallel(cfg.num_experts, cfg.num_experts_per_tok, cfg.hidden_size, rank, world, group, dev,
+                             max_tokens=EP_MAX_TOKENS, impl=args.ep_mode)
+        model = ExpertParallelDecoderLM(cfg, epc, dev, torch.bfloat16).init_random(args.seed)
+        tp_size = 1
     else:
         tp = TensorParallel(rank, world, group)
         model = DecoderLM(cfg, dev, torch.bfloat16, tp=tp).init_random(args.seed)
@@ -255,7 +280,8 @@ def main():
         model.enable_fused_tp(args.streams)
     max_len = args.max_prompt + args.out_tokens + 16
     ecfg = EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=args.streams,
-                                                  max_batched_tokens_per_step=16384, prefill_chunk_size=4096),
+                                                  max_batched_tokens_per_step=EP_MAX_TOKENS if args.ep > 1 else 16384,
+                                                  prefill_chunk_size=4096),
                         max_model_len=max_len, use_cuda_graphs=pp_size == 1, chained_decode=True,
                         kv_fp8=args.kv_fp8,
                         graph_buckets=(args.streams,))
@@ -362,7 +388,7 @@ def main():
             "config": {"model": f"{args.model}-shape" + (f" ({cfg.num_layers} layers, DEBUG)" if args.layers else ""),
                        "global_batch": args.streams, "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}] + "
                                                                 f"{args.out_tokens} out",
-                       "parallelism": f"tp{world}" + (f" ({args.tp_mode} collectives)" if world > 1 else ""), "kv": "paged bf16, page 16",
+                       "parallelism": _par(args, world), "kv": ("paged fp8-e4m3 (per-head scales)" if args.kv_fp8 else "paged bf16") + ", page 16",
                        "l2": "inputs larger than L2 (weights ~16 GB/world + KV per step)"},
             "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
             "itl_p50_ms": round(itl_p50_ms, 3),
@@ -389,6 +415,8 @@ def main():
         if getattr(model, "tp_fused", None) is not None:
             model.tp_fused.comm.close()
             model.tp_fused = None
+        if getattr(model, "ep", None) is not None:
+            model.ep.close()
         torch.cuda.synchronize(dev)
         dist.barrier()
         dist.destroy_process_group()

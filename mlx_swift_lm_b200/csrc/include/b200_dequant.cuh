@@ -8,6 +8,10 @@
 //   scales  [gpb][128] bf16, then biases [gpb][128] bf16 (gpb = groups in the
 //           block: 2 for group size 32, else 1).
 // w = scale * q + bias with one rounding to bf16.
+// WQ = kWqE2M1 (-4): MXFP4 (OCP microscaling) -- 4-bit e2m1 codes (sign,
+// 2 exponent bits, 1 mantissa bit) in the same repacked word order, scales
+// [gpb][128] bf16 powers of two 2^(e8m0 - 127), no biases; w = e2m1(q) * scale
+// (exact).
 // Output: row t of a K-major bf16 tile [128][64] with the 128-byte swizzle
 // the UMMA descriptor expects (16-byte chunk c of row t at c ^ (t & 7)).
 #pragma once
@@ -15,6 +19,27 @@
 #include "b200_common.cuh"
 
 namespace b200 {
+
+constexpr int kWqE2M1 = -4;
+template <int WQ>
+__host__ __device__ constexpr int code_bits() {
+  return WQ < 0 ? -WQ : WQ;
+}
+
+// bf16 pair of two e2m1 codes at bits 0..3 and 16..19 of v, times s2. The
+// magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6} have bf16 patterns 0x0000 0x3F00
+// 0x3F80 0x3FC0 0x4000 0x4040 0x4080 0x40C0: two byte permutes look the low
+// and high bytes up in 8-entry tables held in registers; the sign bit moves
+// to bit 15 of each half.
+__device__ __forceinline__ uint32_t de2m1_pair(uint32_t v, __nv_bfloat162 s2) {
+  const uint32_t mag = v & 0x00070007u;
+  const uint32_t sel = mag | (mag >> 8);  // selector nibbles: 0 = m0, 2 = m1
+  const uint32_t lo = __byte_perm(0xC0800000u, 0xC0804000u, sel);
+  const uint32_t hi = __byte_perm(0x3F3F3F00u, 0x40404040u, sel << 4);
+  const uint32_t x = (lo & 0x00FF00FFu) | (hi & 0xFF00FF00u) | ((v & 0x00080008u) << 12);
+  const __nv_bfloat162 w = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&x), s2);
+  return *reinterpret_cast<const uint32_t*>(&w);
+}
 
 // bf16 pair (q_lo + 128, q_hi + 128) from two 4-bit codes placed at bits 0..3
 // and 16..19 of v (exact: 128..143 are bf16 integers), minus 128, then
@@ -32,12 +57,28 @@ __device__ __forceinline__ uint32_t dq4_pair(uint32_t v, __nv_bfloat162 s2, __nv
 template <int WQ>
 __device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* atile, int t, int half, int g,
                                                  int gpb) {
-  constexpr int kCodeBytes = WQ * 128 * 64 / 8;
+  constexpr int kCodeBytes = code_bits<WQ>() * 128 * 64 / 8;
   const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes);
   const __nv_bfloat16* bi = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes + gpb * 256);
-  const __nv_bfloat16 sv = sc[g * 128 + t], bv = bi[g * 128 + t];
+  const __nv_bfloat16 sv = sc[g * 128 + t];
   uint8_t* arow = atile + t * 128;
-  if constexpr (WQ == 4) {
+  if constexpr (WQ == kWqE2M1) {
+    const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
+    const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+    const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t v = words[w];
+      uint4 o;
+      o.x = de2m1_pair(v, s2);
+      o.y = de2m1_pair(v >> 4, s2);
+      o.z = de2m1_pair(v >> 8, s2);
+      o.w = de2m1_pair(v >> 12, s2);
+      const int chunk = half * 4 + w;
+      *reinterpret_cast<uint4*>(arow + ((chunk ^ (t & 7)) << 4)) = o;
+    }
+  } else if constexpr (WQ == 4) {
+    const __nv_bfloat16 bv = bi[g * 128 + t];
     const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
     const uint32_t words[4] = {c.x, c.y, c.z, c.w};
     const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv), b2 = __halves2bfloat162(bv, bv);
@@ -53,6 +94,7 @@ __device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* at
       *reinterpret_cast<uint4*>(arow + ((chunk ^ (t & 7)) << 4)) = o;
     }
   } else {
+    const __nv_bfloat16 bv = bi[g * 128 + t];
     static_assert(WQ == 8, "4- or 8-bit codes");
     const uint4* cw = reinterpret_cast<const uint4*>(raw + t * 64 + half * 32);
     const uint4 q0 = cw[0], q1 = cw[1];
@@ -79,11 +121,24 @@ __device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* at
 template <int WQ>
 __device__ __forceinline__ void dequant_half_row_regs(const uint8_t* raw, int t, int half, int g, int gpb,
                                                       uint32_t* v) {
-  constexpr int kCodeBytes = WQ * 128 * 64 / 8;
+  constexpr int kCodeBytes = code_bits<WQ>() * 128 * 64 / 8;
   const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes);
   const __nv_bfloat16* bi = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes + gpb * 256);
-  const __nv_bfloat16 sv = sc[g * 128 + t], bv = bi[g * 128 + t];
-  if constexpr (WQ == 4) {
+  const __nv_bfloat16 sv = sc[g * 128 + t];
+  if constexpr (WQ == kWqE2M1) {
+    const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
+    const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+    const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t x = words[w];
+      v[4 * w + 0] = de2m1_pair(x, s2);
+      v[4 * w + 1] = de2m1_pair(x >> 4, s2);
+      v[4 * w + 2] = de2m1_pair(x >> 8, s2);
+      v[4 * w + 3] = de2m1_pair(x >> 12, s2);
+    }
+  } else if constexpr (WQ == 4) {
+    const __nv_bfloat16 bv = bi[g * 128 + t];
     const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
     const uint32_t words[4] = {c.x, c.y, c.z, c.w};
     const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv), b2 = __halves2bfloat162(bv, bv);
@@ -97,6 +152,7 @@ __device__ __forceinline__ void dequant_half_row_regs(const uint8_t* raw, int t,
     }
   } else {
     static_assert(WQ == 8, "4- or 8-bit codes");
+    const __nv_bfloat16 bv = bi[g * 128 + t];
     const uint4* cw = reinterpret_cast<const uint4*>(raw + t * 64 + half * 32);
     const uint4 q0 = cw[0], q1 = cw[1];
     const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};

@@ -87,7 +87,7 @@ template <int BN, int STAGES, int WQ = 0>
 struct GemmSmem {
   static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
   static constexpr int kBBytes = BN * 128;   // BN rows x 64 bf16
-  static constexpr int kCodeBytes = WQ * 128 * 64 / 8;
+  static constexpr int kCodeBytes = code_bits<WQ>() * 128 * 64 / 8;
   static constexpr int kGroupBytes = 2 * 128 * 2;  // up to 2 groups x 128 rows x bf16
   static constexpr int kRawBytes = WQ ? kCodeBytes + 2 * kGroupBytes : 0;
   static constexpr int kStageBytes = ((WQ ? 0 : kABytes) + kBBytes + 1023) / 1024 * 1024;
@@ -740,8 +740,9 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
 int b200_gemm_q(const void* X, int M, int K, int ldx, const void* tiled, int N, int bits, int gs, void* Y, int ldy,
                 const void* R, int ldr, const void* bias, int epi, int num_sms, int force_splits, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
-  if ((bits != 4 && bits != 8) || (gs != 32 && gs != 64 && gs != 128)) return -1;
-  if ((K % 128) || (ldx % 8) || ((uintptr_t)X & 15) || ((uintptr_t)tiled & 15) || (N % 8)) return -1;
+  if ((bits != 4 && bits != 8 && bits != kWqE2M1) || (gs != 32 && gs != 64 && gs != 128)) return -1;
+  if (bits == kWqE2M1 && gs != 32) return -1;
+  if ((K % 64) || (gs == 128 && K % 128) || (ldx % 8) || ((uintptr_t)X & 15) || ((uintptr_t)tiled & 15) || (N % 8)) return -1;
   const bool glu = epi == kEpiSwiGLU || epi == kEpiGeGLU || epi == kEpiSwiGLUOAI;
   if (glu && (N % 128)) return -1;
   const int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
@@ -749,7 +750,7 @@ int b200_gemm_q(const void* X, int M, int K, int ldx, const void* tiled, int N, 
   q.tiled = reinterpret_cast<const uint8_t*>(tiled);
   q.gs = gs;
   q.gpb = gs == 32 ? 2 : 1;
-  q.rec_bytes = bits * 128 * 8 + q.gpb * 512;
+  q.rec_bytes = bits == kWqE2M1 ? 4 * 128 * 8 + q.gpb * 256 : bits * 128 * 8 + q.gpb * 512;
   q.kb_total = K / 64;
   CUtensorMap tx;
   if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
@@ -771,6 +772,7 @@ int b200_gemm_q(const void* X, int M, int K, int ldx, const void* tiled, int N, 
   a.kb_per_split = (a.kb_total + s - 1) / s;
   a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
   const int tiles_n = (N + 127) / 128, tiles_m = (M + BN - 1) / BN;
+  if (bits == kWqE2M1) return launch_bn_q<kWqE2M1>(BN, tx, a, q, tiles_n, tiles_m, stream);
   return bits == 4 ? launch_bn_q<4>(BN, tx, a, q, tiles_n, tiles_m, stream)
                    : launch_bn_q<8>(BN, tx, a, q, tiles_n, tiles_m, stream);
 }

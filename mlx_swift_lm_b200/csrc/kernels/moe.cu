@@ -24,6 +24,7 @@
 
 #include "b200_common.cuh"
 #include "b200_dequant.cuh"
+#include "b200_moe.cuh"
 
 namespace b200 {
 
@@ -35,88 +36,13 @@ bool make_tmap_2d_sw(CUtensorMap* out, const void* ptr, int64_t rows, int64_t co
 namespace moe {
 
 // ---------------------------------------------------------------- router
-// mode 0: softmax over all experts, take top-k, renormalise if norm_topk.
-// mode 1: top-k over logits, softmax over the k (GPT-OSS).
 __global__ void route_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int mode, int norm_topk,
                                   int* __restrict__ ids, float* __restrict__ w) {
   pdl_launch_dependents();
   pdl_wait();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (warp >= T) return;
-  const float* lg = logits + (size_t)warp * E;
-  constexpr int kMaxPer = 8;  // E <= 256
-  float v[kMaxPer];
-  int per = (E + 31) / 32;
-  float mx = -INFINITY;
-  for (int i = 0; i < per; ++i) {
-    const int e = lane + 32 * i;
-    v[i] = e < E ? lg[e] : -INFINITY;
-    mx = fmaxf(mx, v[i]);
-  }
-  mx = warp_max(mx);
-  float denom = 1.f;
-  if (mode == 0) {
-    float s = 0.f;
-    for (int i = 0; i < per; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E) {
-        v[i] = __expf(v[i] - mx);
-        s += v[i];
-      }
-    }
-    denom = warp_sum(s);
-  }
-  float sel_v[16];
-  int sel_i[16];
-  for (int j = 0; j < k; ++j) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = 0; i < per; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E && (v[i] > bv || (v[i] == bv && e < bi))) {
-        bv = v[i];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    sel_v[j] = bv;
-    sel_i[j] = bi;
-    // remove the winner
-    for (int i = 0; i < per; ++i)
-      if (lane + 32 * i == bi) v[i] = -INFINITY;
-  }
-  if (lane == 0) {
-    if (mode == 0) {
-      float s = 0.f;
-      for (int j = 0; j < k; ++j) {
-        sel_v[j] /= denom;
-        s += sel_v[j];
-      }
-      for (int j = 0; j < k; ++j) {
-        ids[warp * k + j] = sel_i[j];
-        w[warp * k + j] = norm_topk ? sel_v[j] / s : sel_v[j];
-      }
-    } else {
-      const float m0 = sel_v[0];
-      float s = 0.f;
-      for (int j = 0; j < k; ++j) {
-        sel_v[j] = __expf(sel_v[j] - m0);
-        s += sel_v[j];
-      }
-      for (int j = 0; j < k; ++j) {
-        ids[warp * k + j] = sel_i[j];
-        w[warp * k + j] = sel_v[j] / s;
-      }
-    }
-  }
+  route_topk_warp(logits + (size_t)warp * E, E, k, mode, norm_topk, ids + (size_t)warp * k, w + (size_t)warp * k);
 }
 
 // ---------------------------------------------------------------- sort
@@ -133,7 +59,7 @@ __global__ void __launch_bounds__(1024) sort_kernel(const int* __restrict__ ids,
   pdl_wait();
   extern __shared__ int sm[];
   int* wcnt = sm;             // [32][E] counts, then exclusive bases
-  int* off = sm + 32 * E;     // [E] expert start offsets
+  int* off = sm + 32 * E;     // [E + 1] expert start offsets, then the valid total
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
   for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) wcnt[i] = 0;
@@ -176,8 +102,12 @@ __global__ void __launch_bounds__(1024) sort_kernel(const int* __restrict__ ids,
     }
     *n_chunks = min(nc, max_chunks);
     if (nc > max_chunks) set_status(kErrBounds);
+    off[E] = acc;  // valid pairs
   }
   __syncthreads();
+  // pairs with an id outside [0, E) (empty expert-parallel receive slots) get
+  // pos -1 and leave the tail of perm at -1
+  for (int s = off[E] + threadIdx.x; s < P; s += blockDim.x) perm[s] = -1;
   for (int b = p0; b < p1; b += 32) {
     const int p = b + lane;
     const int e = p < p1 ? ids[p] : -1;
@@ -187,6 +117,8 @@ __global__ void __launch_bounds__(1024) sort_kernel(const int* __restrict__ ids,
       const int s = off[e] + wcnt[warp * E + e] + __popc(grp & lt);
       perm[s] = p;
       pos[p] = s;
+    } else if (p < p1) {
+      pos[p] = -1;
     }
     __syncwarp();
     if (ok && (grp & lt) == 0) wcnt[warp * E + e] += __popc(grp);
@@ -199,7 +131,7 @@ __global__ void gather_kernel(const __nv_bfloat16* __restrict__ x, int K, const 
   pdl_launch_dependents();
   pdl_wait();
   const int s = blockIdx.x;
-  if (s >= P) return;
+  if (s >= P || perm[s] < 0) return;
   const int t = perm[s] / k;
   const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * K);
   uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)s * K);
@@ -259,7 +191,7 @@ struct GQuant {
 template <int BN, int STAGES, int WQ>
 struct GSmem {
   static constexpr int kA = 128 * 128, kB = BN * 128;
-  static constexpr int kCode = WQ * 128 * 64 / 8, kGroup = 2 * 128 * 2;
+  static constexpr int kCode = code_bits<WQ>() * 128 * 64 / 8, kGroup = 2 * 128 * 2;
   static constexpr int kRaw = WQ ? kCode + 2 * kGroup : 0;
   static constexpr int kStage = (kA + kB + 1023) / 1024 * 1024;
   static constexpr int kRawStages = WQ ? (100 * 1024 - STAGES * kStage) / kRaw : 0;
@@ -486,10 +418,10 @@ int b200_moe_route_topk(const float* logits, int T, int E, int k, int mode, int 
 int b200_moe_sort(const int* ids, int P, int E, int BN, int max_chunks, int* perm, int* pos, int* chunks,
                   int* n_chunks, cudaStream_t st) {
   if (E > 1024 || P <= 0) return P < 0 ? -1 : (E > 1024 ? -1 : 0);
-  const int smem = 33 * E * (int)sizeof(int);
+  const int smem = (33 * E + 1) * (int)sizeof(int);
   static bool cfg = false;
   if (!cfg) {
-    cudaError_t e = cudaFuncSetAttribute(moe::sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 33 * 1024 * 4);
+    cudaError_t e = cudaFuncSetAttribute(moe::sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (33 * 1024 + 1) * 4);
     if (e != cudaSuccess) return (int)e;
     cfg = true;
   }
@@ -538,19 +470,21 @@ int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* tiled, int
                             int ldy, const void* bias, int epi, const int* chunks, const int* n_chunks, int max_chunks,
                             int BN, cudaStream_t st) {
   if (P <= 0) return 0;
-  if ((K % 128) || (N % 8) || (bits != 4 && bits != 8) || (gs != 32 && gs != 64 && gs != 128)) return -1;
-  if ((uintptr_t)tiled & 15) return -1;
+  if ((K % 64) || (gs == 128 && K % 128) || (N % 8) || (bits != 4 && bits != 8 && bits != kWqE2M1) || (gs != 32 && gs != 64 && gs != 128))
+    return -1;
+  if ((bits == kWqE2M1 && gs != 32) || ((uintptr_t)tiled & 15)) return -1;
   CUtensorMap tx;
   moe::GQuant q;
   q.tiled = reinterpret_cast<const uint8_t*>(tiled);
   q.gs = gs;
   q.gpb = gs == 32 ? 2 : 1;
-  q.rec_bytes = bits * 128 * 8 + q.gpb * 512;
+  q.rec_bytes = bits == kWqE2M1 ? 4 * 128 * 8 + q.gpb * 256 : bits * 128 * 8 + q.gpb * 512;
   q.kb_total = K / 64;
   q.tiles_per_expert = (N + 127) / 128;
   if (!make_tmap_2d(&tx, xs, P, K, K, BN, 64, 2)) return -1;
   moe::GArgs a{reinterpret_cast<__nv_bfloat16*>(Y), reinterpret_cast<const __nv_bfloat16*>(bias), chunks, n_chunks,
                N, K, ldy, epi};
+  if (bits == kWqE2M1) return moe::dispatch_grouped<kWqE2M1>(BN, tx, tx, a, q, max_chunks, st);
   return bits == 4 ? moe::dispatch_grouped<4>(BN, tx, tx, a, q, max_chunks, st)
                    : moe::dispatch_grouped<8>(BN, tx, tx, a, q, max_chunks, st);
 }

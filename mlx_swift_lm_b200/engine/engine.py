@@ -254,6 +254,7 @@ class EngineV2:
         if len(logit_idx) != T:
             fb.logit_idx = torch.tensor(logit_idx, dtype=torch.int64)
             fb.logit_idx_host = logit_idx
+        fb.row_ranks = self._row_ranks(rows)
         if dev.type == "cuda":
             for name in ("input_ids", "positions", "slots", "dec_page_table", "dec_seq_lens", "pf_cu_q", "pf_pos0",
                          "pf_page_table", "logit_idx"):
@@ -262,6 +263,31 @@ class EngineV2:
                     self.h2d_bytes += t.numel() * t.element_size()
                     setattr(fb, name, t.pin_memory().to(dev, non_blocking=True))
         return fb
+
+    def _row_ranks(self, rows) -> list[int] | None:
+        """Data-parallel owner of each row for models that split a step's rows
+        across ranks (``model.dp_world > 1``): a request is pinned, at its
+        first step, to the rank with the fewest pinned running requests (ties
+        to the lower rank). Every rank schedules the same requests in the same
+        order, so every rank computes the same assignment."""
+        world = getattr(self.model, "dp_world", 1)
+        if world <= 1:
+            return None
+        load = [0] * world
+        for st in self.sched.running:
+            d = st.extra.get("dp_rank")
+            if d is not None:
+                load[d] += 1
+        out = []
+        for r in rows:
+            st = r.state
+            d = st.extra.get("dp_rank")
+            if d is None:
+                d = min(range(world), key=lambda j: (load[j], j))
+                st.extra["dp_rank"] = d
+                load[d] += 1
+            out.append(d)
+        return out
 
     # ------------------------------------------------------------------ step
     def step_once_for_stream(self) -> bool:

@@ -32,6 +32,11 @@ class DecodeGraphRunner:
         bk = sorted(b for b in engine.cfg.graph_buckets if b <= max(mc, 1))
         if not bk or bk[-1] < mc:
             bk.append(mc)
+        # models that split rows across data-parallel ranks take rank r's rows
+        # in the slice [r * B / world, (r + 1) * B / world) of a bucket of B
+        self.dp = getattr(self.model, "dp_world", 1)
+        if self.dp > 1:
+            bk = sorted({-(-b // self.dp) * self.dp for b in bk})
         self.buckets = bk
         self.Bmax = bk[-1] + (bk[-1] % 2)
         self.maxp = engine.max_pages
@@ -119,9 +124,28 @@ class DecodeGraphRunner:
                 return b
         return None
 
+    def layout(self, plan):
+        """(bucket, buffer position of each plan row), or (None, None)."""
+        rows = plan.rows
+        if self.dp <= 1:
+            return self.bucket(len(rows)), list(range(len(rows)))
+        ranks = self.eng._row_ranks(rows)
+        per = [0] * self.dp
+        for d in ranks:
+            per[d] += 1
+        Bb = self.bucket(self.dp * max(per))
+        if Bb is None:
+            return None, None
+        S = Bb // self.dp
+        nxt = [d * S for d in range(self.dp)]
+        pos = []
+        for d in ranks:
+            pos.append(nxt[d])
+            nxt[d] += 1
+        return Bb, pos
+
     def can_run(self, plan) -> bool:
-        n = len(plan.rows)
-        if self.bucket(n) is None:
+        if self.layout(plan)[0] is None:
             return False
         for r in plan.rows:
             if len(r.state.seq.pages) > self.maxp:
@@ -134,7 +158,7 @@ class DecodeGraphRunner:
     def launch(self, plan, chained_from=None):
         rows = plan.rows
         n = len(rows)
-        Bb = self.bucket(n)
+        Bb, where = self.layout(plan)
         if Bb not in self.graphs:
             # capture's warm-up overwrites the shared output buffer, which may hold
             # the in-flight step's tokens that this launch gathers from
@@ -158,9 +182,11 @@ class DecodeGraphRunner:
         pt = a[self.o_pt:self.o_pt + self.Bmax * P].reshape(self.Bmax, P)
         prev_idx = {}
         if chained_from is not None:
+            prev_where = chained_from[1][3]
             for j, r in enumerate(chained_from[0].rows):
-                prev_idx[id(r.state)] = j
-        for i, r in enumerate(rows):
+                prev_idx[id(r.state)] = prev_where[j]
+        for i0, r in enumerate(rows):
+            i = where[i0]
             st = r.state
             p = r.start
             a[self.o_pos + i] = p
@@ -188,13 +214,15 @@ class DecodeGraphRunner:
         _lib.count(self.launches_per_replay.get(Bb, 0))
         ko = self.out_k
         self.out_k = (self.out_k + 1) % len(self.host_out)
-        self.host_out[ko][:n].copy_(self.out[:n], non_blocking=True)
-        self.d2h_bytes += 4 * n
+        m = max(where) + 1 if where else 0
+        self.host_out[ko][:m].copy_(self.out[:m], non_blocking=True)
+        self.d2h_bytes += 4 * m
         done = torch.cuda.Event()
         done.record()
-        return (ko, done, n)
+        return (ko, done, n, where)
 
     def read_tokens(self, handle, n):
-        ko, done, n0 = handle
+        ko, done, n0, where = handle
         done.synchronize()
-        return self.host_out[ko][:n].tolist()
+        h = self.host_out[ko].tolist()
+        return [h[where[i]] for i in range(n)]

@@ -196,9 +196,10 @@ class MTPDriver:
         seqs = [st.seq for st in states]
         fbv = self._chunk_batch([[0] * (k + 1)] * B, p, [k + 1] * B, seqs, p, logit_last=False)
         fbv.input_ids = vt.reshape(-1)
+        fbv.row_ranks = eng._row_ranks(rows)
         fbv = self._to_dev(fbv)
-        vlog, vh = eng.model.forward(fbv, eng.kv, return_both=True)
-        pred = ops.argmax(vlog).view(B, k + 1)
+        pred, vh = eng.model.forward_greedy_both(fbv, eng.kv)
+        pred = pred.view(B, k + 1)
         both = torch.cat([pred, D], 1).cpu().numpy()
         self.d2h_bytes += both.nbytes
         pred_h, D_h = both[:, :k + 1], both[:, k + 1:]

@@ -102,11 +102,14 @@ def export_tensors(model) -> dict[str, torch.Tensor]:
             if cfg.model_type == "gpt_oss":
                 raise ValueError("export of gpt-oss expert layouts is not supported")
             out[mp + "gate.weight"] = _dense(L.router)
-            for e in range(L.experts_gu.shape[0]):
-                g, u = deinterleave_gate_up(_dense(L.experts_gu[e]))
+            E = L.experts_gu.num_experts if isinstance(L.experts_gu, QuantizedWeight) else L.experts_gu.shape[0]
+            for e in range(E):
+                ge = L.experts_gu.expert(e) if isinstance(L.experts_gu, QuantizedWeight) else L.experts_gu[e]
+                de = L.experts_d.expert(e) if isinstance(L.experts_d, QuantizedWeight) else L.experts_d[e]
+                g, u = deinterleave_gate_up(_dense(ge))
                 out[f"{mp}experts.{e}.gate_proj.weight"] = g
                 out[f"{mp}experts.{e}.up_proj.weight"] = u
-                out[f"{mp}experts.{e}.down_proj.weight"] = _dense(L.experts_d[e])
+                out[f"{mp}experts.{e}.down_proj.weight"] = _dense(de)
             if L.shared_gu is not None:
                 g, u = deinterleave_gate_up(_dense(L.shared_gu))
                 out[mp + "shared_expert.gate_proj.weight"] = g

@@ -89,9 +89,10 @@ class CheckpointView:
             gs, bits, mode = self._qparams(base)
             s = self.raw(base + ".scales")
             b = self.raw(base + ".biases") if self.has(base + ".biases") else None
-            if (self.keep_quantized and packed and mode == "affine" and b is not None and bits in SUPPORTED_BITS
-                    and gs in SUPPORTED_GROUPS):
-                return QuantizedWeight.from_mlx(w, s.to(torch.bfloat16), b.to(torch.bfloat16), bits, gs)
+            if self.keep_quantized and packed:
+                qw = _packed(w, s, b, mode, bits, gs)
+                if qw is not None:
+                    return qw
             return quant.dequantize(w, s, b, mode, gs, bits, torch.float32).to(self.dtype)
         return w.to(self.dtype)
 
@@ -101,6 +102,33 @@ class CheckpointView:
                 raise KeyError(name)
             return None
         return self.raw(name).to(self.dtype)
+
+
+def _packed(w, s, b, mode, bits, gs):
+    """A packed QuantizedWeight for MLX affine 4/8-bit or MXFP4 weights the
+    kernels serve (stacked experts [E, N, ...] keep num_experts), else None."""
+    E = w.shape[0] if w.dim() == 3 else 0
+    w2 = w.reshape(-1, w.shape[-1])
+    s2 = s.reshape(-1, s.shape[-1])
+    if mode == "affine" and b is not None and bits in SUPPORTED_BITS and gs in SUPPORTED_GROUPS:
+        qw = QuantizedWeight.from_mlx(w2, s2.to(torch.bfloat16), b.reshape(-1, b.shape[-1]).to(torch.bfloat16), bits,
+                                      gs)
+    elif mode == "mxfp4" and bits == 4 and gs == 32:
+        qw = QuantizedWeight.from_mlx_mxfp4(w2, s2)
+    else:
+        return None
+    qw.num_experts = E
+    return qw
+
+
+def _stack(parts):
+    if isinstance(parts[0], QuantizedWeight):
+        return QuantizedWeight.stack_experts(parts)
+    return torch.stack(parts)
+
+
+def _expert(w, e):
+    return w.expert(e) if isinstance(w, QuantizedWeight) else w[e]
 
 
 def _shard_rows(w, rank, world):
@@ -239,7 +267,19 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
         mp = p + "mlp."
         L.router = ck.linear(mp + "router", packed=False)
         L.router_b = ck.vec(mp + "router.bias")
-        if ck.has(mp + "experts.gate_up_proj_blocks"):
+        packed = ck.keep_quantized and ck.has(mp + "experts.gate_up_proj_blocks")
+        if packed:
+            # HF MXFP4 blocks stay packed: rows are outputs, gate at even and
+            # up at odd rows of gate_up
+            gq = _mxfp4_packed(ck.raw(mp + "experts.gate_up_proj_blocks"), ck.raw(mp + "experts.gate_up_proj_scales"))
+            dq = _mxfp4_packed(ck.raw(mp + "experts.down_proj_blocks"), ck.raw(mp + "experts.down_proj_scales"))
+            F2 = gq.shape[0] // E
+            even = torch.arange(0, F2, 2)
+            L.experts_gu = QuantizedWeight.stack_experts([
+                interleave_gate_up(_shard_rows(gq.expert(e).select_rows(even), r, w),
+                                   _shard_rows(gq.expert(e).select_rows(even + 1), r, w)) for e in range(E)])
+            L.experts_d = QuantizedWeight.stack_experts([_shard_cols(dq.expert(e), r, w) for e in range(E)])
+        elif ck.has(mp + "experts.gate_up_proj_blocks"):
             blocks = ck.raw(mp + "experts.gate_up_proj_blocks")  # [E, 2F, K/32, 16] uint8
             scales = ck.raw(mp + "experts.gate_up_proj_scales")  # [E, 2F, K/32] uint8
             gu = _mxfp4_blocks(blocks, scales)  # [E, 2F, K]
@@ -250,11 +290,12 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
         else:
             gu = ck.raw(mp + "experts.gate_up_proj").float()  # [E, K, 2F] (gate even, up odd columns)
             down = ck.raw(mp + "experts.down_proj").float()  # [E, F, K]
-        g, u = gu[..., 0::2].transpose(1, 2), gu[..., 1::2].transpose(1, 2)  # [E, F, K]
+        if not packed:
+            g, u = gu[..., 0::2].transpose(1, 2), gu[..., 1::2].transpose(1, 2)  # [E, F, K]
+            L.experts_gu = torch.stack([interleave_gate_up(_shard_rows(g[e], r, w), _shard_rows(u[e], r, w))
+                                        for e in range(E)])
+            L.experts_d = torch.stack([_shard_cols(down[e].t(), r, w) for e in range(E)])  # [E, K, F]
         gub = ck.vec(mp + "experts.gate_up_proj_bias")
-        L.experts_gu = torch.stack([interleave_gate_up(_shard_rows(g[e], r, w), _shard_rows(u[e], r, w))
-                                    for e in range(E)])
-        L.experts_d = torch.stack([_shard_cols(down[e].t(), r, w) for e in range(E)])  # [E, K, F]
         if gub is not None:
             gb, ub = gub[..., 0::2], gub[..., 1::2]
             L.experts_gu_b = torch.stack([interleave_gate_up(_shard_rows(gb[e], r, w)[:, None],
@@ -266,16 +307,20 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
     mp = p + ("block_sparse_moe." if mixtral else "mlp.")
     L.router = ck.linear(mp + "gate", packed=False)
     names = ("w1", "w3", "w2") if mixtral else ("gate_proj", "up_proj", "down_proj")
+    # quantised experts stay packed when every expert's format is one the
+    # grouped kernels serve (else all are dequantised)
     if ck.has(mp + "switch_mlp.gate_proj.weight"):
-        g = ck.linear(mp + "switch_mlp.gate_proj", packed=False)
-        u = ck.linear(mp + "switch_mlp.up_proj", packed=False)
-        d = ck.linear(mp + "switch_mlp.down_proj", packed=False)
+        g = ck.linear(mp + "switch_mlp.gate_proj")
+        u = ck.linear(mp + "switch_mlp.up_proj")
+        d = ck.linear(mp + "switch_mlp.down_proj")
+        g, u, d = ([_expert(t, e) for e in range(E)] for t in (g, u, d))
     else:
-        g = torch.stack([ck.linear(f"{mp}experts.{e}.{names[0]}", packed=False) for e in range(E)])
-        u = torch.stack([ck.linear(f"{mp}experts.{e}.{names[1]}", packed=False) for e in range(E)])
-        d = torch.stack([ck.linear(f"{mp}experts.{e}.{names[2]}", packed=False) for e in range(E)])
-    L.experts_gu = torch.stack([interleave_gate_up(_shard_rows(g[e], r, w), _shard_rows(u[e], r, w)) for e in range(E)])
-    L.experts_d = torch.stack([_shard_cols(d[e], r, w) for e in range(E)])
+        g, u, d = ([ck.linear(f"{mp}experts.{e}.{n}") for e in range(E)] for n in names)
+    if not all(isinstance(t, QuantizedWeight) for t in g + u + d):
+        g, u, d = ([t.dequantize(torch.float32).to(ck.dtype) if isinstance(t, QuantizedWeight) else t for t in x]
+                   for x in (g, u, d))
+    L.experts_gu = _stack([interleave_gate_up(_shard_rows(g[e], r, w), _shard_rows(u[e], r, w)) for e in range(E)])
+    L.experts_d = _stack([_shard_cols(d[e], r, w) for e in range(E)])
     if cfg.shared_expert_intermediate_size:
         sp = mp + "shared_expert."
         L.shared_gu = interleave_gate_up(_shard_rows(ck.linear(sp + "gate_proj"), r, w),
@@ -283,6 +328,17 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
         L.shared_d = _shard_cols(ck.linear(sp + "down_proj"), r, w)
         if ck.has(mp + "shared_expert_gate.weight"):
             L.shared_gate = ck.linear(mp + "shared_expert_gate", packed=False)
+
+
+def _mxfp4_packed(blocks, scales) -> QuantizedWeight:
+    """HF MXFP4 expert stack (blocks [E, N, G, 16] uint8, two e2m1 codes per
+    byte low nibble first; scales [E, N, G] e8m0) -> packed [E*N, 32G]."""
+    E, N, G, _ = blocks.shape
+    b = blocks.reshape(E * N, G * 16).to(torch.int32)
+    codes = torch.stack([b & 0x0F, b >> 4], -1).reshape(E * N, G * 32)
+    qw = QuantizedWeight.from_mxfp4(codes, scales.reshape(E * N, G))
+    qw.num_experts = E
+    return qw
 
 
 def _mxfp4_blocks(blocks, scales):

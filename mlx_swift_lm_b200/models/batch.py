@@ -33,6 +33,8 @@ class ForwardBatch:
     logit_idx_host: list | None = None  # the same indices on the host (microbatch splitting)
     # per-token LoRA adapter slot (-1 = none), used when adapters are active
     lora_slots: torch.Tensor | None = None
+    # data-parallel rank that owns each row's KV (expert-parallel models); host list
+    row_ranks: list | None = None
 
     @property
     def num_tokens(self) -> int:

@@ -361,6 +361,12 @@ class DecoderLM:
         if getattr(self, "tp_fused", None) is not None:
             self.tp_fused.comm.begin_step()
 
+    def forward_greedy_both(self, fb: ForwardBatch, kv):
+        """(greedy token [rows] int32, final hidden [rows, H]) of the logit
+        rows: the batched verify of speculative decoding needs no more."""
+        logits, h = self.forward(fb, kv, return_both=True)
+        return ops.argmax(logits), h
+
     def forward_decode_tokens(self, fb: ForwardBatch, kv, out: torch.Tensor, out2=None):
         """Greedy tokens of a pure-decode batch: the fused TP path when
         enabled, else forward + argmax."""

@@ -74,7 +74,7 @@ def gemm_q(x: torch.Tensor, w: QuantizedWeight, epi: str = "none", residual: tor
     n_out = N // 2 if epi in _GLU else N
     if out is None:
         out = torch.empty((M, n_out), dtype=torch.float32 if epi == "f32" else torch.bfloat16, device=x.device)
-    rc = _lib.lib().b200_gemm_q(x.data_ptr(), M, K, x.stride(0), w.tiled().data_ptr(), N, w.bits, w.gs,
+    rc = _lib.lib().b200_gemm_q(x.data_ptr(), M, K, x.stride(0), w.tiled().data_ptr(), N, w.kernel_bits, w.gs,
                                 out.data_ptr(), out.stride(0),
                                 _lib.ptr(residual), residual.stride(0) if residual is not None else 0,
                                 _lib.ptr(bias), _EPI[epi], num_sms(x.device), int(splits),

@@ -83,7 +83,7 @@ def chunk_rows(P: int, E: int) -> int:
 
 def _grouped(L, xs, P, K, W, E, N, Y, ldy, bias, epi, chunks, n_chunks, max_chunks, BN, st, what):
     if isinstance(W, QuantizedWeight):
-        rc = L.b200_moe_grouped_gemm_q(xs.data_ptr(), P, K, W.tiled().data_ptr(), W.bits, W.gs, E, N, Y.data_ptr(),
+        rc = L.b200_moe_grouped_gemm_q(xs.data_ptr(), P, K, W.tiled().data_ptr(), W.kernel_bits, W.gs, E, N, Y.data_ptr(),
                                        ldy, _lib.ptr(bias), epi, chunks.data_ptr(), n_chunks.data_ptr(), max_chunks,
                                        BN, st)
     else:

@@ -13,6 +13,12 @@ such weights packed in the layout the dequantising tcgen05 GEMM
 * scales_t, biases_t  bf16 [K/gs, N] (transposed: rows of N are what a
   128-row weight tile needs, contiguous for TMA).
 
+MXFP4 (``mode="mxfp4"``, the OCP microscaling format of GPT-OSS and MLX's
+``mxfp4`` mode): 4-bit e2m1 codes (sign, two exponent bits, one mantissa bit)
+in the same repacked nibble order, one power-of-two scale 2^(e8m0 - 127) per
+32 inputs (kept as bf16, exact), no biases; w = e2m1(q) * scale. The kernels
+take it as ``bits = -4``.
+
 Row operations used by the model builder (stacking q|k|v, interleaving
 gate/up, tensor-parallel row / column shards) act on codes, scales and biases
 together; groups run along K, so they commute with quantisation. Column shards
@@ -26,6 +32,34 @@ from . import quant
 
 SUPPORTED_BITS = (4, 8)
 SUPPORTED_GROUPS = (32, 64, 128)
+# e2m1 magnitudes of codes 0..7 (code bit 3 is the sign)
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+def e2m1_decode(q: torch.Tensor) -> torch.Tensor:
+    """float values of e2m1 codes (int tensor, 0..15)."""
+    lut = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=q.device)
+    v = lut[(q & 7).long()]
+    return torch.where((q & 8) != 0, -v, v)
+
+
+def e2m1_encode(x: torch.Tensor) -> torch.Tensor:
+    """Nearest e2m1 code of each value (ties to the even mantissa, saturating
+    at +-6), int32."""
+    a = x.abs().clamp(max=6.0)
+    # midpoints between consecutive magnitudes; ties go to the code with m = 0
+    mids = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], device=x.device)
+    m = torch.bucketize(a, mids, right=False).to(torch.int32)
+    # bucketize puts a value equal to a midpoint in the lower bucket; move
+    # ties whose lower code is odd (m = 1) up to the even code
+    tie = (a.unsqueeze(-1) == mids).any(-1) & (m % 2 == 1)
+    m = torch.where(tie, m + 1, m)
+    return torch.where((x < 0) & (m > 0), m | 8, m).to(torch.int32)
+
+
+def e8m0_to_scale(s: torch.Tensor) -> torch.Tensor:
+    """2^(s - 127) of uint8 e8m0 exponents, as float32."""
+    return torch.exp2(s.to(torch.float32) - 127.0)
 
 
 def _repack4(q: torch.Tensor) -> torch.Tensor:
@@ -51,16 +85,29 @@ def _unpack4(c: torch.Tensor) -> torch.Tensor:
 
 
 class QuantizedWeight:
-    """Packed affine weight of logical shape [N, K]."""
+    """Packed affine or MXFP4 weight of logical shape [N, K]."""
 
-    def __init__(self, codes: torch.Tensor, scales_t: torch.Tensor, biases_t: torch.Tensor, bits: int, gs: int,
-                 num_experts: int = 0):
+    def __init__(self, codes: torch.Tensor, scales_t: torch.Tensor, biases_t: torch.Tensor | None, bits: int, gs: int,
+                 num_experts: int = 0, mode: str = "affine"):
         assert bits in SUPPORTED_BITS and gs in SUPPORTED_GROUPS, (bits, gs)
+        assert mode in ("affine", "mxfp4")
+        assert mode == "affine" or (bits == 4 and gs == 32 and biases_t is None), "mxfp4: 4-bit, group 32, no bias"
         self.codes, self.scales_t, self.biases_t = codes, scales_t, biases_t
-        self.bits, self.gs = bits, gs
+        self.bits, self.gs, self.mode = bits, gs, mode
         self.shape = (codes.shape[0], codes.shape[1] * 8 // bits)
         # > 0: MoE experts stacked along rows, expert e owns rows [e*N/E, (e+1)*N/E)
         self.num_experts = num_experts
+
+    @property
+    def kernel_bits(self) -> int:
+        """Format code of the kernels' C ABI: 4 / 8 affine, -4 MXFP4."""
+        return -4 if self.mode == "mxfp4" else self.bits
+
+    def _like(self, codes, scales_t, biases_t, num_experts: int = 0) -> "QuantizedWeight":
+        return QuantizedWeight(codes, scales_t, biases_t, self.bits, self.gs, num_experts, self.mode)
+
+    def _bsel(self, fn):
+        return None if self.biases_t is None else fn(self.biases_t)
 
     # ---------------------------------------------------------------- construction
     @classmethod
@@ -76,6 +123,33 @@ class QuantizedWeight:
         K = scales.shape[-1] * gs
         q = quant.unpack_codes(packed.cpu(), bits, K)
         return cls.from_codes(q, scales.cpu(), biases.cpu(), bits, gs)
+
+    @classmethod
+    def from_mxfp4(cls, q: torch.Tensor, scales_e8m0: torch.Tensor):
+        """e2m1 codes int [N, K] (0..15) and uint8 e8m0 exponents [N, K/32]."""
+        sc = e8m0_to_scale(scales_e8m0).to(torch.bfloat16)
+        return cls(_repack4(q).contiguous(), sc.t().contiguous(), None, 4, 32, mode="mxfp4")
+
+    @classmethod
+    def from_mlx_mxfp4(cls, packed: torch.Tensor, scales: torch.Tensor):
+        """MLX ``mxfp4`` layout: uint32 words (as int32) [N, K/8], 8 codes
+        per word low nibble first; uint8 scales [N, K/32]."""
+        K = scales.shape[-1] * 32
+        q = quant.unpack_codes(packed.cpu(), 4, K)
+        return cls.from_mxfp4(q, scales.cpu())
+
+    @classmethod
+    def quantize_mxfp4(cls, w: torch.Tensor):
+        """MXFP4 quantisation of a float weight [N, K] where it lives: per 32
+        inputs the shared exponent floor(log2(amax)) - 2 (e2m1's largest
+        exponent), then the nearest e2m1 code of w / 2^exp."""
+        N, K = w.shape
+        g = w.float().reshape(N, K // 32, 32)
+        amax = g.abs().amax(-1, keepdim=True).clamp(min=2.0 ** -120)
+        e = torch.floor(torch.log2(amax)) - 2
+        s = (e + 127).clamp(0, 254)
+        q = e2m1_encode(g / torch.exp2(s - 127)).reshape(N, K)
+        return cls.from_mxfp4(q, s[..., 0].to(torch.uint8))
 
     @classmethod
     def quantize(cls, w: torch.Tensor, bits: int = 4, gs: int = 64):
@@ -114,25 +188,28 @@ class QuantizedWeight:
         return _unpack4(self.codes) if self.bits == 4 else self.codes.to(torch.int32)
 
     def dequantize(self, dtype=torch.float32) -> torch.Tensor:
-        """[N, K] weights with one rounding of scale * q + bias (as the kernel)."""
-        q = self.codes_int().float()
-        N, K = q.shape
+        """[N, K] weights with one rounding of scale * q + bias (as the kernel);
+        MXFP4: e2m1(q) * scale (exact)."""
+        q = self.codes_int()
         s = self.scales_t.t().float().repeat_interleave(self.gs, dim=1)
+        if self.mode == "mxfp4":
+            return (e2m1_decode(q) * s).to(torch.bfloat16).to(dtype)
         b = self.biases_t.t().float().repeat_interleave(self.gs, dim=1)
-        return (q * s + b).to(torch.bfloat16).to(dtype)
+        return (q.float() * s + b).to(torch.bfloat16).to(dtype)
 
     def to(self, device=None, dtype=None):
         dt = dtype if dtype in (torch.bfloat16, torch.float16, torch.float32) else None
+        if self.mode == "mxfp4":
+            dt = None  # power-of-two scales stay bf16
         sc = self.scales_t.to(device=device, dtype=dt or self.scales_t.dtype)
-        bi = self.biases_t.to(device=device, dtype=dt or self.biases_t.dtype)
-        return QuantizedWeight(self.codes.to(device), sc, bi, self.bits, self.gs, self.num_experts)
+        bi = self._bsel(lambda b: b.to(device=device, dtype=dt or b.dtype))
+        return self._like(self.codes.to(device), sc, bi, self.num_experts)
 
     def select_rows(self, idx: torch.Tensor, num_experts: int = 0) -> "QuantizedWeight":
         """Rows `idx` (any order) as a new weight."""
         idx = idx.to(self.codes.device)
-        return QuantizedWeight(self.codes.index_select(0, idx).contiguous(),
-                               self.scales_t.index_select(1, idx).contiguous(),
-                               self.biases_t.index_select(1, idx).contiguous(), self.bits, self.gs, num_experts)
+        return self._like(self.codes.index_select(0, idx).contiguous(), self.scales_t.index_select(1, idx).contiguous(),
+                          self._bsel(lambda b: b.index_select(1, idx).contiguous()), num_experts)
 
     @staticmethod
     def stack_experts(parts: list["QuantizedWeight"]) -> "QuantizedWeight":
@@ -148,7 +225,7 @@ class QuantizedWeight:
     # ---------------------------------------------------------------- device layout
     def record_bytes(self) -> int:
         gpb = 2 if self.gs == 32 else 1
-        return self.bits * 128 * 8 + gpb * 512
+        return self.bits * 128 * 8 + gpb * (256 if self.biases_t is None else 512)
 
     def tiled(self) -> torch.Tensor:
         """Tile-major device layout streamed by the dequantising kernels
@@ -169,7 +246,7 @@ class QuantizedWeight:
         dev = self.codes.device
         codes = self.codes.view(E, Ne, KB, cb)
         sc = self.scales_t.t().reshape(E, Ne, -1)  # [E, Ne, G]
-        bi = self.biases_t.t().reshape(E, Ne, -1)
+        bi = self.biases_t.t().reshape(E, Ne, -1) if self.biases_t is not None else torch.zeros_like(sc)
         pad = tiles * 128 - Ne
         if pad:
             codes = torch.cat([codes, torch.zeros(E, pad, KB, cb, dtype=codes.dtype, device=dev)], 1)
@@ -187,7 +264,7 @@ class QuantizedWeight:
         b_ = bi_kb.reshape(E, tiles, 128, KB, -1).permute(0, 1, 3, 4, 2).contiguous()
         s_b = s_.view(torch.uint8).reshape(E, tiles, KB, -1)
         b_b = b_.view(torch.uint8).reshape(E, tiles, KB, -1)
-        rec = torch.cat([c, s_b, b_b], dim=-1).contiguous()
+        rec = torch.cat([c, s_b] if self.biases_t is None else [c, s_b, b_b], dim=-1).contiguous()
         assert rec.shape[-1] == self.record_bytes()
         self._tiled = rec.reshape(-1)
         return self._tiled
@@ -196,25 +273,26 @@ class QuantizedWeight:
         return self.shape[0] * self.shape[1]
 
     def nbytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in (self.codes, self.scales_t, self.biases_t))
+        return sum(t.numel() * t.element_size() for t in (self.codes, self.scales_t, self.biases_t) if t is not None)
 
     # ---------------------------------------------------------------- row / column ops
     def rows(self, lo: int, hi: int) -> "QuantizedWeight":
-        return QuantizedWeight(self.codes[lo:hi].contiguous(), self.scales_t[:, lo:hi].contiguous(),
-                               self.biases_t[:, lo:hi].contiguous(), self.bits, self.gs)
+        return self._like(self.codes[lo:hi].contiguous(), self.scales_t[:, lo:hi].contiguous(),
+                          self._bsel(lambda b: b[:, lo:hi].contiguous()))
 
     def cols(self, lo: int, hi: int) -> "QuantizedWeight":
         assert lo % self.gs == 0 and hi % self.gs == 0, "column shards must align with quantisation groups"
         c0, c1 = lo * self.bits // 8, hi * self.bits // 8
-        return QuantizedWeight(self.codes[:, c0:c1].contiguous(), self.scales_t[lo // self.gs:hi // self.gs].contiguous(),
-                               self.biases_t[lo // self.gs:hi // self.gs].contiguous(), self.bits, self.gs)
+        g0, g1 = lo // self.gs, hi // self.gs
+        return self._like(self.codes[:, c0:c1].contiguous(), self.scales_t[g0:g1].contiguous(),
+                          self._bsel(lambda b: b[g0:g1].contiguous()))
 
     @staticmethod
     def cat_rows(parts: list["QuantizedWeight"]) -> "QuantizedWeight":
         p0 = parts[0]
-        assert all(p.bits == p0.bits and p.gs == p0.gs for p in parts)
-        return QuantizedWeight(torch.cat([p.codes for p in parts], 0), torch.cat([p.scales_t for p in parts], 1),
-                               torch.cat([p.biases_t for p in parts], 1), p0.bits, p0.gs)
+        assert all(p.bits == p0.bits and p.gs == p0.gs and p.mode == p0.mode for p in parts)
+        bi = None if p0.biases_t is None else torch.cat([p.biases_t for p in parts], 1)
+        return p0._like(torch.cat([p.codes for p in parts], 0), torch.cat([p.scales_t for p in parts], 1), bi)
 
     @staticmethod
     def interleave_gate_up(g: "QuantizedWeight", u: "QuantizedWeight", block: int = 64) -> "QuantizedWeight":

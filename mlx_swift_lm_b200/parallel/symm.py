@@ -52,6 +52,41 @@ def _align(n, a=256):
     return (n + a - 1) // a * a
 
 
+def open_symmetric(group, rank: int, world: int, device, nbytes: int):
+    """Allocate a zeroed device buffer of `nbytes` on every rank of `group`
+    and map every peer's buffer (CUDA IPC handles exchanged over the group).
+    Returns (local pointer, [pointer of rank j's buffer for j in range(world)])."""
+    L = _lib.lib()
+    with torch.cuda.device(device):
+        ptr = C.c_void_p()
+        hsz = L.b200_ipc_handle_size()
+        handle = (C.c_char * hsz)()
+        _lib.check(L.b200_symm_alloc(nbytes, C.byref(ptr), handle), "symm_alloc")
+        handles = [bytes(handle)]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        peers = []
+        for j, h in enumerate(handles):
+            if j == rank:
+                peers.append(ptr.value)
+                continue
+            pp = C.c_void_p()
+            hb = (C.c_char * hsz).from_buffer_copy(h)
+            _lib.check(L.b200_symm_open(hb, C.byref(pp)), f"symm_open peer {j}")
+            peers.append(pp.value)
+    return ptr.value, peers
+
+
+def close_symmetric(rank: int, local_ptr, peer_ptrs):
+    L = _lib.lib()
+    for j, p in enumerate(peer_ptrs):
+        if j != rank and p:
+            L.b200_symm_close(p)
+    if local_ptr:
+        L.b200_symm_free(local_ptr)
+
+
 class SymmetricComm:
     """Symmetric buffer + signal pads for one tensor-parallel group."""
 
@@ -72,25 +107,8 @@ class SymmetricComm:
         self.h_off = _align(self.recv_off + recv)
         self.xarg_off = _align(self.h_off + hbuf)
         self.nbytes = _align(self.xarg_off + xarg)
-        with torch.cuda.device(self.device):
-            ptr = C.c_void_p()
-            hsz = L.b200_ipc_handle_size()
-            handle = (C.c_char * hsz)()
-            _lib.check(L.b200_symm_alloc(self.nbytes, C.byref(ptr), handle), "symm_alloc")
-            self.local_ptr = ptr.value
-            handles = [None] * world
-            dist.all_gather_object(handles, bytes(handle), group=group)
-            self.peer_ptrs = []
-            for j, h in enumerate(handles):
-                if j == rank:
-                    self.peer_ptrs.append(self.local_ptr)
-                    continue
-                pp = C.c_void_p()
-                hb = (C.c_char * hsz).from_buffer_copy(h)
-                _lib.check(L.b200_symm_open(hb, C.byref(pp)), f"symm_open peer {j}")
-                self.peer_ptrs.append(pp.value)
+        self.local_ptr, self.peer_ptrs = open_symmetric(group, rank, world, self.device, self.nbytes)
         self.step = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self.step_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.expect = torch.zeros(NUM_PADS * MAX_RANKS, dtype=torch.int32, device=self.device)
         self.ticket = torch.zeros(4, dtype=torch.int32, device=self.device)
         s = CommCtxStruct()
@@ -110,11 +128,13 @@ class SymmetricComm:
 
     # step / phase bookkeeping ------------------------------------------------
     def begin_step(self, step: int | None = None):
-        """Advance the device step counter (outside CUDA graphs) and restart phases."""
+        """Advance the device step counter (outside CUDA graphs) and restart
+        phases. The update is a stream-ordered device op, so a host running
+        ahead of the device cannot skip or repeat an epoch."""
         if step is None:
-            step = int(self.step_host[0]) + 1
-        self.step_host[0] = step
-        self.step.copy_(self.step_host, non_blocking=True)
+            self.step.add_(1)
+        else:
+            self.step.fill_(step)
         self.phase = 0
 
     def next_phase(self) -> int:
@@ -133,10 +153,5 @@ class SymmetricComm:
         return bool(st.item())
 
     def close(self):
-        L = _lib.lib()
-        for j, p in enumerate(self.peer_ptrs):
-            if j != self.rank and p:
-                L.b200_symm_close(p)
-        if self.local_ptr:
-            L.b200_symm_free(self.local_ptr)
+        close_symmetric(self.rank, self.local_ptr, self.peer_ptrs)
         self.peer_ptrs, self.local_ptr = [], None

@@ -75,3 +75,32 @@ def test_convert_quantizes(tmp_path):
     assert isinstance(mq.layers[1].wd, QuantizedWeight) and mq.layers[1].wd.bits == 8
     a, ref = _logits(mq, TOKS), _logits(m, TOKS)
     assert ((a - ref).norm() / ref.norm()).item() < 0.05
+
+
+def test_quantized_moe_experts_load_packed(tmp_path):
+    cfg_over = dict(model_type="qwen3_moe", num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
+                    norm_topk_prob=True)
+    m = _model(**cfg_over)
+    d = str(tmp_path / "moeq")
+    save_model(m, d, quantize={"bits": 4, "group_size": 64}, dtype=torch.bfloat16)
+    mq, _ = load_model(d, device="cpu", dtype=torch.float32)
+    L = mq.layers[0]
+    assert isinstance(L.experts_gu, QuantizedWeight) and L.experts_gu.num_experts == 8
+    assert isinstance(L.experts_d, QuantizedWeight) and L.experts_d.num_experts == 8
+    md, _ = load_model(d, device="cpu", dtype=torch.float32, keep_quantized=False)
+    a, b = _logits(mq, TOKS), _logits(md, TOKS)
+    assert ((a - b).norm() / b.norm()).item() < 2e-2
+
+
+def test_hf_mxfp4_blocks_pack_exactly():
+    from mlx_swift_lm_b200.loader.load import _mxfp4_blocks, _mxfp4_packed
+
+    g = torch.Generator().manual_seed(0)
+    E, N, G = 3, 64, 4
+    blocks = torch.randint(0, 256, (E, N, G, 16), generator=g, dtype=torch.int32).to(torch.uint8)
+    scales = torch.randint(118, 132, (E, N, G), generator=g, dtype=torch.int32).to(torch.uint8)
+    q = _mxfp4_packed(blocks, scales)
+    assert q.mode == "mxfp4" and q.num_experts == E and q.shape == (E * N, G * 32)
+    dense = _mxfp4_blocks(blocks, scales)  # [E, N, K]
+    for e in range(E):
+        assert torch.equal(q.expert(e).dequantize(), dense[e].to(torch.bfloat16).float())

@@ -159,3 +159,25 @@ def test_quantized_moe_model_graph_matches_eager():
                                                max_model_len=256, use_cuda_graphs=graphs, graph_buckets=(1, 2, 4)))
 
     assert eng(True).generate(ps, max_tokens=12) == eng(False).generate(ps, max_tokens=12)
+
+
+@pytest.mark.parametrize("T", [1, 64, 300])
+def test_moe_experts_mxfp4(T):
+    from mlx_swift_lm_b200.ops.qlinear import QuantizedWeight
+
+    torch.manual_seed(T + 77)
+    E, k, K, F = 16, 4, 512, 256
+    h = torch.randn(T, K, device=DEV, dtype=torch.bfloat16)
+    gu_f = [ref.interleave_gate_up(torch.randn(F, K) * 0.05, torch.randn(F, K) * 0.05) for _ in range(E)]
+    d_f = [torch.randn(K, F) * 0.05 for _ in range(E)]
+    gu = QuantizedWeight.stack_experts([QuantizedWeight.quantize_mxfp4(t) for t in gu_f]).to(DEV)
+    d = QuantizedWeight.stack_experts([QuantizedWeight.quantize_mxfp4(t) for t in d_f]).to(DEV)
+    gub = torch.randn(E, 2 * F, device=DEV, dtype=torch.bfloat16) * 0.1
+    db = torch.randn(E, K, device=DEV, dtype=torch.bfloat16) * 0.1
+    w, idx = moe.route_topk(torch.randn(T, E, device=DEV), k, "topk_softmax")
+    y = moe.moe_experts(h, gu, d, w, idx, "swiglu_oai", gub, db)
+    gud = torch.stack([gu.expert(e).dequantize() for e in range(E)])
+    dd = torch.stack([d.expert(e).dequantize() for e in range(E)])
+    r = _moe_ref(h.cpu(), gud.to(torch.bfloat16).cpu(), dd.to(torch.bfloat16).cpu(), w.cpu(), idx.cpu(), "swiglu_oai",
+                 gub.cpu(), db.cpu())
+    assert _rel(y.cpu(), r) < 2e-2

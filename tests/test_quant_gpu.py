@@ -60,3 +60,29 @@ def test_gemm_q_large_shape_and_batch_invariance():
     assert torch.equal(full[5:6], one)
     r = ref.gemm_ref(x[:8].cpu(), q.dequantize().to(torch.bfloat16).cpu())
     assert _rel(full[:8].cpu(), r) < 1e-2
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 300])
+def test_gemm_mxfp4(M):
+    torch.manual_seed(M)
+    N, K = 384, 1024
+    q = QuantizedWeight.quantize_mxfp4(torch.randn(N, K) * 0.05).to(DEV)
+    assert q.kernel_bits == -4
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    y = ops.gemm(x, q)
+    r = ref.gemm_ref(x.cpu(), q.dequantize().to(torch.bfloat16).cpu())
+    assert _rel(y.cpu(), r) < 1e-2
+
+
+def test_mxfp4_dequant_exact():
+    """One-hot activations read every weight back: the e2m1 table and the
+    power-of-two scales are exact."""
+    torch.manual_seed(3)
+    N, K = 256, 128
+    w = torch.randn(N, K) * torch.logspace(-3, 1, K)  # spread the block exponents
+    q = QuantizedWeight.quantize_mxfp4(w).to(DEV)
+    codes = q.codes_int()
+    assert set(codes.unique().tolist()) == set(range(16)) - {8}  # -0 is never produced
+    eye = torch.eye(K, device=DEV, dtype=torch.bfloat16)
+    y = ops.gemm(eye, q, epi="f32")  # [K, N] = W^T
+    assert torch.equal(y.t().cpu(), q.dequantize().cpu())
