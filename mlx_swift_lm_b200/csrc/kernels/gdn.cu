@@ -1,0 +1,284 @@
+// Gated DeltaNet (linear attention) layers of hybrid models (Qwen3-Next,
+// Qwen 3.5 / 3.6): causal depthwise conv + SiLU, q/k normalisation, decay and
+// write gates, the gated delta-rule recurrence over a per-sequence fp32 state,
+// and the gated RMSNorm of the output.
+//
+// Reference behaviour: MLXLMCommon/GatedDelta.swift:18-140 (decay gate
+// g = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b), and the
+// recurrence of `gated_delta_step`: S <- g S; u = (v - S k) beta; S <- S + u k^T;
+// y = S q) and MLXLLM/Models/Qwen3Next.swift:165-415 (conv1d of kernel 4 over
+// q|k|v with SiLU, q scaled by Dk^-1 and k by Dk^-1/2 after an unweighted
+// RMSNorm, RMSNormGated(y, z) = rmsnorm(y) * w * silu(z)).
+//
+// B200 layout: one flattened batch of rows (decode rows of one token, then
+// prefill chunks); `cu` [R+1] gives each row's tokens, `slot` [R] its state
+// slot and `fresh` [R] whether the row starts at position 0 (zero state).
+//   gdn_conv        one CTA per token: conv taps from the row's tokens or the
+//                   slot's conv state, SiLU into shared memory, per-head q/k
+//                   normalisation (a warp per head), gates; fp32 out.
+//   gdn_recurrence  one warp per (row, value head, value row): the Dk state
+//                   elements of that row live in registers (Dk / 32 per lane)
+//                   across the row's tokens; two warp reductions per token.
+//                   CTA (row, 0, 0) also rolls the conv state forward.
+//   gdn_norm_gate   one CTA per token: per-head RMSNorm * w * silu(z), bf16.
+// State: conv [S][3][C] bf16 (the last three pre-conv inputs), recurrent
+// [S][Hv][Dv][Dk] fp32.
+#include "b200_common.cuh"
+
+namespace b200 {
+namespace gdn {
+
+constexpr int kTaps = 4;
+
+__device__ __forceinline__ int find_row(const int* __restrict__ cu, int R, int t) {
+  int lo = 0, hi = R - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
+
+// P [T][ldp] bf16: q | k | v (C = 2 Hk Dk + Hv Dv channels) | z (Hv Dv) | b (Hv) | a (Hv)
+__global__ void __launch_bounds__(256) conv_kernel(const __nv_bfloat16* __restrict__ P, int ldp, int T,
+                                                   const int* __restrict__ cu, int R, const int* __restrict__ fresh,
+                                                   const int* __restrict__ slot,
+                                                   const __nv_bfloat16* __restrict__ conv_state,
+                                                   const float* __restrict__ conv_w, int C, int Hk, int Dk, int Hv,
+                                                   int Dv, const float* __restrict__ A_log,
+                                                   const float* __restrict__ dt_bias, float eps,
+                                                   float* __restrict__ qkv_out, float* __restrict__ gb_out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  extern __shared__ float y[];  // [C]
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const int r = find_row(cu, R, t);
+  const int s0 = cu[r], i = t - s0;
+  const bool fr = fresh[r] != 0;
+  const __nv_bfloat16* cs = conv_state + (size_t)slot[r] * (kTaps - 1) * C;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < kTaps; ++j) {
+      const int m = i - (kTaps - 1) + j;
+      float x;
+      if (m >= 0) x = bf2f(P[(size_t)(s0 + m) * ldp + c]);
+      else x = fr ? 0.f : bf2f(cs[(size_t)(kTaps - 1 + m) * C + c]);
+      acc = fmaf(conv_w[c * kTaps + j], x, acc);
+    }
+    y[c] = acc / (1.f + __expf(-acc));
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float* out = qkv_out + (size_t)t * C;
+  for (int hh = warp; hh < 2 * Hk; hh += nw) {
+    const float* src = y + hh * Dk;
+    float ss = 0.f;
+    for (int d = lane; d < Dk; d += 32) ss = fmaf(src[d], src[d], ss);
+    ss = warp_sum(ss);
+    const float sc = hh < Hk ? 1.f / (float)Dk : rsqrtf((float)Dk);
+    const float inv = rsqrtf(ss / (float)Dk + eps) * sc;
+    for (int d = lane; d < Dk; d += 32) out[hh * Dk + d] = src[d] * inv;
+  }
+  for (int c = 2 * Hk * Dk + threadIdx.x; c < C; c += blockDim.x) out[c] = y[c];
+  const __nv_bfloat16* pb = P + (size_t)t * ldp + C + Hv * Dv;
+  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
+    const float b = bf2f(pb[h]), a = bf2f(pb[Hv + h]);
+    gb_out[(size_t)t * 2 * Hv + h] = __expf(-__expf(A_log[h]) * softplus(a + dt_bias[h]));
+    gb_out[(size_t)t * 2 * Hv + Hv + h] = 1.f / (1.f + __expf(-b));
+  }
+}
+
+// grid (R, Hv, Dv / 4), 128 threads: warp w owns value row blockIdx.z * 4 + w.
+template <int NK>
+__global__ void __launch_bounds__(128) recurrence_kernel(const float* __restrict__ qkv, const float* __restrict__ gb,
+                                                         const int* __restrict__ cu, const int* __restrict__ fresh,
+                                                         const int* __restrict__ slot, float* __restrict__ state,
+                                                         int Hk, int Hv, int Dv, float* __restrict__ o,
+                                                         const __nv_bfloat16* __restrict__ P, int ldp,
+                                                         __nv_bfloat16* __restrict__ conv_state, int C) {
+  pdl_launch_dependents();
+  pdl_wait();
+  constexpr int Dk = NK * 32;
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dv = blockIdx.z * 4 + warp;
+  const int hk = h / (Hv / Hk);
+  const int s0 = cu[r], n = cu[r + 1] - s0;
+  const bool fr = fresh[r] != 0;
+  const int sl = slot[r];
+  if (dv < Dv) {
+    float* st = state + (((size_t)sl * Hv + h) * Dv + dv) * Dk + lane * NK;
+    float s[NK];
+#pragma unroll
+    for (int i = 0; i < NK; ++i) s[i] = fr ? 0.f : st[i];
+    const int C2 = 2 * Hk * Dk;
+    for (int tt = 0; tt < n; ++tt) {
+      const size_t t = (size_t)(s0 + tt);
+      const float* q = qkv + t * C + hk * Dk + lane * NK;
+      const float* k = qkv + t * C + Hk * Dk + hk * Dk + lane * NK;
+      const float v = qkv[t * C + C2 + h * Dv + dv];
+      const float g = gb[t * 2 * Hv + h], beta = gb[t * 2 * Hv + Hv + h];
+      float kk[NK], qq[NK];
+#pragma unroll
+      for (int i = 0; i < NK; ++i) {
+        kk[i] = k[i];
+        qq[i] = q[i];
+      }
+      float kv = 0.f;
+#pragma unroll
+      for (int i = 0; i < NK; ++i) {
+        s[i] *= g;
+        kv = fmaf(s[i], kk[i], kv);
+      }
+      kv = warp_sum(kv);
+      const float delta = (v - kv) * beta;
+      float out = 0.f;
+#pragma unroll
+      for (int i = 0; i < NK; ++i) {
+        s[i] = fmaf(kk[i], delta, s[i]);
+        out = fmaf(s[i], qq[i], out);
+      }
+      out = warp_sum(out);
+      if (lane == 0) o[t * Hv * Dv + h * Dv + dv] = out;
+    }
+#pragma unroll
+    for (int i = 0; i < NK; ++i) st[i] = s[i];
+  }
+  // roll the conv state to the row's last three inputs (the conv kernel that
+  // read the old state has completed: this grid waited for it)
+  if (h == 0 && blockIdx.z == 0) {
+    __nv_bfloat16* cs = conv_state + (size_t)sl * (kTaps - 1) * C;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+#pragma unroll
+      for (int j = 0; j < kTaps - 1; ++j) {
+        const int m = n - (kTaps - 1) + j;  // index of the input that becomes tap j
+        __nv_bfloat16 x;
+        if (m >= 0) x = P[(size_t)(s0 + m) * ldp + c];
+        else x = fr ? f2bf(0.f) : cs[(size_t)(kTaps - 1 + m) * C + c];  // reads ahead of the writes
+        cs[(size_t)j * C + c] = x;
+      }
+    }
+  }
+}
+
+// one CTA per token; warp per value head: rmsnorm(o) * w * silu(z) -> bf16
+__global__ void __launch_bounds__(256) norm_gate_kernel(const float* __restrict__ o, int T, int Hv, int Dv,
+                                                        const __nv_bfloat16* __restrict__ z, int ldz,
+                                                        const __nv_bfloat16* __restrict__ w, float eps,
+                                                        __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int h = warp; h < Hv; h += nw) {
+    const float* src = o + ((size_t)t * Hv + h) * Dv;
+    float ss = 0.f;
+    for (int d = lane; d < Dv; d += 32) ss = fmaf(src[d], src[d], ss);
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)Dv + eps);
+    for (int d = lane; d < Dv; d += 32) {
+      const float zz = bf2f(z[(size_t)t * ldz + h * Dv + d]);
+      const float g = zz / (1.f + __expf(-zz));
+      out[(size_t)t * ldo + h * Dv + d] = f2bf(src[d] * inv * bf2f(w[d]) * g);
+    }
+  }
+}
+
+// out = x * sigmoid(g) (gated attention output), bf16 [T][N]
+__global__ void sigmoid_mul_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ g,
+                                   int ldg, int T, int N, __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t total = (size_t)T * N;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(e / N), c = (int)(e % N);
+    const float gv = bf2f(g[(size_t)t * ldg + c]);
+    out[(size_t)t * ldo + c] = f2bf(bf2f(x[(size_t)t * ldx + c]) / (1.f + __expf(-gv)));
+  }
+}
+
+}  // namespace gdn
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+int b200_gdn_conv(const void* P, int ldp, int T, const int* cu, int R, const int* fresh, const int* slot,
+                  const void* conv_state, const float* conv_w, int C, int Hk, int Dk, int Hv, int Dv,
+                  const float* A_log, const float* dt_bias, float eps, float* qkv_out, float* gb_out,
+                  cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (R <= 0 || C != 2 * Hk * Dk + Hv * Dv || (size_t)C * 4 > 200 * 1024 || ldp < C + Hv * Dv + 2 * Hv) return -1;
+  const size_t smem = (size_t)C * sizeof(float);
+  static bool cfg = false;
+  if (!cfg) {
+    cudaError_t e = cudaFuncSetAttribute(gdn::conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return (int)e;
+    cfg = true;
+  }
+  cudaError_t e = launch_k(gdn::conv_kernel, dim3(T), dim3(256), smem, st, 1,
+                           reinterpret_cast<const __nv_bfloat16*>(P), ldp, T, cu, R, fresh, slot,
+                           reinterpret_cast<const __nv_bfloat16*>(conv_state), conv_w, C, Hk, Dk, Hv, Dv, A_log,
+                           dt_bias, eps, qkv_out, gb_out);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+int b200_gdn_recurrence(const float* qkv, const float* gb, const int* cu, int R, const int* fresh, const int* slot,
+                        float* state, int Hk, int Dk, int Hv, int Dv, float* o, const void* P, int ldp,
+                        void* conv_state, int C, cudaStream_t st) {
+  if (R <= 0) return 0;
+  if ((Hv % Hk) || (Dv % 4) || C != 2 * Hk * Dk + Hv * Dv) return -1;
+  const dim3 grid(R, Hv, Dv / 4);
+  const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(P);
+  __nv_bfloat16* cs = reinterpret_cast<__nv_bfloat16*>(conv_state);
+  cudaError_t e;
+  switch (Dk) {
+    case 64:
+      e = launch_k(gdn::recurrence_kernel<2>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv, Dv,
+                   o, p, ldp, cs, C);
+      break;
+    case 128:
+      e = launch_k(gdn::recurrence_kernel<4>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv, Dv,
+                   o, p, ldp, cs, C);
+      break;
+    case 256:
+      e = launch_k(gdn::recurrence_kernel<8>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv, Dv,
+                   o, p, ldp, cs, C);
+      break;
+    default:
+      return -1;
+  }
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+int b200_gdn_norm_gate(const float* o, int T, int Hv, int Dv, const void* z, int ldz, const void* w, float eps,
+                       void* out, int ldo, cudaStream_t st) {
+  if (T <= 0) return 0;
+  cudaError_t e = launch_k(gdn::norm_gate_kernel, dim3(T), dim3(256), 0, st, 1, o, T, Hv, Dv,
+                           reinterpret_cast<const __nv_bfloat16*>(z), ldz, reinterpret_cast<const __nv_bfloat16*>(w),
+                           eps, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+int b200_sigmoid_mul(const void* x, int ldx, const void* g, int ldg, int T, int N, void* out, int ldo,
+                     cudaStream_t st) {
+  if (T <= 0 || N <= 0) return 0;
+  const size_t total = (size_t)T * N;
+  const size_t blocks = (total + 255) / 256;
+  const int grid = (int)(blocks < 148 * 8 ? blocks : 148 * 8);
+  cudaError_t e = launch_k(gdn::sigmoid_mul_kernel, dim3(grid), dim3(256), 0, st, 1,
+                           reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<const __nv_bfloat16*>(g),
+                           ldg, T, N, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+}  // extern "C"
+
+B200_STATUS_ACCESSORS(gdn)

@@ -130,12 +130,16 @@ class EngineV2:
         self.device = model.device
         sc = self.cfg.scheduler
         kv_tokens = self.cfg.kv_tokens or sc.max_concurrent_requests * self.cfg.max_model_len
+        # recurrent-state slots (hybrid models): every running request holds one
+        seqs = sc.max_concurrent_requests
         if self.cfg.kv_bytes is not None:
-            self.kv = PagedKVCache.for_model(model, kv_bytes=self.cfg.kv_bytes, kv_fp8=self.cfg.kv_fp8)
+            self.kv = PagedKVCache.for_model(model, kv_bytes=self.cfg.kv_bytes, kv_fp8=self.cfg.kv_fp8, max_seqs=seqs)
         else:
-            self.kv = PagedKVCache.for_model(model, max_tokens=kv_tokens, kv_fp8=self.cfg.kv_fp8)
+            self.kv = PagedKVCache.for_model(model, max_tokens=kv_tokens, kv_fp8=self.cfg.kv_fp8, max_seqs=seqs)
         self.prefix_cache = None
-        if self.cfg.enable_prefix_cache:
+        # a recurrent state cannot be rebuilt from shared KV pages: no prefix
+        # reuse for hybrid models (their prompts are always computed in full)
+        if self.cfg.enable_prefix_cache and self.kv.rec is None:
             from ..kv.prefix_cache import PrefixCache
 
             self.prefix_cache = PrefixCache(self.kv, self.cfg.prefix_block_size)
@@ -171,6 +175,9 @@ class EngineV2:
     def enable_mtp(self, module, config=None):
         """Speculative decoding with an MTP draft module (greedy rows)."""
         from .mtp import MTPDriver
+
+        if self.kv.rec is not None:
+            raise ValueError("MTP rollback needs per-position recurrent states; hybrid models decode without MTP")
 
         self.mtp = MTPDriver(self, module, config)
         return self.mtp
@@ -255,9 +262,11 @@ class EngineV2:
             fb.logit_idx = torch.tensor(logit_idx, dtype=torch.int64)
             fb.logit_idx_host = logit_idx
         fb.row_ranks = self._row_ranks(rows)
+        if self.kv.rec is not None:
+            fb.state_slots = torch.tensor([r.state.seq.state_slot for r in rows], dtype=torch.int32)
         if dev.type == "cuda":
             for name in ("input_ids", "positions", "slots", "dec_page_table", "dec_seq_lens", "pf_cu_q", "pf_pos0",
-                         "pf_page_table", "logit_idx"):
+                         "pf_page_table", "logit_idx", "state_slots"):
                 t = getattr(fb, name)
                 if t is not None:
                     self.h2d_bytes += t.numel() * t.element_size()

@@ -42,11 +42,13 @@ class DecodeGraphRunner:
         self.maxp = engine.max_pages
         self.max_parts = decode_max_parts(engine.cfg.max_model_len)
         B, P = self.Bmax, self.maxp
-        # packed int32 layout: pos | seq_lens | src | host_ids | page_table | slots(int64)
+        # packed int32 layout: pos | seq_lens | src | host_ids | page_table | slots(int64) | state slots
         self.o_pos, self.o_sl, self.o_src, self.o_hid, self.o_pt = 0, B, 2 * B, 3 * B, 4 * B
         self.o_slots = 4 * B + B * P
         self.o_slots += self.o_slots % 2
-        self.n_i32 = self.o_slots + 2 * B
+        self.o_ss = self.o_slots + 2 * B
+        self.n_i32 = self.o_ss + B
+        self.rec = engine.kv.rec
         self.packed = torch.zeros(self.n_i32, dtype=torch.int32, device=self.dev)
         self.staging = [torch.zeros(self.n_i32, dtype=torch.int32).pin_memory() for _ in range(2)]
         self.staging_ev = [None, None]
@@ -57,6 +59,7 @@ class DecodeGraphRunner:
         self.hid = self.packed[self.o_hid:self.o_hid + B]
         self.pt = self.packed[self.o_pt:self.o_pt + B * P].view(B, P)
         self.slots = self.packed[self.o_slots:self.o_slots + 2 * B].view(torch.int64)
+        self.ss = self.packed[self.o_ss:self.o_ss + B]
         self.ids = torch.zeros(B, dtype=torch.int32, device=self.dev)
         self.out = torch.zeros(B, dtype=torch.int32, device=self.dev)
         self.host_out = [torch.zeros(B, dtype=torch.int32).pin_memory() for _ in range(4)]
@@ -80,14 +83,17 @@ class DecodeGraphRunner:
 
     def _fb(self, B):
         return ForwardBatch(input_ids=self.ids[:B], positions=self.pos[:B], slots=self.slots[:B], num_decode=B,
-                            dec_page_table=self.pt[:B], dec_seq_lens=self.sl[:B], dec_max_parts=self.max_parts)
+                            dec_page_table=self.pt[:B], dec_seq_lens=self.sl[:B], dec_max_parts=self.max_parts,
+                            state_slots=self.ss[:B] if self.rec is not None else None)
 
     def _body(self, B):
         self.model.forward_decode_tokens(self._fb(B), self.eng.kv, self.out[:B])
 
     def capture(self, B):
         self._reserve()
-        # inert inputs for warm-up: no KV writes, empty contexts
+        # inert inputs for warm-up: no KV writes, empty contexts, scratch recurrent state
+        if self.rec is not None:
+            self.ss.fill_(self.rec.scratch)
         self.slots.fill_(-1)
         self.sl.zero_()
         self.pos.zero_()
@@ -179,6 +185,8 @@ class DecodeGraphRunner:
         a[self.o_hid:self.o_hid + Bb] = 0
         slots = a[self.o_slots:self.o_slots + 2 * self.Bmax].view(np.int64)
         slots[:Bb] = -1
+        if self.rec is not None:
+            a[self.o_ss:self.o_ss + Bb] = self.rec.scratch
         pt = a[self.o_pt:self.o_pt + self.Bmax * P].reshape(self.Bmax, P)
         prev_idx = {}
         if chained_from is not None:
@@ -192,6 +200,8 @@ class DecodeGraphRunner:
             a[self.o_pos + i] = p
             a[self.o_sl + i] = p + 1
             slots[i] = st.seq.slot(p)
+            if self.rec is not None:
+                a[self.o_ss + i] = st.seq.state_slot
             pg = st.seq.pages
             pt[i, :len(pg)] = pg
             tok = st.all_tokens[p]
@@ -199,7 +209,7 @@ class DecodeGraphRunner:
                 a[self.o_src + i] = prev_idx[id(st)]
             else:
                 a[self.o_hid + i] = tok
-        nbytes = (self.o_slots + 2 * self.Bmax) * 4
+        nbytes = self.n_i32 * 4
         self.packed.copy_(stg, non_blocking=True)
         self.h2d_bytes += nbytes
         e = torch.cuda.Event()

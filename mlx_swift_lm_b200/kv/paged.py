@@ -9,6 +9,12 @@
   rollback :412, commitSpeculativeWrite :348).
 
 Page accounting runs in the native host pool (``_b200host.PagePool``).
+
+Hybrid models (linear-attention layers) also get a :class:`RecurrentStatePool`
+(``cache.rec``): one fixed-size conv + delta-rule state per running sequence
+instead of pages (the reference's recurrent-state rows,
+ContinuousBatchingV2/RecurrentStateV2.swift:13), owned by the sequence's
+:class:`SequenceKV` as ``state_slot``.
 """
 from __future__ import annotations
 
@@ -23,6 +29,39 @@ _LIBDIR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__)
 if _LIBDIR not in sys.path:
     sys.path.insert(0, _LIBDIR)
 import _b200host  # noqa: E402  (native host runtime)
+
+
+class RecurrentStatePool:
+    """Per-sequence state of the linear-attention layers: conv inputs
+    [layers, slots, taps-1, C] (model dtype) and the delta-rule state
+    [layers, slots, Hv, Dv, Dk] (fp32). The last slot is scratch for padding
+    rows of captured decode graphs."""
+
+    def __init__(self, num_layers: int, max_seqs: int, conv_dim: int, Hv: int, Dv: int, Dk: int, taps: int = 4,
+                 dtype=torch.bfloat16, device="cpu"):
+        self.num_layers, self.max_seqs = num_layers, max_seqs
+        self.conv = torch.zeros(num_layers, max_seqs + 1, taps - 1, conv_dim, dtype=dtype, device=device)
+        self.ssm = torch.zeros(num_layers, max_seqs + 1, Hv, Dv, Dk, dtype=torch.float32, device=device)
+        self._free = list(range(max_seqs - 1, -1, -1))
+        self.scratch = max_seqs
+
+    @property
+    def num_free(self) -> int:
+        return len(self._free)
+
+    def alloc(self) -> int | None:
+        return self._free.pop() if self._free else None
+
+    def release(self, slot: int):
+        if 0 <= slot < self.max_seqs:
+            self._free.append(slot)
+
+    def layer(self, i: int):
+        return self.conv[i], self.ssm[i]
+
+    @property
+    def bytes_per_seq(self) -> int:
+        return (self.conv[:, 0].numel() * self.conv.element_size() + self.ssm[:, 0].numel() * 4)
 
 
 class PagedKVCache:
@@ -46,6 +85,7 @@ class PagedKVCache:
             self.k_scales = self.v_scales = None
         self.pool = _b200host.PagePool(num_pages)
         self.page_bytes = 2 * num_layers * num_kv_heads * PAGE * head_dim * self.k.element_size()
+        self.rec: RecurrentStatePool | None = None
 
     def layer(self, li: int):
         return self.k[li], self.v[li]
@@ -70,17 +110,25 @@ class PagedKVCache:
 
     @classmethod
     def for_model(cls, model, max_tokens: int | None = None, kv_bytes: int | None = None, kv_fp8=False,
-                  device=None):
-        """Size the pool by a token budget or a byte budget."""
+                  device=None, max_seqs: int = 64):
+        """Size the pool by a token budget or a byte budget. Only attention
+        layers hold pages; linear-attention layers get `max_seqs` state slots."""
         dev = device or model.device
         dt = model.dtype
         es = 1 if kv_fp8 else torch.empty((), dtype=dt).element_size()
-        per_page = 2 * model.cfg.num_layers * model.KVH * PAGE * model.D * es
+        n_attn = getattr(model, "num_kv_layers", model.cfg.num_layers)
+        per_page = 2 * max(n_attn, 1) * model.KVH * PAGE * model.D * es
         if kv_bytes is not None:
             n = max(1, kv_bytes // per_page)
         else:
             n = cls.pages_for(max_tokens or 4096) + 1
-        return cls(model.cfg.num_layers, n, model.KVH, model.D, dt, dev, kv_fp8)
+        c = cls(max(n_attn, 1), n, model.KVH, model.D, dt, dev, kv_fp8)
+        n_lin = model.cfg.num_layers - n_attn
+        if n_lin > 0:
+            Hk, Dk, Hv, Dv = model.cfg.gdn_dims
+            c.rec = RecurrentStatePool(n_lin, max_seqs, model.cfg.gdn_conv_dim, Hv, Dv, Dk,
+                                       model.cfg.linear_conv_kernel_dim, dt, dev)
+        return c
 
 
 class SequenceKV:
@@ -91,6 +139,7 @@ class SequenceKV:
         self.pages: list[int] = []
         self.num_tokens = 0
         self.shared_prefix_pages = 0  # leading pages borrowed from the prefix cache
+        self.state_slot = -1  # recurrent-state slot (hybrid models)
 
     def capacity(self) -> int:
         return len(self.pages) * PAGE
@@ -100,10 +149,20 @@ class SequenceKV:
 
     def ensure(self, total_tokens: int) -> bool:
         """Grow to hold `total_tokens`; False if the pool cannot supply pages."""
+        rec = self.cache.rec
+        new_slot = False
+        if rec is not None and self.state_slot < 0:
+            slot = rec.alloc()
+            if slot is None:
+                return False
+            self.state_slot, new_slot = slot, True
         need = self.pages_needed(total_tokens)
         if need == 0:
             return True
         if not self.cache.pool.can_alloc(need):
+            if new_slot:  # hold no state slot while waiting for pages
+                rec.release(self.state_slot)
+                self.state_slot = -1
             return False
         self.pages.extend(self.cache.pool.alloc(need))
         return True
@@ -139,3 +198,6 @@ class SequenceKV:
         self.pages = []
         self.num_tokens = 0
         self.shared_prefix_pages = 0
+        if self.state_slot >= 0 and self.cache.rec is not None:
+            self.cache.rec.release(self.state_slot)
+        self.state_slot = -1

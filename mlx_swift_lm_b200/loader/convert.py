@@ -51,6 +51,13 @@ def to_hf_config(cfg, quantization: dict | None = None) -> dict:
                  moe_intermediate_size=cfg.moe_intermediate_size, norm_topk_prob=cfg.norm_topk_prob)
         if cfg.moe_layers is not None:
             d["mlp_only_layers"] = [i for i, x in enumerate(cfg.moe_layers) if not x]
+        if cfg.shared_expert_intermediate_size:
+            d["shared_expert_intermediate_size"] = cfg.shared_expert_intermediate_size
+    if cfg.layer_types:
+        d.update(layer_types=list(cfg.layer_types), attn_output_gate=cfg.attn_output_gate,
+                 linear_num_key_heads=cfg.linear_num_key_heads, linear_num_value_heads=cfg.linear_num_value_heads,
+                 linear_key_head_dim=cfg.linear_key_head_dim, linear_value_head_dim=cfg.linear_value_head_dim,
+                 linear_conv_kernel_dim=cfg.linear_conv_kernel_dim)
     if quantization:
         d["quantization"] = dict(quantization)
     return d
@@ -60,6 +67,27 @@ def _dense(t) -> torch.Tensor:
     if isinstance(t, QuantizedWeight):
         return t.dequantize(torch.float32)
     return t.detach().float().cpu()
+
+
+def _export_linear_attn(out: dict, la: str, L, cfg):
+    """Gated DeltaNet weights under Qwen3-Next names (in_proj_qkvz / in_proj_ba
+    packed per key head) with conv taps as [C, K, 1] (the MLX layout, whose
+    layer norms already hold 1 + w)."""
+    Hk, Dk, Hv, Dv = cfg.gdn_dims
+    vpk = Hv // Hk
+    w = _dense(L.wqkv)
+    kd, vd = Hk * Dk, Hv * Dv
+    q, k, v, z = w[:kd], w[kd:2 * kd], w[2 * kd:2 * kd + vd], w[2 * kd + vd:2 * kd + 2 * vd]
+    b, a = w[2 * kd + 2 * vd:2 * kd + 2 * vd + Hv], w[2 * kd + 2 * vd + Hv:]
+    H = w.shape[1]
+    qkvz = torch.cat([q.view(Hk, Dk, H), k.view(Hk, Dk, H), v.view(Hk, vpk * Dv, H), z.view(Hk, vpk * Dv, H)], 1)
+    out[la + "in_proj_qkvz.weight"] = qkvz.reshape(-1, H)
+    out[la + "in_proj_ba.weight"] = torch.cat([b.view(Hk, vpk, H), a.view(Hk, vpk, H)], 1).reshape(-1, H)
+    out[la + "conv1d.weight"] = _dense(L.conv_w)[:, :, None]
+    out[la + "A_log"] = _dense(L.A_log)
+    out[la + "dt_bias"] = _dense(L.dt_bias)
+    out[la + "norm.weight"] = _dense(L.gdn_norm)
+    out[la + "out_proj.weight"] = _dense(L.wo)
 
 
 def export_tensors(model) -> dict[str, torch.Tensor]:
@@ -84,15 +112,26 @@ def export_tensors(model) -> dict[str, torch.Tensor]:
             out[p + "post_attention_layernorm.weight"] = _dense(L.ln2) - off
         a = p + "self_attn."
         w = _dense(L.wqkv)
-        out[a + "q_proj.weight"], out[a + "k_proj.weight"], out[a + "v_proj.weight"] = (
-            w[:qn], w[qn:qn + kn], w[qn + kn:])
-        if L.bqkv is not None:
+        if L.linear:
+            _export_linear_attn(out, p + "linear_attn.", L, cfg)
+        elif cfg.attn_output_gate:  # q_proj rows per head [q | gate]
+            H, D = model.H, model.D
+            q, gt = w[:qn].view(H, D, -1), w[qn + 2 * kn:].view(H, D, -1)
+            out[a + "q_proj.weight"] = torch.cat([q, gt], 1).reshape(2 * qn, -1)
+            out[a + "k_proj.weight"], out[a + "v_proj.weight"] = w[qn:qn + kn], w[qn + kn:qn + 2 * kn]
+        else:
+            out[a + "q_proj.weight"], out[a + "k_proj.weight"], out[a + "v_proj.weight"] = (
+                w[:qn], w[qn:qn + kn], w[qn + kn:])
+        if L.linear:
+            pass
+        elif L.bqkv is not None:
             b = _dense(L.bqkv)
             out[a + "q_proj.bias"], out[a + "k_proj.bias"], out[a + "v_proj.bias"] = b[:qn], b[qn:qn + kn], b[qn + kn:]
         if L.q_norm is not None:
             out[a + "q_norm.weight"] = _dense(L.q_norm) - off
             out[a + "k_norm.weight"] = _dense(L.k_norm) - off
-        out[a + "o_proj.weight"] = _dense(L.wo)
+        if not L.linear:
+            out[a + "o_proj.weight"] = _dense(L.wo)
         if L.bo is not None:
             out[a + "o_proj.bias"] = _dense(L.bo)
         if L.sinks is not None:

@@ -104,6 +104,75 @@ class CheckpointView:
         return self.raw(name).to(self.dtype)
 
 
+def _rows(w, idx: torch.Tensor):
+    return w.select_rows(idx) if isinstance(w, QuantizedWeight) else w.index_select(0, idx)
+
+
+def _load_attention(ck: CheckpointView, cfg, L, a, norm, r, w):
+    """q|k|v (and, for gated attention, the output gate after v), biases,
+    q/k norms, o_proj and sinks of one attention layer."""
+    if cfg.attn_output_gate:
+        # q_proj rows per head: [q (D) | gate (D)] -> q | k | v | gate
+        assert w == 1, "gated attention loads without tensor parallelism"
+        qg = ck.linear(a + "q_proj")
+        D, H = cfg.head_dim, cfg.num_heads
+        qi = torch.tensor([h * 2 * D + d for h in range(H) for d in range(D)])
+        L.wqkv = _cat_rows([_rows(qg, qi), ck.linear(a + "k_proj"), ck.linear(a + "v_proj"), _rows(qg, qi + D)])
+    else:
+        if cfg.extra.get("fused_qkv"):
+            qkv = ck.linear(a + "qkv_proj", packed=False)
+            qw, kw, vw = torch.split(qkv, [cfg.q_size, cfg.kv_size, cfg.kv_size], 0)
+        else:
+            qw, kw, vw = ck.linear(a + "q_proj"), ck.linear(a + "k_proj"), ck.linear(a + "v_proj")
+        L.wqkv = _cat_rows([_shard_rows(qw, r, w), _kv_rows(kw, cfg, r, w), _kv_rows(vw, cfg, r, w)])
+    if cfg.attention_bias:
+        qb, kb, vb = ck.vec(a + "q_proj.bias"), ck.vec(a + "k_proj.bias"), ck.vec(a + "v_proj.bias")
+        if qb is not None:
+            L.bqkv = torch.cat([_shard_rows(qb, r, w), _kv_rows(kb, cfg, r, w), _kv_rows(vb, cfg, r, w)], 0)
+    if cfg.qk_norm:
+        L.q_norm = norm(a + "q_norm.weight")
+        L.k_norm = norm(a + "k_norm.weight")
+    L.wo = _shard_cols(ck.linear(a + "o_proj"), r, w)
+    if cfg.o_bias:
+        L.bo = ck.vec(a + "o_proj.bias")
+    if cfg.attention_sinks:
+        s = ck.vec(a + "sinks")
+        L.sinks = _shard_rows(s.float(), r, w) if s is not None else torch.zeros(cfg.num_heads // w)
+
+
+def _load_linear_attn(ck: CheckpointView, cfg, L, p):
+    """Gated DeltaNet weights as the fused in-projection q | k | v | z | b | a.
+    Qwen3-Next packs in_proj_qkvz / in_proj_ba per key head ([q, k, v..., z...]
+    and [b..., a...] per head, MLXLLM/Models/Qwen3Next.swift:225-260); Qwen 3.5
+    has separate in_proj_qkv / z / b / a (Qwen35.swift:255)."""
+    la = p + "linear_attn."
+    Hk, Dk, Hv, Dv = cfg.gdn_dims
+    vpk = Hv // Hk
+    if ck.has(la + "in_proj_qkvz.weight"):
+        W = ck.linear(la + "in_proj_qkvz")
+        blk = 2 * Dk + 2 * vpk * Dv
+
+        def sec(off, n):
+            return torch.tensor([h * blk + off + j for h in range(Hk) for j in range(n)])
+
+        BA = ck.linear(la + "in_proj_ba")
+        bi = torch.tensor([h * 2 * vpk + j for h in range(Hk) for j in range(vpk)])
+        parts = [_rows(W, sec(0, Dk)), _rows(W, sec(Dk, Dk)), _rows(W, sec(2 * Dk, vpk * Dv)),
+                 _rows(W, sec(2 * Dk + vpk * Dv, vpk * Dv)), _rows(BA, bi), _rows(BA, bi + vpk)]
+    else:
+        parts = [ck.linear(la + "in_proj_qkv"), ck.linear(la + "in_proj_z"), ck.linear(la + "in_proj_b"),
+                 ck.linear(la + "in_proj_a")]
+    if len({type(t) for t in parts}) > 1 or any(isinstance(t, QuantizedWeight) and t.shape[0] % 8 for t in parts):
+        parts = [t.dequantize(torch.float32) if isinstance(t, QuantizedWeight) else t for t in parts]
+    L.wqkv = _cat_rows(parts)
+    cw = ck.raw(la + "conv1d.weight").float()
+    L.conv_w = (cw[:, 0, :] if cw.shape[-1] != 1 else cw[:, :, 0]).contiguous()
+    L.A_log = ck.raw(la + "A_log").float()
+    L.dt_bias = ck.raw(la + "dt_bias").float()
+    L.gdn_norm = ck.vec(la + "norm.weight", required=True).float()
+    L.wo = ck.linear(la + "out_proj")
+
+
 def _packed(w, s, b, mode, bits, gs):
     """A packed QuantizedWeight for MLX affine 4/8-bit or MXFP4 weights the
     kernels serve (stacked experts [E, N, ...] keep num_experts), else None."""
@@ -186,6 +255,14 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
     r, w = tp.rank, tp.world
     q = cfg.quantization if isinstance(cfg.quantization, dict) else None
     ck = CheckpointView(tensors, q, torch.float32, keep_quantized=keep_quantized and bool(q))
+    if cfg.layer_types and any(cfg.is_linear(i) for i in range(cfg.num_layers)):
+        assert tp.world == 1, "hybrid (linear-attention) models load without tensor parallelism"
+        # HF-format Qwen3-Next / 3.5 checkpoints store zero-centred layer norms
+        # and conv taps as [C, 1, K]; MLX-converted ones already hold 1 + w
+        # and [C, K, 1] (the rule of MLXLLM/Models/Qwen3Next.swift:807-855)
+        li = next(i for i in range(cfg.num_layers) if cfg.is_linear(i))
+        if ck.raw(f"layers.{li}.linear_attn.conv1d.weight").shape[-1] != 1:
+            cfg.norm_offset_one = True
     m = DecoderLM(cfg, "cpu", torch.float32, tp=tp)
     off = 1.0 if cfg.norm_offset_one else 0.0
 
@@ -217,26 +294,11 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
             L.post_ffn_norm = norm(p + "post_feedforward_layernorm.weight")
         else:
             L.ln2 = norm(p + "post_attention_layernorm.weight")
-        a = p + "self_attn."
-        if cfg.extra.get("fused_qkv"):
-            qkv = ck.linear(a + "qkv_proj", packed=False)
-            qw, kw, vw = torch.split(qkv, [cfg.q_size, cfg.kv_size, cfg.kv_size], 0)
+        L.linear = cfg.is_linear(i)
+        if L.linear:
+            _load_linear_attn(ck, cfg, L, p)
         else:
-            qw, kw, vw = ck.linear(a + "q_proj"), ck.linear(a + "k_proj"), ck.linear(a + "v_proj")
-        L.wqkv = _cat_rows([_shard_rows(qw, r, w), _kv_rows(kw, cfg, r, w), _kv_rows(vw, cfg, r, w)])
-        if cfg.attention_bias:
-            qb, kb, vb = ck.vec(a + "q_proj.bias"), ck.vec(a + "k_proj.bias"), ck.vec(a + "v_proj.bias")
-            if qb is not None:
-                L.bqkv = torch.cat([_shard_rows(qb, r, w), _kv_rows(kb, cfg, r, w), _kv_rows(vb, cfg, r, w)], 0)
-        if cfg.qk_norm:
-            L.q_norm = norm(a + "q_norm.weight")
-            L.k_norm = norm(a + "k_norm.weight")
-        L.wo = _shard_cols(ck.linear(a + "o_proj"), r, w)
-        if cfg.o_bias:
-            L.bo = ck.vec(a + "o_proj.bias")
-        if cfg.attention_sinks:
-            s = ck.vec(a + "sinks")
-            L.sinks = _shard_rows(s.float(), r, w) if s is not None else torch.zeros(cfg.num_heads // w)
+            _load_attention(ck, cfg, L, p + "self_attn.", norm, r, w)
         if cfg.is_moe(i):
             _load_moe(ck, cfg, L, p, r, w)
         else:

@@ -35,6 +35,8 @@ class ForwardBatch:
     lora_slots: torch.Tensor | None = None
     # data-parallel rank that owns each row's KV (expert-parallel models); host list
     row_ranks: list | None = None
+    # recurrent-state slot of each row (hybrid models with linear-attention layers)
+    state_slots: torch.Tensor | None = None  # [rows] int32
 
     @property
     def num_tokens(self) -> int:

@@ -57,6 +57,14 @@ class DecoderConfig:
     moe_layers: list[bool] | None = None
     shared_expert_intermediate_size: int = 0
     shared_expert_gate: bool = False
+    # hybrid linear-attention layers (Gated DeltaNet: Qwen3-Next, Qwen 3.5 / 3.6)
+    layer_types: list[str] | None = None  # per layer "full_attention" | "linear_attention"
+    attn_output_gate: bool = False  # q_proj also yields a sigmoid gate on the attention output
+    linear_num_key_heads: int = 0
+    linear_num_value_heads: int = 0
+    linear_key_head_dim: int = 128
+    linear_value_head_dim: int = 128
+    linear_conv_kernel_dim: int = 4
     # quantization of the checkpoint (MLX layout), informational
     quantization: dict | None = None
     # MTP (multi-token prediction) modules
@@ -79,6 +87,26 @@ class DecoderConfig:
         if not self.layer_windows:
             return 0
         return int(self.layer_windows[layer])
+
+    def is_linear(self, layer: int) -> bool:
+        return bool(self.layer_types) and self.layer_types[layer] == "linear_attention"
+
+    @property
+    def gdn_dims(self) -> tuple[int, int, int, int]:
+        """(key heads, key head dim, value heads, value head dim) of the linear layers."""
+        return (self.linear_num_key_heads, self.linear_key_head_dim, self.linear_num_value_heads,
+                self.linear_value_head_dim)
+
+    @property
+    def gdn_conv_dim(self) -> int:
+        Hk, Dk, Hv, Dv = self.gdn_dims
+        return 2 * Hk * Dk + Hv * Dv
+
+    @property
+    def gdn_in_dim(self) -> int:
+        """Rows of the fused linear-layer in-projection: q | k | v | z | b | a."""
+        Hk, Dk, Hv, Dv = self.gdn_dims
+        return self.gdn_conv_dim + Hv * Dv + 2 * Hv
 
     def is_moe(self, layer: int) -> bool:
         if self.num_experts <= 0:

@@ -32,7 +32,12 @@ from .rope import build_rope
 class LayerWeights:
     __slots__ = ("ln1", "wqkv", "bqkv", "q_norm", "k_norm", "wo", "bo", "ln2", "post_attn_norm", "post_ffn_norm",
                  "wgu", "bgu", "wd", "bd", "router", "router_b", "experts_gu", "experts_gu_b", "experts_d",
-                 "experts_d_b", "shared_gu", "shared_d", "shared_gate", "sinks", "moe")
+                 "experts_d_b", "shared_gu", "shared_d", "shared_gate", "sinks", "moe",
+                 # linear-attention (Gated DeltaNet) layers: wqkv is the fused in-projection
+                 # q|k|v|z|b|a and wo the out-projection
+                 "linear", "conv_w", "A_log", "dt_bias", "gdn_norm")
+
+    F32 = ("sinks", "conv_w", "A_log", "dt_bias")  # kept in fp32 whatever the model dtype
 
     def __init__(self):
         for s in self.__slots__:
@@ -85,6 +90,18 @@ class DenseKVCache:
             self.v[layer] = torch.cat([self.v[layer], v], 0)
         return self.k[layer], self.v[layer]
 
+    def rec_state(self, layer: int, model):
+        """(conv, delta-rule) state of a linear-attention layer, one slot."""
+        if not hasattr(self, "_rec"):
+            self._rec = {}
+        if layer not in self._rec:
+            cfg = model.cfg
+            Hk, Dk, Hv, Dv = cfg.gdn_dims
+            dev, dt = model.device, model.dtype
+            self._rec[layer] = (torch.zeros(1, cfg.linear_conv_kernel_dim - 1, cfg.gdn_conv_dim, dtype=dt, device=dev),
+                                torch.zeros(1, Hv, Dv, Dk, dtype=torch.float32, device=dev))
+        return self._rec[layer]
+
     def trim(self, n: int):
         """Drop the last n tokens (speculative rollback)."""
         n = min(n, self.offset)
@@ -121,6 +138,20 @@ class DecoderLM:
         self.cos_sin = self.cos_sin.to(self.device)
         self.lora = None  # adapter whose update is currently added into the weights (adapters.lora)
         self.tp_fused = None  # fused symmetric-memory TP decode path (parallel.tp_fused)
+        # hybrid models: attention layers index the KV slab, linear layers the recurrent-state pool
+        self.kv_index, self.rec_index = [], []
+        na = nl = 0
+        for li in range(cfg.num_layers):
+            if cfg.is_linear(li):
+                assert w == 1, "linear-attention layers run without tensor parallelism"
+                self.kv_index.append(-1)
+                self.rec_index.append(nl)
+                nl += 1
+            else:
+                self.kv_index.append(na)
+                self.rec_index.append(-1)
+                na += 1
+        self.num_kv_layers = na
 
     # ------------------------------------------------------------------ weights
     def named_tensors(self):
@@ -193,8 +224,17 @@ class DecoderLM:
             L = LayerWeights()
             L.ln1 = ones(hd)
             L.ln2 = ones(hd)
+            L.linear = cfg.is_linear(li)
+            if L.linear:
+                self._init_linear_layer(L, rn, g)
+                self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
+                if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
+                    self.layers.append(L)
+                continue
             wq, wk, wv = rn(cfg.q_size, hd), rn(cfg.kv_size, hd), rn(cfg.kv_size, hd)
             L.wqkv = torch.cat([rows(wq, self.H * D), kv_rows(wk), kv_rows(wv)], 0)
+            if cfg.attn_output_gate:  # gate rows after q|k|v: the attention kernels read q|k|v only
+                L.wqkv = torch.cat([L.wqkv, rows(rn(cfg.q_size, hd), self.H * D)], 0)
             if cfg.attention_bias:
                 bq, bk, bv = rn(cfg.q_size), rn(cfg.kv_size), rn(cfg.kv_size)
                 L.bqkv = torch.cat([rows(bq, self.H * D), kv_rows(bk), kv_rows(bv)], 0)
@@ -211,41 +251,63 @@ class DecoderLM:
             if cfg.attention_sinks:
                 s = torch.empty(cfg.num_heads, device=dev, dtype=torch.float32).normal_(0.0, 1.0, generator=g)
                 L.sinks = rows(s, self.H)
-            if cfg.is_moe(li):
-                E = cfg.num_experts
-                Fe = cfg.moe_intermediate_size
-                L.moe = True
-                L.router = rn(E, hd)
-                if cfg.router_bias:
-                    L.router_b = rn(E)
-                L.experts_gu = glu_pair(Fe, self.Fe, hd, (E,))
-                L.experts_d = cols(rn(E, hd, Fe))
-                if cfg.mlp_bias:
-                    gb, ub = rn(E, Fe), rn(E, Fe)
-                    L.experts_gu_b = torch.stack([ref.interleave_gate_up(rows(gb[e], self.Fe)[:, None],
-                                                                         rows(ub[e], self.Fe)[:, None])[:, 0]
-                                                  for e in range(E)])
-                    db = rn(E, hd)
-                    L.experts_d_b = db if r == 0 else torch.zeros_like(db)
-                if cfg.shared_expert_intermediate_size:
-                    Fs = cfg.shared_expert_intermediate_size
-                    L.shared_gu = glu_pair(Fs, Fs // w, hd)
-                    L.shared_d = cols(rn(hd, Fs))
-                    if cfg.shared_expert_gate:
-                        L.shared_gate = rn(1, hd)
-            else:
-                L.moe = False
-                F = cfg.intermediate_size
-                L.wgu = glu_pair(F, self.F, hd)
-                L.wd = cols(rn(hd, F))
-                if cfg.mlp_bias:
-                    gb, ub = rn(F), rn(F)
-                    L.bgu = ref.interleave_gate_up(rows(gb, self.F)[:, None], rows(ub, self.F)[:, None])[:, 0]
-                    bd = rn(hd)
-                    L.bd = bd if r == 0 else torch.zeros_like(bd)
+            self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
             if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
                 self.layers.append(L)
         return self
+
+    def _init_ffn(self, L, li, rn, ones, rows, cols, glu_pair):
+        cfg = self.cfg
+        r, w = self.tp.rank, self.tp.world
+        hd = cfg.hidden_size
+        if cfg.is_moe(li):
+            E = cfg.num_experts
+            Fe = cfg.moe_intermediate_size
+            L.moe = True
+            L.router = rn(E, hd)
+            if cfg.router_bias:
+                L.router_b = rn(E)
+            L.experts_gu = glu_pair(Fe, self.Fe, hd, (E,))
+            L.experts_d = cols(rn(E, hd, Fe))
+            if cfg.mlp_bias:
+                gb, ub = rn(E, Fe), rn(E, Fe)
+                L.experts_gu_b = torch.stack([ref.interleave_gate_up(rows(gb[e], self.Fe)[:, None],
+                                                                     rows(ub[e], self.Fe)[:, None])[:, 0]
+                                              for e in range(E)])
+                db = rn(E, hd)
+                L.experts_d_b = db if r == 0 else torch.zeros_like(db)
+            if cfg.shared_expert_intermediate_size:
+                Fs = cfg.shared_expert_intermediate_size
+                L.shared_gu = glu_pair(Fs, Fs // w, hd)
+                L.shared_d = cols(rn(hd, Fs))
+                if cfg.shared_expert_gate:
+                    L.shared_gate = rn(1, hd)
+        else:
+            L.moe = False
+            F = cfg.intermediate_size
+            L.wgu = glu_pair(F, self.F, hd)
+            L.wd = cols(rn(hd, F))
+            if cfg.mlp_bias:
+                gb, ub = rn(F), rn(F)
+                L.bgu = ref.interleave_gate_up(rows(gb, self.F)[:, None], rows(ub, self.F)[:, None])[:, 0]
+                bd = rn(hd)
+                L.bd = bd if r == 0 else torch.zeros_like(bd)
+
+    def _init_linear_layer(self, L, rn, g):
+        """Gated DeltaNet weights: fused in-projection q|k|v|z|b|a, depthwise
+        conv taps, decay parameters (A_log = log U(1, 16), dt_bias = 1),
+        gated-norm weight, out-projection."""
+        cfg = self.cfg
+        hd = cfg.hidden_size
+        Hk, Dk, Hv, Dv = cfg.gdn_dims
+        C = cfg.gdn_conv_dim
+        dev = self.device
+        L.wqkv = rn(cfg.gdn_in_dim, hd)
+        L.conv_w = rn(C, cfg.linear_conv_kernel_dim).float()
+        L.A_log = torch.empty(Hv, device=dev, dtype=torch.float32).uniform_(1.0, 16.0, generator=g).log_()
+        L.dt_bias = torch.ones(Hv, device=dev, dtype=torch.float32)
+        L.gdn_norm = torch.ones(Dv, device=dev, dtype=self.dtype)
+        L.wo = rn(hd, Hv * Dv)
 
     # ------------------------------------------------------------------ pieces
     def _attn_out(self, L, attn2d):
@@ -307,30 +369,85 @@ class DecoderLM:
         delta = None
         attn = torch.empty((T, self.H, self.D), dtype=x.dtype, device=x.device)
         for li, L in enumerate(self.layers):
-            if delta is not None and L.post_attn_norm is not None:
-                pass
             h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
-            qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
-            kc, vc = kv.layer(li)
-            q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
-                                    L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
-                                    kv.k_scale(li), kv.v_scale(li))
-            win = cfg.window(li)
-            if nd:
-                ops.paged_decode(q[:nd], kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, win, L.sinks,
-                                 cfg.attn_logit_softcap, kv.k_scale(li), kv.v_scale(li), fb.dec_max_parts,
-                                 out=attn[:nd])
-            if T > nd:
-                ops.paged_prefill(q[nd:], kc, vc, fb.pf_page_table, fb.pf_cu_q, fb.pf_pos0, cfg.scale, win, L.sinks,
-                                  cfg.attn_logit_softcap, kv.k_scale(li), kv.v_scale(li), fb.pf_cu_q_host,
-                                  out=attn[nd:])
-            delta = self._attn_out(L, attn.view(T, self.H * self.D))
+            if L.linear:
+                delta = self._gdn(L, h, fb, kv, li)
+            else:
+                delta = self._attention(L, h, fb, kv, li, attn)
             if L.post_attn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
             h = ops.add_rmsnorm(x, delta, L.ln2, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
             delta = self._mlp(L, h)
             if L.post_ffn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_ffn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+        return self._head(x, delta, fb, return_hidden, return_both, return_residual)
+
+    def _attention(self, L, h, fb: ForwardBatch, kv, li: int, attn: torch.Tensor) -> torch.Tensor:
+        """Paged attention of one layer (decode rows, then prefill chunks);
+        returns the output projection (before the residual add)."""
+        cfg = self.cfg
+        T, nd = fb.num_tokens, fb.num_decode
+        ki = self.kv_index[li] if self.kv_index else li
+        qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
+        kc, vc = kv.layer(ki)
+        q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
+                                L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
+                                kv.k_scale(ki), kv.v_scale(ki))
+        win = cfg.window(li)
+        if nd:
+            ops.paged_decode(q[:nd], kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, win, L.sinks,
+                             cfg.attn_logit_softcap, kv.k_scale(ki), kv.v_scale(ki), fb.dec_max_parts,
+                             out=attn[:nd])
+        if T > nd:
+            ops.paged_prefill(q[nd:], kc, vc, fb.pf_page_table, fb.pf_cu_q, fb.pf_pos0, cfg.scale, win, L.sinks,
+                              cfg.attn_logit_softcap, kv.k_scale(ki), kv.v_scale(ki), fb.pf_cu_q_host,
+                              out=attn[nd:])
+        a2 = attn.view(T, self.H * self.D)
+        if cfg.attn_output_gate:
+            from ..ops.gdn import sigmoid_mul
+
+            g0 = (self.H + 2 * self.KVH) * self.D
+            a2 = sigmoid_mul(a2, qkv[:, g0:g0 + self.H * self.D])
+        return self._attn_out(L, a2)
+
+    def _gdn_rows(self, fb: ForwardBatch):
+        """Rows of `fb` for the linear-attention layers (cached on the batch):
+        decode rows are one token each and never fresh; a prefill chunk is
+        fresh when it starts at position 0."""
+        from ..ops.gdn import GdnRows
+
+        rows = getattr(fb, "_gdn_rows", None)
+        if rows is not None:
+            return rows
+        dev = fb.input_ids.device
+        nd = fb.num_decode
+        assert fb.state_slots is not None, "hybrid models need the rows' recurrent-state slots"
+        if fb.num_tokens == nd:  # pure decode: device-side construction (graph-capturable)
+            cu = torch.arange(nd + 1, dtype=torch.int32, device=dev)
+            fresh = torch.zeros(nd, dtype=torch.int32, device=dev)
+            cu_host = None
+        else:
+            pf = fb.pf_cu_q_host or [0]
+            cu_host = list(range(nd + 1)) + [nd + c for c in pf[1:]]
+            cu = torch.tensor(cu_host, dtype=torch.int32).to(dev)
+            fresh = torch.cat([torch.zeros(nd, dtype=torch.int32, device=dev), (fb.pf_pos0 == 0).to(torch.int32)])
+        rows = GdnRows(cu, fresh, fb.state_slots.to(torch.int32), cu_host)
+        fb._gdn_rows = rows
+        return rows
+
+    def _gdn(self, L, h, fb: ForwardBatch, kv, li: int) -> torch.Tensor:
+        from ..ops.gdn import gdn_layer
+
+        cfg = self.cfg
+        Hk, Dk, Hv, Dv = cfg.gdn_dims
+        P = ops.gemm(h, L.wqkv)
+        conv, ssm = kv.rec.layer(self.rec_index[li])
+        y = gdn_layer(P, self._gdn_rows(fb), conv, ssm, L.conv_w, L.A_log, L.dt_bias, L.gdn_norm, Hk, Dk, Hv, Dv,
+                      cfg.rms_norm_eps)
+        return self._attn_out(L, y)
+
+    def _head(self, x, delta, fb, return_hidden, return_both, return_residual):
+        cfg = self.cfg
         if return_residual:
             return (x.float() + delta.float()).to(x.dtype) if delta is not None else x
         if fb.logit_idx is not None:
@@ -392,14 +509,32 @@ class DecoderLM:
         delta = None
         for li, L in enumerate(self.layers):
             h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
-            qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
-            q, k, v = ops.qk_norm_rope_kv(qkv, positions, None, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
-                                          L.q_norm, L.k_norm, cfg.rms_norm_eps, None, None, self.H, self.KVH,
-                                          self.D, return_kv=True)
-            kk, vv = cache.update(li, k, v)
-            a = ref.attention_rows_ref(q.float(), kk.float(), vv.float(), positions, kk.shape[0], cfg.scale,
-                                       cfg.window(li), L.sinks, cfg.attn_logit_softcap).to(x.dtype)
-            delta = self._attn_out(L, a.reshape(Lq, self.H * self.D).contiguous())
+            if L.linear:
+                from ..ops.gdn import GdnRows, gdn_layer
+
+                Hk, Dk, Hv, Dv = cfg.gdn_dims
+                conv, ssm = cache.rec_state(li, self)
+                i32 = dict(dtype=torch.int32, device=x.device)
+                rows = GdnRows(torch.tensor([0, Lq], **i32), torch.tensor([1 if p0 == 0 else 0], **i32),
+                               torch.zeros(1, **i32), [0, Lq])
+                y = gdn_layer(ops.gemm(h, L.wqkv), rows, conv, ssm, L.conv_w, L.A_log, L.dt_bias, L.gdn_norm,
+                              Hk, Dk, Hv, Dv, cfg.rms_norm_eps)
+                delta = self._attn_out(L, y)
+            else:
+                qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
+                q, k, v = ops.qk_norm_rope_kv(qkv, positions, None, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
+                                              L.q_norm, L.k_norm, cfg.rms_norm_eps, None, None, self.H, self.KVH,
+                                              self.D, return_kv=True)
+                kk, vv = cache.update(li, k, v)
+                a = ref.attention_rows_ref(q.float(), kk.float(), vv.float(), positions, kk.shape[0], cfg.scale,
+                                           cfg.window(li), L.sinks, cfg.attn_logit_softcap).to(x.dtype)
+                a2 = a.reshape(Lq, self.H * self.D).contiguous()
+                if cfg.attn_output_gate:
+                    from ..ops.gdn import sigmoid_mul
+
+                    g0 = (self.H + 2 * self.KVH) * self.D
+                    a2 = sigmoid_mul(a2, qkv[:, g0:g0 + self.H * self.D])
+                delta = self._attn_out(L, a2)
             if L.post_attn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
             h = ops.add_rmsnorm(x, delta, L.ln2, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
@@ -436,7 +571,7 @@ class DecoderLM:
             for s in LayerWeights.__slots__:
                 v = getattr(L, s)
                 if isinstance(v, torch.Tensor):
-                    v = cv(v, s == "sinks")
+                    v = cv(v, s in LayerWeights.F32)
                 elif isinstance(v, QuantizedWeight):
                     v = v.to(dev)
                 setattr(N, s, v)
@@ -446,7 +581,7 @@ class DecoderLM:
     def kv_bytes_per_token(self, kv_dtype=None) -> int:
         dt = kv_dtype or self.dtype
         es = torch.empty((), dtype=dt).element_size()
-        return 2 * self.cfg.num_layers * self.KVH * self.D * es
+        return 2 * self.num_kv_layers * self.KVH * self.D * es
 
     def to(self, device=None, dtype=None):
         device = torch.device(device) if device is not None else self.device
@@ -467,7 +602,7 @@ class DecoderLM:
             for s in LayerWeights.__slots__:
                 v = getattr(L, s)
                 if isinstance(v, torch.Tensor):
-                    if s == "sinks":
+                    if s in LayerWeights.F32:
                         setattr(L, s, v.to(device=device, dtype=torch.float32))
                     else:
                         setattr(L, s, v.to(device=device, dtype=dtype))

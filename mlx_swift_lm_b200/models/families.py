@@ -25,7 +25,9 @@ register("llama", "mistral", "smollm3", "helium", "apertus", "granite", "hunyuan
 register("qwen2")  # q/k/v biases
 register("qwen3", qk_norm=True)
 register("qwen3_moe", qk_norm=True, moe=True)
-register("qwen3_next", qk_norm=True, moe=True)
+register("qwen3_next", qk_norm=True, moe=True, hybrid=True)
+register("qwen3_5", "qwen3_5_text", "qwen3_8", "qwen3_8_text", qk_norm=True, hybrid=True)
+register("qwen3_5_moe", "qwen3_8_moe", qk_norm=True, moe=True, hybrid=True)
 register("mixtral", moe=True, mixtral_names=True)
 register("phimoe", moe=True, mixtral_names=True)
 register("olmoe", moe=True, qk_norm=True)
@@ -84,6 +86,22 @@ def build_config(hf: dict) -> DecoderConfig:
         cfg.moe_layers = [(i not in mlp_only) and ((i + 1) % step == 0) for i in range(cfg.num_layers)]
         cfg.shared_expert_intermediate_size = hf.get("shared_expert_intermediate_size", 0)
         cfg.shared_expert_gate = bool(cfg.shared_expert_intermediate_size)
+    if tr.get("hybrid"):
+        # Gated DeltaNet layers with gated full attention every
+        # `full_attention_interval` layers (MLXLLM/Models/Qwen3Next.swift:452)
+        cfg.linear_num_key_heads = hf.get("linear_num_key_heads", 16)
+        cfg.linear_num_value_heads = hf.get("linear_num_value_heads", 32)
+        cfg.linear_key_head_dim = hf.get("linear_key_head_dim", 128)
+        cfg.linear_value_head_dim = hf.get("linear_value_head_dim", 128)
+        cfg.linear_conv_kernel_dim = hf.get("linear_conv_kernel_dim", 4)
+        if layer_types and all(t in ("linear_attention", "full_attention") for t in layer_types):
+            cfg.layer_types = list(layer_types)
+        else:
+            k = hf.get("full_attention_interval", 4)
+            cfg.layer_types = ["full_attention" if (i + 1) % k == 0 else "linear_attention"
+                               for i in range(cfg.num_layers)]
+        cfg.layer_windows = None
+        cfg.attn_output_gate = hf.get("attn_output_gate", True)
     g = tr.get("gemma")
     if g:
         cfg.embed_scale = math.sqrt(hidden)

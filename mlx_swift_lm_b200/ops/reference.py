@@ -326,3 +326,61 @@ def sample_ref(logits, temperature, top_k=0, top_p=1.0, min_p=0.0, key=0, step=0
     g = -np.log(-np.log(u))
     v = np.where(keep, s + g, -np.inf)
     return int(np.argmax(v))
+
+
+# --------------------------------------------------------------------------
+# gated DeltaNet (linear attention)
+# --------------------------------------------------------------------------
+def gdn_layer_ref(P, cu, fresh, slot, conv_state, ssm_state, conv_w, A_log, dt_bias, norm_w, Hk, Dk, Hv, Dv, eps):
+    """Gated DeltaNet layer body over a flattened batch of rows (fp32).
+    P [T, C + Hv*Dv + 2*Hv] = q | k | v | z | b | a (C = 2*Hk*Dk + Hv*Dv);
+    rows r cover tokens cu[r]..cu[r+1]-1 with state slot slot[r] (zero state
+    when fresh[r]). Updates conv_state [S, 3, C] and ssm_state [S, Hv, Dv, Dk]
+    in place; returns rmsnorm(y) * norm_w * silu(z) [T, Hv*Dv] in P.dtype.
+    Semantics of MLXLMCommon/GatedDelta.swift (gated_delta_step) and
+    MLXLLM/Models/Qwen3Next.swift (conv + SiLU, q/k scaling, RMSNormGated)."""
+    T = P.shape[0]
+    C = 2 * Hk * Dk + Hv * Dv
+    taps = conv_w.shape[1]
+    out = torch.zeros(T, Hv * Dv, dtype=torch.float32, device=P.device)
+    cu = [int(c) for c in cu]
+    rep = Hv // Hk
+    for r in range(len(cu) - 1):
+        s0, s1 = cu[r], cu[r + 1]
+        n = s1 - s0
+        if n <= 0:
+            continue
+        sl = int(slot[r])
+        x = P[s0:s1, :C].float()
+        prev = torch.zeros(taps - 1, C, device=P.device) if int(fresh[r]) else conv_state[sl].float()
+        xx = torch.cat([prev, x], 0)
+        conv = torch.zeros(n, C, device=P.device)
+        for j in range(taps):
+            conv += conv_w[:, j].float() * xx[j:j + n]
+        y = conv * torch.sigmoid(conv)
+        q = y[:, :Hk * Dk].reshape(n, Hk, Dk)
+        k = y[:, Hk * Dk:2 * Hk * Dk].reshape(n, Hk, Dk)
+        v = y[:, 2 * Hk * Dk:].reshape(n, Hv, Dv)
+        q = q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + eps) / Dk
+        k = k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + eps) / math.sqrt(Dk)
+        zb = C + Hv * Dv
+        b = P[s0:s1, zb:zb + Hv].float()
+        a = P[s0:s1, zb + Hv:zb + 2 * Hv].float()
+        g = torch.exp(-torch.exp(A_log.float()) * torch.nn.functional.softplus(a + dt_bias.float()))
+        beta = torch.sigmoid(b)
+        S = torch.zeros(Hv, Dv, Dk, device=P.device) if int(fresh[r]) else ssm_state[sl].float().clone()
+        o = torch.zeros(n, Hv, Dv, device=P.device)
+        for t in range(n):
+            kh = k[t].repeat_interleave(rep, 0)
+            qh = q[t].repeat_interleave(rep, 0)
+            S = S * g[t][:, None, None]
+            kv = (S * kh[:, None, :]).sum(-1)
+            delta = (v[t] - kv) * beta[t][:, None]
+            S = S + kh[:, None, :] * delta[:, :, None]
+            o[t] = (S * qh[:, None, :]).sum(-1)
+        ssm_state[sl] = S.to(ssm_state.dtype)
+        conv_state[sl] = xx[-(taps - 1):].to(conv_state.dtype)
+        z = P[s0:s1, C:C + Hv * Dv].float().reshape(n, Hv, Dv)
+        on = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + eps) * norm_w.float() * (z * torch.sigmoid(z))
+        out[s0:s1] = on.reshape(n, -1)
+    return out.to(P.dtype)
