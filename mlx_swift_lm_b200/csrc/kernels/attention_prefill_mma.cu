@@ -102,8 +102,11 @@ __global__ void __launch_bounds__(128) prefill_mma_kernel(const __grid_constant_
   const int pos0 = a.q_pos0[row];
   const int nq = min(kQT, qlen - qoff);  // queries of this tile
   if (nq <= 0) return;
+  // window < 0: bidirectional (encoders) - every query sees the row's keys
+  // [0, pos0 + qlen); else causal, with a sliding window when window > 0.
+  const bool bidir = a.window < 0;
   // key range of the tile: [k_lo, k_hi] (absolute positions, inclusive)
-  const int k_hi = pos0 + qoff + nq - 1;
+  const int k_hi = bidir ? pos0 + qlen - 1 : pos0 + qoff + nq - 1;
   const int k_lo = a.window > 0 ? max(0, pos0 + qoff - a.window + 1) : 0;
   const int pg_lo = k_lo / kPage, pg_hi = k_hi / kPage;
   const int npages = pg_hi - pg_lo + 1;
@@ -131,7 +134,8 @@ __global__ void __launch_bounds__(128) prefill_mma_kernel(const __grid_constant_
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const float smul = a.softcap > 0.f ? a.scale : a.scale * kLog2e;
   // first / last key position this warp's rows can see (for page skipping)
-  const int w_hi = pos0 + qoff + min(nq - 1, warp * 16 + 15);
+  const int w_hi = bidir ? k_hi : pos0 + qoff + min(nq - 1, warp * 16 + 15);
+  const int lim0 = bidir ? k_hi : qp0, lim1 = bidir ? k_hi : qp1;  // last visible key of each row
   const int w_lo = a.window > 0 ? max(0, pos0 + qoff + warp * 16 - a.window + 1) : 0;
 
   const uint32_t ring_s = smem_u32(smem);
@@ -183,8 +187,8 @@ __global__ void __launch_bounds__(128) prefill_mma_kernel(const __grid_constant_
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int kp = kpos0 + n * 8 + 2 * t4 + c;
-          const bool ok0 = v0 && kp <= qp0 && (a.window <= 0 || kp > qp0 - a.window);
-          const bool ok1 = v1 && kp <= qp1 && (a.window <= 0 || kp > qp1 - a.window);
+          const bool ok0 = v0 && kp <= lim0 && (a.window <= 0 || kp > qp0 - a.window);
+          const bool ok1 = v1 && kp <= lim1 && (a.window <= 0 || kp > qp1 - a.window);
           float x0 = sc[n][c] * smul, x1 = sc[n][2 + c] * smul;
           if (a.softcap > 0.f) {
             x0 = a.softcap * tanhf(x0 / a.softcap) * kLog2e;

@@ -67,6 +67,43 @@ __global__ void add_rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfl
   }
 }
 
+// LayerNorm with bias over x + delta (BERT-family post-norm residual): one CTA
+// per row; x <- bf16(x + delta) when delta is given, out = LN(x) * w + b
+// (out may alias x).
+__global__ void add_layernorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
+                                     const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ b,
+                                     __nv_bfloat16* out, int H, int ldx, int ldd, int ldo, float eps) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
+  extern __shared__ float rbuf[];  // H floats
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  __nv_bfloat16* xr = x + (size_t)row * ldx;
+  const __nv_bfloat16* dr = delta ? delta + (size_t)row * ldd : nullptr;
+  float sum = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float v = bf2f(xr[i]);
+    if (dr) {
+      const __nv_bfloat16 s = f2bf(v + bf2f(dr[i]));
+      xr[i] = s;
+      v = bf2f(s);
+    }
+    rbuf[i] = v;
+    sum += v;
+  }
+  const float mean = block_sum(sum, red) / (float)H;
+  float var = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float d = rbuf[i] - mean;
+    var += d * d;
+  }
+  __syncthreads();  // red[] is reused by the second reduction
+  const float inv = rsqrtf(block_sum(var, red) / (float)H + eps);
+  __nv_bfloat16* orow = out + (size_t)row * ldo;
+  for (int i = threadIdx.x; i < H; i += blockDim.x)
+    orow[i] = f2bf((rbuf[i] - mean) * inv * bf2f(w[i]) + (b ? bf2f(b[i]) : 0.f));
+}
+
 // One CTA per token; one warp per head. Heads [0, H) are query heads,
 // [H, H+KVH) key heads, [H+KVH, H+2KVH) value heads of the fused qkv row.
 // cos_sin: [max_pos, rot_dim] fp32, first rot_dim/2 entries cos, then sin.
@@ -240,6 +277,18 @@ b200::launch_k(  add_rmsnorm_kernel, dim3(T), dim3(threads), H * sizeof(float), 
 }
 
 // kv_fp8: 0 -> bf16 pages, 1 -> fp8 e4m3 pages (k_scale / v_scale per KV head).
+int b200_add_layernorm(void* x, const void* delta, const void* w, const void* b, void* out, int T, int H, int ldx,
+                       int ldd, int ldo, float eps, cudaStream_t st) {
+  if (T <= 0) return 0;
+  const size_t smem = (size_t)H * sizeof(float);
+  if (smem > 48 * 1024) return -1;
+  cudaError_t e = launch_k(add_layernorm_kernel, dim3(T), dim3(256), smem, st, 1,
+                           reinterpret_cast<__nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(delta),
+                           reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<const __nv_bfloat16*>(b),
+                           reinterpret_cast<__nv_bfloat16*>(out), H, ldx, ldd, ldo, eps);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
 int b200_qk_norm_rope_kv(const void* qkv, int T, int ld_qkv, const int* positions, const int64_t* slots,
                          const float* cos_sin, int rot_dim, int interleaved, const void* qw, const void* kw,
                          float eps, void* q_out, void* k_cache, void* v_cache, int kv_fp8, const float* k_scale,

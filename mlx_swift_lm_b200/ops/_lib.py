@@ -41,6 +41,7 @@ _SIGS = {
     "b200_paged_decode": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32,
                                 i32, f32, f32, i64, vp]),
     "b200_paged_decode_part_tokens": (i32, []),
+    "b200_add_layernorm": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp]),
     "b200_paged_prefill_mma": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32, f32,
                                      i64, vp]),
     "b200_paged_prefill_simt": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32, f32,

@@ -106,7 +106,9 @@ def prefill_tiles(cu_q: list[int], G: int) -> list[tuple[int, int]]:
 
 def paged_prefill(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0, sinks=None, softcap=0.0,
                   k_scale=None, v_scale=None, cu_q_host=None, out=None):
-    """q [T, H, D] for rows' chunks; cu_q [R+1] int32; q_pos0 [R] int32 (first position of each chunk)."""
+    """q [T, H, D] for rows' chunks; cu_q [R+1] int32; q_pos0 [R] int32 (first position of each chunk).
+    window > 0: sliding window; 0: causal; < 0: bidirectional over each row's
+    keys (encoders; bf16 pages, tensor-core kernel only)."""
     if not q.is_cuda:
         y = ref.paged_prefill_ref(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window, sinks, softcap,
                                   k_scale, v_scale)
@@ -132,6 +134,8 @@ def paged_prefill(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0
         _lib.check(rc, "paged_prefill_mma")
         _lib.count(1)
         return out
+    if window < 0:
+        raise ValueError("bidirectional attention needs bf16 K/V pages and head_dim 64, 128 or 256")
     tiles = prefill_tiles(cu_q_host, G)
     tiles_t = torch.tensor(tiles, dtype=torch.int32).pin_memory().to(q.device, non_blocking=True)
     rc = _lib.lib().b200_paged_prefill_simt(

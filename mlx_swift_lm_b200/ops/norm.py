@@ -29,6 +29,30 @@ def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor | None, w: torch.Tensor, ep
     return out
 
 
+def add_layernorm(x: torch.Tensor, delta: torch.Tensor | None, w: torch.Tensor, b: torch.Tensor | None, eps: float,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """x <- x + delta (in place, rounded to x.dtype); returns LayerNorm(x) * w + b
+    (`out` may be x itself: the post-norm residual of BERT-family encoders)."""
+    if not x.is_cuda:
+        if delta is not None:
+            x.copy_((x.float() + delta.float()).to(x.dtype))
+        y = torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), w.float(),
+                                           None if b is None else b.float(), eps).to(x.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    T, H = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    rc = _lib.lib().b200_add_layernorm(x.data_ptr(), _lib.ptr(delta), w.data_ptr(), _lib.ptr(b), out.data_ptr(), T, H,
+                                       x.stride(0), delta.stride(0) if delta is not None else 0, out.stride(0),
+                                       float(eps), _lib.stream_ptr(x.device))
+    _lib.check(rc, "add_layernorm")
+    _lib.count(1)
+    return out
+
+
 def rmsnorm(x, w, eps, offset_one=False):
     return add_rmsnorm(x, None, w, eps, offset_one=offset_one)
 

@@ -49,7 +49,7 @@ def glu_act_ref(epi, g, u):
 
 def gemm_ref(x, w, epi="none", residual=None, out_dtype=None, bias=None):
     """y = epi(x @ w.T + bias) computed in fp32.
-    epi: none | swiglu | geglu | swiglu_oai | f32 | add."""
+    epi: none | swiglu | geglu | swiglu_oai | f32 | add | gelu | gelu_tanh."""
     acc = x.float() @ w.float().t()
     if bias is not None:
         acc = acc + bias.float()
@@ -65,6 +65,8 @@ def gemm_ref(x, w, epi="none", residual=None, out_dtype=None, bias=None):
         return acc
     if epi == "add":
         return (acc.to(x.dtype).float() + residual.float()).to(dt)
+    if epi in ("gelu", "gelu_tanh"):
+        return torch.nn.functional.gelu(acc, approximate="tanh" if epi == "gelu_tanh" else "none").to(dt)
     return acc.to(dt)
 
 
@@ -91,7 +93,9 @@ def rope_cos_sin(inv_freq: torch.Tensor, max_pos: int, mscale: float = 1.0) -> t
 
 
 def apply_rope_ref(x, positions, cos_sin, rot_dim, interleaved=False):
-    """x: [T, nh, D] float. Returns rotated float tensor."""
+    """x: [T, nh, D] float. Returns rotated float tensor (rot_dim 0: unchanged)."""
+    if rot_dim == 0:
+        return x.float()
     half = rot_dim // 2
     cs = cos_sin[positions.long()]  # [T, rot_dim]
     cos, sin = cs[:, None, :half], cs[:, None, half:]
@@ -157,7 +161,9 @@ def gather_pages(cache, page_ids, n_tokens, scale=None):
 
 def attention_rows_ref(q, k, v, q_pos, kv_len, scale, window=0, sinks=None, softcap=0.0):
     """q [Tq, H, D] float at absolute positions q_pos [Tq]; k,v [kv_len, KVH, D].
-    Causal with optional sliding window; sinks are denominator-only logits."""
+    Causal with optional sliding window (window > 0); window < 0 is
+    bidirectional over all kv_len keys (encoders). Sinks are
+    denominator-only logits."""
     Tq, H, D = q.shape
     KVH = k.shape[1]
     G = H // KVH
@@ -169,6 +175,8 @@ def attention_rows_ref(q, k, v, q_pos, kv_len, scale, window=0, sinks=None, soft
     kp = torch.arange(kv_len, device=q.device)
     qp = q_pos.to(q.device).long()[:, None]
     mask = kp[None, :] <= qp
+    if window < 0:
+        mask = torch.ones_like(mask)
     if window > 0:
         mask = mask & (kp[None, :] > qp - window)
     s = s.masked_fill(~mask[:, None, :], float("-inf"))

@@ -68,7 +68,13 @@ def main(argv=None):
     else:
         print("either --model or --random-config is required", file=sys.stderr)
         return 2
-    svc = OpenAIService(container, tool_parser=args.tool_call_parser, reasoning_parser=args.reasoning_parser)
+    embedder = None
+    if args.embedding_model:
+        from ..api.embed import Embedder
+
+        embedder = Embedder.from_pretrained(args.embedding_model, device=device)
+    svc = OpenAIService(container, tool_parser=args.tool_call_parser, reasoning_parser=args.reasoning_parser,
+                        embedder=embedder)
     uvicorn.run(build_app(svc), host=args.host, port=args.port, log_level="info")
     return 0
 

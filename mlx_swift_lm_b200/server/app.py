@@ -318,6 +318,8 @@ class OpenAIService:
             raise ValidationError("input must be a string or a non-empty list")
         emb = self.embedder or self.c
         vecs = await asyncio.get_running_loop().run_in_executor(None, emb.embed, texts)
+        if hasattr(vecs, "tolist"):  # api.embed.Embedder returns one [N, dim] tensor
+            vecs = vecs.float().cpu().tolist()
         data = [{"object": "embedding", "index": i, "embedding": v} for i, v in enumerate(vecs)]
         n = sum(len(self.c.encode(t)) if isinstance(t, str) else len(t) for t in texts)
         return JSONResponse({"object": "list", "data": data, "model": self.model_name,
