@@ -32,16 +32,29 @@ class ModelContainer:
 
     # ------------------------------------------------------------------ loading
     @classmethod
-    def load(cls, path: str, device=None, dtype=torch.bfloat16, engine_config: EngineConfig | None = None,
-             tp=None):
-        from ..loader.load import eos_token_ids, load_model, load_tokenizer
+    def load(cls, path, device=None, dtype=torch.bfloat16, engine_config: EngineConfig | None = None,
+             tp=None, downloader=None, tokenizer_loader=None):
+        """`path`: a local directory, a hub id found on local disk, or a
+        :class:`.configuration.ModelConfiguration` (resolved through
+        `downloader`, default :class:`.configuration.LocalDownloader`)."""
+        from ..loader.load import eos_token_ids, load_model
+        from .configuration import HFTokenizerLoader, ModelConfiguration, configuration
 
+        mc = path if isinstance(path, ModelConfiguration) else configuration(str(path))
+        res = mc.resolve(downloader)
         device = device or ("cuda" if torch.cuda.is_available() else "cpu")
         if device == "cpu":
             dtype = torch.float32
-        model, hf = load_model(path, device, dtype, tp)
-        tok = load_tokenizer(path)
-        return cls(model, tok, engine_config, eos_token_ids(path, hf, tok), model_id=path, hf_config=hf)
+        model, hf = load_model(res.model_directory, device, dtype, tp)
+        tok = (tokenizer_loader or HFTokenizerLoader()).load(res.tokenizer_directory)
+        eos = eos_token_ids(res.model_directory, hf, getattr(tok, "tok", None)) | set(res.eos_token_ids)
+        for s in res.extra_eos_tokens:
+            ids = tok.encode(s) if hasattr(tok, "encode") else []
+            if len(ids) == 1:
+                eos.add(ids[0])
+        c = cls(model, tok, engine_config, eos, model_id=res.name, hf_config=hf)
+        c.configuration = res
+        return c
 
     @classmethod
     def random(cls, cfg, device="cpu", dtype=torch.float32, seed=0, std=0.02, engine_config=None, tokenizer=None):

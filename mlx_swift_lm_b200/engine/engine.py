@@ -48,8 +48,9 @@ class EngineConfig:
     enable_prefix_cache: bool = False
     prefix_block_size: int = 256
     step_timeout_s: float = 30.0  # watchdog (background mode)
-    admission_timeout_s: float = 0.0  # 0 = no lease
+    admission_timeout_s: float = 0.0  # legacy knobs, folded into `leases` when set
     decode_progress_timeout_s: float = 0.0
+    leases: object = None  # engine.leases.LeaseConfig; None = no leases
     clock: object = None  # injectable monotonic clock (tests)
 
 
@@ -158,6 +159,13 @@ class EngineV2:
         self._stop = threading.Event()
         self._step_started = None
         self._clock = self.cfg.clock or time.monotonic
+        self._lease_cfg = self.cfg.leases
+        if self._lease_cfg is None and (self.cfg.admission_timeout_s > 0 or self.cfg.decode_progress_timeout_s > 0):
+            from .leases import LeaseConfig
+
+            self._lease_cfg = LeaseConfig(admission_s=self.cfg.admission_timeout_s, prefill_s=0.0,
+                                          decode_s=self.cfg.decode_progress_timeout_s, backpressure_s=0.0,
+                                          decode_floor_tps=0.0)
         self.max_pages = PagedKVCache.pages_for(self.cfg.max_model_len)
         self.graphs = graph_runner
         if (self.graphs is None and self.device.type == "cuda" and self.cfg.use_cuda_graphs
@@ -192,9 +200,21 @@ class EngineV2:
         if not self.sched.can_ever_fit(total):
             raise ValueError("request can never fit in the KV pool")
         with self._lock:
+            ftd = req.first_token_deadline
+            if ftd is not None:
+                from .leases import TerminalCause, project_first_token_s
+
+                c = self._clock()
+                if c + project_first_token_s(self.sched, len(req.prompt_tokens), ftd, req.priority) > ftd.deadline:
+                    return self._rejected(req, TerminalCause.FIRST_TOKEN_DEADLINE)
             st = self.sched.add(req)
             st.timing.submitted = now()
             st.extra["submit_clock"] = self._clock()
+            if self._lease_cfg is not None:
+                from .leases import RequestLeases
+
+                st.extra["lease"] = RequestLeases(st.extra["submit_clock"], self._lease_cfg, len(req.prompt_tokens),
+                                                  req.max_tokens)
             if self.tok is not None:
                 st.detok = IncrementalDetokenizer(self.tok)
             st.extra["hold"] = StopHoldback(req.stop_strings)
@@ -472,7 +492,7 @@ class EngineV2:
             events += self._finish(st, reason)
         return events
 
-    def _finish(self, st, reason, error=None) -> list[Event]:
+    def _finish(self, st, reason, error=None, cause=None) -> list[Event]:
         if st.status == Status.FINISHED:
             return []
         tail = ""
@@ -487,31 +507,57 @@ class EngineV2:
         self.sched.finish(st)
         st.seq.release()
         ev = Event(st.req.id, tokens=[], text=tail, finished=True, finish_reason=reason, usage=st.usage,
-                   timing=st.timing, error=error)
+                   timing=st.timing, error=error, cause=cause)
         st.stream.put(ev)
         self.states.pop(st.req.id, None)
         self.streams.pop(st.req.id, None)
         return [ev]
 
     def _handle_preemptions(self, plan):
+        """A preempted request restarts its prefill lease (its admission lease
+        is not re-armed)."""
+        c = self._clock()
         for st in plan.preempted:
-            if self._inflight is not None:
-                # a preempted row may be in the in-flight step: finalize first
-                pass
+            ls = st.extra.get("lease")
+            if ls is not None:
+                ls.mark_preempted(c)
 
     # ------------------------------------------------------------------ leases / watchdog
     def _process_leases(self):
+        """Advance every request's leases from its progress counters and end
+        the ones whose lease expired (typed cause on the terminal event)."""
+        if self._lease_cfg is None:
+            return
+        from .leases import TerminalCause
+
         c = self._clock()
-        cfg = self.cfg
-        if cfg.admission_timeout_s > 0:
-            for st in list(self.sched.waiting):
-                if c - st.extra.get("submit_clock", c) > cfg.admission_timeout_s:
-                    self._finish(st, FinishReason.DEADLINE, "admission lease expired")
-        if cfg.decode_progress_timeout_s > 0:
-            for st in list(self.sched.running):
-                last = st.extra.get("last_progress", st.extra.get("submit_clock", c))
-                if c - last > cfg.decode_progress_timeout_s:
-                    self._finish(st, FinishReason.DEADLINE, "progress lease expired")
+        for st in list(self.sched.running) + list(self.sched.waiting):
+            ls = st.extra.get("lease")
+            if ls is None:
+                continue
+            running = st in self.sched.running
+            if running:
+                ls.record_progress(c, st.num_computed, st.num_output)
+                if st.paused:
+                    ls.mark_paused(c)
+                else:
+                    ls.mark_resumed(c)
+            cause = ls.expired_cause(c, running)
+            if cause is not None:
+                self._finish(st, FinishReason.DEADLINE, TerminalCause.DIAGNOSTIC[cause], cause=cause)
+
+    def _rejected(self, req, cause: str) -> "RequestStream":
+        """A stream that ends at once (request refused at submission)."""
+        from .leases import TerminalCause
+        from .scheduler import RequestState
+
+        st = RequestState(req=req, seq=None, arrival=0)
+        st.status = Status.FINISHED
+        stream = RequestStream(self, st)
+        st.stream = stream
+        stream.put(Event(req.id, finished=True, finish_reason=FinishReason.DEADLINE, usage=st.usage,
+                         timing=st.timing, error=TerminalCause.DIAGNOSTIC[cause], cause=cause))
+        return stream
 
     def _watchdog(self):
         while not self._stop.wait(0.25):
@@ -521,7 +567,7 @@ class EngineV2:
                 for st in list(self.states.values()):
                     try:
                         ev = Event(st.req.id, finished=True, finish_reason=FinishReason.WATCHDOG, usage=st.usage,
-                                   timing=st.timing, error="engine step exceeded its timeout")
+                                   timing=st.timing, error="engine step exceeded its timeout", cause="watchdog")
                         st.status = Status.FINISHED
                         st.stream.put(ev)
                     except Exception:
@@ -568,6 +614,19 @@ class EngineV2:
             for st in list(self.states.values()):
                 self._finish(st, FinishReason.CANCELLED, "engine shutdown")
         self.background = False
+
+    def release_graphs(self):
+        """Drop the captured decode graphs and their memory pool. Graphs that
+        hold collective calls must go before the process group is destroyed,
+        or the exit waits on them."""
+        if self.graphs is not None and hasattr(self.graphs, "graphs"):
+            self.graphs.graphs.clear()
+            self.graphs.pool = None
+        if self.device.type == "cuda":
+            import gc
+
+            gc.collect()
+            torch.cuda.synchronize(self.device)
 
     def run_until_idle(self, max_steps: int = 1 << 30) -> list[Event]:
         events = []

@@ -72,6 +72,7 @@ class Request:
     lora: str | None = None  # adapter name
     ignore_eos: bool = False
     on_prefill_completed: Callable | None = None
+    first_token_deadline: Any = None  # engine.leases.FirstTokenDeadline (admission control)
 
 
 @dataclass
@@ -127,6 +128,7 @@ class Event:
     timing: RequestTiming | None = None
     logprobs: list[TokenLogprob] | None = None
     error: str | None = None
+    cause: str | None = None  # typed terminal cause (engine.leases.TerminalCause) of engine-ended requests
 
 
 @dataclass

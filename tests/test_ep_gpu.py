@@ -125,6 +125,8 @@ def _worker(rank, world, port, q, prompts):
                                                                             prefill_chunk_size=64),
                                                   max_model_len=256, use_cuda_graphs=graphs, graph_buckets=(2, 4)))
             outs.append(eng.generate(prompts, max_tokens=12))
+            eng.release_graphs()  # graphs hold NCCL calls: release before the group goes
+            del eng
         torch.cuda.synchronize()
         status |= _lib.read_status().get("ep", 0)
         ep.close()
@@ -152,10 +154,17 @@ def test_ep_two_ranks():
     ps = [ctx.Process(target=_worker, args=(r, 2, port, q, prompts)) for r in range(2)]
     for p in ps:
         p.start()
-    res = [q.get(timeout=300) for _ in range(2)]
-    for p in ps:
-        p.join(60)
-    assert all(p.exitcode == 0 for p in ps)
+    try:
+        res = [q.get(timeout=300) for _ in range(2)]
+    finally:
+        for p in ps:
+            p.join(60)
+            if p.is_alive():
+                p.kill()
+                p.join(10)
+    for rank, errs, status, outs in res:
+        print(rank, errs, status)
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
     for rank, errs, status, outs in res:
         assert status == 0, (rank, status)
         for e1, e2 in errs:
