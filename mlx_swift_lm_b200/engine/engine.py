@@ -179,6 +179,10 @@ class EngineV2:
         self.d2h_bytes = 0  # eager-path sampled tokens read back
         self.forward_shapes: list[tuple[int, int]] = []
         self.record_shapes = False
+        from .diagnostics import Diagnostics
+
+        d = Diagnostics()
+        self.diagnostics = d if d.profile else None  # opt-in (B200LM_STEP_PROFILE=1 or assign one)
 
     def enable_mtp(self, module, config=None):
         """Speculative decoding with an MTP draft module (greedy rows)."""
@@ -379,10 +383,13 @@ class EngineV2:
                     return events + self.step()
                 fb = self._build_batch(plan, self.device)
                 hid = None
+                dtok = self.diagnostics.begin_forward(self.device) if self.diagnostics is not None else None
                 if self.mtp is not None:
                     logits, hid = self.model.forward(fb, self.kv, return_both=True)
                 else:
                     logits = self.model.forward(fb, self.kv)
+                if self.diagnostics is not None:
+                    self.diagnostics.end_forward(dtok, self.steps, fb, logits)
                 srows = [r for r in plan.rows if r.sample]
                 if getattr(self.model, "pp_stages", 1) > 1:
                     toks, lp = self._pp_tokens(logits, srows)
@@ -681,6 +688,8 @@ class EngineV2:
                               pf_cu_q=torch.tensor([0, len(tokens)], dtype=torch.int32).to(dev),
                               pf_cu_q_host=[0, len(tokens)], pf_pos0=torch.tensor([0], dtype=torch.int32).to(dev),
                               pf_page_table=pt.to(dev))
+            if self.kv.rec is not None:
+                fb.state_slots = torch.tensor([st.seq.state_slot], dtype=torch.int32).to(dev)
             logits = self.model.forward(fb, self.kv)
             return logits.argmax(-1).tolist()
         finally:
