@@ -177,3 +177,90 @@ class TokenIterator:
                 drop = c.k[i].shape[0] - (limit - 1)
                 c.k[i] = torch.cat([c.k[i][:keep], c.k[i][keep + drop:]], 0)
                 c.v[i] = torch.cat([c.v[i][:keep], c.v[i][keep + drop:]], 0)
+
+
+class SpeculativeTokenIterator:
+    """Single-sequence speculative decoding with a draft model over dense KV
+    caches (parity: Evaluate.swift:1239-1715).
+
+    Each round the draft model proposes `num_draft` tokens greedily; the
+    target scores [last token, drafts] in one forward; drafts are accepted
+    while they equal the target's greedy token, then the target's own token
+    follows; both caches are trimmed back past the rejected positions.
+    Greedy (temperature 0) verification, so the output equals plain greedy
+    decoding of the target."""
+
+    def __init__(self, model, draft_model, prompt_tokens, params: GenerateParameters | None = None,
+                 num_draft: int = 2):
+        self.model, self.draft = model, draft_model
+        self.params = params or GenerateParameters(temperature=0.0)
+        self.k = num_draft
+        self.cache, self.dcache = model.new_cache(), draft_model.new_cache()
+        self.tokens = list(prompt_tokens)
+        self.n_generated = 0
+        self.drafted = self.accepted = 0
+        self._pending: list[int] = []
+        dev = model.device
+        toks = torch.tensor(self.tokens[:-1], dtype=torch.int64, device=dev)
+        if len(toks):  # both caches hold every token but the last
+            model.forward_dense(toks, self.cache)
+            draft_model.forward_dense(toks.to(draft_model.device), self.dcache)
+        self._last = self.tokens[-1]
+
+    @property
+    def acceptance_rate(self) -> float:
+        return self.accepted / self.drafted if self.drafted else 0.0
+
+    def __iter__(self):
+        return self
+
+    def _round(self):
+        dev, ddev = self.model.device, self.draft.device
+        drafts, t = [], self._last
+        for _ in range(self.k):
+            lg = self.draft.forward_dense(torch.tensor([t], device=ddev), self.dcache)[-1]
+            t = int(lg.argmax())
+            drafts.append(t)
+        seq = [self._last] + drafts
+        lg = self.model.forward_dense(torch.tensor(seq, device=dev), self.cache)
+        pred = lg.argmax(-1).tolist()  # target token after each position
+        a = 0
+        while a < self.k and drafts[a] == pred[a]:
+            a += 1
+        self.drafted += self.k
+        self.accepted += a
+        emit = drafts[:a] + [pred[a]]
+        # caches hold [last, d1..dk]; keep last + accepted drafts
+        self.cache.trim(self.k - a)
+        self.dcache.trim(max(0, self.dcache.offset - self.cache.offset))
+        if a == self.k:  # the draft cache lacks the last accepted draft
+            self.draft.forward_dense(torch.tensor([drafts[-1]], device=ddev), self.dcache)
+        self._last = emit[-1]
+        return emit
+
+    def __next__(self) -> int:
+        if self.params.max_tokens is not None and self.n_generated >= self.params.max_tokens:
+            raise StopIteration
+        if not self._pending:
+            self._pending = self._round()
+        tok = self._pending.pop(0)
+        self.tokens.append(tok)
+        self.n_generated += 1
+        return tok
+
+
+def generate_mtp(engine, prompt_tokens: list[int], params: GenerateParameters | None = None):
+    """One request through an engine with MTP speculative decoding enabled
+    (parity: MTPSpeculativeTokenIterator.swift:36-805, batch-1 MTP: backbone
+    forward, MTP draft head, batched verify). Returns (tokens, text, info,
+    telemetry) with the round's draft / acceptance counts."""
+    assert engine.mtp is not None, "enable MTP on the engine first (EngineV2.enable_mtp)"
+    s0 = engine.mtp.stats
+    before = (s0.rounds, s0.drafted, s0.accepted, s0.emitted)
+    params = params or GenerateParameters(temperature=0.0)
+    toks, text, info = generate(engine, prompt_tokens, params)
+    s1 = engine.mtp.stats
+    d = [a - b for a, b in zip((s1.rounds, s1.drafted, s1.accepted, s1.emitted), before)]
+    tele = {"rounds": d[0], "drafted": d[1], "accepted": d[2], "emitted": d[3],
+            "acceptance_rate": d[2] / d[1] if d[1] else 0.0}
+    return toks, text, info, tele

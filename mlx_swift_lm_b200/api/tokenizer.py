@@ -15,6 +15,9 @@ class ByteTokenizer:
     """ids 0..255 are bytes; specials follow."""
 
     SPECIALS = ["<|endoftext|>", "<|im_start|>", "<|im_end|>", "<think>", "</think>", "<tool_call>", "</tool_call>"]
+    # markup tokens stay in decoded text even with skip_special_tokens (as in
+    # the Qwen tokenizers, where they are added but not special tokens)
+    KEPT = {"<think>", "</think>", "<tool_call>", "</tool_call>"}
 
     def __init__(self, vocab_size: int = 512):
         self.vocab_size = max(vocab_size, 256 + len(self.SPECIALS))
@@ -48,8 +51,9 @@ class ByteTokenizer:
             else:
                 parts.append(buf.decode("utf-8", errors="replace"))
                 buf = bytearray()
-                if not skip_special_tokens and t in self.id_to_special:
-                    parts.append(self.id_to_special[t])
+                sp = self.id_to_special.get(t)
+                if sp is not None and (not skip_special_tokens or sp in self.KEPT):
+                    parts.append(sp)
         parts.append(buf.decode("utf-8", errors="replace"))
         return "".join(parts)
 
