@@ -122,17 +122,27 @@ class TokenIterator:
     """Legacy single-sequence iterator over a dense KV cache.
 
     Each ``next()`` returns the next token id. Prefill runs in
-    ``prefill_step_size`` chunks; with ``max_kv_size`` the cache keeps the
-    most recent ``max_kv_size`` tokens (rotating window, first tokens kept as
-    in the reference's RotatingKVCache)."""
+    ``prefill_step_size`` chunks; ``max_kv_size`` selects a rotating window
+    cache (the first tokens kept, as the reference's RotatingKVCache) and
+    ``kv_bits`` an affine-quantised cache (:mod:`..kv.legacy`)."""
 
     def __init__(self, model, prompt_tokens, params: GenerateParameters | None = None, cache=None):
         from ..engine.sampler import row_key
         from ..ops import reference as ref
 
+        from ..kv.legacy import QuantizedKVCache, RotatingKVCache
+
         self.model = model
         self.params = params or GenerateParameters()
-        self.cache = cache or model.new_cache()
+        p = self.params
+        if cache is None:
+            if p.max_kv_size:
+                cache = RotatingKVCache(model.cfg.num_layers, p.max_kv_size)
+            elif p.kv_bits:
+                cache = QuantizedKVCache(model.cfg.num_layers, p.kv_bits, p.kv_group_size)
+            else:
+                cache = model.new_cache()
+        self.cache = cache
         self.tokens = list(prompt_tokens)
         self.n_generated = 0
         self._ref = ref
@@ -163,20 +173,8 @@ class TokenIterator:
         tok = self._sample(self._logits)
         self.tokens.append(tok)
         self.n_generated += 1
-        if self.params.max_kv_size and self.cache.offset >= self.params.max_kv_size:
-            self._rotate()
         self._logits = self.model.forward_dense(torch.tensor([tok], device=self.model.device), self.cache)[-1]
         return tok
-
-    def _rotate(self, keep: int = 4):
-        """Drop the oldest tokens past the window, keeping the first `keep`."""
-        c = self.cache
-        limit = self.params.max_kv_size
-        for i in range(len(c.k)):
-            if c.k[i] is not None and c.k[i].shape[0] > limit - 1:
-                drop = c.k[i].shape[0] - (limit - 1)
-                c.k[i] = torch.cat([c.k[i][:keep], c.k[i][keep + drop:]], 0)
-                c.v[i] = torch.cat([c.v[i][:keep], c.v[i][keep + drop:]], 0)
 
 
 class SpeculativeTokenIterator:

@@ -40,6 +40,7 @@ class EngineConfig:
     scheduler: SchedulerConfig = field(default_factory=SchedulerConfig)
     kv_tokens: int | None = None  # pool size in tokens (default: enough for max_concurrent * max_model_len)
     kv_bytes: int | None = None
+    kv_memory_fraction: float | None = None  # CUDA: size the pool to this fraction of the HBM left after weights
     kv_fp8: bool = False
     max_model_len: int = 8192
     use_cuda_graphs: bool = True
@@ -133,6 +134,10 @@ class EngineV2:
         kv_tokens = self.cfg.kv_tokens or sc.max_concurrent_requests * self.cfg.max_model_len
         # recurrent-state slots (hybrid models): every running request holds one
         seqs = sc.max_concurrent_requests
+        if self.cfg.kv_memory_fraction and self.device.type == "cuda" and self.cfg.kv_bytes is None:
+            from ..kv.memory import kv_budget_bytes
+
+            self.cfg.kv_bytes = kv_budget_bytes(self.device, self.cfg.kv_memory_fraction)
         if self.cfg.kv_bytes is not None:
             self.kv = PagedKVCache.for_model(model, kv_bytes=self.cfg.kv_bytes, kv_fp8=self.cfg.kv_fp8, max_seqs=seqs)
         else:

@@ -525,9 +525,13 @@ class DecoderLM:
                 q, k, v = ops.qk_norm_rope_kv(qkv, positions, None, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
                                               L.q_norm, L.k_norm, cfg.rms_norm_eps, None, None, self.H, self.KVH,
                                               self.D, return_kv=True)
-                kk, vv = cache.update(li, k, v)
+                ki = self.kv_index[li] if self.kv_index else li
+                kk, vv = cache.update(ki, k, v)
+                kpos = cache.key_positions(ki) if hasattr(cache, "key_positions") else None
+                extra = cache.chunk_mask if hasattr(cache, "chunk_mask") else None
                 a = ref.attention_rows_ref(q.float(), kk.float(), vv.float(), positions, kk.shape[0], cfg.scale,
-                                           cfg.window(li), L.sinks, cfg.attn_logit_softcap).to(x.dtype)
+                                           cfg.window(li), L.sinks, cfg.attn_logit_softcap, k_pos=kpos,
+                                           extra_mask=extra).to(x.dtype)
                 a2 = a.reshape(Lq, self.H * self.D).contiguous()
                 if cfg.attn_output_gate:
                     from ..ops.gdn import sigmoid_mul

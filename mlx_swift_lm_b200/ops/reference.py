@@ -159,7 +159,8 @@ def gather_pages(cache, page_ids, n_tokens, scale=None):
     return x
 
 
-def attention_rows_ref(q, k, v, q_pos, kv_len, scale, window=0, sinks=None, softcap=0.0):
+def attention_rows_ref(q, k, v, q_pos, kv_len, scale, window=0, sinks=None, softcap=0.0, k_pos=None,
+                       extra_mask=None):
     """q [Tq, H, D] float at absolute positions q_pos [Tq]; k,v [kv_len, KVH, D].
     Causal with optional sliding window (window > 0); window < 0 is
     bidirectional over all kv_len keys (encoders). Sinks are
@@ -172,9 +173,11 @@ def attention_rows_ref(q, k, v, q_pos, kv_len, scale, window=0, sinks=None, soft
     s = torch.einsum("thd,lhd->thl", q.float(), kk.float()) * scale
     if softcap > 0:
         s = softcap * torch.tanh(s / softcap)
-    kp = torch.arange(kv_len, device=q.device)
+    kp = torch.arange(kv_len, device=q.device) if k_pos is None else k_pos.to(q.device).long()
     qp = q_pos.to(q.device).long()[:, None]
     mask = kp[None, :] <= qp
+    if extra_mask is not None:  # e.g. chunked attention: same chunk only
+        mask = mask & extra_mask(qp[:, 0], kp)
     if window < 0:
         mask = torch.ones_like(mask)
     if window > 0:
