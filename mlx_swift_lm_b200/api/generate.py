@@ -40,6 +40,7 @@ class GenerateParameters:
     stop: list[str] = field(default_factory=list)
     kv_bits: int | None = None  # quantized legacy KV (affine 4/8)
     kv_group_size: int = 64
+    kv_scheme: str | None = None  # KV compression (kv.compress): affine4/8, turbo<K>v<V>, varn<K>v<V>[t32|t64]
 
     def sampling(self) -> SamplingParams:
         return SamplingParams(temperature=self.temperature, top_p=self.top_p, top_k=self.top_k, min_p=self.min_p,
@@ -136,7 +137,11 @@ class TokenIterator:
         self.params = params or GenerateParameters()
         p = self.params
         if cache is None:
-            if p.max_kv_size:
+            if p.kv_scheme:
+                from ..kv.compress import CompressedKVCache
+
+                cache = CompressedKVCache(model.cfg.num_layers, p.kv_scheme)
+            elif p.max_kv_size:
                 cache = RotatingKVCache(model.cfg.num_layers, p.max_kv_size)
             elif p.kv_bits:
                 cache = QuantizedKVCache(model.cfg.num_layers, p.kv_bits, p.kv_group_size)
