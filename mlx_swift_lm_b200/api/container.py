@@ -90,14 +90,27 @@ class ModelContainer:
             return self.encode(prompt)
         return list(prompt)
 
-    # ------------------------------------------------------------------ generation
-    def generate(self, prompt=None, messages=None, params: GenerateParameters | None = None, tools=None):
-        toks = self.prepare(prompt, messages, tools)
-        return generate(self.engine, toks, params)
+    def prepare_media(self, toks: list[int], images=None, videos=None):
+        """Vision-language models: expand the image / video placeholders of
+        `toks` and encode the media (models.vlm.Qwen2VLModel.prepare)."""
+        if not images and not videos:
+            return toks, None
+        if not hasattr(self.model, "prepare"):
+            raise ValueError(f"{type(self.model).__name__} takes no image or video input")
+        from .media import MediaInput
 
-    def stream(self, prompt=None, messages=None, params: GenerateParameters | None = None, tools=None):
-        toks = self.prepare(prompt, messages, tools)
-        yield from generate_stream(self.engine, toks, params)
+        return self.model.prepare(toks, MediaInput(list(images or []), list(videos or [])))
+
+    # ------------------------------------------------------------------ generation
+    def generate(self, prompt=None, messages=None, params: GenerateParameters | None = None, tools=None, images=None,
+                 videos=None):
+        toks, mm = self.prepare_media(self.prepare(prompt, messages, tools), images, videos)
+        return generate(self.engine, toks, params, mm=mm)
+
+    def stream(self, prompt=None, messages=None, params: GenerateParameters | None = None, tools=None, images=None,
+               videos=None):
+        toks, mm = self.prepare_media(self.prepare(prompt, messages, tools), images, videos)
+        yield from generate_stream(self.engine, toks, params, mm=mm)
 
     # ------------------------------------------------------------------ embeddings
     @torch.no_grad()

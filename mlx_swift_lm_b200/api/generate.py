@@ -79,12 +79,14 @@ class Generation:
 
 
 def generate_stream(engine, prompt_tokens: list[int], params: GenerateParameters | None = None, stop_tokens=(),
-                    token_constraint=None):
-    """Yield :class:`Generation` events for one request through the engine."""
+                    token_constraint=None, mm=None):
+    """Yield :class:`Generation` events for one request through the engine
+    (`mm`: the multimodal payload of a vision-language prompt)."""
     params = params or GenerateParameters()
     max_tokens = params.max_tokens or (engine.cfg.max_model_len - len(prompt_tokens))
     req = Request(prompt_tokens=list(prompt_tokens), max_tokens=max_tokens, sampling=params.sampling(),
-                  stop_tokens=set(stop_tokens), stop_strings=list(params.stop), token_constraint=token_constraint)
+                  stop_tokens=set(stop_tokens), stop_strings=list(params.stop), token_constraint=token_constraint,
+                  mm=mm)
     t0 = time.perf_counter()
     stream = engine.submit(req)
     n = 0

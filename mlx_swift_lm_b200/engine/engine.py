@@ -208,6 +208,10 @@ class EngineV2:
             raise ValueError(f"prompt + max_tokens = {total} exceeds max_model_len {self.cfg.max_model_len}")
         if not self.sched.can_ever_fit(total):
             raise ValueError("request can never fit in the KV pool")
+        if req.mm is not None:
+            # placeholder token ids do not identify the image: no prefix reuse;
+            # MTP drafts from text positions only
+            req.prefix_cache_enabled = False
         with self._lock:
             ftd = req.first_token_deadline
             if ftd is not None:
@@ -251,7 +255,12 @@ class EngineV2:
             st = r.state
             toks = st.all_tokens[r.start:r.start + r.num_tokens]
             ids.extend(toks)
-            pos.extend(range(r.start, r.start + r.num_tokens))
+            mm = st.req.mm
+            if mm is None:
+                pos.extend(range(r.start, r.start + r.num_tokens))
+            else:  # generated tokens of a multimodal prompt continue at p + delta (M-RoPE)
+                pos.extend(p + (mm["delta"] if p >= mm["prompt_len"] else 0)
+                           for p in range(r.start, r.start + r.num_tokens))
             slots.extend(st.seq.slots(r.start, r.num_tokens))
         T = len(ids)
         fb = ForwardBatch(input_ids=torch.tensor(ids, dtype=torch.int32), positions=torch.tensor(pos, dtype=torch.int32),
@@ -291,6 +300,8 @@ class EngineV2:
             fb.logit_idx = torch.tensor(logit_idx, dtype=torch.int64)
             fb.logit_idx_host = logit_idx
         fb.row_ranks = self._row_ranks(rows)
+        fb.row_states = [r.state for r in rows]
+        fb.pf_pos0_host = [r.start for r in rows[nd:]]
         if self.kv.rec is not None:
             fb.state_slots = torch.tensor([r.state.seq.state_slot for r in rows], dtype=torch.int32)
         if dev.type == "cuda":

@@ -197,7 +197,8 @@ class DecodeGraphRunner:
             i = where[i0]
             st = r.state
             p = r.start
-            a[self.o_pos + i] = p
+            mm = st.req.mm
+            a[self.o_pos + i] = p + (mm["delta"] if mm is not None and p >= mm["prompt_len"] else 0)
             a[self.o_sl + i] = p + 1
             slots[i] = st.seq.slot(p)
             if self.rec is not None:

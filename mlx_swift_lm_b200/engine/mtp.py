@@ -94,7 +94,7 @@ class MTPDriver:
             st = r.state
             sp = st.req.sampling
             if (not sp.greedy or st.req.token_constraint is not None or sp.logprobs or sp.top_logprobs > 0
-                    or sp.needs_processing or "mtp_h" not in st.extra):
+                    or sp.needs_processing or "mtp_h" not in st.extra or st.req.mm is not None):
                 return False
         return True
 

@@ -73,6 +73,7 @@ class Request:
     ignore_eos: bool = False
     on_prefill_completed: Callable | None = None
     first_token_deadline: Any = None  # engine.leases.FirstTokenDeadline (admission control)
+    mm: Any = None  # multimodal payload of a vision-language prompt (models.vlm.Qwen2VLModel.prepare)
 
 
 @dataclass

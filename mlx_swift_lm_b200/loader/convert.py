@@ -185,6 +185,24 @@ def quantize_tensors(tensors: dict, bits: int = 4, group_size: int = 64, dtype=t
     return out
 
 
+def export_vision_tensors(model) -> dict:
+    """HF names (``visual.*``) of a Qwen2-VL vision tower."""
+    v = model.vision
+    out = {"visual.patch_embed.proj.weight": v.patch_w.detach().float().cpu().reshape(
+        v.cfg.embed_dim, v.cfg.in_chans, v.cfg.temporal_patch_size, v.cfg.patch_size, v.cfg.patch_size)}
+    names = {"norm1_w": "norm1.weight", "norm1_b": "norm1.bias", "norm2_w": "norm2.weight", "norm2_b": "norm2.bias",
+             "qkv_w": "attn.qkv.weight", "qkv_b": "attn.qkv.bias", "proj_w": "attn.proj.weight",
+             "proj_b": "attn.proj.bias", "fc1_w": "mlp.fc1.weight", "fc1_b": "mlp.fc1.bias", "fc2_w": "mlp.fc2.weight",
+             "fc2_b": "mlp.fc2.bias"}
+    for i, b in enumerate(v.blocks):
+        for s, n in names.items():
+            out[f"visual.blocks.{i}.{n}"] = getattr(b, s).detach().float().cpu()
+    for s, n in (("ln_q_w", "ln_q.weight"), ("ln_q_b", "ln_q.bias"), ("m1_w", "mlp.0.weight"), ("m1_b", "mlp.0.bias"),
+                 ("m2_w", "mlp.2.weight"), ("m2_b", "mlp.2.bias")):
+        out[f"visual.merger.{n}"] = getattr(v, s).detach().float().cpu()
+    return out
+
+
 def save_model(model, path: str, quantize: dict | None = None, dtype=torch.bfloat16, shard_bytes: int = 5 << 30):
     """Write config.json + model(-NNNNN-of-NNNNN).safetensors (+ index) for `model`."""
     os.makedirs(path, exist_ok=True)
@@ -194,9 +212,20 @@ def save_model(model, path: str, quantize: dict | None = None, dtype=torch.bfloa
         qcfg = {"group_size": int(quantize.get("group_size", 64)), "bits": int(quantize.get("bits", 4)),
                 "mode": "affine"}
         tensors = quantize_tensors(tensors, qcfg["bits"], qcfg["group_size"], dtype)
+    hfc = to_hf_config(model.cfg, qcfg)
+    if getattr(model, "vision", None) is not None:  # Qwen2-VL: the tower stays unquantised
+        tensors.update(export_vision_tensors(model))
+        vc = model.vision.cfg
+        hfc.update(vision_config={"depth": vc.depth, "embed_dim": vc.embed_dim, "num_heads": vc.num_heads,
+                                  "mlp_ratio": vc.mlp_ratio, "patch_size": vc.patch_size,
+                                  "temporal_patch_size": vc.temporal_patch_size,
+                                  "spatial_merge_size": vc.spatial_merge_size, "in_chans": vc.in_chans,
+                                  "hidden_size": vc.hidden_size},
+                   image_token_id=model.image_token_id, video_token_id=model.video_token_id,
+                   rope_scaling={"type": "mrope", "mrope_section": list(model.mrope_section)})
     tensors = {k: (v.to(dtype) if v.is_floating_point() else v) for k, v in tensors.items()}
     with open(os.path.join(path, "config.json"), "w") as f:
-        json.dump(to_hf_config(model.cfg, qcfg), f, indent=2)
+        json.dump(hfc, f, indent=2)
     write_shards(tensors, path, shard_bytes)
 
 

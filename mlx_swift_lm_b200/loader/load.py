@@ -242,7 +242,24 @@ def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParalle
         setattr(cfg, k, v)
     tensors, _ = load_safetensors(path)
     model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized)
+    if hf.get("vision_config") and hf.get("model_type") == "qwen2_vl":
+        model = _attach_vision(model, cfg, hf, tensors, device, dtype)
     return model, hf
+
+
+def _attach_vision(lm, cfg, hf, tensors, device, dtype):
+    """Qwen2-VL: the loaded language model plus its vision tower
+    (``visual.*`` / ``model.visual.*``) as one :class:`Qwen2VLModel`."""
+    from ..models.vision import QwenVisionTower, VisionConfig
+    from ..models.vlm import Qwen2VLModel
+
+    rs = hf.get("rope_scaling") or (hf.get("text_config") or {}).get("rope_scaling") or {}
+    vcfg = VisionConfig.from_hf(hf["vision_config"], cfg.hidden_size)
+    m = Qwen2VLModel(cfg, vcfg, device, dtype, hf.get("image_token_id", 151655), hf.get("video_token_id", 151656),
+                     rs.get("mrope_section", (16, 24, 24)))
+    m.embed, m.norm, m.lm_head, m.layers = lm.embed, lm.norm, lm.lm_head, lm.layers
+    m.vision = QwenVisionTower.from_tensors(vcfg, tensors, device, dtype)
+    return m
 
 
 def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=torch.float32, tp=None,

@@ -37,6 +37,11 @@ class ForwardBatch:
     row_ranks: list | None = None
     # recurrent-state slot of each row (hybrid models with linear-attention layers)
     state_slots: torch.Tensor | None = None  # [rows] int32
+    # engine request state of each row (host; multimodal models read Request.mm)
+    row_states: list | None = None
+    pf_pos0_host: list | None = None
+    # per-token rotary cos|sin table [T, rot_dim] replacing the position lookup (M-RoPE prompts)
+    rope_table: torch.Tensor | None = None
 
     @property
     def num_tokens(self) -> int:

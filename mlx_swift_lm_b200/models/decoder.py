@@ -390,7 +390,11 @@ class DecoderLM:
         ki = self.kv_index[li] if self.kv_index else li
         qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
         kc, vc = kv.layer(ki)
-        q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
+        cos_sin, positions = self.cos_sin, fb.positions
+        if fb.rope_table is not None:  # per-token rotary rows (M-RoPE prompts)
+            cos_sin = fb.rope_table
+            positions = torch.arange(T, dtype=torch.int32, device=fb.positions.device)
+        q = ops.qk_norm_rope_kv(qkv, positions, fb.slots, cos_sin, self.rot_dim, cfg.rope_interleaved,
                                 L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
                                 kv.k_scale(ki), kv.v_scale(ki))
         win = cfg.window(li)

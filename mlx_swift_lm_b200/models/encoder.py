@@ -81,6 +81,23 @@ class EncoderConfig:
         return c
 
 
+def scratch_layout(lens: list[int], device):
+    """Page table [R, max pages] and K/V slots [T] placing each of R
+    sequences of `lens` tokens on its own consecutive scratch pages; returns
+    (page_table, slots, cu, pages)."""
+    npg = [(n + PAGE - 1) // PAGE for n in lens]
+    pt = torch.zeros(len(lens), max(npg), dtype=torch.int32)
+    T = sum(lens)
+    slots = torch.empty(T, dtype=torch.int64)
+    cu, p = [0], 0
+    for r, n in enumerate(lens):
+        pt[r, :npg[r]] = torch.arange(p, p + npg[r])
+        slots[cu[-1]:cu[-1] + n] = torch.arange(n) + p * PAGE
+        cu.append(cu[-1] + n)
+        p += npg[r]
+    return pt.to(device), slots.to(device), cu, p
+
+
 class EncoderLayer:
     __slots__ = ("wqkv", "bqkv", "wo", "bo", "ln1_w", "ln1_b", "w1", "b1", "w2", "b2", "ln2_w", "ln2_b")
 
@@ -180,19 +197,10 @@ class EncoderModel:
             x = (x.float() + self.type[tt.long()].float()).to(self.dtype)
         x = ops.add_layernorm(x.contiguous(), None, self.emb_ln_w, self.emb_ln_b, cfg.layer_norm_eps)
         # scratch pages: each sequence on its own consecutive pages
-        npg = [(n + PAGE - 1) // PAGE for n in lens]
-        maxp = max(npg)
-        pt = torch.zeros(R, maxp, dtype=torch.int32)
-        slots = torch.empty(T, dtype=torch.int64)
-        p = 0
-        for r, n in enumerate(lens):
-            pt[r, :npg[r]] = torch.arange(p, p + npg[r])
-            slots[cu[r]:cu[r + 1]] = torch.arange(n) + p * PAGE
-            p += npg[r]
+        pt, slots, _, p = scratch_layout(lens, dev)
         NH, D = cfg.num_heads, cfg.head_dim
         kc = torch.zeros(p, NH, PAGE, D, dtype=self.dtype, device=dev)
         vc = torch.zeros_like(kc)
-        pt, slots = pt.to(dev), slots.to(dev)
         cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
         pos0 = torch.zeros(R, dtype=torch.int32, device=dev)
         scale = 1.0 / math.sqrt(D)

@@ -72,7 +72,7 @@ def build_rope(head_dim: int, base: float, scaling: dict | None, max_pos: int, p
     rot -= rot % 2
     mscale = 1.0
     kind = (scaling or {}).get("rope_type", (scaling or {}).get("type", "default")) if scaling else "default"
-    if kind in ("default", None):
+    if kind in ("default", None, "mrope"):  # mrope: the 1-D table of text positions (sections equal)
         inv = default_inv_freq(rot, base)
     elif kind == "linear":
         inv = default_inv_freq(rot, base) / float(scaling["factor"])

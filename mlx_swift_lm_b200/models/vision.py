@@ -1,0 +1,197 @@
+"""Qwen2-VL vision tower on the decoder's kernels.
+
+Parity: MLXVLM/Models/Qwen2VL.swift:513-790 and QwenVL.swift:90-160 -
+patch embedding (a Conv3d whose kernel equals its stride, i.e. one linear map
+of each flattened [C, t, p, p] patch), pre-norm blocks (LayerNorm, fused qkv
+with bias, 2-D rotary embedding over (row, column) patch positions with
+rotate-half, bidirectional attention within each frame, quick-GELU MLP) and
+the patch merger (LayerNorm, 2x2 neighbouring patches concatenated, GELU
+MLP into the language model's hidden size).
+
+B200 path: GEMMs with bias / GELU epilogues, the fused residual + LayerNorm
+kernel, and the tensor-core paged prefill kernel in bidirectional mode over
+a scratch page pool (one row per frame). The 2-D rotary angles of every
+patch are tabulated per token and handed to the qk/RoPE/KV-write kernel as
+its cos/sin table with positions 0..N-1.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from ..kv.paged import PAGE
+from .encoder import scratch_layout
+
+
+@dataclass
+class VisionConfig:
+    depth: int = 32
+    embed_dim: int = 1280
+    num_heads: int = 16
+    mlp_ratio: float = 4.0
+    patch_size: int = 14
+    temporal_patch_size: int = 2
+    spatial_merge_size: int = 2
+    in_chans: int = 3
+    hidden_size: int = 3584  # language model hidden size (merger output)
+    eps: float = 1e-6
+
+    @property
+    def head_dim(self) -> int:
+        return self.embed_dim // self.num_heads
+
+    @property
+    def patch_dim(self) -> int:
+        return self.in_chans * self.temporal_patch_size * self.patch_size * self.patch_size
+
+    @classmethod
+    def from_hf(cls, vc: dict, text_hidden: int) -> "VisionConfig":
+        return cls(depth=vc.get("depth", 32), embed_dim=vc.get("embed_dim", 1280), num_heads=vc.get("num_heads", 16),
+                   mlp_ratio=vc.get("mlp_ratio", 4.0), patch_size=vc.get("patch_size", 14),
+                   temporal_patch_size=vc.get("temporal_patch_size", 2),
+                   spatial_merge_size=vc.get("spatial_merge_size", 2), in_chans=vc.get("in_chans", 3),
+                   hidden_size=vc.get("hidden_size", text_hidden))
+
+
+class VisionBlock:
+    __slots__ = ("norm1_w", "norm1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "norm2_w", "norm2_b", "fc1_w", "fc1_b",
+                 "fc2_w", "fc2_b")
+
+    def __init__(self):
+        for s in self.__slots__:
+            setattr(self, s, None)
+
+
+class QwenVisionTower:
+    def __init__(self, cfg: VisionConfig, device="cpu", dtype=torch.float32):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.patch_w = None
+        self.blocks: list[VisionBlock] = []
+        self.ln_q_w = self.ln_q_b = None
+        self.m1_w = self.m1_b = self.m2_w = self.m2_b = None
+        d = cfg.head_dim // 2
+        self.inv_freq = 1.0 / (10000.0 ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
+
+    def init_random(self, seed: int = 0, std: float = 0.02):
+        c = self.cfg
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        E, F = c.embed_dim, int(c.embed_dim * c.mlp_ratio)
+        M = E * c.spatial_merge_size ** 2
+
+        def rn(*shape):
+            return torch.empty(shape, device=self.device, dtype=self.dtype).normal_(0.0, std, generator=g)
+
+        def ones(n):
+            return torch.ones(n, device=self.device, dtype=self.dtype)
+
+        self.patch_w = rn(E, c.patch_dim)
+        self.blocks = []
+        for _ in range(c.depth):
+            b = VisionBlock()
+            b.norm1_w, b.norm1_b, b.norm2_w, b.norm2_b = ones(E), rn(E), ones(E), rn(E)
+            b.qkv_w, b.qkv_b = rn(3 * E, E), rn(3 * E)
+            b.proj_w, b.proj_b = rn(E, E), rn(E)
+            b.fc1_w, b.fc1_b, b.fc2_w, b.fc2_b = rn(F, E), rn(F), rn(E, F), rn(E)
+            self.blocks.append(b)
+        self.ln_q_w, self.ln_q_b = ones(E), rn(E)
+        self.m1_w, self.m1_b, self.m2_w, self.m2_b = rn(M, M), rn(M), rn(c.hidden_size, M), rn(c.hidden_size)
+        return self
+
+    def tensors(self):
+        for n in ("patch_w", "ln_q_w", "ln_q_b", "m1_w", "m1_b", "m2_w", "m2_b"):
+            yield n, getattr(self, n)
+        for i, b in enumerate(self.blocks):
+            for s in VisionBlock.__slots__:
+                yield f"blocks.{i}.{s}", getattr(b, s)
+
+    def to(self, device, dtype):
+        self.device, self.dtype = torch.device(device), dtype
+        for n, v in list(self.tensors()):
+            if v is None:
+                continue
+            if n.startswith("blocks."):
+                _, i, s = n.split(".")
+                setattr(self.blocks[int(i)], s, v.to(self.device, dtype).contiguous())
+            else:
+                setattr(self, n, v.to(self.device, dtype).contiguous())
+        return self
+
+    # ------------------------------------------------------------------ positions
+    def rotary_table(self, grids: list[tuple[int, int, int]]) -> torch.Tensor:
+        """Per-patch cos | sin [N, head_dim] fp32 in patchify order: angles of
+        the row position on the first quarter of the frequencies and of the
+        column position on the second (rotate-half over the head)."""
+        m = self.cfg.spatial_merge_size
+        hs, ws = [], []
+        for t, h, w in grids:
+            hp = torch.arange(h)[:, None].expand(h, w).reshape(h // m, m, w // m, m).permute(0, 2, 1, 3).reshape(-1)
+            wp = torch.arange(w)[None, :].expand(h, w).reshape(h // m, m, w // m, m).permute(0, 2, 1, 3).reshape(-1)
+            hs.append(hp.repeat(t))
+            ws.append(wp.repeat(t))
+        hp, wp = torch.cat(hs).double(), torch.cat(ws).double()
+        ang = torch.cat([hp[:, None] * self.inv_freq[None], wp[:, None] * self.inv_freq[None]], -1)
+        return torch.cat([ang.cos(), ang.sin()], -1).float().to(self.device)
+
+    # ------------------------------------------------------------------ forward
+    @torch.no_grad()
+    def forward(self, patches: torch.Tensor, grids: list[tuple[int, int, int]]) -> torch.Tensor:
+        """patches [N, C*tp*p*p] -> merged embeddings [N / merge^2, hidden]."""
+        c = self.cfg
+        dev, E, NH, D = self.device, c.embed_dim, c.num_heads, c.head_dim
+        x = ops.gemm(patches.to(dev, self.dtype).contiguous(), self.patch_w)
+        N = x.shape[0]
+        lens = [h * w for t, h, w in grids for _ in range(t)]  # attention within each frame
+        pt, slots, cu, npages = scratch_layout(lens, dev)
+        kc = torch.zeros(npages, NH, PAGE, D, dtype=self.dtype, device=dev)
+        vc = torch.zeros_like(kc)
+        cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+        pos0 = torch.zeros(len(lens), dtype=torch.int32, device=dev)
+        table = self.rotary_table(grids)
+        tok = torch.arange(N, dtype=torch.int32, device=dev)
+        delta = None
+        for b in self.blocks:
+            h = ops.add_layernorm(x, delta, b.norm1_w, b.norm1_b, c.eps)
+            qkv = ops.gemm(h, b.qkv_w, bias=b.qkv_b)
+            q = ops.qk_norm_rope_kv(qkv, tok, slots, table, D, False, None, None, c.eps, kc, vc, NH, NH, D)
+            a = ops.paged_prefill(q, kc, vc, pt, cu_t, pos0, D ** -0.5, -1, cu_q_host=cu)
+            d = ops.gemm(a.reshape(N, E), b.proj_w, bias=b.proj_b)
+            h = ops.add_layernorm(x, d, b.norm2_w, b.norm2_b, c.eps)
+            delta = ops.gemm(ops.gemm(h, b.fc1_w, epi="quick_gelu", bias=b.fc1_b), b.fc2_w, bias=b.fc2_b)
+        hq = ops.add_layernorm(x, delta, self.ln_q_w, self.ln_q_b, c.eps)
+        hq = hq.reshape(N // c.spatial_merge_size ** 2, -1).contiguous()
+        return ops.gemm(ops.gemm(hq, self.m1_w, epi="gelu", bias=self.m1_b), self.m2_w, bias=self.m2_b)
+
+    # ------------------------------------------------------------------ loading
+    @classmethod
+    def from_tensors(cls, cfg: VisionConfig, t: dict, device="cpu", dtype=torch.float32) -> "QwenVisionTower":
+        pre = next((p for p in ("visual.", "model.visual.", "vision_tower.") if p + "patch_embed.proj.weight" in t),
+                   None)
+        if pre is None:
+            raise KeyError("no Qwen VL vision tower weights (visual.patch_embed.proj.weight)")
+        m = cls(cfg)
+
+        def g(n):
+            return t[pre + n].float()
+
+        w = g("patch_embed.proj.weight")
+        if w.dim() == 5 and w.shape[-1] == cfg.in_chans:  # MLX layout [out, t, p, p, C]
+            w = w.permute(0, 4, 1, 2, 3)
+        m.patch_w = w.reshape(w.shape[0], -1)
+        for i in range(cfg.depth):
+            p = f"blocks.{i}."
+            b = VisionBlock()
+            b.norm1_w, b.norm1_b = g(p + "norm1.weight"), g(p + "norm1.bias")
+            b.norm2_w, b.norm2_b = g(p + "norm2.weight"), g(p + "norm2.bias")
+            b.qkv_w, b.qkv_b = g(p + "attn.qkv.weight"), g(p + "attn.qkv.bias")
+            b.proj_w, b.proj_b = g(p + "attn.proj.weight"), g(p + "attn.proj.bias")
+            b.fc1_w, b.fc1_b = g(p + "mlp.fc1.weight"), g(p + "mlp.fc1.bias")
+            b.fc2_w, b.fc2_b = g(p + "mlp.fc2.weight"), g(p + "mlp.fc2.bias")
+            m.blocks.append(b)
+        m.ln_q_w, m.ln_q_b = g("merger.ln_q.weight"), g("merger.ln_q.bias")
+        m.m1_w, m.m1_b = g("merger.mlp.0.weight"), g("merger.mlp.0.bias")
+        m.m2_w, m.m2_b = g("merger.mlp.2.weight"), g("merger.mlp.2.bias")
+        return m.to(device, dtype)

@@ -49,7 +49,7 @@ def glu_act_ref(epi, g, u):
 
 def gemm_ref(x, w, epi="none", residual=None, out_dtype=None, bias=None):
     """y = epi(x @ w.T + bias) computed in fp32.
-    epi: none | swiglu | geglu | swiglu_oai | f32 | add | gelu | gelu_tanh."""
+    epi: none | swiglu | geglu | swiglu_oai | f32 | add | gelu | gelu_tanh | quick_gelu."""
     acc = x.float() @ w.float().t()
     if bias is not None:
         acc = acc + bias.float()
@@ -67,6 +67,8 @@ def gemm_ref(x, w, epi="none", residual=None, out_dtype=None, bias=None):
         return (acc.to(x.dtype).float() + residual.float()).to(dt)
     if epi in ("gelu", "gelu_tanh"):
         return torch.nn.functional.gelu(acc, approximate="tanh" if epi == "gelu_tanh" else "none").to(dt)
+    if epi == "quick_gelu":
+        return (acc * torch.sigmoid(1.702 * acc)).to(dt)
     return acc.to(dt)
 
 

@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import asyncio
 import json
+import os
 import time
 import uuid
 
@@ -78,6 +79,21 @@ def validate_sampling(body: dict) -> SamplingParams:
                           logprobs=bool(body.get("logprobs")) or bool(top_lp))
 
 
+def _decode_image(url: str):
+    """A data: URL (base64) or a local file path -> an RGB PIL image. This
+    server never fetches remote URLs."""
+    import base64
+    import io
+
+    from PIL import Image
+
+    if isinstance(url, str) and url.startswith("data:"):
+        return Image.open(io.BytesIO(base64.b64decode(url.split(",", 1)[1]))).convert("RGB")
+    if isinstance(url, str) and os.path.exists(url):
+        return Image.open(url).convert("RGB")
+    raise ValidationError("image_url must be a data: URL or a local file path")
+
+
 class OpenAIService:
     def __init__(self, container, model_name: str = None, tool_parser: str | None = None,
                  reasoning_parser: str | None = None, embedder=None, default_max_tokens: int = 512,
@@ -110,14 +126,37 @@ class OpenAIService:
             return None
         return self.constraint_factory(rf)
 
-    def _submit(self, tokens, body, sampling):
+    def _submit(self, tokens, body, sampling, mm=None):
         stop = body.get("stop") or []
         if isinstance(stop, str):
             stop = [stop]
         req = Request(prompt_tokens=list(tokens), max_tokens=self._max_tokens(body, len(tokens)), sampling=sampling,
                       stop_strings=list(stop), token_constraint=self._constraint(body),
-                      cache_salt=body.get("cache_salt"))
+                      cache_salt=body.get("cache_salt"), mm=mm)
         return self.engine.submit(req)
+
+    @staticmethod
+    def _split_images(msgs: list) -> tuple[list, list]:
+        """OpenAI image parts (``image_url`` with a data: URL or a local path)
+        -> ``{"type": "image"}`` parts for the chat template, plus the decoded
+        images in order."""
+        images, out = [], []
+        for m in msgs:
+            c = m.get("content")
+            if not isinstance(c, list):
+                out.append(m)
+                continue
+            parts = []
+            for p in c:
+                if isinstance(p, dict) and p.get("type") in ("image_url", "input_image", "image"):
+                    url = p.get("image_url")
+                    url = url.get("url") if isinstance(url, dict) else url or p.get("url") or p.get("image")
+                    images.append(_decode_image(url))
+                    parts.append({"type": "image"})
+                else:
+                    parts.append(p)
+            out.append({**m, "content": parts})
+        return out, images
 
     @staticmethod
     def _lp_json(lps, tok):
@@ -140,8 +179,12 @@ class OpenAIService:
             raise ValidationError("messages must be a non-empty list")
         sampling = validate_sampling(body)
         tools = body.get("tools")
+        msgs, images = self._split_images(msgs)
         tokens = self.c.apply_chat_template(msgs, tools=tools)
-        stream = self._submit(tokens, body, sampling)
+        mm = None
+        if images:
+            tokens, mm = self.c.prepare_media(tokens, images)
+        stream = self._submit(tokens, body, sampling, mm)
         rid = "chatcmpl-" + uuid.uuid4().hex[:24]
         created = int(time.time())
         rp = make_reasoning_parser(body.get("reasoning_parser") or self.reasoning_parser_name)
