@@ -8,10 +8,12 @@
 //   scales  [gpb][128] bf16, then biases [gpb][128] bf16 (gpb = groups in the
 //           block: 2 for group size 32, else 1).
 // w = scale * q + bias with one rounding to bf16.
-// WQ = kWqE2M1 (-4): MXFP4 (OCP microscaling) -- 4-bit e2m1 codes (sign,
-// 2 exponent bits, 1 mantissa bit) in the same repacked word order, scales
-// [gpb][128] bf16 powers of two 2^(e8m0 - 127), no biases; w = e2m1(q) * scale
-// (exact).
+// WQ = kWqE2M1 (-4): 4-bit e2m1 codes (sign, 2 exponent bits, 1 mantissa bit)
+// in the same repacked word order, scales [gpb][128] bf16, no biases;
+// w = e2m1(q) * scale. MXFP4 (group 32, gpb 2): scales are powers of two
+// 2^(e8m0 - 127) (exact). NVFP4 (group 16, gpb 4): scales are the e4m3 block
+// scale times the tensor's global scale, rounded to bf16; `g` is then the
+// first of the half's two groups (words 0-1 and 2-3).
 // Output: row t of a K-major bf16 tile [128][64] with the 128-byte swizzle
 // the UMMA descriptor expects (16-byte chunk c of row t at c ^ (t & 7)).
 #pragma once
@@ -65,10 +67,12 @@ __device__ __forceinline__ void dequant_half_row(const uint8_t* raw, uint8_t* at
   if constexpr (WQ == kWqE2M1) {
     const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
     const uint32_t words[4] = {c.x, c.y, c.z, c.w};
-    const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv);
+    const __nv_bfloat16 sv2 = gpb == 4 ? sc[(g + 1) * 128 + t] : sv;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const uint32_t v = words[w];
+      const __nv_bfloat16 sw = w < 2 ? sv : sv2;
+      const __nv_bfloat162 s2 = __halves2bfloat162(sw, sw);
       uint4 o;
       o.x = de2m1_pair(v, s2);
       o.y = de2m1_pair(v >> 4, s2);
@@ -128,10 +132,12 @@ __device__ __forceinline__ void dequant_half_row_regs(const uint8_t* raw, int t,
   if constexpr (WQ == kWqE2M1) {
     const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
     const uint32_t words[4] = {c.x, c.y, c.z, c.w};
-    const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv);
+    const __nv_bfloat16 sv2 = gpb == 4 ? sc[(g + 1) * 128 + t] : sv;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const uint32_t x = words[w];
+      const __nv_bfloat16 sw = w < 2 ? sv : sv2;
+      const __nv_bfloat162 s2 = __halves2bfloat162(sw, sw);
       v[4 * w + 0] = de2m1_pair(x, s2);
       v[4 * w + 1] = de2m1_pair(x >> 4, s2);
       v[4 * w + 2] = de2m1_pair(x >> 8, s2);

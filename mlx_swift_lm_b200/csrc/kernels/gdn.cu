@@ -43,7 +43,7 @@ __device__ __forceinline__ int find_row(const int* __restrict__ cu, int R, int t
 __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 // P [T][ldp] bf16: q | k | v (C = 2 Hk Dk + Hv Dv channels) | z (Hv Dv) | b (Hv) | a (Hv)
-__global__ void __launch_bounds__(256) conv_kernel(const __nv_bfloat16* __restrict__ P, int ldp, int T,
+__global__ void __launch_bounds__(256) conv_kernel(int CB, const __nv_bfloat16* __restrict__ P, int ldp, int T,
                                                    const int* __restrict__ cu, int R, const int* __restrict__ fresh,
                                                    const int* __restrict__ slot,
                                                    const __nv_bfloat16* __restrict__ conv_state,
@@ -53,14 +53,17 @@ __global__ void __launch_bounds__(256) conv_kernel(const __nv_bfloat16* __restri
                                                    float* __restrict__ qkv_out, float* __restrict__ gb_out) {
   pdl_launch_dependents();
   pdl_wait();
-  extern __shared__ float y[];  // [C]
+  extern __shared__ float y_sm[];  // [CB] channels of this block
   const int t = blockIdx.x;
   if (t >= T) return;
+  // channel block [c0, c0 + CB): whole heads of Dk (q / k) or Dv (v) channels
+  const int c0 = blockIdx.y * CB, c1 = min(C, c0 + CB);
+  float* y = y_sm - c0;  // y[c] for c in [c0, c1)
   const int r = find_row(cu, R, t);
   const int s0 = cu[r], i = t - s0;
   const bool fr = fresh[r] != 0;
   const __nv_bfloat16* cs = conv_state + (size_t)slot[r] * (kTaps - 1) * C;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+  for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < kTaps; ++j) {
@@ -75,7 +78,8 @@ __global__ void __launch_bounds__(256) conv_kernel(const __nv_bfloat16* __restri
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   float* out = qkv_out + (size_t)t * C;
-  for (int hh = warp; hh < 2 * Hk; hh += nw) {
+  const int h_lo = c0 / Dk, h_hi = min(2 * Hk, (c1 + Dk - 1) / Dk);
+  for (int hh = h_lo + warp; hh < h_hi; hh += nw) {
     const float* src = y + hh * Dk;
     float ss = 0.f;
     for (int d = lane; d < Dk; d += 32) ss = fmaf(src[d], src[d], ss);
@@ -84,7 +88,8 @@ __global__ void __launch_bounds__(256) conv_kernel(const __nv_bfloat16* __restri
     const float inv = rsqrtf(ss / (float)Dk + eps) * sc;
     for (int d = lane; d < Dk; d += 32) out[hh * Dk + d] = src[d] * inv;
   }
-  for (int c = 2 * Hk * Dk + threadIdx.x; c < C; c += blockDim.x) out[c] = y[c];
+  for (int c = max(c0, 2 * Hk * Dk) + threadIdx.x; c < c1; c += blockDim.x) out[c] = y[c];
+  if (blockIdx.y != 0) return;
   const __nv_bfloat16* pb = P + (size_t)t * ldp + C + Hv * Dv;
   for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
     const float b = bf2f(pb[h]), a = bf2f(pb[Hv + h]);
@@ -93,8 +98,11 @@ __global__ void __launch_bounds__(256) conv_kernel(const __nv_bfloat16* __restri
   }
 }
 
-// grid (R, Hv, Dv / 4), 128 threads: warp w owns value row blockIdx.z * 4 + w.
-template <int NK>
+// grid (R, Hv, Dv / (4 * RPW)), 128 threads: warp w owns the RPW value rows
+// (blockIdx.z * 4 + w) * RPW .. + RPW - 1. Decode batches use RPW = 4 so
+// each lane has 4 state loads of 16 bytes in flight (the step is a pure
+// stream of the fp32 states); long prefill rows use RPW = 1 for parallelism.
+template <int NK, int RPW>
 __global__ void __launch_bounds__(128) recurrence_kernel(const float* __restrict__ qkv, const float* __restrict__ gb,
                                                          const int* __restrict__ cu, const int* __restrict__ fresh,
                                                          const int* __restrict__ slot, float* __restrict__ state,
@@ -104,50 +112,92 @@ __global__ void __launch_bounds__(128) recurrence_kernel(const float* __restrict
   pdl_launch_dependents();
   pdl_wait();
   constexpr int Dk = NK * 32;
+  static_assert(NK % 4 == 0 || NK == 2, "Dk of 64, 128 or 256");
   const int r = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int dv = blockIdx.z * 4 + warp;
+  const int dv0 = (blockIdx.z * 4 + warp) * RPW;
   const int hk = h / (Hv / Hk);
   const int s0 = cu[r], n = cu[r + 1] - s0;
   const bool fr = fresh[r] != 0;
   const int sl = slot[r];
-  if (dv < Dv) {
-    float* st = state + (((size_t)sl * Hv + h) * Dv + dv) * Dk + lane * NK;
-    float s[NK];
+  if (dv0 < Dv) {
+    float* st = state + (((size_t)sl * Hv + h) * Dv + dv0) * Dk + lane * NK;
+    float s[RPW][NK];
 #pragma unroll
-    for (int i = 0; i < NK; ++i) s[i] = fr ? 0.f : st[i];
+    for (int j = 0; j < RPW; ++j) {
+      if (fr) {
+#pragma unroll
+        for (int i = 0; i < NK; ++i) s[j][i] = 0.f;
+      } else if constexpr (NK % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < NK; i += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(st + (size_t)j * Dk + i);
+          s[j][i] = v.x, s[j][i + 1] = v.y, s[j][i + 2] = v.z, s[j][i + 3] = v.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < NK; ++i) s[j][i] = st[(size_t)j * Dk + i];
+      }
+    }
     const int C2 = 2 * Hk * Dk;
     for (int tt = 0; tt < n; ++tt) {
       const size_t t = (size_t)(s0 + tt);
       const float* q = qkv + t * C + hk * Dk + lane * NK;
       const float* k = qkv + t * C + Hk * Dk + hk * Dk + lane * NK;
-      const float v = qkv[t * C + C2 + h * Dv + dv];
       const float g = gb[t * 2 * Hv + h], beta = gb[t * 2 * Hv + Hv + h];
-      float kk[NK], qq[NK];
+      float kk[NK], qq[NK], v[RPW];
 #pragma unroll
       for (int i = 0; i < NK; ++i) {
         kk[i] = k[i];
         qq[i] = q[i];
       }
-      float kv = 0.f;
 #pragma unroll
-      for (int i = 0; i < NK; ++i) {
-        s[i] *= g;
-        kv = fmaf(s[i], kk[i], kv);
-      }
-      kv = warp_sum(kv);
-      const float delta = (v - kv) * beta;
-      float out = 0.f;
+      for (int j = 0; j < RPW; ++j) v[j] = qkv[t * C + C2 + h * Dv + dv0 + j];
+      float kv[RPW];
 #pragma unroll
-      for (int i = 0; i < NK; ++i) {
-        s[i] = fmaf(kk[i], delta, s[i]);
-        out = fmaf(s[i], qq[i], out);
+      for (int j = 0; j < RPW; ++j) {
+        kv[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < NK; ++i) {
+          s[j][i] *= g;
+          kv[j] = fmaf(s[j][i], kk[i], kv[j]);
+        }
       }
-      out = warp_sum(out);
-      if (lane == 0) o[t * Hv * Dv + h * Dv + dv] = out;
+#pragma unroll
+      for (int j = 0; j < RPW; ++j) kv[j] = warp_sum(kv[j]);
+      float out[RPW];
+#pragma unroll
+      for (int j = 0; j < RPW; ++j) {
+        const float delta = (v[j] - kv[j]) * beta;
+        out[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < NK; ++i) {
+          s[j][i] = fmaf(kk[i], delta, s[j][i]);
+          out[j] = fmaf(s[j][i], qq[i], out[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < RPW; ++j) out[j] = warp_sum(out[j]);
+      if (lane < RPW) {  // lane j stores row j (registers indexed by unrolled compare)
+        float oj = out[0];
+#pragma unroll
+        for (int j = 1; j < RPW; ++j)
+          if (lane == j) oj = out[j];
+        o[t * Hv * Dv + h * Dv + dv0 + lane] = oj;
+      }
     }
 #pragma unroll
-    for (int i = 0; i < NK; ++i) st[i] = s[i];
+    for (int j = 0; j < RPW; ++j) {
+      if constexpr (NK % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < NK; i += 4)
+          *reinterpret_cast<float4*>(st + (size_t)j * Dk + i) = make_float4(s[j][i], s[j][i + 1], s[j][i + 2],
+                                                                            s[j][i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < NK; ++i) st[(size_t)j * Dk + i] = s[j][i];
+      }
+    }
   }
   // roll the conv state to the row's last three inputs (the conv kernel that
   // read the old state has completed: this grid waited for it)
@@ -166,6 +216,20 @@ __global__ void __launch_bounds__(128) recurrence_kernel(const float* __restrict
   }
 }
 
+template <int NK>
+static cudaError_t launch_rec(int rpw, int R, int Hv, int Dv, cudaStream_t st, const float* qkv, const float* gb,
+                              const int* cu, const int* fresh, const int* slot, float* state, int Hk, float* o,
+                              const __nv_bfloat16* p, int ldp, __nv_bfloat16* cs, int C) {
+  if (rpw == 4) {
+    const dim3 grid(R, Hv, (Dv + 15) / 16);
+    return launch_k(recurrence_kernel<NK, 4>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv,
+                    Dv, o, p, ldp, cs, C);
+  }
+  const dim3 grid(R, Hv, (Dv + 3) / 4);
+  return launch_k(recurrence_kernel<NK, 1>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv, Dv,
+                  o, p, ldp, cs, C);
+}
+
 // one CTA per token; warp per value head: rmsnorm(o) * w * silu(z) -> bf16
 __global__ void __launch_bounds__(256) norm_gate_kernel(const float* __restrict__ o, int T, int Hv, int Dv,
                                                         const __nv_bfloat16* __restrict__ z, int ldz,
@@ -176,7 +240,7 @@ __global__ void __launch_bounds__(256) norm_gate_kernel(const float* __restrict_
   const int t = blockIdx.x;
   if (t >= T) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int h = warp; h < Hv; h += nw) {
+  for (int h = blockIdx.y * nw + warp; h < Hv; h += gridDim.y * nw) {
     const float* src = o + ((size_t)t * Hv + h) * Dv;
     float ss = 0.f;
     for (int d = lane; d < Dv; d += 32) ss = fmaf(src[d], src[d], ss);
@@ -215,15 +279,18 @@ int b200_gdn_conv(const void* P, int ldp, int T, const int* cu, int R, const int
                   const float* A_log, const float* dt_bias, float eps, float* qkv_out, float* gb_out,
                   cudaStream_t st) {
   if (T <= 0) return 0;
-  if (R <= 0 || C != 2 * Hk * Dk + Hv * Dv || (size_t)C * 4 > 200 * 1024 || ldp < C + Hv * Dv + 2 * Hv) return -1;
-  const size_t smem = (size_t)C * sizeof(float);
+  if (R <= 0 || C != 2 * Hk * Dk + Hv * Dv || ldp < C + Hv * Dv + 2 * Hv || (Dv % Dk && Dk % Dv)) return -1;
+  // channel blocks of whole heads: 8 key heads' worth (multiples of Dk and Dv)
+  int CB = 8 * (Dk > Dv ? Dk : Dv);
+  if ((2 * Hk * Dk) % CB) CB = Dk > Dv ? Dk : Dv;
+  const size_t smem = (size_t)CB * sizeof(float);
   static bool cfg = false;
   if (!cfg) {
     cudaError_t e = cudaFuncSetAttribute(gdn::conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return (int)e;
     cfg = true;
   }
-  cudaError_t e = launch_k(gdn::conv_kernel, dim3(T), dim3(256), smem, st, 1,
+  cudaError_t e = launch_k(gdn::conv_kernel, dim3(T, (C + CB - 1) / CB), dim3(256), smem, st, 1, CB,
                            reinterpret_cast<const __nv_bfloat16*>(P), ldp, T, cu, R, fresh, slot,
                            reinterpret_cast<const __nv_bfloat16*>(conv_state), conv_w, C, Hk, Dk, Hv, Dv, A_log,
                            dt_bias, eps, qkv_out, gb_out);
@@ -232,28 +299,20 @@ int b200_gdn_conv(const void* P, int ldp, int T, const int* cu, int R, const int
 
 int b200_gdn_recurrence(const float* qkv, const float* gb, const int* cu, int R, const int* fresh, const int* slot,
                         float* state, int Hk, int Dk, int Hv, int Dv, float* o, const void* P, int ldp,
-                        void* conv_state, int C, cudaStream_t st) {
+                        void* conv_state, int C, int T, cudaStream_t st) {
   if (R <= 0) return 0;
-  if ((Hv % Hk) || (Dv % 4) || C != 2 * Hk * Dk + Hv * Dv) return -1;
-  const dim3 grid(R, Hv, Dv / 4);
+  if ((Hv % Hk) || (Dv % 16) || C != 2 * Hk * Dk + Hv * Dv) return -1;
   const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(P);
   __nv_bfloat16* cs = reinterpret_cast<__nv_bfloat16*>(conv_state);
+  // several value rows per warp when the batch alone fills the GPU (decode)
+  const long warps4 = (long)R * Hv * Dv / 4;
+  const int rpw = (T <= 2 * R && warps4 >= 148 * 16) ? 4 : 1;
   cudaError_t e;
   switch (Dk) {
-    case 64:
-      e = launch_k(gdn::recurrence_kernel<2>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv, Dv,
-                   o, p, ldp, cs, C);
-      break;
-    case 128:
-      e = launch_k(gdn::recurrence_kernel<4>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv, Dv,
-                   o, p, ldp, cs, C);
-      break;
-    case 256:
-      e = launch_k(gdn::recurrence_kernel<8>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv, Dv,
-                   o, p, ldp, cs, C);
-      break;
-    default:
-      return -1;
+    case 64: e = gdn::launch_rec<2>(rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C); break;
+    case 128: e = gdn::launch_rec<4>(rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C); break;
+    case 256: e = gdn::launch_rec<8>(rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C); break;
+    default: return -1;
   }
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
@@ -261,7 +320,7 @@ int b200_gdn_recurrence(const float* qkv, const float* gb, const int* cu, int R,
 int b200_gdn_norm_gate(const float* o, int T, int Hv, int Dv, const void* z, int ldz, const void* w, float eps,
                        void* out, int ldo, cudaStream_t st) {
   if (T <= 0) return 0;
-  cudaError_t e = launch_k(gdn::norm_gate_kernel, dim3(T), dim3(256), 0, st, 1, o, T, Hv, Dv,
+  cudaError_t e = launch_k(gdn::norm_gate_kernel, dim3(T, (Hv + 7) / 8), dim3(256), 0, st, 1, o, T, Hv, Dv,
                            reinterpret_cast<const __nv_bfloat16*>(z), ldz, reinterpret_cast<const __nv_bfloat16*>(w),
                            eps, reinterpret_cast<__nv_bfloat16*>(out), ldo);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();

@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     // tensor-memory columns of lane t.
     const int t = (threadIdx.x - 128) & 127;
     const int grp = (threadIdx.x - 128) >> 7;
-    const int g1 = qa.gs == 32 ? 1 : 0;
+    const int g1 = qa.gs == 16 ? 2 : qa.gs == 32 ? 1 : 0;  // first group of the second half
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16) + S::kAccCols;
     for (int i = grp; i < nkb; i += 2) {
       const int rs = i % RS, rr = i / RS;
@@ -752,8 +752,9 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
 int b200_gemm_q(const void* X, int M, int K, int ldx, const void* tiled, int N, int bits, int gs, void* Y, int ldy,
                 const void* R, int ldr, const void* bias, int epi, int num_sms, int force_splits, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
-  if ((bits != 4 && bits != 8 && bits != kWqE2M1) || (gs != 32 && gs != 64 && gs != 128)) return -1;
-  if (bits == kWqE2M1 && gs != 32) return -1;
+  if ((bits != 4 && bits != 8 && bits != kWqE2M1) || (gs != 16 && gs != 32 && gs != 64 && gs != 128)) return -1;
+  // e2m1 codes: MXFP4 (group 32) or NVFP4 (group 16); affine codes: groups 32 / 64 / 128
+  if (bits == kWqE2M1 ? (gs != 16 && gs != 32) : (gs == 16)) return -1;
   if ((K % 64) || (gs == 128 && K % 128) || (ldx % 8) || ((uintptr_t)X & 15) || ((uintptr_t)tiled & 15) || (N % 8)) return -1;
   const bool glu = epi == kEpiSwiGLU || epi == kEpiGeGLU || epi == kEpiSwiGLUOAI;
   if (glu && (N % 128)) return -1;
@@ -761,7 +762,7 @@ int b200_gemm_q(const void* X, int M, int K, int ldx, const void* tiled, int N, 
   QArgs q;
   q.tiled = reinterpret_cast<const uint8_t*>(tiled);
   q.gs = gs;
-  q.gpb = gs == 32 ? 2 : 1;
+  q.gpb = gs == 16 ? 4 : gs == 32 ? 2 : 1;
   q.rec_bytes = bits == kWqE2M1 ? 4 * 128 * 8 + q.gpb * 256 : bits * 128 * 8 + q.gpb * 512;
   q.kb_total = K / 64;
   CUtensorMap tx;

@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
   } else if (warp >= 4) {
     if constexpr (WQ != 0) {
       const int t = (threadIdx.x - 128) & 127, half = (threadIdx.x - 128) >> 7;
-      const int g = q.gs == 32 ? half : 0;
+      const int g = q.gs == 16 ? 2 * half : q.gs == 32 ? half : 0;
       for (int i = 0; i < nkb; ++i) {
         const int rs = i % RS, rr = i / RS;
         const int s = i % STAGES, r = i / STAGES;
@@ -470,14 +470,15 @@ int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* tiled, int
                             int ldy, const void* bias, int epi, const int* chunks, const int* n_chunks, int max_chunks,
                             int BN, cudaStream_t st) {
   if (P <= 0) return 0;
-  if ((K % 64) || (gs == 128 && K % 128) || (N % 8) || (bits != 4 && bits != 8 && bits != kWqE2M1) || (gs != 32 && gs != 64 && gs != 128))
+  if ((K % 64) || (gs == 128 && K % 128) || (N % 8) || (bits != 4 && bits != 8 && bits != kWqE2M1) ||
+      (gs != 16 && gs != 32 && gs != 64 && gs != 128))
     return -1;
-  if ((bits == kWqE2M1 && gs != 32) || ((uintptr_t)tiled & 15)) return -1;
+  if ((bits == kWqE2M1 ? (gs != 16 && gs != 32) : (gs == 16)) || ((uintptr_t)tiled & 15)) return -1;
   CUtensorMap tx;
   moe::GQuant q;
   q.tiled = reinterpret_cast<const uint8_t*>(tiled);
   q.gs = gs;
-  q.gpb = gs == 32 ? 2 : 1;
+  q.gpb = gs == 16 ? 4 : gs == 32 ? 2 : 1;
   q.rec_bytes = bits == kWqE2M1 ? 4 * 128 * 8 + q.gpb * 256 : bits * 128 * 8 + q.gpb * 512;
   q.kb_total = K / 64;
   q.tiles_per_expert = (N + 127) / 128;

@@ -30,16 +30,27 @@ from ..ops.reference import interleave_gate_up as _interleave_dense
 from .safetensors import load_safetensors
 
 
+def _same_format(parts) -> bool:
+    p0 = parts[0]
+    return all(isinstance(p, QuantizedWeight) and (p.bits, p.gs, p.mode) == (p0.bits, p0.gs, p0.mode) for p in parts)
+
+
+def _dense(t):
+    return t.dequantize(torch.float32) if isinstance(t, QuantizedWeight) else t
+
+
 def interleave_gate_up(g, u):
-    if isinstance(g, QuantizedWeight):
+    """Gate / up rows in 64-row interleaved blocks; packed when both share a
+    quantised format, else dense (mixed-format checkpoints)."""
+    if _same_format([g, u]):
         return QuantizedWeight.interleave_gate_up(g, u)
-    return _interleave_dense(g, u)
+    return _interleave_dense(_dense(g), _dense(u))
 
 
 def _cat_rows(parts):
-    if isinstance(parts[0], QuantizedWeight):
+    if _same_format(parts):
         return QuantizedWeight.cat_rows(parts)
-    return torch.cat(parts, 0)
+    return torch.cat([_dense(p) for p in parts], 0)
 
 
 class CheckpointView:
@@ -85,8 +96,10 @@ class CheckpointView:
                 raise KeyError(f"missing weight {self.prefix + wname}")
             return None
         w = self.raw(wname)
+        if self.has(base + ".weight_scale"):  # NVIDIA ModelOpt NVFP4 / FP8
+            return self._modelopt(base, w, packed)
         if self.has(base + ".scales"):
-            gs, bits, mode = self._qparams(base)
+            gs, bits, mode = self._qparams(base)  # MLX quantisation
             s = self.raw(base + ".scales")
             b = self.raw(base + ".biases") if self.has(base + ".biases") else None
             if self.keep_quantized and packed:
@@ -95,6 +108,27 @@ class CheckpointView:
                     return qw
             return quant.dequantize(w, s, b, mode, gs, bits, torch.float32).to(self.dtype)
         return w.to(self.dtype)
+
+    def _modelopt(self, base, w, packed):
+        """ModelOpt checkpoints: NVFP4 (uint8 pairs of e2m1 codes, e4m3 block
+        scales per 16 inputs, fp32 ``weight_scale_2``) stays packed for the
+        e2m1 kernels when the view keeps quantised weights; FP8 (e4m3 weights
+        with a per-tensor or per-output-channel ``weight_scale``) is
+        dequantised. ``input_scale`` (activation quantisation) is not used:
+        activations stay bf16."""
+        ws = self.raw(base + ".weight_scale")
+        if w.dtype == torch.uint8 and self.has(base + ".weight_scale_2"):
+            g2 = float(self.raw(base + ".weight_scale_2").float().reshape(-1)[0])
+            b = w.to(torch.int32)
+            codes = torch.stack([b & 0x0F, b >> 4], -1).reshape(w.shape[0], -1)
+            qw = QuantizedWeight.from_nvfp4(codes, ws, g2)
+            if self.keep_quantized and packed and qw.shape[1] % 64 == 0 and qw.shape[0] % 8 == 0:
+                return qw
+            return qw.dequantize(torch.float32).to(self.dtype)
+        s = ws.float()
+        if s.numel() > 1:
+            s = s.reshape(-1, 1)
+        return (w.float() * s).to(self.dtype)
 
     def vec(self, name, required=False):
         if not self.has(name):

@@ -21,7 +21,7 @@ _lib.register_signatures({
                                  _lib.vp, _lib.vp, _lib.vp]),
     "b200_gdn_recurrence": (_lib.i32, [_lib.vp, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.vp, _lib.i32,
                                        _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.i32,
-                                       _lib.vp]),
+                                       _lib.i32, _lib.vp]),
     "b200_gdn_norm_gate": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.f32,
                                       _lib.vp, _lib.i32, _lib.vp]),
     "b200_sigmoid_mul": (_lib.i32, [_lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32,
@@ -68,7 +68,7 @@ def gdn_layer(P: torch.Tensor, rows: GdnRows, conv_state: torch.Tensor, ssm_stat
                "gdn_conv")
     _lib.check(L.b200_gdn_recurrence(qkv.data_ptr(), gb.data_ptr(), rows.cu.data_ptr(), R, rows.fresh.data_ptr(),
                                      rows.slot.data_ptr(), ssm_state.data_ptr(), Hk, Dk, Hv, Dv, o.data_ptr(),
-                                     P.data_ptr(), P.stride(0), conv_state.data_ptr(), C, st), "gdn_recurrence")
+                                     P.data_ptr(), P.stride(0), conv_state.data_ptr(), C, T, st), "gdn_recurrence")
     _lib.check(L.b200_gdn_norm_gate(o.data_ptr(), T, Hv, Dv, P[:, C:].data_ptr(), P.stride(0), norm_w.data_ptr(),
                                     float(eps), y.data_ptr(), y.stride(0), st), "gdn_norm_gate")
     _lib.count(3)

@@ -16,8 +16,10 @@ such weights packed in the layout the dequantising tcgen05 GEMM
 MXFP4 (``mode="mxfp4"``, the OCP microscaling format of GPT-OSS and MLX's
 ``mxfp4`` mode): 4-bit e2m1 codes (sign, two exponent bits, one mantissa bit)
 in the same repacked nibble order, one power-of-two scale 2^(e8m0 - 127) per
-32 inputs (kept as bf16, exact), no biases; w = e2m1(q) * scale. The kernels
-take it as ``bits = -4``.
+32 inputs (kept as bf16, exact), no biases; w = e2m1(q) * scale. NVFP4
+(``mode="nvfp4"``, NVIDIA ModelOpt): the same codes with one scale per 16
+inputs, the e4m3 block scale times the tensor's fp32 global scale (kept as
+bf16). The kernels take both as ``bits = -4`` with the group size.
 
 Row operations used by the model builder (stacking q|k|v, interleaving
 gate/up, tensor-parallel row / column shards) act on codes, scales and biases
@@ -31,7 +33,7 @@ import torch
 from . import quant
 
 SUPPORTED_BITS = (4, 8)
-SUPPORTED_GROUPS = (32, 64, 128)
+SUPPORTED_GROUPS = (32, 64, 128)  # affine / MXFP4; NVFP4 uses 16
 # e2m1 magnitudes of codes 0..7 (code bit 3 is the sign)
 E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
 
@@ -89,9 +91,10 @@ class QuantizedWeight:
 
     def __init__(self, codes: torch.Tensor, scales_t: torch.Tensor, biases_t: torch.Tensor | None, bits: int, gs: int,
                  num_experts: int = 0, mode: str = "affine"):
-        assert bits in SUPPORTED_BITS and gs in SUPPORTED_GROUPS, (bits, gs)
-        assert mode in ("affine", "mxfp4")
-        assert mode == "affine" or (bits == 4 and gs == 32 and biases_t is None), "mxfp4: 4-bit, group 32, no bias"
+        assert mode in ("affine", "mxfp4", "nvfp4")
+        assert bits in SUPPORTED_BITS and (gs in SUPPORTED_GROUPS or (mode == "nvfp4" and gs == 16)), (bits, gs)
+        assert mode == "affine" or (bits == 4 and gs == {"mxfp4": 32, "nvfp4": 16}[mode] and biases_t is None), \
+            "e2m1 formats: 4-bit, group 32 (MXFP4) / 16 (NVFP4), no bias"
         self.codes, self.scales_t, self.biases_t = codes, scales_t, biases_t
         self.bits, self.gs, self.mode = bits, gs, mode
         self.shape = (codes.shape[0], codes.shape[1] * 8 // bits)
@@ -101,7 +104,7 @@ class QuantizedWeight:
     @property
     def kernel_bits(self) -> int:
         """Format code of the kernels' C ABI: 4 / 8 affine, -4 MXFP4."""
-        return -4 if self.mode == "mxfp4" else self.bits
+        return -4 if self.mode in ("mxfp4", "nvfp4") else self.bits
 
     def _like(self, codes, scales_t, biases_t, num_experts: int = 0) -> "QuantizedWeight":
         return QuantizedWeight(codes, scales_t, biases_t, self.bits, self.gs, num_experts, self.mode)
@@ -129,6 +132,26 @@ class QuantizedWeight:
         """e2m1 codes int [N, K] (0..15) and uint8 e8m0 exponents [N, K/32]."""
         sc = e8m0_to_scale(scales_e8m0).to(torch.bfloat16)
         return cls(_repack4(q).contiguous(), sc.t().contiguous(), None, 4, 32, mode="mxfp4")
+
+    @classmethod
+    def from_nvfp4(cls, q: torch.Tensor, block_scales: torch.Tensor, global_scale: float):
+        """e2m1 codes int [N, K] and e4m3 block scales [N, K/16] (float8 or
+        float) times the fp32 global scale (NVIDIA ModelOpt NVFP4)."""
+        sc = (block_scales.float() * float(global_scale)).to(torch.bfloat16)
+        return cls(_repack4(q).contiguous(), sc.t().contiguous(), None, 4, 16, mode="nvfp4")
+
+    @classmethod
+    def quantize_nvfp4(cls, w: torch.Tensor):
+        """NVFP4 quantisation of a float weight [N, K]: global scale
+        amax / (6 * 448), e4m3 block scales of amax16 / 6 / global, nearest
+        e2m1 codes of w / (block * global)."""
+        N, K = w.shape
+        g = w.float().reshape(N, K // 16, 16)
+        gscale = float(w.float().abs().max().clamp(min=1e-12)) / (6.0 * 448.0)
+        bs = (g.abs().amax(-1) / 6.0 / gscale).clamp(max=448.0).to(torch.float8_e4m3fn)
+        denom = (bs.float() * gscale).clamp(min=1e-30)[..., None]
+        q = e2m1_encode(g / denom).reshape(N, K)
+        return cls.from_nvfp4(q, bs, gscale)
 
     @classmethod
     def from_mlx_mxfp4(cls, packed: torch.Tensor, scales: torch.Tensor):
@@ -192,15 +215,15 @@ class QuantizedWeight:
         MXFP4: e2m1(q) * scale (exact)."""
         q = self.codes_int()
         s = self.scales_t.t().float().repeat_interleave(self.gs, dim=1)
-        if self.mode == "mxfp4":
+        if self.mode in ("mxfp4", "nvfp4"):
             return (e2m1_decode(q) * s).to(torch.bfloat16).to(dtype)
         b = self.biases_t.t().float().repeat_interleave(self.gs, dim=1)
         return (q.float() * s + b).to(torch.bfloat16).to(dtype)
 
     def to(self, device=None, dtype=None):
         dt = dtype if dtype in (torch.bfloat16, torch.float16, torch.float32) else None
-        if self.mode == "mxfp4":
-            dt = None  # power-of-two scales stay bf16
+        if self.mode in ("mxfp4", "nvfp4"):
+            dt = None  # block scales stay bf16
         sc = self.scales_t.to(device=device, dtype=dt or self.scales_t.dtype)
         bi = self._bsel(lambda b: b.to(device=device, dtype=dt or b.dtype))
         return self._like(self.codes.to(device), sc, bi, self.num_experts)
@@ -224,7 +247,7 @@ class QuantizedWeight:
 
     # ---------------------------------------------------------------- device layout
     def record_bytes(self) -> int:
-        gpb = 2 if self.gs == 32 else 1
+        gpb = {16: 4, 32: 2}.get(self.gs, 1)
         return self.bits * 128 * 8 + gpb * (256 if self.biases_t is None else 512)
 
     def tiled(self) -> torch.Tensor:
@@ -252,8 +275,9 @@ class QuantizedWeight:
             codes = torch.cat([codes, torch.zeros(E, pad, KB, cb, dtype=codes.dtype, device=dev)], 1)
             sc = torch.cat([sc, torch.zeros(E, pad, sc.shape[2], dtype=sc.dtype, device=dev)], 1)
             bi = torch.cat([bi, torch.zeros(E, pad, bi.shape[2], dtype=bi.dtype, device=dev)], 1)
-        if self.gs == 32:  # groups of each K block: [E, rows, KB, gpb]
-            sc_kb, bi_kb = sc.reshape(E, -1, KB, 2), bi.reshape(E, -1, KB, 2)
+        if self.gs in (16, 32):  # groups of each K block: [E, rows, KB, gpb]
+            gpb = 64 // self.gs
+            sc_kb, bi_kb = sc.reshape(E, -1, KB, gpb), bi.reshape(E, -1, KB, gpb)
         elif self.gs == 64:
             sc_kb, bi_kb = sc.reshape(E, -1, KB, 1), bi.reshape(E, -1, KB, 1)
         else:  # 128: one group per two K blocks

@@ -86,3 +86,29 @@ def test_hybrid_model_graph_matches_eager_and_oracle():
     mc = m.clone_to("cpu", torch.float32)
     r = mc.forward_dense(p, mc.new_cache())
     assert _rel(lg, r) < 0.05
+
+
+@pytest.mark.parametrize("Dk", [64, 128])
+def test_gdn_decode_rows_four_per_warp(Dk):
+    """A decode batch large enough for the several-rows-per-warp kernel."""
+    torch.manual_seed(Dk)
+    Hk, Hv, Dv, B = 2, 8, 128, 48
+    C = 2 * Hk * Dk + Hv * Dv
+    P = (torch.randn(B, C + Hv * Dv + 2 * Hv) * 0.5).to(torch.bfloat16)
+    conv_w = torch.randn(C, 4) * 0.5
+    A_log, dt_bias = torch.rand(Hv) * 2, torch.randn(Hv)
+    norm_w = (torch.rand(Dv) + 0.5).to(torch.bfloat16)
+    cs0 = (torch.randn(B + 1, 3, C) * 0.5).to(torch.bfloat16)
+    ss0 = torch.randn(B + 1, Hv, Dv, Dk) * 0.1
+    cu, fresh, slots = list(range(B + 1)), [0] * B, list(range(B))
+    cs_r, ss_r = cs0.clone(), ss0.clone()
+    want = ref.gdn_layer_ref(P.float(), cu, fresh, slots, cs_r, ss_r, conv_w, A_log, dt_bias, norm_w.float(),
+                             Hk, Dk, Hv, Dv, 1e-6)
+    i32 = dict(dtype=torch.int32, device=DEV)
+    rows = GdnRows(torch.tensor(cu, **i32), torch.tensor(fresh, **i32), torch.tensor(slots, **i32))
+    cs, ss = cs0.to(DEV), ss0.to(DEV)
+    got = gdn_layer(P.to(DEV), rows, cs, ss, conv_w.to(DEV), A_log.to(DEV), dt_bias.to(DEV), norm_w.to(DEV),
+                    Hk, Dk, Hv, Dv, 1e-6)
+    torch.cuda.synchronize()
+    assert _rel(got.cpu(), want) < 1e-2
+    assert _rel(ss.cpu(), ss_r) < 1e-4

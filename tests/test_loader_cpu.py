@@ -104,3 +104,44 @@ def test_hf_mxfp4_blocks_pack_exactly():
     dense = _mxfp4_blocks(blocks, scales)  # [E, N, K]
     for e in range(E):
         assert torch.equal(q.expert(e).dequantize(), dense[e].to(torch.bfloat16).float())
+
+
+def _nvfp4_tensors(w):
+    from mlx_swift_lm_b200.ops.qlinear import QuantizedWeight
+
+    q = QuantizedWeight.quantize_nvfp4(w)
+    codes = q.codes_int()
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).to(torch.uint8)
+    g = float(w.abs().max()) / (6.0 * 448.0)
+    bs = (q.scales_t.t().float() / g).to(torch.float8_e4m3fn)
+    return packed, bs, torch.tensor(g, dtype=torch.float32), q
+
+
+def test_modelopt_nvfp4_and_fp8_checkpoints(tmp_path):
+    from mlx_swift_lm_b200.loader.convert import export_tensors, to_hf_config
+    from mlx_swift_lm_b200.loader.safetensors import save_safetensors
+
+    m = _model()
+    t = export_tensors(m)
+    for k in list(t):
+        if k.endswith(("q_proj.weight", "o_proj.weight", "gate_proj.weight", "down_proj.weight")):
+            packed, bs, g, _ = _nvfp4_tensors(t[k])
+            base = k[:-len(".weight")]
+            t[k], t[base + ".weight_scale"], t[base + ".weight_scale_2"] = packed, bs, g
+        elif k.endswith(("k_proj.weight", "v_proj.weight", "up_proj.weight")):  # FP8 per-tensor
+            s = t[k].abs().max() / 448.0
+            base = k[:-len(".weight")]
+            t[k], t[base + ".weight_scale"] = (t[k] / s).to(torch.float8_e4m3fn), s.reshape(1)
+    d = tmp_path / "mo"
+    d.mkdir()
+    hf = to_hf_config(m.cfg)
+    hf["quantization_config"] = {"quant_method": "modelopt", "quant_algo": "NVFP4"}
+    (d / "config.json").write_text(json.dumps(hf))
+    save_safetensors(str(d / "model.safetensors"), t)
+    mq, _ = load_model(str(d), device="cpu", dtype=torch.float32)
+    assert isinstance(mq.layers[0].wo, QuantizedWeight) and mq.layers[0].wo.mode == "nvfp4"
+    md, _ = load_model(str(d), device="cpu", dtype=torch.float32, keep_quantized=False)
+    a, b = _logits(mq, TOKS), _logits(md, TOKS)
+    assert ((a - b).norm() / b.norm()).item() < 1e-3
+    ref = _logits(m, TOKS)
+    assert ((a - ref).norm() / ref.norm()).item() < 0.5  # fp4 weights: coarse but the same function

@@ -86,3 +86,18 @@ def test_mxfp4_dequant_exact():
     eye = torch.eye(K, device=DEV, dtype=torch.bfloat16)
     y = ops.gemm(eye, q, epi="f32")  # [K, N] = W^T
     assert torch.equal(y.t().cpu(), q.dequantize().cpu())
+
+
+@pytest.mark.parametrize("M", [1, 64, 300])
+def test_gemm_nvfp4(M):
+    torch.manual_seed(M + 5)
+    N, K = 384, 1024
+    q = QuantizedWeight.quantize_nvfp4(torch.randn(N, K) * 0.05).to(DEV)
+    assert q.kernel_bits == -4 and q.gs == 16
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    y = ops.gemm(x, q)
+    r = ref.gemm_ref(x.cpu(), q.dequantize().to(torch.bfloat16).cpu())
+    assert _rel(y.cpu(), r) < 1e-2
+    eye = torch.eye(K, device=DEV, dtype=torch.bfloat16)[:128]
+    yi = ops.gemm(eye, q, epi="f32")  # rows 0..127 of W^T exactly
+    assert torch.equal(yi.t().cpu(), q.dequantize()[:, :128].cpu())
