@@ -39,15 +39,36 @@ def _dense(t):
     return t.dequantize(torch.float32) if isinstance(t, QuantizedWeight) else t
 
 
+def _rotated(parts) -> bool:
+    from ..ops.rotation import RotatedWeight
+
+    return any(isinstance(p, RotatedWeight) for p in parts)
+
+
+def _as_rotated(w):
+    from ..ops.rotation import RotatedWeight
+
+    return w if isinstance(w, RotatedWeight) else RotatedWeight([(None, w)])
+
+
 def interleave_gate_up(g, u):
     """Gate / up rows in 64-row interleaved blocks; packed when both share a
-    quantised format, else dense (mixed-format checkpoints)."""
+    quantised format, else dense (mixed-format checkpoints); rotated (ParoQuant)
+    gate / up keep their own rotations as a GLU pair."""
+    if _rotated([g, u]):
+        from ..ops.rotation import RotatedWeight
+
+        return RotatedWeight(_as_rotated(g).parts + _as_rotated(u).parts, glu=True)
     if _same_format([g, u]):
         return QuantizedWeight.interleave_gate_up(g, u)
     return _interleave_dense(_dense(g), _dense(u))
 
 
 def _cat_rows(parts):
+    if _rotated(parts):
+        from ..ops.rotation import RotatedWeight
+
+        return RotatedWeight([pr for p in parts for pr in _as_rotated(p).parts])
     if _same_format(parts):
         return QuantizedWeight.cat_rows(parts)
     return torch.cat([_dense(p) for p in parts], 0)
@@ -89,6 +110,8 @@ class CheckpointView:
         4/8-bit weights stay packed (QuantizedWeight) when the view keeps
         quantised weights and `packed`; everything else is dequantised."""
         wname = base + ".weight"
+        if self.has(base + ".qweight"):  # AutoAWQ packing (ParoQuant checkpoints)
+            return self._awq(base, packed)
         if not self.has(wname):
             if self.has(base):  # bare parameter (e.g. gpt-oss experts.gate_up_proj)
                 return self.raw(base).to(self.dtype)
@@ -108,6 +131,30 @@ class CheckpointView:
                     return qw
             return quant.dequantize(w, s, b, mode, gs, bits, torch.float32).to(self.dtype)
         return w.to(self.dtype)
+
+    def _awq(self, base, packed):
+        """AutoAWQ 4-bit weight -> affine QuantizedWeight; with ParoQuant
+        rotation tensors (``theta``, ``pairs``, ``channel_scales``) a
+        :class:`RotatedWeight` that rotates the activations first."""
+        from ..ops.rotation import PairwiseRotation, RotatedWeight, awq_to_quantized
+
+        gs = self.q.get("group_size", 128)
+        qw = awq_to_quantized(self.raw(base + ".qweight"), self.raw(base + ".qzeros"), self.raw(base + ".scales"), gs)
+        w = qw if (self.keep_quantized and packed) else qw.dequantize(torch.float32).to(self.dtype)
+        if self.has(base + ".theta"):
+            cs = self.raw(base + ".channel_scales") if self.has(base + ".channel_scales") else None
+            rot = PairwiseRotation(self.raw(base + ".theta"), self.raw(base + ".pairs"), cs)
+            return RotatedWeight([(rot, w)])
+        return w
+
+    def _rotation(self, prefix):
+        """A shared rotation (MoE experts: ``experts.{gate_up,down}_weight_*``)."""
+        from ..ops.rotation import PairwiseRotation
+
+        if not self.has(prefix + "theta"):
+            return None
+        cs = self.raw(prefix + "channel_scales") if self.has(prefix + "channel_scales") else None
+        return PairwiseRotation(self.raw(prefix + "theta"), self.raw(prefix + "pairs"), cs)
 
     def _modelopt(self, base, w, packed):
         """ModelOpt checkpoints: NVFP4 (uint8 pairs of e2m1 codes, e4m3 block
@@ -434,6 +481,9 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
                    for x in (g, u, d))
     L.experts_gu = _stack([interleave_gate_up(_shard_rows(g[e], r, w), _shard_rows(u[e], r, w)) for e in range(E)])
     L.experts_d = _stack([_shard_cols(d[e], r, w) for e in range(E)])
+    # ParoQuant: rotations shared by all experts of the layer
+    L.experts_rot_in = ck._rotation(mp + "experts.gate_up_weight_")
+    L.experts_rot_mid = ck._rotation(mp + "experts.down_weight_")
     if cfg.shared_expert_intermediate_size:
         sp = mp + "shared_expert."
         L.shared_gu = interleave_gate_up(_shard_rows(ck.linear(sp + "gate_proj"), r, w),

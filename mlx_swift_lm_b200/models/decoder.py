@@ -35,7 +35,9 @@ class LayerWeights:
                  "experts_d_b", "shared_gu", "shared_d", "shared_gate", "sinks", "moe",
                  # linear-attention (Gated DeltaNet) layers: wqkv is the fused in-projection
                  # q|k|v|z|b|a and wo the out-projection
-                 "linear", "conv_w", "A_log", "dt_bias", "gdn_norm")
+                 "linear", "conv_w", "A_log", "dt_bias", "gdn_norm",
+                 # ParoQuant: activation rotations shared by the experts (gate/up input, down input)
+                 "experts_rot_in", "experts_rot_mid")
 
     F32 = ("sinks", "conv_w", "A_log", "dt_bias")  # kept in fp32 whatever the model dtype
 
@@ -337,7 +339,8 @@ class DecoderLM:
         cfg = self.cfg
         w, idx = self.route(L, h)
         out = moe_ops.moe_experts(h, L.experts_gu, L.experts_d, w, idx, cfg.glu_epi, L.experts_gu_b,
-                                  L.experts_d_b if self.tp.rank == 0 else None)
+                                  L.experts_d_b if self.tp.rank == 0 else None, rot_in=L.experts_rot_in,
+                                  rot_mid=L.experts_rot_mid)
         if L.shared_gu is not None:
             s = ops.gemm(ops.gemm(h, L.shared_gu, epi=cfg.glu_epi), L.shared_d)
             if L.shared_gate is not None:
@@ -582,6 +585,8 @@ class DecoderLM:
                     v = cv(v, s in LayerWeights.F32)
                 elif isinstance(v, QuantizedWeight):
                     v = v.to(dev)
+                elif v is not None and hasattr(v, "to") and not isinstance(v, bool):  # rotated weights, rotations
+                    v = v.to(dev, dtype)
                 setattr(N, s, v)
             m.layers.append(N)
         return m
@@ -609,6 +614,9 @@ class DecoderLM:
         for L in self.layers:
             for s in LayerWeights.__slots__:
                 v = getattr(L, s)
+                if v is not None and not isinstance(v, (torch.Tensor, bool)) and hasattr(v, "to"):
+                    setattr(L, s, v.to(device, dtype))
+                    continue
                 if isinstance(v, torch.Tensor):
                     if s in LayerWeights.F32:
                         setattr(L, s, v.to(device=device, dtype=torch.float32))

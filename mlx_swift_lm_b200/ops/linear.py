@@ -30,6 +30,8 @@ def gemm(x: torch.Tensor, w: torch.Tensor, epi: str = "none", residual: torch.Te
     """
     if isinstance(w, QuantizedWeight):
         return gemm_q(x, w, epi, residual, out, bias, splits)
+    if not isinstance(w, torch.Tensor) and hasattr(w, "gemm"):  # e.g. rotation.RotatedWeight
+        return w.gemm(x, epi, bias=bias, residual=residual, out=out)
     if not x.is_cuda:
         y = gemm_ref(x, w, epi, residual, bias=bias)
         if out is not None:

@@ -92,7 +92,9 @@ def _grouped(L, xs, P, K, W, E, N, Y, ldy, bias, epi, chunks, n_chunks, max_chun
     _lib.check(rc, f"moe_grouped_gemm {what}")
 
 
-def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias):
+def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias, rot_in=None, rot_mid=None):
+    if rot_in is not None:
+        h = rot_in.rotate(h)
     T, K = h.shape
     k = idx.shape[1]
     if isinstance(experts_gu, QuantizedWeight):
@@ -125,6 +127,8 @@ def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias):
     _lib.check(L.b200_moe_gather(hc.data_ptr(), K, perm.data_ptr(), P, k, xs.data_ptr(), st), "moe_gather")
     _grouped(L, xs, P, K, experts_gu, E, N2, gu, F, gu_bias, _EPI[epi], chunks, n_chunks, max_chunks, BN, st,
              "gate/up")
+    if rot_mid is not None:
+        gu = rot_mid.rotate(gu)
     _grouped(L, gu, P, F, experts_d, E, K, ys, K, d_bias, 0, chunks, n_chunks, max_chunks, BN, st, "down")
     _lib.check(L.b200_moe_combine(ys.data_ptr(), T, K, pos.data_ptr(), w.data_ptr(), k, out.data_ptr(), None, None,
                                   st), "moe_combine")
@@ -132,11 +136,16 @@ def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias):
     return out
 
 
-def moe_experts(h, experts_gu, experts_d, w, idx, epi="swiglu", gu_bias=None, d_bias=None):
+def moe_experts(h, experts_gu, experts_d, w, idx, epi="swiglu", gu_bias=None, d_bias=None, rot_in=None,
+                rot_mid=None):
     """h [T, K]; experts_gu [E, 2F, K] (64-row interleaved gate/up); experts_d [E, K, F];
-    w [T, k] fp32 weights; idx [T, k] expert ids. Returns [T, K] in h.dtype."""
+    w [T, k] fp32 weights; idx [T, k] expert ids. Returns [T, K] in h.dtype.
+    `rot_in` / `rot_mid`: ParoQuant rotations of the gate/up and down inputs
+    shared by all experts (ops.rotation.PairwiseRotation)."""
     if h.is_cuda:
-        return _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias)
+        return _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias, rot_in, rot_mid)
+    if rot_in is not None:
+        h = rot_in.rotate(h)
     if isinstance(experts_gu, QuantizedWeight):
         E = experts_gu.num_experts
         experts_gu = torch.stack([experts_gu.expert(e).dequantize(torch.float32) for e in range(E)]).to(h.dtype)
@@ -156,6 +165,8 @@ def moe_experts(h, experts_gu, experts_d, w, idx, epi="swiglu", gu_bias=None, d_
         rows = tok[start:start + c]
         x = h.index_select(0, rows).contiguous()
         gu = gemm(x, experts_gu[e], epi=epi, bias=None if gu_bias is None else gu_bias[e])
+        if rot_mid is not None:
+            gu = rot_mid.rotate(gu)
         y = gemm(gu, experts_d[e], bias=None if d_bias is None else d_bias[e])
         out.index_add_(0, rows, y.float() * wsorted[start:start + c, None])
         start += c
