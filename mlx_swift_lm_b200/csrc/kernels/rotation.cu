@@ -78,6 +78,43 @@ __global__ void __launch_bounds__(32) pair_rotate_kernel(const __nv_bfloat16* __
   }
 }
 
+// Block Walsh-Hadamard transform of activations (Prism Hadamard checkpoints):
+// per row and per `block` channels, y = H(s * x) / sqrt(block) (forward) or
+// y = s * H(x) / sqrt(block) (inverse); H is the natural-order Walsh-Hadamard
+// matrix, applied by log2(block) butterfly stages in shared memory. One CTA
+// per (row, block).
+__global__ void __launch_bounds__(512) block_hadamard_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
+                                                            int block, const float* __restrict__ signs, int inverse,
+                                                            __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_launch_dependents();
+  pdl_wait();
+  extern __shared__ float hb[];
+  const int row = blockIdx.x, b0 = blockIdx.y * block;
+  const __nv_bfloat16* xr = x + (size_t)row * ldx + b0;
+  for (int i = threadIdx.x; i < block; i += blockDim.x) {
+    float v = bf2f(xr[i]);
+    if (!inverse && signs) v *= signs[b0 + i];
+    hb[i] = v;
+  }
+  __syncthreads();
+  for (int h = 1; h < block; h <<= 1) {
+    for (int p = threadIdx.x; p < block / 2; p += blockDim.x) {
+      const int i = (p / h) * 2 * h + (p % h), j = i + h;
+      const float a = hb[i], b = hb[j];
+      hb[i] = a + b;
+      hb[j] = a - b;
+    }
+    __syncthreads();
+  }
+  const float sc = rsqrtf((float)block);
+  __nv_bfloat16* orow = out + (size_t)row * ldo + b0;
+  for (int i = threadIdx.x; i < block; i += blockDim.x) {
+    float v = hb[i] * sc;
+    if (inverse && signs) v *= signs[b0 + i];
+    orow[i] = f2bf(v);
+  }
+}
+
 }  // namespace rot
 }  // namespace b200
 
@@ -94,6 +131,26 @@ int b200_pair_rotate(const void* x, int ldx, int T, int K, const float* cos_t, c
   const dim3 grid((T + rot::kRows - 1) / rot::kRows, K / rot::kGroup);
   cudaError_t e = launch_k(rot::pair_rotate_kernel, grid, dim3(32), 0, st, 1,
                            reinterpret_cast<const __nv_bfloat16*>(x), ldx, T, K, cos_t, sin_t, pairs, scales, krot,
+                           reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+// x, out [T, K] bf16; block a power of two in [2, 8192] dividing K; signs [K] fp32 or null.
+int b200_block_hadamard(const void* x, int ldx, int T, int K, int block, const float* signs, int inverse, void* out,
+                        int ldo, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (block < 2 || block > 8192 || (block & (block - 1)) || (K % block)) return -1;
+  const size_t smem = (size_t)block * sizeof(float);
+  static bool cfg = false;
+  if (!cfg) {
+    cudaError_t e = cudaFuncSetAttribute(rot::block_hadamard_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         8192 * 4);
+    if (e != cudaSuccess) return (int)e;
+    cfg = true;
+  }
+  const int threads = block / 2 < 512 ? block / 2 : 512;
+  cudaError_t e = launch_k(rot::block_hadamard_kernel, dim3(T, K / block), dim3(threads), smem, st, 1,
+                           reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, block, signs, inverse,
                            reinterpret_cast<__nv_bfloat16*>(out), ldo);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }

@@ -25,8 +25,9 @@ from ..models.config import DecoderConfig
 from ..models.decoder import DecoderLM, LayerWeights, TensorParallel
 from ..models.families import build_config
 from ..ops import quant
-from ..ops.qlinear import SUPPORTED_BITS, SUPPORTED_GROUPS, QuantizedWeight
+from ..ops.qlinear import CARRIED_BITS, SUPPORTED_GROUPS, QuantizedWeight
 from ..ops.reference import interleave_gate_up as _interleave_dense
+from . import prism
 from .safetensors import load_safetensors
 
 
@@ -78,24 +79,34 @@ class CheckpointView:
     """Name lookup over a flat tensor dict with prefix detection and MLX-quantized
     linear dequantisation."""
 
-    def __init__(self, tensors: dict, qcfg: dict | None, dtype, keep_quantized: bool = False):
+    def __init__(self, tensors: dict, qcfg: dict | None, dtype, keep_quantized: bool = False, hadamard=None):
         self.t = tensors
         self.q = qcfg or {}
         self.dtype = dtype
         self.keep_quantized = keep_quantized
+        self.hadamard = hadamard  # Prism Hadamard metadata (loader.prism.HadamardMetadata)
         keys = list(tensors)
         self.prefix = ""
         for pre in ("model.language_model.", "language_model.model.", "model.", "transformer.", ""):
             if any(k.startswith(pre + "layers.0.") or k.startswith(pre + "embed_tokens") for k in keys):
                 self.prefix = pre
                 break
+        # names outside the decoder body (``language_model.lm_head`` next to
+        # ``language_model.model.layers``)
+        self.outer = self.prefix[:-len("model.")] if self.prefix.endswith("model.") else self.prefix
         self.used = set()
 
+    def _key(self, name):
+        for k in (self.prefix + name, name, self.outer + name):
+            if k in self.t:
+                return k
+        return None
+
     def has(self, name):
-        return (self.prefix + name) in self.t or name in self.t
+        return self._key(name) is not None
 
     def raw(self, name):
-        key = self.prefix + name if (self.prefix + name) in self.t else name
+        key = self._key(name) or name
         self.used.add(key)
         return self.t[key]
 
@@ -107,8 +118,30 @@ class CheckpointView:
 
     def linear(self, base, required=True, packed=True):
         """Weight of a linear layer `base` (without the .weight suffix). Affine
-        4/8-bit weights stay packed (QuantizedWeight) when the view keeps
-        quantised weights and `packed`; everything else is dequantised."""
+        2-8-bit weights stay packed (QuantizedWeight) when the view keeps
+        quantised weights and `packed`; everything else is dequantised. A
+        Prism Hadamard module (``.signs``) comes back as a RotatedWeight whose
+        rotation is its Hadamard transform."""
+        w = self._linear(base, required, packed)
+        if w is not None and self.hadamard is not None and self.has(base + ".signs"):
+            from ..ops.rotation import RotatedWeight
+
+            if isinstance(w, QuantizedWeight) and w.shape[0] % 8:  # the packed kernels tile 8 output rows
+                w = w.dequantize(torch.float32).to(self.dtype)
+            return RotatedWeight([(self.hadamard.transform(w.shape[1]), w)])
+        return w
+
+    def embedding(self, base):
+        """Dense embedding table; a Prism Hadamard embedding is inverse-
+        transformed once here, so lookups need no transform."""
+        w = self._linear(base, True, False)
+        if self.hadamard is not None and self.has(base + ".signs"):
+            from .prism import inverse_embedding
+
+            w = inverse_embedding(w.float(), self.hadamard.transform(w.shape[1])).to(self.dtype)
+        return w
+
+    def _linear(self, base, required=True, packed=True):
         wname = base + ".weight"
         if self.has(base + ".qweight"):  # AutoAWQ packing (ParoQuant checkpoints)
             return self._awq(base, packed)
@@ -186,6 +219,12 @@ class CheckpointView:
 
 
 def _rows(w, idx: torch.Tensor):
+    if _rotated([w]):
+        from ..ops.rotation import RotatedWeight
+
+        assert len(w.parts) == 1, "row selection of a single rotated projection"
+        r, inner = w.parts[0]
+        return RotatedWeight([(r, _rows(inner, idx))])
     return w.select_rows(idx) if isinstance(w, QuantizedWeight) else w.index_select(0, idx)
 
 
@@ -260,7 +299,7 @@ def _packed(w, s, b, mode, bits, gs):
     E = w.shape[0] if w.dim() == 3 else 0
     w2 = w.reshape(-1, w.shape[-1])
     s2 = s.reshape(-1, s.shape[-1])
-    if mode == "affine" and b is not None and bits in SUPPORTED_BITS and gs in SUPPORTED_GROUPS:
+    if mode == "affine" and b is not None and bits in CARRIED_BITS and gs in SUPPORTED_GROUPS:
         qw = QuantizedWeight.from_mlx(w2, s2.to(torch.bfloat16), b.reshape(-1, b.shape[-1]).to(torch.bfloat16), bits,
                                       gs)
     elif mode == "mxfp4" and bits == 4 and gs == 32:
@@ -318,11 +357,18 @@ def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParalle
     MLX affine 4/8-bit projections stay packed unless `keep_quantized` is False."""
     with open(os.path.join(path, "config.json")) as f:
         hf = json.load(f)
+    hadamard = None
+    if prism.is_prism(hf):
+        info = prism.parse_config(hf)
+        hadamard = prism.HadamardMetadata.read(path)
+        hf = prism.text_config(hf)
     cfg = build_config(hf)
     for k, v in (config_overrides or {}).items():
         setattr(cfg, k, v)
     tensors, _ = load_safetensors(path)
-    model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized)
+    if hadamard is not None:
+        prism.validate(info, hadamard, tensors)
+    model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized, hadamard=hadamard)
     if hf.get("vision_config") and hf.get("model_type") == "qwen2_vl":
         model = _attach_vision(model, cfg, hf, tensors, device, dtype)
     return model, hf
@@ -344,7 +390,7 @@ def _attach_vision(lm, cfg, hf, tensors, device, dtype):
 
 
 def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=torch.float32, tp=None,
-                       keep_quantized: bool = False):
+                       keep_quantized: bool = False, hadamard=None):
     """Build a DecoderLM from checkpoint tensors. With `keep_quantized`, MLX
     affine 4/8-bit projections of dense layers stay packed and run through
     the dequantising GEMM; embeddings, MoE experts and other formats are
@@ -352,7 +398,7 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
     tp = tp or TensorParallel()
     r, w = tp.rank, tp.world
     q = cfg.quantization if isinstance(cfg.quantization, dict) else None
-    ck = CheckpointView(tensors, q, torch.float32, keep_quantized=keep_quantized and bool(q))
+    ck = CheckpointView(tensors, q, torch.float32, keep_quantized=keep_quantized and bool(q), hadamard=hadamard)
     if cfg.layer_types and any(cfg.is_linear(i) for i in range(cfg.num_layers)):
         assert tp.world == 1, "hybrid (linear-attention) models load without tensor parallelism"
         # HF-format Qwen3-Next / 3.5 checkpoints store zero-centred layer norms
@@ -368,11 +414,11 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         v = ck.vec(name, required=True).float()
         return v + off
 
-    m.embed = ck.linear("embed_tokens", packed=False)
-    if cfg.extra.get("embedding_multiplier"):
-        pass
+    m.embed = ck.embedding("embed_tokens")
     m.norm = norm("norm.weight")
-    if cfg.tie_word_embeddings or not (ck.has("lm_head.weight") or "lm_head.weight" in tensors):
+    if hadamard is not None and not ck.has("lm_head.weight") and ck.has("embed_tokens.signs"):
+        m.lm_head = ck.linear("embed_tokens")  # tied head: packed table behind the forward transform
+    elif cfg.tie_word_embeddings or not (ck.has("lm_head.weight") or "lm_head.weight" in tensors):
         m.lm_head = m.embed
     else:
         m.lm_head = ck.linear("lm_head") if ck.has("lm_head.weight") else ck.linear("lm_head", False)

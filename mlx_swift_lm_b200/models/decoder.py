@@ -603,6 +603,8 @@ class DecoderLM:
         def mv(t):
             if t is None:
                 return None
+            if not isinstance(t, torch.Tensor):  # quantised / rotated weights
+                return t.to(device, dtype) if not isinstance(t, QuantizedWeight) else t.to(device)
             if t.is_floating_point() and t.dtype != torch.float32 or (t.dtype == torch.float32 and dtype != torch.float32):
                 return t.to(device=device, dtype=dtype if t.dtype != torch.float32 or True else t.dtype)
             return t.to(device=device)

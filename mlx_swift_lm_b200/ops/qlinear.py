@@ -33,6 +33,10 @@ import torch
 from . import quant
 
 SUPPORTED_BITS = (4, 8)
+# MLX affine widths the loader accepts; 2 / 3-bit codes ride in 4-bit
+# records and 5 / 6-bit codes in 8-bit records (same scales and biases, so
+# the dequantised values are exact)
+CARRIED_BITS = {2: 4, 3: 4, 4: 4, 5: 8, 6: 8, 8: 8}
 SUPPORTED_GROUPS = (32, 64, 128)  # affine / MXFP4; NVFP4 uses 16
 # e2m1 magnitudes of codes 0..7 (code bit 3 is the sign)
 E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
@@ -122,10 +126,11 @@ class QuantizedWeight:
 
     @classmethod
     def from_mlx(cls, packed: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, bits: int, gs: int):
-        """MLX layout: packed uint32 (as int32) [N, K*bits/32], scales / biases [N, K/gs]."""
+        """MLX layout: packed uint32 (as int32) [N, K*bits/32], scales / biases
+        [N, K/gs]. Widths other than 4 / 8 are stored at their carrier width."""
         K = scales.shape[-1] * gs
         q = quant.unpack_codes(packed.cpu(), bits, K)
-        return cls.from_codes(q, scales.cpu(), biases.cpu(), bits, gs)
+        return cls.from_codes(q, scales.cpu(), biases.cpu(), CARRIED_BITS[bits], gs)
 
     @classmethod
     def from_mxfp4(cls, q: torch.Tensor, scales_e8m0: torch.Tensor):

@@ -1,4 +1,5 @@
-"""ParoQuant: pairwise-rotation quantised linears.
+"""Activation transforms before quantised linears: ParoQuant pairwise
+rotations and Prism block-Hadamard transforms.
 
 Parity: MLXLMCommon/ParoQuant (RotateQuantizedLinear.swift:10-80 - y =
 quantised_matmul(rotate(x), W); PairwiseRotation.swift - channel scales then
@@ -22,6 +23,8 @@ from . import _lib
 _lib.register_signatures({
     "b200_pair_rotate": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.vp, _lib.vp,
                                     _lib.i32, _lib.vp, _lib.i32, _lib.vp]),
+    "b200_block_hadamard": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp,
+                                       _lib.i32, _lib.vp]),
 }, status_tags=("rotation",))
 
 GROUP = 128
@@ -78,6 +81,56 @@ class PairwiseRotation:
                                                _lib.stream_ptr(x.device)), "pair_rotate")
         _lib.count(1)
         return out
+
+
+class HadamardTransform:
+    """Block Walsh-Hadamard transform with sign flips (Prism Hadamard
+    checkpoints): forward y = H_b(s * x) / sqrt(b) per block of b channels;
+    H_b is orthogonal after the scaling, so the inverse is s * H_b(y) / sqrt(b)."""
+
+    def __init__(self, block: int, signs: torch.Tensor | None = None):
+        assert block >= 2 and block & (block - 1) == 0
+        self.block = block
+        self.signs = None if signs is None else signs.float().reshape(-1).contiguous()
+
+    def to(self, device, dtype=None):
+        return HadamardTransform(self.block, None if self.signs is None else self.signs.to(device))
+
+    def _ref(self, x, inverse):
+        T, K = x.shape
+        b = self.block
+        t = x.to(torch.promote_types(x.dtype, torch.float32))
+        if self.signs is not None and not inverse:
+            t = t * self.signs.to(t.device)
+        t = t.reshape(T, K // b, b)
+        h = 1
+        while h < b:
+            t = t.reshape(T, K // b, b // (2 * h), 2, h)
+            a, c = t[..., 0, :], t[..., 1, :]
+            t = torch.stack([a + c, a - c], -2)
+            h *= 2
+        t = t.reshape(T, K) / (b ** 0.5)
+        if self.signs is not None and inverse:
+            t = t * self.signs.to(t.device)
+        return t.to(x.dtype)
+
+    def _apply(self, x, inverse):
+        if not x.is_cuda:
+            return self._ref(x, inverse)
+        T, K = x.shape
+        x = x.contiguous()
+        out = torch.empty_like(x)
+        _lib.check(_lib.lib().b200_block_hadamard(x.data_ptr(), x.stride(0), T, K, self.block, _lib.ptr(self.signs),
+                                                  1 if inverse else 0, out.data_ptr(), out.stride(0),
+                                                  _lib.stream_ptr(x.device)), "block_hadamard")
+        _lib.count(1)
+        return out
+
+    def rotate(self, x):
+        return self._apply(x, False)
+
+    def inverse(self, y):
+        return self._apply(y, True)
 
 
 class RotatedWeight:
