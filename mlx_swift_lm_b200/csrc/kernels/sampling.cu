@@ -463,6 +463,75 @@ b200::launch_k(  sample_kernel, dim3(B), dim3(kThreads), 0, st, 1, a);
   return (int)cudaGetLastError();
 }
 
+// Greedy token, its softmax probability (the confidence of mask-diffusion
+// decoding) and the raw max logit per row, in one pass: each thread keeps a
+// running (max, sum of exp(x - max), index), rescaling the sum when the max
+// moves; warps and then the block merge the triples (ties -> smaller index).
+// p(argmax) = exp(m - logsumexp) = 1 / sum exp(x - m).
+__device__ __forceinline__ void merge_msi(float& m, float& s, int& i, float om, float os, int oi) {
+  if (om > m || (om == m && oi < i)) {
+    s = (m == -INFINITY ? 0.f : s * __expf(m - om)) + os;
+    m = om;
+    i = oi;
+  } else if (om != -INFINITY) {
+    s += os * __expf(om - m);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) argmax_conf_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                                                               int* __restrict__ tok, float* __restrict__ conf,
+                                                               float* __restrict__ mx) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
+  __shared__ float sm[32], ss[32];
+  __shared__ int si[32];
+  const float* lg = logits + (size_t)blockIdx.x * ld;
+  float m = -INFINITY, s = 0.f;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float x = lg[i];
+    if (x > m) {
+      s = (m == -INFINITY ? 0.f : s * __expf(m - x)) + 1.f;
+      m = x;
+      idx = i;
+    } else if (x != -INFINITY) {
+      s += __expf(x - m);
+    }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    merge_msi(m, s, idx, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o),
+              __shfl_xor_sync(0xffffffffu, idx, o));
+  if (lane == 0) {
+    sm[wid] = m;
+    ss[wid] = s;
+    si[wid] = idx;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    const bool live = lane < (int)(blockDim.x >> 5);
+    m = live ? sm[lane] : -INFINITY;
+    s = live ? ss[lane] : 0.f;
+    idx = live ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+      merge_msi(m, s, idx, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o),
+                __shfl_xor_sync(0xffffffffu, idx, o));
+    if (lane == 0) {
+      tok[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+      conf[blockIdx.x] = s > 0.f ? 1.f / s : 0.f;
+      if (mx) mx[blockIdx.x] = m;
+    }
+  }
+}
+
+int b200_argmax_conf(const float* logits, int64_t ld, int B, int V, int* tok, float* conf, float* mx, cudaStream_t st) {
+  if (B <= 0) return 0;
+  cudaError_t e = b200::launch_k(argmax_conf_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, tok, conf, mx);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
 int b200_argmax(const float* logits, int64_t ld, int B, int V, int* out, int* out2, cudaStream_t st) {
   if (B <= 0) return 0;
 b200::launch_k(  argmax_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, out, out2);

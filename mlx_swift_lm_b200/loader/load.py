@@ -87,7 +87,7 @@ class CheckpointView:
         self.hadamard = hadamard  # Prism Hadamard metadata (loader.prism.HadamardMetadata)
         keys = list(tensors)
         self.prefix = ""
-        for pre in ("model.language_model.", "language_model.model.", "model.", "transformer.", ""):
+        for pre in ("model.language_model.", "language_model.model.", "model.", "transformer.", "encoder.", ""):
             if any(k.startswith(pre + "layers.0.") or k.startswith(pre + "embed_tokens") for k in keys):
                 self.prefix = pre
                 break
@@ -418,6 +418,8 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
     m.norm = norm("norm.weight")
     if hadamard is not None and not ck.has("lm_head.weight") and ck.has("embed_tokens.signs"):
         m.lm_head = ck.linear("embed_tokens")  # tied head: packed table behind the forward transform
+    elif ck.has("diffusion_head.weight"):  # Nemotron-Labs-Diffusion
+        m.lm_head = ck.linear("diffusion_head")
     elif cfg.tie_word_embeddings or not (ck.has("lm_head.weight") or "lm_head.weight" in tensors):
         m.lm_head = m.embed
     else:

@@ -42,6 +42,8 @@ class ForwardBatch:
     pf_pos0_host: list | None = None
     # per-token rotary cos|sin table [T, rot_dim] replacing the position lookup (M-RoPE prompts)
     rope_table: torch.Tensor | None = None
+    # prefill rows attend to their whole chunk (mask-diffusion blocks) instead of causally
+    bidirectional: bool = False
 
     @property
     def num_tokens(self) -> int:

@@ -400,13 +400,15 @@ class DecoderLM:
         q = ops.qk_norm_rope_kv(qkv, positions, fb.slots, cos_sin, self.rot_dim, cfg.rope_interleaved,
                                 L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
                                 kv.k_scale(ki), kv.v_scale(ki))
+        q = self._pos_scale_q(q, fb.positions)
         win = cfg.window(li)
         if nd:
             ops.paged_decode(q[:nd], kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, win, L.sinks,
                              cfg.attn_logit_softcap, kv.k_scale(ki), kv.v_scale(ki), fb.dec_max_parts,
                              out=attn[:nd])
         if T > nd:
-            ops.paged_prefill(q[nd:], kc, vc, fb.pf_page_table, fb.pf_cu_q, fb.pf_pos0, cfg.scale, win, L.sinks,
+            ops.paged_prefill(q[nd:], kc, vc, fb.pf_page_table, fb.pf_cu_q, fb.pf_pos0, cfg.scale,
+                              -1 if fb.bidirectional else win, L.sinks,
                               cfg.attn_logit_softcap, kv.k_scale(ki), kv.v_scale(ki), fb.pf_cu_q_host,
                               out=attn[nd:])
         a2 = attn.view(T, self.H * self.D)
@@ -416,6 +418,17 @@ class DecoderLM:
             g0 = (self.H + 2 * self.KVH) * self.D
             a2 = sigmoid_mul(a2, qkv[:, g0:g0 + self.H * self.D])
         return self._attn_out(L, a2)
+
+    def _pos_scale_q(self, q, positions):
+        """Llama-4 query scaling by position (Ministral 3 / Nemotron-Labs-
+        Diffusion ``llama_4_scaling_beta``): q * (1 + beta * log(1 +
+        floor(p / original_max_position_embeddings)))."""
+        ps = self.cfg.extra.get("attn_pos_scale")
+        if not ps:
+            return q
+        beta, orig = ps
+        s = 1.0 + beta * torch.log1p(torch.floor(positions.float() / orig))
+        return (q.float() * s[:, None, None]).to(q.dtype)
 
     def _gdn_rows(self, fb: ForwardBatch):
         """Rows of `fb` for the linear-attention layers (cached on the batch):
@@ -505,9 +518,12 @@ class DecoderLM:
         return DenseKVCache(self.cfg.num_layers)
 
     @torch.no_grad()
-    def forward_dense(self, tokens: torch.Tensor, cache: DenseKVCache, return_hidden: bool = False):
+    def forward_dense(self, tokens: torch.Tensor, cache: DenseKVCache, return_hidden: bool = False,
+                      bidirectional: bool = False):
         """Single-sequence forward with a dense, concatenating KV cache (the
-        legacy single-request path). tokens [L] int; returns logits [L, V]."""
+        legacy single-request path). tokens [L] int; returns logits [L, V].
+        `bidirectional`: the new tokens attend to each other both ways (and
+        to the whole cache), as mask-diffusion blocks do."""
         cfg = self.cfg
         Lq = tokens.shape[0]
         p0 = cache.offset
@@ -536,9 +552,10 @@ class DecoderLM:
                 kk, vv = cache.update(ki, k, v)
                 kpos = cache.key_positions(ki) if hasattr(cache, "key_positions") else None
                 extra = cache.chunk_mask if hasattr(cache, "chunk_mask") else None
+                q = self._pos_scale_q(q, positions)
                 a = ref.attention_rows_ref(q.float(), kk.float(), vv.float(), positions, kk.shape[0], cfg.scale,
-                                           cfg.window(li), L.sinks, cfg.attn_logit_softcap, k_pos=kpos,
-                                           extra_mask=extra).to(x.dtype)
+                                           -1 if bidirectional else cfg.window(li), L.sinks, cfg.attn_logit_softcap,
+                                           k_pos=kpos, extra_mask=extra).to(x.dtype)
                 a2 = a.reshape(Lq, self.H * self.D).contiguous()
                 if cfg.attn_output_gate:
                     from ..ops.gdn import sigmoid_mul

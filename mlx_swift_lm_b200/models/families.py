@@ -38,6 +38,10 @@ register("gemma3", "gemma3_text", gemma=3)
 register("phi3", fused_qkv=True, fused_gate_up=True)
 register("gpt_oss", gpt_oss=True)
 register("glm4", fused_gate_up=True)
+register("mistral3", "ministral3")  # the text model of Mistral 3 / Ministral 3 (Llama-4 query scaling)
+# Ministral 3 backbone under ``encoder.*`` with a ``diffusion_head``; block
+# mask-diffusion decoding (engine/block_diffusion.py)
+register("nemotron_labs_diffusion", diffusion=True)
 register("cohere")
 register("starcoder2")
 
@@ -139,6 +143,18 @@ def build_config(hf: dict) -> DecoderConfig:
         cfg.extra["swiglu_limit"] = hf.get("swiglu_limit", 7.0)
         if not layer_types:
             cfg.layer_windows = [int(sw or 128) if i % 2 == 0 else 0 for i in range(cfg.num_layers)]
+    rp = hf.get("rope_parameters") or {}
+    if rp:
+        if "rope_theta" not in hf and "rope_theta" in rp:
+            cfg.rope_theta = float(rp["rope_theta"])
+        if cfg.rope_scaling is None and rp.get("rope_type", rp.get("type", "default")) != "default":
+            cfg.rope_scaling = dict(rp)
+        if rp.get("llama_4_scaling_beta") and rp.get("original_max_position_embeddings"):
+            cfg.extra["attn_pos_scale"] = (float(rp["llama_4_scaling_beta"]),
+                                           int(rp["original_max_position_embeddings"]))
+    if tr.get("diffusion"):
+        cfg.extra["mask_token_id"] = hf.get("mask_token_id", 100)
+        cfg.extra["diffusion_block"] = hf.get("block_size", 32)
     cfg.extra["fused_qkv"] = tr.get("fused_qkv", False)
     cfg.extra["fused_gate_up"] = tr.get("fused_gate_up", False)
     cfg.extra["mixtral_names"] = tr.get("mixtral_names", False)

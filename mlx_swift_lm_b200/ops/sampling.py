@@ -28,6 +28,27 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None, out2: torch.Te
     return out
 
 
+def argmax_confidence(logits: torch.Tensor):
+    """(greedy tokens [B] int32, softmax probability of that token [B] fp32,
+    max logit [B] fp32) of fp32 logits [B, V] in one pass (mask-diffusion
+    commit scores)."""
+    if not logits.is_cuda:
+        lf = logits.float()
+        mx, tok = lf.max(-1)
+        tok = lf.argmax(-1)
+        conf = torch.exp(mx - torch.logsumexp(lf, -1))
+        return tok.to(torch.int32), conf, mx
+    B, V = logits.shape
+    tok = torch.empty(B, dtype=torch.int32, device=logits.device)
+    conf = torch.empty(B, dtype=torch.float32, device=logits.device)
+    mx = torch.empty(B, dtype=torch.float32, device=logits.device)
+    rc = _lib.lib().b200_argmax_conf(logits.data_ptr(), logits.stride(0), B, V, tok.data_ptr(), conf.data_ptr(),
+                                     mx.data_ptr(), _lib.stream_ptr(logits.device))
+    _lib.check(rc, "argmax_conf")
+    _lib.count(1)
+    return tok, conf, mx
+
+
 def process_logits(logits, bias_ids=None, bias_vals=None, n_bias=None, rep_ids=None, n_rep=None, rep_penalty=None,
                    out_ids=None, n_out=None, freq=None, pres=None, allow_mask=None, mask_rows=None):
     """In-place logit bias, repetition / frequency / presence penalties and token mask (CUDA)."""
