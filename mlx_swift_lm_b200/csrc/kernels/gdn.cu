@@ -23,6 +23,16 @@
 //   gdn_norm_gate   one CTA per token: per-head RMSNorm * w * silu(z), bf16.
 // State: conv [S][3][C] bf16 (the last three pre-conv inputs), recurrent
 // [S][Hv][Dv][Dk] fp32.
+//
+// Mamba-2 mixers (NemotronH, Mamba2, hybrid SSM models) run on the same
+// kernels with mode 1. Reference behaviour: MLXLLM/Models/SSM.swift
+// (computeDt: dt = clip(softplus(dt + dt_bias), limits); the ssm step
+// state = exp(-exp(A_log) dt) state + dt x B^T, y = state C + D x) and
+// MLXLLM/Models/NemotronH.swift:51-160 (conv1d with bias + SiLU over x|B|C,
+// RMSNormGated: y * silu(z) normalised over groups of I / n_groups channels).
+// The mapping: key heads = n_groups with key dim = state size (C plays q and
+// B plays k), value heads = SSM heads with value dim = head dim (x plays v),
+// beta = dt, and the delta rule's S k correction is skipped.
 #include "b200_common.cuh"
 
 namespace b200 {
@@ -43,7 +53,9 @@ __device__ __forceinline__ int find_row(const int* __restrict__ cu, int R, int t
 __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 // P [T][ldp] bf16: q | k | v (C = 2 Hk Dk + Hv Dv channels) | z (Hv Dv) | b (Hv) | a (Hv)
-__global__ void __launch_bounds__(256) conv_kernel(int CB, const __nv_bfloat16* __restrict__ P, int ldp, int T,
+// (mode 1, Mamba-2: C | B | x | z | dt, no b)
+__global__ void __launch_bounds__(256) conv_kernel(int CB, int mode, const float* __restrict__ conv_b, float tmin,
+                                                   float tmax, const __nv_bfloat16* __restrict__ P, int ldp, int T,
                                                    const int* __restrict__ cu, int R, const int* __restrict__ fresh,
                                                    const int* __restrict__ slot,
                                                    const __nv_bfloat16* __restrict__ conv_state,
@@ -64,7 +76,7 @@ __global__ void __launch_bounds__(256) conv_kernel(int CB, const __nv_bfloat16* 
   const bool fr = fresh[r] != 0;
   const __nv_bfloat16* cs = conv_state + (size_t)slot[r] * (kTaps - 1) * C;
   for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
-    float acc = 0.f;
+    float acc = conv_b ? conv_b[c] : 0.f;
 #pragma unroll
     for (int j = 0; j < kTaps; ++j) {
       const int m = i - (kTaps - 1) + j;
@@ -78,7 +90,7 @@ __global__ void __launch_bounds__(256) conv_kernel(int CB, const __nv_bfloat16* 
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   float* out = qkv_out + (size_t)t * C;
-  const int h_lo = c0 / Dk, h_hi = min(2 * Hk, (c1 + Dk - 1) / Dk);
+  const int h_lo = c0 / Dk, h_hi = mode == 1 ? 0 : min(2 * Hk, (c1 + Dk - 1) / Dk);
   for (int hh = h_lo + warp; hh < h_hi; hh += nw) {
     const float* src = y + hh * Dk;
     float ss = 0.f;
@@ -88,9 +100,17 @@ __global__ void __launch_bounds__(256) conv_kernel(int CB, const __nv_bfloat16* 
     const float inv = rsqrtf(ss / (float)Dk + eps) * sc;
     for (int d = lane; d < Dk; d += 32) out[hh * Dk + d] = src[d] * inv;
   }
-  for (int c = max(c0, 2 * Hk * Dk) + threadIdx.x; c < c1; c += blockDim.x) out[c] = y[c];
+  for (int c = (mode == 1 ? c0 : max(c0, 2 * Hk * Dk)) + threadIdx.x; c < c1; c += blockDim.x) out[c] = y[c];
   if (blockIdx.y != 0) return;
   const __nv_bfloat16* pb = P + (size_t)t * ldp + C + Hv * Dv;
+  if (mode == 1) {
+    for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
+      const float dt = fminf(fmaxf(softplus(bf2f(pb[h]) + dt_bias[h]), tmin), tmax);
+      gb_out[(size_t)t * 2 * Hv + h] = __expf(-__expf(A_log[h]) * dt);
+      gb_out[(size_t)t * 2 * Hv + Hv + h] = dt;
+    }
+    return;
+  }
   for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
     const float b = bf2f(pb[h]), a = bf2f(pb[Hv + h]);
     gb_out[(size_t)t * 2 * Hv + h] = __expf(-__expf(A_log[h]) * softplus(a + dt_bias[h]));
@@ -102,13 +122,14 @@ __global__ void __launch_bounds__(256) conv_kernel(int CB, const __nv_bfloat16* 
 // (blockIdx.z * 4 + w) * RPW .. + RPW - 1. Decode batches use RPW = 4 so
 // each lane has 4 state loads of 16 bytes in flight (the step is a pure
 // stream of the fp32 states); long prefill rows use RPW = 1 for parallelism.
-template <int NK, int RPW>
+template <int NK, int RPW, bool MAMBA>
 __global__ void __launch_bounds__(128) recurrence_kernel(const float* __restrict__ qkv, const float* __restrict__ gb,
                                                          const int* __restrict__ cu, const int* __restrict__ fresh,
                                                          const int* __restrict__ slot, float* __restrict__ state,
                                                          int Hk, int Hv, int Dv, float* __restrict__ o,
                                                          const __nv_bfloat16* __restrict__ P, int ldp,
-                                                         __nv_bfloat16* __restrict__ conv_state, int C) {
+                                                         __nv_bfloat16* __restrict__ conv_state, int C,
+                                                         const float* __restrict__ Dskip) {
   pdl_launch_dependents();
   pdl_wait();
   constexpr int Dk = NK * 32;
@@ -160,15 +181,17 @@ __global__ void __launch_bounds__(128) recurrence_kernel(const float* __restrict
 #pragma unroll
         for (int i = 0; i < NK; ++i) {
           s[j][i] *= g;
-          kv[j] = fmaf(s[j][i], kk[i], kv[j]);
+          if constexpr (!MAMBA) kv[j] = fmaf(s[j][i], kk[i], kv[j]);
         }
       }
+      if constexpr (!MAMBA) {
 #pragma unroll
-      for (int j = 0; j < RPW; ++j) kv[j] = warp_sum(kv[j]);
+        for (int j = 0; j < RPW; ++j) kv[j] = warp_sum(kv[j]);
+      }
       float out[RPW];
 #pragma unroll
       for (int j = 0; j < RPW; ++j) {
-        const float delta = (v[j] - kv[j]) * beta;
+        const float delta = (v[j] - kv[j]) * beta;  // kv = 0 for Mamba-2: dt x
         out[j] = 0.f;
 #pragma unroll
         for (int i = 0; i < NK; ++i) {
@@ -178,6 +201,11 @@ __global__ void __launch_bounds__(128) recurrence_kernel(const float* __restrict
       }
 #pragma unroll
       for (int j = 0; j < RPW; ++j) out[j] = warp_sum(out[j]);
+      if constexpr (MAMBA) {
+        const float dd = Dskip[h];
+#pragma unroll
+        for (int j = 0; j < RPW; ++j) out[j] = fmaf(dd, v[j], out[j]);
+      }
       if (lane < RPW) {  // lane j stores row j (registers indexed by unrolled compare)
         float oj = out[0];
 #pragma unroll
@@ -216,18 +244,65 @@ __global__ void __launch_bounds__(128) recurrence_kernel(const float* __restrict
   }
 }
 
-template <int NK>
+template <int NK, bool MAMBA>
 static cudaError_t launch_rec(int rpw, int R, int Hv, int Dv, cudaStream_t st, const float* qkv, const float* gb,
                               const int* cu, const int* fresh, const int* slot, float* state, int Hk, float* o,
-                              const __nv_bfloat16* p, int ldp, __nv_bfloat16* cs, int C) {
+                              const __nv_bfloat16* p, int ldp, __nv_bfloat16* cs, int C, const float* Dskip) {
   if (rpw == 4) {
     const dim3 grid(R, Hv, (Dv + 15) / 16);
-    return launch_k(recurrence_kernel<NK, 4>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv,
-                    Dv, o, p, ldp, cs, C);
+    return launch_k(recurrence_kernel<NK, 4, MAMBA>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk,
+                    Hv, Dv, o, p, ldp, cs, C, Dskip);
   }
   const dim3 grid(R, Hv, (Dv + 3) / 4);
-  return launch_k(recurrence_kernel<NK, 1>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk, Hv, Dv,
-                  o, p, ldp, cs, C);
+  return launch_k(recurrence_kernel<NK, 1, MAMBA>, grid, dim3(128), 0, st, 1, qkv, gb, cu, fresh, slot, state, Hk,
+                  Hv, Dv, o, p, ldp, cs, C, Dskip);
+}
+
+template <int NK>
+static cudaError_t launch_rec_mode(int mode, int rpw, int R, int Hv, int Dv, cudaStream_t st, const float* qkv,
+                                   const float* gb, const int* cu, const int* fresh, const int* slot, float* state,
+                                   int Hk, float* o, const __nv_bfloat16* p, int ldp, __nv_bfloat16* cs, int C,
+                                   const float* Dskip) {
+  if (mode == 1)
+    return launch_rec<NK, true>(rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C, Dskip);
+  return launch_rec<NK, false>(rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C, Dskip);
+}
+
+// Mamba-2 gated norm: one CTA per (token, norm group): v = y * silu(z),
+// out = v * rsqrt(mean(v^2) + eps) * w over the group's channels -> bf16
+__global__ void __launch_bounds__(256) group_norm_gate_kernel(const float* __restrict__ o, int T, int I, int gsize,
+                                                              const __nv_bfloat16* __restrict__ z, int ldz,
+                                                              const __nv_bfloat16* __restrict__ w, float eps,
+                                                              __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float red[32];
+  const int t = blockIdx.x, c0 = blockIdx.y * gsize;
+  if (t >= T) return;
+  const float* src = o + (size_t)t * I + c0;
+  const __nv_bfloat16* zr = z + (size_t)t * ldz + c0;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < gsize; c += blockDim.x) {
+    const float zz = bf2f(zr[c]);
+    const float v = src[c] * (zz / (1.f + __expf(-zz)));
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    ss = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+    ss = warp_sum(ss);
+    if (lane == 0) red[0] = ss;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)gsize + eps);
+  for (int c = threadIdx.x; c < gsize; c += blockDim.x) {
+    const float zz = bf2f(zr[c]);
+    const float v = src[c] * (zz / (1.f + __expf(-zz)));
+    out[(size_t)t * ldo + c0 + c] = f2bf(v * inv * bf2f(w[c0 + c]));
+  }
 }
 
 // one CTA per token; warp per value head: rmsnorm(o) * w * silu(z) -> bf16
@@ -274,12 +349,16 @@ using namespace b200;
 
 extern "C" {
 
+// mode 0: Gated DeltaNet; mode 1: Mamba-2 (conv bias, no q/k normalisation,
+// dt gates clipped to [tmin, tmax], P without the b section)
 int b200_gdn_conv(const void* P, int ldp, int T, const int* cu, int R, const int* fresh, const int* slot,
                   const void* conv_state, const float* conv_w, int C, int Hk, int Dk, int Hv, int Dv,
                   const float* A_log, const float* dt_bias, float eps, float* qkv_out, float* gb_out,
-                  cudaStream_t st) {
+                  int mode, const float* conv_b, float tmin, float tmax, cudaStream_t st) {
   if (T <= 0) return 0;
-  if (R <= 0 || C != 2 * Hk * Dk + Hv * Dv || ldp < C + Hv * Dv + 2 * Hv || (Dv % Dk && Dk % Dv)) return -1;
+  if (R <= 0 || C != 2 * Hk * Dk + Hv * Dv || ldp < C + Hv * Dv + (mode == 1 ? 1 : 2) * Hv ||
+      (Dv % Dk && Dk % Dv))
+    return -1;
   // channel blocks of whole heads: 8 key heads' worth (multiples of Dk and Dv)
   int CB = 8 * (Dk > Dv ? Dk : Dv);
   if ((2 * Hk * Dk) % CB) CB = Dk > Dv ? Dk : Dv;
@@ -290,18 +369,19 @@ int b200_gdn_conv(const void* P, int ldp, int T, const int* cu, int R, const int
     if (e != cudaSuccess) return (int)e;
     cfg = true;
   }
-  cudaError_t e = launch_k(gdn::conv_kernel, dim3(T, (C + CB - 1) / CB), dim3(256), smem, st, 1, CB,
-                           reinterpret_cast<const __nv_bfloat16*>(P), ldp, T, cu, R, fresh, slot,
+  cudaError_t e = launch_k(gdn::conv_kernel, dim3(T, (C + CB - 1) / CB), dim3(256), smem, st, 1, CB, mode, conv_b,
+                           tmin, tmax, reinterpret_cast<const __nv_bfloat16*>(P), ldp, T, cu, R, fresh, slot,
                            reinterpret_cast<const __nv_bfloat16*>(conv_state), conv_w, C, Hk, Dk, Hv, Dv, A_log,
                            dt_bias, eps, qkv_out, gb_out);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
+// mode 1 (Mamba-2): no S k correction, y += D[h] x; Dskip [Hv] fp32
 int b200_gdn_recurrence(const float* qkv, const float* gb, const int* cu, int R, const int* fresh, const int* slot,
                         float* state, int Hk, int Dk, int Hv, int Dv, float* o, const void* P, int ldp,
-                        void* conv_state, int C, int T, cudaStream_t st) {
+                        void* conv_state, int C, int T, int mode, const float* Dskip, cudaStream_t st) {
   if (R <= 0) return 0;
-  if ((Hv % Hk) || (Dv % 16) || C != 2 * Hk * Dk + Hv * Dv) return -1;
+  if ((Hv % Hk) || (Dv % 16) || C != 2 * Hk * Dk + Hv * Dv || (mode == 1 && !Dskip)) return -1;
   const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(P);
   __nv_bfloat16* cs = reinterpret_cast<__nv_bfloat16*>(conv_state);
   // several value rows per warp when the batch alone fills the GPU (decode)
@@ -309,9 +389,18 @@ int b200_gdn_recurrence(const float* qkv, const float* gb, const int* cu, int R,
   const int rpw = (T <= 2 * R && warps4 >= 148 * 16) ? 4 : 1;
   cudaError_t e;
   switch (Dk) {
-    case 64: e = gdn::launch_rec<2>(rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C); break;
-    case 128: e = gdn::launch_rec<4>(rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C); break;
-    case 256: e = gdn::launch_rec<8>(rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C); break;
+    case 64:
+      e = gdn::launch_rec_mode<2>(mode, rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C,
+                                  Dskip);
+      break;
+    case 128:
+      e = gdn::launch_rec_mode<4>(mode, rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C,
+                                  Dskip);
+      break;
+    case 256:
+      e = gdn::launch_rec_mode<8>(mode, rpw, R, Hv, Dv, st, qkv, gb, cu, fresh, slot, state, Hk, o, p, ldp, cs, C,
+                                  Dskip);
+      break;
     default: return -1;
   }
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
@@ -321,6 +410,17 @@ int b200_gdn_norm_gate(const float* o, int T, int Hv, int Dv, const void* z, int
                        void* out, int ldo, cudaStream_t st) {
   if (T <= 0) return 0;
   cudaError_t e = launch_k(gdn::norm_gate_kernel, dim3(T, (Hv + 7) / 8), dim3(256), 0, st, 1, o, T, Hv, Dv,
+                           reinterpret_cast<const __nv_bfloat16*>(z), ldz, reinterpret_cast<const __nv_bfloat16*>(w),
+                           eps, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+// o [T][I] fp32, z [T][ldz] bf16, w [I] bf16; groups of gsize channels (I % gsize == 0)
+int b200_group_norm_gate(const float* o, int T, int I, int gsize, const void* z, int ldz, const void* w, float eps,
+                         void* out, int ldo, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (gsize <= 0 || I % gsize) return -1;
+  cudaError_t e = launch_k(gdn::group_norm_gate_kernel, dim3(T, I / gsize), dim3(256), 0, st, 1, o, T, I, gsize,
                            reinterpret_cast<const __nv_bfloat16*>(z), ldz, reinterpret_cast<const __nv_bfloat16*>(w),
                            eps, reinterpret_cast<__nv_bfloat16*>(out), ldo);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();

@@ -46,11 +46,13 @@ enum GemmEpilogue : int {
   kEpiGelu = 6,       // Y = bf16(gelu(acc)), erf form (BERT-family FFNs)
   kEpiGeluTanh = 7,   // Y = bf16(gelu(acc)), tanh approximation
   kEpiQuickGelu = 8,  // Y = bf16(acc * sigmoid(1.702 acc)) (CLIP / Qwen-VL vision MLPs)
+  kEpiRelu2 = 9,      // Y = bf16(relu(acc)^2) (NemotronH / Nemotron 3 MLPs)
 };
 
 __device__ __forceinline__ float gelu_act(int epi, float x) {
   if (epi == kEpiGelu) return 0.5f * x * (1.f + erff(x * 0.7071067811865476f));
   if (epi == kEpiQuickGelu) return x / (1.f + __expf(-1.702f * x));
+  if (epi == kEpiRelu2) return x > 0.f ? x * x : 0.f;
   const float c = 0.7978845608028654f;  // sqrt(2/pi)
   return 0.5f * x * (1.f + tanhf(c * (x + 0.044715f * x * x * x)));
 }
@@ -483,7 +485,8 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
           if (args.epi == kEpiAddBf16) {
             const float rr = (n + e < args.N) ? bf2f(args.R[m * args.ldr + n + e]) : 0.f;
             o[e] = f2bf(bf2f(f2bf(v[e])) + rr);
-          } else if (args.epi == kEpiGelu || args.epi == kEpiGeluTanh || args.epi == kEpiQuickGelu) {
+          } else if (args.epi == kEpiGelu || args.epi == kEpiGeluTanh || args.epi == kEpiQuickGelu ||
+                     args.epi == kEpiRelu2) {
             o[e] = f2bf(gelu_act(args.epi, v[e]));
           } else {
             o[e] = f2bf(v[e]);

@@ -123,7 +123,7 @@ class PagedKVCache:
         else:
             n = cls.pages_for(max_tokens or 4096) + 1
         c = cls(max(n_attn, 1), n, model.KVH, model.D, dt, dev, kv_fp8)
-        n_lin = model.cfg.num_layers - n_attn
+        n_lin = sum(1 for i in range(model.cfg.num_layers) if model.cfg.is_linear(i))
         if n_lin > 0:
             Hk, Dk, Hv, Dv = model.cfg.gdn_dims
             c.rec = RecurrentStatePool(n_lin, max_seqs, model.cfg.gdn_conv_dim, Hv, Dv, Dk,

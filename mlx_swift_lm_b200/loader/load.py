@@ -87,8 +87,10 @@ class CheckpointView:
         self.hadamard = hadamard  # Prism Hadamard metadata (loader.prism.HadamardMetadata)
         keys = list(tensors)
         self.prefix = ""
-        for pre in ("model.language_model.", "language_model.model.", "model.", "transformer.", "encoder.", ""):
-            if any(k.startswith(pre + "layers.0.") or k.startswith(pre + "embed_tokens") for k in keys):
+        for pre in ("model.language_model.", "language_model.model.", "model.", "transformer.", "encoder.", "backbone.",
+                    ""):
+            if any(k.startswith(pre + "layers.0.") or k.startswith(pre + "embed_tokens") or k.startswith(pre + "embeddings.")
+                   for k in keys):
                 self.prefix = pre
                 break
         # names outside the decoder body (``language_model.lm_head`` next to
@@ -293,6 +295,33 @@ def _load_linear_attn(ck: CheckpointView, cfg, L, p):
     L.wo = ck.linear(la + "out_proj")
 
 
+def _load_mamba(ck: CheckpointView, cfg, L, mx):
+    """Mamba-2 mixer weights. The in-projection's z | x | B | C | dt rows
+    (MLXLLM/Models/NemotronH.swift:140-150) are reordered to C | B | x | z |
+    dt, the layout of the recurrent kernels (C and B take the q and k
+    places), and the conv channels x | B | C to C | B | x."""
+    G, N, H, P = cfg.gdn_dims
+    I, GN = H * P, G * N
+    ar = torch.arange
+    idx = torch.cat([ar(2 * I + GN, 2 * I + 2 * GN), ar(2 * I, 2 * I + GN), ar(I, 2 * I), ar(0, I),
+                     ar(2 * I + 2 * GN, 2 * I + 2 * GN + H)])
+    L.wqkv = _rows(ck.linear(mx + "in_proj"), idx)
+    if ck.has(mx + "in_proj.bias"):
+        L.bqkv = ck.vec(mx + "in_proj.bias")[idx]
+    cidx = torch.cat([ar(I + GN, I + 2 * GN), ar(I, I + GN), ar(0, I)])
+    cw = ck.raw(mx + "conv1d.weight").float()
+    L.conv_w = (cw[:, 0, :] if cw.shape[-1] != 1 else cw[:, :, 0])[cidx].contiguous()
+    if ck.has(mx + "conv1d.bias"):
+        L.conv_b = ck.raw(mx + "conv1d.bias").float()[cidx].contiguous()
+    L.A_log = ck.raw(mx + "A_log").float()
+    L.dt_bias = ck.raw(mx + "dt_bias").float()
+    L.ssm_D = ck.raw(mx + "D").float()
+    L.gdn_norm = ck.vec(mx + "norm.weight", required=True)
+    L.wo = ck.linear(mx + "out_proj")
+    if ck.has(mx + "out_proj.bias"):
+        L.bo = ck.vec(mx + "out_proj.bias")
+
+
 def _packed(w, s, b, mode, bits, gs):
     """A packed QuantizedWeight for MLX affine 4/8-bit or MXFP4 weights the
     kernels serve (stacked experts [E, N, ...] keep num_experts), else None."""
@@ -405,7 +434,7 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         # and conv taps as [C, 1, K]; MLX-converted ones already hold 1 + w
         # and [C, K, 1] (the rule of MLXLLM/Models/Qwen3Next.swift:807-855)
         li = next(i for i in range(cfg.num_layers) if cfg.is_linear(i))
-        if ck.raw(f"layers.{li}.linear_attn.conv1d.weight").shape[-1] != 1:
+        if cfg.linear_kind == "gdn" and ck.raw(f"layers.{li}.linear_attn.conv1d.weight").shape[-1] != 1:
             cfg.norm_offset_one = True
     m = DecoderLM(cfg, "cpu", torch.float32, tp=tp)
     off = 1.0 if cfg.norm_offset_one else 0.0
@@ -414,8 +443,8 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         v = ck.vec(name, required=True).float()
         return v + off
 
-    m.embed = ck.embedding("embed_tokens")
-    m.norm = norm("norm.weight")
+    m.embed = ck.embedding("embed_tokens" if ck.has("embed_tokens.weight") else "embeddings")
+    m.norm = norm("norm.weight" if ck.has("norm.weight") else "norm_f.weight")
     if hadamard is not None and not ck.has("lm_head.weight") and ck.has("embed_tokens.signs"):
         m.lm_head = ck.linear("embed_tokens")  # tied head: packed table behind the forward transform
     elif ck.has("diffusion_head.weight"):  # Nemotron-Labs-Diffusion
@@ -433,6 +462,23 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
     for i in range(cfg.num_layers):
         p = f"layers.{i}."
         L = LayerWeights()
+        if cfg.layer_blocks:  # one block per layer (NemotronH / Mamba2): norm + mixer
+            L.block = cfg.block(i)
+            L.ln1 = norm(p + "norm.weight")
+            L.linear = cfg.is_linear(i)
+            mx = p + "mixer."
+            if L.block == "ffn":  # non-gated relu^2 MLP
+                L.moe = False
+                L.wgu = _shard_rows(ck.linear(mx + "up_proj"), r, w)
+                L.wd = _shard_cols(ck.linear(mx + "down_proj"), r, w)
+                if cfg.mlp_bias:
+                    L.bgu, L.bd = ck.vec(mx + "up_proj.bias"), ck.vec(mx + "down_proj.bias")
+            elif L.linear:
+                _load_mamba(ck, cfg, L, mx)
+            else:
+                _load_attention(ck, cfg, L, mx, norm, r, w)
+            m.layers.append(L)
+            continue
         L.ln1 = norm(p + "input_layernorm.weight")
         if cfg.post_norms:
             L.post_attn_norm = norm(p + "post_attention_layernorm.weight")

@@ -65,6 +65,15 @@ class DecoderConfig:
     linear_key_head_dim: int = 128
     linear_value_head_dim: int = 128
     linear_conv_kernel_dim: int = 4
+    # "gdn" (Gated DeltaNet) | "mamba2" (Mamba-2 mixers: key heads = n_groups,
+    # key dim = ssm state size, value heads = SSM heads, value dim = head dim)
+    linear_kind: str = "gdn"
+    ssm_dt_limits: tuple = (0.0, float("inf"))
+    mamba_norm_group: int = 0  # channels per group of the gated RMSNorm (0: one group)
+    mamba_conv_bias: bool = True
+    # per layer "both" (mixer + FFN), "mixer" (mixer only) or "ffn" (FFN only);
+    # None = "both" everywhere (NemotronH / Mamba2 layers hold one block each)
+    layer_blocks: list[str] | None = None
     # quantization of the checkpoint (MLX layout), informational
     quantization: dict | None = None
     # MTP (multi-token prediction) modules
@@ -89,7 +98,13 @@ class DecoderConfig:
         return int(self.layer_windows[layer])
 
     def is_linear(self, layer: int) -> bool:
-        return bool(self.layer_types) and self.layer_types[layer] == "linear_attention"
+        return bool(self.layer_types) and self.layer_types[layer] in ("linear_attention", "mamba")
+
+    def block(self, layer: int) -> str:
+        return self.layer_blocks[layer] if self.layer_blocks else "both"
+
+    def has_attention(self, layer: int) -> bool:
+        return not self.is_linear(layer) and self.block(layer) != "ffn"
 
     @property
     def gdn_dims(self) -> tuple[int, int, int, int]:
@@ -104,9 +119,10 @@ class DecoderConfig:
 
     @property
     def gdn_in_dim(self) -> int:
-        """Rows of the fused linear-layer in-projection: q | k | v | z | b | a."""
+        """Rows of the fused linear-layer in-projection: q | k | v | z | b | a
+        (Mamba-2: C | B | x | z | dt)."""
         Hk, Dk, Hv, Dv = self.gdn_dims
-        return self.gdn_conv_dim + Hv * Dv + 2 * Hv
+        return self.gdn_conv_dim + Hv * Dv + (Hv if self.linear_kind == "mamba2" else 2 * Hv)
 
     def is_moe(self, layer: int) -> bool:
         if self.num_experts <= 0:
@@ -117,7 +133,8 @@ class DecoderConfig:
 
     @property
     def glu_epi(self) -> str:
-        return {"silu": "swiglu", "gelu_tanh": "geglu", "gelu": "geglu", "swiglu_oai": "swiglu_oai"}[self.hidden_act]
+        return {"silu": "swiglu", "gelu_tanh": "geglu", "gelu": "geglu", "swiglu_oai": "swiglu_oai",
+                "relu2": "relu2"}[self.hidden_act]
 
     def to_dict(self) -> dict:
         return {f.name: getattr(self, f.name) for f in fields(self)}

@@ -36,10 +36,14 @@ class LayerWeights:
                  # linear-attention (Gated DeltaNet) layers: wqkv is the fused in-projection
                  # q|k|v|z|b|a and wo the out-projection
                  "linear", "conv_w", "A_log", "dt_bias", "gdn_norm",
+                 # Mamba-2 mixers (same fused layout; conv bias and the D skip term)
+                 "conv_b", "ssm_D",
+                 # "both" | "mixer" | "ffn": which blocks the layer holds
+                 "block",
                  # ParoQuant: activation rotations shared by the experts (gate/up input, down input)
                  "experts_rot_in", "experts_rot_mid")
 
-    F32 = ("sinks", "conv_w", "A_log", "dt_bias")  # kept in fp32 whatever the model dtype
+    F32 = ("sinks", "conv_w", "A_log", "dt_bias", "conv_b", "ssm_D")  # kept in fp32 whatever the model dtype
 
     def __init__(self):
         for s in self.__slots__:
@@ -149,6 +153,9 @@ class DecoderLM:
                 self.kv_index.append(-1)
                 self.rec_index.append(nl)
                 nl += 1
+            elif cfg.block(li) == "ffn":
+                self.kv_index.append(-1)
+                self.rec_index.append(-1)
             else:
                 self.kv_index.append(na)
                 self.rec_index.append(-1)
@@ -227,9 +234,19 @@ class DecoderLM:
             L.ln1 = ones(hd)
             L.ln2 = ones(hd)
             L.linear = cfg.is_linear(li)
+            L.block = cfg.block(li)
+            if L.block == "ffn":  # FFN-only layer: ln1 is its norm
+                L.ln2 = None
+                self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
+                if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
+                    self.layers.append(L)
+                continue
             if L.linear:
                 self._init_linear_layer(L, rn, g)
-                self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
+                if L.block == "both":
+                    self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
+                else:
+                    L.ln2 = None
                 if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
                     self.layers.append(L)
                 continue
@@ -253,7 +270,10 @@ class DecoderLM:
             if cfg.attention_sinks:
                 s = torch.empty(cfg.num_heads, device=dev, dtype=torch.float32).normal_(0.0, 1.0, generator=g)
                 L.sinks = rows(s, self.H)
-            self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
+            if L.block == "both":
+                self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
+            else:
+                L.ln2 = None
             if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
                 self.layers.append(L)
         return self
@@ -287,6 +307,10 @@ class DecoderLM:
         else:
             L.moe = False
             F = cfg.intermediate_size
+            if cfg.glu_epi == "relu2":  # non-gated MLP: wgu holds the up projection only
+                L.wgu = rows(rn(F, hd), self.F)
+                L.wd = cols(rn(hd, F))
+                return
             L.wgu = glu_pair(F, self.F, hd)
             L.wd = cols(rn(hd, F))
             if cfg.mlp_bias:
@@ -308,7 +332,12 @@ class DecoderLM:
         L.conv_w = rn(C, cfg.linear_conv_kernel_dim).float()
         L.A_log = torch.empty(Hv, device=dev, dtype=torch.float32).uniform_(1.0, 16.0, generator=g).log_()
         L.dt_bias = torch.ones(Hv, device=dev, dtype=torch.float32)
-        L.gdn_norm = torch.ones(Dv, device=dev, dtype=self.dtype)
+        if cfg.linear_kind == "mamba2":  # gated group norm over all channels; conv bias; D skip
+            L.gdn_norm = torch.ones(Hv * Dv, device=dev, dtype=self.dtype)
+            L.conv_b = rn(C).float() if cfg.mamba_conv_bias else None
+            L.ssm_D = torch.ones(Hv, device=dev, dtype=torch.float32)
+        else:
+            L.gdn_norm = torch.ones(Dv, device=dev, dtype=self.dtype)
         L.wo = rn(hd, Hv * Dv)
 
     # ------------------------------------------------------------------ pieces
@@ -373,12 +402,17 @@ class DecoderLM:
         attn = torch.empty((T, self.H, self.D), dtype=x.dtype, device=x.device)
         for li, L in enumerate(self.layers):
             h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            if L.block == "ffn":  # FFN-only layer (NemotronH "-" / "E")
+                delta = self._mlp(L, h)
+                continue
             if L.linear:
                 delta = self._gdn(L, h, fb, kv, li)
             else:
                 delta = self._attention(L, h, fb, kv, li, attn)
             if L.post_attn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+            if L.block == "mixer":
+                continue
             h = ops.add_rmsnorm(x, delta, L.ln2, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
             delta = self._mlp(L, h)
             if L.post_ffn_norm is not None:
@@ -459,12 +493,22 @@ class DecoderLM:
         from ..ops.gdn import gdn_layer
 
         cfg = self.cfg
-        Hk, Dk, Hv, Dv = cfg.gdn_dims
-        P = ops.gemm(h, L.wqkv)
+        P = ops.gemm(h, L.wqkv, bias=L.bqkv)
         conv, ssm = kv.rec.layer(self.rec_index[li])
-        y = gdn_layer(P, self._gdn_rows(fb), conv, ssm, L.conv_w, L.A_log, L.dt_bias, L.gdn_norm, Hk, Dk, Hv, Dv,
-                      cfg.rms_norm_eps)
-        return self._attn_out(L, y)
+        return self._attn_out(L, self._linear_body(L, P, self._gdn_rows(fb), conv, ssm))
+
+    def _linear_body(self, L, P, rows, conv, ssm):
+        """Gated DeltaNet or Mamba-2 body on the fused in-projection P."""
+        from ..ops.gdn import gdn_layer, mamba_layer
+
+        cfg = self.cfg
+        Hk, Dk, Hv, Dv = cfg.gdn_dims
+        if cfg.linear_kind == "mamba2":
+            grp = cfg.mamba_norm_group or Hv * Dv
+            return mamba_layer(P, rows, conv, ssm, L.conv_w, L.conv_b, L.A_log, L.dt_bias, L.ssm_D, L.gdn_norm, Hk,
+                               Dk, Hv, Dv, cfg.rms_norm_eps, grp, cfg.ssm_dt_limits)
+        return gdn_layer(P, rows, conv, ssm, L.conv_w, L.A_log, L.dt_bias, L.gdn_norm, Hk, Dk, Hv, Dv,
+                         cfg.rms_norm_eps)
 
     def _head(self, x, delta, fb, return_hidden, return_both, return_residual):
         cfg = self.cfg
@@ -532,17 +576,17 @@ class DecoderLM:
         delta = None
         for li, L in enumerate(self.layers):
             h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            if L.block == "ffn":
+                delta = self._mlp(L, h)
+                continue
             if L.linear:
-                from ..ops.gdn import GdnRows, gdn_layer
+                from ..ops.gdn import GdnRows
 
-                Hk, Dk, Hv, Dv = cfg.gdn_dims
                 conv, ssm = cache.rec_state(li, self)
                 i32 = dict(dtype=torch.int32, device=x.device)
                 rows = GdnRows(torch.tensor([0, Lq], **i32), torch.tensor([1 if p0 == 0 else 0], **i32),
                                torch.zeros(1, **i32), [0, Lq])
-                y = gdn_layer(ops.gemm(h, L.wqkv), rows, conv, ssm, L.conv_w, L.A_log, L.dt_bias, L.gdn_norm,
-                              Hk, Dk, Hv, Dv, cfg.rms_norm_eps)
-                delta = self._attn_out(L, y)
+                delta = self._attn_out(L, self._linear_body(L, ops.gemm(h, L.wqkv, bias=L.bqkv), rows, conv, ssm))
             else:
                 qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
                 q, k, v = ops.qk_norm_rope_kv(qkv, positions, None, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
@@ -565,6 +609,8 @@ class DecoderLM:
                 delta = self._attn_out(L, a2)
             if L.post_attn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+            if L.block == "mixer":
+                continue
             h = ops.add_rmsnorm(x, delta, L.ln2, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
             delta = self._mlp(L, h)
             if L.post_ffn_norm is not None:

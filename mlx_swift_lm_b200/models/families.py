@@ -42,6 +42,83 @@ register("mistral3", "ministral3")  # the text model of Mistral 3 / Ministral 3 
 # Ministral 3 backbone under ``encoder.*`` with a ``diffusion_head``; block
 # mask-diffusion decoding (engine/block_diffusion.py)
 register("nemotron_labs_diffusion", diffusion=True)
+# Mamba-2 hybrids: one block per layer (M mamba, * attention, - MLP), and pure Mamba-2
+register("nemotron_h", ssm="nemotron_h")
+register("mamba2", ssm="mamba2")
+
+_NEMOTRON_BLOCKS = {"mamba": "M", "attention": "*", "mlp": "-", "moe": "E"}
+
+
+def _ssm_dt_limits(hf: dict) -> tuple[float, float]:
+    """Execution limits of dt: ``time_step_limit`` ([min] or [min, max]),
+    else ``time_step_limit_min`` / ``_max``, else ``time_step_min`` /
+    ``_max``, else (0, inf) - the resolution order of
+    MLXLLM/Models/NemotronH.swift:2252-2280."""
+    lim = hf.get("time_step_limit")
+    if isinstance(lim, (list, tuple)) and lim:
+        if len(lim) > 2:
+            raise ValueError("time_step_limit requires one or two values")
+        lo, hi = float(lim[0]), float(lim[-1])
+    else:
+        lo = hf.get("time_step_limit_min", hf.get("time_step_min", 0.0))
+        hi = hf.get("time_step_limit_max", hf.get("time_step_max", float("inf")))
+        lo, hi = float(lo), float(hi)
+    if not (math.isfinite(lo) and lo >= 0 and hi >= lo):
+        raise ValueError(f"invalid dt limits ({lo}, {hi})")
+    return lo, hi
+
+
+def _ssm_prepare(hf: dict, kind: str) -> dict:
+    """Fill the attention keys a pure / hybrid SSM config may omit."""
+    hf = dict(hf)
+    if kind == "mamba2":
+        hf.setdefault("num_attention_heads", 1)
+        hf.setdefault("num_key_value_heads", 1)
+        hf["ssm_head_dim"] = hf["head_dim"]  # the SSM head dim; no attention layers
+        hf["head_dim"] = 64
+        hf.setdefault("intermediate_size", 0)
+        hf["rms_norm_eps"] = hf.get("layer_norm_epsilon", 1e-5)
+    else:
+        hf["rms_norm_eps"] = hf.get("layer_norm_epsilon", hf.get("norm_eps", 1e-5))
+    return hf
+
+
+def _ssm_config(cfg: DecoderConfig, hf: dict, kind: str):
+    """Mamba-2 mixer geometry and the per-layer block layout."""
+    if kind == "mamba2":
+        H, P = hf["num_heads"], hf["ssm_head_dim"]
+        N = hf.get("ssm_state_size", hf.get("state_size", 128))
+        pattern = "M" * cfg.num_layers
+        norm_groups = 1
+    else:
+        H, P, N = hf["mamba_num_heads"], hf["mamba_head_dim"], hf["ssm_state_size"]
+        pat = hf.get("hybrid_override_pattern")
+        if isinstance(pat, list):
+            pat = "".join(pat)
+        if not pat and hf.get("layers_block_type"):
+            pat = "".join(_NEMOTRON_BLOCKS[b] for b in hf["layers_block_type"])
+        if not pat or len(pat) != cfg.num_layers:
+            raise ValueError("nemotron_h needs hybrid_override_pattern or layers_block_type of num_hidden_layers")
+        if "E" in pat:
+            raise NotImplementedError("NemotronH MoE (E) layers are not served")
+        pattern = pat
+        norm_groups = hf.get("n_groups", 1)
+    G = hf.get("n_groups", 1)
+    cfg.linear_kind = "mamba2"
+    cfg.linear_num_key_heads, cfg.linear_key_head_dim = G, N
+    cfg.linear_num_value_heads, cfg.linear_value_head_dim = H, P
+    cfg.linear_conv_kernel_dim = hf.get("conv_kernel", 4)
+    cfg.mamba_norm_group = (H * P) // norm_groups
+    cfg.mamba_conv_bias = hf.get("use_conv_bias", True)
+    cfg.ssm_dt_limits = _ssm_dt_limits(hf)
+    cfg.layer_types = [{"M": "mamba", "*": "full_attention", "-": "mlp"}[c] for c in pattern]
+    cfg.layer_blocks = ["ffn" if c == "-" else "mixer" for c in pattern]
+    cfg.layer_windows = None
+    cfg.partial_rotary_factor = 0.0  # NemotronH attention has no positional rotation
+    cfg.hidden_act = "relu2"
+    cfg.mlp_bias = hf.get("mlp_bias", False)
+    cfg.attention_bias = hf.get("attention_bias", False)
+    cfg.extra["mamba_proj_bias"] = hf.get("mamba_proj_bias", hf.get("use_bias", False))
 register("cohere")
 register("starcoder2")
 
@@ -58,6 +135,8 @@ def build_config(hf: dict) -> DecoderConfig:
     tr = FAMILIES.get(mt)
     if tr is None:
         raise ValueError(f"unsupported model_type {mt!r}; supported: {', '.join(supported_model_types())}")
+    if tr.get("ssm"):
+        hf = _ssm_prepare(hf, tr["ssm"])
     hidden = hf["hidden_size"]
     heads = hf["num_attention_heads"]
     kvh = hf.get("num_key_value_heads") or heads
@@ -152,6 +231,8 @@ def build_config(hf: dict) -> DecoderConfig:
         if rp.get("llama_4_scaling_beta") and rp.get("original_max_position_embeddings"):
             cfg.extra["attn_pos_scale"] = (float(rp["llama_4_scaling_beta"]),
                                            int(rp["original_max_position_embeddings"]))
+    if tr.get("ssm"):
+        _ssm_config(cfg, hf, tr["ssm"])
     if tr.get("diffusion"):
         cfg.extra["mask_token_id"] = hf.get("mask_token_id", 100)
         cfg.extra["diffusion_block"] = hf.get("block_size", 32)

@@ -18,10 +18,12 @@ from . import reference as ref
 _lib.register_signatures({
     "b200_gdn_conv": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.vp, _lib.vp,
                                  _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.f32,
-                                 _lib.vp, _lib.vp, _lib.vp]),
+                                 _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.f32, _lib.f32, _lib.vp]),
     "b200_gdn_recurrence": (_lib.i32, [_lib.vp, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.vp, _lib.i32,
                                        _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.i32,
-                                       _lib.i32, _lib.vp]),
+                                       _lib.i32, _lib.i32, _lib.vp, _lib.vp]),
+    "b200_group_norm_gate": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.f32,
+                                        _lib.vp, _lib.i32, _lib.vp]),
     "b200_gdn_norm_gate": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.f32,
                                       _lib.vp, _lib.i32, _lib.vp]),
     "b200_sigmoid_mul": (_lib.i32, [_lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32,
@@ -64,13 +66,52 @@ def gdn_layer(P: torch.Tensor, rows: GdnRows, conv_state: torch.Tensor, ssm_stat
     y = torch.empty(T, Hv * Dv, dtype=P.dtype, device=P.device)
     _lib.check(L.b200_gdn_conv(P.data_ptr(), P.stride(0), T, rows.cu.data_ptr(), R, rows.fresh.data_ptr(),
                                rows.slot.data_ptr(), conv_state.data_ptr(), conv_w.data_ptr(), C, Hk, Dk, Hv, Dv,
-                               A_log.data_ptr(), dt_bias.data_ptr(), float(eps), qkv.data_ptr(), gb.data_ptr(), st),
-               "gdn_conv")
+                               A_log.data_ptr(), dt_bias.data_ptr(), float(eps), qkv.data_ptr(), gb.data_ptr(), 0,
+                               None, 0.0, 0.0, st), "gdn_conv")
     _lib.check(L.b200_gdn_recurrence(qkv.data_ptr(), gb.data_ptr(), rows.cu.data_ptr(), R, rows.fresh.data_ptr(),
                                      rows.slot.data_ptr(), ssm_state.data_ptr(), Hk, Dk, Hv, Dv, o.data_ptr(),
-                                     P.data_ptr(), P.stride(0), conv_state.data_ptr(), C, T, st), "gdn_recurrence")
+                                     P.data_ptr(), P.stride(0), conv_state.data_ptr(), C, T, 0, None, st),
+               "gdn_recurrence")
     _lib.check(L.b200_gdn_norm_gate(o.data_ptr(), T, Hv, Dv, P[:, C:].data_ptr(), P.stride(0), norm_w.data_ptr(),
                                     float(eps), y.data_ptr(), y.stride(0), st), "gdn_norm_gate")
+    _lib.count(3)
+    return y
+
+
+def mamba_layer(P: torch.Tensor, rows: GdnRows, conv_state: torch.Tensor, ssm_state: torch.Tensor,
+                conv_w: torch.Tensor, conv_b: torch.Tensor | None, A_log: torch.Tensor, dt_bias: torch.Tensor,
+                D: torch.Tensor, norm_w: torch.Tensor, G: int, N: int, H: int, Pd: int, eps: float, norm_group: int,
+                dt_limits: tuple[float, float] = (0.0, float("inf"))) -> torch.Tensor:
+    """Mamba-2 mixer body. P [T, C + H*Pd + H] = C | B | x (the conv
+    channels, C = 2*G*N + H*Pd) | z | dt rows of the fused in-projection;
+    returns rmsnorm_groups(y * silu(z)) * norm_w [T, H*Pd] (input of
+    out_proj) and advances each row's conv / SSM state ([S, H, Pd, N] fp32).
+    Parity: MLXLLM/Models/SSM.swift (computeDt, the SSM step) and
+    MLXLLM/Models/NemotronH.swift:51-160 (conv + SiLU, gated group norm)."""
+    T = P.shape[0]
+    C = 2 * G * N + H * Pd
+    if not P.is_cuda:
+        cu = rows.cu_host if rows.cu_host is not None else rows.cu.tolist()
+        return ref.mamba_layer_ref(P, cu, rows.fresh.tolist(), rows.slot.tolist(), conv_state, ssm_state, conv_w,
+                                   conv_b, A_log, dt_bias, D, norm_w, G, N, H, Pd, eps, norm_group, dt_limits)
+    L = _lib.lib()
+    st = _lib.stream_ptr(P.device)
+    R = rows.num_rows
+    xbc = torch.empty(T, C, dtype=torch.float32, device=P.device)
+    gb = torch.empty(T, 2 * H, dtype=torch.float32, device=P.device)
+    o = torch.empty(T, H * Pd, dtype=torch.float32, device=P.device)
+    y = torch.empty(T, H * Pd, dtype=P.dtype, device=P.device)
+    tmin, tmax = float(dt_limits[0]), float(min(dt_limits[1], 3.0e38))
+    _lib.check(L.b200_gdn_conv(P.data_ptr(), P.stride(0), T, rows.cu.data_ptr(), R, rows.fresh.data_ptr(),
+                               rows.slot.data_ptr(), conv_state.data_ptr(), conv_w.data_ptr(), C, G, N, H, Pd,
+                               A_log.data_ptr(), dt_bias.data_ptr(), float(eps), xbc.data_ptr(), gb.data_ptr(), 1,
+                               _lib.ptr(conv_b), tmin, tmax, st), "mamba_conv")
+    _lib.check(L.b200_gdn_recurrence(xbc.data_ptr(), gb.data_ptr(), rows.cu.data_ptr(), R, rows.fresh.data_ptr(),
+                                     rows.slot.data_ptr(), ssm_state.data_ptr(), G, N, H, Pd, o.data_ptr(),
+                                     P.data_ptr(), P.stride(0), conv_state.data_ptr(), C, T, 1, D.data_ptr(), st),
+               "mamba_recurrence")
+    _lib.check(L.b200_group_norm_gate(o.data_ptr(), T, H * Pd, norm_group, P[:, C:].data_ptr(), P.stride(0),
+                                      norm_w.data_ptr(), float(eps), y.data_ptr(), y.stride(0), st), "mamba_norm")
     _lib.count(3)
     return y
 

@@ -7,7 +7,8 @@ from . import _lib
 from .qlinear import QuantizedWeight
 from .reference import gemm_ref
 
-_EPI = {"none": 0, "swiglu": 1, "f32": 2, "add": 3, "geglu": 4, "swiglu_oai": 5, "gelu": 6, "gelu_tanh": 7, "quick_gelu": 8}
+_EPI = {"none": 0, "swiglu": 1, "f32": 2, "add": 3, "geglu": 4, "swiglu_oai": 5, "gelu": 6, "gelu_tanh": 7, "quick_gelu": 8,
+        "relu2": 9}
 _GLU = ("swiglu", "geglu", "swiglu_oai")
 _SMS: dict[int, int] = {}
 

@@ -49,7 +49,7 @@ def glu_act_ref(epi, g, u):
 
 def gemm_ref(x, w, epi="none", residual=None, out_dtype=None, bias=None):
     """y = epi(x @ w.T + bias) computed in fp32.
-    epi: none | swiglu | geglu | swiglu_oai | f32 | add | gelu | gelu_tanh | quick_gelu."""
+    epi: none | swiglu | geglu | swiglu_oai | f32 | add | gelu | gelu_tanh | quick_gelu | relu2."""
     acc = x.float() @ w.float().t()
     if bias is not None:
         acc = acc + bias.float()
@@ -69,6 +69,8 @@ def gemm_ref(x, w, epi="none", residual=None, out_dtype=None, bias=None):
         return torch.nn.functional.gelu(acc, approximate="tanh" if epi == "gelu_tanh" else "none").to(dt)
     if epi == "quick_gelu":
         return (acc * torch.sigmoid(1.702 * acc)).to(dt)
+    if epi == "relu2":
+        return torch.relu(acc).square().to(dt)
     return acc.to(dt)
 
 
@@ -396,4 +398,55 @@ def gdn_layer_ref(P, cu, fresh, slot, conv_state, ssm_state, conv_w, A_log, dt_b
         z = P[s0:s1, C:C + Hv * Dv].float().reshape(n, Hv, Dv)
         on = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + eps) * norm_w.float() * (z * torch.sigmoid(z))
         out[s0:s1] = on.reshape(n, -1)
+    return out.to(P.dtype)
+
+
+def mamba_layer_ref(P, cu, fresh, slot, conv_state, ssm_state, conv_w, conv_b, A_log, dt_bias, D, norm_w, G, N, H,
+                    Pd, eps, norm_group, dt_limits=(0.0, float("inf"))):
+    """Mamba-2 mixer body over a flattened batch of rows (fp32).
+    P [T, C + H*Pd + H] = C | B | x (conv channels, C = 2*G*N + H*Pd) | z | dt;
+    conv with bias + SiLU; dt = clip(softplus(dt + dt_bias)); per head h of
+    group g = h // (H // G): S <- exp(-exp(A_log) dt) S + dt x B^T,
+    y = S C + D x; out = rmsnorm over groups of `norm_group` channels of
+    (y * silu(z)) * norm_w. States as in :func:`gdn_layer_ref` with
+    ssm_state [S, H, Pd, N]. Semantics of MLXLLM/Models/SSM.swift and
+    MLXLLM/Models/NemotronH.swift (RMSNormGated with group_size)."""
+    T = P.shape[0]
+    C = 2 * G * N + H * Pd
+    taps = conv_w.shape[1]
+    out = torch.zeros(T, H * Pd, dtype=torch.float32, device=P.device)
+    rep = H // G
+    for r in range(len(cu) - 1):
+        s0, s1 = int(cu[r]), int(cu[r + 1])
+        n = s1 - s0
+        if n <= 0:
+            continue
+        sl = int(slot[r])
+        x = P[s0:s1, :C].float()
+        prev = torch.zeros(taps - 1, C, device=P.device) if int(fresh[r]) else conv_state[sl].float()
+        xx = torch.cat([prev, x], 0)
+        conv = torch.zeros(n, C, device=P.device) + (conv_b.float() if conv_b is not None else 0.0)
+        for j in range(taps):
+            conv += conv_w[:, j].float() * xx[j:j + n]
+        yv = conv * torch.sigmoid(conv)
+        Cm = yv[:, :G * N].reshape(n, G, N)
+        Bm = yv[:, G * N:2 * G * N].reshape(n, G, N)
+        xh = yv[:, 2 * G * N:].reshape(n, H, Pd)
+        dt = torch.nn.functional.softplus(P[s0:s1, C + H * Pd:C + H * Pd + H].float() + dt_bias.float())
+        dt = dt.clamp(dt_limits[0], dt_limits[1])
+        dA = torch.exp(-torch.exp(A_log.float()) * dt)
+        S = torch.zeros(H, Pd, N, device=P.device) if int(fresh[r]) else ssm_state[sl].float().clone()
+        o = torch.zeros(n, H, Pd, device=P.device)
+        for t in range(n):
+            Bh = Bm[t].repeat_interleave(rep, 0)
+            Ch = Cm[t].repeat_interleave(rep, 0)
+            S = S * dA[t][:, None, None] + (xh[t] * dt[t][:, None])[:, :, None] * Bh[:, None, :]
+            o[t] = (S * Ch[:, None, :]).sum(-1) + D.float()[:, None] * xh[t]
+        ssm_state[sl] = S.to(ssm_state.dtype)
+        conv_state[sl] = xx[-(taps - 1):].to(conv_state.dtype)
+        z = P[s0:s1, C:C + H * Pd].float()
+        v = o.reshape(n, -1) * (z * torch.sigmoid(z))
+        vg = v.reshape(n, -1, norm_group)
+        vg = vg * torch.rsqrt(vg.pow(2).mean(-1, keepdim=True) + eps)
+        out[s0:s1] = vg.reshape(n, -1) * norm_w.float()
     return out.to(P.dtype)
