@@ -37,12 +37,12 @@ namespace moe {
 
 // ---------------------------------------------------------------- router
 __global__ void route_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int mode, int norm_topk,
-                                  int* __restrict__ ids, float* __restrict__ w) {
+                                  int* __restrict__ ids, float* __restrict__ w, RouteExtra ex) {
   pdl_launch_dependents();
   pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (warp >= T) return;
-  route_topk_warp(logits + (size_t)warp * E, E, k, mode, norm_topk, ids + (size_t)warp * k, w + (size_t)warp * k);
+  route_topk_warp(logits + (size_t)warp * E, E, k, mode, norm_topk, ids + (size_t)warp * k, w + (size_t)warp * k, ex);
 }
 
 // ---------------------------------------------------------------- sort
@@ -406,12 +406,22 @@ using namespace b200;
 
 extern "C" {
 
+// mode 2 (sigmoid, group-limited, corrected selection): bias [E] or null,
+// n_group dividing E (<= 32), topk_group <= n_group, scale on the weights
 int b200_moe_route_topk(const float* logits, int T, int E, int k, int mode, int norm_topk, int* ids, float* w,
-                        cudaStream_t st) {
+                        const float* bias, int n_group, int topk_group, float scale, cudaStream_t st) {
   if (T <= 0) return 0;
-  if (E > 256 || k > 16) return -1;
+  if (E > 256 || k > 16 || mode < 0 || mode > 2) return -1;
+  if (mode == 2 && (n_group < 1 || n_group > 32 || E % n_group || topk_group < 1 || topk_group > n_group ||
+                    k > (E / n_group) * topk_group))
+    return -1;
+  RouteExtra ex;
+  ex.bias = bias;
+  ex.n_group = n_group;
+  ex.topk_group = topk_group;
+  ex.scale = scale;
   cudaError_t e = launch_k(moe::route_topk_kernel, dim3((T + 3) / 4), dim3(128), 0, st, 1, logits, T, E, k, mode,
-                           norm_topk, ids, w);
+                           norm_topk, ids, w, ex);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

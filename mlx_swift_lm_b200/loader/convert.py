@@ -53,6 +53,12 @@ def to_hf_config(cfg, quantization: dict | None = None) -> dict:
             d["mlp_only_layers"] = [i for i, x in enumerate(cfg.moe_layers) if not x]
         if cfg.shared_expert_intermediate_size:
             d["shared_expert_intermediate_size"] = cfg.shared_expert_intermediate_size
+        if cfg.router_mode == "sigmoid_group":  # GLM-4.5-style keys
+            first = next((i for i, x in enumerate(cfg.moe_layers or []) if x), 0)
+            d.update(n_routed_experts=cfg.num_experts, first_k_dense_replace=first, n_group=cfg.router_n_group,
+                     topk_group=cfg.router_topk_group, routed_scaling_factor=cfg.routed_scaling_factor,
+                     n_shared_experts=cfg.shared_expert_intermediate_size // max(cfg.moe_intermediate_size, 1),
+                     use_qk_norm=cfg.qk_norm, scoring_func="sigmoid")
     if cfg.layer_types:
         d.update(layer_types=list(cfg.layer_types), attn_output_gate=cfg.attn_output_gate,
                  linear_num_key_heads=cfg.linear_num_key_heads, linear_num_value_heads=cfg.linear_num_value_heads,
@@ -141,6 +147,8 @@ def export_tensors(model) -> dict[str, torch.Tensor]:
             if cfg.model_type == "gpt_oss":
                 raise ValueError("export of gpt-oss expert layouts is not supported")
             out[mp + "gate.weight"] = _dense(L.router)
+            if L.router_corr is not None:
+                out[mp + "gate.e_score_correction_bias"] = _dense(L.router_corr)
             E = L.experts_gu.num_experts if isinstance(L.experts_gu, QuantizedWeight) else L.experts_gu.shape[0]
             for e in range(E):
                 ge = L.experts_gu.expert(e) if isinstance(L.experts_gu, QuantizedWeight) else L.experts_gu[e]
@@ -151,9 +159,10 @@ def export_tensors(model) -> dict[str, torch.Tensor]:
                 out[f"{mp}experts.{e}.down_proj.weight"] = _dense(de)
             if L.shared_gu is not None:
                 g, u = deinterleave_gate_up(_dense(L.shared_gu))
-                out[mp + "shared_expert.gate_proj.weight"] = g
-                out[mp + "shared_expert.up_proj.weight"] = u
-                out[mp + "shared_expert.down_proj.weight"] = _dense(L.shared_d)
+                sp = mp + ("shared_experts." if cfg.router_mode == "sigmoid_group" else "shared_expert.")
+                out[sp + "gate_proj.weight"] = g
+                out[sp + "up_proj.weight"] = u
+                out[sp + "down_proj.weight"] = _dense(L.shared_d)
                 if L.shared_gate is not None:
                     out[mp + "shared_expert_gate.weight"] = _dense(L.shared_gate)
         else:

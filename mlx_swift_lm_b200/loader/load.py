@@ -578,8 +578,10 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
     # ParoQuant: rotations shared by all experts of the layer
     L.experts_rot_in = ck._rotation(mp + "experts.gate_up_weight_")
     L.experts_rot_mid = ck._rotation(mp + "experts.down_weight_")
+    if ck.has(mp + "gate.e_score_correction_bias"):  # sigmoid_group routers
+        L.router_corr = ck.raw(mp + "gate.e_score_correction_bias").float()
     if cfg.shared_expert_intermediate_size:
-        sp = mp + "shared_expert."
+        sp = mp + ("shared_experts." if ck.has(mp + "shared_experts.gate_proj.weight") else "shared_expert.")
         L.shared_gu = interleave_gate_up(_shard_rows(ck.linear(sp + "gate_proj"), r, w),
                                          _shard_rows(ck.linear(sp + "up_proj"), r, w))
         L.shared_d = _shard_cols(ck.linear(sp + "down_proj"), r, w)

@@ -52,7 +52,12 @@ class DecoderConfig:
     num_experts_per_tok: int = 0
     moe_intermediate_size: int = 0
     norm_topk_prob: bool = True
-    router_mode: str = "softmax_topk"  # softmax_topk (Qwen/Mixtral) | topk_softmax (GPT-OSS)
+    # softmax_topk (Qwen/Mixtral) | topk_softmax (GPT-OSS) | sigmoid_group (GLM-4.5 / DeepSeek-V3:
+    # sigmoid scores, corrected selection within the best router_topk_group of router_n_group groups)
+    router_mode: str = "softmax_topk"
+    router_n_group: int = 1
+    router_topk_group: int = 1
+    routed_scaling_factor: float = 1.0
     router_bias: bool = False
     moe_layers: list[bool] | None = None
     shared_expert_intermediate_size: int = 0

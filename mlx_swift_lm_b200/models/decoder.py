@@ -33,6 +33,8 @@ class LayerWeights:
     __slots__ = ("ln1", "wqkv", "bqkv", "q_norm", "k_norm", "wo", "bo", "ln2", "post_attn_norm", "post_ffn_norm",
                  "wgu", "bgu", "wd", "bd", "router", "router_b", "experts_gu", "experts_gu_b", "experts_d",
                  "experts_d_b", "shared_gu", "shared_d", "shared_gate", "sinks", "moe",
+                 # sigmoid_group routers: the selection-score correction (e_score_correction_bias)
+                 "router_corr",
                  # linear-attention (Gated DeltaNet) layers: wqkv is the fused in-projection
                  # q|k|v|z|b|a and wo the out-projection
                  "linear", "conv_w", "A_log", "dt_bias", "gdn_norm",
@@ -43,7 +45,7 @@ class LayerWeights:
                  # ParoQuant: activation rotations shared by the experts (gate/up input, down input)
                  "experts_rot_in", "experts_rot_mid")
 
-    F32 = ("sinks", "conv_w", "A_log", "dt_bias", "conv_b", "ssm_D")  # kept in fp32 whatever the model dtype
+    F32 = ("sinks", "conv_w", "A_log", "dt_bias", "conv_b", "ssm_D", "router_corr")  # kept in fp32 whatever the model dtype
 
     def __init__(self):
         for s in self.__slots__:
@@ -289,6 +291,8 @@ class DecoderLM:
             L.router = rn(E, hd)
             if cfg.router_bias:
                 L.router_b = rn(E)
+            if cfg.router_mode == "sigmoid_group":
+                L.router_corr = rn(E).float()
             L.experts_gu = glu_pair(Fe, self.Fe, hd, (E,))
             L.experts_d = cols(rn(E, hd, Fe))
             if cfg.mlp_bias:
@@ -359,7 +363,9 @@ class DecoderLM:
         from ..ops import moe as moe_ops
 
         logits = ops.gemm(h, L.router, epi="f32", bias=L.router_b)
-        w, idx = moe_ops.route_topk(logits, cfg.num_experts_per_tok, cfg.router_mode, cfg.norm_topk_prob)
+        w, idx = moe_ops.route_topk(logits, cfg.num_experts_per_tok, cfg.router_mode, cfg.norm_topk_prob,
+                                    L.router_corr, cfg.router_n_group, cfg.router_topk_group,
+                                    cfg.routed_scaling_factor)
         return w.float(), idx
 
     def _moe(self, L, h):

@@ -38,6 +38,7 @@ register("gemma3", "gemma3_text", gemma=3)
 register("phi3", fused_qkv=True, fused_gate_up=True)
 register("gpt_oss", gpt_oss=True)
 register("glm4", fused_gate_up=True)
+register("glm4_moe", moe=True, deepseek_router=True)  # GLM-4.5 / 4.6 / 4.7
 register("mistral3", "ministral3")  # the text model of Mistral 3 / Ministral 3 (Llama-4 query scaling)
 # Ministral 3 backbone under ``encoder.*`` with a ``diffusion_head``; block
 # mask-diffusion decoding (engine/block_diffusion.py)
@@ -231,6 +232,21 @@ def build_config(hf: dict) -> DecoderConfig:
         if rp.get("llama_4_scaling_beta") and rp.get("original_max_position_embeddings"):
             cfg.extra["attn_pos_scale"] = (float(rp["llama_4_scaling_beta"]),
                                            int(rp["original_max_position_embeddings"]))
+    if tr.get("deepseek_router"):
+        # routed + shared experts after `first_k_dense_replace` dense layers,
+        # sigmoid (or softmax) scores with group-limited corrected selection
+        # (MLXLLM/Models/GLM4MOE.swift:115-240)
+        cfg.num_experts = hf.get("n_routed_experts", 0)
+        cfg.moe_layers = [i >= hf.get("first_k_dense_replace", 0) for i in range(cfg.num_layers)]
+        cfg.norm_topk_prob = hf.get("norm_topk_prob", True)
+        cfg.router_mode = "sigmoid_group" if hf.get("scoring_func", "sigmoid") == "sigmoid" else "softmax_topk"
+        cfg.router_n_group = hf.get("n_group", 1) or 1
+        cfg.router_topk_group = hf.get("topk_group", 1) or 1
+        cfg.routed_scaling_factor = float(hf.get("routed_scaling_factor", 1.0))
+        cfg.shared_expert_intermediate_size = cfg.moe_intermediate_size * (hf.get("n_shared_experts") or 0)
+        cfg.shared_expert_gate = False
+        cfg.qk_norm = hf.get("use_qk_norm", False)
+        cfg.attention_bias = hf.get("attention_bias", False)
     if tr.get("ssm"):
         _ssm_config(cfg, hf, tr["ssm"])
     if tr.get("diffusion"):

@@ -29,7 +29,7 @@ _EPI = {"none": 0, "swiglu": 1, "geglu": 4, "swiglu_oai": 5}
 
 _lib.register_signatures({
     "b200_moe_route_topk": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp,
-                                       _lib.vp]),
+                                       _lib.vp, _lib.i32, _lib.i32, _lib.f32, _lib.vp]),
     "b200_moe_sort": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.vp,
                                  _lib.vp, _lib.vp]),
     "b200_moe_gather": (_lib.i32, [_lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.vp]),
@@ -44,30 +44,66 @@ _lib.register_signatures({
 }, status_tags=("moe",))
 
 
-def route_topk(logits: torch.Tensor, k: int, mode: str = "softmax_topk", norm_topk: bool = True):
+_MODES = {"softmax_topk": 0, "topk_softmax": 1, "sigmoid_group": 2}
+
+
+def route_topk(logits: torch.Tensor, k: int, mode: str = "softmax_topk", norm_topk: bool = True,
+               bias: torch.Tensor | None = None, n_group: int = 1, topk_group: int = 1, scale: float = 1.0):
     """Router top-k over fp32 logits [T, E]. softmax_topk: softmax over experts
     then top-k (optionally renormalised); topk_softmax: top-k logits then
-    softmax over the k. Returns (weights [T, k] fp32, ids [T, k] int32 on CUDA,
-    int64 on CPU)."""
+    softmax over the k; sigmoid_group: sigmoid scores, selection by score +
+    `bias` inside the `topk_group` best of `n_group` groups (group score =
+    sum of its two best biased scores), weights = the chosen sigmoid scores
+    (renormalised when `norm_topk` and k > 1) times `scale`. Returns
+    (weights [T, k] fp32, ids [T, k] int32 on CUDA, int64 on CPU)."""
     T, E = logits.shape
     if logits.is_cuda:
         assert E <= 256 and k <= 16, "router kernel supports up to 256 experts and k <= 16"
         lg = logits.float().contiguous()
         ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
         w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
-        _lib.check(_lib.lib().b200_moe_route_topk(lg.data_ptr(), T, E, k, 1 if mode == "topk_softmax" else 0,
-                                                  1 if norm_topk else 0, ids.data_ptr(), w.data_ptr(),
-                                                  _lib.stream_ptr(logits.device)), "moe_route_topk")
+        b = None if bias is None else bias.float().contiguous()
+        _lib.check(_lib.lib().b200_moe_route_topk(lg.data_ptr(), T, E, k, _MODES[mode], 1 if norm_topk else 0,
+                                                  ids.data_ptr(), w.data_ptr(), _lib.ptr(b), int(n_group),
+                                                  int(topk_group), float(scale), _lib.stream_ptr(logits.device)),
+                   "moe_route_topk")
         _lib.count(1)
         return w, ids
     if mode == "topk_softmax":
         v, idx = torch.topk(logits.float(), k, dim=-1)
         return torch.softmax(v, dim=-1), idx
+    if mode == "sigmoid_group":
+        return _route_sigmoid_group_ref(logits.float(), k, norm_topk, bias, n_group, topk_group, scale)
     p = torch.softmax(logits.float(), dim=-1)
     w, idx = torch.topk(p, k, dim=-1)
     if norm_topk:
         w = w / w.sum(-1, keepdim=True)
     return w, idx
+
+
+def _stable_topk(x: torch.Tensor, k: int):
+    """Top-k along the last dim with ties to the lower index."""
+    n = x.shape[-1]
+    key = x.double() - torch.arange(n, dtype=torch.float64, device=x.device) * 1e-12
+    return torch.topk(key, k, dim=-1).indices
+
+
+def _route_sigmoid_group_ref(lg, k, norm_topk, bias, n_group, topk_group, scale):
+    T, E = lg.shape
+    s = torch.sigmoid(lg)
+    sel = s + (bias.float() if bias is not None else 0.0)
+    if n_group > 1:
+        g = sel.reshape(T, n_group, E // n_group)
+        top2 = torch.sort(g, dim=-1, descending=True).values[..., :2].sum(-1) if E // n_group > 1 else g[..., 0]
+        keep = _stable_topk(top2, topk_group)
+        mask = torch.zeros(T, n_group, dtype=torch.bool, device=lg.device)
+        mask.scatter_(1, keep, True)
+        sel = torch.where(mask[..., None], g, torch.zeros_like(g)).reshape(T, E)
+    idx = _stable_topk(sel, k)
+    w = torch.gather(s, 1, idx)
+    if norm_topk and k > 1:
+        w = w / w.sum(-1, keepdim=True)
+    return w * scale, idx
 
 
 def chunk_rows(P: int, E: int) -> int:

@@ -170,6 +170,8 @@ class ExpertParallel:
         E_local experts. `tokens_max` is the largest T of any rank in this call
         (the same value on every rank; default `max_tokens`)."""
         assert _num_experts(experts_gu) == self.E_local
+        if mode not in ("softmax_topk", "topk_softmax"):
+            raise NotImplementedError(f"expert parallelism serves softmax routers, not {mode!r}")
         if self.impl == "fused":
             return self._moe_fused(h, logits, experts_gu, experts_d, epi, mode, norm_topk, gu_bias, d_bias,
                                    tokens_max or self.max_tokens)

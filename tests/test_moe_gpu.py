@@ -181,3 +181,18 @@ def test_moe_experts_mxfp4(T):
     r = _moe_ref(h.cpu(), gud.to(torch.bfloat16).cpu(), dd.to(torch.bfloat16).cpu(), w.cpu(), idx.cpu(), "swiglu_oai",
                  gub.cpu(), db.cpu())
     assert _rel(y.cpu(), r) < 2e-2
+
+
+@pytest.mark.parametrize("E,k,n_group,topk_group", [(160, 8, 1, 1), (256, 8, 8, 4), (64, 6, 4, 2)])
+def test_sigmoid_group_router_kernel(E, k, n_group, topk_group):
+    """GLM-4.5 / DeepSeek-V3 style router on the warp kernel against the CPU re-statement."""
+    from mlx_swift_lm_b200.ops import moe as moe_ops
+
+    torch.manual_seed(E + k)
+    lg = torch.randn(300, E) * 3
+    bias = torch.randn(E) * 0.2
+    w_ref, i_ref = moe_ops.route_topk(lg, k, "sigmoid_group", True, bias, n_group, topk_group, 2.5)
+    w, i = moe_ops.route_topk(lg.cuda(), k, "sigmoid_group", True, bias.cuda(), n_group, topk_group, 2.5)
+    torch.cuda.synchronize()
+    assert torch.equal(i.cpu().long(), i_ref)
+    assert torch.allclose(w.cpu(), w_ref, atol=1e-5)
