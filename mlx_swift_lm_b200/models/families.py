@@ -23,6 +23,7 @@ def register(*model_types, **traits):
 register("llama", "mistral", "smollm3", "helium", "apertus", "granite", "hunyuan_v1_dense", "exaone4",
          "ernie4_5", "internlm2", "minicpm", "olmo2", "olmo3", "nanbeige", "laguna", "acereason", "mellum")
 register("qwen2")  # q/k/v biases
+register("mimo")  # Xiaomi MiMo: the Qwen2 body (its MTP layers are not loaded)
 register("qwen2_vl", vlm="qwen2_vl")  # the language model of Qwen2-VL (q/k/v biases, M-RoPE)
 register("qwen3", qk_norm=True)
 register("qwen3_moe", qk_norm=True, moe=True)
@@ -150,7 +151,7 @@ def build_config(hf: dict) -> DecoderConfig:
         partial_rotary_factor=hf.get("partial_rotary_factor", 1.0),
         max_position_embeddings=hf.get("max_position_embeddings", 4096),
         tie_word_embeddings=hf.get("tie_word_embeddings", False), qk_norm=tr.get("qk_norm", False),
-        attention_bias=hf.get("attention_bias", mt in ("qwen2", "qwen2_vl")), o_bias=hf.get("o_bias", False),
+        attention_bias=hf.get("attention_bias", mt in ("qwen2", "qwen2_vl", "mimo")), o_bias=hf.get("o_bias", False),
         mlp_bias=hf.get("mlp_bias", False), quantization=hf.get("quantization") or hf.get("quantization_config"),
         hidden_act=_act(hf.get("hidden_activation") or hf.get("hidden_act") or "silu"))
     if cfg.rope_scaling and cfg.rope_scaling.get("rope_type", cfg.rope_scaling.get("type")) == "default":
