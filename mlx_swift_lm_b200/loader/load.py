@@ -487,7 +487,9 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         else:
             L.ln2 = norm(p + "post_attention_layernorm.weight")
         L.linear = cfg.is_linear(i)
-        if L.linear:
+        if L.linear and cfg.linear_kind == "mamba2":  # Granite 4 hybrids: layers.{i}.mamba.*
+            _load_mamba(ck, cfg, L, p + "mamba.")
+        elif L.linear:
             _load_linear_attn(ck, cfg, L, p)
         else:
             _load_attention(ck, cfg, L, p + "self_attn.", norm, r, w)
@@ -495,6 +497,14 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
             _load_moe(ck, cfg, L, p, r, w)
         else:
             mp = p + "mlp."
+            if ck.has(p + "shared_mlp.input_linear.weight"):  # Granite 4 dense: [gate | up] rows
+                mp = p + "shared_mlp."
+                g, u = ck.linear(mp + "input_linear", packed=False).chunk(2, 0)
+                L.moe = False
+                L.wgu = interleave_gate_up(_shard_rows(g, r, w), _shard_rows(u, r, w))
+                L.wd = _shard_cols(ck.linear(mp + "output_linear"), r, w)
+                m.layers.append(L)
+                continue
             if cfg.extra.get("fused_gate_up"):
                 gu = ck.linear(mp + "gate_up_proj", packed=False)
                 g, u = gu.chunk(2, 0)
@@ -511,7 +521,36 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         m.layers.append(L)
     if cfg.norm_offset_one:
         cfg.norm_offset_one = False  # folded into the stored weights
+    _fold_multipliers(m, cfg)
     return m.clone_to(device, dtype)
+
+
+def _scale(w, f: float):
+    if w is None or f == 1.0:
+        return w
+    if isinstance(w, QuantizedWeight):
+        try:
+            return w.scaled(f)
+        except ValueError:
+            return w.dequantize(torch.float32) * f
+    return w * f
+
+
+def _fold_multipliers(m, cfg):
+    """Granite-family multipliers folded into the weights: the residual
+    branch scale into the output projections of every block (o_proj /
+    out_proj, down / expert / shared outputs and their biases), and the
+    logits divisor into the head (untied from the embedding when shared).
+    Parity: MLXLLM/Models/Granite.swift and GraniteMoeHybrid.swift:430-442
+    (residual + branch * residual_multiplier, logits / logits_scaling)."""
+    rm = float(cfg.extra.get("residual_multiplier", 1.0))
+    ls = float(cfg.extra.get("logits_scaling", 1.0))
+    if rm != 1.0:
+        for L in m.layers:
+            for n in ("wo", "bo", "wd", "bd", "experts_d", "experts_d_b", "shared_d"):
+                setattr(L, n, _scale(getattr(L, n), rm))
+    if ls != 1.0:
+        m.lm_head = _scale(m.lm_head, 1.0 / ls)  # a new tensor: the embedding keeps its values
 
 
 def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
@@ -559,6 +598,9 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
         return
     mixtral = cfg.extra.get("mixtral_names")
     mp = p + ("block_sparse_moe." if mixtral else "mlp.")
+    if ck.has(p + "block_sparse_moe.router.layer.weight"):  # Granite 4 hybrids (HF names)
+        _load_granite_moe(ck, cfg, L, p, r, w)
+        return
     L.router = ck.linear(mp + "gate", packed=False)
     names = ("w1", "w3", "w2") if mixtral else ("gate_proj", "up_proj", "down_proj")
     # quantised experts stay packed when every expert's format is one the
@@ -587,6 +629,27 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
         L.shared_d = _shard_cols(ck.linear(sp + "down_proj"), r, w)
         if ck.has(mp + "shared_expert_gate.weight"):
             L.shared_gate = ck.linear(mp + "shared_expert_gate", packed=False)
+
+
+def _load_granite_moe(ck: CheckpointView, cfg, L, p, r, w):
+    """GraniteMoeHybrid experts: router ``block_sparse_moe.router.layer``,
+    ``input_linear`` [E, 2F, H] with the gate rows first, ``output_linear``
+    [E, H, F], and the shared MLP ``shared_mlp.input_linear`` [2Fs, H] /
+    ``output_linear`` (MLXLLM/Models/GraniteMoeHybrid.swift:270-350)."""
+    mp = p + "block_sparse_moe."
+    L.router = ck.linear(mp + "router.layer", packed=False)
+    gu = ck.raw(mp + "input_linear.weight").to(ck.dtype)
+    dn = ck.raw(mp + "output_linear.weight").to(ck.dtype)
+    E = gu.shape[0]
+    F = gu.shape[1] // 2
+    L.experts_gu = torch.stack([interleave_gate_up(_shard_rows(gu[e, :F], r, w), _shard_rows(gu[e, F:], r, w))
+                                for e in range(E)])
+    L.experts_d = torch.stack([_shard_cols(dn[e], r, w) for e in range(E)])
+    sp = p + "shared_mlp."
+    if ck.has(sp + "input_linear.weight"):
+        g, u = ck.linear(sp + "input_linear", packed=False).chunk(2, 0)
+        L.shared_gu = interleave_gate_up(_shard_rows(g, r, w), _shard_rows(u, r, w))
+        L.shared_d = _shard_cols(ck.linear(sp + "output_linear"), r, w)
 
 
 def _mxfp4_packed(blocks, scales) -> QuantizedWeight:

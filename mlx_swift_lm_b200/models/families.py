@@ -46,6 +46,8 @@ register("mistral3", "ministral3")  # the text model of Mistral 3 / Ministral 3 
 register("nemotron_labs_diffusion", diffusion=True)
 # Mamba-2 hybrids: one block per layer (M mamba, * attention, - MLP), and pure Mamba-2
 register("nemotron_h", ssm="nemotron_h")
+# IBM Granite 4 hybrids: Mamba-2 or attention mixer + MoE (top-k softmax over the k) + shared MLP per layer
+register("granitemoehybrid", ssm="granite", moe=True, mixtral_names=False)
 register("mamba2", ssm="mamba2")
 
 _NEMOTRON_BLOCKS = {"mamba": "M", "attention": "*", "mlp": "-", "moe": "E"}
@@ -73,6 +75,8 @@ def _ssm_dt_limits(hf: dict) -> tuple[float, float]:
 def _ssm_prepare(hf: dict, kind: str) -> dict:
     """Fill the attention keys a pure / hybrid SSM config may omit."""
     hf = dict(hf)
+    if kind == "granite":
+        return hf
     if kind == "mamba2":
         hf.setdefault("num_attention_heads", 1)
         hf.setdefault("num_key_value_heads", 1)
@@ -92,6 +96,38 @@ def _ssm_config(cfg: DecoderConfig, hf: dict, kind: str):
         N = hf.get("ssm_state_size", hf.get("state_size", 128))
         pattern = "M" * cfg.num_layers
         norm_groups = 1
+    elif kind == "granite":
+        H, P, N = hf["mamba_n_heads"], hf["mamba_d_head"], hf["mamba_d_state"]
+        G = hf.get("mamba_n_groups", 1)
+        lim = hf.get("time_step_limit") or [0.001, 100.0]
+        cfg.linear_kind = "mamba2"
+        cfg.linear_num_key_heads, cfg.linear_key_head_dim = G, N
+        cfg.linear_num_value_heads, cfg.linear_value_head_dim = H, P
+        cfg.linear_conv_kernel_dim = hf.get("mamba_d_conv", 4)
+        cfg.mamba_norm_group = (H * P) // G
+        cfg.mamba_conv_bias = hf.get("mamba_conv_bias", True)
+        cfg.ssm_dt_limits = (float(lim[0]), float(lim[-1]))
+        cfg.layer_types = ["mamba" if t == "mamba" else "full_attention" for t in hf["layer_types"]]
+        cfg.layer_blocks = None  # mixer + FFN in every layer
+        cfg.layer_windows = None
+        if hf.get("position_embedding_type", "rope") == "nope":
+            cfg.partial_rotary_factor = 0.0
+        cfg.extra["mamba_proj_bias"] = hf.get("mamba_proj_bias", False)
+        if hf.get("num_local_experts"):
+            cfg.num_experts = hf["num_local_experts"]
+            cfg.moe_intermediate_size = hf["intermediate_size"]
+            cfg.router_mode = "topk_softmax"
+            cfg.moe_layers = None
+            cfg.shared_expert_intermediate_size = hf.get("shared_intermediate_size", 0)
+            cfg.shared_expert_gate = False
+        else:
+            cfg.num_experts = 0
+        cfg.extra.update(residual_multiplier=hf.get("residual_multiplier", 1.0),
+                         logits_scaling=hf.get("logits_scaling", 1.0))
+        cfg.embed_scale = hf.get("embedding_multiplier", 1.0)
+        if hf.get("attention_multiplier"):
+            cfg.attn_scale = hf["attention_multiplier"]
+        return
     else:
         H, P, N = hf["mamba_num_heads"], hf["mamba_head_dim"], hf["ssm_state_size"]
         pat = hf.get("hybrid_override_pattern")

@@ -28,6 +28,8 @@ must start on a group boundary.
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 from . import quant
@@ -115,6 +117,14 @@ class QuantizedWeight:
 
     def _bsel(self, fn):
         return None if self.biases_t is None else fn(self.biases_t)
+
+    def scaled(self, m: float) -> "QuantizedWeight":
+        """The weight times `m` (affine records: scales and biases scaled;
+        e2m1 records only by powers of two, else ValueError)."""
+        if self.mode in ("mxfp4", "nvfp4") and not (m > 0 and math.log2(m).is_integer()):
+            raise ValueError("e2m1 records scale only by powers of two")
+        sc = (self.scales_t.float() * m).to(self.scales_t.dtype)
+        return self._like(self.codes, sc, self._bsel(lambda b: (b.float() * m).to(b.dtype)), self.num_experts)
 
     # ---------------------------------------------------------------- construction
     @classmethod
