@@ -145,3 +145,36 @@ def paged_prefill(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0
     _lib.check(rc, "paged_prefill")
     _lib.count(1)
     return out
+
+
+_lib.register_signatures({
+    "b200_paged_selected_decode": (_lib.i32, [_lib.vp, _lib.vp, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.vp,
+                                              _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.f32, _lib.vp,
+                                              _lib.vp]),
+})
+
+
+def paged_selected_decode(q, k_cache, v_cache, page_table, seq_lens, sel, scale, out=None):
+    """Decode attention of q [B, H, D] over only the selected token positions
+    sel [B, S] int32 (-1 = unused slot) of each row's paged KV
+    (csrc/kernels/attention_selected.cu on CUDA, the fp32 re-statement on
+    CPU). Positions outside [0, seq_len) are ignored."""
+    if not q.is_cuda:
+        y = ref.paged_selected_decode_ref(q, k_cache, v_cache, page_table, seq_lens, sel, scale)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    B, H, D = q.shape
+    KVH = k_cache.shape[1]
+    q = q.contiguous()
+    sel = sel.to(torch.int32).contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    _lib.check(_lib.lib().b200_paged_selected_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                                     page_table.data_ptr(), page_table.shape[1], seq_lens.data_ptr(),
+                                                     sel.data_ptr(), sel.shape[1], B, H, KVH, D, float(scale),
+                                                     out.data_ptr(), _lib.stream_ptr(q.device)),
+               "paged_selected_decode")
+    _lib.count(1)
+    return out

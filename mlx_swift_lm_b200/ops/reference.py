@@ -214,6 +214,27 @@ def paged_decode_ref(q, k_cache, v_cache, page_table, seq_lens, scale, window=0,
     return out.to(q.dtype)
 
 
+def paged_selected_decode_ref(q, k_cache, v_cache, page_table, seq_lens, sel, scale):
+    """Attention of q [B, H, D] over the positions sel[b] (-1 / out of range
+    ignored) of each row's pages; returns [B, H, D] in q.dtype."""
+    B, H, D = q.shape
+    KVH = k_cache.shape[1]
+    out = torch.zeros(B, H, D, dtype=torch.float32)
+    for b in range(B):
+        L = int(seq_lens[b])
+        pos = [int(t) for t in sel[b].tolist() if 0 <= int(t) < L]
+        if not pos:
+            continue
+        pids = page_table[b].tolist()
+        k = gather_pages(k_cache, pids, L).float()[pos]  # [n, KVH, D]
+        v = gather_pages(v_cache, pids, L).float()[pos]
+        kk = k.repeat_interleave(H // KVH, 1)
+        vv = v.repeat_interleave(H // KVH, 1)
+        s = torch.einsum("hd,nhd->hn", q[b].float(), kk) * scale
+        out[b] = torch.einsum("hn,nhd->hd", torch.softmax(s, -1), vv)
+    return out.to(q.dtype)
+
+
 def paged_prefill_ref(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0, sinks=None, softcap=0.0,
                       k_scale=None, v_scale=None):
     """q [T, H, D] (rows' chunks concatenated); returns [T, H, D]."""
