@@ -329,6 +329,66 @@ __global__ void __launch_bounds__(256) norm_gate_kernel(const float* __restrict_
   }
 }
 
+// LFM2 short convolution (MLXLLM/Models/LFM2.swift:207-233): P [T][ldp] =
+// B | C | x (C channels each); Bx = B * x; y = C * (sum_j w[c][j] Bx[t-L+1+j]
+// (+ bias)), the taps before a row's chunk read the conv state (the row's
+// last L - 1 Bx values, bf16). One thread per (token, channel); a second
+// kernel rolls the state once every token has read it.
+__global__ void __launch_bounds__(256) short_conv_kernel(const __nv_bfloat16* __restrict__ P, int ldp, int T,
+                                                         const int* __restrict__ cu, int R,
+                                                         const int* __restrict__ fresh, const int* __restrict__ slot,
+                                                         const __nv_bfloat16* __restrict__ conv_state,
+                                                         const float* __restrict__ w, const float* __restrict__ bias,
+                                                         int C, int taps, __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x, c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (t >= T || c >= C) return;
+  const int r = find_row(cu, R, t);
+  const int s0 = cu[r], i = t - s0;
+  const bool fr = fresh[r] != 0;
+  const __nv_bfloat16* cs = conv_state + (size_t)slot[r] * (taps - 1) * C;
+  float acc = bias ? bias[c] : 0.f;
+  for (int j = 0; j < taps; ++j) {
+    const int m = i - (taps - 1) + j;
+    float bx;
+    if (m >= 0) {
+      const __nv_bfloat16* pr = P + (size_t)(s0 + m) * ldp;
+      bx = bf2f(f2bf(bf2f(pr[c]) * bf2f(pr[2 * C + c])));  // Bx rounded as the stored state is
+    } else {
+      bx = fr ? 0.f : bf2f(cs[(size_t)(taps - 1 + m) * C + c]);
+    }
+    acc = fmaf(w[c * taps + j], bx, acc);
+  }
+  out[(size_t)t * ldo + c] = f2bf(bf2f(P[(size_t)t * ldp + C + c]) * acc);
+}
+
+__global__ void __launch_bounds__(256) short_conv_roll_kernel(const __nv_bfloat16* __restrict__ P, int ldp,
+                                                              const int* __restrict__ cu,
+                                                              const int* __restrict__ fresh,
+                                                              const int* __restrict__ slot,
+                                                              __nv_bfloat16* __restrict__ conv_state, int C,
+                                                              int taps) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x, c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const int s0 = cu[r], n = cu[r + 1] - s0;
+  const bool fr = fresh[r] != 0;
+  __nv_bfloat16* cs = conv_state + (size_t)slot[r] * (taps - 1) * C;
+  for (int j = 0; j < taps - 1; ++j) {  // reads ahead of the writes (m - j >= ... keeps order)
+    const int m = n - (taps - 1) + j;
+    __nv_bfloat16 x;
+    if (m >= 0) {
+      const __nv_bfloat16* pr = P + (size_t)(s0 + m) * ldp;
+      x = f2bf(bf2f(pr[c]) * bf2f(pr[2 * C + c]));
+    } else {
+      x = fr ? f2bf(0.f) : cs[(size_t)(taps - 1 + m) * C + c];
+    }
+    cs[(size_t)j * C + c] = x;
+  }
+}
+
 // out = x * sigmoid(g) (gated attention output), bf16 [T][N]
 __global__ void sigmoid_mul_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ g,
                                    int ldg, int T, int N, __nv_bfloat16* __restrict__ out, int ldo) {
@@ -423,6 +483,24 @@ int b200_group_norm_gate(const float* o, int T, int I, int gsize, const void* z,
   cudaError_t e = launch_k(gdn::group_norm_gate_kernel, dim3(T, I / gsize), dim3(256), 0, st, 1, o, T, I, gsize,
                            reinterpret_cast<const __nv_bfloat16*>(z), ldz, reinterpret_cast<const __nv_bfloat16*>(w),
                            eps, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+// LFM2 short conv: P [T][ldp] (B | C | x), rows as the recurrent kernels
+// take them, conv_state [S][taps-1][C] bf16, w [C][taps] fp32, bias [C] or
+// null; out [T][ldo] bf16 = C * conv(B * x). Advances each row's state.
+int b200_short_conv(const void* P, int ldp, int T, const int* cu, int R, const int* fresh, const int* slot,
+                    void* conv_state, const float* w, const float* bias, int C, int taps, void* out, int ldo,
+                    cudaStream_t st) {
+  if (T <= 0 || R <= 0) return 0;
+  if (taps < 2 || taps > 8 || ldp < 3 * C) return -1;
+  const auto* p = reinterpret_cast<const __nv_bfloat16*>(P);
+  auto* cs = reinterpret_cast<__nv_bfloat16*>(conv_state);
+  cudaError_t e = launch_k(gdn::short_conv_kernel, dim3(T, (C + 255) / 256), dim3(256), 0, st, 1, p, ldp, T, cu, R,
+                           fresh, slot, cs, w, bias, C, taps, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+  if (e != cudaSuccess) return (int)e;
+  e = launch_k(gdn::short_conv_roll_kernel, dim3(R, (C + 255) / 256), dim3(256), 0, st, 1, p, ldp, cu, fresh, slot,
+               cs, C, taps);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

@@ -295,6 +295,25 @@ def _load_linear_attn(ck: CheckpointView, cfg, L, p):
     L.wo = ck.linear(la + "out_proj")
 
 
+_LFM2_RENAMES = ((".self_attn.out_proj.", ".self_attn.o_proj."), (".self_attn.q_layernorm.", ".self_attn.q_norm."),
+                 (".self_attn.k_layernorm.", ".self_attn.k_norm."), (".operator_norm.", ".input_layernorm."),
+                 (".ffn_norm.", ".post_attention_layernorm."), (".feed_forward.w1.", ".mlp.gate_proj."),
+                 (".feed_forward.w3.", ".mlp.up_proj."), (".feed_forward.w2.", ".mlp.down_proj."),
+                 ("embedding_norm.", "norm."))
+
+
+def _lfm2_names(tensors: dict) -> dict:
+    """LFM2 tensor names -> the decoder's (operator / ffn norms, w1/w3/w2,
+    out_proj and q/k layernorms of the attention layers, embedding_norm as
+    the final norm); the short-conv layers keep ``conv.*``."""
+    out = {}
+    for k, v in tensors.items():
+        for a, b in _LFM2_RENAMES:
+            k = k.replace(a, b)
+        out[k] = v
+    return out
+
+
 def _load_mamba(ck: CheckpointView, cfg, L, mx):
     """Mamba-2 mixer weights. The in-projection's z | x | B | C | dt rows
     (MLXLLM/Models/NemotronH.swift:140-150) are reordered to C | B | x | z |
@@ -426,6 +445,8 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
     dequantised."""
     tp = tp or TensorParallel()
     r, w = tp.rank, tp.world
+    if cfg.linear_kind == "short_conv":
+        tensors = _lfm2_names(tensors)
     q = cfg.quantization if isinstance(cfg.quantization, dict) else None
     ck = CheckpointView(tensors, q, torch.float32, keep_quantized=keep_quantized and bool(q), hadamard=hadamard)
     if cfg.layer_types and any(cfg.is_linear(i) for i in range(cfg.num_layers)):
@@ -487,7 +508,19 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         else:
             L.ln2 = norm(p + "post_attention_layernorm.weight")
         L.linear = cfg.is_linear(i)
-        if L.linear and cfg.linear_kind == "mamba2":  # Granite 4 hybrids: layers.{i}.mamba.*
+        if L.linear and cfg.linear_kind == "short_conv":  # LFM2: layers.{i}.conv.*
+            mx = p + "conv."
+            L.wqkv = ck.linear(mx + "in_proj")
+            cw = ck.raw(mx + "conv.weight").float()
+            L.conv_w = (cw[:, 0, :] if cw.shape[-1] != 1 else cw[:, :, 0]).contiguous()
+            if ck.has(mx + "conv.bias"):
+                L.conv_b = ck.raw(mx + "conv.bias").float()
+            L.wo = ck.linear(mx + "out_proj")
+            if ck.has(mx + "in_proj.bias"):
+                L.bqkv = ck.vec(mx + "in_proj.bias")
+            if ck.has(mx + "out_proj.bias"):
+                L.bo = ck.vec(mx + "out_proj.bias")
+        elif L.linear and cfg.linear_kind == "mamba2":  # Granite 4 hybrids: layers.{i}.mamba.*
             _load_mamba(ck, cfg, L, p + "mamba.")
         elif L.linear:
             _load_linear_attn(ck, cfg, L, p)

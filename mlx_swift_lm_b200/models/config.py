@@ -103,7 +103,7 @@ class DecoderConfig:
         return int(self.layer_windows[layer])
 
     def is_linear(self, layer: int) -> bool:
-        return bool(self.layer_types) and self.layer_types[layer] in ("linear_attention", "mamba")
+        return bool(self.layer_types) and self.layer_types[layer] in ("linear_attention", "mamba", "conv")
 
     def block(self, layer: int) -> str:
         return self.layer_blocks[layer] if self.layer_blocks else "both"
@@ -119,6 +119,8 @@ class DecoderConfig:
 
     @property
     def gdn_conv_dim(self) -> int:
+        if self.linear_kind == "short_conv":  # LFM2: the conv runs over Bx (hidden channels)
+            return self.hidden_size
         Hk, Dk, Hv, Dv = self.gdn_dims
         return 2 * Hk * Dk + Hv * Dv
 
@@ -126,6 +128,8 @@ class DecoderConfig:
     def gdn_in_dim(self) -> int:
         """Rows of the fused linear-layer in-projection: q | k | v | z | b | a
         (Mamba-2: C | B | x | z | dt)."""
+        if self.linear_kind == "short_conv":
+            return 3 * self.hidden_size
         Hk, Dk, Hv, Dv = self.gdn_dims
         return self.gdn_conv_dim + Hv * Dv + (Hv if self.linear_kind == "mamba2" else 2 * Hv)
 

@@ -336,6 +336,11 @@ class DecoderLM:
         L.conv_w = rn(C, cfg.linear_conv_kernel_dim).float()
         L.A_log = torch.empty(Hv, device=dev, dtype=torch.float32).uniform_(1.0, 16.0, generator=g).log_()
         L.dt_bias = torch.ones(Hv, device=dev, dtype=torch.float32)
+        if cfg.linear_kind == "short_conv":  # LFM2: in_proj B|C|x, depthwise conv taps (+ bias), out_proj
+            L.conv_b = rn(C).float() if cfg.mamba_conv_bias else None
+            L.A_log = L.dt_bias = None
+            L.wo = rn(hd, hd)
+            return
         if cfg.linear_kind == "mamba2":  # gated group norm over all channels; conv bias; D skip
             L.gdn_norm = torch.ones(Hv * Dv, device=dev, dtype=self.dtype)
             L.conv_b = rn(C).float() if cfg.mamba_conv_bias else None
@@ -509,6 +514,10 @@ class DecoderLM:
 
         cfg = self.cfg
         Hk, Dk, Hv, Dv = cfg.gdn_dims
+        if cfg.linear_kind == "short_conv":
+            from ..ops.gdn import short_conv
+
+            return short_conv(P, rows, conv, L.conv_w, L.conv_b)
         if cfg.linear_kind == "mamba2":
             grp = cfg.mamba_norm_group or Hv * Dv
             return mamba_layer(P, rows, conv, ssm, L.conv_w, L.conv_b, L.A_log, L.dt_bias, L.ssm_D, L.gdn_norm, Hk,

@@ -49,6 +49,7 @@ register("nemotron_h", ssm="nemotron_h")
 # IBM Granite 4 hybrids: Mamba-2 or attention mixer + MoE (top-k softmax over the k) + shared MLP per layer
 register("granitemoehybrid", ssm="granite", moe=True, mixtral_names=False)
 register("mamba2", ssm="mamba2")
+register("lfm2", lfm2=True, qk_norm=True)  # Liquid LFM2: short-conv / attention hybrid
 
 _NEMOTRON_BLOCKS = {"mamba": "M", "attention": "*", "mlp": "-", "moe": "E"}
 
@@ -269,6 +270,33 @@ def build_config(hf: dict) -> DecoderConfig:
         if rp.get("llama_4_scaling_beta") and rp.get("original_max_position_embeddings"):
             cfg.extra["attn_pos_scale"] = (float(rp["llama_4_scaling_beta"]),
                                            int(rp["original_max_position_embeddings"]))
+    if tr.get("lfm2"):
+        # gated short-conv layers + attention layers, SwiGLU w1/w3/w2 FFN with
+        # the auto-adjusted width (MLXLLM/Models/LFM2.swift:36-110, 240-262)
+        n = cfg.num_layers
+        lt = hf.get("layer_types")
+        full = hf.get("full_attn_idxs")
+        if lt:
+            kinds = ["full_attention" if t == "full_attention" else "conv" for t in lt]
+        elif full is not None:
+            kinds = ["full_attention" if i in set(full) else "conv" for i in range(n)]
+        else:
+            kinds = ["full_attention"] * n
+        cfg.layer_types = kinds
+        cfg.layer_windows = None
+        cfg.linear_kind = "short_conv"
+        cfg.linear_conv_kernel_dim = hf.get("conv_L_cache", 3)
+        cfg.mamba_conv_bias = hf.get("conv_bias", False)
+        ff = hf.get("block_ff_dim", hf.get("intermediate_size", 4 * hidden))
+        if hf.get("block_auto_adjust_ff_dim", False):
+            ff = int(2 * ff / 3)
+            if hf.get("block_ffn_dim_multiplier"):
+                ff = int(hf["block_ffn_dim_multiplier"] * ff)
+            mo = hf.get("block_multiple_of", 256)
+            ff = mo * ((ff + mo - 1) // mo)
+        cfg.intermediate_size = ff
+        cfg.rms_norm_eps = hf.get("norm_eps", cfg.rms_norm_eps)
+        cfg.tie_word_embeddings = hf.get("tie_word_embeddings", True)
     if tr.get("deepseek_router"):
         # routed + shared experts after `first_k_dense_replace` dense layers,
         # sigmoid (or softmax) scores with group-limited corrected selection

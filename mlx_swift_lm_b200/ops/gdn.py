@@ -26,6 +26,8 @@ _lib.register_signatures({
                                         _lib.vp, _lib.i32, _lib.vp]),
     "b200_gdn_norm_gate": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.f32,
                                       _lib.vp, _lib.i32, _lib.vp]),
+    "b200_short_conv": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.vp,
+                                   _lib.vp, _lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp]),
     "b200_sigmoid_mul": (_lib.i32, [_lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.i32,
                                     _lib.vp]),
 }, status_tags=("gdn",))
@@ -114,6 +116,27 @@ def mamba_layer(P: torch.Tensor, rows: GdnRows, conv_state: torch.Tensor, ssm_st
                                       norm_w.data_ptr(), float(eps), y.data_ptr(), y.stride(0), st), "mamba_norm")
     _lib.count(3)
     return y
+
+
+def short_conv(P: torch.Tensor, rows: GdnRows, conv_state: torch.Tensor, conv_w: torch.Tensor,
+               conv_b: torch.Tensor | None) -> torch.Tensor:
+    """LFM2 short convolution: P [T, 3C] = B | C | x rows of the in-projection;
+    returns C * conv(B * x) [T, C] (input of out_proj) and advances each
+    row's conv state [S, taps-1, C] (the last Bx values).
+    Parity: MLXLLM/Models/LFM2.swift:207-233."""
+    T = P.shape[0]
+    C = conv_w.shape[0]
+    taps = conv_w.shape[1]
+    if not P.is_cuda:
+        cu = rows.cu_host if rows.cu_host is not None else rows.cu.tolist()
+        return ref.short_conv_ref(P, cu, rows.fresh.tolist(), rows.slot.tolist(), conv_state, conv_w, conv_b)
+    out = torch.empty(T, C, dtype=P.dtype, device=P.device)
+    _lib.check(_lib.lib().b200_short_conv(P.data_ptr(), P.stride(0), T, rows.cu.data_ptr(), rows.num_rows,
+                                          rows.fresh.data_ptr(), rows.slot.data_ptr(), conv_state.data_ptr(),
+                                          conv_w.data_ptr(), _lib.ptr(conv_b), C, taps, out.data_ptr(),
+                                          out.stride(0), _lib.stream_ptr(P.device)), "short_conv")
+    _lib.count(2)
+    return out
 
 
 def sigmoid_mul(x: torch.Tensor, g: torch.Tensor) -> torch.Tensor:

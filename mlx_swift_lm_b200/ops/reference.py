@@ -471,3 +471,27 @@ def mamba_layer_ref(P, cu, fresh, slot, conv_state, ssm_state, conv_w, conv_b, A
         vg = vg * torch.rsqrt(vg.pow(2).mean(-1, keepdim=True) + eps)
         out[s0:s1] = vg.reshape(n, -1) * norm_w.float()
     return out.to(P.dtype)
+
+
+def short_conv_ref(P, cu, fresh, slot, conv_state, conv_w, conv_b):
+    """LFM2 short convolution over a flattened batch of rows (fp32 math):
+    P [T, 3C] = B | C | x; y = C * (conv over Bx = B * x with the row's
+    conv state [S, taps-1, C] before its chunk); updates the state in place."""
+    C, taps = conv_w.shape
+    T = P.shape[0]
+    out = torch.zeros(T, C, dtype=torch.float32, device=P.device)
+    for r in range(len(cu) - 1):
+        s0, s1 = int(cu[r]), int(cu[r + 1])
+        n = s1 - s0
+        if n <= 0:
+            continue
+        sl = int(slot[r])
+        bx = (P[s0:s1, :C].float() * P[s0:s1, 2 * C:3 * C].float()).to(P.dtype).float()
+        prev = torch.zeros(taps - 1, C, device=P.device) if int(fresh[r]) else conv_state[sl].float()
+        xx = torch.cat([prev, bx], 0)
+        acc = torch.zeros(n, C, device=P.device) + (conv_b.float() if conv_b is not None else 0.0)
+        for j in range(taps):
+            acc += conv_w[:, j].float() * xx[j:j + n]
+        out[s0:s1] = P[s0:s1, C:2 * C].float() * acc
+        conv_state[sl] = xx[-(taps - 1):].to(conv_state.dtype)
+    return out.to(P.dtype)

@@ -83,3 +83,45 @@ def test_nemotron_h_engine_graphs_and_oracle():
     mc = m.clone_to("cpu", torch.float32)
     r = mc.forward_dense(p, mc.new_cache())
     assert _rel(lg, r) < 0.05
+
+
+@pytest.mark.parametrize("C,taps,lens", [(1024, 3, [1, 1, 40, 2, 300]), (2048, 4, [1] * 64)])
+def test_short_conv_matches_oracle(C, taps, lens):
+    """LFM2 short convolution kernel (and its state roll) against the fp32 oracle."""
+    from mlx_swift_lm_b200.ops.gdn import short_conv
+
+    torch.manual_seed(C + taps)
+    R = len(lens)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    T = cu[-1]
+    fresh = [i % 2 for i in range(R)]
+    slots = list(range(R))
+    P = (torch.randn(T, 3 * C) * 0.5).to(torch.bfloat16)
+    w, b = torch.randn(C, taps) * 0.5, torch.randn(C) * 0.1
+    cs0 = (torch.randn(R, taps - 1, C) * 0.5).to(torch.bfloat16)
+    cs_r = cs0.clone()
+    want = ref.short_conv_ref(P.float(), cu, fresh, slots, cs_r, w, b)
+    i32 = dict(dtype=torch.int32, device=DEV)
+    rows = GdnRows(torch.tensor(cu, **i32), torch.tensor(fresh, **i32), torch.tensor(slots, **i32), cu)
+    cs = cs0.to(DEV)
+    got = short_conv(P.to(DEV), rows, cs, w.to(DEV), b.to(DEV))
+    torch.cuda.synchronize()
+    assert _rel(got.cpu(), want) < 1e-2
+    assert _rel(cs.cpu(), cs_r.to(torch.bfloat16)) < 1e-2
+
+
+def test_lfm2_engine_graphs_match_eager():
+    hf = {"model_type": "lfm2", "vocab_size": 512, "hidden_size": 256, "num_hidden_layers": 4,
+          "num_attention_heads": 4, "num_key_value_heads": 2, "norm_eps": 1e-5, "conv_L_cache": 3,
+          "block_ff_dim": 512, "layer_types": ["conv", "full_attention", "conv", "conv"]}
+    m = DecoderLM(build_config(hf), DEV, torch.bfloat16).init_random(0, std=0.1)
+    g = torch.Generator().manual_seed(1)
+    ps = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (9, 40, 77)]
+
+    def eng(graphs):
+        return EngineV2(m, config=EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=4),
+                                               max_model_len=256, use_cuda_graphs=graphs, graph_buckets=(1, 2, 4)))
+
+    assert eng(True).generate(ps, max_tokens=16) == eng(False).generate(ps, max_tokens=16)
