@@ -447,6 +447,8 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
     r, w = tp.rank, tp.world
     if cfg.linear_kind == "short_conv":
         tensors = _lfm2_names(tensors)
+    if cfg.parallel_block:
+        return _build_phi(cfg, tensors, device, dtype)
     q = cfg.quantization if isinstance(cfg.quantization, dict) else None
     ck = CheckpointView(tensors, q, torch.float32, keep_quantized=keep_quantized and bool(q), hadamard=hadamard)
     if cfg.layer_types and any(cfg.is_linear(i) for i in range(cfg.num_layers)):
@@ -662,6 +664,30 @@ def _load_moe(ck: CheckpointView, cfg, L, p, r, w):
         L.shared_d = _shard_cols(ck.linear(sp + "down_proj"), r, w)
         if ck.has(mp + "shared_expert_gate.weight"):
             L.shared_gate = ck.linear(mp + "shared_expert_gate", packed=False)
+
+
+def _build_phi(cfg, tensors, device, dtype):
+    """Phi-1.5 / Phi-2 (MLXLLM/Models/Phi.swift): q/k/v/dense and fc1/fc2 with
+    biases, input_layernorm weight + bias, final_layernorm, biased lm_head."""
+    ck = CheckpointView(tensors, None, torch.float32)
+    m = DecoderLM(cfg, "cpu", torch.float32)
+    m.embed = ck.linear("embed_tokens", packed=False)
+    m.norm, m.norm_b = ck.vec("final_layernorm.weight", True), ck.vec("final_layernorm.bias", True)
+    m.lm_head = ck.linear("lm_head", packed=False)
+    m.lm_head_b = ck.raw("lm_head.bias").float() if ck.has("lm_head.bias") else None
+    for i in range(cfg.num_layers):
+        p = f"layers.{i}."
+        L = LayerWeights()
+        L.ln1, L.ln1_b = ck.vec(p + "input_layernorm.weight", True), ck.vec(p + "input_layernorm.bias", True)
+        a = p + "self_attn."
+        L.wqkv = torch.cat([ck.linear(a + n, packed=False) for n in ("q_proj", "k_proj", "v_proj")], 0)
+        L.bqkv = torch.cat([ck.vec(a + n + ".bias", True) for n in ("q_proj", "k_proj", "v_proj")], 0)
+        L.wo, L.bo = ck.linear(a + "dense", packed=False), ck.vec(a + "dense.bias", True)
+        L.moe = False
+        L.wgu, L.bgu = ck.linear(p + "mlp.fc1", packed=False), ck.vec(p + "mlp.fc1.bias", True)
+        L.wd, L.bd = ck.linear(p + "mlp.fc2", packed=False), ck.vec(p + "mlp.fc2.bias", True)
+        m.layers.append(L)
+    return m.clone_to(device, dtype)
 
 
 def _load_granite_moe(ck: CheckpointView, cfg, L, p, r, w):

@@ -76,6 +76,9 @@ class DecoderConfig:
     ssm_dt_limits: tuple = (0.0, float("inf"))
     mamba_norm_group: int = 0  # channels per group of the gated RMSNorm (0: one group)
     mamba_conv_bias: bool = True
+    # "rmsnorm" | "layernorm" (with bias; Phi-2); parallel_block: x + attn(ln(x)) + mlp(ln(x))
+    norm_kind: str = "rmsnorm"
+    parallel_block: bool = False
     # per layer "both" (mixer + FFN), "mixer" (mixer only) or "ffn" (FFN only);
     # None = "both" everywhere (NemotronH / Mamba2 layers hold one block each)
     layer_blocks: list[str] | None = None
@@ -143,7 +146,7 @@ class DecoderConfig:
     @property
     def glu_epi(self) -> str:
         return {"silu": "swiglu", "gelu_tanh": "geglu", "gelu": "geglu", "swiglu_oai": "swiglu_oai",
-                "relu2": "relu2"}[self.hidden_act]
+                "relu2": "relu2", "gelu_tanh_mlp": "gelu_tanh"}[self.hidden_act]
 
     def to_dict(self) -> dict:
         return {f.name: getattr(self, f.name) for f in fields(self)}

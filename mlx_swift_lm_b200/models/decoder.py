@@ -42,6 +42,8 @@ class LayerWeights:
                  "conv_b", "ssm_D",
                  # "both" | "mixer" | "ffn": which blocks the layer holds
                  "block",
+                 # LayerNorm bias of the (parallel-block) input norm (Phi-2)
+                 "ln1_b",
                  # ParoQuant: activation rotations shared by the experts (gate/up input, down input)
                  "experts_rot_in", "experts_rot_mid")
 
@@ -138,6 +140,8 @@ class DecoderLM:
         self.Fe = cfg.moe_intermediate_size // w if cfg.moe_intermediate_size else 0
         self.embed = None
         self.norm = None
+        self.norm_b = None  # final LayerNorm bias (norm_kind "layernorm")
+        self.lm_head_b = None  # head bias (Phi-2)
         self.lm_head = None
         self.layers: list[LayerWeights] = []
         self.mtp_layers: list = []
@@ -311,7 +315,7 @@ class DecoderLM:
         else:
             L.moe = False
             F = cfg.intermediate_size
-            if cfg.glu_epi == "relu2":  # non-gated MLP: wgu holds the up projection only
+            if cfg.glu_epi in ("relu2", "gelu_tanh"):  # non-gated MLP: wgu holds the up projection only
                 L.wgu = rows(rn(F, hd), self.F)
                 L.wd = cols(rn(hd, F))
                 return
@@ -389,7 +393,7 @@ class DecoderLM:
         return self.tp.reduce(out)
 
     def _final_logits(self, h):
-        logits = ops.gemm(h, self.lm_head, epi="f32")
+        logits = ops.gemm(h, self.lm_head, epi="f32", bias=self.lm_head_b)
         if self.cfg.final_logit_softcap > 0:
             c = self.cfg.final_logit_softcap
             logits = torch.tanh(logits / c) * c
@@ -412,9 +416,13 @@ class DecoderLM:
         delta = None
         attn = torch.empty((T, self.H, self.D), dtype=x.dtype, device=x.device)
         for li, L in enumerate(self.layers):
-            h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            h = self._norm(x, delta, L.ln1, L.ln1_b)
             if L.block == "ffn":  # FFN-only layer (NemotronH "-" / "E")
                 delta = self._mlp(L, h)
+                continue
+            if cfg.parallel_block:  # Phi-2: attention and MLP read the same normed input
+                a = self._attention(L, h, fb, kv, li, attn)
+                delta = (a.float() + self._mlp(L, h).float()).to(x.dtype)
                 continue
             if L.linear:
                 delta = self._gdn(L, h, fb, kv, li)
@@ -463,6 +471,13 @@ class DecoderLM:
             g0 = (self.H + 2 * self.KVH) * self.D
             a2 = sigmoid_mul(a2, qkv[:, g0:g0 + self.H * self.D])
         return self._attn_out(L, a2)
+
+    def _norm(self, x, delta, w, b=None):
+        """x <- x + delta; the block's input norm (RMSNorm, or LayerNorm with bias)."""
+        cfg = self.cfg
+        if cfg.norm_kind == "layernorm":
+            return ops.add_layernorm(x, delta, w, b, cfg.rms_norm_eps)
+        return ops.add_rmsnorm(x, delta, w, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
 
     def _pos_scale_q(self, q, positions):
         """Llama-4 query scaling by position (Ministral 3 / Nemotron-Labs-
@@ -531,7 +546,12 @@ class DecoderLM:
             return (x.float() + delta.float()).to(x.dtype) if delta is not None else x
         if fb.logit_idx is not None:
             xs = (x.float() + delta.float()).to(x.dtype)[fb.logit_idx] if delta is not None else x[fb.logit_idx]
-            h = ops.rmsnorm(xs.contiguous(), self.norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+            if cfg.norm_kind == "layernorm":
+                h = ops.add_layernorm(xs.contiguous(), None, self.norm, self.norm_b, cfg.rms_norm_eps)
+            else:
+                h = ops.rmsnorm(xs.contiguous(), self.norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+        elif cfg.norm_kind == "layernorm":
+            h = ops.add_layernorm(x, delta, self.norm, self.norm_b, cfg.rms_norm_eps)
         else:
             h = ops.add_rmsnorm(x, delta, self.norm, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
         if return_hidden:
@@ -590,7 +610,7 @@ class DecoderLM:
         x = ops.embedding(tokens.to(torch.int32), self.embed, cfg.embed_scale)
         delta = None
         for li, L in enumerate(self.layers):
-            h = ops.add_rmsnorm(x, delta, L.ln1, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            h = self._norm(x, delta, L.ln1, L.ln1_b)
             if L.block == "ffn":
                 delta = self._mlp(L, h)
                 continue
@@ -622,6 +642,9 @@ class DecoderLM:
                     g0 = (self.H + 2 * self.KVH) * self.D
                     a2 = sigmoid_mul(a2, qkv[:, g0:g0 + self.H * self.D])
                 delta = self._attn_out(L, a2)
+            if cfg.parallel_block:
+                delta = (delta.float() + self._mlp(L, h).float()).to(x.dtype)
+                continue
             if L.post_attn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
             if L.block == "mixer":
@@ -631,7 +654,7 @@ class DecoderLM:
             if L.post_ffn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_ffn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
         cache.offset += Lq
-        h = ops.add_rmsnorm(x, delta, self.norm, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+        h = self._norm(x, delta, self.norm, self.norm_b)
         if return_hidden:
             return h
         return self._final_logits(h)
@@ -649,6 +672,8 @@ class DecoderLM:
 
         m.embed = cv(self.embed)
         m.norm = cv(self.norm)
+        m.norm_b = cv(self.norm_b)
+        m.lm_head_b = cv(self.lm_head_b, keep_f32=True)
         if self.lm_head is self.embed:
             m.lm_head = m.embed
         elif isinstance(self.lm_head, QuantizedWeight):
@@ -690,6 +715,8 @@ class DecoderLM:
         tied = self.lm_head is self.embed
         self.embed = mv(self.embed)
         self.norm = mv(self.norm)
+        self.norm_b = mv(self.norm_b)
+        self.lm_head_b = None if self.lm_head_b is None else self.lm_head_b.to(device=device, dtype=torch.float32)
         self.lm_head = self.embed if tied else mv(self.lm_head)
         for L in self.layers:
             for s in LayerWeights.__slots__:

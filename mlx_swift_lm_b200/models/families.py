@@ -49,7 +49,8 @@ register("nemotron_h", ssm="nemotron_h")
 # IBM Granite 4 hybrids: Mamba-2 or attention mixer + MoE (top-k softmax over the k) + shared MLP per layer
 register("granitemoehybrid", ssm="granite", moe=True, mixtral_names=False)
 register("mamba2", ssm="mamba2")
-register("lfm2", lfm2=True, qk_norm=True)  # Liquid LFM2: short-conv / attention hybrid
+register("lfm2", lfm2=True, qk_norm=True)
+register("phi", phi2=True)  # Phi-1.5 / Phi-2: parallel attention + MLP, LayerNorm, partial rotary  # Liquid LFM2: short-conv / attention hybrid
 
 _NEMOTRON_BLOCKS = {"mamba": "M", "attention": "*", "mlp": "-", "moe": "E"}
 
@@ -270,6 +271,17 @@ def build_config(hf: dict) -> DecoderConfig:
         if rp.get("llama_4_scaling_beta") and rp.get("original_max_position_embeddings"):
             cfg.extra["attn_pos_scale"] = (float(rp["llama_4_scaling_beta"]),
                                            int(rp["original_max_position_embeddings"]))
+    if tr.get("phi2"):
+        # MLXLLM/Models/Phi.swift: LayerNorm (with bias) before a parallel
+        # attention + GELU MLP block, biased projections, final LayerNorm,
+        # biased head, rotary on partial_rotary_factor of the head
+        cfg.norm_kind = "layernorm"
+        cfg.parallel_block = True
+        cfg.hidden_act = "gelu_tanh_mlp"
+        cfg.attention_bias = cfg.o_bias = cfg.mlp_bias = True
+        cfg.partial_rotary_factor = hf.get("partial_rotary_factor", 0.4)
+        cfg.rms_norm_eps = hf.get("layer_norm_eps", 1e-5)
+        cfg.tie_word_embeddings = hf.get("tie_word_embeddings", False)
     if tr.get("lfm2"):
         # gated short-conv layers + attention layers, SwiGLU w1/w3/w2 FFN with
         # the auto-adjusted width (MLXLLM/Models/LFM2.swift:36-110, 240-262)

@@ -41,7 +41,7 @@ def test_split_rows_matches_full_forward():
     full = m.forward(fb, eng.kv)
     parts = [m.forward(mb, eng.kv) for mb in split_rows(fb, 3)]
     assert len(parts) > 1
-    assert torch.allclose(torch.cat(parts, 0), full, atol=1e-5)
+    assert torch.allclose(torch.cat(parts, 0), full, atol=1e-4, rtol=1e-5)  # CPU GEMM blocking varies with M
 
 
 def _free_port():
