@@ -447,7 +447,7 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
     r, w = tp.rank, tp.world
     if cfg.linear_kind == "short_conv":
         tensors = _lfm2_names(tensors)
-    if cfg.parallel_block:
+    if cfg.model_type == "phi":
         return _build_phi(cfg, tensors, device, dtype)
     q = cfg.quantization if isinstance(cfg.quantization, dict) else None
     ck = CheckpointView(tensors, q, torch.float32, keep_quantized=keep_quantized and bool(q), hadamard=hadamard)
@@ -468,6 +468,8 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
 
     m.embed = ck.embedding("embed_tokens" if ck.has("embed_tokens.weight") else "embeddings")
     m.norm = norm("norm.weight" if ck.has("norm.weight") else "norm_f.weight")
+    if cfg.norm_kind == "layernorm":
+        m.norm_b = ck.vec("norm.bias")
     if hadamard is not None and not ck.has("lm_head.weight") and ck.has("embed_tokens.signs"):
         m.lm_head = ck.linear("embed_tokens")  # tied head: packed table behind the forward transform
     elif ck.has("diffusion_head.weight"):  # Nemotron-Labs-Diffusion
@@ -503,7 +505,12 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
             m.layers.append(L)
             continue
         L.ln1 = norm(p + "input_layernorm.weight")
-        if cfg.post_norms:
+        if cfg.norm_kind == "layernorm":
+            L.ln1_b = ck.vec(p + "input_layernorm.bias")
+            L.ln2_b = ck.vec(p + "post_attention_layernorm.bias")
+        if cfg.parallel_block:  # one norm feeds attention and MLP
+            pass
+        elif cfg.post_norms:
             L.post_attn_norm = norm(p + "post_attention_layernorm.weight")
             L.ln2 = norm(p + "pre_feedforward_layernorm.weight")
             L.post_ffn_norm = norm(p + "post_feedforward_layernorm.weight")
@@ -538,6 +545,12 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
                 L.moe = False
                 L.wgu = interleave_gate_up(_shard_rows(g, r, w), _shard_rows(u, r, w))
                 L.wd = _shard_cols(ck.linear(mp + "output_linear"), r, w)
+                m.layers.append(L)
+                continue
+            if ck.has(mp + "c_fc.weight"):  # StarCoder2: non-gated GELU MLP with biases
+                L.moe = False
+                L.wgu, L.wd = ck.linear(mp + "c_fc"), ck.linear(mp + "c_proj")
+                L.bgu, L.bd = ck.vec(mp + "c_fc.bias"), ck.vec(mp + "c_proj.bias")
                 m.layers.append(L)
                 continue
             if cfg.extra.get("fused_gate_up"):

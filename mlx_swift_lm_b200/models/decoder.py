@@ -42,8 +42,8 @@ class LayerWeights:
                  "conv_b", "ssm_D",
                  # "both" | "mixer" | "ffn": which blocks the layer holds
                  "block",
-                 # LayerNorm bias of the (parallel-block) input norm (Phi-2)
-                 "ln1_b",
+                 # LayerNorm biases of the input / post-attention norms (norm_kind "layernorm")
+                 "ln1_b", "ln2_b",
                  # ParoQuant: activation rotations shared by the experts (gate/up input, down input)
                  "experts_rot_in", "experts_rot_mid")
 
@@ -432,7 +432,7 @@ class DecoderLM:
                 delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
             if L.block == "mixer":
                 continue
-            h = ops.add_rmsnorm(x, delta, L.ln2, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            h = self._norm(x, delta, L.ln2, L.ln2_b)
             delta = self._mlp(L, h)
             if L.post_ffn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_ffn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
@@ -649,7 +649,7 @@ class DecoderLM:
                 delta = ops.rmsnorm(delta, L.post_attn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
             if L.block == "mixer":
                 continue
-            h = ops.add_rmsnorm(x, delta, L.ln2, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
+            h = self._norm(x, delta, L.ln2, L.ln2_b)
             delta = self._mlp(L, h)
             if L.post_ffn_norm is not None:
                 delta = ops.rmsnorm(delta, L.post_ffn_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
@@ -673,7 +673,7 @@ class DecoderLM:
         m.embed = cv(self.embed)
         m.norm = cv(self.norm)
         m.norm_b = cv(self.norm_b)
-        m.lm_head_b = cv(self.lm_head_b, keep_f32=True)
+        m.lm_head_b = cv(self.lm_head_b)
         if self.lm_head is self.embed:
             m.lm_head = m.embed
         elif isinstance(self.lm_head, QuantizedWeight):
@@ -716,7 +716,7 @@ class DecoderLM:
         self.embed = mv(self.embed)
         self.norm = mv(self.norm)
         self.norm_b = mv(self.norm_b)
-        self.lm_head_b = None if self.lm_head_b is None else self.lm_head_b.to(device=device, dtype=torch.float32)
+        self.lm_head_b = mv(self.lm_head_b)
         self.lm_head = self.embed if tied else mv(self.lm_head)
         for L in self.layers:
             for s in LayerWeights.__slots__:

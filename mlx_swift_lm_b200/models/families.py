@@ -20,8 +20,12 @@ def register(*model_types, **traits):
 
 
 # --- the registry -----------------------------------------------------------------
-register("llama", "mistral", "smollm3", "helium", "apertus", "granite", "hunyuan_v1_dense", "exaone4",
-         "ernie4_5", "internlm2", "minicpm", "olmo2", "olmo3", "nanbeige", "laguna", "acereason", "mellum")
+register("llama", "mistral", "smollm3", "helium", "granite", "hunyuan_v1_dense", "exaone4",
+         "ernie4_5", "internlm2", "minicpm", "nanbeige", "laguna", "acereason", "mellum")
+# architectures whose distinguishing blocks are not built: refused instead of loaded wrongly
+_REFUSED = {"olmo2": "post-sublayer norms without pre-norms and q/k norms over the whole projection",
+            "olmo3": "post-sublayer norms without pre-norms and q/k norms over the whole projection",
+            "apertus": "the xIELU activation"}
 register("qwen2")  # q/k/v biases
 register("mimo")  # Xiaomi MiMo: the Qwen2 body (its MTP layers are not loaded)
 register("qwen2_vl", vlm="qwen2_vl")  # the language model of Qwen2-VL (q/k/v biases, M-RoPE)
@@ -159,8 +163,8 @@ def _ssm_config(cfg: DecoderConfig, hf: dict, kind: str):
     cfg.mlp_bias = hf.get("mlp_bias", False)
     cfg.attention_bias = hf.get("attention_bias", False)
     cfg.extra["mamba_proj_bias"] = hf.get("mamba_proj_bias", hf.get("use_bias", False))
-register("cohere")
-register("starcoder2")
+register("cohere", cohere=True)  # Command-R: LayerNorm, parallel attention + SwiGLU, logit scale
+register("starcoder2", starcoder2=True)  # LayerNorm with bias, biased GELU MLP (c_fc / c_proj)
 
 
 def supported_model_types() -> list[str]:
@@ -172,6 +176,8 @@ def build_config(hf: dict) -> DecoderConfig:
     if "text_config" in hf and "hidden_size" not in hf:
         hf = {**hf["text_config"], "model_type": hf["text_config"].get("model_type", hf.get("model_type"))}
     mt = hf.get("model_type", "llama")
+    if mt in _REFUSED:
+        raise NotImplementedError(f"model_type {mt!r} needs {_REFUSED[mt]}, which this framework does not serve yet")
     tr = FAMILIES.get(mt)
     if tr is None:
         raise ValueError(f"unsupported model_type {mt!r}; supported: {', '.join(supported_model_types())}")
@@ -332,6 +338,25 @@ def build_config(hf: dict) -> DecoderConfig:
     cfg.extra["fused_qkv"] = tr.get("fused_qkv", False)
     cfg.extra["fused_gate_up"] = tr.get("fused_gate_up", False)
     cfg.extra["mixtral_names"] = tr.get("mixtral_names", False)
+    if tr.get("cohere"):
+        if hf.get("use_qk_norm"):
+            raise NotImplementedError("Cohere per-head LayerNorm q/k norms are not served")
+        cfg.norm_kind = "layernorm"
+        cfg.parallel_block = True
+        cfg.rms_norm_eps = hf.get("layer_norm_eps", 1e-5)
+        cfg.tie_word_embeddings = hf.get("tie_word_embeddings", True)
+        cfg.extra["logits_scaling"] = 1.0 / float(hf.get("logit_scale", 1.0))
+    if tr.get("starcoder2"):
+        cfg.norm_kind = "layernorm"
+        cfg.rms_norm_eps = hf.get("norm_epsilon", hf.get("layer_norm_eps", 1e-5))
+        cfg.attention_bias = cfg.o_bias = cfg.mlp_bias = hf.get("use_bias", True)
+        cfg.hidden_act = "gelu_tanh_mlp"
+        if sw:
+            cfg.layer_windows = [int(sw)] * cfg.num_layers
+    if mt == "minicpm":  # MLXLLM/Models/MiniCPM.swift:107-180
+        cfg.embed_scale = hf.get("scale_emb", 1.0)
+        cfg.extra.update(residual_multiplier=hf.get("scale_depth", 1.0) / math.sqrt(cfg.num_layers),
+                         logits_scaling=cfg.hidden_size / hf.get("dim_model_base", cfg.hidden_size))
     if mt == "granite":
         cfg.extra.update(embedding_multiplier=hf.get("embedding_multiplier", 1.0),
                          residual_multiplier=hf.get("residual_multiplier", 1.0),

@@ -29,6 +29,8 @@ def gemm(x: torch.Tensor, w: torch.Tensor, epi: str = "none", residual: torch.Te
     blocks ([2F, K]); y is [M, F].  epi = "f32": fp32 output.
     epi = "add": y = x @ w.T + residual.  `splits` overrides the split-K count.
     """
+    if bias is not None and x.is_cuda and bias.dtype != x.dtype:  # the epilogues read biases in x's dtype
+        bias = bias.to(x.dtype)
     if isinstance(w, QuantizedWeight):
         return gemm_q(x, w, epi, residual, out, bias, splits)
     if not isinstance(w, torch.Tensor) and hasattr(w, "gemm"):  # e.g. rotation.RotatedWeight
