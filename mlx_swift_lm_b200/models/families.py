@@ -20,12 +20,13 @@ def register(*model_types, **traits):
 
 
 # --- the registry -----------------------------------------------------------------
-register("llama", "mistral", "smollm3", "helium", "granite", "hunyuan_v1_dense", "exaone4",
+register("llama", "mistral", "smollm3", "helium", "granite", "hunyuan_v1_dense",
          "ernie4_5", "internlm2", "minicpm", "nanbeige", "laguna", "acereason", "mellum")
 # architectures whose distinguishing blocks are not built: refused instead of loaded wrongly
 _REFUSED = {"olmo2": "post-sublayer norms without pre-norms and q/k norms over the whole projection",
             "olmo3": "post-sublayer norms without pre-norms and q/k norms over the whole projection",
-            "apertus": "the xIELU activation"}
+            "apertus": "the xIELU activation",
+            "exaone4": "post-sublayer norms without pre-norms"}
 register("qwen2")  # q/k/v biases
 register("mimo")  # Xiaomi MiMo: the Qwen2 body (its MTP layers are not loaded)
 register("qwen2_vl", vlm="qwen2_vl")  # the language model of Qwen2-VL (q/k/v biases, M-RoPE)
@@ -353,6 +354,8 @@ def build_config(hf: dict) -> DecoderConfig:
         cfg.hidden_act = "gelu_tanh_mlp"
         if sw:
             cfg.layer_windows = [int(sw)] * cfg.num_layers
+    if mt == "hunyuan_v1_dense" and hf.get("use_qk_norm"):
+        raise NotImplementedError("Hunyuan q/k norms after the rotation are not served")
     if mt == "minicpm":  # MLXLLM/Models/MiniCPM.swift:107-180
         cfg.embed_scale = hf.get("scale_emb", 1.0)
         cfg.extra.update(residual_multiplier=hf.get("scale_depth", 1.0) / math.sqrt(cfg.num_layers),
