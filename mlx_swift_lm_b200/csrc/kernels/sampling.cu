@@ -526,9 +526,101 @@ __global__ void __launch_bounds__(kThreads) argmax_conf_kernel(const float* __re
   }
 }
 
-int b200_argmax_conf(const float* logits, int64_t ld, int B, int V, int* tok, float* conf, float* mx, cudaStream_t st) {
+// Few rows (fewer CTAs than SMs): each row is split into `nsplit` chunks of
+// `chunk` logits; a CTA per (row, chunk) writes its (max, sum, index) triple,
+// and one warp per row merges the row's triples in chunk order.
+__global__ void __launch_bounds__(kThreads) argmax_conf_part_kernel(const float* __restrict__ logits, int64_t ld,
+                                                                    int V, int chunk, float* __restrict__ pm,
+                                                                    float* __restrict__ ps, int* __restrict__ pi) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
+  __shared__ float sm[32], ss[32];
+  __shared__ int si[32];
+  const float* lg = logits + (size_t)blockIdx.x * ld;
+  const int c0 = blockIdx.y * chunk, c1 = min(V, c0 + chunk);
+  float m = -INFINITY, s = 0.f;
+  int idx = 0x7fffffff;
+  for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+    const float x = lg[i];
+    if (x > m) {
+      s = (m == -INFINITY ? 0.f : s * __expf(m - x)) + 1.f;
+      m = x;
+      idx = i;
+    } else if (x != -INFINITY) {
+      s += __expf(x - m);
+    }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    merge_msi(m, s, idx, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o),
+              __shfl_xor_sync(0xffffffffu, idx, o));
+  if (lane == 0) {
+    sm[wid] = m;
+    ss[wid] = s;
+    si[wid] = idx;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    const bool live = lane < (int)(blockDim.x >> 5);
+    m = live ? sm[lane] : -INFINITY;
+    s = live ? ss[lane] : 0.f;
+    idx = live ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+      merge_msi(m, s, idx, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o),
+                __shfl_xor_sync(0xffffffffu, idx, o));
+    if (lane == 0) {
+      const size_t o = (size_t)blockIdx.x * gridDim.y + blockIdx.y;
+      pm[o] = m;
+      ps[o] = s;
+      pi[o] = idx;
+    }
+  }
+}
+
+__global__ void argmax_conf_merge_kernel(const float* __restrict__ pm, const float* __restrict__ ps,
+                                         const int* __restrict__ pi, int nsplit, int B, int* __restrict__ tok,
+                                         float* __restrict__ conf, float* __restrict__ mx) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= B) return;
+  float m = -INFINITY, s = 0.f;
+  int idx = 0x7fffffff;
+  for (int j = lane; j < nsplit; j += 32) {
+    const size_t o = (size_t)row * nsplit + j;
+    merge_msi(m, s, idx, pm[o], ps[o], pi[o]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    merge_msi(m, s, idx, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o),
+              __shfl_xor_sync(0xffffffffu, idx, o));
+  if (lane == 0) {
+    tok[row] = idx == 0x7fffffff ? 0 : idx;
+    conf[row] = s > 0.f ? 1.f / s : 0.f;
+    if (mx) mx[row] = m;
+  }
+}
+
+// scratch: 3 * B * nsplit words (fp32 max | fp32 sum | int32 index); nsplit <= 1 -> one CTA per row
+int b200_argmax_conf(const float* logits, int64_t ld, int B, int V, int* tok, float* conf, float* mx, void* scratch,
+                     int nsplit, cudaStream_t st) {
   if (B <= 0) return 0;
-  cudaError_t e = b200::launch_k(argmax_conf_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, tok, conf, mx);
+  cudaError_t e;
+  if (nsplit <= 1 || !scratch) {
+    e = b200::launch_k(argmax_conf_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, tok, conf, mx);
+    return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+  }
+  const int chunk = (V + nsplit - 1) / nsplit;
+  float* pm = reinterpret_cast<float*>(scratch);
+  float* ps = pm + (size_t)B * nsplit;
+  int* pi = reinterpret_cast<int*>(ps + (size_t)B * nsplit);
+  e = b200::launch_k(argmax_conf_part_kernel, dim3(B, nsplit), dim3(kThreads), 0, st, 1, logits, ld, V, chunk, pm,
+                     ps, pi);
+  if (e != cudaSuccess) return (int)e;
+  e = b200::launch_k(argmax_conf_merge_kernel, dim3((B * 32 + 255) / 256), dim3(256), 0, st, 1, pm, ps, pi, nsplit,
+                     B, tok, conf, mx);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

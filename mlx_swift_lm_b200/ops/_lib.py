@@ -51,7 +51,7 @@ _SIGS = {
                                   i32, vp, vp]),
     "b200_sample": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "b200_argmax": (i32, [vp, i64, i32, i32, vp, vp, vp]),
-    "b200_argmax_conf": (i32, [vp, i64, i32, i32, vp, vp, vp, vp]),
+    "b200_argmax_conf": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, i32, vp]),
     "b200_logprobs": (i32, [vp, i64, i32, i32, vp, i32, vp, vp, vp, vp]),
     "b200_philox_u32": (C.c_uint32, [u64, u64, C.c_uint32]),
     "b200_gather_tokens": (i32, [vp, vp, vp, vp, i32, vp]),

@@ -42,10 +42,13 @@ def argmax_confidence(logits: torch.Tensor):
     tok = torch.empty(B, dtype=torch.int32, device=logits.device)
     conf = torch.empty(B, dtype=torch.float32, device=logits.device)
     mx = torch.empty(B, dtype=torch.float32, device=logits.device)
+    # fewer rows than two CTAs per SM: split each row's vocabulary so the pass fills the GPU
+    nsplit = 1 if B >= 296 else max(1, min((296 + B - 1) // B, V // 4096))
+    scratch = torch.empty(3 * B * nsplit, dtype=torch.float32, device=logits.device) if nsplit > 1 else None
     rc = _lib.lib().b200_argmax_conf(logits.data_ptr(), logits.stride(0), B, V, tok.data_ptr(), conf.data_ptr(),
-                                     mx.data_ptr(), _lib.stream_ptr(logits.device))
+                                     mx.data_ptr(), _lib.ptr(scratch), nsplit, _lib.stream_ptr(logits.device))
     _lib.check(rc, "argmax_conf")
-    _lib.count(1)
+    _lib.count(2 if nsplit > 1 else 1)
     return tok, conf, mx
 
 
