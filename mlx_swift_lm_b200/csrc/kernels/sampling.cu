@@ -468,6 +468,36 @@ b200::launch_k(  sample_kernel, dim3(B), dim3(kThreads), 0, st, 1, a);
 // running (max, sum of exp(x - max), index), rescaling the sum when the max
 // moves; warps and then the block merge the triples (ties -> smaller index).
 // p(argmax) = exp(m - logsumexp) = 1 / sum exp(x - m).
+__device__ __forceinline__ void msi_push(float& m, float& s, int& idx, float x, int i) {
+  if (x > m) {
+    s = (m == -INFINITY ? 0.f : s * __expf(m - x)) + 1.f;
+    m = x;
+    idx = i;
+  } else if (x != -INFINITY) {
+    s += __expf(x - m);
+  }
+}
+
+// this thread's (max, sum, index) over lg[c0, c1): 16-byte loads (two in
+// flight per iteration) when the range and the row are 4-aligned
+__device__ __forceinline__ void msi_scan(const float* __restrict__ lg, int c0, int c1, bool vec, float& m, float& s,
+                                         int& idx) {
+  if (vec) {
+    const float4* l4 = reinterpret_cast<const float4*>(lg);
+    const int v0 = c0 >> 2, v1 = c1 >> 2;
+#pragma unroll 2
+    for (int i = v0 + (int)threadIdx.x; i < v1; i += blockDim.x) {
+      const float4 x = l4[i];
+      msi_push(m, s, idx, x.x, 4 * i);
+      msi_push(m, s, idx, x.y, 4 * i + 1);
+      msi_push(m, s, idx, x.z, 4 * i + 2);
+      msi_push(m, s, idx, x.w, 4 * i + 3);
+    }
+    c0 = v1 << 2;
+  }
+  for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) msi_push(m, s, idx, lg[i], i);
+}
+
 __device__ __forceinline__ void merge_msi(float& m, float& s, int& i, float om, float os, int oi) {
   if (om > m || (om == m && oi < i)) {
     s = (m == -INFINITY ? 0.f : s * __expf(m - om)) + os;
@@ -488,16 +518,7 @@ __global__ void __launch_bounds__(kThreads) argmax_conf_kernel(const float* __re
   const float* lg = logits + (size_t)blockIdx.x * ld;
   float m = -INFINITY, s = 0.f;
   int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = lg[i];
-    if (x > m) {
-      s = (m == -INFINITY ? 0.f : s * __expf(m - x)) + 1.f;
-      m = x;
-      idx = i;
-    } else if (x != -INFINITY) {
-      s += __expf(x - m);
-    }
-  }
+  msi_scan(lg, 0, V, (ld % 4) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0, m, s, idx);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
@@ -540,16 +561,8 @@ __global__ void __launch_bounds__(kThreads) argmax_conf_part_kernel(const float*
   const int c0 = blockIdx.y * chunk, c1 = min(V, c0 + chunk);
   float m = -INFINITY, s = 0.f;
   int idx = 0x7fffffff;
-  for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
-    const float x = lg[i];
-    if (x > m) {
-      s = (m == -INFINITY ? 0.f : s * __expf(m - x)) + 1.f;
-      m = x;
-      idx = i;
-    } else if (x != -INFINITY) {
-      s += __expf(x - m);
-    }
-  }
+  msi_scan(lg, c0, c1, (ld % 4) == 0 && (chunk % 4) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0, m, s,
+           idx);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)

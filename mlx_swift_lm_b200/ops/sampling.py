@@ -44,6 +44,9 @@ def argmax_confidence(logits: torch.Tensor):
     mx = torch.empty(B, dtype=torch.float32, device=logits.device)
     # fewer rows than two CTAs per SM: split each row's vocabulary so the pass fills the GPU
     nsplit = 1 if B >= 296 else max(1, min((296 + B - 1) // B, V // 4096))
+    # chunks of whole float4s keep the vector loads aligned
+    while nsplit > 1 and ((V + nsplit - 1) // nsplit) % 4:
+        nsplit -= 1
     scratch = torch.empty(3 * B * nsplit, dtype=torch.float32, device=logits.device) if nsplit > 1 else None
     rc = _lib.lib().b200_argmax_conf(logits.data_ptr(), logits.stride(0), B, V, tok.data_ptr(), conf.data_ptr(),
                                      mx.data_ptr(), _lib.ptr(scratch), nsplit, _lib.stream_ptr(logits.device))
