@@ -6,7 +6,7 @@ Two shared objects are produced under ``mlx_swift_lm_b200/_lib/``:
   for sm_100a only (``-gencode arch=compute_100a,code=sm_100a``) and exposed
   through a plain C ABI (loaded with ctypes). nvcc cross-compiles without a GPU.
 * ``_b200host*.so`` - the host runtime in ``csrc/host/*.cpp`` (page pool, block
-  hasher, scheduler core, grammar engine, safetensors reader) as a pybind11
+  hasher, grammar engine, safetensors reader) as a pybind11
   module.
 
 Sources are rebuilt only when they (or a header) are newer than the output.

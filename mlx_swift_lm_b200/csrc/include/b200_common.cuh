@@ -15,6 +15,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <utility>
 
 namespace b200 {
@@ -357,6 +358,28 @@ static inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 blo
   cfg.attrs = attr;
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Host: raise `Kernel`'s dynamic shared-memory limit to `bytes` on the current
+// device. cudaFuncSetAttribute acts on the calling device's context only, so
+// the record of what was set is kept per device (up to 64 devices), in atomics:
+// host threads may launch concurrently, and two of them setting the same
+// attribute at once is harmless. Returns 0 or the CUDA error code.
+constexpr int kMaxDevices = 64;
+template <auto Kernel>
+static inline int smem_attr_once(int bytes) {
+  static std::atomic<int> set_bytes[kMaxDevices];  // zero-initialised (static storage)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+  if (set_bytes[dev].load(std::memory_order_acquire) >= bytes) return 0;
+  e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return (int)e;
+  int cur = set_bytes[dev].load(std::memory_order_relaxed);
+  while (cur < bytes && !set_bytes[dev].compare_exchange_weak(cur, bytes, std::memory_order_acq_rel)) {
+  }
+  return 0;
 }
 }  // namespace b200
 

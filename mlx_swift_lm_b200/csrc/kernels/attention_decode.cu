@@ -573,13 +573,7 @@ template <int D, int G, typename KVT>
 static int launch_decode(const DecodeArgs& a, int B, cudaStream_t st) {
   using C = StreamCfg<D, G>;
   constexpr int smem = C::PS * C::NST * 2 * kPage * D * (int)sizeof(KVT);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_stream_kernel<D, G, KVT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return (int)e;
-    configured = true;
-  }
+  if (int e = b200::smem_attr_once<paged_decode_stream_kernel<D, G, KVT>>(smem)) return e;
   dim3 grid(a.max_parts, a.KVH, B);
 b200::launch_k(  paged_decode_stream_kernel<D, G, KVT>, dim3(grid), dim3(128), smem, st, 1, a);
 b200::launch_k(  paged_decode_merge_kernel<D>, dim3((B * a.H + 3) / 4), dim3(128), 0, st, 1, a, B);

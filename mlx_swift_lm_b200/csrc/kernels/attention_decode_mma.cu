@@ -292,12 +292,7 @@ __global__ void __launch_bounds__(128) decode_mma_kernel(const __grid_constant__
 template <int D, int G>
 int launch(const CUtensorMap& tk, const CUtensorMap& tv, const Args& a, int B, cudaStream_t st) {
   constexpr int smem = 4 * kNst * 2 * kPage * D * 2 + 1024;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_mma_kernel<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return (int)e;
-    configured = true;
-  }
+  if (int e = smem_attr_once<decode_mma_kernel<D, G>>(smem)) return e;
   cudaError_t e = launch_k(decode_mma_kernel<D, G>, dim3(a.max_parts, a.KVH, B), dim3(128), smem, st, 1, tk, tv, a);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }

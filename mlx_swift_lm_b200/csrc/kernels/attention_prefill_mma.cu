@@ -281,12 +281,7 @@ __global__ void __launch_bounds__(128) prefill_mma_kernel(const __grid_constant_
 template <int D>
 int launch(const CUtensorMap& tk, const CUtensorMap& tv, const Args& a, int n_tiles, cudaStream_t st) {
   constexpr int smem = kNst * 2 * kPage * D * 2 + 1024;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return (int)e;
-    configured = true;
-  }
+  if (int e = smem_attr_once<prefill_mma_kernel<D>>(smem)) return e;
   cudaError_t e = launch_k(prefill_mma_kernel<D>, dim3(n_tiles, a.H), dim3(128), smem, st, 1, tk, tv, a);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }

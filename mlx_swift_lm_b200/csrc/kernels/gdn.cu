@@ -423,12 +423,7 @@ int b200_gdn_conv(const void* P, int ldp, int T, const int* cu, int R, const int
   int CB = 8 * (Dk > Dv ? Dk : Dv);
   if ((2 * Hk * Dk) % CB) CB = Dk > Dv ? Dk : Dv;
   const size_t smem = (size_t)CB * sizeof(float);
-  static bool cfg = false;
-  if (!cfg) {
-    cudaError_t e = cudaFuncSetAttribute(gdn::conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return (int)e;
-    cfg = true;
-  }
+  if (int e = b200::smem_attr_once<gdn::conv_kernel>(200 * 1024)) return e;
   cudaError_t e = launch_k(gdn::conv_kernel, dim3(T, (C + CB - 1) / CB), dim3(256), smem, st, 1, CB, mode, conv_b,
                            tmin, tmax, reinterpret_cast<const __nv_bfloat16*>(P), ldp, T, cu, R, fresh, slot,
                            reinterpret_cast<const __nv_bfloat16*>(conv_state), conv_w, C, Hk, Dk, Hv, Dv, A_log,

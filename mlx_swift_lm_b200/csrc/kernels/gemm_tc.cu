@@ -606,13 +606,7 @@ static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmA
                        int tiles_n, int tiles_m, cudaStream_t st, const QArgs& q = no_quant()) {
   using S = GemmSmem<BN, STAGES, WQ>;
   static_assert(S::kTotal <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
-    if (e != cudaSuccess) return (int)e;
-    configured = true;
-  }
+  if (int e = smem_attr_once<gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ>>(S::kTotal)) return e;
   cudaError_t e = launch_k(gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ>, dim3(tiles_n, tiles_m, a.ksplit),
                            dim3(S::kThreads, 1, 1), S::kTotal, st, a.ksplit, tw, tx, a, coll, q);
   if (e != cudaSuccess) return (int)e;

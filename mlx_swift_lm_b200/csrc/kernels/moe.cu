@@ -375,13 +375,7 @@ int launch_grouped(const CUtensorMap& tw, const CUtensorMap& tx, const GArgs& a,
                    cudaStream_t st) {
   using S = GSmem<BN, STAGES, WQ>;
   static_assert(S::kTotal <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
-  static bool cfg = false;
-  if (!cfg) {
-    cudaError_t e =
-        cudaFuncSetAttribute(grouped_kernel<BN, STAGES, WQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
-    if (e != cudaSuccess) return (int)e;
-    cfg = true;
-  }
+  if (int e = smem_attr_once<grouped_kernel<BN, STAGES, WQ>>(S::kTotal)) return e;
   cudaError_t e = launch_k(grouped_kernel<BN, STAGES, WQ>, dim3((a.N + 127) / 128, max_chunks), dim3(S::kThreads),
                            S::kTotal, st, 1, tw, tx, a, q);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
@@ -429,12 +423,7 @@ int b200_moe_sort(const int* ids, int P, int E, int BN, int max_chunks, int* per
                   int* n_chunks, cudaStream_t st) {
   if (E > 1024 || P <= 0) return P < 0 ? -1 : (E > 1024 ? -1 : 0);
   const int smem = (33 * E + 1) * (int)sizeof(int);
-  static bool cfg = false;
-  if (!cfg) {
-    cudaError_t e = cudaFuncSetAttribute(moe::sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (33 * 1024 + 1) * 4);
-    if (e != cudaSuccess) return (int)e;
-    cfg = true;
-  }
+  if (int e = b200::smem_attr_once<moe::sort_kernel>((33 * 1024 + 1) * 4)) return e;
   cudaError_t e = launch_k(moe::sort_kernel, dim3(1), dim3(1024), smem, st, 1, ids, P, E, BN, max_chunks, perm, pos,
                            chunks, n_chunks);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();

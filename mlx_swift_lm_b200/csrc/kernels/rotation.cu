@@ -141,13 +141,7 @@ int b200_block_hadamard(const void* x, int ldx, int T, int K, int block, const f
   if (T <= 0) return 0;
   if (block < 2 || block > 8192 || (block & (block - 1)) || (K % block)) return -1;
   const size_t smem = (size_t)block * sizeof(float);
-  static bool cfg = false;
-  if (!cfg) {
-    cudaError_t e = cudaFuncSetAttribute(rot::block_hadamard_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         8192 * 4);
-    if (e != cudaSuccess) return (int)e;
-    cfg = true;
-  }
+  if (int e = b200::smem_attr_once<rot::block_hadamard_kernel>(8192 * 4)) return e;
   const int threads = block / 2 < 512 ? block / 2 : 512;
   cudaError_t e = launch_k(rot::block_hadamard_kernel, dim3(T, K / block), dim3(threads), smem, st, 1,
                            reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, block, signs, inverse,

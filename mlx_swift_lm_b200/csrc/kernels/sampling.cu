@@ -444,11 +444,7 @@ int b200_logits_process(float* logits, int64_t ld, int B, int V, const int* bias
                 rep_ids, n_rep,  ld_rep,      rep_penalty, out_ids,   n_out,        ld_out,
                 freq_penalty, pres_penalty, allow_mask, ld_mask, mask_rows};
   const size_t smem = ((V + 31) / 32) * sizeof(uint32_t);
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(logits_process_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured = true;
-  }
+  if (int e = b200::smem_attr_once<logits_process_kernel>(200 * 1024)) return e;
   if (smem > 200 * 1024) return -1;
 b200::launch_k(  logits_process_kernel, dim3(B), dim3(kThreads), smem, st, 1, a);
   return (int)cudaGetLastError();
@@ -493,7 +489,7 @@ __device__ __forceinline__ void msi_scan(const float* __restrict__ lg, int c0, i
       msi_push(m, s, idx, x.z, 4 * i + 2);
       msi_push(m, s, idx, x.w, 4 * i + 3);
     }
-    c0 = v1 << 2;
+    c0 = max(c0, v1 << 2);  // an empty range [c0, c1) stays empty
   }
   for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) msi_push(m, s, idx, lg[i], i);
 }
@@ -616,7 +612,9 @@ __global__ void argmax_conf_merge_kernel(const float* __restrict__ pm, const flo
   }
 }
 
-// scratch: 3 * B * nsplit words (fp32 max | fp32 sum | int32 index); nsplit <= 1 -> one CTA per row
+// scratch: 3 * B * nsplit words (fp32 max | fp32 sum | int32 index); nsplit <= 1 -> one CTA per row.
+// The chunk size is ceil(V / nsplit) rounded up to a multiple of 4, and nsplit is
+// reduced to the number of chunks that start inside the row.
 int b200_argmax_conf(const float* logits, int64_t ld, int B, int V, int* tok, float* conf, float* mx, void* scratch,
                      int nsplit, cudaStream_t st) {
   if (B <= 0) return 0;
@@ -625,7 +623,9 @@ int b200_argmax_conf(const float* logits, int64_t ld, int B, int V, int* tok, fl
     e = b200::launch_k(argmax_conf_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, tok, conf, mx);
     return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
   }
-  const int chunk = (V + nsplit - 1) / nsplit;
+  // chunks of whole float4s; no chunk starts at or past V
+  const int chunk = ((V + nsplit - 1) / nsplit + 3) & ~3;
+  nsplit = (V + chunk - 1) / chunk;
   float* pm = reinterpret_cast<float*>(scratch);
   float* ps = pm + (size_t)B * nsplit;
   int* pi = reinterpret_cast<int*>(ps + (size_t)B * nsplit);

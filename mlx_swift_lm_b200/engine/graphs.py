@@ -70,6 +70,9 @@ class DecodeGraphRunner:
         self.d2h_bytes = 0
         self.launches_per_replay: dict[int, int] = {}
         self._reserved = False
+        # chained-decode input ids: the gather_tokens kernel, or a model-supplied
+        # callable(prev_out, src, host_ids, ids, B) (the PyTorch baseline)
+        self.gather_fn = None
 
     # ------------------------------------------------------------------ capture
     def _reserve(self):
@@ -216,10 +219,13 @@ class DecodeGraphRunner:
         e = torch.cuda.Event()
         e.record()
         self.staging_ev[k] = e
-        L = _lib.lib()
-        _lib.check(L.b200_gather_tokens(self.out.data_ptr(), self.src.data_ptr(), self.hid.data_ptr(),
-                                        self.ids.data_ptr(), Bb, _lib.stream_ptr(self.dev)), "gather_tokens")
-        _lib.count(1)
+        if self.gather_fn is not None:
+            self.gather_fn(self.out, self.src, self.hid, self.ids, Bb)
+        else:
+            L = _lib.lib()
+            _lib.check(L.b200_gather_tokens(self.out.data_ptr(), self.src.data_ptr(), self.hid.data_ptr(),
+                                            self.ids.data_ptr(), Bb, _lib.stream_ptr(self.dev)), "gather_tokens")
+            _lib.count(1)
         self.model.begin_step()
         self.graphs[Bb].replay()
         _lib.count(self.launches_per_replay.get(Bb, 0))

@@ -157,23 +157,23 @@ class DecoderConfig:
         return cls(**{k: v for k, v in d.items() if k in names})
 
 
-# --- configs named by BASELINE.json -------------------------------------------------
+# --- benchmark configurations -------------------------------------------------
 def tiny_qwen3() -> DecoderConfig:
-    """4 layers, d 256, 4q/2kv, hd 64, SwiGLU 768, vocab 4096, tied."""
+    """benchmark config 1: 4 layers, d 256, 4q/2kv, hd 64, SwiGLU 768, vocab 4096, tied."""
     return DecoderConfig(model_type="qwen3", vocab_size=4096, hidden_size=256, num_layers=4, num_heads=4,
                          num_kv_heads=2, head_dim=64, intermediate_size=768, rms_norm_eps=1e-6, rope_theta=1e6,
                          tie_word_embeddings=True, qk_norm=True, max_position_embeddings=4096)
 
 
 def qwen3_8b() -> DecoderConfig:
-    """Qwen3-8B shape."""
+    """benchmark config 2: Qwen3-8B shape."""
     return DecoderConfig(model_type="qwen3", vocab_size=151936, hidden_size=4096, num_layers=36, num_heads=32,
                          num_kv_heads=8, head_dim=128, intermediate_size=12288, rms_norm_eps=1e-6, rope_theta=1e6,
                          tie_word_embeddings=False, qk_norm=True, max_position_embeddings=40960)
 
 
 def qwen3_30b_a3b() -> DecoderConfig:
-    """Qwen3-30B-A3B shape (+1 MTP module)."""
+    """benchmark config 3: Qwen3-30B-A3B shape (+1 MTP module)."""
     return DecoderConfig(model_type="qwen3_moe", vocab_size=151936, hidden_size=2048, num_layers=48, num_heads=32,
                          num_kv_heads=4, head_dim=128, intermediate_size=6144, rms_norm_eps=1e-6, rope_theta=1e6,
                          qk_norm=True, num_experts=128, num_experts_per_tok=8, moe_intermediate_size=768,
@@ -181,7 +181,7 @@ def qwen3_30b_a3b() -> DecoderConfig:
 
 
 def gpt_oss_120b() -> DecoderConfig:
-    """GPT-OSS-120B shape."""
+    """benchmark config 4: GPT-OSS-120B shape."""
     return DecoderConfig(model_type="gpt_oss", vocab_size=201088, hidden_size=2880, num_layers=36, num_heads=64,
                          num_kv_heads=8, head_dim=64, intermediate_size=2880, rms_norm_eps=1e-5, rope_theta=150000,
                          rope_scaling={"rope_type": "yarn", "factor": 32.0, "beta_fast": 32.0, "beta_slow": 1.0,
@@ -193,7 +193,7 @@ def gpt_oss_120b() -> DecoderConfig:
 
 
 def llama3_70b() -> DecoderConfig:
-    """Llama-3-70B shape."""
+    """benchmark config 5: Llama-3-70B shape."""
     return DecoderConfig(model_type="llama", vocab_size=128256, hidden_size=8192, num_layers=80, num_heads=64,
                          num_kv_heads=8, head_dim=128, intermediate_size=28672, rms_norm_eps=1e-5, rope_theta=500000,
                          rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,

@@ -2,7 +2,7 @@
 
 These define the semantics the sm_100a kernels must match: the GPU numerics
 tests compare each kernel against the function of the same name here, and the
-CPU execution path of the framework (tiny Qwen3 on CPU in
+CPU execution path of the framework (benchmark config 1: tiny Qwen3 on CPU in
 fp32) runs on them directly. Rounding points mirror the kernels: wherever a
 kernel rounds an intermediate to the activation dtype, the oracle rounds to
 the input tensor's dtype (a no-op for fp32 tensors).

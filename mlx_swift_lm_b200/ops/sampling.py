@@ -28,6 +28,9 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None, out2: torch.Te
     return out
 
 
+CONF_CHUNK = 8192  # logits per CTA of the split greedy-confidence pass
+
+
 def argmax_confidence(logits: torch.Tensor):
     """(greedy tokens [B] int32, softmax probability of that token [B] fp32,
     max logit [B] fp32) of fp32 logits [B, V] in one pass (mask-diffusion
@@ -42,11 +45,11 @@ def argmax_confidence(logits: torch.Tensor):
     tok = torch.empty(B, dtype=torch.int32, device=logits.device)
     conf = torch.empty(B, dtype=torch.float32, device=logits.device)
     mx = torch.empty(B, dtype=torch.float32, device=logits.device)
-    # fewer rows than two CTAs per SM: split each row's vocabulary so the pass fills the GPU
-    nsplit = 1 if B >= 296 else max(1, min((296 + B - 1) // B, V // 4096))
-    # chunks of whole float4s keep the vector loads aligned
-    while nsplit > 1 and ((V + nsplit - 1) // nsplit) % 4:
-        nsplit -= 1
+    # Large vocabularies are split into chunks of about CONF_CHUNK logits, a CTA per
+    # (row, chunk), and the triples are merged per row in chunk order. The split
+    # depends on V only, never on B, so a row's confidence is bit-identical whatever
+    # batch it is scored in (the diffusion engine thresholds it and picks maxima).
+    nsplit = -(-V // CONF_CHUNK) if V > CONF_CHUNK else 1
     scratch = torch.empty(3 * B * nsplit, dtype=torch.float32, device=logits.device) if nsplit > 1 else None
     rc = _lib.lib().b200_argmax_conf(logits.data_ptr(), logits.stride(0), B, V, tok.data_ptr(), conf.data_ptr(),
                                      mx.data_ptr(), _lib.ptr(scratch), nsplit, _lib.stream_ptr(logits.device))

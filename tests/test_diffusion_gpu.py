@@ -13,10 +13,13 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
-@pytest.mark.parametrize("R,V", [(64, 151936), (3, 1000), (1, 32)])
-def test_argmax_confidence_kernel(R, V):
+@pytest.mark.parametrize("R,V,offset", [(64, 151936, 0), (3, 1000, 0), (1, 32, 0), (2, 1001, 0), (3, 151937, 0),
+                                        (4, 20000, 1), (300, 16385, 0)])
+def test_argmax_confidence_kernel(R, V, offset):
+    """V % 4 != 0 runs the scalar tail; an offset view (x[:, 1:]) has an
+    unaligned base and row stride, so the scalar path runs for every chunk."""
     torch.manual_seed(V)
-    x = torch.randn(R, V, device=DEV) * 4
+    x = (torch.randn(R, V + offset, device=DEV) * 4)[:, offset:]
     x[0, V // 2] = 40.0
     x[-1, 5] = x[-1, 7] = x[-1].max() + 1.0  # tie -> lower index
     tok, conf, mx = ops.argmax_confidence(x)
@@ -45,3 +48,17 @@ def test_engine_batched_equals_single(mode, thr):
         assert run([p])[0][0] == toks
         assert 3 not in toks[len(p):] and len(toks) == len(p) + 32
     assert _lib.read_status().get("sampling", 0) == 0
+
+
+def test_argmax_confidence_independent_of_batch():
+    """A row scored alone and inside a batch gets bit-identical results: the
+    vocabulary split depends on V only."""
+    torch.manual_seed(7)
+    V = 151936
+    x = torch.randn(300, V, device=DEV) * 3
+    tok_b, conf_b, mx_b = ops.argmax_confidence(x)
+    for r in (0, 17, 299):
+        tok, conf, mx = ops.argmax_confidence(x[r:r + 1].contiguous())
+        assert tok.item() == tok_b[r].item()
+        assert torch.equal(conf, conf_b[r:r + 1])
+        assert torch.equal(mx, mx_b[r:r + 1])

@@ -37,7 +37,9 @@ def _tp_worker(rank, world, port, q, seed):
         toks = torch.arange(3, 40) % cfg.vocab_size
         lg = m.forward_dense(toks, m.new_cache())
         if rank == 0:
-            q.put(lg)
+            # numpy pickles by value: a torch tensor would travel as a shared-memory fd
+            # that the receiver can only open while this process is still alive
+            q.put(lg.detach().numpy().copy())
     finally:
         dist.destroy_process_group()
 
@@ -55,7 +57,7 @@ def test_tensor_parallel_matches_single_rank():
     ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, q, seed)) for r in range(2)]
     for p in ps:
         p.start()
-    out = q.get(timeout=120)
+    out = torch.from_numpy(q.get(timeout=120))
     for p in ps:
         p.join(60)
     assert all(p.exitcode == 0 for p in ps)

@@ -1,4 +1,4 @@
-"""BASELINE config 1 (tiny Qwen3, CPU fp32): paged engine == dense KV path."""
+"""benchmark config 1 (tiny Qwen3, CPU fp32): paged engine == dense KV path."""
 import torch
 
 from mlx_swift_lm_b200 import DecoderLM, EngineConfig, EngineV2, SchedulerConfig
