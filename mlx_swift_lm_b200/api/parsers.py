@@ -9,21 +9,14 @@ Reasoning parsers split generated text into ``reasoning`` and ``content``:
   * ``gemma4``: ``<start_of_thought> ... <end_of_thought>``.
 Parity: MLXLMServer/Parsing/*ReasoningParser.swift, MLXLMCommon/ReasoningConfig.swift.
 
-Tool-call parsers extract structured calls (name + JSON arguments):
-  * ``hermes`` / ``qwen3`` / ``json``: ``<tool_call>{"name":..,"arguments":{..}}</tool_call>``;
-  * ``llama3``: a bare JSON object ``{"name":..,"parameters":{..}}``;
-  * ``mistral``: ``[TOOL_CALLS][{...}, ...]``;
-  * ``gpt_oss`` (harmony): ``<|channel|>commentary to=functions.NAME ...<|message|>{args}<|call|>``.
+Tool-call parsers (one per model family's call syntax) live in
+:mod:`.tool_formats`; ``make_tool_parser(name, tools)`` picks one.
 Parity: MLXLMCommon/Tool/ToolCallFormat.swift:106-185, ToolCallProcessor.swift.
-Both parsers work incrementally: ``feed(text)`` returns the deltas that are
-safe to emit, holding back any suffix that could still start a tag.
+Parsers work incrementally: ``feed(text)`` returns the deltas that are safe
+to emit, holding back any suffix that could still start a tag.
 """
 from __future__ import annotations
 
-import json
-import re
-import uuid
-from dataclasses import dataclass, field
 
 
 def _holdback(buf: str, tags) -> int:
@@ -145,123 +138,41 @@ def make_reasoning_parser(name: str | None):
 
 
 # ----------------------------------------------------------------------------- tools
-@dataclass
-class ToolCall:
-    name: str
-    arguments: dict
-    id: str = field(default_factory=lambda: "call_" + uuid.uuid4().hex[:24])
+from .tool_formats import (TOOL_FORMATS, HarmonyToolParser, JSONToolParser, Llama3ToolParser,  # noqa: E402,F401
+                           MistralToolParser, ToolCall, infer_tool_format)
 
-    def to_openai(self) -> dict:
-        return {"id": self.id, "type": "function",
-                "function": {"name": self.name, "arguments": json.dumps(self.arguments)}}
+TOOL_PARSERS = TOOL_FORMATS
 
 
-def _loads(s):
-    try:
-        return json.loads(s)
-    except Exception:
-        return None
+class TaggedJSONToolParser(JSONToolParser):
+    """``<tool_call>{json}</tool_call>`` blocks (Hermes / Qwen), no bare-JSON recovery."""
 
-
-class TaggedJSONToolParser:
-    """``<tool_call>{json}</tool_call>`` blocks (Hermes / Qwen)."""
-
-    def __init__(self, start="<tool_call>", end="</tool_call>"):
-        self.start, self.end = start, end
-        self.buf = ""
-        self.inside = False
-
-    def feed(self, text: str) -> tuple[str, list[ToolCall]]:
-        self.buf += text
-        content, calls = [], []
-        while True:
-            if self.inside:
-                i = self.buf.find(self.end)
-                if i < 0:
-                    break
-                obj = _loads(self.buf[:i].strip())
-                if isinstance(obj, dict) and "name" in obj:
-                    calls.append(ToolCall(obj["name"], obj.get("arguments", obj.get("parameters", {})) or {}))
-                self.buf = self.buf[i + len(self.end):]
-                self.inside = False
-                continue
-            i = self.buf.find(self.start)
-            if i >= 0:
-                content.append(self.buf[:i])
-                self.buf = self.buf[i + len(self.start):]
-                self.inside = True
-                continue
-            h = _holdback(self.buf, [self.start])
-            content.append(self.buf[: len(self.buf) - h])
-            self.buf = self.buf[len(self.buf) - h:]
-            break
-        return "".join(content), calls
-
-    def parse(self, text: str) -> tuple[str, list[ToolCall]]:
-        p = type(self)(self.start, self.end)
-        c, calls = p.feed(text)
-        return c + ("" if p.inside else p.buf), calls
+    bare_recovery = False
 
 
 class JSONObjectToolParser:
-    """A reply that is a JSON object (or list) of calls (Llama 3 style)."""
+    """A reply that is a JSON object (or list) of calls, optionally after a
+    prefix tag (Llama 3 ``<|python_tag|>``, Mistral ``[TOOL_CALLS]``)."""
 
     def __init__(self, prefix: str = ""):
-        self.prefix = prefix
-        self.buf = ""
-
-    def feed(self, text: str):
-        self.buf += text
-        return "", []
-
-    def parse(self, text: str):
-        t = text.strip()
-        if self.prefix and t.startswith(self.prefix):
-            t = t[len(self.prefix):].strip()
-        elif self.prefix:
-            return text, []
-        obj = _loads(t)
-        objs = obj if isinstance(obj, list) else [obj]
-        calls = [ToolCall(o["name"], o.get("parameters", o.get("arguments", {})) or {})
-                 for o in objs if isinstance(o, dict) and "name" in o]
-        return ("" if calls else text), calls
-
-
-class HarmonyToolParser:
-    """``<|channel|>commentary to=functions.NAME<|constrain|>json<|message|>{...}<|call|>``."""
-
-    PAT = re.compile(r"to=functions\.([\w\-\.]+)[^<]*(?:<\|constrain\|>\w+)?<\|message\|>(.*?)<\|call\|>", re.S)
+        self.inner = MistralToolParser() if prefix == "[TOOL_CALLS]" else Llama3ToolParser()
 
     def feed(self, text):
-        return text, []
+        return self.inner.feed(text)
+
+    def flush(self):
+        return self.inner.flush()
 
     def parse(self, text):
-        calls = []
-        for m in self.PAT.finditer(text):
-            args = _loads(m.group(2).strip())
-            calls.append(ToolCall(m.group(1), args if isinstance(args, dict) else {"input": m.group(2)}))
-        content = self.PAT.sub("", text) if calls else text
-        return content, calls
+        return self.inner.parse(text)
 
 
-TOOL_PARSERS = {
-    "hermes": TaggedJSONToolParser,
-    "qwen3": TaggedJSONToolParser,
-    "qwen3_5": TaggedJSONToolParser,
-    "json": TaggedJSONToolParser,
-    "llama3": JSONObjectToolParser,
-    "mistral": lambda: JSONObjectToolParser("[TOOL_CALLS]"),
-    "gpt_oss": HarmonyToolParser,
-    "harmony": HarmonyToolParser,
-}
-
-
-def make_tool_parser(name: str | None):
+def make_tool_parser(name: str | None, tools: list | None = None):
     if not name:
         return None
     if name not in TOOL_PARSERS:
         raise ValueError(f"unknown tool-call parser {name!r}; choose from {sorted(TOOL_PARSERS)}")
-    return TOOL_PARSERS[name]()
+    return TOOL_PARSERS[name](tools)
 
 
 def validate_tool_arguments(call: ToolCall, tools: list[dict] | None) -> list[str]:

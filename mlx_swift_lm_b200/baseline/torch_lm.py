@@ -8,9 +8,13 @@ call, as a plain PyTorch serving build would write it:
 * GEMMs: ``torch.nn.functional.linear`` (cuBLAS / cuBLASLt);
 * RMSNorm, SiLU, RoPE, residual adds: torch elementwise ops;
 * K/V append: ``index_put_`` into the page slab;
-* attention: ``scaled_dot_product_attention`` over each row's pages gathered
-  into a contiguous buffer (decode: the graph-static width of the page
-  table with a length mask; prefill: the row's pages, causal);
+* attention on CUDA: FlashAttention-2 as built by vLLM
+  (``vllm.vllm_flash_attn.flash_attn_varlen_func``, ``fa_version=2``),
+  reading the page slab in place through the page table (page size 16): one
+  call for the decode rows, one for the prefill chunks. This is the
+  attention a stock PyTorch serving stack runs; its compiled kernels need no
+  JIT. On CPU (tests): ``scaled_dot_product_attention`` over each row's
+  pages gathered into a contiguous buffer;
 * tensor parallelism: NCCL ``all_reduce`` after the row-parallel projections;
 * greedy tokens: ``torch.argmax``.
 
@@ -137,6 +141,9 @@ class TorchDecoderLM(DecoderLM):
         self._write_kv(vc, fb.slots, v)
         win = cfg.window(li)
         out = attn.view(T, H, D)
+        if q.is_cuda:
+            self._attention_fa(q, kc, vc, fb, win, out)
+            return self._attn_out(L, attn.view(T, H * D))
         if nd:
             pt = fb.dec_page_table[:nd]
             kg, vg = self._gather(kc, pt), self._gather(vc, pt)
@@ -174,6 +181,33 @@ class TorchDecoderLM(DecoderLM):
                 out[a:b] = o[0].transpose(0, 1)
         return self._attn_out(L, attn.view(T, H * D))
 
+    def _attention_fa(self, q, kc, vc, fb: ForwardBatch, win: int, out):
+        from vllm.vllm_flash_attn import flash_attn_varlen_func
+
+        T, nd = fb.num_tokens, fb.num_decode
+        # [pages, KVH, 16, D] viewed as [pages, 16, KVH, D]: the kernel takes the strides
+        kn, vn = kc.permute(0, 2, 1, 3), vc.permute(0, 2, 1, 3)
+        wsz = (win - 1, 0) if win > 0 else (-1, -1)
+        if nd:
+            if self._dec_cu is None or self._dec_cu.shape[0] < nd + 1 or self._dec_cu.device != q.device:
+                self._dec_cu = torch.arange(1024 + 1, dtype=torch.int32, device=q.device)
+            flash_attn_varlen_func(
+                q[:nd], kn, vn, out=out[:nd], max_seqlen_q=1, cu_seqlens_q=self._dec_cu[:nd + 1],
+                max_seqlen_k=fb.dec_page_table.shape[1] * PAGE, seqused_k=fb.dec_seq_lens[:nd].clamp(min=1),
+                block_table=fb.dec_page_table[:nd], causal=True, softmax_scale=self.cfg.scale, window_size=wsz,
+                fa_version=2)
+        if T > nd:
+            cu = fb.pf_cu_q_host
+            pos0 = fb.pf_pos0_host if fb.pf_pos0_host is not None else fb.pf_pos0.tolist()
+            lens = [cu[r + 1] - cu[r] for r in range(len(cu) - 1)]
+            kv_lens = [int(p0) + n for p0, n in zip(pos0, lens)]
+            flash_attn_varlen_func(
+                q[nd:], kn, vn, out=out[nd:], max_seqlen_q=max(lens), cu_seqlens_q=fb.pf_cu_q, max_seqlen_k=max(kv_lens),
+                seqused_k=fb.pf_pos0 + (fb.pf_cu_q[1:] - fb.pf_cu_q[:-1]), block_table=fb.pf_page_table,
+                causal=True, softmax_scale=self.cfg.scale, window_size=wsz, fa_version=2)
+
+    _dec_cu = None
+
     # ------------------------------------------------------------------ forward
     def forward(self, fb: ForwardBatch, kv, return_hidden: bool = False, inputs_embeds=None, return_both=False,
                 return_residual=False):
@@ -198,9 +232,11 @@ class TorchDecoderLM(DecoderLM):
         logits = F.linear(h, self.lm_head).float()
         return (logits, h) if return_both else logits
 
-    def forward_decode_tokens(self, fb: ForwardBatch, kv, out: torch.Tensor, out2=None):
+    def forward_decode_tokens(self, fb: ForwardBatch, kv, out: torch.Tensor, out2=None, flags=None):
         logits = self.forward(fb, kv)
         out.copy_(torch.argmax(logits, dim=-1).to(torch.int32))
+        if flags is not None:
+            flags.copy_((~torch.isfinite(logits)).any(-1).to(torch.int32))
         return out
 
 

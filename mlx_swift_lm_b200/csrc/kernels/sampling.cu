@@ -13,6 +13,8 @@
 // digits. For top-p the pass histograms accumulate probability mass as
 // 2^30-scaled integers in 64-bit counters, so the result does not depend on
 // the order of atomic additions.
+#include <cfloat>
+
 #include "b200_common.cuh"
 
 namespace b200 {
@@ -351,9 +353,11 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   }
 }
 
-// Greedy argmax only (the all-greedy fast path).
+// Greedy argmax only (the all-greedy fast path). With `flags`, flags[b] = 1
+// when any logit of the row is NaN or +-infinity (NaN never wins the argmax,
+// so the token alone cannot show it), else 0.
 __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restrict__ logits, int64_t ld, int V,
-                                                          int* out, int* out2) {
+                                                          int* out, int* out2, int* flags) {
   b200::pdl_launch_dependents();
   b200::pdl_wait();
   __shared__ float sv[32];
@@ -364,23 +368,30 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
   int bi = 0x7fffffff;
   const int V4 = (ld % 4 == 0) ? V / 4 : 0;
   const float4* lg4 = reinterpret_cast<const float4*>(lg);
+  // |x| <= FLT_MAX is false exactly for NaN and +-infinity
+  bool bad = false;
   for (int i = threadIdx.x; i < V4; i += blockDim.x) {
     const float4 x = lg4[i];
+    bad |= !(fabsf(x.x) <= FLT_MAX) | !(fabsf(x.y) <= FLT_MAX) | !(fabsf(x.z) <= FLT_MAX) | !(fabsf(x.w) <= FLT_MAX);
     if (x.x > bv) { bv = x.x; bi = 4 * i; }
     if (x.y > bv) { bv = x.y; bi = 4 * i + 1; }
     if (x.z > bv) { bv = x.z; bi = 4 * i + 2; }
     if (x.w > bv) { bv = x.w; bi = 4 * i + 3; }
   }
-  for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x)
+  for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x) {
+    bad |= !(fabsf(lg[i]) <= FLT_MAX);
     if (lg[i] > bv) {
       bv = lg[i];
       bi = i;
     }
+  }
+  const int any_bad = flags ? __syncthreads_or(bad ? 1 : 0) : 0;
   block_argmax(bv, bi, sv, si);
   if (threadIdx.x == 0) {
     const int tok = bi == 0x7fffffff ? 0 : bi;
     out[b] = tok;
     if (out2) out2[b] = tok;
+    if (flags) flags[b] = any_bad;
   }
 }
 
@@ -637,10 +648,10 @@ int b200_argmax_conf(const float* logits, int64_t ld, int B, int V, int* tok, fl
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
-int b200_argmax(const float* logits, int64_t ld, int B, int V, int* out, int* out2, cudaStream_t st) {
+int b200_argmax(const float* logits, int64_t ld, int B, int V, int* out, int* out2, int* flags, cudaStream_t st) {
   if (B <= 0) return 0;
-b200::launch_k(  argmax_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, out, out2);
-  return (int)cudaGetLastError();
+  cudaError_t e = b200::launch_k(argmax_kernel, dim3(B), dim3(kThreads), 0, st, 1, logits, ld, V, out, out2, flags);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 int b200_logprobs(const float* logits, int64_t ld, int B, int V, const int* tokens, int n_top, float* out_lp,

@@ -35,6 +35,9 @@ from .types import CapacitySnapshot, Event, FinishReason, Request, now
 STREAM_CAPACITY = 256  # events buffered per request before backpressure pauses it
 
 
+NON_FINITE_MESSAGE = "non-finite logits: the model produced NaN or infinity"
+
+
 @dataclass
 class EngineConfig:
     scheduler: SchedulerConfig = field(default_factory=SchedulerConfig)
@@ -53,6 +56,8 @@ class EngineConfig:
     decode_progress_timeout_s: float = 0.0
     leases: object = None  # engine.leases.LeaseConfig; None = no leases
     clock: object = None  # injectable monotonic clock (tests)
+    # (open_id, close_id[, starts_inside]) thought markers for integer Request.reasoning_budget values
+    reasoning_markers: tuple | None = None
 
 
 class RequestStream:
@@ -183,6 +188,7 @@ class EngineV2:
         self.h2d_bytes = 0  # eager-path step inputs copied host -> device
         self.d2h_bytes = 0  # eager-path sampled tokens read back
         self.forward_shapes: list[tuple[int, int]] = []
+        self.non_finite_rows = 0  # rows ended because their logits held NaN / infinity
         self.record_shapes = False
         from .diagnostics import Diagnostics
 
@@ -212,6 +218,9 @@ class EngineV2:
             # placeholder token ids do not identify the image: no prefix reuse;
             # MTP drafts from text positions only
             req.prefix_cache_enabled = False
+        from .reasoning import ReasoningBudgetState, resolve_budget
+
+        budget = resolve_budget(req.reasoning_budget, self.cfg.reasoning_markers)
         with self._lock:
             ftd = req.first_token_deadline
             if ftd is not None:
@@ -231,6 +240,8 @@ class EngineV2:
             if self.tok is not None:
                 st.detok = IncrementalDetokenizer(self.tok)
             st.extra["hold"] = StopHoldback(req.stop_strings)
+            if budget is not None:
+                st.extra["budget"] = ReasoningBudgetState(budget)
             stream = RequestStream(self, st)
             st.stream = stream
             self.states[req.id] = st
@@ -413,11 +424,19 @@ class EngineV2:
                     toks, lp = self.sampler.sample(logits, [r.state for r in srows])
                 toks_host = toks.cpu().tolist() if toks.numel() else []
                 self.d2h_bytes += toks.numel() * toks.element_size()
+                bad_rows = set()
+                flags = getattr(self.sampler, "last_flags", None)
+                if flags is not None and len(toks_host):
+                    bad_rows = {i for i, f in enumerate(flags.cpu().tolist()) if f}
+                    self.d2h_bytes += flags.numel() * flags.element_size()
                 for r in plan.rows:
                     self.sched.commit(r)
                     r.state.timing.prefill_chunks += 0 if r.is_decode else 1
                 lps = self.sampler.logprob_entries(lp, toks_host, [r.state for r in srows])
                 for i, (r, t, l) in enumerate(zip(srows, toks_host, lps)):
+                    if i in bad_rows:
+                        events += self._non_finite(r.state)
+                        continue
                     events += self._accept_token(r.state, int(t), l)
                     if hid is not None and r.state.status != Status.FINISHED:
                         self.mtp.on_first_token(r.state, hid[i])
@@ -445,20 +464,30 @@ class EngineV2:
     def _row_needs_eager(self, st) -> bool:
         sp = st.req.sampling
         return (not sp.greedy or st.req.token_constraint is not None or sp.logprobs or sp.top_logprobs > 0
-                or sp.needs_processing or st.req.lora is not None)
+                or sp.needs_processing or st.req.lora is not None or "budget" in st.extra)
 
     def _finalize_inflight(self, inflight) -> list[Event]:
         plan, handle = inflight
-        toks_host = self.graphs.read_tokens(handle, len(plan.rows))
+        toks_host, flags = self.graphs.read_tokens(handle, len(plan.rows))
         events = []
-        for r, t in zip(plan.rows, toks_host):
+        for r, t, bad in zip(plan.rows, toks_host, flags):
             st = r.state
             if st.status == Status.FINISHED:
                 # the row finished while this step was in flight; its extra K/V went to
                 # pages it already released (stream order makes their reuse safe)
                 continue
+            if bad:
+                events += self._non_finite(st)
+                continue
             events += self._accept_token(st, int(t), None, index=r.start + 1)
         return events
+
+    def _non_finite(self, st) -> list[Event]:
+        """A row whose logits held NaN or infinity defines no token: it ends
+        with an error and commits nothing from that position
+        (ContinuousBatchingV2/CBv2NonFiniteLogits.swift:16)."""
+        self.non_finite_rows += 1
+        return self._finish(st, FinishReason.ERROR, error=NON_FINITE_MESSAGE, cause="non_finite_logits")
 
     def _drain_inflight(self) -> list[Event]:
         if self._inflight is None:
@@ -488,6 +517,9 @@ class EngineV2:
         st.extra["last_progress"] = self._clock()
         if st.req.token_constraint is not None:
             st.req.token_constraint.commit(tok)
+        budget = st.extra.get("budget")
+        if budget is not None:
+            budget.confirm(tok)
         reason = None
         if (tok in st.req.stop_tokens or (tok in self.eos and not st.req.ignore_eos)):
             reason = FinishReason.STOP
@@ -511,6 +543,8 @@ class EngineV2:
         ev = Event(st.req.id, tokens=emit_tokens, text=text, logprobs=[lp] if lp is not None else None)
         events = [ev]
         st.stream.put(ev)
+        if budget is not None and budget.failure is not None:
+            return events + self._finish(st, FinishReason.ERROR, error=budget.failure)
         if reason is not None:
             events += self._finish(st, reason)
         return events

@@ -62,7 +62,10 @@ class DecodeGraphRunner:
         self.ss = self.packed[self.o_ss:self.o_ss + B]
         self.ids = torch.zeros(B, dtype=torch.int32, device=self.dev)
         self.out = torch.zeros(B, dtype=torch.int32, device=self.dev)
+        # non-finite-logit flag per row, read back with the tokens
+        self.flags = torch.zeros(B, dtype=torch.int32, device=self.dev)
         self.host_out = [torch.zeros(B, dtype=torch.int32).pin_memory() for _ in range(4)]
+        self.host_flags = [torch.zeros(B, dtype=torch.int32).pin_memory() for _ in range(4)]
         self.out_k = 0
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.pool = None
@@ -90,7 +93,7 @@ class DecodeGraphRunner:
                             state_slots=self.ss[:B] if self.rec is not None else None)
 
     def _body(self, B):
-        self.model.forward_decode_tokens(self._fb(B), self.eng.kv, self.out[:B])
+        self.model.forward_decode_tokens(self._fb(B), self.eng.kv, self.out[:B], flags=self.flags[:B])
 
     def capture(self, B):
         self._reserve()
@@ -233,13 +236,16 @@ class DecodeGraphRunner:
         self.out_k = (self.out_k + 1) % len(self.host_out)
         m = max(where) + 1 if where else 0
         self.host_out[ko][:m].copy_(self.out[:m], non_blocking=True)
-        self.d2h_bytes += 4 * m
+        self.host_flags[ko][:m].copy_(self.flags[:m], non_blocking=True)
+        self.d2h_bytes += 8 * m
         done = torch.cuda.Event()
         done.record()
         return (ko, done, n, where)
 
     def read_tokens(self, handle, n):
+        """(tokens, non-finite flags) of the plan rows of a launched step."""
         ko, done, n0, where = handle
         done.synchronize()
         h = self.host_out[ko].tolist()
-        return [h[where[i]] for i in range(n)]
+        f = self.host_flags[ko].tolist()
+        return [h[where[i]] for i in range(n)], [f[where[i]] for i in range(n)]

@@ -94,7 +94,8 @@ class MTPDriver:
             st = r.state
             sp = st.req.sampling
             if (not sp.greedy or st.req.token_constraint is not None or sp.logprobs or sp.top_logprobs > 0
-                    or sp.needs_processing or "mtp_h" not in st.extra or st.req.mm is not None):
+                    or sp.needs_processing or "mtp_h" not in st.extra or st.req.mm is not None
+                    or "budget" in st.extra):
                 return False
         return True
 

@@ -43,11 +43,28 @@ class Sampler:
         return rep, outs
 
     def _allow_mask(self, st):
+        """numpy bool [V] of allowed tokens (grammar / tool constraint AND the
+        reasoning budget), or None when every token is allowed."""
         c = st.req.token_constraint
-        if c is None:
-            return None
-        m = c.allowed_mask(self.V)  # numpy bool [V] or None
+        m = c.allowed_mask(self.V) if c is not None else None
+        budget = st.extra.get("budget") if hasattr(st, "extra") else None
+        if budget is not None:
+            bm = budget.allowed_mask(self.V)
+            if bm is not None:
+                m = bm if m is None else (m & bm)
         return m
+
+    @staticmethod
+    def _forced(states):
+        """(row, token) pairs whose next token is fixed (an exhausted reasoning
+        budget forces the thought closer, even over a -inf logit)."""
+        out = []
+        for i, st in enumerate(states):
+            b = st.extra.get("budget") if hasattr(st, "extra") else None
+            f = b.forced() if b is not None else None
+            if f is not None:
+                out.append((i, f))
+        return out
 
     # ------------------------------------------------------------------ main
     def sample(self, logits: torch.Tensor, states: list, out: torch.Tensor | None = None):
@@ -62,15 +79,25 @@ class Sampler:
         masks = [self._allow_mask(st) for st in states]
         need_proc = any(st.req.sampling.needs_processing for st in states) or any(m is not None for m in masks)
         all_greedy = all(st.req.sampling.greedy for st in states)
+        # non-finite flags describe the model's logits, before bias / penalties / masks
+        # add their -inf entries; the all-greedy unprocessed path gets them from the argmax pass
+        fused_flags = logits.is_cuda and all_greedy and not need_proc
+        self.last_flags = None if fused_flags else (~torch.isfinite(logits)).any(-1).to(torch.int32)
         if not logits.is_cuda:
             toks = self._sample_cpu(logits, states, masks)
         else:
             if need_proc:
                 self._process_cuda(logits, states, masks)
             if all_greedy:
-                toks = ops.argmax(logits, out=out)
+                if fused_flags:
+                    self.last_flags = torch.empty(R, dtype=torch.int32, device=logits.device)
+                toks = ops.argmax(logits, out=out, flags=self.last_flags if fused_flags else None)
             else:
                 toks = self._sample_cuda(logits, states, out)
+        forced = self._forced(states)
+        if forced:
+            idx = torch.tensor([i for i, _ in forced], dtype=torch.long, device=toks.device)
+            toks[idx] = torch.tensor([t for _, t in forced], dtype=toks.dtype, device=toks.device)
         if want_lp:
             n_top = max(st.req.sampling.top_logprobs for st in states)
             tok_lp, top_ids, top_lp = ops.logprobs(raw, toks, n_top)

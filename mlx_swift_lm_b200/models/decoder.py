@@ -583,14 +583,16 @@ class DecoderLM:
         logits, h = self.forward(fb, kv, return_both=True)
         return ops.argmax(logits), h
 
-    def forward_decode_tokens(self, fb: ForwardBatch, kv, out: torch.Tensor, out2=None):
+    def forward_decode_tokens(self, fb: ForwardBatch, kv, out: torch.Tensor, out2=None, flags=None):
         """Greedy tokens of a pure-decode batch: the fused TP path when
-        enabled, else forward + argmax."""
+        enabled, else forward + argmax. `flags` (int32 [rows]) receives the
+        non-finite-logit flag of each row (the fused TP path's split argmax
+        leaves it untouched)."""
         tpf = getattr(self, "tp_fused", None)
         if tpf is not None and fb.num_decode == fb.num_tokens and fb.num_tokens <= tpf.M_pad:
             return tpf.decode_tokens(fb, kv, out, out2)
         logits = self.forward(fb, kv)
-        return ops.argmax(logits, out=out, out2=out2)
+        return ops.argmax(logits, out=out, out2=out2, flags=flags)
 
     # ------------------------------------------------------------------ dense forward
     def new_cache(self) -> DenseKVCache:

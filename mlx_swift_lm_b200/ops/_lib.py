@@ -50,7 +50,7 @@ _SIGS = {
     "b200_logits_process": (i32, [vp, i64, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp, vp, vp, i32, vp, vp, vp,
                                   i32, vp, vp]),
     "b200_sample": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
-    "b200_argmax": (i32, [vp, i64, i32, i32, vp, vp, vp]),
+    "b200_argmax": (i32, [vp, i64, i32, i32, vp, vp, vp, vp]),
     "b200_argmax_conf": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, i32, vp]),
     "b200_logprobs": (i32, [vp, i64, i32, i32, vp, i32, vp, vp, vp, vp]),
     "b200_philox_u32": (C.c_uint32, [u64, u64, C.c_uint32]),

@@ -7,22 +7,28 @@ from . import _lib
 from . import reference as ref
 
 
-def argmax(logits: torch.Tensor, out: torch.Tensor | None = None, out2: torch.Tensor | None = None):
+def argmax(logits: torch.Tensor, out: torch.Tensor | None = None, out2: torch.Tensor | None = None,
+           flags: torch.Tensor | None = None):
     """Greedy tokens [B] int32 from fp32 logits [B, V]. `out2` optionally
-    receives a second copy (e.g. the next decode step's input ids)."""
+    receives a second copy (e.g. the next decode step's input ids); `flags`
+    (int32 [B]) receives 1 for rows holding a NaN or infinite logit, from the
+    same pass over the logits."""
     if not logits.is_cuda:
-        y = logits.float().argmax(-1).to(torch.int32)
+        lf = logits.float()
+        y = torch.nan_to_num(lf, nan=-float("inf")).argmax(-1).to(torch.int32)
         if out is not None:
             out.copy_(y)
             y = out
         if out2 is not None:
             out2.copy_(y)
+        if flags is not None:
+            flags.copy_((~torch.isfinite(lf)).any(-1).to(torch.int32))
         return y
     B, V = logits.shape
     if out is None:
         out = torch.empty(B, dtype=torch.int32, device=logits.device)
     rc = _lib.lib().b200_argmax(logits.data_ptr(), logits.stride(0), B, V, out.data_ptr(), _lib.ptr(out2),
-                                _lib.stream_ptr(logits.device))
+                                _lib.ptr(flags), _lib.stream_ptr(logits.device))
     _lib.check(rc, "argmax")
     _lib.count(1)
     return out

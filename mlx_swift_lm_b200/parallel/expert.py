@@ -479,7 +479,7 @@ class ExpertParallelDecoderLM(DecoderLM):
         return (self._gather_rows(tok, counts).index_select(0, inv),
                 self._gather_rows(h, counts).index_select(0, inv))
 
-    def forward_decode_tokens(self, fb: ForwardBatch, kv, out: torch.Tensor, out2=None):
+    def forward_decode_tokens(self, fb: ForwardBatch, kv, out: torch.Tensor, out2=None, flags=None):
         """Greedy tokens of a pure-decode batch whose row count is a multiple
         of the EP world (decode graph buckets): rank r computes rows
         [r * S, (r + 1) * S) and the tokens are all-gathered."""
@@ -487,7 +487,7 @@ class ExpertParallelDecoderLM(DecoderLM):
         B = fb.num_tokens
         if ep.world == 1 or B % ep.world or fb.num_decode != B:
             logits = self.forward(fb, kv)
-            return ops.argmax(logits, out=out, out2=out2)
+            return ops.argmax(logits, out=out, out2=out2, flags=flags)
         if not self._capturing():
             self.begin_step()
         S = B // ep.world

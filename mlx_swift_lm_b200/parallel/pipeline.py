@@ -125,7 +125,7 @@ class PipelinedDecoderLM(DecoderLM):
             return torch.cat([o[0] for o in outs], 0), torch.cat([o[1] for o in outs], 0)
         return torch.cat(outs, 0)
 
-    def forward_decode_tokens(self, fb, kv, out, out2=None):
+    def forward_decode_tokens(self, fb, kv, out, out2=None, flags=None):
         from .. import ops
 
         logits = self.forward(fb, kv)

@@ -188,7 +188,7 @@ class OpenAIService:
         rid = "chatcmpl-" + uuid.uuid4().hex[:24]
         created = int(time.time())
         rp = make_reasoning_parser(body.get("reasoning_parser") or self.reasoning_parser_name)
-        tp = make_tool_parser(self.tool_parser_name) if tools else None
+        tp = make_tool_parser(self.tool_parser_name, tools) if tools else None
         want_stream = body.get("stream", False) if stream_override is None else stream_override
         if want_stream:
             return StreamingResponse(self._chat_sse(stream, rid, created, rp, tp, len(tokens), body),
@@ -258,7 +258,22 @@ class OpenAIService:
             if r:
                 yield frame({"reasoning_content": r})
             if t:
-                yield frame({"content": t})
+                if tp is not None:
+                    c, calls = tp.feed(t)
+                    if c:
+                        yield frame({"content": c})
+                    for i, call in enumerate(calls):
+                        yield frame({"tool_calls": [{"index": len(buffered) + i, **call.to_openai()}]})
+                    buffered.extend(calls)
+                else:
+                    yield frame({"content": t})
+        if tp is not None:  # a frame cut off by end-of-sequence, or content held back at the end
+            c, calls = tp.flush()
+            if c:
+                yield frame({"content": c})
+            for i, call in enumerate(calls):
+                yield frame({"tool_calls": [{"index": len(buffered) + i, **call.to_openai()}]})
+            buffered.extend(calls)
         self._count_usage(usage)
         fin = "tool_calls" if buffered else _finish(finish)
         extra = {"usage": _usage(usage)} if (body.get("stream_options") or {}).get("include_usage") else None

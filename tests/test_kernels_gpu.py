@@ -300,3 +300,21 @@ def test_paged_decode_cuda_core_path(H, KVH, D):
     finally:
         att.USE_MMA_DECODE[0] = True
     assert _rel(y.cpu(), r) < 1e-2
+
+
+@pytest.mark.parametrize("V", [151936, 1001])
+def test_argmax_nonfinite_flags(V):
+    """The greedy pass flags rows holding NaN or +-inf (NaN never wins the
+    argmax, so the token alone cannot show it) and leaves finite rows as torch."""
+    torch.manual_seed(3)
+    x = torch.randn(5, V, device="cuda")
+    x[1, 17] = float("nan")
+    x[2, V - 1] = float("inf")
+    x[3, 0] = -float("inf")
+    flags = torch.full((5,), 7, dtype=torch.int32, device="cuda")
+    tok = ops.argmax(x, flags=flags)
+    torch.cuda.synchronize()
+    assert flags.tolist() == [0, 1, 1, 1, 0]
+    for r in (0, 3, 4):
+        assert tok[r].item() == x[r].argmax().item()
+    assert tok[2].item() == V - 1
