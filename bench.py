@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--out-tokens", type=int, default=256)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the headline)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--temperature", type=float, default=0.0, help="sampled traffic (0 = greedy)")
+    ap.add_argument("--top-p", type=float, default=1.0)
     ap.add_argument("--tp-mode", default=None, choices=["fused", "nccl"],
                     help="tensor-parallel collectives: fused symmetric-memory kernels (default with 2+ GPUs) or "
                          "NCCL all-reduce")
@@ -253,12 +255,25 @@ def run_arm(args, impl, world, rank, local, dev, group):
     from mlx_swift_lm_b200.ops import _lib
 
     cfg, model, eng, mtp = _build(args, impl, world, rank, dev, group)
+    # untimed warm-up request: first-use costs (lazy module loads, library
+    # initialisation, first graph captures of small buckets) stay out of TTFT
+    warm = [eng.submit(Request(prompt_tokens=list(range(1, 65 + 31 * i)), max_tokens=4,
+                               sampling=SamplingParams(temperature=0.0), ignore_eos=True)) for i in range(2)]
+    while any(s.st.status != Status.FINISHED for s in warm):
+        eng.step()
+    eng._drain_inflight()
+    if world > 1:
+        dist.barrier()
     rng = np.random.default_rng(args.seed)
     lens = rng.integers(args.min_prompt, args.max_prompt + 1, size=args.streams)
     prompts = [rng.integers(0, cfg.vocab_size, size=int(n)).tolist() for n in lens]
-    greedy = SamplingParams(temperature=0.0)
-    streams = [eng.submit(Request(prompt_tokens=p, max_tokens=args.out_tokens, sampling=greedy, ignore_eos=True))
-               for p in prompts]
+    def sp(i):
+        if args.temperature <= 0:
+            return SamplingParams(temperature=0.0)
+        return SamplingParams(temperature=args.temperature, top_p=args.top_p, seed=args.seed * 1000 + i)
+
+    streams = [eng.submit(Request(prompt_tokens=p, max_tokens=args.out_tokens, sampling=sp(i), ignore_eos=True))
+               for i, p in enumerate(prompts)]
 
     def barrier():
         if world > 1:
@@ -366,12 +381,14 @@ def main():
 
     res = run_arm(args, args.impl, world, rank, local, dev, group)
     base, why = None, None
-    dense = not (args.pp > 1 or args.ep > 1 or args.mtp or args.quant_experts or args.quant_dense or args.kv_fp8)
+    dense = not (args.pp > 1 or args.ep > 1 or args.mtp or args.quant_experts or args.quant_dense or args.kv_fp8
+                 or args.temperature > 0)
     if args.impl == "ours" and args.compare and dense:
         gc.collect()
         base = run_arm(args, "baseline", world, rank, local, dev, group)
     elif args.impl == "ours":
-        why = "no NCCL+cuBLAS arm for this configuration (dense bf16 TP only)" if not dense else "--no-compare"
+        why = ("no NCCL+cuBLAS arm for this configuration (dense bf16 greedy TP only)" if not dense
+               else "--no-compare")
     cfg = res.pop("cfg")
     if rank == 0:
         out = {"metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -390,6 +407,8 @@ def main():
                        "parallelism": _par(args, world) if args.impl == "ours" else f"tp{world} (NCCL all_reduce)",
                        "experts": f"q{args.quant_experts} g64" if args.quant_experts else "bf16", "mtp_k": args.mtp,
                        "kv": ("paged fp8-e4m3 (per-head scales)" if args.kv_fp8 else "paged bf16") + ", page 16",
+                       "sampling": ("greedy" if args.temperature <= 0 else
+                                    f"temperature {args.temperature}, top_p {args.top_p}, per-request seeds"),
                        "l2": "inputs larger than L2 (weights ~16 GB/world + KV per step)",
                        "timed": f"value: {args.steps} consecutive engine decode steps (64 rows, live KV positions) "
                                 f"after {args.warmup} warm-up steps, CUDA events, max over ranks"},

@@ -38,6 +38,7 @@ class TorchDecoderLM(DecoderLM):
     """:class:`DecoderLM` with every op replaced by a PyTorch / cuBLAS / NCCL call."""
 
     scratch_page = None
+    graph_sampling = False  # its engine sampler is greedy-only
 
     # ------------------------------------------------------------------ engine hooks
     def bind_engine(self, engine):

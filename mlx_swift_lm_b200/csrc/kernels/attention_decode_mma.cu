@@ -41,6 +41,10 @@ struct Args {
   int H, KVH, ld_pt, max_parts, window;
   int64_t num_pages;
   float scale, softcap;
+  // fused merge (null counters: partials only, merged by paged_decode_merge_kernel)
+  int* counters;        // [B * KVH] arrival counts, zero between launches (the merging CTA resets its own)
+  const float* sinks;   // [H] or null
+  __nv_bfloat16* out;   // [B, H, D]
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -95,7 +99,13 @@ __global__ void __launch_bounds__(128) decode_mma_kernel(const __grid_constant__
   pdl_wait();
   const int L = a.seq_lens[b];
   const int start = a.window > 0 ? max(0, L - a.window) : 0;
-  if (L <= 0) return;
+  if (L <= 0) {
+    // an empty row (graph padding): its output is zero, written once
+    if (a.counters && part == 0)
+      for (int e = threadIdx.x; e < G * D; e += 128)
+        a.out[((size_t)b * a.H + kvh * G + e / D) * D + e % D] = f2bf(0.f);
+    return;
+  }
   const int p_first = start / kPart, p_last = (L - 1) / kPart;
   if (part < p_first || part > p_last) return;
   __syncthreads();
@@ -287,6 +297,76 @@ __global__ void __launch_bounds__(128) decode_mma_kernel(const __grid_constant__
       a.part_ml[pidx * 2 + 1] = Ls;
     }
   }
+  if (!a.counters) return;
+  // ---- fused merge: the last of the row's live partitions to finish merges
+  // all of them, in partition order (the same sums as the separate merge pass)
+  __shared__ int s_last;
+  __threadfence();  // publish this CTA's partials before counting it
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int n_live = p_last - p_first + 1;
+    int* cnt = a.counters + (size_t)b * a.KVH + kvh;
+    const int prev = atomicAdd(cnt, 1);
+    s_last = prev == n_live - 1;
+    if (s_last) *cnt = 0;  // ready for the next launch (stream order separates them)
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // see the other CTAs' partials
+  // (max, sum) pairs of the G heads' live partitions -> shared memory (the
+  // page rings are free now), then per-head weights; partial rows are read
+  // with cache-global loads (L1 does not hold other SMs' writes), all issued
+  // independently so their L2 latencies overlap
+  const int n_live = p_last - p_first + 1;
+  if (3 * G * n_live + G > 128 * D) {  // more partitions than the staging area holds: direct loads
+    for (int e = threadIdx.x; e < G * D; e += 128) {
+      const int row = e / D, d = e % D, h = kvh * G + row;
+      const size_t base = ((size_t)b * a.H + h) * a.max_parts;
+      float M = a.sinks ? a.sinks[h] * kLog2e : -INFINITY;
+      for (int p = p_first; p <= p_last; ++p) M = fmaxf(M, __ldcg(a.part_ml + (base + p) * 2));
+      float den = a.sinks ? exp2f(a.sinks[h] * kLog2e - M) : 0.f, accv = 0.f;
+      for (int p = p_first; p <= p_last; ++p) {
+        const float mp = __ldcg(a.part_ml + (base + p) * 2);
+        const float w = (mp == -INFINITY) ? 0.f : exp2f(mp - M);
+        den += __ldcg(a.part_ml + (base + p) * 2 + 1) * w;
+        accv += __ldcg(a.part_acc + (base + p) * D + d) * w;
+      }
+      a.out[((size_t)b * a.H + h) * D + d] = f2bf(accv * (den > 0.f ? 1.f / den : 0.f));
+    }
+    return;
+  }
+  float* sml = reinterpret_cast<float*>(smem);      // [G][n_live][2]
+  float* swt = sml + 2 * G * n_live;                 // [G][n_live] weights
+  float* sinv = swt + G * n_live;                    // [G] 1 / denominator
+  for (int e = threadIdx.x; e < G * n_live; e += 128) {
+    const int row = e / n_live, p = p_first + e % n_live;
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(a.part_ml) +
+                            ((size_t)b * a.H + kvh * G + row) * a.max_parts + p);
+    sml[2 * e] = v.x;
+    sml[2 * e + 1] = v.y;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int row = threadIdx.x, h = kvh * G + row;
+    float M = a.sinks ? a.sinks[h] * kLog2e : -INFINITY;
+    for (int i = 0; i < n_live; ++i) M = fmaxf(M, sml[2 * (row * n_live + i)]);
+    float den = a.sinks ? exp2f(a.sinks[h] * kLog2e - M) : 0.f;
+    for (int i = 0; i < n_live; ++i) {
+      const float mp = sml[2 * (row * n_live + i)];
+      const float w = (mp == -INFINITY) ? 0.f : exp2f(mp - M);
+      den += sml[2 * (row * n_live + i) + 1] * w;
+      swt[row * n_live + i] = w;
+    }
+    sinv[row] = den > 0.f ? 1.f / den : 0.f;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += 128) {
+    const int row = e / D, d = e % D;
+    const size_t base = ((size_t)b * a.H + kvh * G + row) * a.max_parts;
+    float accv = 0.f;
+    for (int i = 0; i < n_live; ++i) accv += __ldcg(a.part_acc + (base + p_first + i) * D + d) * swt[row * n_live + i];
+    a.out[((size_t)b * a.H + kvh * G + row) * D + d] = f2bf(accv * sinv[row]);
+  }
 }
 
 template <int D, int G>
@@ -315,7 +395,35 @@ extern "C" int b200_paged_decode_mma_part(const void* q, const void* k_cache, co
   if (!make_tmap_2d(&tk, k_cache, rows, D, D, 16, 64, 2)) return -1;
   if (!make_tmap_2d(&tv, v_cache, rows, D, D, 16, 64, 2)) return -1;
   mmadec::Args a{reinterpret_cast<const __nv_bfloat16*>(q), page_table, seq_lens, part_acc, part_ml, H, KVH, ld_pt,
-                 max_parts, window, num_pages, scale, softcap};
+                 max_parts, window, num_pages, scale, softcap, nullptr, nullptr, nullptr};
+#define B200_DEC(DD, GG) \
+  if (D == DD && G == GG) return mmadec::launch<DD, GG>(tk, tv, a, B, st);
+  B200_DEC(64, 1) B200_DEC(64, 2) B200_DEC(64, 4) B200_DEC(64, 8) B200_DEC(64, 16)
+  B200_DEC(128, 1) B200_DEC(128, 2) B200_DEC(128, 4) B200_DEC(128, 8) B200_DEC(128, 16)
+  B200_DEC(256, 1) B200_DEC(256, 2) B200_DEC(256, 4) B200_DEC(256, 8)
+#undef B200_DEC
+  return -1;
+}
+
+// Partition pass with the merge fused in: the last CTA of each (row, KV head)
+// to finish merges the row's partitions in partition order and writes `out`.
+// `counters` [B * KVH] int32 must be zero at the first call; every call leaves
+// it zero again.
+extern "C" int b200_paged_decode_mma(const void* q, const void* k_cache, const void* v_cache,
+                                          const int* page_table, int ld_pt, const int* seq_lens, float* part_acc,
+                                          float* part_ml, int* counters, const float* sinks, void* out, int B, int H, int KVH,
+                                     int D, int max_parts, int window,
+                                          float scale, float softcap, int64_t num_pages, cudaStream_t st) {
+  if (B <= 0) return 0;
+  if (H % KVH || !counters || !out) return -1;
+  const int G = H / KVH;
+  CUtensorMap tk, tv;
+  const int64_t rows = num_pages * KVH * 16;
+  if (!make_tmap_2d(&tk, k_cache, rows, D, D, 16, 64, 2)) return -1;
+  if (!make_tmap_2d(&tv, v_cache, rows, D, D, 16, 64, 2)) return -1;
+  mmadec::Args a{reinterpret_cast<const __nv_bfloat16*>(q), page_table, seq_lens, part_acc, part_ml, H, KVH, ld_pt,
+                 max_parts, window, num_pages, scale, softcap, counters, sinks,
+                 reinterpret_cast<__nv_bfloat16*>(out)};
 #define B200_DEC(DD, GG) \
   if (D == DD && G == GG) return mmadec::launch<DD, GG>(tk, tv, a, B, st);
   B200_DEC(64, 1) B200_DEC(64, 2) B200_DEC(64, 4) B200_DEC(64, 8) B200_DEC(64, 16)

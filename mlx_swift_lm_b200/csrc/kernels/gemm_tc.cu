@@ -47,6 +47,30 @@ enum GemmEpilogue : int {
   kEpiGeluTanh = 7,   // Y = bf16(gelu(acc)), tanh approximation
   kEpiQuickGelu = 8,  // Y = bf16(acc * sigmoid(1.702 acc)) (CLIP / Qwen-VL vision MLPs)
   kEpiRelu2 = 9,      // Y = bf16(relu(acc)^2) (NemotronH / Nemotron 3 MLPs)
+  kEpiQKRope = 10,    // fused q|k|v projection, head dim 128: qk-norm + RoPE + paged K/V append (RopeKvEpi)
+};
+
+// kEpiQKRope: each 128-row weight tile is one head of the q|k|v projection
+// (head dim 128, full non-interleaved rotary). The epilogue rounds the
+// projection to bf16 (as the unfused GEMM output), applies the q/k RMSNorm
+// weights (warp reduction over the head), rotates with the cos|sin table row
+// of the token's position (partners 64 channels apart = lane ^ 16), stores q
+// into q_out [M, H, 128] and k / v into the paged cache slot of the token
+// (bf16, or fp8-e4m3 divided by the per-head scale); slot < 0 skips.
+struct RopeKvEpi {
+  const int* positions;
+  const int64_t* slots;
+  const float* cos_sin;  // [max_pos, 128] fp32: cos | sin
+  const __nv_bfloat16* qw;
+  const __nv_bfloat16* kw;
+  __nv_bfloat16* q_out;
+  void* k_cache;  // [pages, KVH, 16, 128]
+  void* v_cache;
+  const float* k_scale;
+  const float* v_scale;
+  int64_t num_slots;
+  float eps;
+  int H, KVH, kv_fp8;
 };
 
 __device__ __forceinline__ float gelu_act(int epi, float x) {
@@ -79,7 +103,25 @@ struct GemmArgs {
   int epi;
   unsigned long long* trace;  // optional [ctas][6] %globaltimer stamps (diagnostics), null in production
   unsigned long long* ktrace;  // optional per-K-block stamps of CTA 0 (diagnostics), null in production
+  RopeKvEpi rk;                // kEpiQKRope only
 };
+
+__device__ __forceinline__ void store4_kv(void* cache, bool fp8, size_t idx, const float* x, float sc) {
+  if (fp8) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_fp8_e4m3 f(x[e] * sc);
+      w |= (uint32_t)(*reinterpret_cast<uint8_t*>(&f)) << (8 * e);
+    }
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(cache) + idx) = w;
+  } else {
+    __nv_bfloat16 o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = f2bf(x[e]);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(cache) + idx) = *reinterpret_cast<const uint2*>(o);
+  }
+}
 
 // Shared-memory plan of one CTA.
 // bf16 weights (WQ = 0): STAGES stages of {A weight tile (TMA), B activation
@@ -458,6 +500,56 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
       const float4 v4 = red4(j, r4);
       const float v[4] = {v4.x + bb[0], v4.y + bb[1], v4.z + bb[2], v4.w + bb[3]};
       const size_t m = (size_t)(m0 + j);
+      if (MODE == kModeLocal && args.epi == kEpiQKRope) {
+        // one warp per token column: the warp holds the token's whole head (4 channels per lane)
+        const RopeKvEpi& rk = args.rk;
+        const int head = n0 >> 7, d0 = r4 * 4;
+        float x[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = bf2f(f2bf(v[e]));
+        const int64_t slot = rk.slots ? rk.slots[m] : -1;
+        const bool slot_ok = slot >= 0 && slot < rk.num_slots;
+        if (rk.slots && slot >= rk.num_slots && r4 == 0) set_status(kErrBounds);
+        if (head < rk.H + rk.KVH) {
+          const bool is_q = head < rk.H;
+          const __nv_bfloat16* nw = is_q ? rk.qw : rk.kw;
+          if (nw) {
+            const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+            const float inv = rsqrtf(ss / 128.f + rk.eps);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) x[e] = bf2f(f2bf(x[e] * inv * bf2f(nw[d0 + e])));
+          }
+          // cos|sin of the 4 channels' frequencies: two 16-byte loads
+          const float* cs = rk.cos_sin + (size_t)rk.positions[m] * 128 + (d0 & 63);
+          const float4 c4 = *reinterpret_cast<const float4*>(cs);
+          const float4 s4 = *reinterpret_cast<const float4*>(cs + 64);
+          const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+          float o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p = __shfl_xor_sync(0xffffffffu, x[e], 16);
+            o[e] = d0 < 64 ? x[e] * cv[e] - p * sv[e] : x[e] * cv[e] + p * sv[e];
+          }
+          if (is_q) {
+            __nv_bfloat16 q[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) q[e] = f2bf(o[e]);
+            *reinterpret_cast<uint2*>(rk.q_out + (m * rk.H + head) * 128 + d0) = *reinterpret_cast<const uint2*>(q);
+          } else if (slot_ok) {
+            const int kvh = head - rk.H;
+            float kb[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) kb[e] = bf2f(f2bf(o[e]));
+            const size_t idx = ((size_t)((slot >> 4) * rk.KVH + kvh) * 16 + (slot & 15)) * 128 + d0;
+            store4_kv(rk.k_cache, rk.kv_fp8, idx, kb, rk.k_scale ? 1.f / rk.k_scale[kvh] : 1.f);
+          }
+        } else if (slot_ok) {
+          const int kvh = head - rk.H - rk.KVH;
+          const size_t idx = ((size_t)((slot >> 4) * rk.KVH + kvh) * 16 + (slot & 15)) * 128 + d0;
+          store4_kv(rk.v_cache, rk.kv_fp8, idx, x, rk.v_scale ? 1.f / rk.v_scale[kvh] : 1.f);
+        }
+        continue;
+      }
       if constexpr (MODE == kModeRS) {
         // fp32 partial row m -> inbox slot [parity][this rank][row] of its owner rank
         const int rpr = coll.comm.rows_per_rank;
@@ -697,6 +789,57 @@ void b200_gemm_set_trace(unsigned long long* buf) { g_gemm_trace = buf; }
 // [4][nkb] = {raw/weights landed, operand ready (dequantised), MMA issued, activation landed}.
 static unsigned long long* g_gemm_ktrace = nullptr;
 void b200_gemm_set_ktrace(unsigned long long* buf) { g_gemm_ktrace = buf; }
+
+// q|k|v projection with the qk-norm + RoPE + paged K/V append fused into the
+// epilogue (kEpiQKRope): head dim 128, full non-interleaved rotary, N =
+// (H + 2 KVH) * 128. Writes q_out [M, H, 128] and the K/V cache slots of the
+// tokens; no projection output. Same K partition and reduction order as
+// b200_gemm_bf16 for this (N, K). Returns 0, a CUDA error code, or -1.
+int b200_gemm_qkv_rope(const void* X, int M, int K, int ldx, const void* W, int N, int ldw, const void* bias,
+                       const int* positions, const int64_t* slots, const float* cos_sin, const void* qw,
+                       const void* kw, float eps, void* q_out, void* k_cache, void* v_cache, int kv_fp8,
+                       const float* k_scale, const float* v_scale, int H, int KVH, int64_t num_slots, int num_sms,
+                       int force_splits, cudaStream_t stream) {
+  if (M <= 0) return 0;
+  if (N != (H + 2 * KVH) * 128 || !positions || !cos_sin || !q_out) return -1;
+  if ((K % 8) || (ldx % 8) || (ldw % 8) || ((uintptr_t)X & 15) || ((uintptr_t)W & 15) || ((uintptr_t)q_out & 7))
+    return -1;
+  const int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
+  if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
+  GemmArgs a = {};
+  a.Y = nullptr;
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.epi = kEpiQKRope;
+  a.trace = g_gemm_trace;
+  a.ktrace = g_gemm_ktrace;
+  a.rk.positions = positions;
+  a.rk.slots = slots;
+  a.rk.cos_sin = cos_sin;
+  a.rk.qw = reinterpret_cast<const __nv_bfloat16*>(qw);
+  a.rk.kw = reinterpret_cast<const __nv_bfloat16*>(kw);
+  a.rk.q_out = reinterpret_cast<__nv_bfloat16*>(q_out);
+  a.rk.k_cache = k_cache;
+  a.rk.v_cache = v_cache;
+  a.rk.k_scale = k_scale;
+  a.rk.v_scale = v_scale;
+  a.rk.num_slots = k_cache ? num_slots : 0;
+  a.rk.eps = eps;
+  a.rk.H = H;
+  a.rk.KVH = KVH;
+  a.rk.kv_fp8 = kv_fp8;
+  a.kb_total = (K + 63) / 64;
+  const int s = force_splits > 0 ? force_splits : choose_splits(N, K, num_sms);
+  if (s > 8) return -1;
+  a.kb_per_split = (a.kb_total + s - 1) / s;
+  a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  const int tiles_n = N / 128, tiles_m = (M + BN - 1) / BN;
+  return launch_bn<kModeLocal>(BN, tw, tx, a, local_coll(), tiles_n, tiles_m, stream);
+}
 
 int b200_gemm_num_splits(int M, int N, int K, int num_sms) {
   (void)M;

@@ -156,6 +156,7 @@ struct SampleArgs {
   int* out_tokens;           // [B]
   int* out_tokens2;          // optional second destination (next step's input ids)
   float* out_logit;          // optional [B] value of the chosen logit (raw)
+  int* flags;                // optional [B]: 1 when the row holds a NaN or +-inf logit
 };
 
 __device__ __forceinline__ void block_argmax(float& v, int& idx, float* sv, int* si) {
@@ -204,21 +205,47 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   __shared__ float sv[32];
   __shared__ int si[32];
   __shared__ unsigned long long hist[256];
+  // per-warp private histograms [kThreads / 32][256] (dynamic shared memory):
+  // with near-uniform logits almost every key of a radix pass falls into one
+  // or two bins, and one block-wide histogram would serialise every thread's
+  // atomic on those bins; integer sums keep the result order-independent
+  extern __shared__ unsigned long long whist[];
+  const int hw = threadIdx.x >> 5;
+  auto hist_zero = [&]() {
+    for (int i = threadIdx.x; i < (kThreads / 32) * 256; i += blockDim.x) whist[i] = 0;
+    __syncthreads();
+  };
+  auto hist_collect = [&]() {  // after the adds: hist[bin] = sum over warps
+    __syncthreads();
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+      unsigned long long t = 0;
+      for (int w = 0; w < kThreads / 32; ++w) t += whist[w * 256 + i];
+      hist[i] = t;
+    }
+    __syncthreads();
+  };
   __shared__ uint32_t s_prefix;
   __shared__ unsigned long long s_rem;
   const int b = blockIdx.x;
   const float* lg = a.logits + (size_t)b * a.ld;
   const float T = a.temperature[b];
 
-  // greedy / max pass (argmax of raw logits also gives the softmax max)
+  // greedy / max pass (argmax of raw logits also gives the softmax max), and
+  // the non-finite check (|x| <= FLT_MAX is false exactly for NaN and +-inf)
   float bv = -INFINITY;
   int bi = 0x7fffffff;
+  bool bad = false;
   for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
     const float x = lg[i];
+    bad |= !(fabsf(x) <= FLT_MAX);
     if (x > bv) {
       bv = x;
       bi = i;
     }
+  }
+  if (a.flags) {
+    const int any_bad = __syncthreads_or(bad ? 1 : 0);
+    if (threadIdx.x == 0) a.flags[b] = any_bad;
   }
   block_argmax(bv, bi, sv, si);
   if (T <= 0.f || bv == -INFINITY) {
@@ -241,14 +268,13 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     unsigned long long rem = (unsigned long long)k;
     for (int pass = 0; pass < 4; ++pass) {
       const int shift = 24 - 8 * pass;
-      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
-      __syncthreads();
+      hist_zero();
       const uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
       for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
         const uint32_t key = fkey(lg[i] * invT);
-        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1ull);
+        if ((key & pmask) == prefix) atomicAdd(&whist[hw * 256 + ((key >> shift) & 255u)], 1ull);
       }
-      __syncthreads();
+      hist_collect();
       if (threadIdx.x == 0) {
         unsigned long long cum = 0;
         int d = 255;
@@ -296,17 +322,16 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     unsigned long long rem = target > 0 ? target : 1;
     for (int pass = 0; pass < 4; ++pass) {
       const int shift = 24 - 8 * pass;
-      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
-      __syncthreads();
+      hist_zero();
       const uint32_t pmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
       for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
         const float s = lg[i] * invT;
         const uint32_t key = fkey(s);
         if (key >= thr && (key & pmask) == prefix)
-          atomicAdd(&hist[(key >> shift) & 255u],
+          atomicAdd(&whist[hw * 256 + ((key >> shift) & 255u)],
                     (unsigned long long)__float2uint_rn(exp2f((s - mx) * 1.4426950408889634f) * 1073741824.f));
       }
-      __syncthreads();
+      hist_collect();
       if (threadIdx.x == 0) {
         unsigned long long cum = 0;
         int d = 255;
@@ -463,11 +488,14 @@ b200::launch_k(  logits_process_kernel, dim3(B), dim3(kThreads), smem, st, 1, a)
 
 int b200_sample(const float* logits, int64_t ld, int B, int V, const float* temperature, const int* top_k,
                 const float* top_p, const float* min_p, const uint64_t* keys, const int64_t* steps, int* out_tokens,
-                int* out_tokens2, float* out_logit, cudaStream_t st) {
+                int* out_tokens2, float* out_logit, int* flags, cudaStream_t st) {
   if (B <= 0) return 0;
-  SampleArgs a{logits, ld, V, temperature, top_k, top_p, min_p, keys, steps, out_tokens, out_tokens2, out_logit};
-b200::launch_k(  sample_kernel, dim3(B), dim3(kThreads), 0, st, 1, a);
-  return (int)cudaGetLastError();
+  SampleArgs a{logits, ld, V, temperature, top_k, top_p, min_p, keys, steps, out_tokens, out_tokens2, out_logit,
+               flags};
+  constexpr int smem = (kThreads / 32) * 256 * (int)sizeof(unsigned long long);
+  if (int r = b200::smem_attr_once<sample_kernel>(smem)) return r;
+  cudaError_t e = b200::launch_k(sample_kernel, dim3(B), dim3(kThreads), smem, st, 1, a);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 // Greedy token, its softmax probability (the confidence of mask-diffusion

@@ -462,9 +462,14 @@ class EngineV2:
         return toks, lp
 
     def _row_needs_eager(self, st) -> bool:
+        """Rows the captured decode graphs cannot serve: logit processing
+        (bias, penalties), token masks (grammar, reasoning budget), logprobs,
+        adapters. Plain temperature / top-k / top-p / min-p sampling runs in
+        the sampled graph variant when the model supports it."""
         sp = st.req.sampling
-        return (not sp.greedy or st.req.token_constraint is not None or sp.logprobs or sp.top_logprobs > 0
-                or sp.needs_processing or st.req.lora is not None or "budget" in st.extra)
+        sampled_ok = self.graphs is not None and getattr(self.graphs, "sampling", False)
+        return ((not sp.greedy and not sampled_ok) or st.req.token_constraint is not None or sp.logprobs
+                or sp.top_logprobs > 0 or sp.needs_processing or st.req.lora is not None or "budget" in st.extra)
 
     def _finalize_inflight(self, inflight) -> list[Event]:
         plan, handle = inflight
@@ -678,6 +683,7 @@ class EngineV2:
         or the exit waits on them."""
         if self.graphs is not None and hasattr(self.graphs, "graphs"):
             self.graphs.graphs.clear()
+            getattr(self.graphs, "sgraphs", {}).clear()
             self.graphs.pool = None
         if self.device.type == "cuda":
             import gc

@@ -18,7 +18,8 @@ import torch
 from .. import ops
 from ..models.batch import ForwardBatch
 from ..ops import _lib
-from ..ops.attention import SCRATCH, decode_max_parts
+from ..ops.attention import SCRATCH, decode_max_parts, merge_counters
+from .sampler import row_key
 
 PENDING = -1
 
@@ -42,12 +43,17 @@ class DecodeGraphRunner:
         self.maxp = engine.max_pages
         self.max_parts = decode_max_parts(engine.cfg.max_model_len)
         B, P = self.Bmax, self.maxp
-        # packed int32 layout: pos | seq_lens | src | host_ids | page_table | slots(int64) | state slots
+        # packed int32 layout: pos | seq_lens | src | host_ids | page_table | slots(int64) | state slots |
+        # sampling: rng keys (int64) | rng steps (int64) | temperature f32 | top_k | top_p f32 | min_p f32
         self.o_pos, self.o_sl, self.o_src, self.o_hid, self.o_pt = 0, B, 2 * B, 3 * B, 4 * B
         self.o_slots = 4 * B + B * P
         self.o_slots += self.o_slots % 2
         self.o_ss = self.o_slots + 2 * B
-        self.n_i32 = self.o_ss + B
+        self.o_key = self.o_ss + B + (self.o_ss + B) % 2
+        self.o_step = self.o_key + 2 * B
+        self.o_temp = self.o_step + 2 * B
+        self.o_topk, self.o_topp, self.o_minp = self.o_temp + B, self.o_temp + 2 * B, self.o_temp + 3 * B
+        self.n_i32 = self.o_temp + 4 * B
         self.rec = engine.kv.rec
         self.packed = torch.zeros(self.n_i32, dtype=torch.int32, device=self.dev)
         self.staging = [torch.zeros(self.n_i32, dtype=torch.int32).pin_memory() for _ in range(2)]
@@ -60,6 +66,16 @@ class DecodeGraphRunner:
         self.pt = self.packed[self.o_pt:self.o_pt + B * P].view(B, P)
         self.slots = self.packed[self.o_slots:self.o_slots + 2 * B].view(torch.int64)
         self.ss = self.packed[self.o_ss:self.o_ss + B]
+        self.s_key = self.packed[self.o_key:self.o_key + 2 * B].view(torch.int64)
+        self.s_step = self.packed[self.o_step:self.o_step + 2 * B].view(torch.int64)
+        self.s_temp = self.packed[self.o_temp:self.o_temp + B].view(torch.float32)
+        self.s_topk = self.packed[self.o_topk:self.o_topk + B]
+        self.s_topp = self.packed[self.o_topp:self.o_topp + B].view(torch.float32)
+        self.s_minp = self.packed[self.o_minp:self.o_minp + B].view(torch.float32)
+        # sampled rows (temperature / top-k / top-p / min-p) run a second graph per bucket
+        # whose last kernel draws from the logits instead of taking the argmax
+        self.sampling = self._supports_sampling()
+        self.sgraphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.ids = torch.zeros(B, dtype=torch.int32, device=self.dev)
         self.out = torch.zeros(B, dtype=torch.int32, device=self.dev)
         # non-finite-logit flag per row, read back with the tokens
@@ -84,6 +100,7 @@ class DecodeGraphRunner:
         m = self.model
         SCRATCH.get(self.dev, "dec_acc", self.Bmax * m.H * self.max_parts * m.D)
         SCRATCH.get(self.dev, "dec_ml", self.Bmax * m.H * self.max_parts * 2)
+        merge_counters(self.dev, self.Bmax * max(m.KVH, 1))
         ops.WORKSPACE.reserve(self.dev, 512 << 20)
         self._reserved = True
 
@@ -92,10 +109,22 @@ class DecodeGraphRunner:
                             dec_page_table=self.pt[:B], dec_seq_lens=self.sl[:B], dec_max_parts=self.max_parts,
                             state_slots=self.ss[:B] if self.rec is not None else None)
 
-    def _body(self, B):
-        self.model.forward_decode_tokens(self._fb(B), self.eng.kv, self.out[:B], flags=self.flags[:B])
+    def _supports_sampling(self) -> bool:
+        """Sampled graphs need the full logits on every rank: not the fused TP
+        path (vocab-split head), not row-split data-parallel models."""
+        m = self.model
+        return (self.dp <= 1 and getattr(m, "tp_fused", None) is None and getattr(m, "pp_stages", 1) == 1
+                and getattr(m, "graph_sampling", True))
 
-    def capture(self, B):
+    def _body(self, B, sampled=False):
+        if not sampled:
+            self.model.forward_decode_tokens(self._fb(B), self.eng.kv, self.out[:B], flags=self.flags[:B])
+            return
+        logits = self.model.forward(self._fb(B), self.eng.kv)
+        ops.sample(logits, self.s_temp[:B], self.s_topk[:B], self.s_topp[:B], self.s_minp[:B], self.s_key[:B],
+                   self.s_step[:B], out=self.out[:B], flags=self.flags[:B])
+
+    def capture(self, B, sampled=False):
         self._reserve()
         # inert inputs for warm-up: no KV writes, empty contexts, scratch recurrent state
         if self.rec is not None:
@@ -104,24 +133,25 @@ class DecodeGraphRunner:
         self.sl.zero_()
         self.pos.zero_()
         self.ids.zero_()
+        self.s_temp.zero_()
         cur = torch.cuda.current_stream(self.dev)
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(cur)
         with torch.cuda.stream(s):
             for _ in range(2):
                 self.model.begin_step()
-                self._body(B)
+                self._body(B, sampled)
         cur.wait_stream(s)
         torch.cuda.synchronize(self.dev)
         n0 = _lib.launch_counter[0]
         g = torch.cuda.CUDAGraph()
         self.model.begin_step()  # the capture itself does not run; every replay advances the step first
         with torch.cuda.graph(g, pool=self.pool):
-            self._body(B)
-        self.launches_per_replay[B] = _lib.launch_counter[0] - n0
+            self._body(B, sampled)
+        self.launches_per_replay[("s", B) if sampled else B] = _lib.launch_counter[0] - n0
         if self.pool is None:
             self.pool = g.pool()
-        self.graphs[B] = g
+        (self.sgraphs if sampled else self.graphs)[B] = g
         torch.cuda.synchronize(self.dev)
 
     def capture_all(self):
@@ -171,11 +201,13 @@ class DecodeGraphRunner:
         rows = plan.rows
         n = len(rows)
         Bb, where = self.layout(plan)
-        if Bb not in self.graphs:
+        sampled = any(not r.state.req.sampling.greedy for r in rows)
+        graphs = self.sgraphs if sampled else self.graphs
+        if Bb not in graphs:
             # capture's warm-up overwrites the shared output buffer, which may hold
             # the in-flight step's tokens that this launch gathers from
             saved = self.out.clone()
-            self.capture(Bb)
+            self.capture(Bb, sampled)
             self.out.copy_(saved)
         k = self.slot_k
         self.slot_k ^= 1
@@ -194,6 +226,14 @@ class DecodeGraphRunner:
         if self.rec is not None:
             a[self.o_ss:self.o_ss + Bb] = self.rec.scratch
         pt = a[self.o_pt:self.o_pt + self.Bmax * P].reshape(self.Bmax, P)
+        if sampled:
+            keys = a[self.o_key:self.o_key + 2 * self.Bmax].view(np.uint64)
+            steps = a[self.o_step:self.o_step + 2 * self.Bmax].view(np.int64)
+            temp = a[self.o_temp:self.o_temp + self.Bmax].view(np.float32)
+            topk = a[self.o_topk:self.o_topk + self.Bmax]
+            topp = a[self.o_topp:self.o_topp + self.Bmax].view(np.float32)
+            minp = a[self.o_minp:self.o_minp + self.Bmax].view(np.float32)
+            temp[:Bb] = 0.0
         prev_idx = {}
         if chained_from is not None:
             prev_where = chained_from[1][3]
@@ -211,6 +251,16 @@ class DecodeGraphRunner:
                 a[self.o_ss + i] = st.seq.state_slot
             pg = st.seq.pages
             pt[i, :len(pg)] = pg
+            if sampled:
+                sp = st.req.sampling
+                keys[i] = row_key(st)
+                # the Philox counter is the index of the token being drawn: accepted
+                # tokens plus the in-flight step's placeholder, as the eager sampler counts
+                steps[i] = st.gen_step + (1 if st.all_tokens[-1] == PENDING else 0)
+                temp[i] = sp.temperature if not sp.greedy else 0.0
+                topk[i] = sp.top_k
+                topp[i] = sp.top_p
+                minp[i] = sp.min_p
             tok = st.all_tokens[p]
             if tok == PENDING:
                 a[self.o_src + i] = prev_idx[id(st)]
@@ -230,8 +280,8 @@ class DecodeGraphRunner:
                                             self.ids.data_ptr(), Bb, _lib.stream_ptr(self.dev)), "gather_tokens")
             _lib.count(1)
         self.model.begin_step()
-        self.graphs[Bb].replay()
-        _lib.count(self.launches_per_replay.get(Bb, 0))
+        graphs[Bb].replay()
+        _lib.count(self.launches_per_replay.get(("s", Bb) if sampled else Bb, 0))
         ko = self.out_k
         self.out_k = (self.out_k + 1) % len(self.host_out)
         m = max(where) + 1 if where else 0

@@ -18,6 +18,7 @@ is :class:`DecoderLM`'s ``new_cache`` / ``forward_dense`` / ``forward``.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -409,6 +410,10 @@ class DecoderLM:
         pipeline stages after the first); `return_residual` returns the
         residual stream of every token after the last layer instead (pipeline
         stages before the last)."""
+        with ops.row_roles(fb.num_tokens, fb.num_decode):
+            return self._forward(fb, kv, return_hidden, inputs_embeds, return_both, return_residual)
+
+    def _forward(self, fb, kv, return_hidden, inputs_embeds, return_both, return_residual):
         cfg = self.cfg
         T = fb.num_tokens
         nd = fb.num_decode
@@ -444,15 +449,20 @@ class DecoderLM:
         cfg = self.cfg
         T, nd = fb.num_tokens, fb.num_decode
         ki = self.kv_index[li] if self.kv_index else li
-        qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
         kc, vc = kv.layer(ki)
         cos_sin, positions = self.cos_sin, fb.positions
         if fb.rope_table is not None:  # per-token rotary rows (M-RoPE prompts)
             cos_sin = fb.rope_table
             positions = torch.arange(T, dtype=torch.int32, device=fb.positions.device)
-        q = ops.qk_norm_rope_kv(qkv, positions, fb.slots, cos_sin, self.rot_dim, cfg.rope_interleaved,
-                                L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
-                                kv.k_scale(ki), kv.v_scale(ki))
+        qkv = None
+        if self._fused_qkv_rope(L, h, fb):
+            q = ops.gemm_qkv_rope(h, L.wqkv, L.bqkv, positions, fb.slots, cos_sin, L.q_norm, L.k_norm,
+                                  cfg.rms_norm_eps, kc, vc, self.H, self.KVH, kv.k_scale(ki), kv.v_scale(ki))
+        else:
+            qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
+            q = ops.qk_norm_rope_kv(qkv, positions, fb.slots, cos_sin, self.rot_dim, cfg.rope_interleaved,
+                                    L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
+                                    kv.k_scale(ki), kv.v_scale(ki))
         q = self._pos_scale_q(q, fb.positions)
         win = cfg.window(li)
         if nd:
@@ -471,6 +481,18 @@ class DecoderLM:
             g0 = (self.H + 2 * self.KVH) * self.D
             a2 = sigmoid_mul(a2, qkv[:, g0:g0 + self.H * self.D])
         return self._attn_out(L, a2)
+
+    # class switch: qkv GEMM with the qk-norm / RoPE / KV append epilogue where it applies
+    fused_qkv_rope = os.environ.get("B200LM_FUSED_QKV_ROPE", "1") != "0"
+
+    def _fused_qkv_rope(self, L, h, fb) -> bool:
+        """The fused epilogue covers head dim 128 with full non-interleaved
+        rotary from the position table, bf16 weights, no output gate rows."""
+        cfg = self.cfg
+        return (self.fused_qkv_rope and h.is_cuda and self.D == 128 and self.rot_dim == 128
+                and not cfg.rope_interleaved and not cfg.attn_output_gate and fb.rope_table is None
+                and isinstance(L.wqkv, torch.Tensor) and L.wqkv.dtype == torch.bfloat16
+                and self.cos_sin.shape[-1] == 128)
 
     def _norm(self, x, delta, w, b=None):
         """x <- x + delta; the block's input norm (RMSNorm, or LayerNorm with bias)."""

@@ -29,6 +29,8 @@ sz = C.c_size_t
 # name -> (restype, argtypes)
 _SIGS = {
     "b200_gemm_bf16": (i32, [vp, i32, i32, i32, vp, i32, i32, vp, i32, vp, i32, vp, i32, i32, i32, vp]),
+    "b200_gemm_qkv_rope": (i32, [vp, i32, i32, i32, vp, i32, i32, vp, vp, vp, vp, vp, vp, f32, vp, vp, vp, i32, vp, vp,
+                                 i32, i32, i64, i32, i32, vp]),
     "b200_gemm_num_splits": (i32, [i32, i32, i32, i32]),
     "b200_gemm_q": (i32, [vp, i32, i32, i32, vp, i32, i32, i32, vp, i32, vp, i32, vp, i32, i32, i32, vp]),
     "b200_gemm_q_num_splits": (i32, [i32, i32, i32]),
@@ -49,7 +51,7 @@ _SIGS = {
     "b200_prefill_simt_q_tile": (i32, [i32]),
     "b200_logits_process": (i32, [vp, i64, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp, vp, vp, i32, vp, vp, vp,
                                   i32, vp, vp]),
-    "b200_sample": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "b200_sample": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "b200_argmax": (i32, [vp, i64, i32, i32, vp, vp, vp, vp]),
     "b200_argmax_conf": (i32, [vp, i64, i32, i32, vp, vp, vp, vp, i32, vp]),
     "b200_logprobs": (i32, [vp, i64, i32, i32, vp, i32, vp, vp, vp, vp]),
@@ -57,6 +59,8 @@ _SIGS = {
     "b200_gather_tokens": (i32, [vp, vp, vp, vp, i32, vp]),
     "b200_paged_decode_mma_part": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, f32,
                                          i64, vp]),
+    "b200_paged_decode_mma": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, f32,
+                                    i64, vp]),
     "b200_paged_decode_merge": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "b200_set_pdl": (None, [i32]),
     "b200_get_pdl": (i32, []),

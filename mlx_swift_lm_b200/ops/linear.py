@@ -1,6 +1,8 @@
 """Dense GEMM entry points (tcgen05 kernel on CUDA, fp32 oracle on CPU)."""
 from __future__ import annotations
 
+import threading
+
 import torch
 
 from . import _lib
@@ -11,6 +13,39 @@ _EPI = {"none": 0, "swiglu": 1, "f32": 2, "add": 3, "geglu": 4, "swiglu_oai": 5,
         "relu2": 9}
 _GLU = ("swiglu", "geglu", "swiglu_oai")
 _SMS: dict[int, int] = {}
+
+# Row roles of the step being run: (T, nd) = the step's token count and how many
+# leading rows are decode rows. GEMMs over exactly T rows then run the decode
+# rows with the (N, K)-chosen split-K and the prefill rows with no split (one
+# 128 x 256 tile per CTA over the whole K range). Each token's arithmetic depends
+# only on its role, never on the batch, so batch-composition invariance holds,
+# and prefill GEMMs are not chopped into 8 K-slices reduced over the cluster.
+_ROLES = threading.local()
+
+
+class row_roles:
+    """Context: the current step has `T` tokens, the first `nd` of them decode rows."""
+
+    def __init__(self, T: int, nd: int):
+        self.v = (int(T), int(nd))
+
+    def __enter__(self):
+        self.prev = getattr(_ROLES, "v", None)
+        _ROLES.v = self.v
+        return self
+
+    def __exit__(self, *exc):
+        _ROLES.v = self.prev
+        return False
+
+
+def _split_rows(x: torch.Tensor):
+    """(nd, T) when x holds the current step's rows and both roles are present,
+    (0, T) for an all-prefill step, else None (default split rule)."""
+    v = getattr(_ROLES, "v", None)
+    if v is None or x.shape[0] != v[0] or v[1] >= v[0]:
+        return None
+    return v[1], v[0]
 
 
 def num_sms(device: torch.device) -> int:
@@ -50,6 +85,14 @@ def gemm(x: torch.Tensor, w: torch.Tensor, epi: str = "none", residual: torch.Te
     n_out = N // 2 if epi in _GLU else N
     if out is None:
         out = torch.empty((M, n_out), dtype=torch.float32 if epi == "f32" else torch.bfloat16, device=x.device)
+    roles = _split_rows(x) if splits == 0 else None
+    if roles is not None:
+        nd, T = roles
+        r = residual
+        if nd:
+            gemm(x[:nd], w, epi, r[:nd] if r is not None else None, out[:nd], bias, 0)
+        gemm(x[nd:], w, epi, r[nd:] if r is not None else None, out[nd:], bias, 1)
+        return out
     rc = _lib.lib().b200_gemm_bf16(x.data_ptr(), M, K, x.stride(0), w.data_ptr(), N, w.stride(0), out.data_ptr(),
                                    out.stride(0), _lib.ptr(residual),
                                    residual.stride(0) if residual is not None else 0, _lib.ptr(bias), _EPI[epi],
@@ -79,6 +122,14 @@ def gemm_q(x: torch.Tensor, w: QuantizedWeight, epi: str = "none", residual: tor
     n_out = N // 2 if epi in _GLU else N
     if out is None:
         out = torch.empty((M, n_out), dtype=torch.float32 if epi == "f32" else torch.bfloat16, device=x.device)
+    roles = _split_rows(x) if splits == 0 else None
+    if roles is not None:
+        nd, T = roles
+        r = residual
+        if nd:
+            gemm_q(x[:nd], w, epi, r[:nd] if r is not None else None, out[:nd], bias, 0)
+        gemm_q(x[nd:], w, epi, r[nd:] if r is not None else None, out[nd:], bias, 1)
+        return out
     rc = _lib.lib().b200_gemm_q(x.data_ptr(), M, K, x.stride(0), w.tiled().data_ptr(), N, w.kernel_bits, w.gs,
                                 out.data_ptr(), out.stride(0),
                                 _lib.ptr(residual), residual.stride(0) if residual is not None else 0,
@@ -98,3 +149,40 @@ class _NoWorkspace:
 
 
 WORKSPACE = _NoWorkspace()
+
+
+def gemm_qkv_rope(x: torch.Tensor, w: torch.Tensor, bias, positions, slots, cos_sin, q_norm, k_norm, eps: float,
+                  k_cache, v_cache, H: int, KVH: int, k_scale=None, v_scale=None, q_out=None,
+                  splits: int = 0) -> torch.Tensor:
+    """q|k|v projection with qk-norm + RoPE + paged K/V append in the GEMM
+    epilogue (head dim 128, full non-interleaved rotary): returns q [M, H, 128]
+    and writes the tokens' K/V into the cache at `slots`. Same result as
+    ``gemm`` followed by ``qk_norm_rope_kv``, without the projection's round
+    trip through memory and without the separate launch."""
+    M, K = x.shape
+    N = w.shape[0]
+    assert N == (H + 2 * KVH) * 128 and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if bias is not None and bias.dtype != x.dtype:
+        bias = bias.to(x.dtype)
+    if q_out is None:
+        q_out = torch.empty((M, H, 128), dtype=torch.bfloat16, device=x.device)
+    fp8 = k_cache is not None and k_cache.dtype == torch.float8_e4m3fn
+    num_slots = k_cache.shape[0] * 16 if k_cache is not None else 0
+    roles = _split_rows(x) if splits == 0 else None
+    if roles is not None:
+        nd, T = roles
+        parts = ((0, nd, 0), (nd, T, 1)) if nd else ((0, T, 1),)
+    else:
+        parts = ((0, M, splits),)
+    for lo, hi, sp in parts:
+        rc = _lib.lib().b200_gemm_qkv_rope(
+            x[lo:hi].data_ptr(), hi - lo, K, x.stride(0), w.data_ptr(), N, w.stride(0), _lib.ptr(bias),
+            positions[lo:hi].data_ptr(), _lib.ptr(slots[lo:hi] if slots is not None else None), cos_sin.data_ptr(),
+            _lib.ptr(q_norm), _lib.ptr(k_norm), float(eps), q_out[lo:hi].data_ptr(), _lib.ptr(k_cache),
+            _lib.ptr(v_cache), 1 if fp8 else 0, _lib.ptr(k_scale), _lib.ptr(v_scale), H, KVH, num_slots,
+            num_sms(x.device), sp, _lib.stream_ptr(x.device))
+        _lib.check(rc, f"gemm_qkv_rope M={hi - lo} N={N} K={K}")
+        _lib.count(1)
+    return q_out

@@ -79,14 +79,15 @@ def process_logits(logits, bias_ids=None, bias_vals=None, n_bias=None, rep_ids=N
     return logits
 
 
-def sample(logits, temperature, top_k, top_p, min_p, keys, steps, out=None, out2=None, out_logit=None):
-    """Per-row temperature / top-k / top-p / min-p + Gumbel-max draw (CUDA)."""
+def sample(logits, temperature, top_k, top_p, min_p, keys, steps, out=None, out2=None, out_logit=None, flags=None):
+    """Per-row temperature / top-k / top-p / min-p + Gumbel-max draw (CUDA);
+    `flags` (int32 [B]) receives the rows' non-finite-logit flags."""
     B, V = logits.shape
     if out is None:
         out = torch.empty(B, dtype=torch.int32, device=logits.device)
     rc = _lib.lib().b200_sample(logits.data_ptr(), logits.stride(0), B, V, temperature.data_ptr(), top_k.data_ptr(),
                                 top_p.data_ptr(), min_p.data_ptr(), keys.data_ptr(), steps.data_ptr(), out.data_ptr(),
-                                _lib.ptr(out2), _lib.ptr(out_logit), _lib.stream_ptr(logits.device))
+                                _lib.ptr(out2), _lib.ptr(out_logit), _lib.ptr(flags), _lib.stream_ptr(logits.device))
     _lib.check(rc, "sample")
     _lib.count(1)
     return out

@@ -91,3 +91,27 @@ def test_seeded_sampling_gpu_matches_cpu_rule():
     s2 = [e2.submit(Request(prompt_tokens=ps[0], max_tokens=12, sampling=sp, id=900))]
     e2.run_until_idle()
     assert s1[0].tokens() == s2[0].tokens()
+
+
+def test_graph_sampled_decode_matches_eager():
+    """Temperature / top-k / top-p / min-p rows run the sampled decode graph
+    (chained); under the same seeds they draw exactly the tokens the eager
+    sampler draws, mixed with greedy rows in the same batch."""
+    m = _model(seed=4, std=0.3)
+    ps = _prompts(m.cfg.vocab_size, (12, 40, 7, 90), seed=5)
+    sps = [SamplingParams(temperature=0.8, top_p=0.9, seed=11), SamplingParams(temperature=0.0),
+           SamplingParams(temperature=1.2, top_k=50, seed=12), SamplingParams(temperature=0.7, min_p=0.05, seed=13)]
+
+    def run(graphs, chained=True):
+        eng = _eng(m, graphs=graphs, chained=chained)
+        # the RNG key mixes the seed with the request id: pin the ids
+        ss = [eng.submit(Request(prompt_tokens=p, max_tokens=30, sampling=sp, id=9000 + i))
+              for i, (p, sp) in enumerate(zip(ps, sps))]
+        eng.run_until_idle()
+        return [s.tokens() for s in ss], eng
+
+    eager, _ = run(False)
+    graph, eng = run(True)
+    assert eng.graphs.sgraphs, "sampled rows did not use a sampled graph"
+    assert graph == eager
+    assert run(True, chained=False)[0] == eager

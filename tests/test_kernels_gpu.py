@@ -5,6 +5,7 @@ import pytest
 import torch
 
 from mlx_swift_lm_b200 import ops
+from mlx_swift_lm_b200.ops import _lib
 from mlx_swift_lm_b200.ops import reference as ref
 
 pytestmark = pytest.mark.gpu
@@ -318,3 +319,96 @@ def test_argmax_nonfinite_flags(V):
     for r in (0, 3, 4):
         assert tok[r].item() == x[r].argmax().item()
     assert tok[2].item() == V - 1
+
+
+@pytest.mark.parametrize("M,fp8,norms,bias", [(1, False, True, False), (7, False, True, True), (64, False, True, False),
+                                              (64, True, True, False), (300, False, False, True)])
+def test_gemm_qkv_rope_matches_unfused(M, fp8, norms, bias):
+    """The qkv GEMM with the qk-norm + RoPE + K/V-append epilogue against the
+    separate GEMM and qk_norm_rope_kv kernels: same q, same cache contents
+    (at most bf16 rounding-order differences in the norm)."""
+    from mlx_swift_lm_b200.models.rope import build_rope
+
+    torch.manual_seed(M)
+    H, KVH, D, K = 8, 2, 128, 512
+    dev = torch.device("cuda")
+    N = (H + 2 * KVH) * D
+    x = (torch.randn(M, K, device=dev) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, device=dev) * 0.1).to(torch.bfloat16) if bias else None
+    qn = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16) if norms else None
+    kn = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16) if norms else None
+    cos_sin, rd = build_rope(D, 1e6, None, 4096)
+    cos_sin = cos_sin.to(dev)
+    pos = torch.randint(0, 4000, (M,), device=dev, dtype=torch.int32)
+    pages = 64
+    slots = torch.randperm(pages * 16, device=dev)[:M].to(torch.int64)
+    slots[0] = -1  # a padding row writes nothing
+    cdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    ks = (torch.rand(KVH, device=dev) + 0.5) if fp8 else None
+    vs = (torch.rand(KVH, device=dev) + 0.5) if fp8 else None
+    kc1 = torch.zeros(pages, KVH, 16, D, device=dev).to(cdt)
+    vc1, kc2, vc2 = kc1.clone(), kc1.clone(), kc1.clone()
+    qkv = ops.gemm(x, w, bias=b)
+    q1 = ops.qk_norm_rope_kv(qkv, pos, slots, cos_sin, rd, False, qn, kn, 1e-6, kc1, vc1, H, KVH, D, ks, vs)
+    q2 = ops.gemm_qkv_rope(x, w, b, pos, slots, cos_sin, qn, kn, 1e-6, kc2, vc2, H, KVH, ks, vs)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(q2.float(), q1.float(), atol=2e-2, rtol=2e-2)
+    assert (q2 == q1).float().mean() > 0.95
+    for a, c in ((kc2, kc1), (vc2, vc1)):
+        torch.testing.assert_close(a.float(), c.float(), atol=6e-2, rtol=6e-2)
+    assert _lib.read_status().get("gemm", 0) == 0
+
+
+@pytest.mark.parametrize("G,window,sinks", [(4, 0, False), (8, 300, True), (1, 0, True)])
+def test_decode_fused_merge_matches_separate_merge(G, window, sinks):
+    """Tensor-core decode with the split-KV merge fused into the partition
+    kernel (last CTA of a row merges, partition order) against the CUDA-core
+    kernel + separate merge pass: empty rows give zeros, the arrival counters
+    reset themselves (three launches in a row, different batch sizes)."""
+    from mlx_swift_lm_b200.ops import attention as att
+
+    torch.manual_seed(G)
+    KVH, D, pages = 2, 128, 400
+    H = KVH * G
+    kc = torch.randn(pages, KVH, 16, D, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(pages, KVH, 16, D, device="cuda").to(torch.bfloat16)
+    sk = torch.randn(H, device="cuda") if sinks else None
+    for B, lens in ((5, [0, 1, 257, 1000, 2047]), (3, [600, 0, 31]), (5, [0, 1, 257, 1000, 2047])):
+        q = torch.randn(B, H, D, device="cuda").to(torch.bfloat16)
+        pt = torch.randint(0, pages, (B, 128), device="cuda", dtype=torch.int32)
+        sl = torch.tensor(lens, device="cuda", dtype=torch.int32)
+        att.USE_MMA_DECODE[0] = True
+        att.USE_FUSED_MERGE[0] = True
+        try:
+            fused = ops.paged_decode(q, kc, vc, pt, sl, D ** -0.5, window, sk)
+        finally:
+            att.USE_FUSED_MERGE[0] = False
+        att.USE_MMA_DECODE[0] = False
+        try:
+            simt = ops.paged_decode(q, kc, vc, pt, sl, D ** -0.5, window, sk)
+        finally:
+            att.USE_MMA_DECODE[0] = True
+        torch.cuda.synchronize()
+        for b, n in enumerate(lens):
+            if n == 0:
+                assert (fused[b] == 0).all()
+        torch.testing.assert_close(fused.float(), simt.float(), atol=2e-2, rtol=2e-2)
+    assert int(att.merge_counters(q.device, 1)[:B * KVH].abs().sum()) == 0
+
+
+def test_gemm_row_roles_split_launch():
+    """A step of decode rows + prefill rows: the decode rows use the (N, K)
+    split, the prefill rows no split; the whole output is written and each
+    part equals the GEMM of that part run alone."""
+    torch.manual_seed(0)
+    x = (torch.randn(300, 512, device="cuda") * 0.5).to(torch.bfloat16)
+    w = (torch.randn(1024, 512, device="cuda") * 0.05).to(torch.bfloat16)
+    with ops.row_roles(300, 37):
+        y = ops.gemm(x, w)
+    y_dec = ops.gemm(x[:37], w)
+    y_pf = ops.gemm(x[37:], w, splits=1)
+    torch.cuda.synchronize()
+    assert y.shape == (300, 1024)
+    assert torch.equal(y[:37], y_dec) and torch.equal(y[37:], y_pf)
+    torch.testing.assert_close(y.float(), x.float() @ w.float().T, atol=3e-2, rtol=3e-2)
