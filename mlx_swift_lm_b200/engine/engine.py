@@ -58,6 +58,7 @@ class EngineConfig:
     clock: object = None  # injectable monotonic clock (tests)
     # (open_id, close_id[, starts_inside]) thought markers for integer Request.reasoning_budget values
     reasoning_markers: tuple | None = None
+    admission: object = None  # engine.admission.AdmissionConfig (watermark, auxiliary bytes); None = defaults
 
 
 class RequestStream:
@@ -154,7 +155,13 @@ class EngineV2:
             from ..kv.prefix_cache import PrefixCache
 
             self.prefix_cache = PrefixCache(self.kv, self.cfg.prefix_block_size)
-        self.sched = Scheduler(sc, self.kv, self.prefix_cache)
+        from .admission import AdmissionConfig, AdmissionLedger, layer_kinds_for
+
+        rec_bytes = self.kv.rec.bytes_per_seq if self.kv.rec is not None else 0
+        cap = self.kv.num_pages * self.kv.page_bytes + rec_bytes * seqs
+        self.ledger = AdmissionLedger(layer_kinds_for(model, self.cfg.kv_fp8), cap,
+                                      self.cfg.admission or AdmissionConfig(fixed_bytes_per_request=rec_bytes))
+        self.sched = Scheduler(sc, self.kv, self.prefix_cache, self.ledger)
         self.sampler = Sampler(model.cfg.vocab_size, self.device)
         self.eos = set(eos_token_ids or [])
         self.states: dict[int, object] = {}
@@ -203,6 +210,10 @@ class EngineV2:
             raise ValueError("MTP rollback needs per-position recurrent states; hybrid models decode without MTP")
 
         self.mtp = MTPDriver(self, module, config)
+        # the draft module's own paged KV is per-token auxiliary memory of every request
+        mk = self.mtp.kv
+        self.ledger.cfg.auxiliary_bytes_per_token = mk.page_bytes // 16
+        self.ledger.update_capacity(self.ledger.capacity_bytes + mk.num_pages * mk.page_bytes)
         return self.mtp
 
     # ------------------------------------------------------------------ submit / cancel
@@ -709,7 +720,9 @@ class EngineV2:
                                 active_tokens=sum(s.num_computed for s in self.sched.running), steps=self.steps,
                                 last_step_ms=self.last_step_ms, decode_rows=sum(1 for s in self.sched.running
                                                                                 if s.is_decode),
-                                healthy=self.healthy)
+                                healthy=self.healthy, ledger_bytes_capacity=self.ledger.capacity_bytes,
+                                ledger_bytes_reserved=self.ledger.reserved_bytes + self.ledger.snapshot().external_bytes,
+                                admission_watermark_bytes=self.ledger.watermark_bytes)
 
     # ------------------------------------------------------------------ convenience
     def generate(self, prompts: list[list[int]], max_tokens: int = 64, sampling=None, **kw) -> list[list[int]]:

@@ -115,10 +115,11 @@ class StepPlan:
 
 
 class Scheduler:
-    def __init__(self, cfg: SchedulerConfig, cache: PagedKVCache, prefix_cache=None):
+    def __init__(self, cfg: SchedulerConfig, cache: PagedKVCache, prefix_cache=None, ledger=None):
         self.cfg = cfg
         self.cache = cache
         self.prefix_cache = prefix_cache
+        self.ledger = ledger  # engine.admission.AdmissionLedger: byte admission with a watermark
         self.waiting: list[RequestState] = []
         self.running: list[RequestState] = []
         self._arrival = 0
@@ -145,6 +146,8 @@ class Scheduler:
         return bool(self.running) or bool(self.waiting)
 
     def can_ever_fit(self, num_tokens: int) -> bool:
+        if self.ledger is not None and not self.ledger.can_ever_fit(num_tokens):
+            return False
         return PagedKVCache.pages_for(num_tokens) <= self.cache.num_pages
 
     # ------------------------------------------------------------------ preemption
@@ -156,6 +159,8 @@ class Scheduler:
 
     def preempt(self, st: RequestState):
         st.seq.release()
+        if self.ledger is not None:
+            self.ledger.release_all(st.req.id)
         st.status = Status.WAITING
         st.timing.preemptions += 1
         if st in self.running:
@@ -165,13 +170,14 @@ class Scheduler:
     def _ensure(self, st: RequestState, total_tokens: int) -> bool:
         """Grow a row's pages; on pool exhaustion first evict unreferenced
         prefix-cache blocks, then report failure (the caller may preempt)."""
-        if st.seq.ensure(total_tokens):
-            return True
-        if self.prefix_cache is not None:
+        ok = st.seq.ensure(total_tokens)
+        if not ok and self.prefix_cache is not None:
             need = st.seq.pages_needed(total_tokens) - self.cache.pool.num_free
             if need > 0 and self.prefix_cache.evict(need) > 0:
-                return st.seq.ensure(total_tokens)
-        return False
+                ok = st.seq.ensure(total_tokens)
+        if ok and self.ledger is not None:
+            self.ledger.reserve(st.req.id, total_tokens)
+        return ok
 
     # ------------------------------------------------------------------ plan
     def plan(self) -> StepPlan:
@@ -236,6 +242,9 @@ class Scheduler:
                 n = min(st.remaining, cfg.prefill_chunk_size, pbudget)
                 if n <= 0:
                     continue
+                if self.ledger is not None and not self.ledger.has_headroom(
+                        self.ledger.admission_tokens(st.num_prompt, st.num_computed + n, st.req.max_tokens)):
+                    break  # byte ledger above the admission watermark: admit later (FCFS order kept)
                 if not self._ensure(st, st.num_computed + n):
                     if st.seq.num_tokens and st.seq.shared_prefix_pages:
                         st.seq.release()
@@ -262,6 +271,8 @@ class Scheduler:
         row.state.seq.num_tokens = row.start + row.num_tokens
 
     def finish(self, st: RequestState):
+        if self.ledger is not None:
+            self.ledger.release_all(st.req.id)
         st.status = Status.FINISHED
         if st in self.running:
             self.running.remove(st)

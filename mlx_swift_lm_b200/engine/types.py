@@ -145,6 +145,9 @@ class CapacitySnapshot:
     last_step_ms: float
     decode_rows: int
     healthy: bool
+    ledger_bytes_capacity: int = 0  # admission ledger: bytes the requests may hold
+    ledger_bytes_reserved: int = 0  # ledger charge of the live requests (soft truth)
+    admission_watermark_bytes: int = 0
 
     @property
     def kv_bytes_in_use(self) -> int:
