@@ -149,6 +149,43 @@ def reference_arm(args):
     return 0
 
 
+def receipt(dev) -> dict:
+    """Provenance of a run (the reference's bench receipts: revision stamp,
+    hardware, software): a hash of the framework's sources (the snapshot that
+    ran, with or without git), the GPU SKU, driver, CUDA / torch / NCCL
+    versions."""
+    import hashlib
+
+    import torch
+
+    h = hashlib.sha256()
+    pkg = os.path.join(ROOT, "mlx_swift_lm_b200")
+    for d, _, files in sorted(os.walk(pkg)):
+        if "_lib" in d or "__pycache__" in d:
+            continue
+        for f in sorted(files):
+            if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h")):
+                with open(os.path.join(d, f), "rb") as fh:
+                    h.update(f.encode() + fh.read())
+    with open(os.path.abspath(__file__), "rb") as fh:
+        h.update(fh.read())
+    drv = None
+    try:
+        drv = subprocess.run(["nvidia-smi", "--query-gpu=driver_version", "--format=csv,noheader"],
+                             capture_output=True, text=True, timeout=10).stdout.strip().splitlines()[0]
+    except Exception:
+        pass
+    props = torch.cuda.get_device_properties(dev)
+    nccl = None
+    try:
+        nccl = ".".join(str(x) for x in torch.cuda.nccl.version())
+    except Exception:
+        pass
+    return {"source_sha256": h.hexdigest()[:16], "gpu": props.name, "sm": f"{props.major}{props.minor}",
+            "sms": props.multi_processor_count, "hbm_gb": round(props.total_memory / 1e9, 1), "driver": drv,
+            "cuda": torch.version.cuda, "torch": torch.__version__, "nccl": nccl}
+
+
 def _release(eng, model, world):
     """Drop graphs (they may hold NCCL work), peer mappings and the model's
     memory so the next arm starts from a clean device."""
@@ -415,6 +452,7 @@ def main():
         })
         for k in ("ttft_p50_ms", "itl_p50_ms", "prefill_s", "e2e", "gpu_launches", "clocks", "mtp", "kernel_status"):
             out[k] = res[k]
+        out["receipt"] = receipt(dev)
         if base is not None:
             out["baseline"] = {"impl": "PyTorch: cuBLAS GEMMs (F.linear), SDPA over gathered pages, NCCL all_reduce, "
                                        "same engine and CUDA-graph decode",

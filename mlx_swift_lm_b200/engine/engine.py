@@ -16,6 +16,7 @@ reference's chained-decode fast path, EngineLoopV2.swift:3115-3250, 4394).
 from __future__ import annotations
 
 import collections
+import os
 import threading
 import time
 from dataclasses import dataclass, field
@@ -36,6 +37,23 @@ STREAM_CAPACITY = 256  # events buffered per request before backpressure pauses 
 
 
 NON_FINITE_MESSAGE = "non-finite logits: the model produced NaN or infinity"
+_NVTX = os.environ.get("B200LM_NVTX", "0") == "1"
+
+
+class _nvtx:
+    """NVTX range around a phase of a step (no-op unless B200LM_NVTX=1)."""
+
+    def __init__(self, name):
+        self.name = name
+
+    def __enter__(self):
+        if _NVTX:
+            torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        if _NVTX:
+            torch.cuda.nvtx.range_pop()
+        return False
 
 
 @dataclass
@@ -369,7 +387,18 @@ class EngineV2:
             return True
 
     def step(self) -> list[Event]:
-        """Run one engine step; returns the events it emitted."""
+        """Run one engine step; returns the events it emitted. With
+        B200LM_NVTX=1 every step (and its forward / finalize phases) is an
+        NVTX range, so a system profiler's timeline shows engine steps."""
+        if _NVTX and self.device.type == "cuda":
+            torch.cuda.nvtx.range_push(f"engine.step {self.steps}")
+            try:
+                return self._step()
+            finally:
+                torch.cuda.nvtx.range_pop()
+        return self._step()
+
+    def _step(self) -> list[Event]:
         with self._lock:
             t0 = time.perf_counter()
             self._step_started = t0
@@ -404,7 +433,8 @@ class EngineV2:
                 if self.mtp is not None:
                     for r in plan.rows:
                         self.mtp.drop(r.state)  # history broken: MTP restarts after an eager step
-                handle = self.graphs.launch(plan, chained_from=prev)
+                with _nvtx("decode_graph"):
+                    handle = self.graphs.launch(plan, chained_from=prev)
                 for r in plan.rows:
                     self.sched.commit(r)
                     r.state.all_tokens.append(PENDING)
@@ -422,10 +452,11 @@ class EngineV2:
                 fb = self._build_batch(plan, self.device)
                 hid = None
                 dtok = self.diagnostics.begin_forward(self.device) if self.diagnostics is not None else None
-                if self.mtp is not None:
-                    logits, hid = self.model.forward(fb, self.kv, return_both=True)
-                else:
-                    logits = self.model.forward(fb, self.kv)
+                with _nvtx("forward"):
+                    if self.mtp is not None:
+                        logits, hid = self.model.forward(fb, self.kv, return_both=True)
+                    else:
+                        logits = self.model.forward(fb, self.kv)
                 if self.diagnostics is not None:
                     self.diagnostics.end_forward(dtok, self.steps, fb, logits)
                 srows = [r for r in plan.rows if r.sample]

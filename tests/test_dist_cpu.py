@@ -92,3 +92,31 @@ def test_collective_timeout_reports_dead_rank():
         if p.is_alive():
             p.kill()
     assert res != "no-error"
+
+
+def _max_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+
+    from mlx_swift_lm_b200.parallel.timing import max_over_ranks
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        out = max_over_ranks([1.0 + rank, 5.0 - rank], "cpu")
+        if rank == 0:
+            q.put(out)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_max_over_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_max_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = q.get(timeout=120)
+    for p in ps:
+        p.join(60)
+    assert out == [2.0, 5.0]
