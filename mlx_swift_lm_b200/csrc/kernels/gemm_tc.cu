@@ -137,14 +137,19 @@ __device__ __forceinline__ void store4_kv(void* cache, bool fp8, size_t idx, con
 // activation tile. Barriers: full[s] (activation bytes + one arrive per
 // dequantising warp + the producer's arrive), empty[s] (MMA consumed the
 // stage), rfull/rempty per raw record.
-template <int BN, int STAGES, int WQ = 0>
+// MT = 2 (bf16 weights, no split-K): two 128-row weight tiles share each
+// activation tile, with two accumulators in tensor memory (2 x BN columns):
+// a 256 x BN output tile per CTA moves half the operand bytes per FLOP of the
+// 128 x BN tile, which keeps large (prefill) GEMMs off the L2-to-SM bandwidth
+// limit.
+template <int BN, int STAGES, int WQ = 0, int MT = 1>
 struct GemmSmem {
-  static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16
+  static constexpr int kABytes = 128 * 128;  // 128 rows x 64 bf16 (one weight tile of a stage)
   static constexpr int kBBytes = BN * 128;   // BN rows x 64 bf16
   static constexpr int kCodeBytes = code_bits<WQ>() * 128 * 64 / 8;
   static constexpr int kGroupBytes = 2 * 128 * 2;  // up to 2 groups x 128 rows x bf16
   static constexpr int kRawBytes = WQ ? kCodeBytes + 2 * kGroupBytes : 0;
-  static constexpr int kStageBytes = ((WQ ? 0 : kABytes) + kBBytes + 1023) / 1024 * 1024;
+  static constexpr int kStageBytes = ((WQ ? 0 : MT * kABytes) + kBBytes + 1023) / 1024 * 1024;
   static constexpr int kPipeBytes = STAGES * kStageBytes;
   static constexpr int kRawBudget = 200 * 1024 - kPipeBytes;
   static constexpr int kRawStages = WQ ? (kRawBudget / kRawBytes > 24 ? 24 : kRawBudget / kRawBytes) : 0;
@@ -156,7 +161,8 @@ struct GemmSmem {
   static constexpr int kNumBars = 2 * STAGES + 1 + (WQ ? 2 * kRawStages : 0);
   static constexpr int kTotal = kBarOffset + kNumBars * 8 + 16 + 1024;  // + alignment slack
   static constexpr int kAccCols = BN < 32 ? 32 : BN;
-  static constexpr int kNeedCols = kAccCols + (WQ ? STAGES * 32 : 0);
+  static constexpr int kNeedCols = MT * kAccCols + (WQ ? STAGES * 32 : 0);
+  static_assert(MT == 1 || WQ == 0, "two weight tiles per CTA serve bf16 weights only");
   static constexpr int kTmemCols = kNeedCols <= 32 ? 32 : kNeedCols <= 64 ? 64 : kNeedCols <= 128 ? 128
                                    : kNeedCols <= 256 ? 256 : 512;
   static_assert(kNeedCols <= 512, "tensor memory plan exceeds 512 columns");
@@ -198,11 +204,11 @@ struct QArgs {
   int gs, gpb, rec_bytes, kb_total;
 };
 
-template <int BN, int STAGES, int MODE, int WQ>
-__global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
+template <int BN, int STAGES, int MODE, int WQ, int MT = 1>
+__global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ, MT>::kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                         GemmArgs args, const __grid_constant__ CollArgs coll, const __grid_constant__ QArgs qa) {
-  using S = GemmSmem<BN, STAGES, WQ>;
+  using S = GemmSmem<BN, STAGES, WQ, MT>;
   constexpr int kThreads = S::kThreads;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kBarOffset + S::kNumBars * 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * 128;
+  const int n0 = blockIdx.x * 128 * MT;
   const int m0 = blockIdx.y * BN;
   const int z = blockIdx.z;
   const int kb_begin = z * args.kb_per_split;
@@ -256,7 +262,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     // ---------------- TMA producer ----------------
     const uint64_t pol_w = l2_policy_evict_first();
     const uint64_t pol_x = l2_policy_evict_last();
-    const uint32_t stage_tx = (uint32_t)(S::kABytes + S::kBBytes);
+    const uint32_t stage_tx = (uint32_t)(MT * S::kABytes + S::kBBytes);
     // Weights are written by no kernel: the first STAGES weight tiles are
     // requested before waiting on the previous kernel (PDL), so their HBM
     // latency overlaps the predecessor's tail.
@@ -264,7 +270,9 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
     for (int i = 0; i < pre; ++i) {
       const uint32_t a = sbase + i * S::kStageBytes;
       mbar_arrive_expect_tx(bar_full + 8 * i, stage_tx);
-      tma_load_2d(a, &tmW, bar_full + 8 * i, (kb_begin + i) * 64, n0, pol_w);
+#pragma unroll
+      for (int h = 0; h < MT; ++h)
+        tma_load_2d(a + h * S::kABytes, &tmW, bar_full + 8 * i, (kb_begin + i) * 64, n0 + 128 * h, pol_w);
     }
     pdl_wait();
     // Activation tile: local TMA; in all-gather mode from the gathered buffer
@@ -282,16 +290,17 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
       for (int j = 0; j < coll.comm.world; ++j) wait_counter(coll.comm.pad_ptr(coll.comm.rank, kPadAG, j), ep);
     }
     for (int i = 0; i < pre; ++i)
-      load_x(sbase + i * S::kStageBytes + S::kABytes, bar_full + 8 * i, (kb_begin + i) * 64);
+      load_x(sbase + i * S::kStageBytes + MT * S::kABytes, bar_full + 8 * i, (kb_begin + i) * 64);
     int issued = pre;
     for (int i = pre; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
       const uint32_t a = sbase + s * S::kStageBytes;
-      const uint32_t b = a + S::kABytes;
+      const uint32_t b = a + MT * S::kABytes;
       mbar_arrive_expect_tx(bar_full + 8 * s, stage_tx);
       const int kc = (kb_begin + i) * 64;
-      tma_load_2d(a, &tmW, bar_full + 8 * s, kc, n0, pol_w);
+#pragma unroll
+      for (int h = 0; h < MT; ++h) tma_load_2d(a + h * S::kABytes, &tmW, bar_full + 8 * s, kc, n0 + 128 * h, pol_w);
       load_x(b, bar_full + 8 * s, kc);
       issued = i + 1;
     }
@@ -308,11 +317,15 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
       if (trace && i == 0) trace[2] = globaltimer();
       tc_fence_after();
       const uint32_t a = sbase + s * S::kStageBytes;
-      const uint32_t b = a + S::kABytes;
-      const uint64_t ad = umma_desc_k_sw128(a, 1024);
+      const uint32_t b = a + MT * S::kABytes;
       const uint64_t bd = umma_desc_k_sw128(b, 1024);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) tc_mma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+      for (int h = 0; h < MT; ++h) {
+        const uint64_t ad = umma_desc_k_sw128(a + h * S::kABytes, 1024);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_f16(tmem + h * S::kAccCols, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+      }
       tc_commit(bar_empty + 8 * s);
     }
     tc_commit(bar_accum);
@@ -407,190 +420,196 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ>::kThreads, 1)
   const bool acc_ok = __syncthreads_and(mbar_wait(bar_accum, 0, kErrTmemWait) ? 1 : 0) != 0;
   tc_fence_after();
   if (trace && threadIdx.x == 0) trace[3] = globaltimer();
-  const int r = warp * 32 + lane;  // TMEM lane == weight row within the tile
-  float* part = reinterpret_cast<float*>(smem);
-  if (warp < 4) {
-    const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+  // one pass per weight tile of the CTA (MT = 2: the second accumulator after the first)
+  for (int hh = 0; hh < MT; ++hh) {
+    const int n0e = n0 + 128 * hh;
+    if (n0e >= args.N) break;     // a last CTA's second tile past the weight rows (uniform branch)
+    if (hh > 0) __syncthreads();  // the previous pass's epilogue has finished reading the partial
+    const int r = warp * 32 + lane;  // TMEM lane == weight row within the tile
+    float* part = reinterpret_cast<float*>(smem);
+    if (warp < 4) {
+      const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16) + hh * S::kAccCols;
 #pragma unroll 1
-    for (int jc = 0; jc < BN; jc += 16) {
-      uint32_t v[16];
-      tmem_ld16(t_lane + jc, v);
-      tc_wait_ld();
+      for (int jc = 0; jc < BN; jc += 16) {
+        uint32_t v[16];
+        tmem_ld16(t_lane + jc, v);
+        tc_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) part[(jc + j) * 128 + r] = (acc_ok && nkb > 0) ? __uint_as_float(v[j]) : 0.f;
+        for (int j = 0; j < 16; ++j) part[(jc + j) * 128 + r] = (acc_ok && nkb > 0) ? __uint_as_float(v[j]) : 0.f;
+      }
     }
-  }
-  tc_fence_before();
-  if (args.ksplit > 1) cluster_sync();
-  else __syncthreads();
-  if (trace && threadIdx.x == 0) trace[4] = globaltimer();
+    tc_fence_before();
+    if (args.ksplit > 1) cluster_sync();
+    else __syncthreads();
+    if (trace && threadIdx.x == 0) trace[4] = globaltimer();
 
-  // ---------------- cluster reduction + epilogue ----------------
-  const int ks = args.ksplit;
-  const int js = (BN + ks - 1) / ks;
-  const int j_lo = z * js;
-  const int j_hi = min(BN, min(j_lo + js, args.M - m0));
-  // Partials are [BN][128] fp32 rows = 32 float4 per token column. Each thread
-  // sums whole float4s of the S partials in split order 0..S-1; all S loads of
-  // a float4 are issued before the adds so their DSMEM latencies overlap.
-  const float4* rp[8];
-#pragma unroll
-  for (int q = 0; q < 8; ++q)
-    rp[q] = reinterpret_cast<const float4*>((q < ks) ? (ks > 1 ? map_cluster_rank(part, q) : part) : part);
-  auto red4 = [&](int j, int r4) -> float4 {
-    const int off = j * 32 + r4;
-    float4 v[8];
+    // ---------------- cluster reduction + epilogue ----------------
+    const int ks = args.ksplit;
+    const int js = (BN + ks - 1) / ks;
+    const int j_lo = z * js;
+    const int j_hi = min(BN, min(j_lo + js, args.M - m0));
+    // Partials are [BN][128] fp32 rows = 32 float4 per token column. Each thread
+    // sums whole float4s of the S partials in split order 0..S-1; all S loads of
+    // a float4 are issued before the adds so their DSMEM latencies overlap.
+    const float4* rp[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q)
-      if (q < ks) v[q] = rp[q][off];
-    float4 acc = v[0];
+      rp[q] = reinterpret_cast<const float4*>((q < ks) ? (ks > 1 ? map_cluster_rank(part, q) : part) : part);
+    auto red4 = [&](int j, int r4) -> float4 {
+      const int off = j * 32 + r4;
+      float4 v[8];
 #pragma unroll
-    for (int q = 1; q < 8; ++q)
-      if (q < ks) {
-        acc.x += v[q].x;
-        acc.y += v[q].y;
-        acc.z += v[q].z;
-        acc.w += v[q].w;
-      }
-    return acc;
-  };
-  const bool glu = args.epi == kEpiSwiGLU || args.epi == kEpiGeGLU || args.epi == kEpiSwiGLUOAI;
-  if (glu) {
-    // 16 threads per token column (64 gate rows as 16 float4), 8 columns per pass
-    const int jj = threadIdx.x >> 4, f4 = threadIdx.x & 15;
-    constexpr int kColsPerPass = kThreads / 16;
-    __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(args.Y);
-    float bg[4], bu[4];
+      for (int q = 0; q < 8; ++q)
+        if (q < ks) v[q] = rp[q][off];
+      float4 acc = v[0];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      bg[e] = args.bias ? bf2f(args.bias[n0 + f4 * 4 + e]) : 0.f;
-      bu[e] = args.bias ? bf2f(args.bias[n0 + 64 + f4 * 4 + e]) : 0.f;
-    }
-    for (int j = j_lo + jj; j < j_hi; j += kColsPerPass) {
-      const float4 g4 = red4(j, f4), u4 = red4(j, f4 + 16);
-      const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
-      __nv_bfloat16 o[4];
+      for (int q = 1; q < 8; ++q)
+        if (q < ks) {
+          acc.x += v[q].x;
+          acc.y += v[q].y;
+          acc.z += v[q].z;
+          acc.w += v[q].w;
+        }
+      return acc;
+    };
+    const bool glu = args.epi == kEpiSwiGLU || args.epi == kEpiGeGLU || args.epi == kEpiSwiGLUOAI;
+    if (glu) {
+      // 16 threads per token column (64 gate rows as 16 float4), 8 columns per pass
+      const int jj = threadIdx.x >> 4, f4 = threadIdx.x & 15;
+      constexpr int kColsPerPass = kThreads / 16;
+      __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(args.Y);
+      float bg[4], bu[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        // round the gate and up projections to bf16 first, as an unfused bf16
-        // model would, then apply the activation in fp32
-        const float g = bf2f(f2bf(gv[e] + bg[e]));
-        const float u = bf2f(f2bf(uv[e] + bu[e]));
-        o[e] = f2bf(glu_act(args.epi, g, u));
+        bg[e] = args.bias ? bf2f(args.bias[n0e + f4 * 4 + e]) : 0.f;
+        bu[e] = args.bias ? bf2f(args.bias[n0e + 64 + f4 * 4 + e]) : 0.f;
       }
-      const int f = (n0 >> 1) + f4 * 4;
-      __nv_bfloat16* dst = Y + (size_t)(m0 + j) * args.ldy + f;
-      if (f + 3 < (args.N >> 1) && (((uintptr_t)dst) & 7) == 0) {
-        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (f + e < (args.N >> 1)) dst[e] = o[e];
-      }
-    }
-  } else {
-    // 32 threads per token column (128 rows as 32 float4), 4 columns per pass
-    const int jj = threadIdx.x >> 5, r4 = threadIdx.x & 31;
-    constexpr int kColsPerPass = kThreads / 32;
-    const int n = n0 + r4 * 4;
-    float bb[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) bb[e] = (args.bias && n + e < args.N) ? bf2f(args.bias[n + e]) : 0.f;
-    for (int j = j_lo + jj; j < j_hi; j += kColsPerPass) {
-      const float4 v4 = red4(j, r4);
-      const float v[4] = {v4.x + bb[0], v4.y + bb[1], v4.z + bb[2], v4.w + bb[3]};
-      const size_t m = (size_t)(m0 + j);
-      if (MODE == kModeLocal && args.epi == kEpiQKRope) {
-        // one warp per token column: the warp holds the token's whole head (4 channels per lane)
-        const RopeKvEpi& rk = args.rk;
-        const int head = n0 >> 7, d0 = r4 * 4;
-        float x[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) x[e] = bf2f(f2bf(v[e]));
-        const int64_t slot = rk.slots ? rk.slots[m] : -1;
-        const bool slot_ok = slot >= 0 && slot < rk.num_slots;
-        if (rk.slots && slot >= rk.num_slots && r4 == 0) set_status(kErrBounds);
-        if (head < rk.H + rk.KVH) {
-          const bool is_q = head < rk.H;
-          const __nv_bfloat16* nw = is_q ? rk.qw : rk.kw;
-          if (nw) {
-            const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
-            const float inv = rsqrtf(ss / 128.f + rk.eps);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) x[e] = bf2f(f2bf(x[e] * inv * bf2f(nw[d0 + e])));
-          }
-          // cos|sin of the 4 channels' frequencies: two 16-byte loads
-          const float* cs = rk.cos_sin + (size_t)rk.positions[m] * 128 + (d0 & 63);
-          const float4 c4 = *reinterpret_cast<const float4*>(cs);
-          const float4 s4 = *reinterpret_cast<const float4*>(cs + 64);
-          const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
-          float o[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p = __shfl_xor_sync(0xffffffffu, x[e], 16);
-            o[e] = d0 < 64 ? x[e] * cv[e] - p * sv[e] : x[e] * cv[e] + p * sv[e];
-          }
-          if (is_q) {
-            __nv_bfloat16 q[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) q[e] = f2bf(o[e]);
-            *reinterpret_cast<uint2*>(rk.q_out + (m * rk.H + head) * 128 + d0) = *reinterpret_cast<const uint2*>(q);
-          } else if (slot_ok) {
-            const int kvh = head - rk.H;
-            float kb[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) kb[e] = bf2f(f2bf(o[e]));
-            const size_t idx = ((size_t)((slot >> 4) * rk.KVH + kvh) * 16 + (slot & 15)) * 128 + d0;
-            store4_kv(rk.k_cache, rk.kv_fp8, idx, kb, rk.k_scale ? 1.f / rk.k_scale[kvh] : 1.f);
-          }
-        } else if (slot_ok) {
-          const int kvh = head - rk.H - rk.KVH;
-          const size_t idx = ((size_t)((slot >> 4) * rk.KVH + kvh) * 16 + (slot & 15)) * 128 + d0;
-          store4_kv(rk.v_cache, rk.kv_fp8, idx, x, rk.v_scale ? 1.f / rk.v_scale[kvh] : 1.f);
-        }
-        continue;
-      }
-      if constexpr (MODE == kModeRS) {
-        // fp32 partial row m -> inbox slot [parity][this rank][row] of its owner rank
-        const int rpr = coll.comm.rows_per_rank;
-        float* dst = coll.comm.recv_row((int)m / rpr, coll.parity, coll.comm.rank, (int)m % rpr) + n;
-        if (n + 3 < args.N) {
-          *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (n + e < args.N) dst[e] = v[e];
-        }
-      } else if (args.epi == kEpiStoreF32) {
-        float* dst = reinterpret_cast<float*>(args.Y) + m * args.ldy + n;
-        if (n + 3 < args.N && (((uintptr_t)dst) & 15) == 0) {
-          *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (n + e < args.N) dst[e] = v[e];
-        }
-      } else {
+      for (int j = j_lo + jj; j < j_hi; j += kColsPerPass) {
+        const float4 g4 = red4(j, f4), u4 = red4(j, f4 + 16);
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
         __nv_bfloat16 o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          if (args.epi == kEpiAddBf16) {
-            const float rr = (n + e < args.N) ? bf2f(args.R[m * args.ldr + n + e]) : 0.f;
-            o[e] = f2bf(bf2f(f2bf(v[e])) + rr);
-          } else if (args.epi == kEpiGelu || args.epi == kEpiGeluTanh || args.epi == kEpiQuickGelu ||
-                     args.epi == kEpiRelu2) {
-            o[e] = f2bf(gelu_act(args.epi, v[e]));
-          } else {
-            o[e] = f2bf(v[e]);
-          }
+          // round the gate and up projections to bf16 first, as an unfused bf16
+          // model would, then apply the activation in fp32
+          const float g = bf2f(f2bf(gv[e] + bg[e]));
+          const float u = bf2f(f2bf(uv[e] + bu[e]));
+          o[e] = f2bf(glu_act(args.epi, g, u));
         }
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.Y) + m * args.ldy + n;
-        if (n + 3 < args.N && (((uintptr_t)dst) & 7) == 0) {
+        const int f = (n0e >> 1) + f4 * 4;
+        __nv_bfloat16* dst = Y + (size_t)(m0 + j) * args.ldy + f;
+        if (f + 3 < (args.N >> 1) && (((uintptr_t)dst) & 7) == 0) {
           *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
         } else {
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            if (n + e < args.N) dst[e] = o[e];
+            if (f + e < (args.N >> 1)) dst[e] = o[e];
+        }
+      }
+    } else {
+      // 32 threads per token column (128 rows as 32 float4), 4 columns per pass
+      const int jj = threadIdx.x >> 5, r4 = threadIdx.x & 31;
+      constexpr int kColsPerPass = kThreads / 32;
+      const int n = n0e + r4 * 4;
+      float bb[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) bb[e] = (args.bias && n + e < args.N) ? bf2f(args.bias[n + e]) : 0.f;
+      for (int j = j_lo + jj; j < j_hi; j += kColsPerPass) {
+        const float4 v4 = red4(j, r4);
+        const float v[4] = {v4.x + bb[0], v4.y + bb[1], v4.z + bb[2], v4.w + bb[3]};
+        const size_t m = (size_t)(m0 + j);
+        if (MODE == kModeLocal && args.epi == kEpiQKRope) {
+          // one warp per token column: the warp holds the token's whole head (4 channels per lane)
+          const RopeKvEpi& rk = args.rk;
+          const int head = n0e >> 7, d0 = r4 * 4;
+          float x[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) x[e] = bf2f(f2bf(v[e]));
+          const int64_t slot = rk.slots ? rk.slots[m] : -1;
+          const bool slot_ok = slot >= 0 && slot < rk.num_slots;
+          if (rk.slots && slot >= rk.num_slots && r4 == 0) set_status(kErrBounds);
+          if (head < rk.H + rk.KVH) {
+            const bool is_q = head < rk.H;
+            const __nv_bfloat16* nw = is_q ? rk.qw : rk.kw;
+            if (nw) {
+              const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+              const float inv = rsqrtf(ss / 128.f + rk.eps);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) x[e] = bf2f(f2bf(x[e] * inv * bf2f(nw[d0 + e])));
+            }
+            // cos|sin of the 4 channels' frequencies: two 16-byte loads
+            const float* cs = rk.cos_sin + (size_t)rk.positions[m] * 128 + (d0 & 63);
+            const float4 c4 = *reinterpret_cast<const float4*>(cs);
+            const float4 s4 = *reinterpret_cast<const float4*>(cs + 64);
+            const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float p = __shfl_xor_sync(0xffffffffu, x[e], 16);
+              o[e] = d0 < 64 ? x[e] * cv[e] - p * sv[e] : x[e] * cv[e] + p * sv[e];
+            }
+            if (is_q) {
+              __nv_bfloat16 q[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) q[e] = f2bf(o[e]);
+              *reinterpret_cast<uint2*>(rk.q_out + (m * rk.H + head) * 128 + d0) = *reinterpret_cast<const uint2*>(q);
+            } else if (slot_ok) {
+              const int kvh = head - rk.H;
+              float kb[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) kb[e] = bf2f(f2bf(o[e]));
+              const size_t idx = ((size_t)((slot >> 4) * rk.KVH + kvh) * 16 + (slot & 15)) * 128 + d0;
+              store4_kv(rk.k_cache, rk.kv_fp8, idx, kb, rk.k_scale ? 1.f / rk.k_scale[kvh] : 1.f);
+            }
+          } else if (slot_ok) {
+            const int kvh = head - rk.H - rk.KVH;
+            const size_t idx = ((size_t)((slot >> 4) * rk.KVH + kvh) * 16 + (slot & 15)) * 128 + d0;
+            store4_kv(rk.v_cache, rk.kv_fp8, idx, x, rk.v_scale ? 1.f / rk.v_scale[kvh] : 1.f);
+          }
+          continue;
+        }
+        if constexpr (MODE == kModeRS) {
+          // fp32 partial row m -> inbox slot [parity][this rank][row] of its owner rank
+          const int rpr = coll.comm.rows_per_rank;
+          float* dst = coll.comm.recv_row((int)m / rpr, coll.parity, coll.comm.rank, (int)m % rpr) + n;
+          if (n + 3 < args.N) {
+            *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (n + e < args.N) dst[e] = v[e];
+          }
+        } else if (args.epi == kEpiStoreF32) {
+          float* dst = reinterpret_cast<float*>(args.Y) + m * args.ldy + n;
+          if (n + 3 < args.N && (((uintptr_t)dst) & 15) == 0) {
+            *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (n + e < args.N) dst[e] = v[e];
+          }
+        } else {
+          __nv_bfloat16 o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (args.epi == kEpiAddBf16) {
+              const float rr = (n + e < args.N) ? bf2f(args.R[m * args.ldr + n + e]) : 0.f;
+              o[e] = f2bf(bf2f(f2bf(v[e])) + rr);
+            } else if (args.epi == kEpiGelu || args.epi == kEpiGeluTanh || args.epi == kEpiQuickGelu ||
+                       args.epi == kEpiRelu2) {
+              o[e] = f2bf(gelu_act(args.epi, v[e]));
+            } else {
+              o[e] = f2bf(v[e]);
+            }
+          }
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.Y) + m * args.ldy + n;
+          if (n + 3 < args.N && (((uintptr_t)dst) & 7) == 0) {
+            *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(o);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (n + e < args.N) dst[e] = o[e];
+          }
         }
       }
     }
@@ -693,13 +712,13 @@ static const CollArgs& local_coll_q() {
   return c;
 }
 
-template <int BN, int STAGES, int MODE, int WQ = 0>
+template <int BN, int STAGES, int MODE, int WQ = 0, int MT = 1>
 static int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, const CollArgs& coll,
                        int tiles_n, int tiles_m, cudaStream_t st, const QArgs& q = no_quant()) {
-  using S = GemmSmem<BN, STAGES, WQ>;
+  using S = GemmSmem<BN, STAGES, WQ, MT>;
   static_assert(S::kTotal <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
-  if (int e = smem_attr_once<gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ>>(S::kTotal)) return e;
-  cudaError_t e = launch_k(gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ>, dim3(tiles_n, tiles_m, a.ksplit),
+  if (int e = smem_attr_once<gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ, MT>>(S::kTotal)) return e;
+  cudaError_t e = launch_k(gemm_bf16_tc_kernel<BN, STAGES, MODE, WQ, MT>, dim3(tiles_n, tiles_m, a.ksplit),
                            dim3(S::kThreads, 1, 1), S::kTotal, st, a.ksplit, tw, tx, a, coll, q);
   if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
@@ -837,6 +856,8 @@ int b200_gemm_qkv_rope(const void* X, int M, int K, int ldx, const void* W, int 
   if (s > 8) return -1;
   a.kb_per_split = (a.kb_total + s - 1) / s;
   a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  if (a.ksplit == 1 && BN == 256 && N > 128)  // prefill-sized, unsplit: 256 x 256 tiles
+    return launch_gemm<256, 3, kModeLocal, 0, 2>(tw, tx, a, local_coll(), (N + 255) / 256, (M + 255) / 256, stream);
   const int tiles_n = N / 128, tiles_m = (M + BN - 1) / BN;
   return launch_bn<kModeLocal>(BN, tw, tx, a, local_coll(), tiles_n, tiles_m, stream);
 }
@@ -878,6 +899,8 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   if (s > 8) return -1;
   a.kb_per_split = (a.kb_total + s - 1) / s;
   a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  if (a.ksplit == 1 && BN == 256 && N > 128)  // prefill-sized, unsplit: 256 x 256 tiles
+    return launch_gemm<256, 3, kModeLocal, 0, 2>(tw, tx, a, local_coll(), (N + 255) / 256, (M + 255) / 256, stream);
   const int tiles_n = (N + 127) / 128, tiles_m = (M + BN - 1) / BN;
   return launch_bn<kModeLocal>(BN, tw, tx, a, local_coll(), tiles_n, tiles_m, stream);
 }

@@ -40,10 +40,12 @@ from ..ops.attention import decode_max_parts
 
 @dataclass
 class MTPConfig:
-    k: int = 3
+    k: int = 3  # draft depth (the maximum depth when adaptive)
     acceptance: str = "exact"  # exact | bernoulli
     p: float = 0.7
     seed: int = 0
+    adaptive: bool = False  # choose the depth per round (engine.mtp_depth.DepthController)
+    max_rows: int = 0  # > 0: steps with more decode rows run without drafts (bounded drafter work)
 
 
 @dataclass
@@ -68,6 +70,11 @@ class MTPDriver:
         self.kv = module.new_kv(max_tokens=(engine.kv.num_pages - 1) * 16, kv_fp8=engine.cfg.kv_fp8)
         self.rng = np.random.default_rng(self.cfg.seed)
         self.stats = MTPStats()
+        self.depth = None
+        if self.cfg.adaptive:
+            from .mtp_depth import DepthController
+
+            self.depth = DepthController(self.cfg.k)
         self.h2d_bytes = 0  # step inputs copied host -> device
         self.d2h_bytes = 0  # drafts + target tokens read back
 
@@ -90,6 +97,8 @@ class MTPDriver:
     def eligible(self, plan) -> bool:
         if not plan.pure_decode:
             return False
+        if self.cfg.max_rows > 0 and len(plan.rows) > self.cfg.max_rows:
+            return False
         for r in plan.rows:
             st = r.state
             sp = st.req.sampling
@@ -100,8 +109,8 @@ class MTPDriver:
         return True
 
     # ------------------------------------------------------------------ round
-    def _ensure(self, rows) -> bool:
-        k = self.cfg.k
+    def _ensure(self, rows, k: int | None = None) -> bool:
+        k = self.cfg.k if k is None else k
         for r in rows:
             st = r.state
             if not self.eng.sched._ensure(st, r.start + k + 1):
@@ -163,9 +172,13 @@ class MTPDriver:
         """Run one MTP round for a pure-decode greedy plan. Returns the emitted
         events, or None when KV capacity does not allow a round (the caller
         then runs a normal decode step)."""
-        eng, k = self.eng, self.cfg.k
+        import time
+
+        eng = self.eng
+        k = self.depth.choose() if self.depth is not None else self.cfg.k
+        t_round = time.perf_counter()
         rows = plan.rows
-        if not self._ensure(rows):
+        if not self._ensure(rows, k):
             return None
         states = [r.state for r in rows]
         B = len(rows)
@@ -209,6 +222,7 @@ class MTPDriver:
         st_ = self.stats
         st_.rounds += 1
         st_.rows += B
+        acc_rows = []
         for i, st in enumerate(states):
             if self.cfg.acceptance == "bernoulli":
                 a = 0
@@ -221,6 +235,7 @@ class MTPDriver:
             emit = [int(t) for t in D_h[i, :a]] + [int(pred_h[i, a])]
             st_.drafted += k
             st_.accepted += a
+            acc_rows.append(a)
             # target K/V: x and the accepted drafts; the rest is rolled back
             st.seq.num_tokens = p[i] + a + 1
             # next round: step-1 history p+1 .. p+a+1 with verify hiddens of columns 0..a
@@ -231,4 +246,7 @@ class MTPDriver:
                 events += eng._accept_token(st, t, None)
                 if st.status.name == "FINISHED":
                     break
+        if self.depth is not None:
+            # the round ends with the host readback above: its wall time is the round's cost
+            self.depth.observe(k, acc_rows, time.perf_counter() - t_round)
         return events

@@ -412,3 +412,50 @@ def test_gemm_row_roles_split_launch():
     assert y.shape == (300, 1024)
     assert torch.equal(y[:37], y_dec) and torch.equal(y[37:], y_pf)
     torch.testing.assert_close(y.float(), x.float() @ w.float().T, atol=3e-2, rtol=3e-2)
+
+
+@pytest.mark.parametrize("N,epi", [(1024, "none"), (384, "none"), (640, "swiglu"), (1280, "f32"), (768, "add"),
+                                   (512, "gelu")])
+def test_gemm_two_tile_unsplit(N, epi):
+    """Unsplit GEMMs with >128 rows run 256 x 256 tiles (two weight tiles and
+    two accumulators per CTA); N not a multiple of 256 leaves a half-used last
+    tile. Checked against the fp32 oracle and the split-K path."""
+    torch.manual_seed(N)
+    M, K = 300, 1024
+    x = (torch.randn(M, K, device="cuda") * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, device="cuda") * 0.1).to(torch.bfloat16)
+    r = torch.randn(M, N, device="cuda").to(torch.bfloat16) if epi == "add" else None
+    y1 = ops.gemm(x, w, epi=epi, residual=r, bias=b, splits=1)
+    y4 = ops.gemm(x, w, epi=epi, residual=r, bias=b, splits=4)
+    want = ref.gemm_ref(x.float(), w.float(), epi, r.float() if r is not None else None, bias=b.float())
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y1.float(), want.float(), atol=5e-2, rtol=5e-2)
+    torch.testing.assert_close(y1.float(), y4.float(), atol=5e-2, rtol=5e-2)
+
+
+def test_gemm_qkv_rope_two_tile():
+    """The fused qkv epilogue on the 256 x 256 tile path (unsplit, >128 rows)."""
+    from mlx_swift_lm_b200.models.rope import build_rope
+
+    torch.manual_seed(9)
+    H, KVH, D, K, M = 6, 1, 128, 512, 260  # 8 heads: the last CTA's second tile is a value head
+    dev = torch.device("cuda")
+    N = (H + 2 * KVH) * D
+    x = (torch.randn(M, K, device=dev) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+    cos_sin, rd = build_rope(D, 1e6, None, 4096)
+    cos_sin = cos_sin.to(dev)
+    pos = torch.randint(0, 4000, (M,), device=dev, dtype=torch.int32)
+    slots = torch.randperm(64 * 16, device=dev)[:M].to(torch.int64)
+    kc1 = torch.zeros(64, KVH, 16, D, device=dev, dtype=torch.bfloat16)
+    vc1, kc2, vc2 = kc1.clone(), kc1.clone(), kc1.clone()
+    qkv = ops.gemm(x, w, splits=1)
+    q1 = ops.qk_norm_rope_kv(qkv, pos, slots, cos_sin, rd, False, qn, kn, 1e-6, kc1, vc1, H, KVH, D)
+    q2 = ops.gemm_qkv_rope(x, w, None, pos, slots, cos_sin, qn, kn, 1e-6, kc2, vc2, H, KVH, splits=1)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(q2.float(), q1.float(), atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(kc2.float(), kc1.float(), atol=6e-2, rtol=6e-2)
+    assert torch.equal(vc2, vc1)
