@@ -64,6 +64,20 @@ class ModelContainer:
         return cls(m, tokenizer, engine_config or EngineConfig(scheduler=SchedulerConfig(),
                                                                use_cuda_graphs=torch.device(device).type == "cuda"))
 
+    def replicate(self, devices: list, engine_config: EngineConfig | None = None):
+        """Data parallelism: one more engine per extra device, each with a copy
+        of the model, behind an :class:`..engine.replicas.EngineReplicas` router
+        that becomes this container's engine (the server sees one engine)."""
+        from ..engine.replicas import EngineReplicas
+
+        cfg = engine_config or self.engine.cfg
+        engines = [self.engine]
+        for d in devices:
+            m = self.model.clone_to(d, self.model.dtype)
+            engines.append(EngineV2(m, self.tokenizer, cfg, eos_token_ids=self.eos))
+        self.engine = EngineReplicas(engines)
+        return self
+
     # ------------------------------------------------------------------ actor-style access
     def perform(self, fn):
         with self.lock:

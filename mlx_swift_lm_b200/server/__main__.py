@@ -33,6 +33,8 @@ def parse(argv=None):
     ap.add_argument("--random-config", default=env("random_config"),
                     help="serve random weights of a named shape: tiny_qwen3 | qwen3_8b | ...")
     ap.add_argument("--device", default=env("device"))
+    ap.add_argument("--data-parallel", type=int, default=int(env("data_parallel", "1")),
+                    help="engine replicas, one per GPU (cuda:0..N-1), behind a load / prefix-affinity router")
     return ap.parse_args(argv)
 
 
@@ -68,6 +70,8 @@ def main(argv=None):
     else:
         print("either --model or --random-config is required", file=sys.stderr)
         return 2
+    if args.data_parallel > 1:
+        container.replicate([f"cuda:{i}" for i in range(1, args.data_parallel)], ecfg)
     embedder = None
     if args.embedding_model:
         from ..api.embed import Embedder
