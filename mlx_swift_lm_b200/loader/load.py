@@ -251,7 +251,9 @@ def _load_attention(ck: CheckpointView, cfg, L, a, norm, r, w):
         qb, kb, vb = ck.vec(a + "q_proj.bias"), ck.vec(a + "k_proj.bias"), ck.vec(a + "v_proj.bias")
         if qb is not None:
             L.bqkv = torch.cat([_shard_rows(qb, r, w), _kv_rows(kb, cfg, r, w), _kv_rows(vb, cfg, r, w)], 0)
-    if cfg.qk_norm:
+    if cfg.qk_norm or cfg.qk_norm_full:
+        if cfg.qk_norm_full and w > 1:
+            raise NotImplementedError("q/k norms over the whole projection need every head on one rank")
         L.q_norm = norm(a + "q_norm.weight")
         L.k_norm = norm(a + "k_norm.weight")
     L.wo = _shard_cols(ck.linear(a + "o_proj"), r, w)
@@ -510,6 +512,10 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
             L.ln2_b = ck.vec(p + "post_attention_layernorm.bias")
         if cfg.parallel_block:  # one norm feeds attention and MLP
             pass
+        elif not cfg.pre_norms:  # post-sublayer norms only (OLMo 2/3, EXAONE 4)
+            L.ln1 = None
+            L.post_attn_norm = norm(p + "post_attention_layernorm.weight")
+            L.post_ffn_norm = norm(p + "post_feedforward_layernorm.weight")
         elif cfg.post_norms:
             L.post_attn_norm = norm(p + "post_attention_layernorm.weight")
             L.ln2 = norm(p + "pre_feedforward_layernorm.weight")

@@ -44,6 +44,12 @@ class DecoderConfig:
     embed_scale: float = 1.0
     norm_offset_one: bool = False  # weight stored as (w - 1), applied as (1 + w) (Gemma)
     post_norms: bool = False  # sandwich norms around attention and FFN (Gemma 2/3)
+    # False: no input norms before attention / FFN, only the post-sublayer norms (OLMo 2/3, EXAONE 4)
+    pre_norms: bool = True
+    # q/k RMSNorm over the whole projection (all heads; weights [H*D], [KVH*D]) instead of per head (OLMo 2/3)
+    qk_norm_full: bool = False
+    # layers that apply no rotary embedding (EXAONE 4's global layers)
+    nope_layers: list[int] | None = None
     # FFN
     hidden_act: str = "silu"  # silu | gelu_tanh | swiglu_oai
     mlp_bias: bool = False

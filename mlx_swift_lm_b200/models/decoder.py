@@ -149,6 +149,14 @@ class DecoderLM:
         self.cos_sin, self.rot_dim = build_rope(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling,
                                                 cfg.max_position_embeddings, cfg.partial_rotary_factor)
         self.cos_sin = self.cos_sin.to(self.device)
+        # sliding-window layers with their own rotary base (Gemma 3 local layers, OLMo 3 sliding layers)
+        self.cos_sin_local = None
+        lt = cfg.extra.get("rope_local_theta")
+        if lt is not None:
+            self.cos_sin_local, _ = build_rope(cfg.head_dim, float(lt), None, cfg.max_position_embeddings,
+                                               cfg.partial_rotary_factor)
+            self.cos_sin_local = self.cos_sin_local.to(self.device)
+        self._nope = set(cfg.nope_layers or ())
         self.lora = None  # adapter whose update is currently added into the weights (adapters.lora)
         self.tp_fused = None  # fused symmetric-memory TP decode path (parallel.tp_fused)
         # hybrid models: attention layers index the KV slab, linear layers the recurrent-state pool
@@ -264,7 +272,10 @@ class DecoderLM:
             if cfg.attention_bias:
                 bq, bk, bv = rn(cfg.q_size), rn(cfg.kv_size), rn(cfg.kv_size)
                 L.bqkv = torch.cat([rows(bq, self.H * D), kv_rows(bk), kv_rows(bv)], 0)
-            if cfg.qk_norm:
+            if cfg.qk_norm_full:
+                L.q_norm = ones(self.H * D)
+                L.k_norm = ones(self.KVH * D)
+            elif cfg.qk_norm:
                 L.q_norm = ones(D)
                 L.k_norm = ones(D)
             L.wo = cols(rn(hd, cfg.q_size))
@@ -281,6 +292,10 @@ class DecoderLM:
                 self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
             else:
                 L.ln2 = None
+            if not cfg.pre_norms:  # post-sublayer norms only
+                L.ln1 = L.ln2 = None
+                L.post_attn_norm = ones(hd)
+                L.post_ffn_norm = ones(hd)
             if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
                 self.layers.append(L)
         return self
@@ -450,18 +465,23 @@ class DecoderLM:
         T, nd = fb.num_tokens, fb.num_decode
         ki = self.kv_index[li] if self.kv_index else li
         kc, vc = kv.layer(ki)
-        cos_sin, positions = self.cos_sin, fb.positions
+        cos_sin, rot_dim = self.rope_for(li)
+        positions = fb.positions
         if fb.rope_table is not None:  # per-token rotary rows (M-RoPE prompts)
             cos_sin = fb.rope_table
             positions = torch.arange(T, dtype=torch.int32, device=fb.positions.device)
         qkv = None
-        if self._fused_qkv_rope(L, h, fb):
+        if self._fused_qkv_rope(L, h, fb, rot_dim):
             q = ops.gemm_qkv_rope(h, L.wqkv, L.bqkv, positions, fb.slots, cos_sin, L.q_norm, L.k_norm,
                                   cfg.rms_norm_eps, kc, vc, self.H, self.KVH, kv.k_scale(ki), kv.v_scale(ki))
         else:
             qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
-            q = ops.qk_norm_rope_kv(qkv, positions, fb.slots, cos_sin, self.rot_dim, cfg.rope_interleaved,
-                                    L.q_norm, L.k_norm, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
+            qn, kn = L.q_norm, L.k_norm
+            if cfg.qk_norm_full:
+                qkv = self._qk_full_norm(L, qkv)
+                qn = kn = None
+            q = ops.qk_norm_rope_kv(qkv, positions, fb.slots, cos_sin, rot_dim, cfg.rope_interleaved,
+                                    qn, kn, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
                                     kv.k_scale(ki), kv.v_scale(ki))
         q = self._pos_scale_q(q, fb.positions)
         win = cfg.window(li)
@@ -485,18 +505,42 @@ class DecoderLM:
     # class switch: qkv GEMM with the qk-norm / RoPE / KV append epilogue where it applies
     fused_qkv_rope = os.environ.get("B200LM_FUSED_QKV_ROPE", "1") != "0"
 
-    def _fused_qkv_rope(self, L, h, fb) -> bool:
+    def rope_for(self, li: int):
+        """(cos|sin table, rotary dims) of layer li: the local table for
+        sliding-window layers when the model has one, none for NoPE layers."""
+        if li in self._nope:
+            return self.cos_sin, 0
+        if self.cos_sin_local is not None and self.cfg.window(li) > 0:
+            return self.cos_sin_local, self.rot_dim
+        return self.cos_sin, self.rot_dim
+
+    def _fused_qkv_rope(self, L, h, fb, rot_dim) -> bool:
         """The fused epilogue covers head dim 128 with full non-interleaved
         rotary from the position table, bf16 weights, no output gate rows."""
         cfg = self.cfg
-        return (self.fused_qkv_rope and h.is_cuda and self.D == 128 and self.rot_dim == 128
-                and not cfg.rope_interleaved and not cfg.attn_output_gate and fb.rope_table is None
-                and isinstance(L.wqkv, torch.Tensor) and L.wqkv.dtype == torch.bfloat16
+        return (self.fused_qkv_rope and h.is_cuda and self.D == 128 and rot_dim == 128
+                and not cfg.rope_interleaved and not cfg.attn_output_gate and not cfg.qk_norm_full
+                and fb.rope_table is None and isinstance(L.wqkv, torch.Tensor) and L.wqkv.dtype == torch.bfloat16
                 and self.cos_sin.shape[-1] == 128)
 
-    def _norm(self, x, delta, w, b=None):
-        """x <- x + delta; the block's input norm (RMSNorm, or LayerNorm with bias)."""
+    def _qk_full_norm(self, L, qkv):
+        """RMSNorm over the whole q and k projections (all heads), in place."""
         cfg = self.cfg
+        H, KVH, D = self.H, self.KVH, self.D
+        q = ops.rmsnorm(qkv[:, :H * D].contiguous(), L.q_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+        k = ops.rmsnorm(qkv[:, H * D:(H + KVH) * D].contiguous(), L.k_norm, cfg.rms_norm_eps, cfg.norm_offset_one)
+        qkv[:, :H * D] = q
+        qkv[:, H * D:(H + KVH) * D] = k
+        return qkv
+
+    def _norm(self, x, delta, w, b=None):
+        """x <- x + delta; the block's input norm (RMSNorm, or LayerNorm with bias).
+        Blocks without input norms (OLMo 2/3, EXAONE 4) get the residual stream itself."""
+        cfg = self.cfg
+        if w is None and not cfg.pre_norms:
+            if delta is not None:
+                x.add_(delta)
+            return x
         if cfg.norm_kind == "layernorm":
             return ops.add_layernorm(x, delta, w, b, cfg.rms_norm_eps)
         return ops.add_rmsnorm(x, delta, w, cfg.rms_norm_eps, offset_one=cfg.norm_offset_one)
@@ -648,8 +692,13 @@ class DecoderLM:
                 delta = self._attn_out(L, self._linear_body(L, ops.gemm(h, L.wqkv, bias=L.bqkv), rows, conv, ssm))
             else:
                 qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
-                q, k, v = ops.qk_norm_rope_kv(qkv, positions, None, self.cos_sin, self.rot_dim, cfg.rope_interleaved,
-                                              L.q_norm, L.k_norm, cfg.rms_norm_eps, None, None, self.H, self.KVH,
+                qn, kn = L.q_norm, L.k_norm
+                if cfg.qk_norm_full:
+                    qkv = self._qk_full_norm(L, qkv)
+                    qn = kn = None
+                cs, rd = self.rope_for(li)
+                q, k, v = ops.qk_norm_rope_kv(qkv, positions, None, cs, rd, cfg.rope_interleaved,
+                                              qn, kn, cfg.rms_norm_eps, None, None, self.H, self.KVH,
                                               self.D, return_kv=True)
                 ki = self.kv_index[li] if self.kv_index else li
                 kk, vv = cache.update(ki, k, v)
@@ -754,6 +803,8 @@ class DecoderLM:
                     else:
                         setattr(L, s, v.to(device=device, dtype=dtype))
         self.cos_sin = self.cos_sin.to(device)
+        if self.cos_sin_local is not None:
+            self.cos_sin_local = self.cos_sin_local.to(device)
         self.device, self.dtype = device, dtype
         return self
 

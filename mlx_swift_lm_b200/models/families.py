@@ -23,10 +23,11 @@ def register(*model_types, **traits):
 register("llama", "mistral", "smollm3", "helium", "granite", "hunyuan_v1_dense",
          "ernie4_5", "internlm2", "minicpm", "nanbeige", "laguna", "acereason", "mellum")
 # architectures whose distinguishing blocks are not built: refused instead of loaded wrongly
-_REFUSED = {"olmo2": "post-sublayer norms without pre-norms and q/k norms over the whole projection",
-            "olmo3": "post-sublayer norms without pre-norms and q/k norms over the whole projection",
-            "apertus": "the xIELU activation",
-            "exaone4": "post-sublayer norms without pre-norms"}
+_REFUSED = {"apertus": "the xIELU activation"}
+# post-sublayer norms only (no input norms), q/k RMSNorm over the whole projection
+register("olmo2", "olmo3", post_only_norms=True, qk_norm_full=True)
+# post-sublayer norms only, per-head q/k norms, local (L) / global (G) layer pattern, NoPE global layers
+register("exaone4", post_only_norms=True, qk_norm=True, exaone4=True)
 register("qwen2")  # q/k/v biases
 register("mimo")  # Xiaomi MiMo: the Qwen2 body (its MTP layers are not loaded)
 register("qwen2_vl", vlm="qwen2_vl")  # the language model of Qwen2-VL (q/k/v biases, M-RoPE)
@@ -233,6 +234,22 @@ def build_config(hf: dict) -> DecoderConfig:
                                for i in range(cfg.num_layers)]
         cfg.layer_windows = None
         cfg.attn_output_gate = hf.get("attn_output_gate", True)
+    if tr.get("post_only_norms"):
+        cfg.pre_norms = False
+        cfg.post_norms = True
+    if tr.get("qk_norm_full"):
+        cfg.qk_norm_full = True
+    if tr.get("exaone4"):
+        pat = hf.get("sliding_window_pattern")
+        if isinstance(pat, int):  # every pat-th layer global
+            pat = "L" * (pat - 1) + "G"
+        if pat:
+            local = [pat[i % len(pat)] == "L" for i in range(cfg.num_layers)]
+            cfg.layer_windows = [int(sw or 0) if lo else 0 for lo in local]
+            cfg.nope_layers = [i for i, lo in enumerate(local) if not lo]
+    if mt == "olmo3" and layer_types and cfg.rope_scaling:
+        # sliding layers rotate with the plain base; full layers with the scaled table
+        cfg.extra["rope_local_theta"] = cfg.rope_theta
     g = tr.get("gemma")
     if g:
         cfg.embed_scale = math.sqrt(hidden)

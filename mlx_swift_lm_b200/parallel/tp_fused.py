@@ -108,7 +108,8 @@ class FusedTP:
         for li, Lw in enumerate(m.layers):
             qkv = self._gemm_ag(ag, T, Lw.wqkv, self.qkv, bias=Lw.bqkv)[:T]
             kc, vc = kv.layer(li)
-            q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, m.cos_sin, m.rot_dim, cfg.rope_interleaved,
+            cs, rd = m.rope_for(li)
+            q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, cs, rd, cfg.rope_interleaved,
                                     Lw.q_norm, Lw.k_norm, cfg.rms_norm_eps, kc, vc, m.H, m.KVH, m.D,
                                     kv.k_scale(li), kv.v_scale(li))
             attn = ops.paged_decode(q, kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, cfg.window(li),
