@@ -47,5 +47,32 @@ bool pdl_enabled() {
 }
 }  // namespace b200
 
+// xIELU activation in place over bf16 x [n] (Apertus MLPs), from the layer's
+// raw parameters p = {alpha_p, alpha_n, beta, eps}:
+//   a_p = softplus(alpha_p), a_n = beta + softplus(alpha_n)
+//   x > 0:  a_p x^2 + beta x
+//   x <= 0: a_n (exp(min(x, eps)) - 1) - a_n x + beta x
+__global__ void xielu_kernel(__nv_bfloat16* x, int64_t n, const float* p) {
+  b200::pdl_launch_dependents();
+  b200::pdl_wait();
+  const float sp_a = p[0] > 20.f ? p[0] : log1pf(expf(p[0]));
+  const float sp_n = p[1] > 20.f ? p[1] : log1pf(expf(p[1]));
+  const float beta = p[2], eps = p[3];
+  const float an = beta + sp_n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = __bfloat162float(x[i]);
+    const float y = v > 0.f ? sp_a * v * v + beta * v : an * expm1f(fminf(v, eps)) - an * v + beta * v;
+    x[i] = __float2bfloat16_rn(y);
+  }
+}
+
+extern "C" int b200_xielu(void* x, int64_t n, const float* params, cudaStream_t st) {
+  if (n <= 0) return 0;
+  const int blocks = (int)((n + 1023) / 1024 < 2048 ? (n + 1023) / 1024 : 2048);
+  cudaError_t e = b200::launch_k(xielu_kernel, dim3(blocks), dim3(256), 0, st, 1,
+                                 reinterpret_cast<__nv_bfloat16*>(x), n, params);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
 extern "C" void b200_set_pdl(int on) { b200::g_pdl = on ? 1 : 0; }
 extern "C" int b200_get_pdl() { return b200::pdl_enabled() ? 1 : 0; }

@@ -506,7 +506,8 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
                 _load_attention(ck, cfg, L, mx, norm, r, w)
             m.layers.append(L)
             continue
-        L.ln1 = norm(p + "input_layernorm.weight")
+        n_in, n_post = cfg.extra.get("norm_names", ("input_layernorm", "post_attention_layernorm"))
+        L.ln1 = norm(p + n_in + ".weight")
         if cfg.norm_kind == "layernorm":
             L.ln1_b = ck.vec(p + "input_layernorm.bias")
             L.ln2_b = ck.vec(p + "post_attention_layernorm.bias")
@@ -521,7 +522,7 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
             L.ln2 = norm(p + "pre_feedforward_layernorm.weight")
             L.post_ffn_norm = norm(p + "post_feedforward_layernorm.weight")
         else:
-            L.ln2 = norm(p + "post_attention_layernorm.weight")
+            L.ln2 = norm(p + n_post + ".weight")
         L.linear = cfg.is_linear(i)
         if L.linear and cfg.linear_kind == "short_conv":  # LFM2: layers.{i}.conv.*
             mx = p + "conv."
@@ -557,6 +558,14 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
                 L.moe = False
                 L.wgu, L.wd = ck.linear(mp + "c_fc"), ck.linear(mp + "c_proj")
                 L.bgu, L.bd = ck.vec(mp + "c_fc.bias"), ck.vec(mp + "c_proj.bias")
+                m.layers.append(L)
+                continue
+            if cfg.glu_epi == "xielu":  # Apertus: non-gated up -> xIELU -> down
+                L.moe = False
+                L.wgu = _shard_rows(ck.linear(mp + "up_proj"), r, w)
+                L.wd = _shard_cols(ck.linear(mp + "down_proj"), r, w)
+                L.act_params = torch.stack([ck.raw(mp + "act_fn." + n).float().reshape(())
+                                            for n in ("alpha_p", "alpha_n", "beta", "eps")])
                 m.layers.append(L)
                 continue
             if cfg.extra.get("fused_gate_up"):

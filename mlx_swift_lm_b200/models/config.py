@@ -152,7 +152,7 @@ class DecoderConfig:
     @property
     def glu_epi(self) -> str:
         return {"silu": "swiglu", "gelu_tanh": "geglu", "gelu": "geglu", "swiglu_oai": "swiglu_oai",
-                "relu2": "relu2", "gelu_tanh_mlp": "gelu_tanh"}[self.hidden_act]
+                "relu2": "relu2", "gelu_tanh_mlp": "gelu_tanh", "xielu": "xielu"}[self.hidden_act]
 
     def to_dict(self) -> dict:
         return {f.name: getattr(self, f.name) for f in fields(self)}

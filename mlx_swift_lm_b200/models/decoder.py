@@ -46,9 +46,11 @@ class LayerWeights:
                  # LayerNorm biases of the input / post-attention norms (norm_kind "layernorm")
                  "ln1_b", "ln2_b",
                  # ParoQuant: activation rotations shared by the experts (gate/up input, down input)
-                 "experts_rot_in", "experts_rot_mid")
+                 "experts_rot_in", "experts_rot_mid",
+                 # xIELU MLP activation: raw (alpha_p, alpha_n, beta, eps) of the layer (Apertus)
+                 "act_params")
 
-    F32 = ("sinks", "conv_w", "A_log", "dt_bias", "conv_b", "ssm_D", "router_corr")  # kept in fp32 whatever the model dtype
+    F32 = ("sinks", "conv_w", "A_log", "dt_bias", "conv_b", "ssm_D", "router_corr", "act_params")  # kept in fp32 whatever the model dtype
 
     def __init__(self):
         for s in self.__slots__:
@@ -331,9 +333,11 @@ class DecoderLM:
         else:
             L.moe = False
             F = cfg.intermediate_size
-            if cfg.glu_epi in ("relu2", "gelu_tanh"):  # non-gated MLP: wgu holds the up projection only
+            if cfg.glu_epi in ("relu2", "gelu_tanh", "xielu"):  # non-gated MLP: wgu holds the up projection only
                 L.wgu = rows(rn(F, hd), self.F)
                 L.wd = cols(rn(hd, F))
+                if cfg.glu_epi == "xielu":
+                    L.act_params = torch.tensor([0.55, 0.55, 0.5, -1e-6], dtype=torch.float32, device=self.device)
                 return
             L.wgu = glu_pair(F, self.F, hd)
             L.wd = cols(rn(hd, F))
@@ -378,7 +382,10 @@ class DecoderLM:
         cfg = self.cfg
         if L.moe:
             return self._moe(L, h)
-        gu = ops.gemm(h, L.wgu, epi=cfg.glu_epi, bias=L.bgu)
+        if cfg.glu_epi == "xielu":
+            gu = ops.xielu(ops.gemm(h, L.wgu, bias=L.bgu), L.act_params)
+        else:
+            gu = ops.gemm(h, L.wgu, epi=cfg.glu_epi, bias=L.bgu)
         delta = ops.gemm(gu, L.wd, bias=L.bd if self.tp.rank == 0 else None)
         return self.tp.reduce(delta)
 

@@ -23,7 +23,9 @@ def register(*model_types, **traits):
 register("llama", "mistral", "smollm3", "helium", "granite", "hunyuan_v1_dense",
          "ernie4_5", "internlm2", "minicpm", "nanbeige", "laguna", "acereason", "mellum")
 # architectures whose distinguishing blocks are not built: refused instead of loaded wrongly
-_REFUSED = {"apertus": "the xIELU activation"}
+_REFUSED: dict[str, str] = {}
+# Apertus: Llama body with per-head q/k norms and a non-gated xIELU MLP (learned per-layer scalars)
+register("apertus", qk_norm=True, apertus=True)
 # post-sublayer norms only (no input norms), q/k RMSNorm over the whole projection
 register("olmo2", "olmo3", post_only_norms=True, qk_norm_full=True)
 # post-sublayer norms only, per-head q/k norms, local (L) / global (G) layer pattern, NoPE global layers
@@ -234,6 +236,9 @@ def build_config(hf: dict) -> DecoderConfig:
                                for i in range(cfg.num_layers)]
         cfg.layer_windows = None
         cfg.attn_output_gate = hf.get("attn_output_gate", True)
+    if tr.get("apertus"):
+        cfg.hidden_act = "xielu"
+        cfg.extra["norm_names"] = ("attention_layernorm", "feedforward_layernorm")
     if tr.get("post_only_norms"):
         cfg.pre_norms = False
         cfg.post_norms = True

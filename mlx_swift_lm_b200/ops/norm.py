@@ -128,3 +128,19 @@ def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None):
     _lib.check(rc, "silu_mul")
     _lib.count(1)
     return out
+
+
+def xielu(x: torch.Tensor, params: torch.Tensor) -> torch.Tensor:
+    """xIELU activation in place (Apertus MLPs). params = raw (alpha_p,
+    alpha_n, beta, eps) of the layer (fp32 [4]); see xielu_ref."""
+    if not x.is_cuda:
+        x.copy_(ref.xielu_ref(x, params))
+        return x
+    assert x.dtype == torch.bfloat16 and x.is_contiguous()
+    rc = _lib.lib().b200_xielu(x.data_ptr(), x.numel(), params.data_ptr(), _lib.stream_ptr(x.device))
+    _lib.check(rc, "xielu")
+    _lib.count(1)
+    return x
+
+
+_lib.register_signatures({"b200_xielu": (_lib.i32, [_lib.vp, _lib.i64, _lib.vp, _lib.vp])})

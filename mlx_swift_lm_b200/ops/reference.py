@@ -495,3 +495,15 @@ def short_conv_ref(P, cu, fresh, slot, conv_state, conv_w, conv_b):
         out[s0:s1] = P[s0:s1, C:2 * C].float() * acc
         conv_state[sl] = xx[-(taps - 1):].to(conv_state.dtype)
     return out.to(P.dtype)
+
+
+def xielu_ref(x, params):
+    """xIELU: a_p = softplus(alpha_p), a_n = beta + softplus(alpha_n);
+    x > 0 -> a_p x^2 + beta x, else a_n (exp(min(x, eps)) - 1) - a_n x + beta x."""
+    p = params.float()
+    ap = torch.nn.functional.softplus(p[0])
+    an = p[2] + torch.nn.functional.softplus(p[1])
+    beta, eps = p[2], p[3]
+    xf = x.float()
+    y = torch.where(xf > 0, ap * xf * xf + beta * xf, an * torch.expm1(torch.minimum(xf, eps)) - an * xf + beta * xf)
+    return y.to(x.dtype)

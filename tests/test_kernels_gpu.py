@@ -468,3 +468,13 @@ def test_gemm_qkv_rope_two_tile():
     torch.testing.assert_close(q2.float(), q1.float(), atol=2e-2, rtol=2e-2)
     torch.testing.assert_close(kc2.float(), kc1.float(), atol=6e-2, rtol=6e-2)
     assert torch.equal(vc2, vc1)
+
+
+def test_xielu_kernel_matches_oracle():
+    torch.manual_seed(2)
+    x = (torch.randn(37, 1000) * 3).to(torch.bfloat16)
+    p = torch.tensor([0.3, -0.2, 0.5, -1e-6])
+    want = ref.xielu_ref(x, p).float()
+    y = ops.xielu(x.to("cuda").contiguous(), p.to("cuda"))
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y.float().cpu(), want, atol=3e-2, rtol=2e-2)

@@ -99,3 +99,19 @@ def test_post_norm_block_math():
     mlp = (torch.nn.functional.silu(h @ g.T) * (h @ u.T)) @ L.wd.T
     out = rms(h + rms(mlp, L.post_ffn_norm), m.norm)
     torch.testing.assert_close(got, out, atol=2e-4, rtol=2e-4)
+
+
+def test_apertus_xielu_mlp():
+    from mlx_swift_lm_b200.ops.reference import xielu_ref
+
+    cfg = build_config(_hf("apertus"))
+    assert cfg.hidden_act == "xielu" and cfg.qk_norm and cfg.glu_epi == "xielu"
+    m = _engine_vs_dense(cfg)
+    L = m.layers[0]
+    assert L.act_params.shape == (4,) and L.wgu.shape[0] == cfg.intermediate_size
+    x = torch.linspace(-4, 4, 101)
+    p = torch.tensor([0.3, -0.2, 0.5, -1e-6])
+    y = xielu_ref(x, p)
+    ap, an = torch.nn.functional.softplus(p[0]), 0.5 + torch.nn.functional.softplus(p[1])
+    want = torch.where(x > 0, ap * x * x + 0.5 * x, an * (torch.exp(torch.clamp(x, max=-1e-6)) - 1) - an * x + 0.5 * x)
+    torch.testing.assert_close(y, want)
