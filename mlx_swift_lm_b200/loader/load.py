@@ -297,7 +297,9 @@ def _load_linear_attn(ck: CheckpointView, cfg, L, p):
     L.wo = ck.linear(la + "out_proj")
 
 
-_LFM2_RENAMES = ((".self_attn.out_proj.", ".self_attn.o_proj."), (".self_attn.q_layernorm.", ".self_attn.q_norm."),
+_LFM2_RENAMES = ((".feed_forward.expert_bias", ".mlp.gate.e_score_correction_bias"),
+                 (".feed_forward.gate.", ".mlp.gate."), (".feed_forward.experts.", ".mlp.experts."),
+                 (".self_attn.out_proj.", ".self_attn.o_proj."), (".self_attn.q_layernorm.", ".self_attn.q_norm."),
                  (".self_attn.k_layernorm.", ".self_attn.k_norm."), (".operator_norm.", ".input_layernorm."),
                  (".ffn_norm.", ".post_attention_layernorm."), (".feed_forward.w1.", ".mlp.gate_proj."),
                  (".feed_forward.w3.", ".mlp.up_proj."), (".feed_forward.w2.", ".mlp.down_proj."),
@@ -307,10 +309,28 @@ _LFM2_RENAMES = ((".self_attn.out_proj.", ".self_attn.o_proj."), (".self_attn.q_
 def _lfm2_names(tensors: dict) -> dict:
     """LFM2 tensor names -> the decoder's (operator / ffn norms, w1/w3/w2,
     out_proj and q/k layernorms of the attention layers, embedding_norm as
-    the final norm); the short-conv layers keep ``conv.*``."""
+    the final norm; LFM2-MoE routers, expert biases and experts); the
+    short-conv layers keep ``conv.*``."""
     out = {}
     for k, v in tensors.items():
         for a, b in _LFM2_RENAMES:
+            k = k.replace(a, b)
+        if ".mlp.experts." in k:
+            k = k.replace(".w1.", ".gate_proj.").replace(".w3.", ".up_proj.").replace(".w2.", ".down_proj.")
+        out[k] = v
+    return out
+
+
+_BAILING_RENAMES = (("word_embeddings.", "embed_tokens."), (".attention.query_key_value.", ".self_attn.qkv_proj."),
+                    (".attention.dense.", ".self_attn.o_proj."), (".attention.query_layernorm.", ".self_attn.q_norm."),
+                    (".attention.key_layernorm.", ".self_attn.k_norm."), (".mlp.gate.gate_proj.", ".mlp.gate."),
+                    (".mlp.gate.expert_bias", ".mlp.gate.e_score_correction_bias"))
+
+
+def _renamed(tensors: dict, renames) -> dict:
+    out = {}
+    for k, v in tensors.items():
+        for a, b in renames:
             k = k.replace(a, b)
         out[k] = v
     return out
@@ -449,6 +469,8 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
     r, w = tp.rank, tp.world
     if cfg.linear_kind == "short_conv":
         tensors = _lfm2_names(tensors)
+    if cfg.model_type == "bailing_moe":
+        tensors = _renamed(tensors, _BAILING_RENAMES)
     if cfg.model_type == "phi":
         return _build_phi(cfg, tensors, device, dtype)
     q = cfg.quantization if isinstance(cfg.quantization, dict) else None

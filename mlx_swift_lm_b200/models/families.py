@@ -58,6 +58,12 @@ register("nemotron_h", ssm="nemotron_h")
 register("granitemoehybrid", ssm="granite", moe=True, mixtral_names=False)
 register("mamba2", ssm="mamba2")
 register("lfm2", lfm2=True, qk_norm=True)
+# LFM2-MoE: LFM2 layers whose FFN is a sigmoid-routed MoE (expert-bias corrected selection)
+# after `num_dense_layers` dense ones
+register("lfm2_moe", lfm2=True, qk_norm=True, lfm2_moe=True)
+# Ling (Bailing MoE): fused query_key_value, optional q/k norms, partial rotary, sigmoid group-limited
+# routing with expert bias, shared experts after `first_k_dense_replace` dense layers
+register("bailing_moe", fused_qkv=True, bailing=True)
 register("phi", phi2=True)  # Phi-1.5 / Phi-2: parallel attention + MLP, LayerNorm, partial rotary  # Liquid LFM2: short-conv / attention hybrid
 
 _NEMOTRON_BLOCKS = {"mamba": "M", "attention": "*", "mlp": "-", "moe": "E"}
@@ -236,6 +242,30 @@ def build_config(hf: dict) -> DecoderConfig:
                                for i in range(cfg.num_layers)]
         cfg.layer_windows = None
         cfg.attn_output_gate = hf.get("attn_output_gate", True)
+    if tr.get("lfm2_moe") or tr.get("bailing"):
+        cfg.num_experts = hf.get("num_experts", 0)
+        cfg.num_experts_per_tok = hf.get("num_experts_per_tok", 2)
+        cfg.moe_intermediate_size = hf.get("moe_intermediate_size", cfg.intermediate_size)
+        cfg.norm_topk_prob = hf.get("norm_topk_prob", True)
+        cfg.routed_scaling_factor = float(hf.get("routed_scaling_factor", 1.0))
+        n_dense = hf.get("num_dense_layers", hf.get("first_k_dense_replace", 0))
+        cfg.moe_layers = [i >= n_dense for i in range(cfg.num_layers)]
+        sig = tr.get("lfm2_moe") or hf.get("score_function", "sigmoid") == "sigmoid" or \
+            hf.get("moe_router_enable_expert_bias", False)
+        cfg.router_mode = "sigmoid_group" if sig else "softmax_topk"
+        cfg.router_n_group = hf.get("n_group", 1) or 1
+        cfg.router_topk_group = hf.get("topk_group", 1) or 1
+    if tr.get("lfm2_moe"):
+        cfg.intermediate_size = hf.get("intermediate_size", cfg.intermediate_size)
+        cfg.extra["lfm2_moe"] = True
+    if tr.get("bailing"):
+        ns = hf.get("num_shared_experts") or 0
+        cfg.shared_expert_intermediate_size = (hf.get("moe_shared_expert_intermediate_size")
+                                               or cfg.moe_intermediate_size) * ns if ns else 0
+        cfg.qk_norm = bool(hf.get("use_qk_norm", False))
+        cfg.attention_bias = bool(hf.get("use_qkv_bias", False))
+        cfg.o_bias = bool(hf.get("use_bias", False))
+        cfg.tie_word_embeddings = hf.get("tie_word_embeddings", False)
     if tr.get("apertus"):
         cfg.hidden_act = "xielu"
         cfg.extra["norm_names"] = ("attention_layernorm", "feedforward_layernorm")

@@ -115,3 +115,33 @@ def test_apertus_xielu_mlp():
     ap, an = torch.nn.functional.softplus(p[0]), 0.5 + torch.nn.functional.softplus(p[1])
     want = torch.where(x > 0, ap * x * x + 0.5 * x, an * (torch.exp(torch.clamp(x, max=-1e-6)) - 1) - an * x + 0.5 * x)
     torch.testing.assert_close(y, want)
+
+
+def test_lfm2_moe_and_bailing_configs_run():
+    cfg = build_config(_hf("lfm2_moe", num_experts=8, num_experts_per_tok=2, moe_intermediate_size=64,
+                           num_dense_layers=1, use_expert_bias=True, routed_scaling_factor=2.0,
+                           layer_types=["conv", "full_attention", "conv", "full_attention"], conv_L_cache=3))
+    assert cfg.moe_layers == [False, True, True, True] and cfg.router_mode == "sigmoid_group"
+    assert cfg.routed_scaling_factor == 2.0
+    _engine_vs_dense(cfg)
+    cfg = build_config(_hf("bailing_moe", num_experts=8, num_experts_per_tok=2, moe_intermediate_size=64,
+                           first_k_dense_replace=1, num_shared_experts=1, use_qk_norm=True, n_group=2,
+                           topk_group=1, partial_rotary_factor=0.5))
+    assert cfg.qk_norm and cfg.shared_expert_intermediate_size == 64 and cfg.router_n_group == 2
+    assert cfg.partial_rotary_factor == 0.5 and cfg.extra["fused_qkv"]
+    _engine_vs_dense(cfg)
+
+
+def test_family_name_maps():
+    from mlx_swift_lm_b200.loader.load import _BAILING_RENAMES, _lfm2_names, _renamed
+
+    t = _lfm2_names({"model.layers.2.feed_forward.experts.3.w1.weight": 1, "model.layers.2.feed_forward.gate.weight": 2,
+                     "model.layers.2.feed_forward.expert_bias": 3, "model.layers.0.feed_forward.w2.weight": 4})
+    assert set(t) == {"model.layers.2.mlp.experts.3.gate_proj.weight", "model.layers.2.mlp.gate.weight",
+                      "model.layers.2.mlp.gate.e_score_correction_bias", "model.layers.0.mlp.down_proj.weight"}
+    t = _renamed({"model.word_embeddings.weight": 0, "model.layers.0.attention.query_key_value.weight": 1,
+                  "model.layers.0.attention.dense.weight": 2, "model.layers.1.mlp.gate.gate_proj.weight": 3,
+                  "model.layers.1.mlp.gate.expert_bias": 4}, _BAILING_RENAMES)
+    assert set(t) == {"model.embed_tokens.weight", "model.layers.0.self_attn.qkv_proj.weight",
+                      "model.layers.0.self_attn.o_proj.weight", "model.layers.1.mlp.gate.weight",
+                      "model.layers.1.mlp.gate.e_score_correction_bias"}
