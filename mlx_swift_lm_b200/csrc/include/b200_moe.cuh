@@ -1,7 +1,10 @@
 // Router top-k of one token by one warp, shared by the MoE kernels and the
 // expert-parallel dispatch.
 //
-// mode 0: softmax over all experts, take top-k, renormalise if norm_topk.
+// mode 0: softmax over all experts, take top-k, renormalise if norm_topk,
+//         times `scale`; with n_group > 1 only the `topk_group` groups with
+//         the highest best probability compete, the others' probabilities set
+//         to 0 (DeepSeek V2 group_limited_greedy, MLXLLM/Models/DeepseekV2.swift:252-274).
 // mode 1: top-k over the logits, softmax over the k (GPT-OSS).
 // mode 2: sigmoid scores; selection by score + correction bias within the
 //         `topk_group` groups (of n_group) whose two best biased scores sum
@@ -49,9 +52,15 @@ __device__ __forceinline__ void route_topk_warp(const float* __restrict__ lg, in
         so[i] = 0.f;
       }
     }
-    if (ex.n_group > 1) {
+  }
+  // group-limited selection: sigmoid_group ranks groups by the sum of their two
+  // best biased scores, softmax_topk (DeepSeek V2 group_limited_greedy) by the
+  // group's best logit, which orders groups as their best probability does
+  unsigned keep = 0xffffffffu;  // bit g: group g survives
+  if ((mode == 2 || mode == 0) && ex.n_group > 1) {
+    {
       const int gsz = E / ex.n_group;
-      unsigned keep = 0;  // bit g: group g survives
+      keep = 0;
       float gscore[32];
       for (int g = 0; g < ex.n_group; ++g) {
         // best and second best biased score of the group (the best's lowest id excluded once)
@@ -79,7 +88,7 @@ __device__ __forceinline__ void route_topk_warp(const float* __restrict__ lg, in
           if (e < E && e / gsz == g && e != i1) b2 = fmaxf(b2, v[i]);
         }
         b2 = warp_max(b2);
-        gscore[g] = b1 + (gsz > 1 ? b2 : 0.f);
+        gscore[g] = mode == 0 ? b1 : b1 + (gsz > 1 ? b2 : 0.f);
       }
       for (int j = 0; j < ex.topk_group && j < ex.n_group; ++j) {
         int bg = -1;
@@ -87,10 +96,11 @@ __device__ __forceinline__ void route_topk_warp(const float* __restrict__ lg, in
           if (!(keep >> g & 1u) && (bg < 0 || gscore[g] > gscore[bg])) bg = g;
         keep |= 1u << bg;
       }
-      for (int i = 0; i < per; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E && !(keep >> (e / gsz) & 1u)) v[i] = 0.f;
-      }
+      if (mode == 2)
+        for (int i = 0; i < per; ++i) {
+          const int e = lane + 32 * i;
+          if (e < E && !(keep >> (e / gsz) & 1u)) v[i] = 0.f;
+        }
     }
   }
   if (mode == 0) {
@@ -103,6 +113,13 @@ __device__ __forceinline__ void route_topk_warp(const float* __restrict__ lg, in
       }
     }
     denom = warp_sum(s);
+    if (ex.n_group > 1) {  // dropped groups' probabilities become 0 (still in the denominator)
+      const int gsz = E / ex.n_group;
+      for (int i = 0; i < per; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && !(keep >> (e / gsz) & 1u)) v[i] = 0.f;
+      }
+    }
   }
   float sel_v[16], sel_s[16];
   int sel_i[16];
@@ -151,7 +168,7 @@ __device__ __forceinline__ void route_topk_warp(const float* __restrict__ lg, in
       }
       for (int j = 0; j < k; ++j) {
         ids[j] = sel_i[j];
-        w[j] = norm_topk ? sel_v[j] / s : sel_v[j];
+        w[j] = (norm_topk ? sel_v[j] / s : sel_v[j]) * ex.scale;
       }
     } else {
       const float m0 = sel_v[0];

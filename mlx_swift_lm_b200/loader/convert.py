@@ -59,6 +59,20 @@ def to_hf_config(cfg, quantization: dict | None = None) -> dict:
                      topk_group=cfg.router_topk_group, routed_scaling_factor=cfg.routed_scaling_factor,
                      n_shared_experts=cfg.shared_expert_intermediate_size // max(cfg.moe_intermediate_size, 1),
                      use_qk_norm=cfg.qk_norm, scoring_func="sigmoid")
+    if cfg.extra.get("mla"):  # DeepSeek-style keys: latent attention dims and the router
+        e = cfg.extra
+        first = next((i for i, x in enumerate(cfg.moe_layers or []) if x), cfg.num_layers)
+        d.update(q_lora_rank=e["mla_q_lora"] or None, kv_lora_rank=e["mla_kv_lora"],
+                 qk_nope_head_dim=e["mla_qk_nope"], qk_rope_head_dim=e["mla_qk_rope"], v_head_dim=e["mla_v"],
+                 n_routed_experts=cfg.num_experts, first_k_dense_replace=first, n_group=cfg.router_n_group,
+                 topk_group=cfg.router_topk_group, routed_scaling_factor=cfg.routed_scaling_factor,
+                 n_shared_experts=cfg.shared_expert_intermediate_size // max(cfg.moe_intermediate_size, 1),
+                 norm_topk_prob=cfg.norm_topk_prob,
+                 scoring_func="sigmoid" if cfg.router_mode == "sigmoid_group" else "softmax",
+                 topk_method="group_limited_greedy" if cfg.router_n_group > 1 else "greedy")
+        d.pop("num_key_value_heads")
+        d.pop("head_dim")
+        d.pop("partial_rotary_factor", None)
     if cfg.layer_types:
         d.update(layer_types=list(cfg.layer_types), attn_output_gate=cfg.attn_output_gate,
                  linear_num_key_heads=cfg.linear_num_key_heads, linear_num_value_heads=cfg.linear_num_value_heads,
@@ -117,8 +131,18 @@ def export_tensors(model) -> dict[str, torch.Tensor]:
         else:
             out[p + "post_attention_layernorm.weight"] = _dense(L.ln2) - off
         a = p + "self_attn."
-        w = _dense(L.wqkv)
-        if L.linear:
+        w = _dense(L.wqkv) if L.wqkv is not None else None
+        if L.mla_kv_a is not None:
+            if L.mla_q_a is not None:
+                out[a + "q_a_proj.weight"] = _dense(L.mla_q_a)
+                out[a + "q_a_layernorm.weight"] = _dense(L.mla_q_a_norm)
+                out[a + "q_b_proj.weight"] = _dense(L.mla_q_b)
+            else:
+                out[a + "q_proj.weight"] = _dense(L.mla_q_b)
+            out[a + "kv_a_proj_with_mqa.weight"] = _dense(L.mla_kv_a)
+            out[a + "kv_a_layernorm.weight"] = _dense(L.mla_kv_a_norm)
+            out[a + "kv_b_proj.weight"] = _dense(L.mla_kv_b)
+        elif L.linear:
             _export_linear_attn(out, p + "linear_attn.", L, cfg)
         elif cfg.attn_output_gate:  # q_proj rows per head [q | gate]
             H, D = model.H, model.D
@@ -159,7 +183,8 @@ def export_tensors(model) -> dict[str, torch.Tensor]:
                 out[f"{mp}experts.{e}.down_proj.weight"] = _dense(de)
             if L.shared_gu is not None:
                 g, u = deinterleave_gate_up(_dense(L.shared_gu))
-                sp = mp + ("shared_experts." if cfg.router_mode == "sigmoid_group" else "shared_expert.")
+                sp = mp + ("shared_experts." if cfg.router_mode == "sigmoid_group" or cfg.extra.get("mla")
+                       else "shared_expert.")
                 out[sp + "gate_proj.weight"] = g
                 out[sp + "up_proj.weight"] = u
                 out[sp + "down_proj.weight"] = _dense(L.shared_d)

@@ -230,9 +230,40 @@ def _rows(w, idx: torch.Tensor):
     return w.select_rows(idx) if isinstance(w, QuantizedWeight) else w.index_select(0, idx)
 
 
+def _load_mla(ck: CheckpointView, cfg, L, a, norm):
+    """Multi-head latent attention projections (DeepSeek V2 / V3, GLM-4.7-Flash).
+    MLX conversions that split kv_b_proj into per-head ``embed_q`` [H, kv_lora,
+    qk_nope] and ``unembed_out`` [H, v_head, kv_lora]
+    (MLXLLM/Models/GLM4MOELite.swift:523-570) are put back together as
+    kv_b [H * (qk_nope + v_head), kv_lora]."""
+    from ..models import mla
+
+    ql, kl, nope, rope_d, vd = mla.mla_dims(cfg)
+    H = cfg.num_heads
+    if ck.has(a + "q_a_proj.weight"):
+        L.mla_q_a = ck.linear(a + "q_a_proj", packed=False)
+        L.mla_q_a_norm = norm(a + "q_a_layernorm.weight")
+        L.mla_q_b = ck.linear(a + "q_b_proj", packed=False)
+    else:
+        L.mla_q_b = ck.linear(a + "q_proj", packed=False)
+    L.mla_kv_a = ck.linear(a + "kv_a_proj_with_mqa", packed=False)
+    L.mla_kv_a_norm = norm(a + "kv_a_layernorm.weight")
+    if ck.has(a + "kv_b_proj.weight"):
+        L.mla_kv_b = ck.linear(a + "kv_b_proj", packed=False)
+    else:
+        wk = ck.linear(a + "embed_q", packed=False).reshape(H, kl, nope)
+        wv = ck.linear(a + "unembed_out", packed=False).reshape(H, vd, kl)
+        L.mla_kv_b = torch.cat([wk.transpose(1, 2), wv], 1).reshape(H * (nope + vd), kl).contiguous()
+    L.wo = ck.linear(a + "o_proj", packed=False)
+
+
 def _load_attention(ck: CheckpointView, cfg, L, a, norm, r, w):
     """q|k|v (and, for gated attention, the output gate after v), biases,
     q/k norms, o_proj and sinks of one attention layer."""
+    if cfg.extra.get("mla"):
+        if w > 1:
+            raise NotImplementedError("multi-head latent attention loads without tensor parallelism")
+        return _load_mla(ck, cfg, L, a, norm)
     if cfg.attn_output_gate:
         # q_proj rows per head: [q (D) | gate (D)] -> q | k | v | gate
         assert w == 1, "gated attention loads without tensor parallelism"

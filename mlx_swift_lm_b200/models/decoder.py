@@ -48,7 +48,10 @@ class LayerWeights:
                  # ParoQuant: activation rotations shared by the experts (gate/up input, down input)
                  "experts_rot_in", "experts_rot_mid",
                  # xIELU MLP activation: raw (alpha_p, alpha_n, beta, eps) of the layer (Apertus)
-                 "act_params")
+                 "act_params",
+                 # multi-head latent attention (DeepSeek V2 / V3): query LoRA down / norm / up, the
+                 # joint latent + shared rotary-key projection, its norm, and the per-head k_nope | v up
+                 "mla_q_a", "mla_q_a_norm", "mla_q_b", "mla_kv_a", "mla_kv_a_norm", "mla_kv_b")
 
     F32 = ("sinks", "conv_w", "A_log", "dt_bias", "conv_b", "ssm_D", "router_corr", "act_params")  # kept in fp32 whatever the model dtype
 
@@ -267,6 +270,19 @@ class DecoderLM:
                 if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
                     self.layers.append(L)
                 continue
+            if cfg.extra.get("mla"):
+                from . import mla
+
+                assert w == 1, "multi-head latent attention loads without tensor parallelism"
+                mla.init_random(self, L, rn, ones)
+                if cfg.post_norms:
+                    L.post_attn_norm = ones(hd)
+                    L.post_ffn_norm = ones(hd)
+                if L.block == "both":
+                    self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
+                if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
+                    self.layers.append(L)
+                continue
             wq, wk, wv = rn(cfg.q_size, hd), rn(cfg.kv_size, hd), rn(cfg.kv_size, hd)
             L.wqkv = torch.cat([rows(wq, self.H * D), kv_rows(wk), kv_rows(wv)], 0)
             if cfg.attn_output_gate:  # gate rows after q|k|v: the attention kernels read q|k|v only
@@ -468,6 +484,10 @@ class DecoderLM:
     def _attention(self, L, h, fb: ForwardBatch, kv, li: int, attn: torch.Tensor) -> torch.Tensor:
         """Paged attention of one layer (decode rows, then prefill chunks);
         returns the output projection (before the residual add)."""
+        if L.mla_kv_a is not None:
+            from . import mla
+
+            return mla.attention(self, L, h, fb, kv, li, attn)
         cfg = self.cfg
         T, nd = fb.num_tokens, fb.num_decode
         ki = self.kv_index[li] if self.kv_index else li
@@ -697,6 +717,10 @@ class DecoderLM:
                 rows = GdnRows(torch.tensor([0, Lq], **i32), torch.tensor([1 if p0 == 0 else 0], **i32),
                                torch.zeros(1, **i32), [0, Lq])
                 delta = self._attn_out(L, self._linear_body(L, ops.gemm(h, L.wqkv, bias=L.bqkv), rows, conv, ssm))
+            elif L.mla_kv_a is not None:
+                from . import mla
+
+                delta = mla.dense_attention(self, L, h, cache, li, positions)
             else:
                 qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
                 qn, kn = L.q_norm, L.k_norm

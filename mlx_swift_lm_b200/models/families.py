@@ -48,6 +48,8 @@ register("phi3", fused_qkv=True, fused_gate_up=True)
 register("gpt_oss", gpt_oss=True)
 register("glm4", fused_gate_up=True)
 register("glm4_moe", moe=True, deepseek_router=True)  # GLM-4.5 / 4.6 / 4.7
+# multi-head latent attention + DeepSeek routing (DeepSeek V2 / V3, GLM-4.7-Flash)
+register("deepseek_v2", "deepseek_v3", "glm4_moe_lite", moe=True, deepseek_router=True, mla=True)
 register("mistral3", "ministral3")  # the text model of Mistral 3 / Ministral 3 (Llama-4 query scaling)
 # Ministral 3 backbone under ``encoder.*`` with a ``diffusion_head``; block
 # mask-diffusion decoding (engine/block_diffusion.py)
@@ -383,6 +385,19 @@ def build_config(hf: dict) -> DecoderConfig:
         cfg.shared_expert_gate = False
         cfg.qk_norm = hf.get("use_qk_norm", False)
         cfg.attention_bias = hf.get("attention_bias", False)
+    if tr.get("mla"):
+        from . import mla
+
+        mla.config_from_hf(cfg, hf)
+        if mt == "deepseek_v2":
+            # softmax gate, greedy or group-limited greedy top-k, no renormalisation
+            # (MLXLLM/Models/DeepseekV2.swift:252-274)
+            if hf.get("scoring_func", "softmax") != "softmax":
+                raise NotImplementedError(f"DeepSeek V2 scoring_func {hf.get('scoring_func')!r} is not served")
+            cfg.norm_topk_prob = hf.get("norm_topk_prob", False)
+            cfg.router_mode = "softmax_topk"
+            if hf.get("topk_method", "greedy") != "group_limited_greedy":
+                cfg.router_n_group = cfg.router_topk_group = 1
     if tr.get("ssm"):
         _ssm_config(cfg, hf, tr["ssm"])
     if tr.get("diffusion"):

@@ -51,7 +51,8 @@ def route_topk(logits: torch.Tensor, k: int, mode: str = "softmax_topk", norm_to
                bias: torch.Tensor | None = None, n_group: int = 1, topk_group: int = 1, scale: float = 1.0):
     """Router top-k over fp32 logits [T, E]. softmax_topk: softmax over experts
     then top-k (optionally renormalised); topk_softmax: top-k logits then
-    softmax over the k; sigmoid_group: sigmoid scores, selection by score +
+    softmax over the k (softmax_topk and sigmoid_group weights are multiplied
+    by `scale`); sigmoid_group: sigmoid scores, selection by score +
     `bias` inside the `topk_group` best of `n_group` groups (group score =
     sum of its two best biased scores), weights = the chosen sigmoid scores
     (renormalised when `norm_topk` and k > 1) times `scale`. Returns
@@ -75,10 +76,17 @@ def route_topk(logits: torch.Tensor, k: int, mode: str = "softmax_topk", norm_to
     if mode == "sigmoid_group":
         return _route_sigmoid_group_ref(logits.float(), k, norm_topk, bias, n_group, topk_group, scale)
     p = torch.softmax(logits.float(), dim=-1)
-    w, idx = torch.topk(p, k, dim=-1)
+    if n_group > 1:  # group-limited greedy: groups ranked by their best probability
+        g = p.reshape(T, n_group, E // n_group)
+        keep = _stable_topk(g.max(-1).values, topk_group)
+        mask = torch.zeros(T, n_group, dtype=torch.bool, device=p.device)
+        mask.scatter_(1, keep, True)
+        p = torch.where(mask[..., None], g, torch.zeros_like(g)).reshape(T, E)
+    idx = _stable_topk(p, k)
+    w = torch.gather(p, 1, idx)
     if norm_topk:
         w = w / w.sum(-1, keepdim=True)
-    return w, idx
+    return w * scale, idx
 
 
 def _stable_topk(x: torch.Tensor, k: int):

@@ -110,8 +110,12 @@ def test_layernorm_family_matches_direct(tmp_path, kind):
     assert torch.allclose(got, want, atol=2e-3, rtol=1e-3), (got - want).abs().max()
 
 
-@pytest.mark.parametrize("mt", ["apertus"])
-def test_refused_architectures(mt):
+def test_refused_architectures():
+    """Variants outside what the families serve fail at config time."""
     with pytest.raises(NotImplementedError):
-        build_config({"model_type": mt, "vocab_size": 10, "hidden_size": 8, "num_hidden_layers": 1,
-                      "num_attention_heads": 1})
+        build_config({"model_type": "cohere", "vocab_size": 10, "hidden_size": 8, "num_hidden_layers": 1,
+                      "num_attention_heads": 1, "use_qk_norm": True})
+    with pytest.raises(NotImplementedError):
+        build_config({"model_type": "deepseek_v2", "vocab_size": 10, "hidden_size": 8, "num_hidden_layers": 1,
+                      "num_attention_heads": 1, "kv_lora_rank": 8, "qk_nope_head_dim": 8, "qk_rope_head_dim": 4,
+                      "v_head_dim": 8, "scoring_func": "sigmoid"})

@@ -28,6 +28,18 @@ def test_route_topk(mode, T, E, k):
     assert torch.allclose(w.cpu(), wr, atol=1e-5, rtol=1e-4)
 
 
+@pytest.mark.parametrize("E,G,TG,k", [(64, 8, 3, 6), (160, 8, 3, 6), (32, 4, 2, 4)])
+def test_route_softmax_group_limited(E, G, TG, k):
+    """DeepSeek V2 group-limited greedy gate (softmax, groups by best
+    probability, no renormalisation, routed scale) against the CPU oracle."""
+    torch.manual_seed(E + G)
+    lg = torch.randn(200, E, device=DEV) * 2
+    w, ids = moe.route_topk(lg, k, "softmax_topk", False, None, G, TG, 16.0)
+    wr, ir = moe.route_topk(lg.cpu(), k, "softmax_topk", False, None, G, TG, 16.0)
+    assert torch.equal(ids.long().cpu(), ir)
+    assert torch.allclose(w.cpu(), wr, atol=1e-5, rtol=1e-4)
+
+
 def test_route_topk_ties_pick_lower_id():
     lg = torch.zeros(4, 16, device=DEV)
     lg[:, 3] = 1.0
