@@ -180,18 +180,15 @@ class AdmissionLedger:
 
 
 def layer_kinds_for(model, kv_fp8: bool = False) -> list[LayerKind]:
-    """Layer kinds of a :class:`DecoderLM`: attention layers grouped by
-    (window, KV heads, head dim); linear-attention and FFN-only layers own no
-    paged KV (their state is the fixed per-request part)."""
+    """Layer kinds of a :class:`DecoderLM`: the layers that own paged KV,
+    grouped by (window, KV heads, head dim); linear-attention, FFN-only and
+    KV-sharing layers own none (recurrent state is the fixed per-request part)."""
     import torch
 
     es = 1 if kv_fp8 else torch.empty((), dtype=model.dtype).element_size()
     groups: dict[tuple, int] = {}
-    cfg = model.cfg
-    for li in range(cfg.num_layers):
-        if model.kv_index and model.kv_index[li] < 0:
-            continue
-        key = (cfg.window(li), model.KVH, model.D)
+    for kvh, d, w in model.kv_layer_geom():
+        key = (w, kvh, d)
         groups[key] = groups.get(key, 0) + 1
     return [LayerKind(n, kvh, d, es, window=w) for (w, kvh, d), n in sorted(groups.items())]
 

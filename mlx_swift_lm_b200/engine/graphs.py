@@ -98,8 +98,9 @@ class DecodeGraphRunner:
         if self._reserved:
             return
         m = self.model
-        SCRATCH.get(self.dev, "dec_acc", self.Bmax * m.H * self.max_parts * m.D)
-        SCRATCH.get(self.dev, "dec_ml", self.Bmax * m.H * self.max_parts * 2)
+        H, D = m.attn_scratch_dims()
+        SCRATCH.get(self.dev, "dec_acc", self.Bmax * H * self.max_parts * D)
+        SCRATCH.get(self.dev, "dec_ml", self.Bmax * H * self.max_parts * 2)
         merge_counters(self.dev, self.Bmax * max(m.KVH, 1))
         ops.WORKSPACE.reserve(self.dev, 512 << 20)
         self._reserved = True

@@ -153,7 +153,7 @@ def measure(model, kv=None, device=None) -> MemoryMeasurement:
     w = model_bytes(model)
     k = 0
     if kv is not None:
-        k = kv.k.numel() * kv.k.element_size() * 2
+        k = kv.slab_bytes
         if kv.rec is not None:
             k += kv.rec.conv.numel() * kv.rec.conv.element_size() + kv.rec.ssm.numel() * 4
     peak = torch.cuda.max_memory_allocated(device) if torch.cuda.is_available() else 0

@@ -1,9 +1,15 @@
 """Paged KV storage: one device slab per model, host-side page accounting.
 
 * :class:`PagedKVCache` owns the K and V slabs ``[layers, pages, KVH, 16, D]``
-  (bf16, or fp8-e4m3 with a per-layer per-KV-head scale) - a single slab
-  allocation for the whole model, never per-page buffers, as the reference's
+  (bf16, or fp8-e4m3 with a per-layer per-KV-head scale) - one slab
+  allocation per layer group, never per-page buffers, as the reference's
   ``PagedKVPool`` (ContinuousBatchingV2/Paged/PagedKVPool.swift:23-148).
+  Models whose attention layers differ in KV heads or head dim (Gemma 4:
+  sliding layers 256-dim, global layers 512-dim with their own KV-head count)
+  get one slab per distinct (KVH, D); the groups are co-indexed - page ``p``
+  of a sequence addresses page ``p`` of every group's slab - so a page table,
+  a slot and a prefix-cache entry cover every layer at once
+  (per-layer-kind geometry: ContinuousBatchingV2/LayerKindDerivation.swift:23-189).
 * :class:`SequenceKV` is one request's page list and token count, with
   growth, speculative rollback and release (PagedSequenceKV.swift:37-1072,
   rollback :412, commitSpeculativeWrite :348).
@@ -66,35 +72,60 @@ class RecurrentStatePool:
 
 class PagedKVCache:
     def __init__(self, num_layers: int, num_pages: int, num_kv_heads: int, head_dim: int,
-                 dtype=torch.bfloat16, device="cpu", kv_fp8: bool = False):
-        self.num_layers = num_layers
+                 dtype=torch.bfloat16, device="cpu", kv_fp8: bool = False, layer_shapes=None):
+        """`layer_shapes`: optional (KVH, D) of every KV layer; layers of one
+        shape share a slab. Default: every layer (num_kv_heads, head_dim)."""
+        shapes = [tuple(x) for x in layer_shapes] if layer_shapes else [(num_kv_heads, head_dim)] * num_layers
+        self.num_layers = len(shapes)
         self.num_pages = num_pages
-        self.kvh = num_kv_heads
-        self.head_dim = head_dim
         self.device = torch.device(device)
         self.kv_fp8 = kv_fp8
         sdt = torch.float8_e4m3fn if kv_fp8 else dtype
-        shape = (num_layers, num_pages, num_kv_heads, PAGE, head_dim)
-        self.k = torch.zeros(shape, dtype=sdt, device=self.device)
-        self.v = torch.zeros(shape, dtype=sdt, device=self.device)
+        # group g: layers of shape group_shapes[g]; _where[li] = (g, index within the group)
+        self.group_shapes: list[tuple[int, int]] = []
+        self._where: list[tuple[int, int]] = []
+        counts: dict[tuple[int, int], int] = {}
+        for sh in shapes:
+            if sh not in counts:
+                counts[sh] = 0
+                self.group_shapes.append(sh)
+            self._where.append((self.group_shapes.index(sh), counts[sh]))
+            counts[sh] += 1
+        self.gk, self.gv = [], []
+        for sh in self.group_shapes:
+            kvh, d = sh
+            shape = (counts[sh], num_pages, kvh, PAGE, d)
+            self.gk.append(torch.zeros(shape, dtype=sdt, device=self.device))
+            self.gv.append(torch.zeros(shape, dtype=sdt, device=self.device))
+        # the first group's slabs and geometry (single-group models: the whole cache)
+        self.k, self.v = self.gk[0], self.gv[0]
+        self.kvh, self.head_dim = self.group_shapes[0]
+        self.layer_shapes = shapes
+        kvh_max = max(k for k, _ in shapes)
         if kv_fp8:
             # per-layer, per-KV-head dequantisation scales (stored = x / scale)
-            self.k_scales = torch.ones((num_layers, num_kv_heads), dtype=torch.float32, device=self.device)
-            self.v_scales = torch.ones((num_layers, num_kv_heads), dtype=torch.float32, device=self.device)
+            self.k_scales = torch.ones((self.num_layers, kvh_max), dtype=torch.float32, device=self.device)
+            self.v_scales = torch.ones((self.num_layers, kvh_max), dtype=torch.float32, device=self.device)
         else:
             self.k_scales = self.v_scales = None
         self.pool = _b200host.PagePool(num_pages)
-        self.page_bytes = 2 * num_layers * num_kv_heads * PAGE * head_dim * self.k.element_size()
+        es = self.k.element_size()
+        self.page_bytes = sum(2 * kvh * PAGE * d * es for kvh, d in shapes)
         self.rec: RecurrentStatePool | None = None
 
+    @property
+    def slab_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.gk + self.gv)
+
     def layer(self, li: int):
-        return self.k[li], self.v[li]
+        g, j = self._where[li]
+        return self.gk[g][j], self.gv[g][j]
 
     def k_scale(self, li: int):
-        return None if self.k_scales is None else self.k_scales[li]
+        return None if self.k_scales is None else self.k_scales[li, :self.layer_shapes[li][0]]
 
     def v_scale(self, li: int):
-        return None if self.v_scales is None else self.v_scales[li]
+        return None if self.v_scales is None else self.v_scales[li, :self.layer_shapes[li][0]]
 
     def set_fp8_scales(self, k_scales: torch.Tensor, v_scales: torch.Tensor):
         self.k_scales.copy_(k_scales)
@@ -116,13 +147,18 @@ class PagedKVCache:
         dev = device or model.device
         dt = model.dtype
         es = 1 if kv_fp8 else torch.empty((), dtype=dt).element_size()
-        n_attn = getattr(model, "num_kv_layers", model.cfg.num_layers)
-        per_page = 2 * max(n_attn, 1) * model.KVH * PAGE * model.D * es
+        geom = model.kv_layer_geom() if hasattr(model, "kv_layer_geom") else None
+        shapes = [(kvh, d) for kvh, d, _ in geom] if geom else None
+        n_attn = len(shapes) if shapes else getattr(model, "num_kv_layers", model.cfg.num_layers)
+        if shapes:
+            per_page = sum(2 * kvh * PAGE * d * es for kvh, d in shapes)
+        else:
+            per_page = 2 * max(n_attn, 1) * model.KVH * PAGE * model.D * es
         if kv_bytes is not None:
             n = max(1, kv_bytes // per_page)
         else:
             n = cls.pages_for(max_tokens or 4096) + 1
-        c = cls(max(n_attn, 1), n, model.KVH, model.D, dt, dev, kv_fp8)
+        c = cls(max(n_attn, 1), n, model.KVH, model.D, dt, dev, kv_fp8, layer_shapes=shapes or None)
         n_lin = sum(1 for i in range(model.cfg.num_layers) if model.cfg.is_linear(i))
         if n_lin > 0:
             Hk, Dk, Hv, Dv = model.cfg.gdn_dims

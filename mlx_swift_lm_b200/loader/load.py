@@ -506,6 +506,12 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         return _build_phi(cfg, tensors, device, dtype)
     q = cfg.quantization if isinstance(cfg.quantization, dict) else None
     ck = CheckpointView(tensors, q, torch.float32, keep_quantized=keep_quantized and bool(q), hadamard=hadamard)
+    if cfg.extra.get("gemma4"):
+        from ..models import gemma4
+
+        if tp.world != 1:
+            raise NotImplementedError("Gemma 4 loads without tensor parallelism")
+        return gemma4.build_from_tensors(cfg, ck, tensors, device, dtype)
     if cfg.layer_types and any(cfg.is_linear(i) for i in range(cfg.num_layers)):
         assert tp.world == 1, "hybrid (linear-attention) models load without tensor parallelism"
         # HF-format Qwen3-Next / 3.5 checkpoints store zero-centred layer norms

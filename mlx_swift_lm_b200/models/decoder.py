@@ -51,9 +51,13 @@ class LayerWeights:
                  "act_params",
                  # multi-head latent attention (DeepSeek V2 / V3): query LoRA down / norm / up, the
                  # joint latent + shared rotary-key projection, its norm, and the per-head k_nope | v up
-                 "mla_q_a", "mla_q_a_norm", "mla_q_b", "mla_kv_a", "mla_kv_a_norm", "mla_kv_b")
+                 "mla_q_a", "mla_q_a_norm", "mla_q_b", "mla_kv_a", "mla_kv_a_norm", "mla_kv_b",
+                 # Gemma 4: router input scale and per-expert weight scales, the dense / expert branch
+                 # norms of the MoE block, the per-layer-input gate / projection / norm, the layer scalar
+                 "g4_router_scale", "g4_expert_scale", "g4_post_ffn1", "g4_pre_ffn2", "g4_post_ffn2",
+                 "ple_gate", "ple_proj", "ple_norm", "layer_scalar")
 
-    F32 = ("sinks", "conv_w", "A_log", "dt_bias", "conv_b", "ssm_D", "router_corr", "act_params")  # kept in fp32 whatever the model dtype
+    F32 = ("sinks", "conv_w", "A_log", "dt_bias", "conv_b", "ssm_D", "router_corr", "act_params", "layer_scalar")  # kept in fp32 whatever the model dtype
 
     def __init__(self):
         for s in self.__slots__:
@@ -131,6 +135,14 @@ class DenseKVCache:
 
 class DecoderLM:
     """A decoder-only language model with paged-KV and dense-KV forwards."""
+
+    def __new__(cls, cfg: DecoderConfig, *args, **kwargs):
+        # families whose layers differ in attention geometry have their own subclass
+        if cls is DecoderLM and cfg.extra.get("gemma4"):
+            from .gemma4 import Gemma4LM
+
+            cls = Gemma4LM
+        return super().__new__(cls)
 
     def __init__(self, cfg: DecoderConfig, device="cpu", dtype=torch.float32, tp: TensorParallel | None = None):
         self.cfg = cfg
@@ -798,10 +810,21 @@ class DecoderLM:
             m.layers.append(N)
         return m
 
+    def kv_layer_geom(self) -> list[tuple[int, int, int]]:
+        """(KV heads, head dim, window) of every layer that owns paged KV, in
+        KV-slab order."""
+        cfg = self.cfg
+        return [(self.KVH, self.D, cfg.window(li)) for li in range(cfg.num_layers)
+                if not self.kv_index or self.kv_index[li] >= 0]
+
+    def attn_scratch_dims(self) -> tuple[int, int]:
+        """(query heads, head dim) bounding every attention layer's split-KV scratch."""
+        return self.H, self.D
+
     def kv_bytes_per_token(self, kv_dtype=None) -> int:
         dt = kv_dtype or self.dtype
         es = torch.empty((), dtype=dt).element_size()
-        return 2 * self.num_kv_layers * self.KVH * self.D * es
+        return sum(2 * kvh * d * es for kvh, d, _ in self.kv_layer_geom())
 
     def to(self, device=None, dtype=None):
         device = torch.device(device) if device is not None else self.device

@@ -44,6 +44,7 @@ register("olmoe", moe=True, qk_norm=True)
 register("gemma", gemma=1)
 register("gemma2", gemma=2)
 register("gemma3", "gemma3_text", gemma=3)
+register("gemma4", "gemma4_text", gemma4=True)  # per-kind head dims, shared KV, per-layer inputs, MoE block
 register("phi3", fused_qkv=True, fused_gate_up=True)
 register("gpt_oss", gpt_oss=True)
 register("glm4", fused_gate_up=True)
@@ -398,6 +399,10 @@ def build_config(hf: dict) -> DecoderConfig:
             cfg.router_mode = "softmax_topk"
             if hf.get("topk_method", "greedy") != "group_limited_greedy":
                 cfg.router_n_group = cfg.router_topk_group = 1
+    if tr.get("gemma4"):
+        from . import gemma4
+
+        gemma4.config_from_hf(cfg, hf)
     if tr.get("ssm"):
         _ssm_config(cfg, hf, tr["ssm"])
     if tr.get("diffusion"):
