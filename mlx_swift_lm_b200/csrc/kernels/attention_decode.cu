@@ -619,6 +619,7 @@ int b200_paged_decode_merge(const float* part_acc, const float* part_ml, const i
     case 64: e = launch_k(paged_decode_merge_kernel<64>, grid, dim3(128), 0, st, 1, a, B); break;
     case 128: e = launch_k(paged_decode_merge_kernel<128>, grid, dim3(128), 0, st, 1, a, B); break;
     case 256: e = launch_k(paged_decode_merge_kernel<256>, grid, dim3(128), 0, st, 1, a, B); break;
+    case 512: e = launch_k(paged_decode_merge_kernel<512>, grid, dim3(128), 0, st, 1, a, B); break;
     default: return -1;
   }
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();

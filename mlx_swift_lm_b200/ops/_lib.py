@@ -62,13 +62,15 @@ _SIGS = {
     "b200_paged_decode_mma": (i32, [vp, vp, vp, vp, i32, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, f32,
                                     i64, vp]),
     "b200_paged_decode_merge": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+    "b200_paged_decode_wide_part": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32,
+                                          i32, f32, f32, i64, vp]),
     "b200_set_pdl": (None, [i32]),
     "b200_get_pdl": (i32, []),
 }
 
 # status accessors exported per translation unit
 _STATUS_TAGS = ["gemm", "norm", "attn_decode", "attn_prefill_simt", "sampling", "misc", "attn_decode_mma",
-                "attn_prefill_mma", "attn_prefill_tc"]
+                "attn_prefill_mma", "attn_prefill_tc", "attn_wide"]
 
 
 class KernelLibraryMissing(RuntimeError):

@@ -77,6 +77,19 @@ def paged_decode(q, k_cache, v_cache, page_table, seq_lens, scale, window=0, sin
     ml = SCRATCH.get(q.device, "dec_ml", B * H * max_parts * 2)
     kv_fp8 = k_cache.dtype == torch.float8_e4m3fn
     L = _lib.lib()
+    if D == 512:  # wide heads: lanes split the head dim, then the common merge pass
+        st = _lib.stream_ptr(q.device)
+        rc = L.b200_paged_decode_wide_part(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), 1 if kv_fp8 else 0,
+                                           _lib.ptr(k_scale), _lib.ptr(v_scale), page_table.data_ptr(),
+                                           page_table.stride(0), seq_lens.data_ptr(), acc.data_ptr(), ml.data_ptr(),
+                                           B, H, KVH, D, max_parts, int(window), float(scale), float(softcap),
+                                           k_cache.shape[0], st)
+        _lib.check(rc, "paged_decode_wide_part")
+        rc = L.b200_paged_decode_merge(acc.data_ptr(), ml.data_ptr(), seq_lens.data_ptr(), _lib.ptr(sinks),
+                                       out.data_ptr(), B, H, D, max_parts, int(window), st)
+        _lib.check(rc, "paged_decode_merge")
+        _lib.count(2)
+        return out
     if not kv_fp8 and D in (64, 128, 256) and H // KVH <= (16 if D < 256 else 8) and USE_MMA_DECODE[0]:
         st = _lib.stream_ptr(q.device)
         if not USE_FUSED_MERGE[0]:
@@ -156,6 +169,11 @@ def paged_prefill(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0
         out = torch.empty_like(q)
     if cu_q_host is None:
         cu_q_host = cu_q.tolist()
+    if D == 512:
+        if window < 0:
+            raise ValueError("bidirectional attention is not served at head dim 512")
+        return _prefill_wide(q, k_cache, v_cache, page_table, cu_q_host, q_pos0, scale, window, sinks, softcap,
+                             k_scale, v_scale, out)
     if USE_TC_PREFILL[0] and k_scale is None and k_cache.dtype == torch.bfloat16 and D in (64, 128):
         # tcgen05 kernel: 128-query tiles of one head, longest rows first
         tiles = prefill_tiles_mma(cu_q_host, 128)
@@ -189,6 +207,33 @@ def paged_prefill(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0
         D, int(window), float(scale), float(softcap), k_cache.shape[0], _lib.stream_ptr(q.device))
     _lib.check(rc, "paged_prefill")
     _lib.count(1)
+    return out
+
+
+WIDE_PREFILL_SLICE = 128  # query tokens per partition pass (bounds the split-KV scratch)
+
+
+def _prefill_wide(q, k_cache, v_cache, page_table, cu_q_host, q_pos0, scale, window, sinks, softcap, k_scale,
+                  v_scale, out):
+    """Prefill at head dim 512: every chunk token is a decode row of its own
+    (its row's page table, context = its position + 1), attended by the wide
+    decode kernel in slices of WIDE_PREFILL_SLICE tokens. The chunk's K/V are
+    already in the pages, so each token sees exactly its causal (windowed)
+    history, as the prefill kernels do."""
+    T = q.shape[0]
+    dev = q.device
+    R = len(cu_q_host) - 1
+    counts = torch.tensor([cu_q_host[r + 1] - cu_q_host[r] for r in range(R)], dtype=torch.int64)
+    row = torch.repeat_interleave(torch.arange(R), counts).to(dev, non_blocking=True)
+    start = torch.tensor(cu_q_host[:-1], dtype=torch.int64).to(dev, non_blocking=True)
+    offs = torch.arange(T, device=dev, dtype=torch.int64) - start[row]
+    seq_lens = (q_pos0.long()[row] + offs + 1).to(torch.int32)
+    pt = page_table.index_select(0, row)
+    max_parts = decode_max_parts(page_table.shape[1] * 16)
+    for t0 in range(0, T, WIDE_PREFILL_SLICE):
+        t1 = min(T, t0 + WIDE_PREFILL_SLICE)
+        paged_decode(q[t0:t1], k_cache, v_cache, pt[t0:t1], seq_lens[t0:t1], scale, window, sinks, softcap,
+                     k_scale, v_scale, max_parts, out=out[t0:t1])
     return out
 
 

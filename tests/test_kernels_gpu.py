@@ -195,6 +195,57 @@ def test_paged_decode_batch_invariance():
         assert torch.equal(one[0], full[b])
 
 
+@pytest.mark.parametrize("H,KVH", [(8, 1), (16, 4), (2, 2), (32, 2)])
+@pytest.mark.parametrize("window,sinks,softcap,fp8", [(0, False, 0.0, False), (100, True, 0.0, False),
+                                                      (0, False, 30.0, False), (0, False, 0.0, True)])
+def test_paged_decode_wide(H, KVH, window, sinks, softcap, fp8):
+    """Head dim 512 (Gemma 4 global layers): lanes split the head dim."""
+    torch.manual_seed(18)
+    D = 512
+    lens = [1, 16, 17, 256, 257, 900]
+    B = len(lens)
+    P = sum((l + 15) // 16 for l in lens) + 4
+    kc, vc, pt = _make_paged(B, lens, KVH, D, P, torch.float32)
+    ks = vs = None
+    if fp8:
+        ks, vs = torch.rand(KVH) + 0.5, torch.rand(KVH) + 0.5
+        kc = (kc / ks[None, :, None, None]).to(torch.float8_e4m3fn)
+        vc = (vc / vs[None, :, None, None]).to(torch.float8_e4m3fn)
+    else:
+        kc, vc = kc.to(torch.bfloat16), vc.to(torch.bfloat16)
+    q = torch.randn(B, H, D, dtype=torch.bfloat16)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    sk = torch.randn(H) if sinks else None
+    scale = D ** -0.5
+    r = ref.paged_decode_ref(q, kc, vc, pt, sl, scale, window, sk, softcap, ks, vs)
+    y = ops.paged_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), pt.to(DEV), sl.to(DEV), scale, window,
+                         None if sk is None else sk.to(DEV), softcap, None if ks is None else ks.to(DEV),
+                         None if vs is None else vs.to(DEV))
+    assert _lib.read_status().get("attn_wide", 0) == 0
+    assert _rel(y.cpu(), r) < 1e-2
+
+
+@pytest.mark.parametrize("window", [0, 40])
+def test_paged_prefill_wide(window):
+    """Head dim 512 prefill: each chunk token attends as a decode row."""
+    torch.manual_seed(19)
+    H, KVH, D = 8, 1, 512
+    rows = [(0, 37), (100, 64), (16, 1), (250, 300)]
+    lens = [h + c for h, c in rows]
+    P = sum((l + 15) // 16 for l in lens) + 3
+    kc, vc, pt = _make_paged(len(rows), lens, KVH, D, P)
+    cu = [0]
+    for h, c in rows:
+        cu.append(cu[-1] + c)
+    q = torch.randn(cu[-1], H, D, dtype=torch.bfloat16)
+    cu_t = torch.tensor(cu, dtype=torch.int32)
+    p0 = torch.tensor([h for h, _ in rows], dtype=torch.int32)
+    r = ref.paged_prefill_ref(q, kc, vc, pt, cu_t, p0, 1.0 / 16, window, None, 0.0)
+    y = ops.paged_prefill(q.to(DEV), kc.to(DEV), vc.to(DEV), pt.to(DEV), cu_t.to(DEV), p0.to(DEV), 1.0 / 16,
+                          window, cu_q_host=cu)
+    assert _rel(y.cpu(), r) < 1e-2
+
+
 @pytest.mark.parametrize("kernel", ["tc", "mma", "simt"])
 @pytest.mark.parametrize("H,KVH,D", [(32, 8, 128), (4, 2, 64), (64, 8, 64), (8, 2, 256)])
 @pytest.mark.parametrize("window,sinks,softcap", [(0, False, 0.0), (64, True, 0.0), (0, False, 30.0),
