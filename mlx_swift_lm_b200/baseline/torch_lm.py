@@ -37,6 +37,8 @@ PAGE = 16
 class TorchDecoderLM(DecoderLM):
     """:class:`DecoderLM` with every op replaced by a PyTorch / cuBLAS / NCCL call."""
 
+    supports_window_ring = False  # attention reads the row-wide page tables only
+
     scratch_page = None
     graph_sampling = False  # its engine sampler is greedy-only
 

@@ -69,6 +69,9 @@ class EngineConfig:
     chained_decode: bool = True
     enable_prefix_cache: bool = False
     prefix_block_size: int = 256
+    # ring storage for sliding-window layers (window + one step of pages per
+    # request instead of the whole context); None: on unless prefix caching is
+    window_ring: bool | None = None
     step_timeout_s: float = 30.0  # watchdog (background mode)
     admission_timeout_s: float = 0.0  # legacy knobs, folded into `leases` when set
     decode_progress_timeout_s: float = 0.0
@@ -162,20 +165,25 @@ class EngineV2:
             from ..kv.memory import kv_budget_bytes
 
             self.cfg.kv_bytes = kv_budget_bytes(self.device, self.cfg.kv_memory_fraction)
+        ring_chunk = self._window_ring_chunk(model)
         if self.cfg.kv_bytes is not None:
-            self.kv = PagedKVCache.for_model(model, kv_bytes=self.cfg.kv_bytes, kv_fp8=self.cfg.kv_fp8, max_seqs=seqs)
+            self.kv = PagedKVCache.for_model(model, kv_bytes=self.cfg.kv_bytes, kv_fp8=self.cfg.kv_fp8, max_seqs=seqs,
+                                             ring_chunk=ring_chunk, max_len=self.cfg.max_model_len)
         else:
-            self.kv = PagedKVCache.for_model(model, max_tokens=kv_tokens, kv_fp8=self.cfg.kv_fp8, max_seqs=seqs)
+            self.kv = PagedKVCache.for_model(model, max_tokens=kv_tokens, kv_fp8=self.cfg.kv_fp8, max_seqs=seqs,
+                                             ring_chunk=ring_chunk, max_len=self.cfg.max_model_len)
         self.prefix_cache = None
-        # a recurrent state cannot be rebuilt from shared KV pages: no prefix
-        # reuse for hybrid models (their prompts are always computed in full)
-        if self.cfg.enable_prefix_cache and self.kv.rec is None:
+        # a recurrent state cannot be rebuilt from shared KV pages, nor can an
+        # overwritten window ring: no prefix reuse for hybrid models or ring storage
+        if self.cfg.enable_prefix_cache and self.kv.rec is None and not self.kv.ring_pages:
             from ..kv.prefix_cache import PrefixCache
 
             self.prefix_cache = PrefixCache(self.kv, self.cfg.prefix_block_size)
         from .admission import AdmissionConfig, AdmissionLedger, layer_kinds_for
 
         rec_bytes = self.kv.rec.bytes_per_seq if self.kv.rec is not None else 0
+        # a ring-storage request holds a fixed number of ring pages whatever its length
+        rec_bytes += self.kv.ring_pages * self.kv.ring_page_bytes
         cap = self.kv.num_pages * self.kv.page_bytes + rec_bytes * seqs
         self.ledger = AdmissionLedger(layer_kinds_for(model, self.cfg.kv_fp8), cap,
                                       self.cfg.admission or AdmissionConfig(fixed_bytes_per_request=rec_bytes))
@@ -220,12 +228,31 @@ class EngineV2:
         d = Diagnostics()
         self.diagnostics = d if d.profile else None  # opt-in (B200LM_STEP_PROFILE=1 or assign one)
 
+    def _window_ring_chunk(self, model) -> int:
+        """Tokens one step may write for a sequence when sliding-window layers
+        get ring storage, else 0. Ring storage is on by default where it
+        applies (``EngineConfig.window_ring`` None), and off with prefix
+        caching (ring pages are overwritten, so they cannot be shared) or for
+        models whose forward does not route per-layer tables."""
+        on = self.cfg.window_ring
+        if on is None:
+            on = not self.cfg.enable_prefix_cache
+        if not on or not getattr(model, "supports_window_ring", False):
+            return 0
+        if model.tp.world != 1 or getattr(model, "pp_stages", 1) != 1:
+            return 0
+        sc = self.cfg.scheduler
+        return max(sc.prefill_chunk_size, 1) + 1
+
     def enable_mtp(self, module, config=None):
         """Speculative decoding with an MTP draft module (greedy rows)."""
         from .mtp import MTPDriver
 
         if self.kv.rec is not None:
             raise ValueError("MTP rollback needs per-position recurrent states; hybrid models decode without MTP")
+        if self.kv.ring_pages:
+            raise ValueError("MTP verification does not route ring-storage page tables; build the engine with "
+                             "EngineConfig(window_ring=False)")
 
         self.mtp = MTPDriver(self, module, config)
         # the draft module's own paged KV is per-token auxiliary memory of every request
@@ -306,6 +333,14 @@ class EngineV2:
         fb = ForwardBatch(input_ids=torch.tensor(ids, dtype=torch.int32), positions=torch.tensor(pos, dtype=torch.int32),
                           slots=torch.tensor(slots, dtype=torch.int64), num_decode=nd)
         maxp = max(len(r.state.seq.pages) for r in rows)
+        if self.kv.ring_pages:  # sliding-window ring layers: their own slots and logical page tables
+            fb.ring_slots = torch.tensor([s for r in rows for s in r.state.seq.ring_slots(r.start, r.num_tokens)],
+                                         dtype=torch.int64)
+            tabs = [r.state.seq.ring_table(maxp) for r in rows]
+            if nd:
+                fb.ring_dec_page_table = torch.from_numpy(np.stack(tabs[:nd]))
+            if len(rows) > nd:
+                fb.ring_pf_page_table = torch.from_numpy(np.stack(tabs[nd:]))
         logit_idx = []
         off = 0
         for r in rows:
@@ -346,7 +381,8 @@ class EngineV2:
             fb.state_slots = torch.tensor([r.state.seq.state_slot for r in rows], dtype=torch.int32)
         if dev.type == "cuda":
             for name in ("input_ids", "positions", "slots", "dec_page_table", "dec_seq_lens", "pf_cu_q", "pf_pos0",
-                         "pf_page_table", "logit_idx", "state_slots"):
+                         "pf_page_table", "logit_idx", "state_slots", "ring_slots", "ring_dec_page_table",
+                         "ring_pf_page_table"):
                 t = getattr(fb, name)
                 if t is not None:
                     self.h2d_bytes += t.numel() * t.element_size()
@@ -790,6 +826,11 @@ class EngineV2:
                               pf_page_table=pt.to(dev))
             if self.kv.rec is not None:
                 fb.state_slots = torch.tensor([st.seq.state_slot], dtype=torch.int32).to(dev)
+            if self.kv.ring_pages:
+                if len(tokens) > self.kv.ring_pages * 16 - self.model.cfg.max_window():
+                    raise ValueError("a one-shot prefill longer than the window ring; use window_ring=False")
+                fb.ring_slots = torch.tensor(st.seq.ring_slots(0, len(tokens)), dtype=torch.int64).to(dev)
+                fb.ring_pf_page_table = torch.from_numpy(st.seq.ring_table(len(st.seq.pages))[None]).to(dev)
             logits = self.model.forward(fb, self.kv)
             return logits.argmax(-1).tolist()
         finally:

@@ -54,6 +54,12 @@ class DecodeGraphRunner:
         self.o_temp = self.o_step + 2 * B
         self.o_topk, self.o_topp, self.o_minp = self.o_temp + B, self.o_temp + 2 * B, self.o_temp + 3 * B
         self.n_i32 = self.o_temp + 4 * B
+        # sliding-window ring layers: ring slots (int64) | ring page table
+        self.ring = engine.kv.ring_pages > 0
+        if self.ring:
+            self.o_rslots = self.n_i32 + self.n_i32 % 2
+            self.o_rpt = self.o_rslots + 2 * B
+            self.n_i32 = self.o_rpt + B * P
         self.rec = engine.kv.rec
         self.packed = torch.zeros(self.n_i32, dtype=torch.int32, device=self.dev)
         self.staging = [torch.zeros(self.n_i32, dtype=torch.int32).pin_memory() for _ in range(2)]
@@ -72,6 +78,9 @@ class DecodeGraphRunner:
         self.s_topk = self.packed[self.o_topk:self.o_topk + B]
         self.s_topp = self.packed[self.o_topp:self.o_topp + B].view(torch.float32)
         self.s_minp = self.packed[self.o_minp:self.o_minp + B].view(torch.float32)
+        if self.ring:
+            self.rslots = self.packed[self.o_rslots:self.o_rslots + 2 * B].view(torch.int64)
+            self.rpt = self.packed[self.o_rpt:self.o_rpt + B * P].view(B, P)
         # sampled rows (temperature / top-k / top-p / min-p) run a second graph per bucket
         # whose last kernel draws from the logits instead of taking the argmax
         self.sampling = self._supports_sampling()
@@ -106,9 +115,12 @@ class DecodeGraphRunner:
         self._reserved = True
 
     def _fb(self, B):
-        return ForwardBatch(input_ids=self.ids[:B], positions=self.pos[:B], slots=self.slots[:B], num_decode=B,
-                            dec_page_table=self.pt[:B], dec_seq_lens=self.sl[:B], dec_max_parts=self.max_parts,
-                            state_slots=self.ss[:B] if self.rec is not None else None)
+        fb = ForwardBatch(input_ids=self.ids[:B], positions=self.pos[:B], slots=self.slots[:B], num_decode=B,
+                          dec_page_table=self.pt[:B], dec_seq_lens=self.sl[:B], dec_max_parts=self.max_parts,
+                          state_slots=self.ss[:B] if self.rec is not None else None)
+        if self.ring:
+            fb.ring_slots, fb.ring_dec_page_table = self.rslots[:B], self.rpt[:B]
+        return fb
 
     def _supports_sampling(self) -> bool:
         """Sampled graphs need the full logits on every rank: not the fused TP
@@ -131,6 +143,8 @@ class DecodeGraphRunner:
         if self.rec is not None:
             self.ss.fill_(self.rec.scratch)
         self.slots.fill_(-1)
+        if self.ring:
+            self.rslots.fill_(-1)
         self.sl.zero_()
         self.pos.zero_()
         self.ids.zero_()
@@ -224,6 +238,10 @@ class DecodeGraphRunner:
         a[self.o_hid:self.o_hid + Bb] = 0
         slots = a[self.o_slots:self.o_slots + 2 * self.Bmax].view(np.int64)
         slots[:Bb] = -1
+        if self.ring:
+            rslots = a[self.o_rslots:self.o_rslots + 2 * self.Bmax].view(np.int64)
+            rslots[:Bb] = -1
+            rpt = a[self.o_rpt:self.o_rpt + self.Bmax * P].reshape(self.Bmax, P)
         if self.rec is not None:
             a[self.o_ss:self.o_ss + Bb] = self.rec.scratch
         pt = a[self.o_pt:self.o_pt + self.Bmax * P].reshape(self.Bmax, P)
@@ -252,6 +270,9 @@ class DecodeGraphRunner:
                 a[self.o_ss + i] = st.seq.state_slot
             pg = st.seq.pages
             pt[i, :len(pg)] = pg
+            if self.ring:
+                rslots[i] = st.seq.ring_slot(p)
+                rpt[i] = st.seq.ring_table(P)
             if sampled:
                 sp = st.req.sampling
                 keys[i] = row_key(st)

@@ -44,6 +44,16 @@ class ForwardBatch:
     rope_table: torch.Tensor | None = None
     # prefill rows attend to their whole chunk (mask-diffusion blocks) instead of causally
     bidirectional: bool = False
+    # sliding-window ring layers (kv.paged ring storage): their own slots and page tables
+    ring_slots: torch.Tensor | None = None  # [T] int64
+    ring_dec_page_table: torch.Tensor | None = None  # [Bd, maxp] int32
+    ring_pf_page_table: torch.Tensor | None = None  # [R, maxp] int32
+
+    def tables(self, kv, ki: int):
+        """(slots, decode page table, prefill page table) of KV layer ki."""
+        if self.ring_slots is not None and kv.is_ring(ki):
+            return self.ring_slots, self.ring_dec_page_table, self.ring_pf_page_table
+        return self.slots, self.dec_page_table, self.pf_page_table
 
     @property
     def num_tokens(self) -> int:

@@ -111,6 +111,9 @@ class DecoderConfig:
             return 0
         return int(self.layer_windows[layer])
 
+    def max_window(self) -> int:
+        return max((int(w) for w in self.layer_windows or ()), default=0)
+
     def is_linear(self, layer: int) -> bool:
         return bool(self.layer_types) and self.layer_types[layer] in ("linear_attention", "mamba", "conv")
 

@@ -136,6 +136,9 @@ class DenseKVCache:
 class DecoderLM:
     """A decoder-only language model with paged-KV and dense-KV forwards."""
 
+    # the paged forward routes each KV layer's slots and page tables through ForwardBatch.tables
+    supports_window_ring = True
+
     def __new__(cls, cfg: DecoderConfig, *args, **kwargs):
         # families whose layers differ in attention geometry have their own subclass
         if cls is DecoderLM and cfg.extra.get("gemma4"):
@@ -510,8 +513,9 @@ class DecoderLM:
             cos_sin = fb.rope_table
             positions = torch.arange(T, dtype=torch.int32, device=fb.positions.device)
         qkv = None
+        slots, dec_pt, pf_pt = fb.tables(kv, ki)
         if self._fused_qkv_rope(L, h, fb, rot_dim):
-            q = ops.gemm_qkv_rope(h, L.wqkv, L.bqkv, positions, fb.slots, cos_sin, L.q_norm, L.k_norm,
+            q = ops.gemm_qkv_rope(h, L.wqkv, L.bqkv, positions, slots, cos_sin, L.q_norm, L.k_norm,
                                   cfg.rms_norm_eps, kc, vc, self.H, self.KVH, kv.k_scale(ki), kv.v_scale(ki))
         else:
             qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
@@ -519,17 +523,17 @@ class DecoderLM:
             if cfg.qk_norm_full:
                 qkv = self._qk_full_norm(L, qkv)
                 qn = kn = None
-            q = ops.qk_norm_rope_kv(qkv, positions, fb.slots, cos_sin, rot_dim, cfg.rope_interleaved,
+            q = ops.qk_norm_rope_kv(qkv, positions, slots, cos_sin, rot_dim, cfg.rope_interleaved,
                                     qn, kn, cfg.rms_norm_eps, kc, vc, self.H, self.KVH, self.D,
                                     kv.k_scale(ki), kv.v_scale(ki))
         q = self._pos_scale_q(q, fb.positions)
         win = cfg.window(li)
         if nd:
-            ops.paged_decode(q[:nd], kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, win, L.sinks,
+            ops.paged_decode(q[:nd], kc, vc, dec_pt, fb.dec_seq_lens, cfg.scale, win, L.sinks,
                              cfg.attn_logit_softcap, kv.k_scale(ki), kv.v_scale(ki), fb.dec_max_parts,
                              out=attn[:nd])
         if T > nd:
-            ops.paged_prefill(q[nd:], kc, vc, fb.pf_page_table, fb.pf_cu_q, fb.pf_pos0, cfg.scale,
+            ops.paged_prefill(q[nd:], kc, vc, pf_pt, fb.pf_cu_q, fb.pf_pos0, cfg.scale,
                               -1 if fb.bidirectional else win, L.sinks,
                               cfg.attn_logit_softcap, kv.k_scale(ki), kv.v_scale(ki), fb.pf_cu_q_host,
                               out=attn[nd:])

@@ -307,17 +307,19 @@ class Gemma4LM(DecoderLM):
             ki = self.kv_index[li]
             kc, vc = kv.layer(ki)
             cs, rd = self._rope(li)
-            slots = fb.slots if self.kv_owner[li] else torch.full_like(fb.slots, -1)
+            slots, dec_pt, pf_pt = fb.tables(kv, ki)
+            if not self.kv_owner[li]:
+                slots = torch.full_like(slots, -1)
             q = ops.qk_norm_rope_kv(packed, fb.positions, slots, cs, rd, False, L.q_norm, L.k_norm,
                                     cfg.rms_norm_eps, kc, vc, H, kvh, D, kv.k_scale(ki), kv.v_scale(ki))
             if D not in bufs:
                 bufs[D] = torch.empty((T, H, D), dtype=x.dtype, device=x.device)
             attn = bufs[D]
             if nd:
-                ops.paged_decode(q[:nd], kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, win, None, 0.0,
+                ops.paged_decode(q[:nd], kc, vc, dec_pt, fb.dec_seq_lens, cfg.scale, win, None, 0.0,
                                  kv.k_scale(ki), kv.v_scale(ki), fb.dec_max_parts, out=attn[:nd])
             if T > nd:
-                ops.paged_prefill(q[nd:], kc, vc, fb.pf_page_table, fb.pf_cu_q, fb.pf_pos0, cfg.scale, win, None,
+                ops.paged_prefill(q[nd:], kc, vc, pf_pt, fb.pf_cu_q, fb.pf_pos0, cfg.scale, win, None,
                                   0.0, kv.k_scale(ki), kv.v_scale(ki), fb.pf_cu_q_host, out=attn[nd:])
             a = ops.gemm(attn.view(T, H * D), L.wo)
             x = self._block_tail(L, li, x, a, ple)

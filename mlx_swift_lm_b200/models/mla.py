@@ -103,14 +103,15 @@ def attention(model, L, h, fb, kv_cache, li: int, attn):
     kc, vc = kv_cache.layer(ki)
     # append K/V at the tokens' slots (no further norm / rotary: rot_dim 0)
     packed = torch.cat([q.reshape(T, H * Dp), k.reshape(T, H * Dp), v.reshape(T, H * Dp)], 1)
-    q = ops.qk_norm_rope_kv(packed, fb.positions, fb.slots, model.cos_sin, 0, False, None, None, cfg.rms_norm_eps,
+    slots, dec_pt, pf_pt = fb.tables(kv_cache, ki)
+    q = ops.qk_norm_rope_kv(packed, fb.positions, slots, model.cos_sin, 0, False, None, None, cfg.rms_norm_eps,
                             kc, vc, H, H, Dp, kv_cache.k_scale(ki), kv_cache.v_scale(ki))
     win = cfg.window(li)
     if nd:
-        ops.paged_decode(q[:nd], kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, win, None, 0.0,
+        ops.paged_decode(q[:nd], kc, vc, dec_pt, fb.dec_seq_lens, cfg.scale, win, None, 0.0,
                          kv_cache.k_scale(ki), kv_cache.v_scale(ki), fb.dec_max_parts, out=attn[:nd])
     if T > nd:
-        ops.paged_prefill(q[nd:], kc, vc, fb.pf_page_table, fb.pf_cu_q, fb.pf_pos0, cfg.scale, win, None, 0.0,
+        ops.paged_prefill(q[nd:], kc, vc, pf_pt, fb.pf_cu_q, fb.pf_pos0, cfg.scale, win, None, 0.0,
                           kv_cache.k_scale(ki), kv_cache.v_scale(ki), fb.pf_cu_q_host, out=attn[nd:])
     a2 = attn.view(T, H, Dp)[..., :vd].reshape(T, H * vd).contiguous()
     return model._attn_out(L, a2)
