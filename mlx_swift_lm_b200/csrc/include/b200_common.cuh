@@ -43,6 +43,30 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ void set_status(unsigned code) { atomicOr(&g_status, code); }
 
+// CHECKED builds (-DB200_CHECKED=1, the libb200kernels_checked.so variant)
+// add bounds checks that the release build leaves out of the hot loops; a
+// failed check records kErrBounds in the unit's status word and the access
+// is redirected to a safe index instead of trapping.
+#ifndef B200_CHECKED
+#define B200_CHECKED 0
+#endif
+
+// Page id of entry `idx` of a row's page table: a page id outside the slab
+// (always) or an entry past the row's `ld_pt` entries (CHECKED builds)
+// records kErrBounds and reads page 0.
+__device__ __forceinline__ int64_t checked_page(const int* row_table, int idx, int ld_pt, int64_t num_pages) {
+  if (B200_CHECKED && (idx < 0 || idx >= ld_pt)) {
+    set_status(kErrBounds);
+    return 0;
+  }
+  int64_t page = row_table[idx];
+  if (page < 0 || page >= num_pages) {
+    set_status(kErrBounds);
+    page = 0;
+  }
+  return page;
+}
+
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

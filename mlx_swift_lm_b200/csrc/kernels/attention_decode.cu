@@ -153,11 +153,7 @@ __global__ void __launch_bounds__(128) paged_decode_part_kernel(DecodeArgs a) {
   const int* pt = a.page_table + (size_t)b * a.ld_pt;
   auto issue = [&](int i) {
     const int s = i % kStages;
-    int64_t page = pt[pg_lo + i];
-    if (page < 0 || page >= a.num_pages) {
-      set_status(kErrBounds);
-      page = 0;
-    }
+    const int64_t page = checked_page(pt, pg_lo + i, a.ld_pt, a.num_pages);
     const size_t off = ((size_t)page * a.KVH + kvh) * kPage * D;
     mbar_arrive_expect_tx(bar0 + 8 * s, 2 * kPageBytes);
     bulk_copy_g2s(smem_u32(ring[s][0]), kc + off, kPageBytes, bar0 + 8 * s);
@@ -368,11 +364,7 @@ __global__ void __launch_bounds__(128) paged_decode_stream_kernel(DecodeArgs a) 
   const bool producer = (hg == 0 && lane == 0);
   auto issue = [&](int i) {  // i-th page of this stream
     const int s = i % NST;
-    int64_t page = pt[pg_lo + ps + i * PS];
-    if (page < 0 || page >= a.num_pages) {
-      set_status(kErrBounds);
-      page = 0;
-    }
+    const int64_t page = checked_page(pt, pg_lo + ps + i * PS, a.ld_pt, a.num_pages);
     const size_t off = ((size_t)page * a.KVH + kvh) * kPage * D;
     const uint32_t fb = smem_u32(&full_bar[ps][s]);
     mbar_arrive_expect_tx(fb, 2 * kPageBytes);

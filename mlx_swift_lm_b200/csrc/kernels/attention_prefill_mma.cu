@@ -142,11 +142,7 @@ __global__ void __launch_bounds__(128) prefill_mma_kernel(const __grid_constant_
   const int* pt = a.page_table + (size_t)row * a.ld_pt;
   auto issue = [&](int i) {
     const int s = i % kNst;
-    int64_t page = pt[pg_lo + i];
-    if (page < 0 || page >= a.num_pages) {
-      set_status(kErrBounds);
-      page = 0;
-    }
+    const int64_t page = checked_page(pt, pg_lo + i, a.ld_pt, a.num_pages);
     const int krow = (int)((page * a.KVH + kvh) * kPage);
     const uint32_t fb = smem_u32(&full_bar[s]);
     mbar_arrive_expect_tx(fb, 2 * kTile);

@@ -68,11 +68,7 @@ __global__ void __launch_bounds__(128) paged_prefill_simt_kernel(PrefillArgs a) 
 
   const int* pt = a.page_table + (size_t)row * a.ld_pt;
   for (int pg = tile_lo / 16; pg <= tile_hi / 16; ++pg) {
-    int64_t page = pt[pg];
-    if (page < 0 || page >= a.num_pages) {
-      if (threadIdx.x == 0) set_status(kErrBounds);
-      page = 0;
-    }
+    const int64_t page = checked_page(pt, pg, a.ld_pt, a.num_pages);
     __syncthreads();
     const size_t off = ((size_t)page * a.KVH + kvh) * 16 * D;
     for (int i = threadIdx.x * 8; i < 16 * D; i += blockDim.x * 8) {

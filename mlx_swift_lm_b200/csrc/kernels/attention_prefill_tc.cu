@@ -136,11 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         mbar_arrive_expect_tx(fb, S::kStage);
         for (int p = 0; p < kKB / kPage; ++p) {
           const int lp = min(max((kb_lo + j) * (kKB / kPage) + p, pg_lo), pg_hi);
-          int64_t page = pt[lp];
-          if (page < 0 || page >= a.num_pages) {
-            set_status(kErrBounds);
-            page = 0;
-          }
+          const int64_t page = checked_page(pt, lp, a.ld_pt, a.num_pages);
           const int r = (int)((page * a.KVH + kvh) * kPage);
 #pragma unroll
           for (int h = 0; h < NB; ++h) {

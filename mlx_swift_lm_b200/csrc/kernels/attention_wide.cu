@@ -125,11 +125,7 @@ __global__ void __launch_bounds__(128) wide_decode_part_kernel(Args a) {
   auto stage = [&](int s, int kv) { return ring_raw + (s * 2 + kv) * kPageBytes; };
   auto issue = [&](int i) {
     const int s = i % kStages;
-    int64_t page = pt[pg_lo + i];
-    if (page < 0 || page >= a.num_pages) {
-      set_status(kErrBounds);
-      page = 0;
-    }
+    const int64_t page = checked_page(pt, pg_lo + i, a.ld_pt, a.num_pages);
     const size_t off = ((size_t)page * a.KVH + kvh) * kPage * D;
     mbar_arrive_expect_tx(bar0 + 8 * s, 2 * kPageBytes);
     bulk_page(smem_u32(stage(s, 0)), kc + off, kPageBytes, bar0 + 8 * s);

@@ -14,7 +14,9 @@ import threading
 import torch
 
 _PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(_PKG, "_lib", "libb200kernels.so")
+# B200LM_CHECKED=1: the bounds-checked build of the same kernels
+CHECKED = os.environ.get("B200LM_CHECKED", "0") == "1"
+LIB_PATH = os.path.join(_PKG, "_lib", "libb200kernels_checked.so" if CHECKED else "libb200kernels.so")
 
 _lock = threading.Lock()
 _lib = None
