@@ -72,7 +72,7 @@ _SIGS = {
 
 # status accessors exported per translation unit
 _STATUS_TAGS = ["gemm", "norm", "attn_decode", "attn_prefill_simt", "sampling", "misc", "attn_decode_mma",
-                "attn_prefill_mma", "attn_prefill_tc", "attn_wide"]
+                "attn_prefill_mma", "attn_wide"]
 
 
 class KernelLibraryMissing(RuntimeError):

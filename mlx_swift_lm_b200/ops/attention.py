@@ -123,9 +123,6 @@ def paged_decode(q, k_cache, v_cache, page_table, seq_lens, scale, window=0, sin
 
 
 USE_MMA_PREFILL = [True]  # tests flip it to cover the CUDA-core kernel
-# tcgen05 prefill attention (S / O in tensor memory) for head dims 64 / 128 with bf16 pages;
-# B200LM_TC_PREFILL=0 selects the mma.sync kernel
-USE_TC_PREFILL = [os.environ.get("B200LM_TC_PREFILL", "0") == "1"]
 
 
 def prefill_tiles_mma(cu_q: list[int], qt: int = 64) -> list[tuple[int, int]]:
@@ -174,18 +171,6 @@ def paged_prefill(q, k_cache, v_cache, page_table, cu_q, q_pos0, scale, window=0
             raise ValueError("bidirectional attention is not served at head dim 512")
         return _prefill_wide(q, k_cache, v_cache, page_table, cu_q_host, q_pos0, scale, window, sinks, softcap,
                              k_scale, v_scale, out)
-    if USE_TC_PREFILL[0] and k_scale is None and k_cache.dtype == torch.bfloat16 and D in (64, 128):
-        # tcgen05 kernel: 128-query tiles of one head, longest rows first
-        tiles = prefill_tiles_mma(cu_q_host, 128)
-        tiles_t = torch.tensor(tiles, dtype=torch.int32).pin_memory().to(q.device, non_blocking=True)
-        qc = q if q.is_contiguous() else q.contiguous()
-        rc = _lib.lib().b200_paged_prefill_tc(
-            qc.data_ptr(), T, k_cache.data_ptr(), v_cache.data_ptr(), page_table.data_ptr(), page_table.stride(0),
-            cu_q.data_ptr(), q_pos0.data_ptr(), tiles_t.data_ptr(), len(tiles), _lib.ptr(sinks), out.data_ptr(), H,
-            KVH, D, int(window), float(scale), float(softcap), k_cache.shape[0], _lib.stream_ptr(q.device))
-        _lib.check(rc, "paged_prefill_tc")
-        _lib.count(1)
-        return out
     if USE_MMA_PREFILL[0] and k_scale is None and k_cache.dtype == torch.bfloat16 and D in (64, 128, 256):
         # tensor-core kernel: 64-query tiles of one head, longest rows first
         tiles = prefill_tiles_mma(cu_q_host)
@@ -238,9 +223,6 @@ def _prefill_wide(q, k_cache, v_cache, page_table, cu_q_host, q_pos0, scale, win
 
 
 _lib.register_signatures({
-    "b200_paged_prefill_tc": (_lib.i32, [_lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.vp,
-                                         _lib.vp, _lib.i32, _lib.vp, _lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.i32,
-                                         _lib.f32, _lib.f32, _lib.i64, _lib.vp]),
     "b200_paged_selected_decode": (_lib.i32, [_lib.vp, _lib.vp, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.vp,
                                               _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.f32, _lib.vp,
                                               _lib.vp]),

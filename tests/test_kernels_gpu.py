@@ -246,7 +246,7 @@ def test_paged_prefill_wide(window):
     assert _rel(y.cpu(), r) < 1e-2
 
 
-@pytest.mark.parametrize("kernel", ["tc", "mma", "simt"])
+@pytest.mark.parametrize("kernel", ["mma", "simt"])
 @pytest.mark.parametrize("H,KVH,D", [(32, 8, 128), (4, 2, 64), (64, 8, 64), (8, 2, 256)])
 @pytest.mark.parametrize("window,sinks,softcap", [(0, False, 0.0), (64, True, 0.0), (0, False, 30.0),
                                                   (-1, False, 0.0), (300, False, 0.0)])
@@ -255,8 +255,6 @@ def test_paged_prefill(kernel, H, KVH, D, window, sinks, softcap):
 
     if kernel == "simt" and D == 256:
         pytest.skip("the CUDA-core prefill kernel takes D <= 128")
-    if kernel == "tc" and D == 256:
-        pytest.skip("the tcgen05 prefill kernel takes D 64 / 128")
     if kernel == "simt" and window < 0:
         pytest.skip("bidirectional prefill runs on the tensor-core kernels")
     torch.manual_seed(11)
@@ -275,15 +273,11 @@ def test_paged_prefill(kernel, H, KVH, D, window, sinks, softcap):
     sk = torch.randn(H) if sinks else None
     r = ref.paged_prefill_ref(q, kc, vc, pt, cu_t, p0, D ** -0.5, window, sk, softcap)
     att.USE_MMA_PREFILL[0] = kernel != "simt"
-    tc0 = att.USE_TC_PREFILL[0]
-    att.USE_TC_PREFILL[0] = kernel == "tc"
     try:
         y = ops.paged_prefill(q.to(DEV), kc.to(DEV), vc.to(DEV), pt.to(DEV), cu_t.to(DEV), p0.to(DEV), D ** -0.5,
                               window, None if sk is None else sk.to(DEV), softcap, cu_q_host=cu)
     finally:
         att.USE_MMA_PREFILL[0] = True
-        att.USE_TC_PREFILL[0] = tc0
-    assert _lib.read_status().get("attn_prefill_tc", 0) == 0
     assert _rel(y.cpu(), r) < 1e-2
 
 
