@@ -35,6 +35,13 @@ def test_gemma4_engine_on_gpu(variant):
                                                  num_global_key_value_heads=2, enable_moe_block=True,
                                                  num_experts=8, top_k_experts=2, moe_intermediate_size=128)
     m = DecoderLM(build_config(hf), DEV, torch.bfloat16).init_random(0, std=0.05)
+    # attention scale is 1: unit q/k norm weights make random-init scores ~N(0, D) and the
+    # softmax an argmax that bf16 rounding flips; D^-1/4 on each keeps them O(1)
+    for li, L in enumerate(m.layers):
+        d = m.geom(li)[1]
+        L.q_norm.mul_(d ** -0.25)
+        if L.k_norm is not None:
+            L.k_norm.mul_(d ** -0.25)
     g = torch.Generator().manual_seed(1)
     ps = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (9, 40, 77)]
 
