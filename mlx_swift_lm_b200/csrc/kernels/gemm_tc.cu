@@ -760,30 +760,20 @@ static const CollArgs& local_coll() {
 
 // Split count S (1..8, the cluster size) for a weight of N rows and K inputs.
 // A function of (N, K) only: every M uses the same K partition and the same
-// reduction order. Skinny (decode) GEMMs stream the weight once, so the grid
-// should fill the machine's CTA slots (ctas_per_sm per SM) in a single wave:
-// among the S whose grid fits one wave and whose splits keep at least 6 K
-// blocks, take the one that occupies the most slots, less 2% per extra split
-// (partial sums cost DSMEM traffic and a cluster reduction). Non-power-of-two
-// clusters are allowed (any size up to 8 is portable).
+// reduction order. Chosen so skinny (decode) GEMMs fill the machine with about
+// two CTAs per SM while every split keeps at least 8 K blocks.
+// Powers of two only (clusters of 2/4/8 pack into GPCs without stranding
+// slots), the largest that keeps the grid within one wave of ~90% of the
+// 2-per-SM CTA slots and at least 8 K blocks per split.
 static int choose_splits(int N, int K, int num_sms, int ctas_per_sm = 2) {
   const int kb = (K + 63) / 64;
-  const long tiles = (N + 127) / 128;
-  const long slots = (long)ctas_per_sm * num_sms;
-  int best = 1;
-  double best_score = (double)tiles / slots;
-  for (int s = 2; s <= 8; ++s) {
-    const int per = (kb + s - 1) / s;
-    if (per < 6) break;
-    if ((long)per * (s - 1) >= kb) continue;  // the last split must own a K block
-    if (tiles * s > slots) break;              // one wave only
-    const double score = (double)(tiles * s) / slots - 0.02 * (s - 1);
-    if (score > best_score) {
-      best_score = score;
-      best = s;
-    }
-  }
-  return best;
+  const int tiles = (N + 127) / 128;
+  const long budget = (long)(0.9 * ctas_per_sm * num_sms);
+  int s = 1;
+  while (s < 8 && (long)tiles * (s * 2) <= budget && (kb + 2 * s - 1) / (2 * s) >= 8) s *= 2;
+  // the last split must own at least one K block
+  while (s > 1 && (long)((kb + s - 1) / s) * (s - 1) >= kb) s /= 2;
+  return s;
 }
 
 // Split count of the quantised GEMM (one CTA per SM): the largest S <= 8
