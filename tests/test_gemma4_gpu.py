@@ -58,3 +58,22 @@ def test_gemma4_engine_on_gpu(variant):
     mc = m.clone_to("cpu", torch.float32)
     r = mc.forward_dense(p, mc.new_cache())
     assert ((lg - r).norm() / r.norm()).item() < 0.05
+
+
+def test_gemma4_moe_block_and_router_on_gpu():
+    """The MoE feed-forward of one layer (router on the normed residual with
+    per-expert scales, GeGLU experts, the dense branch and the four norms) on
+    the GPU against the fp32 CPU restatement of the same weights."""
+    hf = _hf(hidden_size_per_layer_input=0, num_kv_shared_layers=0, use_double_wide_mlp=False,
+             enable_moe_block=True, num_experts=8, top_k_experts=2, moe_intermediate_size=128)
+    m = DecoderLM(build_config(hf), DEV, torch.bfloat16).init_random(3, std=0.05)
+    L = m.layers[0]
+    L.router.mul_(8.0)
+    mc = m.clone_to("cpu", torch.float32)
+    x = (torch.randn(37, 256, generator=torch.Generator().manual_seed(5)) * 0.5).to(torch.bfloat16)
+    w, idx = m._route(L, x.to(DEV))
+    wc, ic = mc._route(mc.layers[0], x.float())
+    assert torch.equal(idx.long().cpu().sort(-1).values, ic.long().sort(-1).values)
+    y = m._ffn(L, x.to(DEV)).float().cpu()
+    yc = mc._ffn(mc.layers[0], x.float())
+    assert ((y - yc).norm() / yc.norm()).item() < 0.03
