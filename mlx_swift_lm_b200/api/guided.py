@@ -1,8 +1,11 @@
 """Guided (grammar-constrained) generation.
 
-Front ends lower to the native engine's regular-expression dialect
-(csrc/host/grammar.cpp, a byte-level lazily determinised automaton with
-per-state token masks):
+Two native engines: a pushdown (context-free) matcher over EBNF rules
+(csrc/host/grammar_pda.cpp; :class:`CfgConstraint`, the default for JSON
+objects, JSON schemas and EBNF grammars - recursion is kept, not unrolled)
+and a byte-level lazily determinised regex automaton (csrc/host/grammar.cpp;
+:class:`GrammarConstraint`, for regex requests). Front ends of the regex
+engine:
   * :func:`json_schema_to_regex` - objects (properties in declaration order,
     required / optional), arrays (min/max items), strings (enum, const,
     pattern, min/max length), integers, numbers, booleans, null, anyOf / oneOf,
@@ -275,14 +278,253 @@ def constraint_factory(vocab: GrammarVocabulary):
     def make(rf: dict):
         t = rf.get("type")
         if t == "json_object":
-            return GrammarConstraint.json_object(vocab)
+            return CfgConstraint.json_object(vocab)
         if t == "json_schema":
             js = rf.get("json_schema", {})
-            return GrammarConstraint.from_json_schema(vocab, js.get("schema", js))
+            return CfgConstraint.from_json_schema(vocab, js.get("schema", js))
         if t == "regex":
             return GrammarConstraint(vocab, rf["regex"])
         if t == "grammar":
-            return GrammarConstraint.from_ebnf(vocab, rf["grammar"])
+            return CfgConstraint.from_ebnf(vocab, rf["grammar"], rf.get("root", "root"))
         return None
 
     return make
+
+
+# ----------------------------------------------------------------------------- context-free front ends
+# The pushdown engine (csrc/host/grammar_pda.cpp) takes EBNF rules directly, so
+# recursive schemas and grammars need no unrolling.
+JSON_EBNF_BASE = r'''
+ws ::= [ \n]?
+json-char ::= [^"\\\x00-\x1f] | "\\" ( ["\\/bfnrt] | "u" [0-9a-fA-F]{4} )
+json-string ::= "\"" json-char* "\""
+json-int ::= "-"? ( "0" | [1-9] [0-9]{0,15} )
+json-number ::= json-int ( "." [0-9]{1,16} )? ( [eE] [+-]? [0-9]{1,3} )?
+json-bool ::= "true" | "false"
+json-null ::= "null"
+json-value ::= json-object | json-array | json-string | json-number | json-bool | json-null
+json-object ::= "{" ws ( json-string ws ":" ws json-value ( ws "," ws json-string ws ":" ws json-value )* )? ws "}"
+json-array ::= "[" ws ( json-value ( ws "," ws json-value )* )? ws "]"
+'''
+
+
+def _ebnf_lit(s: str) -> str:
+    """A quoted EBNF literal of the text s."""
+    out = ['"']
+    for ch in s:
+        o = ord(ch)
+        if ch in '"\\':
+            out.append("\\" + ch)
+        elif o < 0x20:
+            out.append(f"\\x{o:02x}")
+        else:
+            out.append(ch)
+    out.append('"')
+    return "".join(out)
+
+
+_RX_ESC = {"d": "[0-9]", "w": "[A-Za-z0-9_]", "s": "[ \\t\\n\\r]", "D": "[^0-9]", "W": "[^A-Za-z0-9_]",
+           "S": "[^ \\t\\n\\r]", "n": '"\\n"', "t": '"\\t"', "r": '"\\r"'}
+
+
+def regex_to_ebnf(rx: str) -> str:
+    """The EBNF body of a (JSON-schema ``pattern`` style) regular expression:
+    literals become quoted strings, classes / groups / alternation /
+    quantifiers carry over, anchors are dropped."""
+    out, i, n = [], 0, len(rx)
+    while i < n:
+        c = rx[i]
+        if c in "^$" and (i == 0 or i == n - 1):
+            i += 1
+        elif c == "[":
+            j = i + 1
+            if j < n and rx[j] == "^":
+                j += 1
+            if j < n and rx[j] == "]":
+                j += 1
+            while j < n and rx[j] != "]":
+                j += 2 if rx[j] == "\\" else 1
+            out.append(rx[i:j + 1])
+            i = j + 1
+        elif c == "\\" and i + 1 < n:
+            e = rx[i + 1]
+            out.append(_RX_ESC.get(e, _ebnf_lit(e)))
+            i += 2
+        elif c in "()|*+?":
+            out.append(c)
+            i += 1
+        elif c == "{":
+            j = rx.index("}", i)
+            out.append(rx[i:j + 1])
+            i = j + 1
+        elif c == ".":
+            out.append("[^\\n]")
+            i += 1
+        else:
+            out.append(_ebnf_lit(c))
+            i += 1
+    return " ".join(out) if out else '""'
+
+
+class _SchemaEbnf:
+    def __init__(self, schema: dict):
+        self.root_schema = schema
+        self.defs = schema.get("$defs", schema.get("definitions", {}))
+        self.rules: dict[str, str] = {}
+        self.ref_rules: dict[str, str] = {}
+        self.n = 0
+
+    def new(self, hint: str) -> str:
+        self.n += 1
+        return f"s{self.n}-{re.sub(r'[^A-Za-z0-9]', '', hint)[:16] or 'x'}"
+
+    def rule(self, schema, hint="v") -> str:
+        """Name of a rule matching `schema`."""
+        if isinstance(schema, bool):
+            return "json-value" if schema else self._never()
+        if "$ref" in schema:
+            ref = schema["$ref"]
+            if ref in self.ref_rules:
+                return self.ref_rules[ref]
+            name = self.new(ref.split("/")[-1])
+            self.ref_rules[ref] = name  # registered before the body: recursion refers to it
+            target = self.root_schema if ref == "#" else self.defs[ref.split("/")[-1]]
+            self.rules[name] = self.rule(target, ref.split("/")[-1])
+            return name
+        body = self.body(schema, hint)
+        name = self.new(hint)
+        self.rules[name] = body
+        return name
+
+    def _never(self) -> str:
+        self.rules.setdefault("never", "[^\\x00-\\xff]")  # an empty byte class
+        return "never"
+
+    def body(self, schema: dict, hint: str) -> str:
+        if "const" in schema:
+            return _ebnf_lit(json.dumps(schema["const"]))
+        if "enum" in schema:
+            return " | ".join(_ebnf_lit(json.dumps(v)) for v in schema["enum"])
+        for key in ("anyOf", "oneOf"):
+            if key in schema:
+                return " | ".join(self.rule(s, hint) for s in schema[key])
+        if "allOf" in schema:  # merged shallowly: properties and required of every part
+            merged: dict = {}
+            for part in schema["allOf"]:
+                part = self.defs[part["$ref"].split("/")[-1]] if "$ref" in part else part
+                for k, v in part.items():
+                    if k == "properties":
+                        merged.setdefault("properties", {}).update(v)
+                    elif k == "required":
+                        merged.setdefault("required", []).extend(v)
+                    else:
+                        merged[k] = v
+            return self.body(merged, hint)
+        t = schema.get("type")
+        if isinstance(t, list):
+            return " | ".join(self.rule({**schema, "type": x}, hint) for x in t)
+        if t == "object" or (t is None and "properties" in schema):
+            return self.obj(schema, hint)
+        if t == "array" or (t is None and "items" in schema):
+            return self.arr(schema, hint)
+        if t == "string":
+            return self.string(schema)
+        if t == "integer":
+            return "json-int"
+        if t == "number":
+            return "json-number"
+        if t == "boolean":
+            return "json-bool"
+        if t == "null":
+            return "json-null"
+        return "json-value"
+
+    def obj(self, schema, hint):
+        props = schema.get("properties", {})
+        extra = schema.get("additionalProperties", not props)
+        if not props:
+            if extra is False:
+                return '"{" ws "}"'
+            val = "json-value" if extra in (True, None) or extra == {} else self.rule(extra, hint + "v")
+            kv = f"json-string ws \":\" ws {val}"
+            return f'"{{" ws ( {kv} ( ws "," ws {kv} )* )? ws "}}"'
+        required = set(schema.get("required", []))
+        parts = [(f"{_ebnf_lit(json.dumps(name))} ws \":\" ws {self.rule(sub, name)}", name in required)
+                 for name, sub in props.items()]
+        # declaration order; a comma precedes every emitted property but the first
+        body, first_possible = "", True
+        for i, (kv, req) in enumerate(parts):
+            if i == 0:
+                piece = kv
+            elif first_possible:
+                piece = f'( ws "," ws )? {kv}'
+            else:
+                piece = f'ws "," ws {kv}'
+            body += f" {piece}" if req else f" ( {piece} )?"
+            if req:
+                first_possible = False
+        return f'"{{" ws{body} ws "}}"'
+
+    def arr(self, schema, hint):
+        item = self.rule(schema.get("items", {}), hint + "i")
+        lo = int(schema.get("minItems", 0))
+        hi = schema.get("maxItems")
+        more = f'ws "," ws {item}'
+        if hi is not None and int(hi) == 0:
+            return '"[" ws "]"'
+        if lo > 0:
+            rest = f"( {more} ){{{lo - 1},{'' if hi is None else int(hi) - 1}}}"
+            return f'"[" ws {item} {rest} ws "]"'
+        rest = f"( {more} )*" if hi is None else f"( {more} ){{0,{int(hi) - 1}}}"
+        return f'"[" ws ( {item} {rest} )? ws "]"'
+
+    def string(self, schema):
+        if "pattern" in schema:
+            return f'"\\"" ( {regex_to_ebnf(schema["pattern"])} ) "\\""'
+        fmt = schema.get("format")
+        if fmt == "date":
+            return '"\\"" [0-9]{4} "-" [0-9]{2} "-" [0-9]{2} "\\""'
+        if fmt == "date-time":
+            return ('"\\"" [0-9]{4} "-" [0-9]{2} "-" [0-9]{2} "T" [0-9]{2} ":" [0-9]{2} ":" [0-9]{2} '
+                    '( "." [0-9]{1,9} )? ( "Z" | [+-] [0-9]{2} ":" [0-9]{2} ) "\\""')
+        if fmt == "uuid":
+            return ('"\\"" [0-9a-fA-F]{8} "-" [0-9a-fA-F]{4} "-" [0-9a-fA-F]{4} "-" [0-9a-fA-F]{4} "-" '
+                    '[0-9a-fA-F]{12} "\\""')
+        lo, hi = schema.get("minLength"), schema.get("maxLength")
+        if lo is not None or hi is not None:
+            return f'"\\"" json-char{{{int(lo or 0)},{"" if hi is None else int(hi)}}} "\\""'
+        return "json-string"
+
+
+def json_schema_to_ebnf(schema) -> str:
+    """EBNF (root rule ``root``) of the JSON documents a schema admits, with
+    ``$ref`` recursion kept as rule references (no depth bound)."""
+    if isinstance(schema, str):
+        schema = json.loads(schema)
+    conv = _SchemaEbnf(schema)
+    top = conv.rule(schema, "root")
+    lines = [f"root ::= ws {top} ws"] + [f"{k} ::= {v}" for k, v in conv.rules.items()]
+    return "\n".join(lines) + "\n" + JSON_EBNF_BASE
+
+
+class CfgConstraint(GrammarConstraint):
+    """Per-request constraint on the pushdown (context-free) engine: same
+    interface as :class:`GrammarConstraint`."""
+
+    def __init__(self, vocab: GrammarVocabulary, grammar: str, root: str = "root"):
+        self.vocab = vocab
+        self.grammar = grammar
+        self.m = _b200host.CfgMatcher(vocab.native, grammar, root)
+        self.n_committed = 0
+
+    @classmethod
+    def from_json_schema(cls, vocab, schema):
+        return cls(vocab, json_schema_to_ebnf(schema))
+
+    @classmethod
+    def from_ebnf(cls, vocab, grammar, root="root"):
+        return cls(vocab, grammar, root)
+
+    @classmethod
+    def json_object(cls, vocab):
+        return cls(vocab, "root ::= ws json-object ws\n" + JSON_EBNF_BASE)

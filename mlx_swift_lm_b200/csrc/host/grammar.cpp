@@ -30,6 +30,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include "grammar_vocab.h"
+
 namespace py = pybind11;
 
 namespace b200host {
@@ -405,42 +407,6 @@ class Dfa {
     index_[set] = (int)dstates_.size() - 1;
     return (int)dstates_.size() - 1;
   }
-};
-
-// ------------------------------------------------------------------ vocabulary trie
-class Vocab {
- public:
-  Vocab(const std::vector<py::bytes>& tokens, std::vector<int> eos) : eos_(std::move(eos)) {
-    n_ = (int)tokens.size();
-    nodes_.push_back(Node{});
-    for (int id = 0; id < n_; ++id) {
-      std::string s = tokens[id];
-      if (s.empty()) continue;  // special / unrepresentable tokens never match text
-      int cur = 0;
-      for (unsigned char c : s) {
-        auto it = nodes_[cur].kids.find(c);
-        if (it == nodes_[cur].kids.end()) {
-          nodes_.push_back(Node{});
-          nodes_[cur].kids[c] = (int)nodes_.size() - 1;
-          cur = (int)nodes_.size() - 1;
-        } else {
-          cur = it->second;
-        }
-      }
-      nodes_[cur].ids.push_back(id);
-    }
-  }
-  int size() const { return n_; }
-  const std::vector<int>& eos() const { return eos_; }
-  struct Node {
-    std::map<unsigned char, int> kids;
-    std::vector<int> ids;
-  };
-  std::vector<Node> nodes_;
-
- private:
-  int n_;
-  std::vector<int> eos_;
 };
 
 class Matcher {

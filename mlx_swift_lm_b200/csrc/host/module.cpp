@@ -6,10 +6,12 @@ namespace py = pybind11;
 void register_page_pool(py::module_& m);
 void register_safetensors(py::module_& m);
 void register_grammar(py::module_& m);
+void register_grammar_pda(py::module_& m);
 
 PYBIND11_MODULE(_b200host, m) {
-  m.doc() = "B200 LM host runtime: page pool, block hashing, scheduler core, grammar, safetensors IO";
+  m.doc() = "B200 LM host runtime: page pool, block hashing, grammar engines (regex DFA, pushdown), safetensors IO";
   register_page_pool(m);
   register_safetensors(m);
   register_grammar(m);
+  register_grammar_pda(m);
 }
