@@ -507,6 +507,23 @@ def json_schema_to_ebnf(schema) -> str:
     return "\n".join(lines) + "\n" + JSON_EBNF_BASE
 
 
+_COMPILED: "dict[tuple, object]" = {}
+_COMPILED_MAX = 64
+
+
+def compiled_grammar(vocab: GrammarVocabulary, grammar: str, root: str = "root"):
+    """The grammar compiled against `vocab`, shared by every request that uses
+    it (its per-state token classes are computed once); a small LRU."""
+    key = (id(vocab.native), grammar, root)
+    c = _COMPILED.pop(key, None)
+    if c is None:
+        c = _b200host.CfgGrammar(vocab.native, grammar, root)
+    _COMPILED[key] = c
+    while len(_COMPILED) > _COMPILED_MAX:
+        _COMPILED.pop(next(iter(_COMPILED)))
+    return c
+
+
 class CfgConstraint(GrammarConstraint):
     """Per-request constraint on the pushdown (context-free) engine: same
     interface as :class:`GrammarConstraint`."""
@@ -514,7 +531,7 @@ class CfgConstraint(GrammarConstraint):
     def __init__(self, vocab: GrammarVocabulary, grammar: str, root: str = "root"):
         self.vocab = vocab
         self.grammar = grammar
-        self.m = _b200host.CfgMatcher(vocab.native, grammar, root)
+        self.m = _b200host.CfgMatcher(compiled_grammar(vocab, grammar, root))
         self.n_committed = 0
 
     @classmethod

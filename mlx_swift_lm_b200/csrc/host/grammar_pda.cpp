@@ -20,10 +20,13 @@
 //     top has an edge for it;
 //   * token masks: per (rule, state) a trie walk classifies every token as
 //     consumed inside the rule (allowed whatever the stack holds), rejected
-//     inside the rule, or undecided (the walk met a call or a possible
-//     return); a step's mask is the union of its tops' allowed sets plus the
-//     undecided tokens that a full stack simulation accepts, cached per
-//     stack set; EOS is allowed where the root rule can end;
+//     inside the rule, or undecided below a trie node (the walk met a call or
+//     a possible return); these classes live in the compiled grammar, shared
+//     by every request using it. A step's mask is the union of its tops'
+//     allowed sets plus a trie walk of the undecided subtrees carrying the
+//     whole stack set (stack sets interned, byte transitions between them
+//     memoised), cached per stack set; EOS is allowed where the root rule
+//     can end;
 //   * rollback by history of stack sets, forced prefix (jump-forward) while a
 //     single byte is possible.
 // Left recursion (a rule reaching a call of itself without consuming input)
@@ -36,6 +39,7 @@
 #include <array>
 #include <bitset>
 #include <cstdint>
+#include <functional>
 #include <map>
 #include <memory>
 #include <stdexcept>
@@ -554,6 +558,84 @@ static RuleDfa determinise(const RuleNfa& n) {
   return d;
 }
 
+// ------------------------------------------------------------------ rule inlining
+// Rules that take no part in a recursion cycle are expanded into their
+// callers (lexical rules such as a JSON string or number become byte-level
+// states of the rule that uses them), so calls remain only where recursion
+// needs a stack; this keeps most tokens decidable inside one rule.
+static AstP clone(const Ast* a) {
+  auto c = std::make_unique<Ast>();
+  c->kind = a->kind;
+  c->cls = a->cls;
+  c->name = a->name;
+  c->rule = a->rule;
+  c->lo = a->lo;
+  c->hi = a->hi;
+  for (auto& k : a->kids) c->kids.push_back(clone(k.get()));
+  return c;
+}
+
+static void refs(const Ast* a, std::vector<int>& out) {
+  if (a->kind == Ast::kRule) out.push_back(a->rule);
+  for (auto& k : a->kids) refs(k.get(), out);
+}
+
+static size_t ast_size(const Ast* a) {
+  size_t n = 1;
+  for (auto& k : a->kids) n += ast_size(k.get());
+  return n;
+}
+
+static void inline_rules(std::vector<AstP>& bodies) {
+  const int R = (int)bodies.size();
+  std::vector<std::vector<int>> edges(R);
+  for (int r = 0; r < R; ++r) refs(bodies[r].get(), edges[r]);
+  // cyclic[r]: r reaches itself through calls
+  std::vector<char> cyclic(R, 0);
+  for (int r = 0; r < R; ++r) {
+    std::vector<char> seen(R, 0);
+    std::vector<int> st = edges[r];
+    while (!st.empty() && !cyclic[r]) {
+      int x = st.back();
+      st.pop_back();
+      if (x == r) cyclic[r] = 1;
+      if (seen[x]) continue;
+      seen[x] = 1;
+      for (int y : edges[x]) st.push_back(y);
+    }
+  }
+  // expand references to acyclic rules, bottom-up (memoised expanded bodies)
+  std::vector<AstP> expanded(R);
+  std::vector<char> state(R, 0);  // 0 new, 1 in progress, 2 done
+  constexpr size_t kMaxAst = 1 << 18;
+  std::function<void(int)> expand_rule;
+  std::function<AstP(const Ast*)> expand = [&](const Ast* a) -> AstP {
+    if (a->kind == Ast::kRule && !cyclic[a->rule]) {
+      expand_rule(a->rule);
+      if (ast_size(expanded[a->rule].get()) <= kMaxAst / 16) return clone(expanded[a->rule].get());
+      return clone(a);
+    }
+    auto c = std::make_unique<Ast>();
+    c->kind = a->kind;
+    c->cls = a->cls;
+    c->name = a->name;
+    c->rule = a->rule;
+    c->lo = a->lo;
+    c->hi = a->hi;
+    for (auto& k : a->kids) c->kids.push_back(expand(k.get()));
+    return c;
+  };
+  expand_rule = [&](int r) {
+    if (state[r] == 2) return;
+    state[r] = 1;
+    expanded[r] = expand(bodies[r].get());
+    state[r] = 2;
+  };
+  for (int r = 0; r < R; ++r) expand_rule(r);
+  for (int r = 0; r < R; ++r)
+    if (ast_size(expanded[r].get()) <= kMaxAst) bodies[r] = std::move(expanded[r]);
+}
+
 // ------------------------------------------------------------------ compiled grammar
 class Grammar {
  public:
@@ -563,6 +645,7 @@ class Grammar {
     root_ = p.index(root);
     if (root_ < 0) throw std::invalid_argument("grammar: no root rule '" + root + "'");
     names_ = p.names;
+    inline_rules(p.bodies);
     for (auto& body : p.bodies) {
       RuleNfa n;
       NfaBuilder b(n);
@@ -588,13 +671,64 @@ class Grammar {
   std::vector<RuleDfa> dfas_;
 };
 
+// Token classes of one (rule, state) top: allowed whatever the stack holds,
+// and the trie nodes below which the rest of every token is undecided (the
+// walk met a call or a possible return before the token's bytes ran out).
+struct Local {
+  std::vector<uint32_t> allowed;
+  std::vector<int> undecided_roots;
+};
+
+// A grammar compiled against one vocabulary: shared by every matcher of it,
+// so the per-(rule, state) token classes are computed once.
+class Compiled {
+ public:
+  Compiled(std::shared_ptr<Vocab> vocab, const std::string& text, const std::string& root)
+      : vocab(std::move(vocab)), g(std::make_shared<Grammar>(text, root)) {}
+  std::shared_ptr<Vocab> vocab;
+  std::shared_ptr<Grammar> g;
+
+  const Local& local(int rule, int state) {
+    auto key = std::make_pair(rule, state);
+    auto it = local_.find(key);
+    if (it != local_.end()) return it->second;
+    Local L;
+    L.allowed.assign((vocab->size() + 31) / 32, 0u);
+    struct Item {
+      int node, state;
+      bool branch;
+    };
+    std::vector<Item> stack{{0, state, false}};
+    while (!stack.empty()) {
+      Item cur = stack.back();
+      stack.pop_back();
+      const auto& tn = vocab->nodes_[cur.node];
+      if (cur.node != 0)
+        for (int id : tn.ids) L.allowed[id >> 5] |= 1u << (id & 31);
+      const DState& d = g->st(rule, cur.state);
+      const bool branch = cur.branch || !d.calls.empty() || d.accept;
+      for (auto& kv : tn.kids) {
+        const int nx = d.next[kv.first];
+        if (nx >= 0) {
+          stack.push_back({kv.second, nx, branch});
+        } else if (branch) {
+          L.undecided_roots.push_back(kv.second);
+        }
+      }
+    }
+    return local_.emplace(key, std::move(L)).first->second;
+  }
+
+ private:
+  std::map<std::pair<int, int>, Local> local_;
+};
+
 // ------------------------------------------------------------------ matcher
 constexpr int kMaxClosure = 1 << 16;
 
 class Matcher {
  public:
-  Matcher(std::shared_ptr<Vocab> vocab, const std::string& text, const std::string& root)
-      : vocab_(std::move(vocab)), g_(std::make_shared<Grammar>(text, root)) {
+  explicit Matcher(std::shared_ptr<Compiled> c) : c_(std::move(c)), vocab_(c_->vocab), g_(c_->g) {
     history_.push_back(close({node(g_->root(), 0, -1)}));
   }
 
@@ -676,11 +810,8 @@ class Matcher {
   struct Frame {
     int rule, state, parent;
   };
-  struct Local {  // token classes of one (rule, state) top
-    std::vector<uint32_t> allowed;
-    std::vector<int> undecided;
-  };
 
+  std::shared_ptr<Compiled> c_;
   std::shared_ptr<Vocab> vocab_;
   std::shared_ptr<Grammar> g_;
   std::vector<Frame> arena_;
@@ -688,7 +819,10 @@ class Matcher {
   std::vector<std::vector<int>> history_;
   bool terminated_ = false;
   std::map<std::vector<int>, std::vector<uint32_t>> mask_cache_;
-  std::map<std::pair<int, int>, Local> local_;
+  // stack sets interned to ids, and memoised byte transitions between them
+  std::map<std::vector<int>, int> set_ids_;
+  std::vector<std::vector<int>> sets_;
+  std::unordered_map<uint64_t, int> step_memo_;
 
   int node(int rule, int state, int parent) {
     const uint64_t key = ((uint64_t)(uint32_t)rule * 1000003ull + (uint32_t)state) * 2654435761ull ^
@@ -757,68 +891,60 @@ class Matcher {
     return false;
   }
 
-  const Local& local(int rule, int state) {
-    auto key = std::make_pair(rule, state);
-    auto it = local_.find(key);
-    if (it != local_.end()) return it->second;
-    Local L;
-    L.allowed.assign((vocab_->size() + 31) / 32, 0u);
-    // trie walk inside the rule: (trie node, rule state, a call / return was possible on the way)
-    struct Item {
-      int node, state;
-      bool branch;
-    };
-    std::vector<Item> stack{{0, state, false}};
-    std::vector<int> sub;
-    while (!stack.empty()) {
-      Item it2 = stack.back();
-      stack.pop_back();
-      const auto& tn = vocab_->nodes_[it2.node];
-      if (it2.node != 0)
-        for (int id : tn.ids) L.allowed[id >> 5] |= 1u << (id & 31);
-      const DState& d = g_->st(rule, it2.state);
-      const bool branch = it2.branch || !d.calls.empty() || d.accept;
-      for (auto& kv : tn.kids) {
-        const int nx = d.next[kv.first];
-        if (nx >= 0) {
-          stack.push_back({kv.second, nx, branch});
-        } else if (branch) {  // the rest of every token below may continue through a call or a return
-          sub.push_back(kv.second);
-          while (!sub.empty()) {
-            int t = sub.back();
-            sub.pop_back();
-            for (int id : vocab_->nodes_[t].ids) L.undecided.push_back(id);
-            for (auto& k2 : vocab_->nodes_[t].kids) sub.push_back(k2.second);
-          }
-        }
-      }
-    }
-    return local_.emplace(key, std::move(L)).first->second;
+  int set_id(const std::vector<int>& set) {
+    auto it = set_ids_.find(set);
+    if (it != set_ids_.end()) return it->second;
+    set_ids_[set] = (int)sets_.size();
+    sets_.push_back(set);
+    return (int)sets_.size() - 1;
+  }
+  // id of the set after byte b (-1: empty), memoised
+  int step(int sid, unsigned char b) {
+    const uint64_t key = (uint64_t)sid * 256 + b;
+    auto it = step_memo_.find(key);
+    if (it != step_memo_.end()) return it->second;
+    std::vector<int> nx = advance(sets_[sid], b);
+    const int r = nx.empty() ? -1 : set_id(nx);
+    step_memo_[key] = r;
+    return r;
   }
 
   std::vector<uint32_t> compute_mask(const std::vector<int>& set) {
     std::vector<uint32_t> m((vocab_->size() + 31) / 32, 0u);
-    std::vector<int> undecided;
+    std::vector<int> roots;
     std::map<std::pair<int, int>, char> tops;
     for (int n : set) {
       const Frame& f = arena_[n];
       if (!g_->st(f.rule, f.state).has_bytes) continue;
       if (tops[{f.rule, f.state}]) continue;
       tops[{f.rule, f.state}] = 1;
-      const Local& L = local(f.rule, f.state);
+      const Local& L = c_->local(f.rule, f.state);
       for (size_t w = 0; w < m.size(); ++w) m[w] |= L.allowed[w];
-      undecided.insert(undecided.end(), L.undecided.begin(), L.undecided.end());
+      roots.insert(roots.end(), L.undecided_roots.begin(), L.undecided_roots.end());
     }
-    std::sort(undecided.begin(), undecided.end());
-    undecided.erase(std::unique(undecided.begin(), undecided.end()), undecided.end());
-    for (int id : undecided) {
-      if (m[id >> 5] >> (id & 31) & 1u) continue;
-      std::vector<int> s = set;
-      for (unsigned char c : vocab_->bytes(id)) {
-        s = advance(s, c);
-        if (s.empty()) break;
+    std::sort(roots.begin(), roots.end());
+    roots.erase(std::unique(roots.begin(), roots.end()), roots.end());
+    // undecided subtrees: walk the trie from each root with the whole stack set,
+    // pruning where no stack can take the next byte
+    const int s0 = set_id(set);
+    std::vector<std::pair<int, int>> work;  // (trie node, set id after its path)
+    for (int r : roots) {
+      int sid = s0;
+      for (unsigned char b : vocab_->path(r)) {
+        sid = step(sid, b);
+        if (sid < 0) break;
       }
-      if (!s.empty()) m[id >> 5] |= 1u << (id & 31);
+      if (sid >= 0) work.push_back({r, sid});
+    }
+    while (!work.empty()) {
+      auto [t, sid] = work.back();
+      work.pop_back();
+      const auto& tn = vocab_->nodes_[t];
+      for (int id : tn.ids) m[id >> 5] |= 1u << (id & 31);
+      for (auto& kv : tn.kids) {
+        const int nx = step(sid, kv.first);
+        if (nx >= 0) work.push_back({kv.second, nx});
+      }
     }
     if (accepting(set))
       for (int e : vocab_->eos()) m[e >> 5] |= 1u << (e & 31);
@@ -831,9 +957,12 @@ class Matcher {
 
 void register_grammar_pda(py::module_& m) {
   using namespace b200host;
-  py::class_<cfg::Matcher>(m, "CfgMatcher")
+  py::class_<cfg::Compiled, std::shared_ptr<cfg::Compiled>>(m, "CfgGrammar")
       .def(py::init<std::shared_ptr<Vocab>, const std::string&, const std::string&>(), py::arg("vocab"),
            py::arg("grammar"), py::arg("root") = std::string("root"))
+      .def_property_readonly("num_states", [](const cfg::Compiled& c) { return c.g->num_states(); });
+  py::class_<cfg::Matcher>(m, "CfgMatcher")
+      .def(py::init<std::shared_ptr<cfg::Compiled>>(), py::arg("grammar"))
       .def("mask", &cfg::Matcher::mask)
       .def("accept_token", &cfg::Matcher::accept_token)
       .def("accept_string", &cfg::Matcher::accept_string)

@@ -17,6 +17,8 @@ class Vocab {
     n_ = (int)tokens.size();
     bytes_.resize(n_);
     nodes_.push_back(Node{});
+    parent_.push_back(-1);
+    byte_.push_back(0);
     for (int id = 0; id < n_; ++id) {
       std::string s = tokens[id];
       bytes_[id] = s;
@@ -26,6 +28,8 @@ class Vocab {
         auto it = nodes_[cur].kids.find(c);
         if (it == nodes_[cur].kids.end()) {
           nodes_.push_back(Node{});
+          parent_.push_back(cur);
+          byte_.push_back(c);
           nodes_[cur].kids[c] = (int)nodes_.size() - 1;
           cur = (int)nodes_.size() - 1;
         } else {
@@ -43,6 +47,12 @@ class Vocab {
     return false;
   }
   const std::string& bytes(int id) const { return bytes_[id]; }
+  // bytes from the trie root to trie node `node`
+  std::string path(int node) const {
+    std::string out;
+    for (int n = node; n > 0; n = parent_[n]) out.push_back((char)byte_[n]);
+    return std::string(out.rbegin(), out.rend());
+  }
   struct Node {
     std::map<unsigned char, int> kids;
     std::vector<int> ids;
@@ -53,6 +63,8 @@ class Vocab {
   int n_;
   std::vector<int> eos_;
   std::vector<std::string> bytes_;
+  std::vector<int> parent_;
+  std::vector<unsigned char> byte_;
 };
 
 }  // namespace b200host
