@@ -453,9 +453,12 @@ def _kv_rows(w, cfg, rank, world):
 
 
 def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParallel | None = None,
-               config_overrides: dict | None = None, keep_quantized: bool = True):
+               config_overrides: dict | None = None, keep_quantized: bool = True, with_mtp: bool = False):
     """Load a model directory (config.json + *.safetensors). Returns (model, hf_config).
-    MLX affine 4/8-bit projections stay packed unless `keep_quantized` is False."""
+    MLX affine 4/8-bit projections stay packed unless `keep_quantized` is False.
+    `with_mtp`: also load the checkpoint's MTP head (Qwen 3.5 ``mtp.*``,
+    DeepSeek V3 / GLM nextn layers, MiMo ``mtp_layers``) as ``model.mtp_head``
+    (None when the checkpoint has none)."""
     with open(os.path.join(path, "config.json")) as f:
         hf = json.load(f)
     hadamard = None
@@ -472,6 +475,10 @@ def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParalle
     model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized, hadamard=hadamard)
     if hf.get("vision_config") and hf.get("model_type") == "qwen2_vl":
         model = _attach_vision(model, cfg, hf, tensors, device, dtype)
+    if with_mtp:
+        from ..models.mtp import load_mtp
+
+        model.mtp_head = load_mtp(model, tensors)
     return model, hf
 
 
@@ -643,6 +650,7 @@ def build_from_tensors(cfg: DecoderConfig, tensors: dict, device="cpu", dtype=to
         m.layers.append(L)
     if cfg.norm_offset_one:
         cfg.norm_offset_one = False  # folded into the stored weights
+        cfg.extra["norms_zero_centred"] = True  # the checkpoint stores w - 1 (MTP heads beside it too)
     _fold_multipliers(m, cfg)
     return m.clone_to(device, dtype)
 
