@@ -473,7 +473,7 @@ def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParalle
     if hadamard is not None:
         prism.validate(info, hadamard, tensors)
     model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized, hadamard=hadamard)
-    if hf.get("vision_config") and hf.get("model_type") == "qwen2_vl":
+    if hf.get("vision_config") and hf.get("model_type") in ("qwen2_vl", "qwen2_5_vl"):
         model = _attach_vision(model, cfg, hf, tensors, device, dtype)
     if with_mtp:
         from ..models.mtp import load_mtp
@@ -483,13 +483,14 @@ def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParalle
 
 
 def _attach_vision(lm, cfg, hf, tensors, device, dtype):
-    """Qwen2-VL: the loaded language model plus its vision tower
+    """Qwen2-VL / Qwen2.5-VL: the loaded language model plus its vision tower
     (``visual.*`` / ``model.visual.*``) as one :class:`Qwen2VLModel`."""
     from ..models.vision import QwenVisionTower, VisionConfig
     from ..models.vlm import Qwen2VLModel
 
     rs = hf.get("rope_scaling") or (hf.get("text_config") or {}).get("rope_scaling") or {}
-    vcfg = VisionConfig.from_hf(hf["vision_config"], cfg.hidden_size)
+    kind = "qwen2_5" if hf.get("model_type") == "qwen2_5_vl" else "qwen2"
+    vcfg = VisionConfig.from_hf(hf["vision_config"], cfg.hidden_size, kind)
     m = Qwen2VLModel(cfg, vcfg, device, dtype, hf.get("image_token_id", 151655), hf.get("video_token_id", 151656),
                      rs.get("mrope_section", (16, 24, 24)))
     m.embed, m.norm, m.lm_head, m.layers = lm.embed, lm.norm, lm.lm_head, lm.layers

@@ -33,6 +33,7 @@ register("exaone4", post_only_norms=True, qk_norm=True, exaone4=True)
 register("qwen2")  # q/k/v biases
 register("mimo")  # Xiaomi MiMo: the Qwen2 body (its MTP layers are not loaded)
 register("qwen2_vl", vlm="qwen2_vl")  # the language model of Qwen2-VL (q/k/v biases, M-RoPE)
+register("qwen2_5_vl", vlm="qwen2_vl")  # Qwen2.5-VL: the same language model; window-attention vision tower
 register("qwen3", qk_norm=True)
 register("qwen3_moe", qk_norm=True, moe=True)
 register("qwen3_next", qk_norm=True, moe=True, hybrid=True)
@@ -208,7 +209,8 @@ def build_config(hf: dict) -> DecoderConfig:
         partial_rotary_factor=hf.get("partial_rotary_factor", 1.0),
         max_position_embeddings=hf.get("max_position_embeddings", 4096),
         tie_word_embeddings=hf.get("tie_word_embeddings", False), qk_norm=tr.get("qk_norm", False),
-        attention_bias=hf.get("attention_bias", mt in ("qwen2", "qwen2_vl", "mimo")), o_bias=hf.get("o_bias", False),
+        attention_bias=hf.get("attention_bias", mt in ("qwen2", "qwen2_vl", "qwen2_5_vl", "mimo")),
+        o_bias=hf.get("o_bias", False),
         mlp_bias=hf.get("mlp_bias", False), quantization=hf.get("quantization") or hf.get("quantization_config"),
         hidden_act=_act(hf.get("hidden_activation") or hf.get("hidden_act") or "silu"))
     if cfg.rope_scaling and cfg.rope_scaling.get("rope_type", cfg.rope_scaling.get("type")) == "default":

@@ -1,4 +1,10 @@
-"""Qwen2-VL vision tower on the decoder's kernels.
+"""Qwen2-VL and Qwen2.5-VL vision towers on the decoder's kernels.
+
+Qwen2.5-VL (MLXVLM/Models/Qwen25VL.swift) changes the blocks to RMSNorm and a
+biased SwiGLU MLP, attends within windows of ``window_size`` pixels except in
+its ``fullatt_block_indexes`` blocks (patches reordered window by window, in
+units of merged 2x2 patches, and restored after the merger), and merges with
+an RMSNorm.
 
 Parity: MLXVLM/Models/Qwen2VL.swift:513-790 and QwenVL.swift:90-160 -
 patch embedding (a Conv3d whose kernel equals its stride, i.e. one linear map
@@ -22,6 +28,7 @@ import torch
 
 from .. import ops
 from ..kv.paged import PAGE
+from ..ops import reference as ref
 from .encoder import scratch_layout
 
 
@@ -37,6 +44,10 @@ class VisionConfig:
     in_chans: int = 3
     hidden_size: int = 3584  # language model hidden size (merger output)
     eps: float = 1e-6
+    kind: str = "qwen2"  # "qwen2" | "qwen2_5"
+    intermediate_size: int = 0  # qwen2_5: SwiGLU width
+    window_size: int = 112  # qwen2_5: attention window in pixels
+    fullatt_blocks: tuple = ()  # qwen2_5: blocks attending whole frames
 
     @property
     def head_dim(self) -> int:
@@ -47,17 +58,40 @@ class VisionConfig:
         return self.in_chans * self.temporal_patch_size * self.patch_size * self.patch_size
 
     @classmethod
-    def from_hf(cls, vc: dict, text_hidden: int) -> "VisionConfig":
-        return cls(depth=vc.get("depth", 32), embed_dim=vc.get("embed_dim", 1280), num_heads=vc.get("num_heads", 16),
-                   mlp_ratio=vc.get("mlp_ratio", 4.0), patch_size=vc.get("patch_size", 14),
-                   temporal_patch_size=vc.get("temporal_patch_size", 2),
-                   spatial_merge_size=vc.get("spatial_merge_size", 2), in_chans=vc.get("in_chans", 3),
-                   hidden_size=vc.get("hidden_size", text_hidden))
+    def from_hf(cls, vc: dict, text_hidden: int, kind: str = "qwen2") -> "VisionConfig":
+        common = dict(depth=vc.get("depth", 32), num_heads=vc.get("num_heads", 16),
+                      patch_size=vc.get("patch_size", 14), temporal_patch_size=vc.get("temporal_patch_size", 2),
+                      spatial_merge_size=vc.get("spatial_merge_size", 2),
+                      in_chans=vc.get("in_chans", vc.get("in_channels", 3)))
+        if kind == "qwen2_5":  # hidden_size is the tower width, out_hidden_size the language model's
+            return cls(embed_dim=vc.get("hidden_size", 1280), hidden_size=vc.get("out_hidden_size", text_hidden),
+                       intermediate_size=vc.get("intermediate_size", 3420), window_size=vc.get("window_size", 112),
+                       fullatt_blocks=tuple(vc.get("fullatt_block_indexes", (7, 15, 23, 31))), kind="qwen2_5",
+                       **common)
+        return cls(embed_dim=vc.get("embed_dim", 1280), mlp_ratio=vc.get("mlp_ratio", 4.0),
+                   hidden_size=vc.get("hidden_size", text_hidden), **common)
+
+
+def _swiglu(gate, up, gate_b, up_b, down):
+    """Fused SwiGLU operands: gate/up rows (and biases) interleaved in 64-row
+    blocks, the width padded with zero rows to a multiple of 64 (zero gate and
+    up give a zero product, and the matching zero columns of down add nothing)."""
+    I = gate.shape[0]
+    pad = -I % 64
+    if pad:
+        z = lambda t: torch.cat([t, t.new_zeros((pad,) + tuple(t.shape[1:]))], 0)  # noqa: E731
+        gate, up, gate_b, up_b = z(gate), z(up), z(gate_b), z(up_b)
+        down = torch.cat([down, down.new_zeros(down.shape[0], pad)], 1)
+    gu_w = ref.interleave_gate_up(gate, up)
+    gu_b = ref.interleave_gate_up(gate_b[:, None], up_b[:, None])[:, 0].contiguous()
+    return gu_w, gu_b, down.contiguous()
 
 
 class VisionBlock:
     __slots__ = ("norm1_w", "norm1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "norm2_w", "norm2_b", "fc1_w", "fc1_b",
-                 "fc2_w", "fc2_b")
+                 "fc2_w", "fc2_b",
+                 # qwen2_5: SwiGLU gate/up (64-row interleaved, with biases) and down projections
+                 "gu_w", "gu_b", "dn_w", "dn_b")
 
     def __init__(self):
         for s in self.__slots__:
@@ -90,14 +124,21 @@ class QwenVisionTower:
 
         self.patch_w = rn(E, c.patch_dim)
         self.blocks = []
+        q25 = c.kind == "qwen2_5"
         for _ in range(c.depth):
             b = VisionBlock()
-            b.norm1_w, b.norm1_b, b.norm2_w, b.norm2_b = ones(E), rn(E), ones(E), rn(E)
             b.qkv_w, b.qkv_b = rn(3 * E, E), rn(3 * E)
             b.proj_w, b.proj_b = rn(E, E), rn(E)
-            b.fc1_w, b.fc1_b, b.fc2_w, b.fc2_b = rn(F, E), rn(F), rn(E, F), rn(E)
+            if q25:
+                I = c.intermediate_size
+                b.norm1_w, b.norm2_w = ones(E), ones(E)
+                b.gu_w, b.gu_b, b.dn_w = _swiglu(rn(I, E), rn(I, E), rn(I), rn(I), rn(E, I))
+                b.dn_b = rn(E)
+            else:
+                b.norm1_w, b.norm1_b, b.norm2_w, b.norm2_b = ones(E), rn(E), ones(E), rn(E)
+                b.fc1_w, b.fc1_b, b.fc2_w, b.fc2_b = rn(F, E), rn(F), rn(E, F), rn(E)
             self.blocks.append(b)
-        self.ln_q_w, self.ln_q_b = ones(E), rn(E)
+        self.ln_q_w, self.ln_q_b = ones(E), (None if q25 else rn(E))
         self.m1_w, self.m1_b, self.m2_w, self.m2_b = rn(M, M), rn(M), rn(c.hidden_size, M), rn(c.hidden_size)
         return self
 
@@ -136,34 +177,84 @@ class QwenVisionTower:
         ang = torch.cat([hp[:, None] * self.inv_freq[None], wp[:, None] * self.inv_freq[None]], -1)
         return torch.cat([ang.cos(), ang.sin()], -1).float().to(self.device)
 
+    def window_index(self, grids: list[tuple[int, int, int]]):
+        """(order of the merged units window by window, window lengths in
+        patches): units of each frame grouped into windows of
+        window_size / merge / patch units per side, row-major over windows."""
+        c = self.cfg
+        m = c.spatial_merge_size
+        ws = c.window_size // m // c.patch_size
+        order, lens, base = [], [], 0
+        for t, h, w in grids:
+            gh, gw = h // m, w // m
+            idx = torch.arange(t * gh * gw).reshape(t, gh, gw)
+            nh, nw = -(-gh // ws), -(-gw // ws)
+            for ti in range(t):
+                for wi in range(nh):
+                    for wj in range(nw):
+                        blk = idx[ti, wi * ws:(wi + 1) * ws, wj * ws:(wj + 1) * ws].reshape(-1)
+                        if blk.numel():
+                            order.append(blk + base)
+                            lens.append(blk.numel() * m * m)
+            base += t * gh * gw
+        return torch.cat(order), lens
+
     # ------------------------------------------------------------------ forward
     @torch.no_grad()
     def forward(self, patches: torch.Tensor, grids: list[tuple[int, int, int]]) -> torch.Tensor:
         """patches [N, C*tp*p*p] -> merged embeddings [N / merge^2, hidden]."""
         c = self.cfg
         dev, E, NH, D = self.device, c.embed_dim, c.num_heads, c.head_dim
+        q25 = c.kind == "qwen2_5"
+        U = c.spatial_merge_size ** 2
         x = ops.gemm(patches.to(dev, self.dtype).contiguous(), self.patch_w)
         N = x.shape[0]
-        lens = [h * w for t, h, w in grids for _ in range(t)]  # attention within each frame
-        pt, slots, cu, npages = scratch_layout(lens, dev)
+        table = self.rotary_table(grids)
+        frames = [h * w for t, h, w in grids for _ in range(t)]  # attention within each frame
+
+        def layout(lens):
+            pt, slots, cu, npages = scratch_layout(lens, dev)
+            return (pt, slots, cu, torch.tensor(cu, dtype=torch.int32, device=dev),
+                    torch.zeros(len(lens), dtype=torch.int32, device=dev), npages)
+
+        full = layout(frames)
+        if q25:  # window order of merged units; the full-attention frames stay contiguous in it
+            order, wlens = self.window_index(grids)
+            order = order.to(dev)
+            perm = (order[:, None] * U + torch.arange(U, device=dev)[None]).reshape(-1)
+            x = x.index_select(0, perm).contiguous()
+            table = table.index_select(0, perm).contiguous()
+            win = layout(wlens)
+        npages = max(full[5], win[5]) if q25 else full[5]
         kc = torch.zeros(npages, NH, PAGE, D, dtype=self.dtype, device=dev)
         vc = torch.zeros_like(kc)
-        cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
-        pos0 = torch.zeros(len(lens), dtype=torch.int32, device=dev)
-        table = self.rotary_table(grids)
         tok = torch.arange(N, dtype=torch.int32, device=dev)
         delta = None
-        for b in self.blocks:
-            h = ops.add_layernorm(x, delta, b.norm1_w, b.norm1_b, c.eps)
+        for i, b in enumerate(self.blocks):
+            pt, slots, cu, cu_t, pos0, _ = win if q25 and i not in c.fullatt_blocks else full
+            if q25:
+                h = ops.add_rmsnorm(x, delta, b.norm1_w, c.eps)
+            else:
+                h = ops.add_layernorm(x, delta, b.norm1_w, b.norm1_b, c.eps)
             qkv = ops.gemm(h, b.qkv_w, bias=b.qkv_b)
             q = ops.qk_norm_rope_kv(qkv, tok, slots, table, D, False, None, None, c.eps, kc, vc, NH, NH, D)
             a = ops.paged_prefill(q, kc, vc, pt, cu_t, pos0, D ** -0.5, -1, cu_q_host=cu)
             d = ops.gemm(a.reshape(N, E), b.proj_w, bias=b.proj_b)
-            h = ops.add_layernorm(x, d, b.norm2_w, b.norm2_b, c.eps)
-            delta = ops.gemm(ops.gemm(h, b.fc1_w, epi="quick_gelu", bias=b.fc1_b), b.fc2_w, bias=b.fc2_b)
-        hq = ops.add_layernorm(x, delta, self.ln_q_w, self.ln_q_b, c.eps)
-        hq = hq.reshape(N // c.spatial_merge_size ** 2, -1).contiguous()
-        return ops.gemm(ops.gemm(hq, self.m1_w, epi="gelu", bias=self.m1_b), self.m2_w, bias=self.m2_b)
+            if q25:
+                h = ops.add_rmsnorm(x, d, b.norm2_w, c.eps)
+                delta = ops.gemm(ops.gemm(h, b.gu_w, epi="swiglu", bias=b.gu_b), b.dn_w, bias=b.dn_b)
+            else:
+                h = ops.add_layernorm(x, d, b.norm2_w, b.norm2_b, c.eps)
+                delta = ops.gemm(ops.gemm(h, b.fc1_w, epi="quick_gelu", bias=b.fc1_b), b.fc2_w, bias=b.fc2_b)
+        if q25:
+            hq = ops.add_rmsnorm(x, delta, self.ln_q_w, c.eps)
+        else:
+            hq = ops.add_layernorm(x, delta, self.ln_q_w, self.ln_q_b, c.eps)
+        hq = hq.reshape(N // U, -1).contiguous()
+        out = ops.gemm(ops.gemm(hq, self.m1_w, epi="gelu", bias=self.m1_b), self.m2_w, bias=self.m2_b)
+        if q25:  # back to patchify order
+            out = out.index_select(0, torch.argsort(order)).contiguous()
+        return out
 
     # ------------------------------------------------------------------ loading
     @classmethod
@@ -181,17 +272,26 @@ class QwenVisionTower:
         if w.dim() == 5 and w.shape[-1] == cfg.in_chans:  # MLX layout [out, t, p, p, C]
             w = w.permute(0, 4, 1, 2, 3)
         m.patch_w = w.reshape(w.shape[0], -1)
+        q25 = cfg.kind == "qwen2_5"
         for i in range(cfg.depth):
             p = f"blocks.{i}."
             b = VisionBlock()
-            b.norm1_w, b.norm1_b = g(p + "norm1.weight"), g(p + "norm1.bias")
-            b.norm2_w, b.norm2_b = g(p + "norm2.weight"), g(p + "norm2.bias")
             b.qkv_w, b.qkv_b = g(p + "attn.qkv.weight"), g(p + "attn.qkv.bias")
             b.proj_w, b.proj_b = g(p + "attn.proj.weight"), g(p + "attn.proj.bias")
-            b.fc1_w, b.fc1_b = g(p + "mlp.fc1.weight"), g(p + "mlp.fc1.bias")
-            b.fc2_w, b.fc2_b = g(p + "mlp.fc2.weight"), g(p + "mlp.fc2.bias")
+            if q25:
+                b.norm1_w, b.norm2_w = g(p + "norm1.weight"), g(p + "norm2.weight")
+                b.gu_w, b.gu_b, b.dn_w = _swiglu(g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight"),
+                                                 g(p + "mlp.gate_proj.bias"), g(p + "mlp.up_proj.bias"),
+                                                 g(p + "mlp.down_proj.weight"))
+                b.dn_b = g(p + "mlp.down_proj.bias")
+            else:
+                b.norm1_w, b.norm1_b = g(p + "norm1.weight"), g(p + "norm1.bias")
+                b.norm2_w, b.norm2_b = g(p + "norm2.weight"), g(p + "norm2.bias")
+                b.fc1_w, b.fc1_b = g(p + "mlp.fc1.weight"), g(p + "mlp.fc1.bias")
+                b.fc2_w, b.fc2_b = g(p + "mlp.fc2.weight"), g(p + "mlp.fc2.bias")
             m.blocks.append(b)
-        m.ln_q_w, m.ln_q_b = g("merger.ln_q.weight"), g("merger.ln_q.bias")
+        m.ln_q_w = g("merger.ln_q.weight")
+        m.ln_q_b = None if q25 else g("merger.ln_q.bias")
         m.m1_w, m.m1_b = g("merger.mlp.0.weight"), g("merger.mlp.0.bias")
         m.m2_w, m.m2_b = g("merger.mlp.2.weight"), g("merger.mlp.2.bias")
         return m.to(device, dtype)

@@ -146,3 +146,35 @@ def test_vlm_checkpoint_roundtrip_and_container(tmp_path):
                                                       max_model_len=128, use_cuda_graphs=False))
     toks, _, info = c.generate([5, IMG, 6], params=GenerateParameters(temperature=0.0, max_tokens=5), images=[img])
     assert len(toks) == 5 and info.prompt_tokens == 2 + 4
+
+
+def test_qwen25_vision_tower_matches_transformers():
+    """Qwen2.5-VL tower (window attention with full-attention blocks, RMSNorm,
+    biased SwiGLU of a width that is not a multiple of 64, RMSNorm merger,
+    window order restored) against the transformers implementation."""
+    import pytest
+
+    tf = pytest.importorskip("transformers.models.qwen2_5_vl.modeling_qwen2_5_vl")
+    from transformers.models.qwen2_5_vl.configuration_qwen2_5_vl import Qwen2_5_VLVisionConfig
+
+    hc = Qwen2_5_VLVisionConfig(depth=4, hidden_size=64, intermediate_size=100, num_heads=2, patch_size=14,
+                                spatial_merge_size=2, temporal_patch_size=2, window_size=56,
+                                fullatt_block_indexes=[1, 3], out_hidden_size=96)
+    torch.manual_seed(0)
+    hf = tf.Qwen2_5_VisionTransformerPretrainedModel._from_config(hc).float().eval()
+    with torch.no_grad():
+        for n, p in hf.named_parameters():
+            p.copy_((1.0 + 0.1 * torch.randn_like(p)) if n.endswith("norm1.weight") or n.endswith("norm2.weight")
+                    or n.endswith("ln_q.weight") else 0.1 * torch.randn_like(p))
+    grids = [(1, 8, 12), (2, 4, 6)]
+    N = sum(t * h * w for t, h, w in grids)
+    patches = torch.randn(N, 3 * 2 * 14 * 14, generator=torch.Generator().manual_seed(2))
+    with torch.no_grad():
+        want = hf(patches, grid_thw=torch.tensor(grids)).pooler_output
+    vc = VisionConfig.from_hf(hc.to_dict(), 96, "qwen2_5")
+    assert vc.embed_dim == 64 and vc.fullatt_blocks == (1, 3) and vc.hidden_size == 96
+    tower = QwenVisionTower.from_tensors(vc, {"visual." + k: v for k, v in hf.state_dict().items()}, "cpu",
+                                         torch.float32)
+    got = tower.forward(patches, grids)
+    assert got.shape == want.shape
+    assert torch.allclose(got, want, atol=2e-4, rtol=1e-3), (got - want).abs().max()
