@@ -475,6 +475,8 @@ def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParalle
     model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized, hadamard=hadamard)
     if hf.get("vision_config") and hf.get("model_type") in ("qwen2_vl", "qwen2_5_vl"):
         model = _attach_vision(model, cfg, hf, tensors, device, dtype)
+    elif hf.get("vision_config") and hf.get("model_type") == "gemma3":
+        model = _attach_siglip(model, cfg, hf, tensors, device, dtype)
     if with_mtp:
         from ..models.mtp import load_mtp
 
@@ -495,6 +497,23 @@ def _attach_vision(lm, cfg, hf, tensors, device, dtype):
                      rs.get("mrope_section", (16, 24, 24)))
     m.embed, m.norm, m.lm_head, m.layers = lm.embed, lm.norm, lm.lm_head, lm.layers
     m.vision = QwenVisionTower.from_tensors(vcfg, tensors, device, dtype)
+    return m
+
+
+def _attach_siglip(lm, cfg, hf, tensors, device, dtype):
+    """Gemma 3 VLM: the loaded language model plus the SigLIP tower and the
+    pooled projector (``multi_modal_projector.*``) as one Gemma3VLModel."""
+    from ..models.siglip import Gemma3VLModel, SiglipConfig, SiglipVisionTower
+
+    vcfg = SiglipConfig.from_hf(hf["vision_config"])
+    m = Gemma3VLModel(cfg, vcfg, device, dtype, hf.get("image_token_index", hf.get("image_token_id", 262144)),
+                      hf.get("mm_tokens_per_image", 256))
+    m.embed, m.norm, m.lm_head, m.layers = lm.embed, lm.norm, lm.lm_head, lm.layers
+    m.vision = SiglipVisionTower.from_tensors(vcfg, tensors, device, dtype)
+    pre = next(p for p in ("model.multi_modal_projector.", "multi_modal_projector.")
+               if p + "mm_input_projection_weight" in tensors)
+    m.proj_w = tensors[pre + "mm_input_projection_weight"].to(device, dtype)
+    m.proj_norm = tensors[pre + "mm_soft_emb_norm.weight"].to(device, dtype)
     return m
 
 

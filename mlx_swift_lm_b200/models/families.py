@@ -327,8 +327,19 @@ def build_config(hf: dict) -> DecoderConfig:
         if not layer_types:
             cfg.layer_windows = [int(sw or 128) if i % 2 == 0 else 0 for i in range(cfg.num_layers)]
     rp = hf.get("rope_parameters") or {}
+    if rp and isinstance(rp.get("full_attention"), dict) and not tr.get("gemma4"):
+        # per-layer-type parameters (transformers 5 configs): full layers take the
+        # main table, sliding layers their own base
+        full, slide = rp["full_attention"], rp.get("sliding_attention") or {}
+        if full.get("rope_theta") is not None:
+            cfg.rope_theta = float(full["rope_theta"])
+        if full.get("rope_type", "default") not in ("default", None) and cfg.rope_scaling is None:
+            cfg.rope_scaling = dict(full)
+        if slide.get("rope_theta") is not None and cfg.layer_windows:
+            cfg.extra["rope_local_theta"] = float(slide["rope_theta"])
+        rp = {}
     if rp:
-        if "rope_theta" not in hf and "rope_theta" in rp:
+        if "rope_theta" not in hf and rp.get("rope_theta") is not None:
             cfg.rope_theta = float(rp["rope_theta"])
         if cfg.rope_scaling is None and rp.get("rope_type", rp.get("type", "default")) != "default":
             cfg.rope_scaling = dict(rp)
