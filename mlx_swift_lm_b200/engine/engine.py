@@ -69,6 +69,7 @@ class EngineConfig:
     chained_decode: bool = True
     enable_prefix_cache: bool = False
     prefix_block_size: int = 256
+    prefix_host_blocks: int = 0  # pinned host tier of the prefix cache (blocks of prefix_block_size tokens)
     # ring storage for sliding-window layers (window + one step of pages per
     # request instead of the whole context); None: on unless prefix caching is
     window_ring: bool | None = None
@@ -178,7 +179,8 @@ class EngineV2:
         if self.cfg.enable_prefix_cache and self.kv.rec is None and not self.kv.ring_pages:
             from ..kv.prefix_cache import PrefixCache
 
-            self.prefix_cache = PrefixCache(self.kv, self.cfg.prefix_block_size)
+            self.prefix_cache = PrefixCache(self.kv, self.cfg.prefix_block_size,
+                                            host_blocks=self.cfg.prefix_host_blocks)
         from .admission import AdmissionConfig, AdmissionLedger, layer_kinds_for
 
         rec_bytes = self.kv.rec.bytes_per_seq if self.kv.rec is not None else 0

@@ -9,25 +9,94 @@ Paged/PrefixBlocks/PagedPrefixBlockIndex.swift:10). A match never covers a
 prompt's last token (its logits must be computed), the cache evicts least
 recently used blocks whose pages no live request holds, and requests with
 ``prefix_cache_enabled=False`` neither read nor donate.
+
+Tiers (the reference's snapshot tier and prefix checkpoints,
+PrefixCacheV2.swift:69-545): with ``host_blocks`` > 0 a block evicted from
+the device is first copied into a pinned host pool (every KV layer group of
+its pages) and a later match brings it back into fresh device pages instead
+of recomputing it; :meth:`PrefixCache.save` / :meth:`PrefixCache.load` write
+every cached block (both tiers) to safetensors files and read them back, so a
+restarted server starts with its prefixes warm.
 """
 from __future__ import annotations
 
 import collections
+import json
+import os
+
+import torch
 
 from .paged import PAGE, PagedKVCache, _b200host
 
 
+class HostTier:
+    """Pinned host copies of evicted prefix blocks: per KV layer group a slab
+    [layers, blocks * pages_per_block, KVH, 16, D] (K and V), LRU over blocks."""
+
+    def __init__(self, cache: PagedKVCache, max_blocks: int, pages_per_block: int):
+        self.cache = cache
+        self.ppb = pages_per_block
+        pin = cache.device.type == "cuda"
+        self.k = [torch.empty((g.shape[0], max_blocks * pages_per_block) + tuple(g.shape[2:]), dtype=g.dtype,
+                              pin_memory=pin) for g in cache.gk]
+        self.v = [torch.empty_like(t) for t in self.k]
+        self.free = list(range(max_blocks))
+        self.entries: "collections.OrderedDict[bytes, int]" = collections.OrderedDict()
+        self.stores = 0
+        self.loads = 0
+
+    def _rows(self, slot):
+        return slice(slot * self.ppb, (slot + 1) * self.ppb)
+
+    def store(self, h: bytes, pages: list[int]):
+        if h in self.entries:
+            self.entries.move_to_end(h)
+            return
+        if not self.free:
+            if not self.entries:
+                return
+            _, slot = self.entries.popitem(last=False)
+            self.free.append(slot)
+        slot = self.free.pop()
+        idx = torch.tensor(pages, dtype=torch.long, device=self.cache.device)
+        for g in range(len(self.k)):
+            self.k[g][:, self._rows(slot)].copy_(self.cache.gk[g].index_select(1, idx))
+            self.v[g][:, self._rows(slot)].copy_(self.cache.gv[g].index_select(1, idx))
+        self.entries[h] = slot
+        self.stores += 1
+
+    def load(self, h: bytes, pages: list[int]) -> bool:
+        slot = self.entries.get(h)
+        if slot is None:
+            return False
+        self.entries.move_to_end(h)
+        idx = torch.tensor(pages, dtype=torch.long, device=self.cache.device)
+        for g in range(len(self.k)):
+            dev = self.cache.gk[g].device
+            self.cache.gk[g].index_copy_(1, idx, self.k[g][:, self._rows(slot)].to(dev, non_blocking=True))
+            self.cache.gv[g].index_copy_(1, idx, self.v[g][:, self._rows(slot)].to(dev, non_blocking=True))
+        self.loads += 1
+        return True
+
+    def block(self, h: bytes):
+        """(K, V) host tensors of a stored block, per group."""
+        slot = self.entries[h]
+        return [t[:, self._rows(slot)] for t in self.k], [t[:, self._rows(slot)] for t in self.v]
+
+
 class PrefixCache:
-    def __init__(self, cache: PagedKVCache, block_size: int = 256, default_salt: str = ""):
+    def __init__(self, cache: PagedKVCache, block_size: int = 256, default_salt: str = "", host_blocks: int = 0):
         assert block_size % PAGE == 0, "block size must be a multiple of the page size"
         self.cache = cache
         self.block = block_size
         self.pages_per_block = block_size // PAGE
         self.salt = default_salt
         self.entries: "collections.OrderedDict[bytes, list[int]]" = collections.OrderedDict()
+        self.host = HostTier(cache, host_blocks, self.pages_per_block) if host_blocks > 0 else None
         self.hits = 0
         self.misses = 0
         self.hit_tokens = 0
+        self.host_hits = 0
 
     def _hashes(self, tokens, salt):
         return _b200host.block_hashes(list(tokens), self.block, salt if salt is not None else self.salt)
@@ -43,8 +112,12 @@ class PrefixCache:
             return 0
         hashes = self._hashes(toks[: usable * self.block], req.cache_salt)
         pages = []
+        chain = set()
         for h in hashes:
             ent = self.entries.get(h)
+            if ent is None and self.host is not None and h in self.host.entries:
+                ent = self._promote(h, chain)
+            chain.add(h)
             if ent is None:
                 break
             self.entries.move_to_end(h)
@@ -79,18 +152,113 @@ class PrefixCache:
             self.cache.pool.incref(pages)
             self.entries[h] = list(pages)
 
-    def evict(self, need_pages: int) -> int:
-        """Free least-recently-used blocks whose pages only the cache holds."""
+    def _promote(self, h: bytes, keep=()):
+        """Bring a host-tier block back into fresh device pages, evicting
+        other least-recently-used device blocks (not those in `keep`) to make
+        room; None if the pool still has none."""
+        pool = self.cache.pool
+        if not pool.can_alloc(self.pages_per_block):
+            self.evict(self.pages_per_block - pool.num_free, keep)
+        if not pool.can_alloc(self.pages_per_block):
+            return None
+        pages = list(pool.alloc(self.pages_per_block))
+        self.host.load(h, pages)
+        self.entries[h] = pages
+        self.host_hits += 1
+        return pages
+
+    def evict(self, need_pages: int, keep=()) -> int:
+        """Free least-recently-used blocks whose pages only the cache holds
+        (copied to the host tier first when there is one), except `keep`."""
         freed = 0
         pool = self.cache.pool
         for h in list(self.entries.keys()):
             if freed >= need_pages:
                 break
+            if h in keep:
+                continue
             pages = self.entries[h]
             if all(pool.refcount(p) == 1 for p in pages):
+                if self.host is not None:
+                    self.host.store(h, pages)
                 del self.entries[h]
                 freed += pool.decref(pages)
         return freed
+
+    # ------------------------------------------------------------------ checkpoints
+    def save(self, path: str, shard_blocks: int = 64):
+        """Every cached block (device and host tier) to `path`: shards of
+        K / V tensors per block and layer group plus ``index.json`` (hash ->
+        shard), with the cache geometry it belongs to."""
+        from ..loader.safetensors import save_safetensors
+
+        os.makedirs(path, exist_ok=True)
+        blocks = []
+        for h, pages in self.entries.items():
+            idx = torch.tensor(pages, dtype=torch.long, device=self.cache.device)
+            blocks.append((h, [g.index_select(1, idx) for g in self.cache.gk],
+                           [g.index_select(1, idx) for g in self.cache.gv]))
+        if self.host is not None:
+            for h in self.host.entries:
+                if h not in self.entries:
+                    k, v = self.host.block(h)
+                    blocks.append((h, k, v))
+        index = {}
+        for s0 in range(0, len(blocks), shard_blocks):
+            name = f"prefix-{s0 // shard_blocks:05d}.safetensors"
+            tens = {}
+            for h, ks, vs in blocks[s0:s0 + shard_blocks]:
+                for g, (k, v) in enumerate(zip(ks, vs)):
+                    tens[f"{h.hex()}.{g}.k"] = k
+                    tens[f"{h.hex()}.{g}.v"] = v
+                index[h.hex()] = name
+            save_safetensors(os.path.join(path, name), tens)
+        meta = {"block_size": self.block, "group_shapes": [list(s) for s in self.cache.group_shapes],
+                "layers": [int(g.shape[0]) for g in self.cache.gk], "dtype": str(self.cache.gk[0].dtype),
+                "blocks": index}
+        with open(os.path.join(path, "index.json"), "w") as f:
+            json.dump(meta, f)
+        return len(blocks)
+
+    def load(self, path: str) -> int:
+        """Blocks saved by :meth:`save` into this cache (device pages while the
+        pool has room, then the host tier). The geometry must match."""
+        from ..loader.safetensors import load_safetensors
+
+        with open(os.path.join(path, "index.json")) as f:
+            meta = json.load(f)
+        if meta["block_size"] != self.block or meta["group_shapes"] != [list(s) for s in self.cache.group_shapes] \
+                or meta["layers"] != [int(g.shape[0]) for g in self.cache.gk]:
+            raise ValueError("prefix checkpoint was written for another cache geometry")
+        n = 0
+        by_shard: dict[str, list[str]] = {}
+        for hx, shard in meta["blocks"].items():
+            by_shard.setdefault(shard, []).append(hx)
+        pool = self.cache.pool
+        for shard, hxs in by_shard.items():
+            tens, _ = load_safetensors(os.path.join(path, shard))
+            for hx in hxs:
+                h = bytes.fromhex(hx)
+                if h in self.entries:
+                    continue
+                G = len(self.cache.gk)
+                if pool.can_alloc(self.pages_per_block):
+                    pages = list(pool.alloc(self.pages_per_block))
+                    idx = torch.tensor(pages, dtype=torch.long, device=self.cache.device)
+                    for g in range(G):
+                        self.cache.gk[g].index_copy_(1, idx, tens[f"{hx}.{g}.k"].to(self.cache.gk[g].device))
+                        self.cache.gv[g].index_copy_(1, idx, tens[f"{hx}.{g}.v"].to(self.cache.gv[g].device))
+                    self.entries[h] = pages
+                elif self.host is not None and self.host.free:
+                    slot = self.host.free.pop()
+                    for g in range(G):
+                        self.host.k[g][:, self.host._rows(slot)].copy_(tens[f"{hx}.{g}.k"])
+                        self.host.v[g][:, self.host._rows(slot)].copy_(tens[f"{hx}.{g}.v"])
+                    self.host.entries[h] = slot
+                else:
+                    break
+                n += 1
+        return n
 
     def clear(self):
         for pages in self.entries.values():
