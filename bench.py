@@ -67,6 +67,8 @@ def parse():
                     help="tensor-parallel collectives: fused symmetric-memory kernels (default with 2+ GPUs) or "
                          "NCCL all-reduce")
     ap.add_argument("--quant-experts", type=int, default=0, help="MLX affine bits for MoE experts (0 = bf16)")
+    ap.add_argument("--expert-format", default="affine", choices=["affine", "mxfp4"],
+                    help="quantised expert records: MLX affine (group 64) or MXFP4 (e2m1 + e8m0 per 32, GPT-OSS)")
     ap.add_argument("--quant-dense", type=int, default=0, help="MLX affine bits for dense projections (0 = bf16)")
     ap.add_argument("--mtp", type=int, default=0, help="MTP draft depth k (0 = off); acceptance: seeded Bernoulli(0.7)")
     ap.add_argument("--pp", type=int, default=1, help="pipeline stages (world = pp x tp); stages exchange hidden "
@@ -247,7 +249,8 @@ def _build(args, impl, world, rank, dev, group):
         from mlx_swift_lm_b200.models.quantize import quantize_model
 
         if args.quant_experts:
-            quantize_model(model, bits=args.quant_experts, group_size=64, dense=False, experts=True)
+            quantize_model(model, bits=args.quant_experts, group_size=64, dense=False, experts=True,
+                           mode=args.expert_format)
         if args.quant_dense:
             quantize_model(model, bits=args.quant_dense, group_size=64, dense=True, experts=False)
         torch.cuda.empty_cache()
@@ -442,7 +445,8 @@ def main():
                        "global_batch": args.streams,
                        "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}] + {args.out_tokens} out",
                        "parallelism": _par(args, world) if args.impl == "ours" else f"tp{world} (NCCL all_reduce)",
-                       "experts": f"q{args.quant_experts} g64" if args.quant_experts else "bf16", "mtp_k": args.mtp,
+                       "experts": ("mxfp4 g32" if args.expert_format == "mxfp4" else f"q{args.quant_experts} g64")
+                       if args.quant_experts else "bf16", "mtp_k": args.mtp,
                        "kv": ("paged fp8-e4m3 (per-head scales)" if args.kv_fp8 else "paged bf16") + ", page 16",
                        "sampling": ("greedy" if args.temperature <= 0 else
                                     f"temperature {args.temperature}, top_p {args.top_p}, per-request seeds"),
