@@ -286,6 +286,8 @@ def constraint_factory(vocab: GrammarVocabulary):
             return GrammarConstraint(vocab, rf["regex"])
         if t == "grammar":
             return CfgConstraint.from_ebnf(vocab, rf["grammar"], rf.get("root", "root"))
+        if t == "structural_tag":
+            return CfgConstraint.from_structural_tag(vocab, rf["structures"], rf["triggers"])
         return None
 
     return make
@@ -545,3 +547,95 @@ class CfgConstraint(GrammarConstraint):
     @classmethod
     def json_object(cls, vocab):
         return cls(vocab, "root ::= ws json-object ws\n" + JSON_EBNF_BASE)
+
+    @classmethod
+    def from_structural_tag(cls, vocab, structures, triggers):
+        return cls(vocab, structural_tag_to_ebnf(structures, triggers))
+
+
+# ----------------------------------------------------------------------------- structural tags
+def _byte_class(bs) -> str:
+    """EBNF byte class of the byte values `bs` (sorted ranges, \\xHH escapes)."""
+    bs = sorted(set(bs))
+    parts, i = [], 0
+    while i < len(bs):
+        j = i
+        while j + 1 < len(bs) and bs[j + 1] == bs[j] + 1:
+            j += 1
+        parts.append(f"\\x{bs[i]:02x}" if i == j else f"\\x{bs[i]:02x}-\\x{bs[j]:02x}")
+        i = j + 1
+    return "[" + "".join(parts) + "]"
+
+
+def structural_tag_to_ebnf(structures: list[dict], triggers: list[str]) -> str:
+    """EBNF of free text in which every occurrence of a trigger starts a tagged
+    call: ``begin`` (which starts with the trigger), a JSON document of the
+    tag's ``schema``, then ``end``; free text resumes after it. The free text
+    is the Aho-Corasick automaton of the triggers written as right-linear
+    rules (one per automaton state; tail calls keep the stack flat). Triggers
+    are ASCII. Parity: the structural tags of xgrammar
+    (Libraries/MLXCXGrammar/xgrammar/cpp/structural_tag.cc) as used for tool
+    calls."""
+    if not triggers:
+        raise ValueError("structural tag: at least one trigger")
+    for t in triggers:
+        if not t or any(ord(c) > 0x7F for c in t):
+            raise ValueError(f"structural tag: trigger {t!r} must be non-empty ASCII")
+    by_trigger: dict[str, list[dict]] = {t: [] for t in triggers}
+    for s in structures:
+        trig = next((t for t in triggers if s["begin"].startswith(t)), None)
+        if trig is None:
+            raise ValueError(f"structural tag: begin {s['begin']!r} starts with no trigger")
+        by_trigger[trig].append(s)
+    # Aho-Corasick over the trigger bytes
+    goto: list[dict[int, int]] = [{}]
+    out: list[str | None] = [None]
+    for t in triggers:
+        q = 0
+        for b in t.encode():
+            if b not in goto[q]:
+                goto.append({})
+                out.append(None)
+                goto[q][b] = len(goto) - 1
+            q = goto[q][b]
+        out[q] = t
+    fail = [0] * len(goto)
+    order = list(goto[0].values())
+    i = 0
+    while i < len(order):
+        q = order[i]
+        i += 1
+        for b, r in goto[q].items():
+            f = fail[q]
+            while f and b not in goto[f]:
+                f = fail[f]
+            fail[r] = goto[f][b] if b in goto[f] and goto[f][b] != r else 0
+            if out[r] is None and out[fail[r]] is not None:
+                out[r] = out[fail[r]]
+            order.append(r)
+
+    def step(q, b):
+        while q and b not in goto[q]:
+            q = fail[q]
+        return goto[q].get(b, 0)
+
+    conv = _SchemaEbnf({})
+    lines = ["root ::= text-0"]
+    for q in range(len(goto)):
+        if out[q] is not None:  # a trigger just completed: one of its tags follows
+            trig = out[q]
+            alts = []
+            for s in by_trigger[trig]:
+                body = conv.rule(s.get("schema", {}), "tag")
+                rest = s["begin"][len(trig):]
+                alts.append(" ".join(x for x in (_ebnf_lit(rest) if rest else "", f"ws {body} ws",
+                                                _ebnf_lit(s["end"]), "text-0") if x))
+            lines.append(f"text-{q} ::= " + (" | ".join(alts) if alts else '[^\\x00-\\xff]'))
+            continue
+        targets: dict[int, list[int]] = {}
+        for b in range(256):
+            targets.setdefault(step(q, b), []).append(b)
+        alts = ['""'] + [f"{_byte_class(bs)} text-{r}" for r, bs in sorted(targets.items())]
+        lines.append(f"text-{q} ::= " + " | ".join(alts))
+    lines += [f"{k} ::= {v}" for k, v in conv.rules.items()]
+    return "\n".join(lines) + "\n" + JSON_EBNF_BASE

@@ -27,6 +27,9 @@
 //     whole stack set (stack sets interned, byte transitions between them
 //     memoised), cached per stack set; EOS is allowed where the root rule
 //     can end;
+//   * calls in tail position (the return state only accepts) push no return
+//     frame, so right-recursive rules (free text up to a trigger, lists
+//     written as `x ::= item x | ""`) keep a constant stack depth;
 //   * rollback by history of stack sets, forced prefix (jump-forward) while a
 //     single byte is possible.
 // Left recursion (a rule reaching a call of itself without consuming input)
@@ -853,7 +856,12 @@ class Matcher {
       const DState& d = g_->st(f.rule, f.state);
       if (d.has_bytes || (d.accept && f.parent < 0)) out.push_back(n);
       for (auto& c : d.calls) {
-        const int ret = node(f.rule, c.second, f.parent);
+        // a call in tail position (its return state only accepts) returns
+        // straight to this frame's caller: right-recursive rules run in
+        // constant stack depth
+        const DState& rs = g_->st(f.rule, c.second);
+        const bool tail = rs.accept && !rs.has_bytes && rs.calls.empty();
+        const int ret = tail ? f.parent : node(f.rule, c.second, f.parent);
         const int child = node(c.first, 0, ret);
         if (!seen[child]) {
           seen[child] = 1;

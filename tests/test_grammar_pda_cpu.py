@@ -187,3 +187,36 @@ def test_cfg_guided_generation_through_engine():
     else:  # budget hit: still a valid prefix of some document
         c2 = CfgConstraint.from_json_schema(v, schema)
         assert c2.m.accept_string(text.encode())
+
+
+def test_structural_tag(mb_vocab):
+    """Free text with tagged tool calls: after the trigger the call must be
+    the tag's JSON schema and end string; near-misses of the trigger stay free
+    text; long free text keeps a flat stack (tail calls)."""
+    from mlx_swift_lm_b200.api.guided import structural_tag_to_ebnf
+
+    t, v = mb_vocab
+    schema = {"type": "object", "properties": {"name": {"enum": ["get_weather", "add"]},
+                                               "arguments": {"type": "object"}}, "required": ["name", "arguments"]}
+    g = structural_tag_to_ebnf([{"begin": "<tool_call>", "schema": schema, "end": "</tool_call>"}], ["<tool_call>"])
+    ok = ('Sure <tool> <tool_cal <b> let me check. <tool_call>{"name": "add", "arguments": {"a": 1}}</tool_call>'
+          ' and <tool_call>{"name": "get_weather", "arguments": {}}</tool_call> done')
+    c = CfgConstraint(v, g)
+    for ch in ok.encode():
+        assert ch in _allowed(c, 301), (ok, chr(ch))
+        c.commit(ch)
+        assert c.m.num_stacks <= 8
+    assert 300 in _allowed(c, 301)
+    for bad in ['x <tool_call>{"name": "rm"', 'x <tool_call>{"name": "add", "arguments": {}}</tool_cal> ']:
+        c = CfgConstraint(v, g)
+        good = True
+        for ch in bad.encode():
+            if ch not in _allowed(c, 301):
+                good = False
+                break
+            c.commit(ch)
+        assert not good, bad
+    c = CfgConstraint(v, g)
+    for ch in (b"free text " * 200):
+        c.commit(ch)
+    assert c.m.num_stacks <= 4
