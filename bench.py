@@ -244,11 +244,21 @@ def _build(args, impl, world, rank, dev, group):
         model = ExpertParallelDecoderLM(cfg, epc, dev, torch.bfloat16).init_random(args.seed)
         tp_size = 1
     else:
-        model = DecoderLM(cfg, dev, torch.bfloat16, tp=TensorParallel(rank, world, group)).init_random(args.seed)
+        hook = None
+        if impl == "ours" and args.quant_experts:
+            # quantise each layer's experts as it is drawn: the bf16 experts of
+            # a GPT-OSS-120B-shaped model alone would not fit on one device
+            from mlx_swift_lm_b200.models.quantize import quantize_layer
+
+            def hook(L):
+                return quantize_layer(L, dev, bits=args.quant_experts, group_size=64, dense=False, experts=True,
+                                      mode=args.expert_format)
+        model = DecoderLM(cfg, dev, torch.bfloat16, tp=TensorParallel(rank, world, group)).init_random(
+            args.seed, layer_hook=hook)
     if impl == "ours" and (args.quant_experts or args.quant_dense):
         from mlx_swift_lm_b200.models.quantize import quantize_model
 
-        if args.quant_experts:
+        if args.quant_experts:  # no-op for layers the init hook already quantised
             quantize_model(model, bits=args.quant_experts, group_size=64, dense=False, experts=True,
                            mode=args.expert_format)
         if args.quant_dense:

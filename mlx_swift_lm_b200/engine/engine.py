@@ -197,6 +197,7 @@ class EngineV2:
         self.background = False
         self.healthy = True
         self.on_step_wedge = None
+        self.comm_guard = None  # parallel.health.CommGuard of a multi-rank engine
         self.steps = 0
         self.last_step_ms = 0.0
         self._lock = threading.RLock()
@@ -428,13 +429,27 @@ class EngineV2:
         """Run one engine step; returns the events it emitted. With
         B200LM_NVTX=1 every step (and its forward / finalize phases) is an
         NVTX range, so a system profiler's timeline shows engine steps."""
-        if _NVTX and self.device.type == "cuda":
-            torch.cuda.nvtx.range_push(f"engine.step {self.steps}")
-            try:
-                return self._step()
-            finally:
-                torch.cuda.nvtx.range_pop()
-        return self._step()
+        guard = self.comm_guard
+        try:
+            if _NVTX and self.device.type == "cuda":
+                torch.cuda.nvtx.range_push(f"engine.step {self.steps}")
+                try:
+                    events = self._step()
+                finally:
+                    torch.cuda.nvtx.range_pop()
+            else:
+                events = self._step()
+        except Exception as e:
+            # a failed collective aborts the communicator and ends the live streams
+            if guard is not None and guard.on_step_error(e):
+                with self._lock:
+                    self._inflight = None
+                    self._step_started = None
+                return []
+            raise
+        if guard is not None:
+            guard.after_step(self.steps)
+        return events
 
     def _step(self) -> list[Event]:
         with self._lock:

@@ -211,14 +211,16 @@ class DecoderLM:
         return sum(t.numel() for _, t in self.named_tensors() if t is not None)
 
     def init_random(self, seed: int = 0, std: float = 0.02, with_embeddings: bool = True,
-                    keep_layers: tuple[int, int] | None = None):
+                    keep_layers: tuple[int, int] | None = None, layer_hook=None):
         """Random N(0, std) weights (norm weights 1, sinks N(0,1)), generated on
         the model's device. Every rank draws the full tensors from the same
         seed and keeps its tensor-parallel shard, so a TP=N model computes the
         same function as the TP=1 model of that seed. With `keep_layers`
         (lo, hi) every layer is still drawn (the generator advances exactly
         as for the full model) but only layers lo..hi-1 are kept: a pipeline
-        stage of the same function."""
+        stage of the same function. `layer_hook(L)` runs on each kept layer
+        as soon as it is drawn (quantising the experts of a model whose bf16
+        weights would not fit on the device at once)."""
         cfg = self.cfg
         g = torch.Generator(device=self.device)
         g.manual_seed(seed)
@@ -274,7 +276,7 @@ class DecoderLM:
                 L.ln2 = None
                 self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
                 if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
-                    self.layers.append(L)
+                    self.layers.append(L if layer_hook is None else layer_hook(L) or L)
                 continue
             if L.linear:
                 self._init_linear_layer(L, rn, g)
@@ -283,7 +285,7 @@ class DecoderLM:
                 else:
                     L.ln2 = None
                 if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
-                    self.layers.append(L)
+                    self.layers.append(L if layer_hook is None else layer_hook(L) or L)
                 continue
             if cfg.extra.get("mla"):
                 from . import mla
@@ -296,7 +298,7 @@ class DecoderLM:
                 if L.block == "both":
                     self._init_ffn(L, li, rn, ones, rows, cols, glu_pair)
                 if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
-                    self.layers.append(L)
+                    self.layers.append(L if layer_hook is None else layer_hook(L) or L)
                 continue
             wq, wk, wv = rn(cfg.q_size, hd), rn(cfg.kv_size, hd), rn(cfg.kv_size, hd)
             L.wqkv = torch.cat([rows(wq, self.H * D), kv_rows(wk), kv_rows(wv)], 0)
@@ -330,7 +332,7 @@ class DecoderLM:
                 L.post_attn_norm = ones(hd)
                 L.post_ffn_norm = ones(hd)
             if keep_layers is None or keep_layers[0] <= li < keep_layers[1]:
-                self.layers.append(L)
+                self.layers.append(L if layer_hook is None else layer_hook(L) or L)
         return self
 
     def _init_ffn(self, L, li, rn, ones, rows, cols, glu_pair):

@@ -152,8 +152,18 @@ class SiglipVisionTower:
         dev, E, NH, D = self.device, c.hidden_size, c.num_heads, c.head_dim
         B = pixels.shape[0]
         P = c.grid * c.grid
-        x = ops.gemm(self.patchify(pixels.to(dev, self.dtype), c.patch_size).contiguous(), self.patch_w,
-                     bias=self.patch_b)
+        patches = self.patchify(pixels.to(dev, self.dtype), c.patch_size)
+        w = self.patch_w
+        K = w.shape[1]
+        if patches.is_cuda and K % 8:
+            # the GEMM's TMA rows need K * 2 bytes to be a multiple of 16: zero
+            # columns pad both operands (C*14*14 = 588 for RGB patches of 14)
+            K8 = (K + 7) // 8 * 8
+            if getattr(self, "_patch_w8", None) is None or self._patch_w8.shape[1] != K8:
+                self._patch_w8 = torch.nn.functional.pad(w, (0, K8 - K)).contiguous()
+            w = self._patch_w8
+            patches = torch.nn.functional.pad(patches, (0, K8 - K))
+        x = ops.gemm(patches.contiguous(), w, bias=self.patch_b)
         x = (x.float() + self.pos.float().repeat(B, 1)).to(self.dtype)
         N = x.shape[0]
         Dk = D if D in (64, 128, 256) or not x.is_cuda else (64 if D < 64 else 128 if D < 128 else 256)

@@ -120,3 +120,73 @@ def test_max_over_ranks():
     for p in ps:
         p.join(60)
     assert out == [2.0, 5.0]
+
+
+def _guard_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    from mlx_swift_lm_b200 import DecoderLM, EngineConfig, EngineV2, SchedulerConfig
+    from mlx_swift_lm_b200.engine.types import Request
+    from mlx_swift_lm_b200.models.config import tiny_qwen3
+    from mlx_swift_lm_b200.models.decoder import TensorParallel
+    from mlx_swift_lm_b200.parallel.health import CommGuard
+
+    m = DecoderLM(tiny_qwen3(), "cpu", torch.float32, tp=TensorParallel(rank, world, dist.group.WORLD)).init_random(
+        3, std=0.2)
+    eng = EngineV2(m, config=EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=2), max_model_len=64,
+                                          use_cuda_graphs=False))
+    aborted = []
+    CommGuard(eng, dist.group.WORLD, abort_fn=lambda g: aborted.append(True))
+    s = eng.submit(Request(prompt_tokens=[5, 6, 7, 8], max_tokens=20))
+    for _ in range(3):  # both ranks step together
+        eng.step()
+    if rank == 1:
+        os._exit(0)  # leaves between steps, with nothing in flight
+    for _ in range(30):
+        if not eng.healthy:
+            break
+        eng.step()
+    evs = list(s.q)
+    q.put((eng.healthy, bool(aborted), evs[-1].cause if evs else None, evs[-1].finished if evs else None))
+
+
+def test_comm_guard_aborts_on_dead_rank():
+    """A rank that leaves: the survivor's next collective times out, the guard
+    aborts the communicator, the engine turns unhealthy and the stream ends
+    with cause comm_abort (no hang)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_guard_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    healthy, aborted, cause, finished = q.get(timeout=180)
+    for p in ps:
+        p.join(30)
+        if p.is_alive():
+            p.kill()
+    assert not healthy and aborted and cause == "comm_abort" and finished
+
+
+def test_comm_guard_reads_kernel_status():
+    class Eng:
+        healthy = True
+        on_step_wedge = None
+        states = {}
+
+    from mlx_swift_lm_b200.parallel.health import CommGuard
+
+    calls = []
+    e = Eng()
+    g = CommGuard(e, None, abort_fn=lambda grp: calls.append(grp), check_every=2,
+                  read_status=lambda clear=False: {"gemm": 0, "tp": 4})
+    g.after_step(1)
+    assert e.healthy
+    g.after_step(2)
+    assert not e.healthy and calls == [None] and "collective wait expired" in g.aborted
+    e2 = Eng()
+    g2 = CommGuard(e2, None, abort_fn=lambda grp: calls.append("w"))
+    e2.on_step_wedge()  # the watchdog's wedge callback aborts too
+    assert not e2.healthy and calls[-1] == "w"
