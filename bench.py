@@ -386,8 +386,26 @@ def run_arm(args, impl, world, rank, local, dev, group):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dev_ms, e2e_s = t.tolist()
+    # diagnostic: the decode graph replayed back to back (device time of one
+    # step with no host work between replays; not the reported value)
+    replay_ms = None
+    g = eng.graphs
+    if g is not None and args.streams in g.graphs:
+        barrier()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for _ in range(20):
+            model.begin_step()
+            g.graphs[args.streams].replay()
+        r1.record()
+        barrier()
+        rt = torch.tensor([r0.elapsed_time(r1) / 20], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(rt, op=dist.ReduceOp.MAX)
+        replay_ms = round(rt.item(), 4)
     st = mtp.stats if mtp is not None else None
     res = {
+        "diag": {"graph_replay_ms": replay_ms, "host_step_ms_p50": round(statistics.median(step_times) * 1e3, 3)},
         "value": round(tok_timed / (dev_ms / 1e3), 2), "ms_per_step": round(dev_ms / args.steps, 4),
         "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
         "itl_p50_ms": round(statistics.median(step_times) * 1e3, 3), "prefill_s": round(prefill_s, 3),
@@ -464,7 +482,8 @@ def main():
                        "timed": f"value: {args.steps} consecutive engine decode steps (64 rows, live KV positions) "
                                 f"after {args.warmup} warm-up steps, CUDA events, max over ranks"},
         })
-        for k in ("ttft_p50_ms", "itl_p50_ms", "prefill_s", "e2e", "gpu_launches", "clocks", "mtp", "kernel_status"):
+        for k in ("ttft_p50_ms", "itl_p50_ms", "prefill_s", "e2e", "gpu_launches", "clocks", "mtp", "kernel_status",
+                  "diag"):
             out[k] = res[k]
         out["receipt"] = receipt(dev)
         if base is not None:

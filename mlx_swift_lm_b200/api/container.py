@@ -54,7 +54,28 @@ class ModelContainer:
                 eos.add(ids[0])
         c = cls(model, tok, engine_config, eos, model_id=res.name, hf_config=hf)
         c.configuration = res
+        c._resolve_image_markers()
         return c
+
+    def _resolve_image_markers(self):
+        """SmolVLM tiling needs the ids of its marker tokens (SmolVLM2.swift:179-232);
+        without them images go in as one global tile."""
+        m = self.model
+        if getattr(m, "kind", None) != "idefics3" or not getattr(m, "tile_longest_edge", 0):
+            return
+        enc = getattr(self.tokenizer, "encode", None)
+        if enc is None:
+            return
+
+        def one(text):
+            ids = enc(text)
+            return ids[0] if len(ids) == 1 else None
+
+        fake = one("<fake_token_around_image>")
+        if fake is None:
+            return
+        m.marker_ids = {"fake": fake, "global": enc("<global-img>"), "newline": enc("\n"),
+                        "row": lambda r, c: enc(f"<row_{r + 1}_col_{c + 1}>")}
 
     @classmethod
     def random(cls, cfg, device="cpu", dtype=torch.float32, seed=0, std=0.02, engine_config=None, tokenizer=None):

@@ -277,6 +277,11 @@ class EngineV2:
             # placeholder token ids do not identify the image: no prefix reuse;
             # MTP drafts from text positions only
             req.prefix_cache_enabled = False
+            sc = self.cfg.scheduler
+            if req.mm.get("prefix_lm") and len(req.prompt_tokens) > min(sc.prefill_chunk_size,
+                                                                         sc.max_batched_tokens_per_step):
+                raise ValueError(f"a prefix-LM prompt of {len(req.prompt_tokens)} tokens is prefilled in one chunk: "
+                                 f"raise prefill_chunk_size / max_batched_tokens_per_step")
         from .reasoning import ReasoningBudgetState, resolve_budget
 
         budget = resolve_budget(req.reasoning_budget, self.cfg.reasoning_markers)

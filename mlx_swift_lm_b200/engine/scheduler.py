@@ -242,6 +242,9 @@ class Scheduler:
                 n = min(st.remaining, cfg.prefill_chunk_size, pbudget)
                 if n <= 0:
                     continue
+                mm = st.req.mm
+                if mm is not None and mm.get("prefix_lm") and st.num_computed == 0 and n < st.remaining:
+                    break  # a prefix-LM prompt attends both ways: it is prefilled in one chunk (FCFS kept)
                 if self.ledger is not None and not self.ledger.has_headroom(
                         self.ledger.admission_tokens(st.num_prompt, st.num_computed + n, st.req.max_tokens)):
                     break  # byte ledger above the admission watermark: admit later (FCFS order kept)

@@ -87,8 +87,8 @@ class CheckpointView:
         self.hadamard = hadamard  # Prism Hadamard metadata (loader.prism.HadamardMetadata)
         keys = list(tensors)
         self.prefix = ""
-        for pre in ("model.language_model.", "language_model.model.", "model.", "transformer.", "encoder.", "backbone.",
-                    ""):
+        for pre in ("model.language_model.", "language_model.model.", "model.text_model.", "text_model.", "model.",
+                    "transformer.", "encoder.", "backbone.", ""):
             if any(k.startswith(pre + "layers.0.") or k.startswith(pre + "embed_tokens") or k.startswith(pre + "embeddings.")
                    for k in keys):
                 self.prefix = pre
@@ -475,8 +475,8 @@ def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParalle
     model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized, hadamard=hadamard)
     if hf.get("vision_config") and hf.get("model_type") in ("qwen2_vl", "qwen2_5_vl"):
         model = _attach_vision(model, cfg, hf, tensors, device, dtype)
-    elif hf.get("vision_config") and hf.get("model_type") == "gemma3":
-        model = _attach_siglip(model, cfg, hf, tensors, device, dtype)
+    elif hf.get("vision_config") and hf.get("model_type") in ("gemma3", "paligemma", "idefics3", "smolvlm"):
+        model = _attach_siglip(model, cfg, hf, tensors, device, dtype, path)
     if with_mtp:
         from ..models.mtp import load_mtp
 
@@ -500,20 +500,55 @@ def _attach_vision(lm, cfg, hf, tensors, device, dtype):
     return m
 
 
-def _attach_siglip(lm, cfg, hf, tensors, device, dtype):
-    """Gemma 3 VLM: the loaded language model plus the SigLIP tower and the
-    pooled projector (``multi_modal_projector.*``) as one Gemma3VLModel."""
-    from ..models.siglip import Gemma3VLModel, SiglipConfig, SiglipVisionTower
+def _attach_siglip(lm, cfg, hf, tensors, device, dtype, path=None):
+    """SigLIP-tower VLMs: the loaded language model plus the vision tower and
+    the connector as one :class:`..models.siglip.SiglipVLM` - Gemma 3 (pooled
+    projector ``multi_modal_projector.*``), PaliGemma (``multi_modal_projector
+    .linear``), Idefics3 / SmolVLM (``connector.modality_projection.proj``)."""
+    from ..models.siglip import SiglipConfig, SiglipVisionTower, SiglipVLM
 
-    vcfg = SiglipConfig.from_hf(hf["vision_config"])
-    m = Gemma3VLModel(cfg, vcfg, device, dtype, hf.get("image_token_index", hf.get("image_token_id", 262144)),
+    mt = hf["model_type"]
+    vc = hf["vision_config"]
+    vcfg = SiglipConfig.from_hf(vc)
+    itok = hf.get("image_token_index", hf.get("image_token_id"))
+    if mt == "gemma3":
+        m = SiglipVLM(cfg, vcfg, device, dtype, "gemma3", itok if itok is not None else 262144,
                       hf.get("mm_tokens_per_image", 256))
+    elif mt == "paligemma":
+        m = SiglipVLM(cfg, vcfg, device, dtype, "paligemma", itok if itok is not None else 257152,
+                      vc.get("num_image_tokens", vcfg.grid * vcfg.grid))
+    else:
+        sf = int(hf.get("scale_factor", 2))
+        m = SiglipVLM(cfg, vcfg, device, dtype, "idefics3", itok if itok is not None else 128257,
+                      (vcfg.grid // sf) ** 2, sf)
     m.embed, m.norm, m.lm_head, m.layers = lm.embed, lm.norm, lm.lm_head, lm.layers
     m.vision = SiglipVisionTower.from_tensors(vcfg, tensors, device, dtype)
-    pre = next(p for p in ("model.multi_modal_projector.", "multi_modal_projector.")
-               if p + "mm_input_projection_weight" in tensors)
-    m.proj_w = tensors[pre + "mm_input_projection_weight"].to(device, dtype)
-    m.proj_norm = tensors[pre + "mm_soft_emb_norm.weight"].to(device, dtype)
+
+    def find(*names):
+        for n in names:
+            for pre in ("model.multi_modal_projector.", "multi_modal_projector.", "model.connector.", "connector."):
+                if pre + n in tensors:
+                    return tensors[pre + n].to(device, dtype)
+        return None
+
+    if mt == "gemma3":
+        m.proj_w = find("mm_input_projection_weight")
+        m.proj_norm = find("mm_soft_emb_norm.weight")
+    elif mt == "paligemma":
+        m.proj_w, m.proj_b = find("linear.weight"), find("linear.bias")
+    else:
+        m.proj_w = find("modality_projection.proj.weight")
+    if m.proj_w is None:
+        raise KeyError(f"no {mt} projector weights")
+    if path is not None:  # processor: normalisation and (SmolVLM) tiling
+        pp = os.path.join(path, "preprocessor_config.json")
+        if os.path.exists(pp):
+            with open(pp) as f:
+                pc = json.load(f)
+            m.image_mean = tuple(pc.get("image_mean", m.image_mean))
+            m.image_std = tuple(pc.get("image_std", m.image_std))
+            if mt == "smolvlm" and pc.get("do_image_splitting", True):
+                m.tile_longest_edge = int((pc.get("size") or {}).get("longest_edge", 0))
     return m
 
 

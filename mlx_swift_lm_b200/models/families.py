@@ -187,7 +187,7 @@ def supported_model_types() -> list[str]:
 
 def build_config(hf: dict) -> DecoderConfig:
     """Translate a HF / MLX config.json dict."""
-    if "text_config" in hf and "hidden_size" not in hf:
+    if "text_config" in hf and ("hidden_size" not in hf or hf.get("model_type") not in FAMILIES):
         hf = {**hf["text_config"], "model_type": hf["text_config"].get("model_type", hf.get("model_type"))}
     mt = hf.get("model_type", "llama")
     if mt in _REFUSED:

@@ -120,7 +120,8 @@ class SiglipVisionTower:
     @classmethod
     def from_tensors(cls, cfg: SiglipConfig, t: dict, device="cpu", dtype=torch.float32):
         pre = next((p for p in ("vision_tower.vision_model.", "model.vision_tower.vision_model.",
-                                "vision_model.", "") if p + "embeddings.patch_embedding.weight" in t), None)
+                                "vision_model.", "model.vision_model.", "vision_tower.", "model.vision_tower.", "")
+                    if p + "embeddings.patch_embedding.weight" in t), None)
         if pre is None:
             raise KeyError("no SigLIP weights (vision_model.embeddings.patch_embedding.weight)")
         m = cls(cfg)
@@ -209,83 +210,263 @@ def siglip_pixels(image, size: int, mean=(0.5, 0.5, 0.5), std=(0.5, 0.5, 0.5)) -
     return (t - m) / s
 
 
-class Gemma3VLModel(DecoderLM):
-    """Gemma 3 language model + SigLIP tower + pooled projector; multimodal
-    requests carry ``Request.mm`` from :meth:`prepare`."""
+def _image_tensor(image) -> torch.Tensor:
+    """An image (PIL, HWC uint8 / float array or CHW tensor) as [3, H, W] fp32 in [0, 1]."""
+    import numpy as np
 
-    def __init__(self, cfg, vision_cfg: SiglipConfig, device="cpu", dtype=torch.float32,
-                 image_token_id: int = 262144, mm_tokens: int = 256):
+    if hasattr(image, "convert"):
+        image = np.asarray(image.convert("RGB"))
+    t = torch.as_tensor(np.asarray(image) if not torch.is_tensor(image) else image).float()
+    if t.dim() == 3 and t.shape[-1] in (1, 3, 4) and t.shape[0] not in (1, 3):
+        t = t[..., :3].permute(2, 0, 1)
+    if t.max() > 1.5:
+        t = t / 255.0
+    return t
+
+
+def _resize(t: torch.Tensor, h: int, w: int) -> torch.Tensor:
+    if tuple(t.shape[-2:]) == (h, w):
+        return t
+    return torch.nn.functional.interpolate(t[None], size=(h, w), mode="bicubic", align_corners=False,
+                                           antialias=True)[0].clamp(0.0, 1.0)
+
+
+def smolvlm_tiles(image, tile: int, longest: int) -> tuple[list[torch.Tensor], int, int]:
+    """SmolVLM's image split (SmolVLM2.swift:264-299): the image resized so its
+    longest edge is min(longest, its own) and each side is a multiple of
+    `tile` (aspect kept), cut into rows x cols tiles of `tile` pixels in
+    row-major order, plus the whole image resized to tile x tile last.
+    Returns ([3, tile, tile] tiles in [0, 1], rows, cols)."""
+    t = _image_tensor(image)
+    H, W = t.shape[-2:]
+    edge = min(longest, max(H, W))
+    if W >= H:
+        w1 = edge
+        h1 = edge * H / W
+        w2 = -(-w1 // tile) * tile
+        h2 = -(-int(round(w2 * H / W)) // tile) * tile
+    else:
+        h1 = edge
+        w1 = edge * W / H
+        h2 = -(-h1 // tile) * tile
+        w2 = -(-int(round(h2 * W / H)) // tile) * tile
+    h2, w2 = max(int(h2), tile), max(int(w2), tile)
+    big = _resize(t, h2, w2)
+    rows, cols = h2 // tile, w2 // tile
+    tiles = [big[:, r * tile:(r + 1) * tile, c * tile:(c + 1) * tile] for r in range(rows) for c in range(cols)]
+    tiles.append(_resize(t, tile, tile))
+    return tiles, rows, cols
+
+
+class SiglipVLM(DecoderLM):
+    """A decoder language model with a SigLIP-family vision tower and one of
+    the connectors built on it; multimodal requests carry ``Request.mm`` from
+    :meth:`prepare` (image features replace the image placeholder rows).
+
+    Connectors (``kind``):
+
+    * ``gemma3`` (Gemma3.swift:783-850): the patch grid average-pooled to
+      ``mm_tokens`` tokens, Gemma RMSNorm (weights stored w - 1), a
+      [vision, text] projection; one placeholder expands to ``mm_tokens``.
+    * ``paligemma`` (Paligemma.swift:505-600): a biased linear projection; the
+      features are divided by sqrt(text hidden) and the decoder's embedding
+      scale multiplies them back, so the rows are the projection itself; the
+      prompt is ``mm_tokens`` image tokens then the text, and the whole prompt
+      (image and text) attends both ways (prefix-LM: the prompt is prefilled
+      in one chunk, generated tokens attend causally).
+    * ``idefics3`` (Idefics3.swift:136-183, 629-760; SmolVLM2.swift for
+      ``smolvlm``): pixel shuffle by ``scale_factor`` (each s x s block of
+      patches concatenated into one token) and a bias-free linear projection;
+      ``image_seq_len`` tokens per image (tile). A prompt without a
+      placeholder gets the image tokens at its middle (the reference
+      processor's rule). ``smolvlm`` also splits large images into tiles with
+      row / column marker tokens when ``marker_ids`` are known.
+    """
+
+    def __init__(self, cfg, vision_cfg: SiglipConfig, device="cpu", dtype=torch.float32, kind: str = "gemma3",
+                 image_token_id: int = 262144, mm_tokens: int = 256, scale_factor: int = 1):
         super().__init__(cfg, device, dtype)
+        self.kind = kind
         self.vision = SiglipVisionTower(vision_cfg, device, dtype)
         self.image_token_id = image_token_id
         self.mm_tokens = mm_tokens
-        self.proj_norm = None  # [vision hidden] (Gemma RMSNorm weight, stored w - 1)
-        self.proj_w = None  # [vision hidden, text hidden]
+        self.scale_factor = scale_factor
+        self.proj_norm = None  # gemma3: [vision hidden] (Gemma RMSNorm weight, stored w - 1)
+        self.proj_w = None  # gemma3: [vision hidden, text hidden]; others: [text hidden, in] (nn.Linear)
+        self.proj_b = None  # paligemma: [text hidden]
+        self.image_mean = (0.5, 0.5, 0.5)
+        self.image_std = (0.5, 0.5, 0.5)
+        # smolvlm tiling: ids of '<fake_token_around_image>' ("fake"), '<global-img>' ("global"),
+        # "\n" ("newline"), and row(r, c) -> ids of '<row_{r+1}_col_{c+1}>'
+        self.marker_ids: dict | None = None
+        self.tile_longest_edge = 0
 
-    def init_random(self, seed: int = 0, std: float = 0.02, with_embeddings: bool = True, keep_layers=None):
-        super().init_random(seed, std, with_embeddings, keep_layers)
+    @property
+    def prefix_lm(self) -> bool:
+        return self.kind == "paligemma"
+
+    def _proj_in(self) -> int:
+        E = self.vision.cfg.hidden_size
+        return E * self.scale_factor ** 2 if self.kind == "idefics3" else E
+
+    def init_random(self, seed: int = 0, std: float = 0.02, with_embeddings: bool = True, keep_layers=None,
+                    layer_hook=None):
+        super().init_random(seed, std, with_embeddings, keep_layers, layer_hook)
         self.vision.init_random(seed + 17, std)
         g = torch.Generator().manual_seed(seed + 29)
-        E = self.vision.cfg.hidden_size
-        self.proj_norm = torch.zeros(E, device=self.device, dtype=self.dtype)
-        self.proj_w = torch.empty(E, self.cfg.hidden_size).normal_(0.0, std, generator=g).to(self.device, self.dtype)
+        E, Hd = self.vision.cfg.hidden_size, self.cfg.hidden_size
+        if self.kind == "gemma3":
+            self.proj_norm = torch.zeros(E, device=self.device, dtype=self.dtype)
+            self.proj_w = torch.empty(E, Hd).normal_(0.0, std, generator=g).to(self.device, self.dtype)
+        else:
+            self.proj_w = torch.empty(Hd, self._proj_in()).normal_(0.0, std, generator=g).to(self.device, self.dtype)
+            if self.kind == "paligemma":
+                self.proj_b = torch.empty(Hd).normal_(0.0, std, generator=g).to(self.device, self.dtype)
         return self
+
+    def _same_kind(self, device, dtype):
+        out = SiglipVLM(self.cfg, self.vision.cfg, device, dtype, self.kind, self.image_token_id, self.mm_tokens,
+                        self.scale_factor)
+        out.__class__ = self.__class__
+        return out
 
     def clone_to(self, device, dtype):
         m = super().clone_to(device, dtype)
-        out = Gemma3VLModel(self.cfg, self.vision.cfg, device, dtype, self.image_token_id, self.mm_tokens)
+        out = self._same_kind(device, dtype)
         out.embed, out.norm, out.lm_head, out.layers = m.embed, m.norm, m.lm_head, m.layers
         v = SiglipVisionTower(self.vision.cfg)
         v.patch_w, v.patch_b, v.pos, v.post_w, v.post_b = (self.vision.patch_w, self.vision.patch_b, self.vision.pos,
                                                          self.vision.post_w, self.vision.post_b)
         v.layers = [{k: t for k, t in L.items() if k not in ("qkv_w", "qkv_b")} for L in self.vision.layers]
         out.vision = v.to(device, dtype)
-        out.proj_norm, out.proj_w = self.proj_norm.to(device, dtype), self.proj_w.to(device, dtype)
+        for n in ("proj_norm", "proj_w", "proj_b"):
+            t = getattr(self, n)
+            setattr(out, n, None if t is None else t.to(device, dtype))
+        out.image_mean, out.image_std = self.image_mean, self.image_std
+        out.marker_ids, out.tile_longest_edge = self.marker_ids, self.tile_longest_edge
         return out
+
+    @staticmethod
+    def pixel_shuffle(f: torch.Tensor, s: int) -> torch.Tensor:
+        """[B, P, E] -> [B, P / s^2, E * s^2]: each s x s block of the patch
+        grid becomes one token (Idefics3.swift:145-173)."""
+        B, P, E = f.shape
+        n = int(round(P ** 0.5))
+        x = f.reshape(B, n, n // s, E * s).permute(0, 2, 1, 3)
+        x = x.reshape(B, n // s, n // s, E * s * s).permute(0, 2, 1, 3)
+        return x.reshape(B, P // (s * s), E * s * s)
 
     @torch.no_grad()
     def image_embeddings(self, pixels: torch.Tensor) -> torch.Tensor:
         """[B, C, S, S] -> [B * mm_tokens, text hidden]."""
         f = self.vision.forward(pixels)  # [B, P, E]
         B, P, E = f.shape
-        n = self.vision.cfg.grid
-        side = int(round(self.mm_tokens ** 0.5))
-        k = n // side
-        pooled = f.float().view(B, side, k, side, k, E).mean((2, 4)).reshape(B * side * side, E)
-        h = ops.rmsnorm(pooled.to(self.dtype).contiguous(), self.proj_norm, self.vision.cfg.eps, True)
-        return ops.gemm(h, self.proj_w.t().contiguous())
+        if self.kind == "gemma3":
+            n = self.vision.cfg.grid
+            side = int(round(self.mm_tokens ** 0.5))
+            k = n // side
+            pooled = f.float().view(B, side, k, side, k, E).mean((2, 4)).reshape(B * side * side, E)
+            h = ops.rmsnorm(pooled.to(self.dtype).contiguous(), self.proj_norm, self.vision.cfg.eps, True)
+            return ops.gemm(h, self.proj_w.t().contiguous())
+        if self.kind == "paligemma":
+            y = ops.gemm(f.reshape(B * P, E).contiguous(), self.proj_w, bias=self.proj_b)
+            # / sqrt(hidden) then the decoder's x sqrt(hidden): the rounded round trip of the reference
+            sc = float(self.cfg.hidden_size) ** 0.5
+            return ((y.float() / sc).to(self.dtype).float() * self.cfg.embed_scale).to(self.dtype)
+        x = self.pixel_shuffle(f, self.scale_factor)
+        return ops.gemm(x.reshape(-1, x.shape[-1]).contiguous(), self.proj_w)
+
+    def _pixels(self, image) -> torch.Tensor:
+        size = self.vision.cfg.image_size
+        t = _resize(_image_tensor(image), size, size)
+        m = torch.tensor(self.image_mean)[:, None, None]
+        s = torch.tensor(self.image_std)[:, None, None]
+        return (t - m) / s
+
+    def _image_token_run(self, n_tiles: int, rows: int, cols: int) -> list[int]:
+        """SmolVLM prompt of one tiled image (SmolVLM2.swift:208-232)."""
+        mk = self.marker_ids
+        run = []
+        for r in range(rows):
+            for c in range(cols):
+                run += [mk["fake"]] + list(mk["row"](r, c)) + [self.image_token_id] * self.mm_tokens
+            run += list(mk["newline"])
+        run += list(mk["newline"]) + [mk["fake"]] + list(mk["global"]) + [self.image_token_id] * self.mm_tokens
+        return run + [mk["fake"]]
 
     @torch.no_grad()
     def prepare(self, prompt_tokens: list[int], media) -> tuple[list[int], dict | None]:
-        """Expand each image placeholder to mm_tokens image tokens and encode
-        the images. Returns (tokens, mm) with mm = {embeds, image_pos,
-        prompt_len}; positions stay 1-D."""
+        """Expand the image placeholders and encode the images. Returns
+        (tokens, mm) with mm = {embeds, image_pos, prompt_len, delta[, prefix_lm]};
+        positions stay 1-D."""
         images = list(getattr(media, "images", None) or []) if media is not None else []
         if not images:
             return list(prompt_tokens), None
-        size = self.vision.cfg.image_size
-        pix = torch.stack([siglip_pixels(im, size) for im in images])
+        it = self.image_token_id
+        toks = list(prompt_tokens)
+        if self.kind == "idefics3" and self.marker_ids and self.tile_longest_edge:
+            if len(images) != 1:
+                raise ValueError("SmolVLM serves one image per request")
+            tile = self.vision.cfg.image_size
+            tiles, rows, cols = smolvlm_tiles(images[0], tile, self.tile_longest_edge)
+            m = torch.tensor(self.image_mean)[:, None, None]
+            s = torch.tensor(self.image_std)[:, None, None]
+            pix = torch.stack([(t - m) / s for t in tiles])
+            run = self._image_token_run(len(tiles), rows, cols) if rows * cols > 1 else (
+                [self.marker_ids["fake"]] + list(self.marker_ids["global"]) + [it] * self.mm_tokens
+                + [self.marker_ids["fake"]])
+            if rows * cols == 1:
+                pix = pix[-1:]
+            if it in toks:
+                j = toks.index(it)
+                toks = toks[:j] + run + toks[j + 1:]
+            else:
+                j = len(toks) // 2
+                toks = toks[:j] + run + toks[j:]
+        else:
+            pix = torch.stack([self._pixels(im) for im in images])
+            n_ph = sum(1 for t in toks if t == it)
+            if n_ph == 0:
+                run = [it] * (self.mm_tokens * len(images))
+                j = 0 if self.kind == "paligemma" else len(toks) // 2
+                toks = toks[:j] + run + toks[j:]
+            elif n_ph == len(images):
+                out = []
+                for t in toks:
+                    out.extend([t] * self.mm_tokens if t == it else [t])
+                toks = out
+            elif n_ph != self.mm_tokens * len(images):
+                raise ValueError(f"{n_ph} image tokens for {len(images)} images of {self.mm_tokens} tokens")
         emb = self.image_embeddings(pix)
-        toks = []
-        for t in prompt_tokens:
-            toks.extend([t] * self.mm_tokens if t == self.image_token_id else [t])
-        image_pos = [i for i, t in enumerate(toks) if t == self.image_token_id]
-        assert len(image_pos) == emb.shape[0], "one image per placeholder token"
-        return toks, {"embeds": emb, "image_pos": torch.tensor(image_pos), "prompt_len": len(toks), "delta": 0}
+        image_pos = [i for i, t in enumerate(toks) if t == it]
+        if len(image_pos) != emb.shape[0]:
+            raise ValueError(f"{len(image_pos)} image tokens for {emb.shape[0]} image features")
+        mm = {"embeds": emb, "image_pos": torch.tensor(image_pos), "prompt_len": len(toks), "delta": 0}
+        if self.prefix_lm:
+            mm["prefix_lm"] = True
+        return toks, mm
 
     def forward(self, fb, kv, return_hidden: bool = False, inputs_embeds=None, return_both=False,
                 return_residual=False):
         states = getattr(fb, "row_states", None)
         rows = []
+        whole_prompts = True
         if inputs_embeds is None and states:
             nd = fb.num_decode
             pf = fb.pf_cu_q_host or [0]
             for i, st in enumerate(states):
-                mm = st.req.mm if st is not None else None
-                if mm is None or i < nd:
+                if i < nd:
                     continue
+                mm = st.req.mm if st is not None else None
                 a, n = nd + pf[i - nd], pf[i - nd + 1] - pf[i - nd]
-                rows.append((a, n, int(fb.pf_pos0_host[i - nd]), mm))
+                p0 = int(fb.pf_pos0_host[i - nd])
+                if mm is None or not mm.get("prefix_lm") or p0 != 0 or n != mm["prompt_len"]:
+                    whole_prompts = False
+                if mm is not None:
+                    rows.append((a, n, p0, mm))
+        if self.prefix_lm and rows and whole_prompts and fb.num_tokens > fb.num_decode:
+            # prefix-LM: every prefill row is a whole image + text prompt
+            fb.bidirectional = True
         if not rows:
             return super().forward(fb, kv, return_hidden, inputs_embeds, return_both, return_residual)
         x = ops.embedding(fb.input_ids, self.embed, self.cfg.embed_scale).clone()
@@ -294,4 +475,16 @@ class Gemma3VLModel(DecoderLM):
             sel = ((ip >= p0) & (ip < p0 + n)).nonzero()[:, 0]
             if len(sel):
                 x[(ip[sel] - p0 + a).to(x.device)] = mm["embeds"][sel.to(mm["embeds"].device)].to(x.dtype)
-        return super().forward(fb, kv, return_hidden, x, return_both, return_residual)
+        try:
+            return super().forward(fb, kv, return_hidden, x, return_both, return_residual)
+        finally:
+            if self.prefix_lm:
+                fb.bidirectional = False
+
+
+class Gemma3VLModel(SiglipVLM):
+    """Gemma 3 language model + SigLIP tower + pooled projector."""
+
+    def __init__(self, cfg, vision_cfg: SiglipConfig, device="cpu", dtype=torch.float32,
+                 image_token_id: int = 262144, mm_tokens: int = 256):
+        super().__init__(cfg, vision_cfg, device, dtype, "gemma3", image_token_id, mm_tokens)
