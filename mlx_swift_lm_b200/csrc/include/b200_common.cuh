@@ -349,6 +349,23 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
+// Gated activations of an interleaved gate/up projection (codes shared with
+// the GEMM epilogues): silu(g) * u, gelu-tanh(g) * u, and GPT-OSS's clamped
+// (u + 1) * g * sigmoid(1.702 g).
+enum GluKind : int { kGluSwi = 1, kGluGe = 4, kGluOAI = 5 };
+__device__ __forceinline__ float glu_act(int kind, float g, float u) {
+  if (kind == kGluGe) {
+    const float c = 0.7978845608028654f;  // sqrt(2/pi)
+    return 0.5f * g * (1.f + tanhf(c * (g + 0.044715f * g * g * g))) * u;
+  }
+  if (kind == kGluOAI) {
+    g = fminf(g, 7.f);
+    u = fminf(fmaxf(u, -7.f), 7.f);
+    return (u + 1.f) * g / (1.f + __expf(-1.702f * g));
+  }
+  return silu(g) * u;
+}
+
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch (PDL). Kernels are launched with programmatic
 // stream serialization, so the next kernel may start while this one runs.

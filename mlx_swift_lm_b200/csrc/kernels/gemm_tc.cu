@@ -81,18 +81,7 @@ __device__ __forceinline__ float gelu_act(int epi, float x) {
   return 0.5f * x * (1.f + tanhf(c * (x + 0.044715f * x * x * x)));
 }
 
-__device__ __forceinline__ float glu_act(int epi, float g, float u) {
-  if (epi == kEpiGeGLU) {
-    const float c = 0.7978845608028654f;  // sqrt(2/pi)
-    return 0.5f * g * (1.f + tanhf(c * (g + 0.044715f * g * g * g))) * u;
-  }
-  if (epi == kEpiSwiGLUOAI) {
-    g = fminf(g, 7.f);
-    u = fminf(fmaxf(u, -7.f), 7.f);
-    return (u + 1.f) * g / (1.f + __expf(-1.702f * g));
-  }
-  return silu(g) * u;
-}
+static_assert(kEpiSwiGLU == kGluSwi && kEpiGeGLU == kGluGe && kEpiSwiGLUOAI == kGluOAI, "glu_act codes");
 
 struct GemmArgs {
   void* Y;

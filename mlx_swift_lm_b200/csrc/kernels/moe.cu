@@ -165,18 +165,7 @@ struct GArgs {
   int N, K, ldy, epi;
 };
 
-__device__ __forceinline__ float glu(int epi, float g, float u) {
-  if (epi == 4) {
-    const float c = 0.7978845608028654f;
-    return 0.5f * g * (1.f + tanhf(c * (g + 0.044715f * g * g * g))) * u;
-  }
-  if (epi == 5) {
-    g = fminf(g, 7.f);
-    u = fminf(fmaxf(u, -7.f), 7.f);
-    return (u + 1.f) * g / (1.f + __expf(-1.702f * g));
-  }
-  return silu(g) * u;
-}
+__device__ __forceinline__ float glu(int epi, float g, float u) { return glu_act(epi, g, u); }
 
 // Quantised expert weights (WQ = 4 or 8): codes [E*N, K*WQ/8] bytes,
 // scales / biases [K/gs, E*N] bf16 (layout of b200_dequant.cuh).

@@ -282,6 +282,13 @@ class EngineV2:
                                                                          sc.max_batched_tokens_per_step):
                 raise ValueError(f"a prefix-LM prompt of {len(req.prompt_tokens)} tokens is prefilled in one chunk: "
                                  f"raise prefill_chunk_size / max_batched_tokens_per_step")
+        lora_slot = -1
+        if req.lora is not None:
+            bl = getattr(self.model, "batched_lora", None)
+            if bl is None:
+                raise ValueError(f"request names adapter {req.lora!r} but the model serves no batched adapters "
+                                 "(attach adapters.batched.BatchedLoRA, or merge the adapter)")
+            lora_slot = bl.slot(req.lora)
         from .reasoning import ReasoningBudgetState, resolve_budget
 
         budget = resolve_budget(req.reasoning_budget, self.cfg.reasoning_markers)
@@ -304,6 +311,8 @@ class EngineV2:
             if self.tok is not None:
                 st.detok = IncrementalDetokenizer(self.tok)
             st.extra["hold"] = StopHoldback(req.stop_strings)
+            if lora_slot >= 0:
+                st.extra["lora_slot"] = lora_slot
             if budget is not None:
                 st.extra["budget"] = ReasoningBudgetState(budget)
             stream = RequestStream(self, st)
@@ -387,10 +396,14 @@ class EngineV2:
         fb.pf_pos0_host = [r.start for r in rows[nd:]]
         if self.kv.rec is not None:
             fb.state_slots = torch.tensor([r.state.seq.state_slot for r in rows], dtype=torch.int32)
+        if getattr(self.model, "batched_lora", None) is not None and any(
+                r.state.extra.get("lora_slot", -1) >= 0 for r in rows):
+            fb.lora_slots = torch.tensor([r.state.extra.get("lora_slot", -1) for r in rows
+                                          for _ in range(r.num_tokens)], dtype=torch.int32)
         if dev.type == "cuda":
             for name in ("input_ids", "positions", "slots", "dec_page_table", "dec_seq_lens", "pf_cu_q", "pf_pos0",
                          "pf_page_table", "logit_idx", "state_slots", "ring_slots", "ring_dec_page_table",
-                         "ring_pf_page_table"):
+                         "ring_pf_page_table", "lora_slots"):
                 t = getattr(fb, name)
                 if t is not None:
                     self.h2d_bytes += t.numel() * t.element_size()
@@ -563,13 +576,15 @@ class EngineV2:
 
     def _row_needs_eager(self, st) -> bool:
         """Rows the captured decode graphs cannot serve: logit processing
-        (bias, penalties), token masks (grammar, reasoning budget), logprobs,
-        adapters. Plain temperature / top-k / top-p / min-p sampling runs in
-        the sampled graph variant when the model supports it."""
+        (bias, penalties), token masks (grammar, reasoning budget), logprobs.
+        Plain temperature / top-k / top-p / min-p sampling runs in the sampled
+        graph variant when the model supports it; batched-LoRA rows in the
+        LoRA variants."""
         sp = st.req.sampling
         sampled_ok = self.graphs is not None and getattr(self.graphs, "sampling", False)
         return ((not sp.greedy and not sampled_ok) or st.req.token_constraint is not None or sp.logprobs
-                or sp.top_logprobs > 0 or sp.needs_processing or st.req.lora is not None or "budget" in st.extra)
+                or sp.top_logprobs > 0 or sp.needs_processing or "budget" in st.extra
+                or (st.req.lora is not None and getattr(self.model, "tp_fused", None) is not None))
 
     def _finalize_inflight(self, inflight) -> list[Event]:
         plan, handle = inflight

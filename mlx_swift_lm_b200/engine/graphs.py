@@ -60,6 +60,9 @@ class DecodeGraphRunner:
             self.o_rslots = self.n_i32 + self.n_i32 % 2
             self.o_rpt = self.o_rslots + 2 * B
             self.n_i32 = self.o_rpt + B * P
+        # per-row batched-LoRA adapter slot (-1 = none)
+        self.o_lora = self.n_i32
+        self.n_i32 += B
         self.rec = engine.kv.rec
         self.packed = torch.zeros(self.n_i32, dtype=torch.int32, device=self.dev)
         self.staging = [torch.zeros(self.n_i32, dtype=torch.int32).pin_memory() for _ in range(2)]
@@ -81,6 +84,7 @@ class DecodeGraphRunner:
         if self.ring:
             self.rslots = self.packed[self.o_rslots:self.o_rslots + 2 * B].view(torch.int64)
             self.rpt = self.packed[self.o_rpt:self.o_rpt + B * P].view(B, P)
+        self.lslots = self.packed[self.o_lora:self.o_lora + B]
         # sampled rows (temperature / top-k / top-p / min-p) run a second graph per bucket
         # whose last kernel draws from the logits instead of taking the argmax
         self.sampling = self._supports_sampling()
@@ -93,6 +97,9 @@ class DecodeGraphRunner:
         self.host_flags = [torch.zeros(B, dtype=torch.int32).pin_memory() for _ in range(4)]
         self.out_k = 0
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        # rows with batched LoRA adapters: unfused projections plus adapter deltas
+        self.lgraphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.lsgraphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.pool = None
         self.h2d_bytes = 0
         self.d2h_bytes = 0
@@ -129,15 +136,27 @@ class DecodeGraphRunner:
         return (self.dp <= 1 and getattr(m, "tp_fused", None) is None and getattr(m, "pp_stages", 1) == 1
                 and getattr(m, "graph_sampling", True))
 
-    def _body(self, B, sampled=False):
+    def _store(self, sampled: bool, lora: bool) -> dict:
+        if lora:
+            return self.lsgraphs if sampled else self.lgraphs
+        return self.sgraphs if sampled else self.graphs
+
+    @staticmethod
+    def _key(B, sampled, lora):
+        return (("l" if lora else "") + ("s" if sampled else ""), B) if (sampled or lora) else B
+
+    def _body(self, B, sampled=False, lora=False):
+        fb = self._fb(B)
+        if lora:
+            fb.lora_slots = self.lslots[:B]
         if not sampled:
-            self.model.forward_decode_tokens(self._fb(B), self.eng.kv, self.out[:B], flags=self.flags[:B])
+            self.model.forward_decode_tokens(fb, self.eng.kv, self.out[:B], flags=self.flags[:B])
             return
-        logits = self.model.forward(self._fb(B), self.eng.kv)
+        logits = self.model.forward(fb, self.eng.kv)
         ops.sample(logits, self.s_temp[:B], self.s_topk[:B], self.s_topp[:B], self.s_minp[:B], self.s_key[:B],
                    self.s_step[:B], out=self.out[:B], flags=self.flags[:B])
 
-    def capture(self, B, sampled=False):
+    def capture(self, B, sampled=False, lora=False):
         self._reserve()
         # inert inputs for warm-up: no KV writes, empty contexts, scratch recurrent state
         if self.rec is not None:
@@ -152,21 +171,22 @@ class DecodeGraphRunner:
         cur = torch.cuda.current_stream(self.dev)
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(cur)
+        self.lslots.fill_(-1)
         with torch.cuda.stream(s):
             for _ in range(2):
                 self.model.begin_step()
-                self._body(B, sampled)
+                self._body(B, sampled, lora)
         cur.wait_stream(s)
         torch.cuda.synchronize(self.dev)
         n0 = _lib.launch_counter[0]
         g = torch.cuda.CUDAGraph()
         self.model.begin_step()  # the capture itself does not run; every replay advances the step first
         with torch.cuda.graph(g, pool=self.pool):
-            self._body(B, sampled)
-        self.launches_per_replay[("s", B) if sampled else B] = _lib.launch_counter[0] - n0
+            self._body(B, sampled, lora)
+        self.launches_per_replay[self._key(B, sampled, lora)] = _lib.launch_counter[0] - n0
         if self.pool is None:
             self.pool = g.pool()
-        (self.sgraphs if sampled else self.graphs)[B] = g
+        self._store(sampled, lora)[B] = g
         torch.cuda.synchronize(self.dev)
 
     def capture_all(self):
@@ -217,12 +237,13 @@ class DecodeGraphRunner:
         n = len(rows)
         Bb, where = self.layout(plan)
         sampled = any(not r.state.req.sampling.greedy for r in rows)
-        graphs = self.sgraphs if sampled else self.graphs
+        lora = any(r.state.extra.get("lora_slot", -1) >= 0 for r in rows)
+        graphs = self._store(sampled, lora)
         if Bb not in graphs:
             # capture's warm-up overwrites the shared output buffer, which may hold
             # the in-flight step's tokens that this launch gathers from
             saved = self.out.clone()
-            self.capture(Bb, sampled)
+            self.capture(Bb, sampled, lora)
             self.out.copy_(saved)
         k = self.slot_k
         self.slot_k ^= 1
@@ -244,6 +265,7 @@ class DecodeGraphRunner:
             rpt = a[self.o_rpt:self.o_rpt + self.Bmax * P].reshape(self.Bmax, P)
         if self.rec is not None:
             a[self.o_ss:self.o_ss + Bb] = self.rec.scratch
+        a[self.o_lora:self.o_lora + Bb] = -1
         pt = a[self.o_pt:self.o_pt + self.Bmax * P].reshape(self.Bmax, P)
         if sampled:
             keys = a[self.o_key:self.o_key + 2 * self.Bmax].view(np.uint64)
@@ -268,6 +290,8 @@ class DecodeGraphRunner:
             slots[i] = st.seq.slot(p)
             if self.rec is not None:
                 a[self.o_ss + i] = st.seq.state_slot
+            if lora:
+                a[self.o_lora + i] = st.extra.get("lora_slot", -1)
             pg = st.seq.pages
             pt[i, :len(pg)] = pg
             if self.ring:
@@ -303,7 +327,7 @@ class DecodeGraphRunner:
             _lib.count(1)
         self.model.begin_step()
         graphs[Bb].replay()
-        _lib.count(self.launches_per_replay.get(("s", Bb) if sampled else Bb, 0))
+        _lib.count(self.launches_per_replay.get(self._key(Bb, sampled, lora), 0))
         ko = self.out_k
         self.out_k = (self.out_k + 1) % len(self.host_out)
         m = max(where) + 1 if where else 0

@@ -243,7 +243,8 @@ class Scheduler:
                 if n <= 0:
                     continue
                 mm = st.req.mm
-                if mm is not None and mm.get("prefix_lm") and st.num_computed == 0 and n < st.remaining:
+                if mm is not None and mm.get("prefix_lm") and st.num_computed == 0 and n < min(st.remaining,
+                                                                                              mm["prompt_len"]):
                     break  # a prefix-LM prompt attends both ways: it is prefilled in one chunk (FCFS kept)
                 if self.ledger is not None and not self.ledger.has_headroom(
                         self.ledger.admission_tokens(st.num_prompt, st.num_computed + n, st.req.max_tokens)):

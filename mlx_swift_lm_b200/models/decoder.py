@@ -178,6 +178,8 @@ class DecoderLM:
             self.cos_sin_local = self.cos_sin_local.to(self.device)
         self._nope = set(cfg.nope_layers or ())
         self.lora = None  # adapter whose update is currently added into the weights (adapters.lora)
+        self.batched_lora = None  # adapters.batched.BatchedLoRA: per-row adapters, base weights untouched
+        self._lora_slots = None  # per-token adapter slots of the forward in progress
         self.tp_fused = None  # fused symmetric-memory TP decode path (parallel.tp_fused)
         # hybrid models: attention layers index the KV slab, linear layers the recurrent-state pool
         self.kv_index, self.rec_index = [], []
@@ -409,17 +411,33 @@ class DecoderLM:
     # ------------------------------------------------------------------ pieces
     def _attn_out(self, L, attn2d):
         delta = ops.gemm(attn2d, L.wo, bias=L.bo if self.tp.rank == 0 or L.bo is None else None)
+        lo = self._lora(L, "o")
+        if lo is not None:
+            self._lora_add(lo, attn2d, delta)
         return self.tp.reduce(delta)
 
     def _mlp(self, L, h):
         cfg = self.cfg
         if L.moe:
             return self._moe(L, h)
-        if cfg.glu_epi == "xielu":
+        lo = self._lora(L, "gu")
+        if lo is not None and cfg.glu_epi in ("swiglu", "geglu", "swiglu_oai"):
+            from ..ops import lora as lops
+
+            pre = ops.gemm(h, L.wgu, bias=L.bgu)
+            slots, A, Bt, scale = lo
+            t = lops.lora_shrink(h, A, slots, out=self.batched_lora.scratch(h.shape[0], A.shape[1], h.device))
+            gu = lops.lora_expand_glu(pre, Bt, t, slots, scale, cfg.glu_epi)
+        elif lo is not None:
+            raise NotImplementedError(f"batched LoRA on a {cfg.glu_epi!r} MLP")
+        elif cfg.glu_epi == "xielu":
             gu = ops.xielu(ops.gemm(h, L.wgu, bias=L.bgu), L.act_params)
         else:
             gu = ops.gemm(h, L.wgu, epi=cfg.glu_epi, bias=L.bgu)
         delta = ops.gemm(gu, L.wd, bias=L.bd if self.tp.rank == 0 else None)
+        lo = self._lora(L, "d")
+        if lo is not None:
+            self._lora_add(lo, gu, delta)
         return self.tp.reduce(delta)
 
     def route(self, L, h):
@@ -456,6 +474,23 @@ class DecoderLM:
         return logits
 
     # ------------------------------------------------------------------ paged forward
+    def _lora(self, L, target):
+        """(slots, A, B^T, scale) of the batched adapters of this layer's
+        projection when the forward in progress has adapter rows, else None."""
+        bl, slots = self.batched_lora, self._lora_slots
+        if bl is None or slots is None:
+            return None
+        ab = bl.tensors(L, target)
+        return None if ab is None else (slots, ab[0], ab[1], bl.scale)
+
+    def _lora_add(self, lo, x, y):
+        """y += per-row adapter delta of input x (in place)."""
+        from ..ops import lora as lops
+
+        slots, A, Bt, scale = lo
+        t = lops.lora_shrink(x, A, slots, out=self.batched_lora.scratch(x.shape[0], A.shape[1], x.device))
+        return lops.lora_expand(y, Bt, t, slots, scale)
+
     def forward(self, fb: ForwardBatch, kv, return_hidden: bool = False, inputs_embeds: torch.Tensor | None = None,
                 return_both: bool = False, return_residual: bool = False):
         """Paged-KV forward over a flattened batch. Returns fp32 logits for
@@ -465,8 +500,12 @@ class DecoderLM:
         pipeline stages after the first); `return_residual` returns the
         residual stream of every token after the last layer instead (pipeline
         stages before the last)."""
-        with ops.row_roles(fb.num_tokens, fb.num_decode):
-            return self._forward(fb, kv, return_hidden, inputs_embeds, return_both, return_residual)
+        self._lora_slots = fb.lora_slots if self.batched_lora is not None else None
+        try:
+            with ops.row_roles(fb.num_tokens, fb.num_decode):
+                return self._forward(fb, kv, return_hidden, inputs_embeds, return_both, return_residual)
+        finally:
+            self._lora_slots = None
 
     def _forward(self, fb, kv, return_hidden, inputs_embeds, return_both, return_residual):
         cfg = self.cfg
@@ -516,11 +555,14 @@ class DecoderLM:
             positions = torch.arange(T, dtype=torch.int32, device=fb.positions.device)
         qkv = None
         slots, dec_pt, pf_pt = fb.tables(kv, ki)
-        if self._fused_qkv_rope(L, h, fb, rot_dim):
+        lo = self._lora(L, "qkv")
+        if lo is None and self._fused_qkv_rope(L, h, fb, rot_dim):
             q = ops.gemm_qkv_rope(h, L.wqkv, L.bqkv, positions, slots, cos_sin, L.q_norm, L.k_norm,
                                   cfg.rms_norm_eps, kc, vc, self.H, self.KVH, kv.k_scale(ki), kv.v_scale(ki))
         else:
             qkv = ops.gemm(h, L.wqkv, bias=L.bqkv)
+            if lo is not None:
+                self._lora_add(lo, h, qkv)
             qn, kn = L.q_norm, L.k_norm
             if cfg.qk_norm_full:
                 qkv = self._qk_full_norm(L, qkv)
