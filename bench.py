@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "baseline", "reference"],
                     help="ours: the framework; baseline: the same engine with PyTorch/cuBLAS/NCCL ops only; "
                          "reference: the upstream project (unavailable here)")
+    ap.add_argument("--timeline", default="",
+                    help="diagnostic: write the device timeline of one decode-graph replay to this path "
+                         "({rank} is replaced by the rank)")
     ap.add_argument("--no-compare", dest="compare", action="store_false",
                     help="skip the NCCL+cuBLAS arm that --impl ours runs after itself for vs_baseline")
     ap.add_argument("--model", default="qwen3_8b")
@@ -403,6 +406,19 @@ def run_arm(args, impl, world, rank, local, dev, group):
         if world > 1:
             dist.all_reduce(rt, op=dist.ReduceOp.MAX)
         replay_ms = round(rt.item(), 4)
+        if args.timeline and impl == "ours":
+            from mlx_swift_lm_b200.engine.diagnostics import timeline_summary
+
+            tl = _lib.timeline_start(dev)
+            model.begin_step()
+            g.graphs[args.streams].replay()
+            torch.cuda.synchronize(dev)
+            marks = _lib.timeline_read(tl)
+            _lib.timeline_stop()
+            with open(args.timeline.replace("{rank}", str(rank)), "w") as f:
+                f.write(timeline_summary(marks, f"decode graph replay, rank {rank} of {world}, "
+                                                f"{args.streams} rows") + "\n")
+            barrier()
     st = mtp.stats if mtp is not None else None
     res = {
         "diag": {"graph_replay_ms": replay_ms, "host_step_ms_p50": round(statistics.median(step_times) * 1e3, 3)},

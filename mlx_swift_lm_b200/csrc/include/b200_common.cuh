@@ -378,7 +378,34 @@ __device__ __forceinline__ float glu_act(int kind, float g, float u) {
 // pdl_wait() returns once all prerequisite grids have completed and their
 // writes are visible; it is a no-op for launches without the attribute.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Device timeline (diagnostics, off unless a buffer is installed through
+// b200_timeline_<unit>): block (0,0,0) of every kernel records, right after
+// its pdl_wait() returns, {globaltimer, launch signature} into a buffer shared
+// by all units (one device counter hands out the entries). In a chain of
+// dependent launches pdl_wait() returns when the previous grid has completed,
+// so consecutive marks bracket each kernel's cost in the chain.
+// Signature: grid x (20 bits) | y (12) | z (8) | block x (11) | 1 in bit 63.
+static __device__ unsigned long long* g_tl_buf;  // [cap][2]
+static __device__ unsigned int* g_tl_head;
+static __device__ unsigned int g_tl_cap;
+
+__device__ __forceinline__ void timeline_mark() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  const unsigned i = atomicAdd(g_tl_head, 1u);
+  if (i < g_tl_cap) {
+    const unsigned long long sig = (1ull << 63) | ((unsigned long long)(gridDim.x & 0xFFFFF) << 31) |
+                                   ((unsigned long long)(gridDim.y & 0xFFF) << 19) |
+                                   ((unsigned long long)(gridDim.z & 0xFF) << 11) | (blockDim.x & 0x7FF);
+    g_tl_buf[2 * i] = t;
+    g_tl_buf[2 * i + 1] = sig;
+  }
+}
+
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0 && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 && g_tl_buf != nullptr) timeline_mark();
+}
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 }  // namespace b200
@@ -440,6 +467,12 @@ static inline int smem_attr_once(int bytes) {
 // Host accessor for this translation unit's status word: copies it out and
 // clears it. Returns the CUDA error code of the copy.
 #define B200_STATUS_ACCESSORS(tag)                                                              \
+  extern "C" int b200_timeline_##tag(unsigned long long* buf, unsigned int* head, unsigned int cap) { \
+    cudaError_t e = cudaMemcpyToSymbol(b200::g_tl_buf, &buf, sizeof(buf));                        \
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(b200::g_tl_head, &head, sizeof(head));             \
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(b200::g_tl_cap, &cap, sizeof(cap));                \
+    return (int)e;                                                                              \
+  }                                                                                             \
   extern "C" int b200_status_##tag(unsigned int* out, int clear) {                               \
     cudaError_t e = cudaMemcpyFromSymbol(out, b200::g_status, sizeof(unsigned int));              \
     if (e == cudaSuccess && clear) {                                                            \

@@ -169,3 +169,28 @@ def teacher_forced_scores(engine, prompt: list[int], continuation: list[int]) ->
         return lp.gather(1, tgt[:, None])[:, 0].tolist()
     finally:
         seq.release()
+
+
+def timeline_summary(marks, title: str = "") -> str:
+    """Text summary of device timeline marks (``ops._lib.timeline_read``):
+    each kernel's cost in the dependent chain is the time from its mark to the
+    next one (its predecessor finished at its mark, it finished at the next).
+    Lists the chain in order and totals per launch signature."""
+    lines = [title] if title else []
+    if len(marks) < 2:
+        return "\n".join(lines + ["(fewer than two marks)"])
+    t0 = marks[0][0]
+    agg: dict = {}
+    for i in range(len(marks) - 1):
+        t, sig = marks[i]
+        dt = (marks[i + 1][0] - t) / 1e3
+        lines.append(f"{(t - t0) / 1e3:10.2f} us  {dt:8.2f} us  grid {sig[0]}x{sig[1]}x{sig[2]} block {sig[3]}")
+        a = agg.setdefault(sig, [0, 0.0])
+        a[0] += 1
+        a[1] += dt
+    total = (marks[-1][0] - t0) / 1e3
+    lines.append(f"span {total:.2f} us over {len(marks)} marks; per signature (count, total us, mean us, share):")
+    for sig, (n, tot) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+        lines.append(f"  grid {sig[0]}x{sig[1]}x{sig[2]} block {sig[3]:4d}: {n:5d} {tot:10.2f} {tot / n:8.2f} "
+                     f"{tot / total:6.1%}")
+    return "\n".join(lines)

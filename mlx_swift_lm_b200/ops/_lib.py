@@ -167,6 +167,47 @@ def read_status(clear: bool = True) -> dict:
     return out
 
 
+def timeline_start(device, cap: int = 1 << 16):
+    """Install a device timeline buffer in every kernel unit: each kernel's
+    block 0 records {globaltimer ns, launch signature} after its pdl_wait()
+    (see b200_common.cuh). Returns the (buf, head) tensors for
+    :func:`timeline_read`; :func:`timeline_stop` turns recording off."""
+    L = lib()
+    buf = torch.zeros(cap, 2, dtype=torch.int64, device=device)
+    head = torch.zeros(1, dtype=torch.int32, device=device)
+    for tag in _STATUS_TAGS + _EXTRA_STATUS_TAGS:
+        fn = getattr(L, "b200_timeline_" + tag, None)
+        if fn is not None:
+            fn.restype = i32
+            fn.argtypes = [vp, vp, C.c_uint]
+            check(fn(buf.data_ptr(), head.data_ptr(), cap), f"timeline {tag}")
+    return buf, head
+
+
+def timeline_stop():
+    L = lib()
+    for tag in _STATUS_TAGS + _EXTRA_STATUS_TAGS:
+        fn = getattr(L, "b200_timeline_" + tag, None)
+        if fn is not None:
+            fn.restype = i32
+            fn.argtypes = [vp, vp, C.c_uint]
+            fn(None, None, 0)
+
+
+def timeline_read(tl) -> list[tuple[int, tuple[int, int, int, int]]]:
+    """Recorded marks in time order: (ns, (grid x, grid y, grid z, block x))."""
+    buf, head = tl
+    torch.cuda.synchronize(buf.device)
+    n = min(int(head.item()), buf.shape[0])
+    rows = buf[:n].cpu().tolist()
+    out = []
+    for t, sig in rows:
+        sig &= (1 << 63) - 1
+        out.append((t, ((sig >> 31) & 0xFFFFF, (sig >> 19) & 0xFFF, (sig >> 11) & 0xFF, sig & 0x7FF)))
+    out.sort()
+    return out
+
+
 # Count of kernel launches issued through this binding (for bench accounting).
 launch_counter = [0]
 
