@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "baseline", "reference"],
                     help="ours: the framework; baseline: the same engine with PyTorch/cuBLAS/NCCL ops only; "
                          "reference: the upstream project (unavailable here)")
+    ap.add_argument("--diag", action="store_true",
+                    help="diagnostic: replay the full-batch decode graph after the warm-up and report its time")
     ap.add_argument("--timeline", default="",
                     help="diagnostic: write the device timeline of one decode-graph replay to this path "
                          "({rank} is replaced by the rank)")
@@ -355,6 +357,38 @@ def run_arm(args, impl, world, rank, local, dev, group):
     for _ in range(args.warmup):
         eng.step()
     barrier()
+    # diagnostic (opt-in, --diag / --timeline): the decode graph of the full batch
+    # replayed back to back after the warm-up (device time of one step with no host
+    # work between replays; it rewrites the K/V of the last step's positions)
+    replay_ms = None
+    g = eng.graphs
+    if (args.diag or args.timeline) and g is not None and args.streams in g.graphs:
+        eng._drain_inflight()
+        barrier()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for _ in range(20):
+            model.begin_step()
+            g.graphs[args.streams].replay()
+        r1.record()
+        barrier()
+        rt = torch.tensor([r0.elapsed_time(r1) / 20], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(rt, op=dist.ReduceOp.MAX)
+        replay_ms = round(rt.item(), 4)
+        if args.timeline and impl == "ours":
+            from mlx_swift_lm_b200.engine.diagnostics import timeline_summary
+
+            tl = _lib.timeline_start(dev)
+            model.begin_step()
+            g.graphs[args.streams].replay()
+            torch.cuda.synchronize(dev)
+            marks = _lib.timeline_read(tl)
+            _lib.timeline_stop()
+            with open(args.timeline.replace("{rank}", str(rank)), "w") as f:
+                f.write(timeline_summary(marks, f"decode graph replay, rank {rank} of {world}, "
+                                                f"{args.streams} rows") + "\n")
+            barrier()
     clocks = ClockSampler(local)
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -389,39 +423,10 @@ def run_arm(args, impl, world, rank, local, dev, group):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dev_ms, e2e_s = t.tolist()
-    # diagnostic: the decode graph replayed back to back (device time of one
-    # step with no host work between replays; not the reported value)
-    replay_ms = None
-    g = eng.graphs
-    if g is not None and args.streams in g.graphs:
-        barrier()
-        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        r0.record()
-        for _ in range(20):
-            model.begin_step()
-            g.graphs[args.streams].replay()
-        r1.record()
-        barrier()
-        rt = torch.tensor([r0.elapsed_time(r1) / 20], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(rt, op=dist.ReduceOp.MAX)
-        replay_ms = round(rt.item(), 4)
-        if args.timeline and impl == "ours":
-            from mlx_swift_lm_b200.engine.diagnostics import timeline_summary
-
-            tl = _lib.timeline_start(dev)
-            model.begin_step()
-            g.graphs[args.streams].replay()
-            torch.cuda.synchronize(dev)
-            marks = _lib.timeline_read(tl)
-            _lib.timeline_stop()
-            with open(args.timeline.replace("{rank}", str(rank)), "w") as f:
-                f.write(timeline_summary(marks, f"decode graph replay, rank {rank} of {world}, "
-                                                f"{args.streams} rows") + "\n")
-            barrier()
     st = mtp.stats if mtp is not None else None
     res = {
-        "diag": {"graph_replay_ms": replay_ms, "host_step_ms_p50": round(statistics.median(step_times) * 1e3, 3)},
+        "diag": {"graph_replay_ms": replay_ms, "host_step_ms_p50": round(statistics.median(step_times) * 1e3, 3),
+                 "step_kinds": dict(eng.step_kinds)},
         "value": round(tok_timed / (dev_ms / 1e3), 2), "ms_per_step": round(dev_ms / args.steps, 4),
         "ttft_p50_ms": round(statistics.median(ttfts) * 1e3, 2),
         "itl_p50_ms": round(statistics.median(step_times) * 1e3, 3), "prefill_s": round(prefill_s, 3),

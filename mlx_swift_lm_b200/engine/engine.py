@@ -198,6 +198,8 @@ class EngineV2:
         self.healthy = True
         self.on_step_wedge = None
         self.comm_guard = None  # parallel.health.CommGuard of a multi-rank engine
+        # steps by kind: decode-graph launches, eager forwards, MTP rounds
+        self.step_kinds = {"graph": 0, "eager": 0, "mtp": 0}
         self.steps = 0
         self.last_step_ms = 0.0
         self._lock = threading.RLock()
@@ -490,6 +492,7 @@ class EngineV2:
                     return events + self.step()
                 mev = self.mtp.round(plan)
                 if mev is not None:
+                    self.step_kinds["mtp"] += 1
                     self.steps += 1
                     self.last_step_ms = (time.perf_counter() - t0) * 1e3
                     self._step_started = None
@@ -504,6 +507,7 @@ class EngineV2:
                 if self.mtp is not None:
                     for r in plan.rows:
                         self.mtp.drop(r.state)  # history broken: MTP restarts after an eager step
+                self.step_kinds["graph"] += 1
                 with _nvtx("decode_graph"):
                     handle = self.graphs.launch(plan, chained_from=prev)
                 for r in plan.rows:
@@ -520,6 +524,7 @@ class EngineV2:
                     events += self._drain_inflight()
                     self._step_started = None
                     return events + self.step()
+                self.step_kinds["eager"] += 1
                 fb = self._build_batch(plan, self.device)
                 hid = None
                 dtok = self.diagnostics.begin_forward(self.device) if self.diagnostics is not None else None

@@ -189,6 +189,12 @@ class DecodeGraphRunner:
         self._store(sampled, lora)[B] = g
         torch.cuda.synchronize(self.dev)
 
+    def invalidate(self):
+        """Drop every captured graph (buffers they point to are about to move)."""
+        for d in (self.graphs, self.sgraphs, self.lgraphs, self.lsgraphs):
+            d.clear()
+        self._reserved = False
+
     def capture_all(self):
         for b in reversed(self.buckets):
             if b not in self.graphs:

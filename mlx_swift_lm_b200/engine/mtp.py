@@ -46,6 +46,7 @@ class MTPConfig:
     seed: int = 0
     adaptive: bool = False  # choose the depth per round (engine.mtp_depth.DepthController)
     max_rows: int = 0  # > 0: steps with more decode rows run without drafts (bounded drafter work)
+    graph_round: bool = True  # fixed-geometry rounds (engine.mtp_graph), CUDA graphs on GPU
 
 
 @dataclass
@@ -75,8 +76,31 @@ class MTPDriver:
             from .mtp_depth import DepthController
 
             self.depth = DepthController(self.cfg.k)
-        self.h2d_bytes = 0  # step inputs copied host -> device
-        self.d2h_bytes = 0  # drafts + target tokens read back
+        self._h2d = 0  # step inputs copied host -> device (eager rounds)
+        self._d2h = 0  # drafts + target tokens read back (eager rounds)
+        self.runner = None
+        m = engine.model
+        if (self.cfg.graph_round and m.tp.world == 1 and getattr(m, "pp_stages", 1) == 1
+                and getattr(m, "dp_world", 1) == 1):
+            from .mtp_graph import MTPGraphRunner
+
+            self.runner = MTPGraphRunner(self)
+
+    @property
+    def h2d_bytes(self):
+        return self._h2d + (self.runner.h2d_bytes if self.runner is not None else 0)
+
+    @h2d_bytes.setter
+    def h2d_bytes(self, v):
+        self._h2d = v - (self.runner.h2d_bytes if self.runner is not None else 0)
+
+    @property
+    def d2h_bytes(self):
+        return self._d2h + (self.runner.d2h_bytes if self.runner is not None else 0)
+
+    @d2h_bytes.setter
+    def d2h_bytes(self, v):
+        self._d2h = v - (self.runner.d2h_bytes if self.runner is not None else 0)
 
     # ------------------------------------------------------------------ row state
     def on_first_token(self, st, hidden_row: torch.Tensor):
@@ -86,11 +110,15 @@ class MTPDriver:
         st.extra["mtp_p0"] = len(st.all_tokens) - 1  # position of the pending token
         st.extra["mtp_m"] = st.extra["mtp_p0"]
         st.extra["mtp_h"] = hidden_row.reshape(1, -1)
+        if self.runner is not None and not self.runner.attach(st, hidden_row):
+            self.drop(st)
 
     def drop(self, st):
         seq = st.extra.pop("mtp_seq", None)
         if seq is not None:
             seq.release()
+        if self.runner is not None:
+            self.runner.detach(st)
         for k in ("mtp_p0", "mtp_m", "mtp_h"):
             st.extra.pop(k, None)
 
@@ -180,6 +208,56 @@ class MTPDriver:
         rows = plan.rows
         if not self._ensure(rows, k):
             return None
+        if self.runner is not None and self.runner.can_run(plan, k):
+            return self._round_fixed(plan, k, t_round)
+        return self._round_eager(plan, k, t_round)
+
+    def _draw_accepts(self, n: int, k: int) -> list[int]:
+        out = []
+        for _ in range(n):
+            a = 0
+            while a < k and self.rng.random() < self.cfg.p:
+                a += 1
+            out.append(a)
+        return out
+
+    def _round_fixed(self, plan, k: int, t_round: float):
+        """A round through the fixed-geometry runner (one graph replay)."""
+        import time
+
+        eng = self.eng
+        rows = plan.rows
+        forced = self._draw_accepts(len(rows), k) if self.cfg.acceptance == "bernoulli" else None
+        emit, acc = self.runner.run(plan, k, forced)
+        events = []
+        st_ = self.stats
+        st_.rounds += 1
+        st_.rows += len(rows)
+        acc_rows = []
+        for i, r in enumerate(rows):
+            st = r.state
+            p = r.start
+            a = int(acc[i])
+            st_.drafted += k
+            st_.accepted += a
+            acc_rows.append(a)
+            st.extra["mtp_seq"].num_tokens = p + 1 - st.extra["mtp_p0"]
+            st.seq.num_tokens = p + a + 1
+            st.extra["mtp_m"] = p + 1
+            for t in emit[i, :a + 1]:
+                st_.emitted += 1
+                events += eng._accept_token(st, int(t), None)
+                if st.status.name == "FINISHED":
+                    break
+        if self.depth is not None:
+            self.depth.observe(k, acc_rows, time.perf_counter() - t_round)
+        return events
+
+    def _round_eager(self, plan, k: int, t_round: float):
+        import time
+
+        eng = self.eng
+        rows = plan.rows
         states = [r.state for r in rows]
         B = len(rows)
         p = [r.start for r in rows]
@@ -225,9 +303,7 @@ class MTPDriver:
         acc_rows = []
         for i, st in enumerate(states):
             if self.cfg.acceptance == "bernoulli":
-                a = 0
-                while a < k and self.rng.random() < self.cfg.p:
-                    a += 1
+                a = self._draw_accepts(1, k)[0]
             else:
                 a = 0
                 while a < k and D_h[i, a] == pred_h[i, a]:

@@ -69,13 +69,14 @@ _SIGS = {
     "b200_lora_shrink": (i32, [vp, i32, vp, i32, i32, vp, i32, vp, i32, vp]),
     "b200_lora_expand": (i32, [vp, i32, vp, i32, i32, vp, vp, vp, i32, i32, vp]),
     "b200_lora_expand_glu": (i32, [vp, i32, vp, i32, i32, vp, i32, vp, vp, vp, i32, i32, i32, vp]),
+    "b200_mtp_accept": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, vp, vp, vp, i32, vp]),
     "b200_set_pdl": (None, [i32]),
     "b200_get_pdl": (i32, []),
 }
 
 # status accessors exported per translation unit
 _STATUS_TAGS = ["gemm", "norm", "attn_decode", "attn_prefill_simt", "sampling", "misc", "attn_decode_mma",
-                "attn_prefill_mma", "attn_wide", "lora"]
+                "attn_prefill_mma", "attn_wide", "lora", "mtp"]
 
 
 class KernelLibraryMissing(RuntimeError):
