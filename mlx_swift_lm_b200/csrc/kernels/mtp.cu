@@ -7,7 +7,8 @@
 // [B * (k+1), H]:
 //   a      = forced[r] >= 0 ? min(forced[r], k)       (scheduled acceptance)
 //                           : leading j with D[r, j] == pred[r, j]
-//   emit   = D[r, 0..a-1], pred[r, a]                  (a + 1 tokens; the rest -1)
+//   res[r, 0..k] = D[r, 0..a-1], pred[r, a], -1 ...     (the a + 1 emitted tokens)
+//   res[r, k+1]  = a                                     (res rows of k + 2 ints)
 //   hist[hslot[r], K - a + j] = vh[r * (k+1) + j]      for j = 0..a
 // (K >= k: the depth the history rows are sized for). The history row of a
 // request holds, right-aligned, the target hiddens of
@@ -21,8 +22,7 @@ __global__ void __launch_bounds__(256) mtp_accept_kernel(const int* __restrict__
                                                        const int* __restrict__ forced, int k,
                                                        const int* __restrict__ hslot, int n_hist, int K,
                                                        const __nv_bfloat16* __restrict__ vh, int H,
-                                                       __nv_bfloat16* __restrict__ hist, int* __restrict__ emit,
-                                                       int* __restrict__ acc) {
+                                                       __nv_bfloat16* __restrict__ hist, int* __restrict__ res) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ int s_a;
@@ -35,8 +35,9 @@ __global__ void __launch_bounds__(256) mtp_accept_kernel(const int* __restrict__
     } else {
       while (a < k && D[r * k + a] == pred[r * (k + 1) + a]) ++a;
     }
-    for (int j = 0; j <= k; ++j) emit[r * (k + 1) + j] = j < a ? D[r * k + j] : (j == a ? pred[r * (k + 1) + a] : -1);
-    acc[r] = a;
+    int* row = res + (size_t)r * (k + 2);
+    for (int j = 0; j <= k; ++j) row[j] = j < a ? D[r * k + j] : (j == a ? pred[r * (k + 1) + a] : -1);
+    row[k + 1] = a;
     s_a = a;
   }
   __syncthreads();
@@ -60,12 +61,12 @@ __global__ void __launch_bounds__(256) mtp_accept_kernel(const int* __restrict__
 using namespace b200;
 
 extern "C" int b200_mtp_accept(const int* pred, const int* D, const int* forced, int k, const int* hslot, int n_hist,
-                               int K, const void* vh, int H, void* hist, int* emit, int* acc, int B, cudaStream_t st) {
+                               int K, const void* vh, int H, void* hist, int* res, int B, cudaStream_t st) {
   if (B <= 0) return 0;
   if (k < 1 || K < k || (H % 8) || (((uintptr_t)vh | (uintptr_t)hist) & 15)) return -1;
   cudaError_t e = launch_k(mtp_accept_kernel, dim3(B), dim3(256), 0, st, 1, pred, D, forced, k, hslot, n_hist, K,
                            reinterpret_cast<const __nv_bfloat16*>(vh), H, reinterpret_cast<__nv_bfloat16*>(hist),
-                           emit, acc);
+                           res);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

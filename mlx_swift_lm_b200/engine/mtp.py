@@ -229,6 +229,11 @@ class MTPDriver:
         rows = plan.rows
         forced = self._draw_accepts(len(rows), k) if self.cfg.acceptance == "bernoulli" else None
         emit, acc = self.runner.run(plan, k, forced)
+        V = eng.model.cfg.vocab_size
+        for i in range(len(rows)):
+            a = int(acc[i])
+            if not (0 <= a <= k) or any(not (0 <= int(t) < V) for t in emit[i, :a + 1]):
+                raise RuntimeError(f"MTP round returned accept count {a} / tokens {emit[i].tolist()} for row {i}")
         events = []
         st_ = self.stats
         st_.rounds += 1

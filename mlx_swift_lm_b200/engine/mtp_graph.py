@@ -208,10 +208,11 @@ class MTPGraphRunner:
         B, k = R.B, R.k
         emit, acc = R.res[:, :k + 1], R.res[:, k + 1]
         if R.packed.is_cuda:
+            # res rows: k + 1 emitted tokens, then the accept count (one contiguous [B, k+2] buffer)
+            assert R.res.is_contiguous() and R.D.is_contiguous() and pred.is_contiguous() and vh.is_contiguous()
             rc = _lib.lib().b200_mtp_accept(pred.data_ptr(), R.D.data_ptr(), R.forced.data_ptr(), k,
                                             R.hs.data_ptr(), self.S, self.drv.cfg.k, vh.data_ptr(), self.Hd,
-                                            self.hist.data_ptr(),
-                                            emit.data_ptr(), acc.data_ptr(), B, _lib.stream_ptr(self.dev))
+                                            self.hist.data_ptr(), R.res.data_ptr(), B, _lib.stream_ptr(self.dev))
             _lib.check(rc, "mtp_accept")
             _lib.count(1)
             return
@@ -240,9 +241,7 @@ class MTPGraphRunner:
     def _capture(self, R: _Round):
         m = self.eng.model
         cur = torch.cuda.current_stream(self.dev)
-        s = torch.cuda.Stream(self.dev)
-        s.wait_stream(cur)
-        # warm-up on inert inputs: no K/V writes, one-key contexts, history slot -1 rows skipped
+        # warm-up on inert inputs: no K/V writes, one-key contexts, the padding history row
         R.packed.zero_()
         R.s1_slots.fill_(-1)
         R.dr_slots.fill_(-1)
@@ -253,6 +252,8 @@ class MTPGraphRunner:
         R.forced.fill_(0)
         R.hs.fill_(self.pad_slot)
         saved = self.hist.clone()
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(cur)
         with torch.cuda.stream(s):
             for _ in range(2):
                 m.begin_step()
