@@ -104,6 +104,7 @@ __device__ __forceinline__ void last_cta_signal(const CommCtx& c, int pad, uint3
     __threadfence_system();
     *c.ticket = 0;  // self-reset for the next launch / graph replay
     for (int j = 0; j < c.world; ++j) signal_store(c.pad_ptr(j, pad, c.rank), epoch);
+    timeline_tag(0x100 + pad);  // diagnostics: the phase's signal went out
   }
 }
 
@@ -114,6 +115,7 @@ __device__ __forceinline__ bool wait_all_ranks(const CommCtx& c, int pad, uint32
     bool ok = true;
     for (int j = 0; j < c.world; ++j) ok &= wait_counter(c.pad_ptr(c.rank, pad, j), epoch);
     s_ok = ok;
+    if (blockIdx.x == 0) timeline_tag(0x200 + pad);  // diagnostics: every rank's signal arrived
   }
   __syncthreads();
   return s_ok != 0;

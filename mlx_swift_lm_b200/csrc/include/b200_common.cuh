@@ -402,6 +402,19 @@ __device__ __forceinline__ void timeline_mark() {
   }
 }
 
+// A tagged mark from the calling thread (bit 62 set, `tag` in the low bits):
+// points inside a kernel (a wait returning, a signal going out).
+__device__ __forceinline__ void timeline_tag(unsigned tag) {
+  if (g_tl_buf == nullptr) return;
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  const unsigned i = atomicAdd(g_tl_head, 1u);
+  if (i < g_tl_cap) {
+    g_tl_buf[2 * i] = t;
+    g_tl_buf[2 * i + 1] = (1ull << 63) | (1ull << 62) | tag;
+  }
+}
+
 __device__ __forceinline__ void pdl_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0 && (blockIdx.x | blockIdx.y | blockIdx.z) == 0 && g_tl_buf != nullptr) timeline_mark();

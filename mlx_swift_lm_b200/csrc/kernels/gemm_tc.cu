@@ -277,6 +277,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ, MT>::kThreads, 1)
       // every rank must have published this phase's rows (bounded wait)
       const uint32_t ep = coll.comm.epoch(coll.phase);
       for (int j = 0; j < coll.comm.world; ++j) wait_counter(coll.comm.pad_ptr(coll.comm.rank, kPadAG, j), ep);
+      if ((blockIdx.x | blockIdx.y | blockIdx.z) == 0) timeline_tag(0x200 + kPadAG);
     }
     for (int i = 0; i < pre; ++i)
       load_x(sbase + i * S::kStageBytes + MT * S::kABytes, bar_full + 8 * i, (kb_begin + i) * 64);
@@ -607,6 +608,7 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ, MT>::kThreads, 1)
   if (args.ksplit > 1) cluster_sync();
   else __syncthreads();
   if constexpr (MODE == kModeRS) {
+    if ((blockIdx.x | blockIdx.y | blockIdx.z) == 0 && threadIdx.x == 0) timeline_tag(0x300);  // epilogue done
     // all of this CTA's inbox stores are issued; the last CTA of the grid
     // publishes the phase to every rank
     if (threadIdx.x == 0) last_cta_signal(coll.comm, kPadRS, coll.comm.epoch(coll.phase));

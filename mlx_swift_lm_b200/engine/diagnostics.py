@@ -174,22 +174,30 @@ def teacher_forced_scores(engine, prompt: list[int], continuation: list[int]) ->
 def timeline_summary(marks, title: str = "") -> str:
     """Text summary of device timeline marks (``ops._lib.timeline_read``):
     each kernel's cost in the dependent chain is the time from its mark to the
-    next one (its predecessor finished at its mark, it finished at the next).
-    Lists the chain in order and totals per launch signature."""
+    next kernel's (its predecessor finished at its mark, it finished at the
+    next). Tagged points inside kernels (collective waits returning, signals
+    going out) are listed in place. Totals per launch signature follow."""
     lines = [title] if title else []
-    if len(marks) < 2:
-        return "\n".join(lines + ["(fewer than two marks)"])
+    kern = [m for m in marks if not isinstance(m[1], int)]
+    if len(kern) < 2:
+        return "\n".join(lines + ["(fewer than two kernel marks)"])
     t0 = marks[0][0]
     agg: dict = {}
-    for i in range(len(marks) - 1):
-        t, sig = marks[i]
-        dt = (marks[i + 1][0] - t) / 1e3
+    ki = 0
+    for t, sig in marks:
+        if isinstance(sig, int):
+            lines.append(f"{(t - t0) / 1e3:10.2f} us      -     tag 0x{sig:x}")
+            continue
+        if ki + 1 >= len(kern):
+            break
+        dt = (kern[ki + 1][0] - t) / 1e3
+        ki += 1
         lines.append(f"{(t - t0) / 1e3:10.2f} us  {dt:8.2f} us  grid {sig[0]}x{sig[1]}x{sig[2]} block {sig[3]}")
         a = agg.setdefault(sig, [0, 0.0])
         a[0] += 1
         a[1] += dt
-    total = (marks[-1][0] - t0) / 1e3
-    lines.append(f"span {total:.2f} us over {len(marks)} marks; per signature (count, total us, mean us, share):")
+    total = (kern[-1][0] - kern[0][0]) / 1e3
+    lines.append(f"span {total:.2f} us over {len(kern)} kernel marks; per signature (count, total us, mean us, share):")
     for sig, (n, tot) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
         lines.append(f"  grid {sig[0]}x{sig[1]}x{sig[2]} block {sig[3]:4d}: {n:5d} {tot:10.2f} {tot / n:8.2f} "
                      f"{tot / total:6.1%}")

@@ -195,8 +195,9 @@ def timeline_stop():
             fn(None, None, 0)
 
 
-def timeline_read(tl) -> list[tuple[int, tuple[int, int, int, int]]]:
-    """Recorded marks in time order: (ns, (grid x, grid y, grid z, block x))."""
+def timeline_read(tl) -> list:
+    """Recorded marks in time order: (ns, (grid x, grid y, grid z, block x)) for
+    kernel marks, (ns, tag) for tagged points inside kernels."""
     buf, head = tl
     torch.cuda.synchronize(buf.device)
     n = min(int(head.item()), buf.shape[0])
@@ -204,8 +205,11 @@ def timeline_read(tl) -> list[tuple[int, tuple[int, int, int, int]]]:
     out = []
     for t, sig in rows:
         sig &= (1 << 63) - 1
+        if sig >> 62:  # tagged point inside a kernel: the tag
+            out.append((t, sig & ((1 << 62) - 1)))
+            continue
         out.append((t, ((sig >> 31) & 0xFFFFF, (sig >> 19) & 0xFFF, (sig >> 11) & 0xFF, sig & 0x7FF)))
-    out.sort()
+    out.sort(key=lambda m: m[0])
     return out
 
 
