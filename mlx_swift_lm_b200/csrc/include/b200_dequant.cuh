@@ -43,6 +43,15 @@ __device__ __forceinline__ uint32_t de2m1_pair(uint32_t v, __nv_bfloat162 s2) {
   return *reinterpret_cast<const uint32_t*>(&w);
 }
 
+// Hardware conversion of the two e2m1 codes of one byte to an f16 pair
+// (cvt.rn.f16x2.e2m1x2, sm_100a): which code lands in which half is pinned by
+// tests/test_moe_gpu.py through b200_e2m1_pairs.
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+  uint32_t r;
+  asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}" : "=r"(r) : "r"(byte));
+  return r;
+}
+
 // bf16 pair (q_lo + 128, q_hi + 128) from two 4-bit codes placed at bits 0..3
 // and 16..19 of v (exact: 128..143 are bf16 integers), minus 128, then
 // scale * q + bias with one rounding.

@@ -359,6 +359,264 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
   }
 }
 
+// ---------------------------------------------------------------- persistent grouped GEMM
+// Decode-sized expert chunks (<= 32 rows) with quantised experts: one CTA per
+// SM loops over the (chunk, 128-row weight tile) work items w = blockIdx.x,
+// blockIdx.x + gridDim.x, ... (the same fixed item -> CTA map whatever the
+// batch, each item's K order fixed). Set-up (barriers, tensor memory) is paid
+// once per SM instead of once per item, and the pipelines run across item
+// boundaries: the raw producer streams the next item's records while the
+// current one finishes, and the accumulator is double-buffered in tensor
+// memory so the epilogue of item j overlaps the MMAs of item j + 1.
+// Warps: 0 activation TMA | 1 MMA | 2 raw records | 3 idle | 4-11 dequantise
+// (thread = row t, half of the 64-input block) | 12-15 epilogue (tensor
+// memory lanes 32 * (warp % 4)).
+template <int BN, int WQ>
+struct PSmem {
+  static constexpr int kA = 128 * 128, kB = BN * 128;
+  static constexpr int kStage = (kA + kB + 1023) / 1024 * 1024;
+  static constexpr int kStages = 6;
+  static constexpr int kCode = code_bits<WQ>() * 128 * 64 / 8, kGroup = 2 * 128 * 2;
+  static constexpr int kRaw = kCode + 2 * kGroup;
+  static constexpr int kRawOff = kStages * kStage;
+  static constexpr int kRawStages = (196 * 1024 - kRawOff) / kRaw;
+  static constexpr int kBars = 3 * kStages + 2 * kRawStages + 4;
+  static constexpr int kXOff = kRawOff + kRawStages * kRaw;
+  static constexpr int kXBytes = 64 * BN * 4;
+  static constexpr int kTotal = kXOff + kXBytes + kBars * 8 + 16 + 1024;
+  static constexpr int kThreads = 512;
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kTmem = 2 * kAccCols;
+  static_assert(kRawStages >= 8, "raw ring too shallow");
+  static_assert(kTotal <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
+};
+
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int BN, int WQ>
+__global__ void __launch_bounds__(512, 1)
+    grouped_persistent_kernel(const __grid_constant__ CUtensorMap tmX, GArgs a, const __grid_constant__ GQuant q) {
+  using S = PSmem<BN, WQ>;
+  constexpr int ST = S::kStages, RS = S::kRawStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  float* xbuf = reinterpret_cast<float*>(smem + S::kXOff);  // [64][BN]: up rows handed to the gate warps
+  const uint32_t bar_full = sbase + S::kXOff + S::kXBytes;
+  const uint32_t bar_empty = bar_full + 8 * ST;
+  const uint32_t bar_aready = bar_empty + 8 * ST;
+  const uint32_t bar_rfull = bar_aready + 8 * ST;
+  const uint32_t bar_rempty = bar_rfull + 8 * RS;
+  const uint32_t bar_accf = bar_rempty + 8 * RS;  // [2]
+  const uint32_t bar_acce = bar_accf + 16;        // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kXOff + S::kXBytes + S::kBars * 8);
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = a.K / 64;
+  const int ntiles = (a.N + 127) / 128;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+      mbar_init(bar_aready + 8 * s, 8);
+    }
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(bar_rfull + 8 * s, 1);
+      mbar_init(bar_rempty + 8 * s, 8);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_accf + 8 * b, 1);
+      mbar_init(bar_acce + 8 * b, 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), S::kTmem);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  const int n_items = *a.n_chunks * ntiles;
+  const uint64_t pw = l2_policy_evict_first(), px = l2_policy_evict_last();
+  auto item = [&](int w, int& e, int& r0, int& rc, int& tile) {
+    const int c = w / ntiles;
+    tile = w - c * ntiles;
+    e = a.chunks[3 * c];
+    r0 = a.chunks[3 * c + 1];
+    rc = a.chunks[3 * c + 2];
+  };
+  if (warp == 0) {
+    if (lane == 0) {  // activation tiles: x rows r0.. of the item's chunk
+      int g = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+        int e, r0, rc, tile;
+        item(w, e, r0, rc, tile);
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % ST;
+          if (g >= ST && !mbar_wait(bar_empty + 8 * s, ((g / ST) - 1) & 1, kErrGemmWait)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_full + 8 * s, (uint32_t)S::kB);
+          tma_load_2d(sbase + s * S::kStage + S::kA, &tmX, bar_full + 8 * s, kb * 64, r0, px);
+        }
+      }
+    }
+  } else if (warp == 2) {
+    if (lane == 0) {  // raw weight records of the item's expert tile
+      int g = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+        int e, r0, rc, tile;
+        item(w, e, r0, rc, tile);
+        const uint8_t* rec = q.tiled + ((size_t)e * q.tiles_per_expert + tile) * q.kb_total * q.rec_bytes;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % RS;
+          if (g >= RS && !mbar_wait(bar_rempty + 8 * s, ((g / RS) - 1) & 1, kErrGemmWait)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_rfull + 8 * s, (uint32_t)q.rec_bytes);
+          bulk_g2s(sbase + S::kRawOff + s * S::kRaw, rec + (size_t)kb * q.rec_bytes, (uint32_t)q.rec_bytes,
+                   bar_rfull + 8 * s, pw);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer: item j accumulates into buffer j & 1
+      constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+      int g = 0, j = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(bar_acce + 8 * b, ((j >> 1) - 1) & 1, kErrTmemWait)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * S::kAccCols);
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % ST;
+          if (!mbar_wait(bar_full + 8 * s, (g / ST) & 1, kErrGemmWait) ||
+              !mbar_wait(bar_aready + 8 * s, (g / ST) & 1, kErrGemmWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_k_sw128(sbase + s * S::kStage, 1024);
+          const uint64_t bd = umma_desc_k_sw128(sbase + s * S::kStage + S::kA, 1024);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) tc_mma_f16(acc, ad + 2 * kk, bd + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(bar_empty + 8 * s);
+        }
+        if (ok) tc_commit(bar_accf + 8 * b);
+      }
+    }
+  } else if (warp >= 4 && warp < 12) {  // dequantise raw records into the A tiles
+    const int t = (threadIdx.x - 128) & 127, half = (threadIdx.x - 128) >> 7;
+    const int gsel = q.gs == 16 ? 2 * half : q.gs == 32 ? half : 0;
+    int g = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+      for (int kb = 0; kb < nkb; ++kb, ++g) {
+        const int rs = g % RS, s = g % ST;
+        if (!mbar_wait(bar_rfull + 8 * rs, (g / RS) & 1, kErrGemmWait) ||
+            (g >= ST && !mbar_wait(bar_empty + 8 * s, ((g / ST) - 1) & 1, kErrGemmWait))) {
+          ok = false;
+          break;
+        }
+        dequant_half_row<WQ>(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, gsel, q.gpb);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar_rempty + 8 * rs);
+          mbar_arrive(bar_aready + 8 * s);
+        }
+      }
+    }
+  } else if (warp >= 12) {  // epilogue: tensor memory -> rows of Y
+    const int ew = warp & 3, rl = ew * 32 + lane;
+    const bool isglu = a.epi == 1 || a.epi == 4 || a.epi == 5;
+    int j = 0;
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++j) {
+      int e, r0, rc, tile;
+      item(w, e, r0, rc, tile);
+      const int n0 = tile * 128;
+      const int b = j & 1;
+      const bool ok = mbar_wait(bar_accf + 8 * b, (j >> 1) & 1, kErrTmemWait);
+      tc_fence_after();
+      const float bb = (a.bias && n0 + rl < a.N) ? bf2f(a.bias[(size_t)e * a.N + n0 + rl]) : 0.f;
+      const uint32_t tl = tmem + (uint32_t)(b * S::kAccCols) + ((uint32_t)(ew * 32) << 16);
+      for (int jc = 0; jc < BN; jc += 16) {
+        float f[16];
+        uint32_t v[16];
+        tmem_ld16(tl + jc, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 16; ++c) f[c] = ok ? __uint_as_float(v[c]) + bb : 0.f;
+        if (isglu) {
+          if (ew >= 2) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) xbuf[(rl - 64) * BN + jc + c] = f[c];
+          }
+          epi_bar_sync();
+          if (ew < 2) {
+            const int fo = (n0 >> 1) + rl;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const int row = jc + c;
+              if (row < rc && fo < (a.N >> 1)) {
+                const float gg = bf2f(f2bf(f[c])), u = bf2f(f2bf(xbuf[rl * BN + jc + c]));
+                a.Y[(size_t)(r0 + row) * a.ldy + fo] = f2bf(glu(a.epi, gg, u));
+              }
+            }
+          }
+          epi_bar_sync();
+        } else if (n0 + rl < a.N) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int row = jc + c;
+            if (row < rc) a.Y[(size_t)(r0 + row) * a.ldy + n0 + rl] = f2bf(f[c]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_acce + 8 * b);
+      if (!ok) break;
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::kTmem);
+  }
+}
+
+template <int BN, int WQ>
+int launch_persistent(const CUtensorMap& tx, const GArgs& a, const GQuant& q, int num_sms, cudaStream_t st) {
+  using S = PSmem<BN, WQ>;
+  if (int e = smem_attr_once<grouped_persistent_kernel<BN, WQ>>(S::kTotal)) return e;
+  cudaError_t e = launch_k(grouped_persistent_kernel<BN, WQ>, dim3(num_sms), dim3(S::kThreads), S::kTotal, st, 1, tx,
+                           a, q);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+template <int WQ>
+int dispatch_persistent(int BN, const CUtensorMap& tx, const GArgs& a, const GQuant& q, int num_sms,
+                        cudaStream_t st) {
+  switch (BN) {
+    case 16: return launch_persistent<16, WQ>(tx, a, q, num_sms, st);
+    case 32: return launch_persistent<32, WQ>(tx, a, q, num_sms, st);
+    default: return -1;
+  }
+}
+
+__global__ void e2m1_pairs_kernel(uint32_t* out) { out[threadIdx.x] = e2m1x2_to_f16x2(threadIdx.x); }
+
 template <int BN, int STAGES, int WQ>
 int launch_grouped(const CUtensorMap& tw, const CUtensorMap& tx, const GArgs& a, const GQuant& q, int max_chunks,
                    cudaStream_t st) {
@@ -454,9 +712,11 @@ int b200_moe_grouped_gemm(const void* xs, int P, int K, const void* W, int E, in
 // Same with affine-quantised experts in the tile-major device layout: per
 // expert ceil(N/128) tiles of K/64 records {codes [128][bits*8 B], scales,
 // biases [gpb][128] bf16} (rows past N are zero).
+// `persistent` > 0: chunks of <= 32 rows run on that many persistent CTAs
+// (one per SM); 0 = one CTA per (tile, chunk).
 int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* tiled, int bits, int gs, int E, int N, void* Y,
                             int ldy, const void* bias, int epi, const int* chunks, const int* n_chunks, int max_chunks,
-                            int BN, cudaStream_t st) {
+                            int BN, int persistent, cudaStream_t st) {
   if (P <= 0) return 0;
   if ((K % 64) || (gs == 128 && K % 128) || (N % 8) || (bits != 4 && bits != 8 && bits != kWqE2M1) ||
       (gs != 16 && gs != 32 && gs != 64 && gs != 128))
@@ -473,9 +733,20 @@ int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* tiled, int
   if (!make_tmap_2d(&tx, xs, P, K, K, BN, 64, 2)) return -1;
   moe::GArgs a{reinterpret_cast<__nv_bfloat16*>(Y), reinterpret_cast<const __nv_bfloat16*>(bias), chunks, n_chunks,
                N, K, ldy, epi};
+  if (BN <= 32 && persistent > 0) {  // decode-sized chunks: one CTA per SM over all work items
+    if (bits == kWqE2M1) return moe::dispatch_persistent<kWqE2M1>(BN, tx, a, q, persistent, st);
+    return bits == 4 ? moe::dispatch_persistent<4>(BN, tx, a, q, persistent, st)
+                     : moe::dispatch_persistent<8>(BN, tx, a, q, persistent, st);
+  }
   if (bits == kWqE2M1) return moe::dispatch_grouped<kWqE2M1>(BN, tx, tx, a, q, max_chunks, st);
   return bits == 4 ? moe::dispatch_grouped<4>(BN, tx, tx, a, q, max_chunks, st)
                    : moe::dispatch_grouped<8>(BN, tx, tx, a, q, max_chunks, st);
+}
+
+// Diagnostics / test hook: out[b] = cvt.rn.f16x2.e2m1x2 of byte b, b = 0..255.
+int b200_e2m1_pairs(uint32_t* out, cudaStream_t st) {
+  cudaError_t e = launch_k(moe::e2m1_pairs_kernel, dim3(1), dim3(256), 0, st, 0, out);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 }  // extern "C"

@@ -70,6 +70,7 @@ _SIGS = {
     "b200_lora_expand": (i32, [vp, i32, vp, i32, i32, vp, vp, vp, i32, i32, vp]),
     "b200_lora_expand_glu": (i32, [vp, i32, vp, i32, i32, vp, i32, vp, vp, vp, i32, i32, i32, vp]),
     "b200_mtp_accept": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, vp, vp, i32, vp]),
+    "b200_e2m1_pairs": (i32, [vp, vp]),
     "b200_set_pdl": (None, [i32]),
     "b200_get_pdl": (i32, []),
 }

@@ -19,6 +19,8 @@ CPU tensors take the plain PyTorch path (used by the CPU test suite).
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib
@@ -40,7 +42,7 @@ _lib.register_signatures({
                                          _lib.vp]),
     "b200_moe_grouped_gemm_q": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.i32,
                                            _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.vp,
-                                           _lib.i32, _lib.i32, _lib.vp]),
+                                           _lib.i32, _lib.i32, _lib.i32, _lib.vp]),
 }, status_tags=("moe",))
 
 
@@ -125,11 +127,18 @@ def chunk_rows(P: int, E: int) -> int:
     return 128
 
 
+# quantised experts, chunks of <= 32 rows (decode): persistent CTAs, one per SM,
+# looping over (chunk, weight tile) items; B200LM_MOE_PERSISTENT=0 launches a CTA per item
+PERSISTENT = [os.environ.get("B200LM_MOE_PERSISTENT", "1") != "0"]
+
+
 def _grouped(L, xs, P, K, W, E, N, Y, ldy, bias, epi, chunks, n_chunks, max_chunks, BN, st, what):
     if isinstance(W, QuantizedWeight):
+        from .linear import num_sms
+
         rc = L.b200_moe_grouped_gemm_q(xs.data_ptr(), P, K, W.tiled().data_ptr(), W.kernel_bits, W.gs, E, N, Y.data_ptr(),
                                        ldy, _lib.ptr(bias), epi, chunks.data_ptr(), n_chunks.data_ptr(), max_chunks,
-                                       BN, st)
+                                       BN, num_sms(xs.device) if PERSISTENT[0] else 0, st)
     else:
         rc = L.b200_moe_grouped_gemm(xs.data_ptr(), P, K, W.data_ptr(), E, N, Y.data_ptr(), ldy, _lib.ptr(bias), epi,
                                      chunks.data_ptr(), n_chunks.data_ptr(), max_chunks, BN, st)

@@ -208,3 +208,63 @@ def test_sigmoid_group_router_kernel(E, k, n_group, topk_group):
     torch.cuda.synchronize()
     assert torch.equal(i.cpu().long(), i_ref)
     assert torch.allclose(w.cpu(), w_ref, atol=1e-5)
+
+
+def test_e2m1_hardware_pairs():
+    """cvt.rn.f16x2.e2m1x2 on every byte: the low nibble lands in the low f16
+    of the pair, the high nibble in the high f16, values from the e2m1 table."""
+    from mlx_swift_lm_b200.ops import _lib
+
+    out = torch.empty(256, dtype=torch.int32, device="cuda")
+    _lib.check(_lib.lib().b200_e2m1_pairs(out.data_ptr(), _lib.stream_ptr(out.device)), "e2m1_pairs")
+    got = out.cpu().view(torch.float16).view(256, 2).float()
+    mag = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+
+    def val(c):
+        return (-1.0 if c & 8 else 1.0) * mag[c & 7]
+
+    want = torch.tensor([[val(b & 15), val(b >> 4)] for b in range(256)])
+    assert torch.equal(got, want), (got[:20], want[:20])
+
+
+@pytest.mark.parametrize("fmt", ["q4", "q8", "mxfp4"])
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (64, 128, 4), (24, 32, 8)])
+def test_persistent_grouped_gemm_equals_per_item(fmt, T, E, k):
+    """Decode-sized chunks on persistent CTAs (one per SM, looping over
+    (chunk, tile) items, double-buffered accumulators) give the same bits as
+    one CTA per item: the same K order and epilogue per output element."""
+    from mlx_swift_lm_b200.ops import moe as moe_ops
+    from mlx_swift_lm_b200.ops.qlinear import QuantizedWeight
+
+    torch.manual_seed(T * 7 + E)
+    K, F = 512, 256
+    h = torch.randn(T, K, device=DEV, dtype=torch.bfloat16)
+    gu_f = [ref.interleave_gate_up(torch.randn(F, K) * 0.05, torch.randn(F, K) * 0.05) for _ in range(E)]
+    d_f = [torch.randn(K, F) * 0.05 for _ in range(E)]
+    if fmt == "mxfp4":
+        q = QuantizedWeight.quantize_mxfp4
+    else:
+        bits = 4 if fmt == "q4" else 8
+
+        def q(t):
+            return QuantizedWeight.quantize(t, bits, 64)
+    gu = QuantizedWeight.stack_experts([q(t) for t in gu_f]).to(DEV)
+    d = QuantizedWeight.stack_experts([q(t) for t in d_f]).to(DEV)
+    w, idx = moe.route_topk(torch.randn(T, E, device=DEV), k)
+    epi = "swiglu_oai" if fmt == "mxfp4" else "swiglu"
+    outs = []
+    for pers in (True, False):
+        moe_ops.PERSISTENT[0] = pers
+        try:
+            outs.append(moe.moe_experts(h, gu, d, w, idx, epi))
+        finally:
+            moe_ops.PERSISTENT[0] = True
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    assert _lib_status_ok()
+
+
+def _lib_status_ok():
+    from mlx_swift_lm_b200.ops import _lib
+
+    return _lib.read_status().get("moe", 0) == 0
