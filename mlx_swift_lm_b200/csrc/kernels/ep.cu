@@ -76,16 +76,16 @@ __device__ __forceinline__ void copy_row(__nv_bfloat16* dst, const __nv_bfloat16
   for (int i = t; i < H / 8; i += nt) d[i] = s[i];
 }
 
-// The last CTA of a grid (thread 0, after its own writes) runs `last`, then
-// publishes `epoch` to flag(pad, rank) of every rank.
+// The last CTA of a grid (thread 0, after its own writes, behind a CTA
+// barrier) runs `last`, then publishes `epoch` to flag(pad, rank) of every
+// rank. Ordering as in last_cta_signal (b200_comm.cuh): GPU-scope acq_rel
+// ticket increments, system-scope release flag stores, no full fences.
 template <typename F>
 __device__ __forceinline__ void last_cta(const EpCtx& c, int* ticket, int pad, uint32_t epoch, F&& last) {
-  __threadfence_system();
-  if (atomicAdd(ticket, 1) == (int)(gridDim.x * gridDim.y * gridDim.z) - 1) {
-    __threadfence_system();
+  const int t = (int)ticket_add_acq_rel(reinterpret_cast<uint32_t*>(ticket), 1u);
+  if (t == (int)(gridDim.x * gridDim.y * gridDim.z) - 1) {
     *ticket = 0;
     last();
-    __threadfence_system();
     for (int j = 0; j < c.world; ++j) signal_store(c.pad(j, pad, c.rank), epoch);
   }
 }
