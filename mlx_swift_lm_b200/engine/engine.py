@@ -70,6 +70,9 @@ class EngineConfig:
     enable_prefix_cache: bool = False
     prefix_block_size: int = 256
     prefix_host_blocks: int = 0  # pinned host tier of the prefix cache (blocks of prefix_block_size tokens)
+    # hybrid models (recurrent-state layers): device snapshots of the state at prefix block
+    # boundaries; a prefix is reused only up to a block with a snapshot (0 = no prefix cache)
+    prefix_state_snapshots: int = 16
     # ring storage for sliding-window layers (window + one step of pages per
     # request instead of the whole context); None: on unless prefix caching is
     window_ring: bool | None = None
@@ -174,13 +177,16 @@ class EngineV2:
             self.kv = PagedKVCache.for_model(model, max_tokens=kv_tokens, kv_fp8=self.cfg.kv_fp8, max_seqs=seqs,
                                              ring_chunk=ring_chunk, max_len=self.cfg.max_model_len)
         self.prefix_cache = None
-        # a recurrent state cannot be rebuilt from shared KV pages, nor can an
-        # overwritten window ring: no prefix reuse for hybrid models or ring storage
-        if self.cfg.enable_prefix_cache and self.kv.rec is None and not self.kv.ring_pages:
+        # an overwritten window ring cannot be shared; hybrid models reuse a
+        # prefix only up to a block boundary with a recurrent-state snapshot
+        if (self.cfg.enable_prefix_cache and not self.kv.ring_pages
+                and (self.kv.rec is None or self.cfg.prefix_state_snapshots > 0)):
             from ..kv.prefix_cache import PrefixCache
 
             self.prefix_cache = PrefixCache(self.kv, self.cfg.prefix_block_size,
-                                            host_blocks=self.cfg.prefix_host_blocks)
+                                            host_blocks=self.cfg.prefix_host_blocks,
+                                            state_snapshots=self.cfg.prefix_state_snapshots
+                                            if self.kv.rec is not None else 0)
         from .admission import AdmissionConfig, AdmissionLedger, layer_kinds_for
 
         rec_bytes = self.kv.rec.bytes_per_seq if self.kv.rec is not None else 0
@@ -528,6 +534,11 @@ class EngineV2:
                 fb = self._build_batch(plan, self.device)
                 hid = None
                 dtok = self.diagnostics.begin_forward(self.device) if self.diagnostics is not None else None
+                pc = self.prefix_cache
+                if pc is not None and pc.states is not None:
+                    for r in plan.rows:
+                        if "state_restore" in r.state.extra:
+                            pc.restore_state(r.state)
                 with _nvtx("forward"):
                     if self.mtp is not None:
                         logits, hid = self.model.forward(fb, self.kv, return_both=True)
@@ -535,6 +546,10 @@ class EngineV2:
                         logits = self.model.forward(fb, self.kv)
                 if self.diagnostics is not None:
                     self.diagnostics.end_forward(dtok, self.steps, fb, logits)
+                if pc is not None and pc.states is not None:
+                    for r in plan.rows:
+                        if not r.is_decode:
+                            pc.after_prefill_chunk(r.state, r.start + r.num_tokens)
                 srows = [r for r in plan.rows if r.sample]
                 if getattr(self.model, "pp_stages", 1) > 1:
                     toks, lp = self._pp_tokens(logits, srows)

@@ -180,6 +180,18 @@ class Scheduler:
         return ok
 
     # ------------------------------------------------------------------ plan
+    def _snap_cap(self, st, n: int) -> int:
+        """Hybrid models with a prefix cache: a prefill chunk stops at the
+        prompt's last full block boundary, so the recurrent state there can be
+        kept for later requests with the same prefix."""
+        pc = self.prefix_cache
+        if pc is None or pc.states is None:
+            return n
+        b = pc.snapshot_boundary(st)
+        if st.num_computed < b < st.num_computed + n:
+            return b - st.num_computed
+        return n
+
     def plan(self) -> StepPlan:
         cfg = self.cfg
         budget = cfg.max_batched_tokens_per_step
@@ -223,7 +235,7 @@ class Scheduler:
                 break
             if st.status != Status.RUNNING:
                 continue
-            n = min(st.remaining, cfg.prefill_chunk_size, pbudget)
+            n = self._snap_cap(st, min(st.remaining, cfg.prefill_chunk_size, pbudget))
             if not self._ensure(st, st.num_computed + n):
                 continue
             rows.append(ScheduledRow(st, st.num_computed, n, False, st.num_computed + n == len(st.all_tokens)))
@@ -239,7 +251,7 @@ class Scheduler:
                     continue
                 if self.prefix_cache is not None and st.num_computed == 0 and cfg.enable_prefix_cache:
                     self.prefix_cache.match_and_adopt(st)
-                n = min(st.remaining, cfg.prefill_chunk_size, pbudget)
+                n = self._snap_cap(st, min(st.remaining, cfg.prefill_chunk_size, pbudget))
                 if n <= 0:
                     continue
                 mm = st.req.mm

@@ -84,8 +84,56 @@ class HostTier:
         return [t[:, self._rows(slot)] for t in self.k], [t[:, self._rows(slot)] for t in self.v]
 
 
+class StateSnapshots:
+    """Recurrent-state snapshots of hybrid models (linear-attention / SSM
+    layers) at prefix block boundaries: the state after a sequence consumed
+    blocks 0..b is kept under block b's chain hash, so a later request with
+    that prefix adopts the blocks' KV pages and continues from the copied
+    state instead of recomputing the prefix (the reference's hybrid prefix
+    cache, ContinuousBatchingV2/Prefix/HybridPrefixCache.swift:7). LRU over a
+    fixed number of device slots shaped like the recurrent-state pool."""
+
+    def __init__(self, rec, max_snapshots: int):
+        self.rec = rec
+        L = rec.conv.shape[0]
+        self.conv = torch.empty((L, max_snapshots) + tuple(rec.conv.shape[2:]), dtype=rec.conv.dtype,
+                                device=rec.conv.device)
+        self.ssm = torch.empty((L, max_snapshots) + tuple(rec.ssm.shape[2:]), dtype=rec.ssm.dtype,
+                               device=rec.ssm.device)
+        self.free = list(range(max_snapshots))
+        self.entries: "collections.OrderedDict[bytes, int]" = collections.OrderedDict()
+        self.saves = 0
+        self.restores = 0
+
+    def save(self, h: bytes, slot: int):
+        if h in self.entries:
+            self.entries.move_to_end(h)
+            return
+        if not self.free:
+            if not self.entries:
+                return
+            _, i = self.entries.popitem(last=False)
+            self.free.append(i)
+        i = self.free.pop()
+        self.conv[:, i].copy_(self.rec.conv[:, slot])
+        self.ssm[:, i].copy_(self.rec.ssm[:, slot])
+        self.entries[h] = i
+        self.saves += 1
+
+    def restore(self, h: bytes, slot: int) -> bool:
+        i = self.entries.get(h)
+        if i is None:
+            return False
+        self.entries.move_to_end(h)
+        self.rec.conv[:, slot].copy_(self.conv[:, i])
+        self.rec.ssm[:, slot].copy_(self.ssm[:, i])
+        self.restores += 1
+        return True
+
+
 class PrefixCache:
-    def __init__(self, cache: PagedKVCache, block_size: int = 256, default_salt: str = "", host_blocks: int = 0):
+    def __init__(self, cache: PagedKVCache, block_size: int = 256, default_salt: str = "", host_blocks: int = 0,
+                 state_snapshots: int = 0):
         assert block_size % PAGE == 0, "block size must be a multiple of the page size"
         self.cache = cache
         self.block = block_size
@@ -93,6 +141,10 @@ class PrefixCache:
         self.salt = default_salt
         self.entries: "collections.OrderedDict[bytes, list[int]]" = collections.OrderedDict()
         self.host = HostTier(cache, host_blocks, self.pages_per_block) if host_blocks > 0 else None
+        # hybrid models: a match must end at a block whose recurrent state was kept
+        self.states = StateSnapshots(cache.rec, state_snapshots) if cache.rec is not None else None
+        if cache.rec is not None and state_snapshots <= 0:
+            raise ValueError("a prefix cache over recurrent-state layers needs state_snapshots > 0")
         self.hits = 0
         self.misses = 0
         self.hit_tokens = 0
@@ -111,6 +163,15 @@ class PrefixCache:
             self.misses += 1
             return 0
         hashes = self._hashes(toks[: usable * self.block], req.cache_salt)
+        if self.states is not None:
+            # the longest cached chain that ends at a block with a state snapshot
+            n_ok = 0
+            for b, h in enumerate(hashes):
+                if h not in self.entries and not (self.host is not None and h in self.host.entries):
+                    break
+                if h in self.states.entries:
+                    n_ok = b + 1
+            hashes = hashes[:n_ok]
         pages = []
         chain = set()
         for h in hashes:
@@ -122,12 +183,16 @@ class PrefixCache:
                 break
             self.entries.move_to_end(h)
             pages.extend(ent)
+        if self.states is not None and pages and len(pages) != len(hashes) * self.pages_per_block:
+            pages = []  # a block of the chain could not be brought back: its state has no KV
         if not pages:
             self.misses += 1
             return 0
         self.cache.pool.incref(pages)
         n = len(pages) * PAGE
         st.seq.adopt_prefix(pages, n)
+        if self.states is not None:
+            st.extra["state_restore"] = hashes[len(pages) // self.pages_per_block - 1]
         st.usage.cached_prompt_tokens = n
         self.hits += 1
         self.hit_tokens += n
@@ -151,6 +216,32 @@ class PrefixCache:
                 break
             self.cache.pool.incref(pages)
             self.entries[h] = list(pages)
+
+    # ------------------------------------------------------------------ hybrid models
+    def snapshot_boundary(self, st) -> int:
+        """Token count at which a hybrid request's recurrent state is worth
+        keeping: the last full block before the prompt's last token (the
+        longest prefix a later identical prompt can reuse); 0 if none."""
+        if self.states is None or not st.req.prefix_cache_enabled:
+            return 0
+        return ((st.num_prompt - 1) // self.block) * self.block
+
+    def after_prefill_chunk(self, st, end: int):
+        """Keep the state of a hybrid request whose prefill reached a block
+        boundary (its state slot now holds the state after `end` tokens)."""
+        if self.states is None or not st.req.prefix_cache_enabled or end <= 0 or end % self.block:
+            return
+        if end > self.snapshot_boundary(st):
+            return
+        h = self._hashes(st.all_tokens[:end], st.req.cache_salt)[-1]
+        self.states.save(h, st.seq.state_slot)
+
+    def restore_state(self, st):
+        """Before a matched hybrid request's first forward: its state slot
+        gets the snapshot at the end of the adopted prefix."""
+        h = st.extra.pop("state_restore", None)
+        if h is not None and not self.states.restore(h, st.seq.state_slot):
+            raise RuntimeError("prefix state snapshot evicted between match and first forward")
 
     def _promote(self, h: bytes, keep=()):
         """Bring a host-tier block back into fresh device pages, evicting
