@@ -335,6 +335,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn = 
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }
 
+// kind::f16 with both operands f16 (A and B must share the type).
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // Byte offset of element (row, col) inside a 128B-swizzled K-major tile of
 // 64-element (128-byte) rows: 16-byte chunk index XOR (row % 8).
 __device__ __forceinline__ uint32_t sw128_offset(int row, int col_bytes) {

@@ -18,6 +18,8 @@
 // the UMMA descriptor expects (16-byte chunk c of row t at c ^ (t & 7)).
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "b200_common.cuh"
 
 namespace b200 {
@@ -50,6 +52,38 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   uint32_t r;
   asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}" : "=r"(r) : "r"(byte));
   return r;
+}
+
+// MXFP4 records in natural order (input 2j in the low nibble of byte j, 2j+1
+// in the high nibble), dequantised to f16 for f16 x f16 MMAs: one hardware
+// conversion per pair of inputs and one f16 multiply by the block scale
+// (a power of two, exact while the product stays in f16 range). Thread
+// (t, half) converts inputs [32*half, 32*half + 32) of row t into the
+// 128B-swizzled f16 tile.
+__device__ __forceinline__ void dequant_half_row_e2m1_f16(const uint8_t* raw, uint8_t* atile, int t, int half,
+                                                          int g, int gpb) {
+  constexpr int kCodeBytes = 4 * 128 * 64 / 8;
+  const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(raw + kCodeBytes);
+  const __half s0 = __float2half(bf2f(sc[g * 128 + t]));
+  const __half s1 = gpb == 4 ? __float2half(bf2f(sc[(g + 1) * 128 + t])) : s0;
+  const uint4 c = *reinterpret_cast<const uint4*>(raw + t * 32 + half * 16);
+  const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+  uint8_t* arow = atile + t * 128;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t v = words[w];
+    const __half sw = w < 2 ? s0 : s1;
+    const __half2 s2 = __halves2half2(sw, sw);
+    uint32_t o[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t p = e2m1x2_to_f16x2((v >> (8 * b)) & 0xFFu);
+      const __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&p), s2);
+      o[b] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    const int chunk = half * 4 + w;
+    *reinterpret_cast<uint4*>(arow + ((chunk ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 // bf16 pair (q_lo + 128, q_hi + 128) from two 4-bit codes placed at bits 0..3

@@ -22,6 +22,8 @@
 //   moe_combine      out[t] = sum_j w[t, j] * y[pos(t, j)] in slot order j.
 #include <cudaTypedefs.h>
 
+#include <cuda_fp16.h>
+
 #include "b200_common.cuh"
 #include "b200_dequant.cuh"
 #include "b200_moe.cuh"
@@ -127,7 +129,7 @@ __global__ void __launch_bounds__(1024) sort_kernel(const int* __restrict__ ids,
 }
 
 __global__ void gather_kernel(const __nv_bfloat16* __restrict__ x, int K, const int* __restrict__ perm, int P,
-                              int k, __nv_bfloat16* __restrict__ xs) {
+                              int k, __nv_bfloat16* __restrict__ xs, int to_f16) {
   pdl_launch_dependents();
   pdl_wait();
   const int s = blockIdx.x;
@@ -135,7 +137,19 @@ __global__ void gather_kernel(const __nv_bfloat16* __restrict__ x, int K, const 
   const int t = perm[s] / k;
   const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * K);
   uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)s * K);
-  for (int i = threadIdx.x; i < K / 8; i += blockDim.x) dst[i] = src[i];
+  for (int i = threadIdx.x; i < K / 8; i += blockDim.x) {
+    uint4 v = src[i];
+    if (to_f16) {  // activations of the f16 MXFP4 path (saturating at the f16 range)
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+        const __half2 h = __floats2half2_rn(fminf(fmaxf(f.x, -65504.f), 65504.f), fminf(fmaxf(f.y, -65504.f), 65504.f));
+        w[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+    dst[i] = v;
+  }
 }
 
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ ys, int N, const int* __restrict__ pos,
@@ -158,12 +172,18 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ ys, int N, cons
 
 // ---------------------------------------------------------------- grouped GEMM
 struct GArgs {
-  __nv_bfloat16* Y;  // [P, ldy] sorted rows
+  __nv_bfloat16* Y;  // [P, ldy] sorted rows (f16 when y_f16)
   const __nv_bfloat16* bias;  // [E, N] or null
   const int* chunks;
   const int* n_chunks;
   int N, K, ldy, epi;
+  int y_f16;  // f16 output rows (the f16 MXFP4 path's gate/up output feeds the f16 down GEMM)
 };
+
+__device__ __forceinline__ void store_y(const GArgs& a, size_t idx, float v) {
+  if (a.y_f16) reinterpret_cast<__half*>(a.Y)[idx] = __float2half_rn(v);
+  else a.Y[idx] = f2bf(v);
+}
 
 __device__ __forceinline__ float glu(int epi, float g, float u) { return glu_act(epi, g, u); }
 
@@ -193,10 +213,13 @@ struct GSmem {
   static_assert(!WQ || kRawStages >= 4, "raw ring too shallow");
 };
 
-template <int BN, int STAGES, int WQ>
+// F16: MXFP4 experts (natural-order records) dequantised to f16 and
+// multiplied with f16 activations (kind::f16, both operands f16).
+template <int BN, int STAGES, int WQ, bool F16 = false>
 __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STAGES, WQ>::kMinBlocks)
     grouped_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GArgs a,
                    const __grid_constant__ GQuant q) {
+  static_assert(!F16 || WQ == kWqE2M1, "the f16 path serves MXFP4 records");
   using S = GSmem<BN, STAGES, WQ>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -274,7 +297,7 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
         mbar_wait(bar_rfull + 8 * (i % RS), (i / RS) & 1, kErrGemmWait);
     }
   } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+    constexpr uint32_t idesc = F16 ? umma_idesc_f16(128, BN) : umma_idesc_bf16(128, BN);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
       if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
@@ -298,7 +321,11 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
         const int s = i % STAGES, r = i / STAGES;
         if (!mbar_wait(bar_rfull + 8 * rs, rr & 1, kErrGemmWait)) break;
         if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
-        dequant_half_row<WQ>(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, g, q.gpb);
+        if constexpr (F16) {
+          dequant_half_row_e2m1_f16(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, g, q.gpb);
+        } else {
+          dequant_half_row<WQ>(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, g, q.gpb);
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -339,7 +366,7 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
           const int row = jc + j;
           if (row < rc && fo < (a.N >> 1)) {
             const float gg = bf2f(f2bf(f[j])), u = bf2f(f2bf(xbuf[rl][j]));
-            a.Y[(size_t)(r0 + row) * a.ldy + fo] = f2bf(glu(a.epi, gg, u));
+            store_y(a, (size_t)(r0 + row) * a.ldy + fo, glu(a.epi, gg, u));
           }
         }
       }
@@ -347,7 +374,7 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int row = jc + j;
-        if (row < rc) a.Y[(size_t)(r0 + row) * a.ldy + n0 + rl] = f2bf(f[j]);
+        if (row < rc) store_y(a, (size_t)(r0 + row) * a.ldy + n0 + rl, f[j]);
       }
     }
   }
@@ -568,7 +595,7 @@ __global__ void __launch_bounds__(512, 1)
               const int row = jc + c;
               if (row < rc && fo < (a.N >> 1)) {
                 const float gg = bf2f(f2bf(f[c])), u = bf2f(f2bf(xbuf[rl * BN + jc + c]));
-                a.Y[(size_t)(r0 + row) * a.ldy + fo] = f2bf(glu(a.epi, gg, u));
+                store_y(a, (size_t)(r0 + row) * a.ldy + fo, glu(a.epi, gg, u));
               }
             }
           }
@@ -577,7 +604,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const int row = jc + c;
-            if (row < rc) a.Y[(size_t)(r0 + row) * a.ldy + n0 + rl] = f2bf(f[c]);
+            if (row < rc) store_y(a, (size_t)(r0 + row) * a.ldy + n0 + rl, f[c]);
           }
         }
       }
@@ -616,6 +643,27 @@ int dispatch_persistent(int BN, const CUtensorMap& tx, const GArgs& a, const GQu
 }
 
 __global__ void e2m1_pairs_kernel(uint32_t* out) { out[threadIdx.x] = e2m1x2_to_f16x2(threadIdx.x); }
+
+template <int BN, int STAGES, int WQ, bool F16>
+int launch_grouped_f(const CUtensorMap& tw, const CUtensorMap& tx, const GArgs& a, const GQuant& q, int max_chunks,
+                     cudaStream_t st) {
+  using S = GSmem<BN, STAGES, WQ>;
+  if (int e = smem_attr_once<grouped_kernel<BN, STAGES, WQ, F16>>(S::kTotal)) return e;
+  cudaError_t e = launch_k(grouped_kernel<BN, STAGES, WQ, F16>, dim3((a.N + 127) / 128, max_chunks),
+                           dim3(S::kThreads), S::kTotal, st, 1, tw, tx, a, q);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+inline int dispatch_grouped_f16(int BN, const CUtensorMap& tx, const GArgs& a, const GQuant& q, int max_chunks,
+                                cudaStream_t st) {
+  switch (BN) {
+    case 16: return launch_grouped_f<16, 3, kWqE2M1, true>(tx, tx, a, q, max_chunks, st);
+    case 32: return launch_grouped_f<32, 3, kWqE2M1, true>(tx, tx, a, q, max_chunks, st);
+    case 64: return launch_grouped_f<64, 2, kWqE2M1, true>(tx, tx, a, q, max_chunks, st);
+    case 128: return launch_grouped_f<128, 2, kWqE2M1, true>(tx, tx, a, q, max_chunks, st);
+    default: return -1;
+  }
+}
 
 template <int BN, int STAGES, int WQ>
 int launch_grouped(const CUtensorMap& tw, const CUtensorMap& tx, const GArgs& a, const GQuant& q, int max_chunks,
@@ -676,11 +724,12 @@ int b200_moe_sort(const int* ids, int P, int E, int BN, int max_chunks, int* per
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
-int b200_moe_gather(const void* x, int K, const int* perm, int P, int k, void* xs, cudaStream_t st) {
+int b200_moe_gather(const void* x, int K, const int* perm, int P, int k, void* xs, int to_f16, cudaStream_t st) {
   if (P <= 0) return 0;
   if (K % 8) return -1;
   cudaError_t e = launch_k(moe::gather_kernel, dim3(P), dim3(128), 0, st, 1,
-                           reinterpret_cast<const __nv_bfloat16*>(x), K, perm, P, k, reinterpret_cast<__nv_bfloat16*>(xs));
+                           reinterpret_cast<const __nv_bfloat16*>(x), K, perm, P, k, reinterpret_cast<__nv_bfloat16*>(xs),
+                           to_f16);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
@@ -704,7 +753,7 @@ int b200_moe_grouped_gemm(const void* xs, int P, int K, const void* W, int E, in
   if (!make_tmap_2d(&tw, W, (int64_t)E * N, K, K, 128, 64, 2)) return -1;
   if (!make_tmap_2d(&tx, xs, P, K, K, BN, 64, 2)) return -1;
   moe::GArgs a{reinterpret_cast<__nv_bfloat16*>(Y), reinterpret_cast<const __nv_bfloat16*>(bias), chunks, n_chunks,
-               N, K, ldy, epi};
+               N, K, ldy, epi, 0};
   moe::GQuant q = {};
   return moe::dispatch_grouped<0>(BN, tw, tx, a, q, max_chunks, st);
 }
@@ -714,9 +763,11 @@ int b200_moe_grouped_gemm(const void* xs, int P, int K, const void* W, int E, in
 // biases [gpb][128] bf16} (rows past N are zero).
 // `persistent` > 0: chunks of <= 32 rows run on that many persistent CTAs
 // (one per SM); 0 = one CTA per (tile, chunk).
+// `f16` (MXFP4 only): natural-order records, f16 activation rows xs, f16
+// dequantised weights (kind::f16 with both operands f16); `y_f16`: f16 Y.
 int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* tiled, int bits, int gs, int E, int N, void* Y,
                             int ldy, const void* bias, int epi, const int* chunks, const int* n_chunks, int max_chunks,
-                            int BN, int persistent, cudaStream_t st) {
+                            int BN, int persistent, int f16, int y_f16, cudaStream_t st) {
   if (P <= 0) return 0;
   if ((K % 64) || (gs == 128 && K % 128) || (N % 8) || (bits != 4 && bits != 8 && bits != kWqE2M1) ||
       (gs != 16 && gs != 32 && gs != 64 && gs != 128))
@@ -732,7 +783,11 @@ int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* tiled, int
   q.tiles_per_expert = (N + 127) / 128;
   if (!make_tmap_2d(&tx, xs, P, K, K, BN, 64, 2)) return -1;
   moe::GArgs a{reinterpret_cast<__nv_bfloat16*>(Y), reinterpret_cast<const __nv_bfloat16*>(bias), chunks, n_chunks,
-               N, K, ldy, epi};
+               N, K, ldy, epi, y_f16};
+  if (f16) {
+    if (bits != kWqE2M1) return -1;
+    return moe::dispatch_grouped_f16(BN, tx, a, q, max_chunks, st);
+  }
   if (BN <= 32 && persistent > 0) {  // decode-sized chunks: one CTA per SM over all work items
     if (bits == kWqE2M1) return moe::dispatch_persistent<kWqE2M1>(BN, tx, a, q, persistent, st);
     return bits == 4 ? moe::dispatch_persistent<4>(BN, tx, a, q, persistent, st)

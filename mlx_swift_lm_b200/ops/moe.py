@@ -34,7 +34,7 @@ _lib.register_signatures({
                                        _lib.vp, _lib.i32, _lib.i32, _lib.f32, _lib.vp]),
     "b200_moe_sort": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.vp,
                                  _lib.vp, _lib.vp]),
-    "b200_moe_gather": (_lib.i32, [_lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.vp]),
+    "b200_moe_gather": (_lib.i32, [_lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.vp]),
     "b200_moe_combine": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.vp, _lib.i32, _lib.vp, _lib.vp,
                                     _lib.vp, _lib.vp]),
     "b200_moe_grouped_gemm": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.vp,
@@ -42,7 +42,7 @@ _lib.register_signatures({
                                          _lib.vp]),
     "b200_moe_grouped_gemm_q": (_lib.i32, [_lib.vp, _lib.i32, _lib.i32, _lib.vp, _lib.i32, _lib.i32, _lib.i32,
                                            _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.i32, _lib.vp, _lib.vp,
-                                           _lib.i32, _lib.i32, _lib.i32, _lib.vp]),
+                                           _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.i32, _lib.vp]),
 }, status_tags=("moe",))
 
 
@@ -127,18 +127,31 @@ def chunk_rows(P: int, E: int) -> int:
     return 128
 
 
-# quantised experts, chunks of <= 32 rows (decode): persistent CTAs, one per SM,
-# looping over (chunk, weight tile) items; B200LM_MOE_PERSISTENT=0 launches a CTA per item
-PERSISTENT = [os.environ.get("B200LM_MOE_PERSISTENT", "1") != "0"]
+# quantised experts, chunks of <= 32 rows (decode): B200LM_MOE_PERSISTENT=1 runs
+# persistent CTAs (one per SM, looping over (chunk, weight tile) items). Off by
+# default: with one CTA per SM it has half the dequantising warps per SM of the
+# two-CTAs-per-SM launch, and the dequantisation is the limit at decode sizes.
+PERSISTENT = [os.environ.get("B200LM_MOE_PERSISTENT", "0") == "1"]
+# MXFP4 experts: f16 operands (hardware e2m1 pair conversion, f16 activations
+# and gate/up rows) when every block scale keeps the weights normal f16
+F16_MXFP4 = [os.environ.get("B200LM_MOE_F16", "1") != "0"]
 
 
-def _grouped(L, xs, P, K, W, E, N, Y, ldy, bias, epi, chunks, n_chunks, max_chunks, BN, st, what):
+def _f16_path(W) -> bool:
+    return (F16_MXFP4[0] and isinstance(W, QuantizedWeight) and W.kernel_bits == -4 and W.gs == 32
+            and W.f16_scales_ok())
+
+
+def _grouped(L, xs, P, K, W, E, N, Y, ldy, bias, epi, chunks, n_chunks, max_chunks, BN, st, what, f16=False,
+             y_f16=False):
     if isinstance(W, QuantizedWeight):
         from .linear import num_sms
 
-        rc = L.b200_moe_grouped_gemm_q(xs.data_ptr(), P, K, W.tiled().data_ptr(), W.kernel_bits, W.gs, E, N, Y.data_ptr(),
+        rec = W.tiled_natural() if f16 else W.tiled()
+        rc = L.b200_moe_grouped_gemm_q(xs.data_ptr(), P, K, rec.data_ptr(), W.kernel_bits, W.gs, E, N, Y.data_ptr(),
                                        ldy, _lib.ptr(bias), epi, chunks.data_ptr(), n_chunks.data_ptr(), max_chunks,
-                                       BN, num_sms(xs.device) if PERSISTENT[0] else 0, st)
+                                       BN, num_sms(xs.device) if PERSISTENT[0] else 0, 1 if f16 else 0,
+                                       1 if y_f16 else 0, st)
     else:
         rc = L.b200_moe_grouped_gemm(xs.data_ptr(), P, K, W.data_ptr(), E, N, Y.data_ptr(), ldy, _lib.ptr(bias), epi,
                                      chunks.data_ptr(), n_chunks.data_ptr(), max_chunks, BN, st)
@@ -168,8 +181,9 @@ def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias, ro
     pos = torch.empty(P, dtype=torch.int32, device=dev)
     chunks = torch.empty(max_chunks * 3, dtype=torch.int32, device=dev)
     n_chunks = torch.empty(1, dtype=torch.int32, device=dev)
-    xs = torch.empty(P, K, dtype=h.dtype, device=dev)
-    gu = torch.empty(P, F, dtype=h.dtype, device=dev)
+    f16 = rot_mid is None and _f16_path(experts_gu) and _f16_path(experts_d)
+    xs = torch.empty(P, K, dtype=torch.float16 if f16 else h.dtype, device=dev)
+    gu = torch.empty(P, F, dtype=torch.float16 if f16 else h.dtype, device=dev)
     ys = torch.empty(P, K, dtype=h.dtype, device=dev)
     out = torch.empty(T, K, dtype=h.dtype, device=dev)
     L = _lib.lib()
@@ -177,12 +191,13 @@ def _moe_experts_cuda(h, experts_gu, experts_d, w, idx, epi, gu_bias, d_bias, ro
     hc = h.contiguous()
     _lib.check(L.b200_moe_sort(ids.data_ptr(), P, E, BN, max_chunks, perm.data_ptr(), pos.data_ptr(),
                                chunks.data_ptr(), n_chunks.data_ptr(), st), "moe_sort")
-    _lib.check(L.b200_moe_gather(hc.data_ptr(), K, perm.data_ptr(), P, k, xs.data_ptr(), st), "moe_gather")
+    _lib.check(L.b200_moe_gather(hc.data_ptr(), K, perm.data_ptr(), P, k, xs.data_ptr(), 1 if f16 else 0, st),
+               "moe_gather")
     _grouped(L, xs, P, K, experts_gu, E, N2, gu, F, gu_bias, _EPI[epi], chunks, n_chunks, max_chunks, BN, st,
-             "gate/up")
+             "gate/up", f16=f16, y_f16=f16)
     if rot_mid is not None:
         gu = rot_mid.rotate(gu)
-    _grouped(L, gu, P, F, experts_d, E, K, ys, K, d_bias, 0, chunks, n_chunks, max_chunks, BN, st, "down")
+    _grouped(L, gu, P, F, experts_d, E, K, ys, K, d_bias, 0, chunks, n_chunks, max_chunks, BN, st, "down", f16=f16)
     _lib.check(L.b200_moe_combine(ys.data_ptr(), T, K, pos.data_ptr(), w.data_ptr(), k, out.data_ptr(), None, None,
                                   st), "moe_combine")
     _lib.count(5)

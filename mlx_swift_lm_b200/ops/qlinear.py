@@ -265,14 +265,37 @@ class QuantizedWeight:
         gpb = {16: 4, 32: 2}.get(self.gs, 1)
         return self.bits * 128 * 8 + gpb * (256 if self.biases_t is None else 512)
 
-    def tiled(self) -> torch.Tensor:
+    def tiled_natural(self) -> torch.Tensor:
+        """e2m1 records with the codes in natural order (input 2j in the low
+        nibble of byte j, 2j+1 in the high nibble): the layout the hardware
+        pair conversion of the f16 MoE path reads (built once, cached)."""
+        t = getattr(self, "_tiled_nat", None)
+        if t is None:
+            assert self.kernel_bits == -4, "natural-order records are for e2m1 codes"
+            q = _unpack4(self.codes)
+            nat = (q[:, 0::2] | (q[:, 1::2] << 4)).to(torch.uint8).contiguous()
+            t = self._tiled_nat = self.tiled(codes=nat, cache=False)
+        return t
+
+    def f16_scales_ok(self) -> bool:
+        """Every e2m1 weight times its block scale is a normal f16 (scales in
+        [2^-14, 2^13]): the f16 MoE path is exact then."""
+        ok = getattr(self, "_f16_ok", None)
+        if ok is None:
+            sc = self.scales_t.float().abs()
+            nz = sc[sc > 0]
+            ok = self._f16_ok = bool(sc.numel() == 0 or (nz.numel() == 0 or (nz.min() >= 2.0 ** -14
+                                                                           and sc.max() <= 2.0 ** 13)))
+        return ok
+
+    def tiled(self, codes: torch.Tensor | None = None, cache: bool = True) -> torch.Tensor:
         """Tile-major device layout streamed by the dequantising kernels
         (built once, cached): for each 128-row tile (per expert when experts
         are stacked; rows past the end are zero) and each 64-input K block one
         contiguous record {codes [128][bits*8 B], scales [gpb][128] bf16,
         biases [gpb][128] bf16}; gpb = 2 for group size 32, else 1 (a
         128-input group repeats its scale and bias in both of its blocks)."""
-        t = getattr(self, "_tiled", None)
+        t = getattr(self, "_tiled", None) if cache else None
         if t is not None:
             return t
         E = self.num_experts or 1
@@ -282,7 +305,7 @@ class QuantizedWeight:
         KB = K // 64
         cb = self.bits * 8  # code bytes per row per K block
         dev = self.codes.device
-        codes = self.codes.view(E, Ne, KB, cb)
+        codes = (self.codes if codes is None else codes).view(E, Ne, KB, cb)
         sc = self.scales_t.t().reshape(E, Ne, -1)  # [E, Ne, G]
         bi = self.biases_t.t().reshape(E, Ne, -1) if self.biases_t is not None else torch.zeros_like(sc)
         pad = tiles * 128 - Ne
@@ -305,8 +328,10 @@ class QuantizedWeight:
         b_b = b_.view(torch.uint8).reshape(E, tiles, KB, -1)
         rec = torch.cat([c, s_b] if self.biases_t is None else [c, s_b, b_b], dim=-1).contiguous()
         assert rec.shape[-1] == self.record_bytes()
-        self._tiled = rec.reshape(-1)
-        return self._tiled
+        rec = rec.reshape(-1)
+        if cache:
+            self._tiled = rec
+        return rec
 
     def numel(self) -> int:
         return self.shape[0] * self.shape[1]

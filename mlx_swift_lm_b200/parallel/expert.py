@@ -218,7 +218,7 @@ class ExpertParallel:
         ys = torch.empty(P, H, dtype=h.dtype, device=dev)
         _lib.check(L.b200_moe_sort(ids_local.data_ptr(), P, El, BN, max_chunks, perm.data_ptr(), pos.data_ptr(),
                                    chunks.data_ptr(), n_chunks.data_ptr(), st), "moe_sort")
-        _lib.check(L.b200_moe_gather(self.local_ptr + self.rx_off, H, perm.data_ptr(), P, 1, xs.data_ptr(), st),
+        _lib.check(L.b200_moe_gather(self.local_ptr + self.rx_off, H, perm.data_ptr(), P, 1, xs.data_ptr(), 0, st),
                    "moe_gather")
         moe_ops._grouped(L, xs, P, H, Wgu, El, N2, gu, F, gu_bias, moe_ops._EPI[epi], chunks, n_chunks, max_chunks,
                          BN, st, "gate/up")

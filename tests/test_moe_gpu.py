@@ -253,14 +253,48 @@ def test_persistent_grouped_gemm_equals_per_item(fmt, T, E, k):
     w, idx = moe.route_topk(torch.randn(T, E, device=DEV), k)
     epi = "swiglu_oai" if fmt == "mxfp4" else "swiglu"
     outs = []
-    for pers in (True, False):
-        moe_ops.PERSISTENT[0] = pers
-        try:
+    moe_ops.F16_MXFP4[0] = False  # the bf16 dequantising kernels on both launch shapes
+    try:
+        for pers in (True, False):
+            moe_ops.PERSISTENT[0] = pers
             outs.append(moe.moe_experts(h, gu, d, w, idx, epi))
-        finally:
-            moe_ops.PERSISTENT[0] = True
+    finally:
+        moe_ops.PERSISTENT[0] = False
+        moe_ops.F16_MXFP4[0] = True
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1])
+    assert _lib_status_ok()
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (64, 128, 4), (300, 16, 4)])
+def test_mxfp4_f16_path(T, E, k):
+    """MXFP4 experts on the f16 path (hardware e2m1 pairs, f16 activations and
+    gate/up rows, kind::f16 with f16 operands) against the fp32 reference of
+    the dequantised experts, and close to the bf16 path."""
+    from mlx_swift_lm_b200.ops import moe as moe_ops
+    from mlx_swift_lm_b200.ops.qlinear import QuantizedWeight
+
+    torch.manual_seed(T + E)
+    K, F = 512, 256
+    h = torch.randn(T, K, device=DEV, dtype=torch.bfloat16)
+    gu_f = [ref.interleave_gate_up(torch.randn(F, K) * 0.05, torch.randn(F, K) * 0.05) for _ in range(E)]
+    d_f = [torch.randn(K, F) * 0.05 for _ in range(E)]
+    gu = QuantizedWeight.stack_experts([QuantizedWeight.quantize_mxfp4(t) for t in gu_f]).to(DEV)
+    d = QuantizedWeight.stack_experts([QuantizedWeight.quantize_mxfp4(t) for t in d_f]).to(DEV)
+    assert gu.f16_scales_ok() and d.f16_scales_ok()
+    gub = torch.randn(E, 2 * F, device=DEV, dtype=torch.bfloat16) * 0.1
+    w, idx = moe.route_topk(torch.randn(T, E, device=DEV), k, "topk_softmax")
+    y16 = moe.moe_experts(h, gu, d, w, idx, "swiglu_oai", gub)
+    moe_ops.F16_MXFP4[0] = False
+    try:
+        ybf = moe.moe_experts(h, gu, d, w, idx, "swiglu_oai", gub)
+    finally:
+        moe_ops.F16_MXFP4[0] = True
+    gud = torch.stack([gu.expert(e).dequantize() for e in range(E)])
+    dd = torch.stack([d.expert(e).dequantize() for e in range(E)])
+    r = _moe_ref(h.cpu(), gud.to(torch.bfloat16).cpu(), dd.to(torch.bfloat16).cpu(), w.cpu(), idx.cpu(), "swiglu_oai",
+                 gub.cpu())
+    assert _rel(y16.cpu(), r) < 2e-2 and _rel(y16.cpu(), ybf.cpu()) < 2e-2
     assert _lib_status_ok()
 
 
