@@ -362,7 +362,34 @@ def run_arm(args, impl, world, rank, local, dev, group):
     # work between replays; it rewrites the K/V of the last step's positions)
     replay_ms = None
     g = eng.graphs
-    if (args.diag or args.timeline) and g is not None and args.streams in g.graphs:
+    runner = getattr(mtp, "runner", None) if mtp is not None else None
+    if (args.diag or args.timeline) and runner is not None and impl == "ours":
+        # MTP: the captured round of the full batch instead of a decode graph
+        R = next((R for (B, k), R in sorted(runner.rounds.items()) if B >= args.streams and R.graph is not None),
+                 None)
+        if R is not None:
+            eng._drain_inflight()
+            barrier()
+            r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            r0.record()
+            for _ in range(10):
+                model.begin_step()
+                R.graph.replay()
+            r1.record()
+            barrier()
+            replay_ms = round(r0.elapsed_time(r1) / 10, 4)
+            if args.timeline:
+                from mlx_swift_lm_b200.engine.diagnostics import timeline_summary
+
+                tl = _lib.timeline_start(dev)
+                model.begin_step()
+                R.graph.replay()
+                torch.cuda.synchronize(dev)
+                marks = _lib.timeline_read(tl)
+                _lib.timeline_stop()
+                with open(args.timeline.replace("{rank}", str(rank)), "w") as f:
+                    f.write(timeline_summary(marks, f"MTP round graph replay (B={R.B}, k={R.k}), rank {rank}") + "\n")
+    elif (args.diag or args.timeline) and g is not None and args.streams in g.graphs:
         eng._drain_inflight()
         barrier()
         r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -420,9 +420,10 @@ struct PSmem {
 
 __device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int BN, int WQ>
+template <int BN, int WQ, bool F16 = false>
 __global__ void __launch_bounds__(512, 1)
     grouped_persistent_kernel(const __grid_constant__ CUtensorMap tmX, GArgs a, const __grid_constant__ GQuant q) {
+  static_assert(!F16 || WQ == kWqE2M1, "the f16 path serves MXFP4 records");
   using S = PSmem<BN, WQ>;
   constexpr int ST = S::kStages, RS = S::kRawStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -515,7 +516,7 @@ __global__ void __launch_bounds__(512, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer: item j accumulates into buffer j & 1
-      constexpr uint32_t idesc = umma_idesc_bf16(128, BN);
+      constexpr uint32_t idesc = F16 ? umma_idesc_f16(128, BN) : umma_idesc_bf16(128, BN);
       int g = 0, j = 0;
       bool ok = true;
       for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++j) {
@@ -553,7 +554,11 @@ __global__ void __launch_bounds__(512, 1)
           ok = false;
           break;
         }
-        dequant_half_row<WQ>(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, gsel, q.gpb);
+        if constexpr (F16) {
+          dequant_half_row_e2m1_f16(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, gsel, q.gpb);
+        } else {
+          dequant_half_row<WQ>(smem + S::kRawOff + rs * S::kRaw, smem + s * S::kStage, t, half, gsel, q.gpb);
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -623,21 +628,21 @@ __global__ void __launch_bounds__(512, 1)
   }
 }
 
-template <int BN, int WQ>
+template <int BN, int WQ, bool F16 = false>
 int launch_persistent(const CUtensorMap& tx, const GArgs& a, const GQuant& q, int num_sms, cudaStream_t st) {
   using S = PSmem<BN, WQ>;
-  if (int e = smem_attr_once<grouped_persistent_kernel<BN, WQ>>(S::kTotal)) return e;
-  cudaError_t e = launch_k(grouped_persistent_kernel<BN, WQ>, dim3(num_sms), dim3(S::kThreads), S::kTotal, st, 1, tx,
-                           a, q);
+  if (int e = smem_attr_once<grouped_persistent_kernel<BN, WQ, F16>>(S::kTotal)) return e;
+  cudaError_t e = launch_k(grouped_persistent_kernel<BN, WQ, F16>, dim3(num_sms), dim3(S::kThreads), S::kTotal, st,
+                           1, tx, a, q);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
-template <int WQ>
+template <int WQ, bool F16 = false>
 int dispatch_persistent(int BN, const CUtensorMap& tx, const GArgs& a, const GQuant& q, int num_sms,
                         cudaStream_t st) {
   switch (BN) {
-    case 16: return launch_persistent<16, WQ>(tx, a, q, num_sms, st);
-    case 32: return launch_persistent<32, WQ>(tx, a, q, num_sms, st);
+    case 16: return launch_persistent<16, WQ, F16>(tx, a, q, num_sms, st);
+    case 32: return launch_persistent<32, WQ, F16>(tx, a, q, num_sms, st);
     default: return -1;
   }
 }
@@ -786,6 +791,7 @@ int b200_moe_grouped_gemm_q(const void* xs, int P, int K, const void* tiled, int
                N, K, ldy, epi, y_f16};
   if (f16) {
     if (bits != kWqE2M1) return -1;
+    if (BN <= 32 && persistent > 0) return moe::dispatch_persistent<kWqE2M1, true>(BN, tx, a, q, persistent, st);
     return moe::dispatch_grouped_f16(BN, tx, a, q, max_chunks, st);
   }
   if (BN <= 32 && persistent > 0) {  // decode-sized chunks: one CTA per SM over all work items

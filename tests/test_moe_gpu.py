@@ -285,6 +285,11 @@ def test_mxfp4_f16_path(T, E, k):
     gub = torch.randn(E, 2 * F, device=DEV, dtype=torch.bfloat16) * 0.1
     w, idx = moe.route_topk(torch.randn(T, E, device=DEV), k, "topk_softmax")
     y16 = moe.moe_experts(h, gu, d, w, idx, "swiglu_oai", gub)
+    moe_ops.PERSISTENT[0] = True  # the persistent launch of the f16 path: the same bits
+    try:
+        assert torch.equal(moe.moe_experts(h, gu, d, w, idx, "swiglu_oai", gub), y16)
+    finally:
+        moe_ops.PERSISTENT[0] = False
     moe_ops.F16_MXFP4[0] = False
     try:
         ybf = moe.moe_experts(h, gu, d, w, idx, "swiglu_oai", gub)
