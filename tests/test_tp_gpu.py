@@ -18,7 +18,16 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, mode, q):
+def _cfg(wide):
+    from mlx_swift_lm_b200.models.config import tiny_qwen3
+
+    c = tiny_qwen3()
+    if wide:  # heads, KV-head replication and MLP shards that split 8 ways
+        c.hidden_size, c.num_heads, c.num_kv_heads, c.head_dim, c.intermediate_size = 512, 8, 2, 64, 1024
+    return c
+
+
+def _worker(rank, world, port, mode, q, wide=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     from datetime import timedelta
 
@@ -32,7 +41,7 @@ def _worker(rank, world, port, mode, q):
         from mlx_swift_lm_b200.models.config import tiny_qwen3
         from mlx_swift_lm_b200.models.decoder import TensorParallel
 
-        cfg = tiny_qwen3()
+        cfg = _cfg(wide)
         m = DecoderLM(cfg, dev, torch.bfloat16, tp=TensorParallel(rank, world, dist.group.WORLD)).init_random(
             5, std=0.2)
         ok = True
@@ -68,11 +77,11 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-def _run(mode):
+def _run(mode, world=2, wide=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, mode, q, wide)) for r in range(world)]
     for p in ps:
         p.start()
     res = q.get(timeout=600)
@@ -101,3 +110,25 @@ def test_tp2_fused_and_nccl_match_single_gpu():
     agree_f = sum(a == b for x, y in zip(fused, ref) for a, b in zip(x, y)) / 36
     agree_n = sum(a == b for x, y in zip(nccl, ref) for a, b in zip(x, y)) / 36
     assert agree_f >= 0.75 and agree_n >= 0.75, (fused, nccl, ref)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_tp_wide_fused_matches_single_gpu(world):
+    """The fused path at 4 and 8 ranks (rows per rank down to 8, KV heads
+    replicated where there are fewer than ranks)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from mlx_swift_lm_b200 import DecoderLM, EngineConfig, EngineV2, SchedulerConfig
+    from mlx_swift_lm_b200.models.config import tiny_qwen3
+
+    cfg = _cfg(True)
+    m = DecoderLM(cfg, torch.device("cuda", 0), torch.bfloat16).init_random(5, std=0.2)
+    eng = EngineV2(m, config=EngineConfig(scheduler=SchedulerConfig(max_concurrent_requests=8), max_model_len=256,
+                                          graph_buckets=(1, 2, 4, 8)))
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (20, 7, 33)]
+    ref = eng.generate(prompts, max_tokens=12)
+    fused, ok, st = _run("fused", world, wide=True)
+    assert ok and all(v == 0 for v in st.values()), st
+    agree = sum(a == b for x, y in zip(fused, ref) for a, b in zip(x, y)) / 36
+    assert agree >= 0.75, (fused, ref)
