@@ -814,10 +814,7 @@ int b200_gemm_qkv_rope(const void* X, int M, int K, int ldx, const void* W, int 
   if (N != (H + 2 * KVH) * 128 || !positions || !cos_sin || !q_out) return -1;
   if ((K % 8) || (ldx % 8) || (ldw % 8) || ((uintptr_t)X & 15) || ((uintptr_t)W & 15) || ((uintptr_t)q_out & 7))
     return -1;
-  const int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  CUtensorMap tw, tx;
-  if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
-  if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
+  int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   GemmArgs a = {};
   a.Y = nullptr;
   a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
@@ -847,6 +844,10 @@ int b200_gemm_qkv_rope(const void* X, int M, int K, int ldx, const void* W, int 
   if (s > 8) return -1;
   a.kb_per_split = (a.kb_total + s - 1) / s;
   a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  if (a.ksplit > 1 && BN == 256) BN = 128;  // as in b200_gemm_bf16
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
+  if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
   if (a.ksplit == 1 && BN == 256 && N > 128)  // prefill-sized, unsplit: 256 x 256 tiles
     return launch_gemm<256, 3, kModeLocal, 0, 2>(tw, tx, a, local_coll(), (N + 255) / 256, (M + 255) / 256, stream);
   const int tiles_n = N / 128, tiles_m = (M + BN - 1) / BN;
@@ -870,9 +871,6 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   const bool glu = epi == kEpiSwiGLU || epi == kEpiGeGLU || epi == kEpiSwiGLUOAI;
   if (glu && (N % 128)) return -1;
   int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  CUtensorMap tw, tx;
-  if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
-  if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
   GemmArgs a;
   a.Y = Y;
   a.R = reinterpret_cast<const __nv_bfloat16*>(R);
@@ -890,6 +888,12 @@ int b200_gemm_bf16(const void* X, int M, int K, int ldx, const void* W, int N, i
   if (s > 8) return -1;
   a.kb_per_split = (a.kb_total + s - 1) / s;
   a.ksplit = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  // split-K launches (decode rows) of more than 128 rows take 128-row tiles: twice
+  // the CTAs and half the epilogue each; a row's K order is the same either way
+  if (a.ksplit > 1 && BN == 256) BN = 128;
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d(&tw, W, N, K, ldw, 128, 64, 2)) return -1;
+  if (!make_tmap_2d(&tx, X, M, K, ldx, BN, 64, 2)) return -1;
   if (a.ksplit == 1 && BN == 256 && N > 128)  // prefill-sized, unsplit: 256 x 256 tiles
     return launch_gemm<256, 3, kModeLocal, 0, 2>(tw, tx, a, local_coll(), (N + 255) / 256, (M + 255) / 256, stream);
   const int tiles_n = (N + 127) / 128, tiles_m = (M + BN - 1) / BN;

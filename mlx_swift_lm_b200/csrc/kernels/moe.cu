@@ -202,10 +202,16 @@ struct GSmem {
   static constexpr int kA = 128 * 128, kB = BN * 128;
   static constexpr int kCode = code_bits<WQ>() * 128 * 64 / 8, kGroup = 2 * 128 * 2;
   static constexpr int kRaw = WQ ? kCode + 2 * kGroup : 0;
-  static constexpr int kStage = (kA + kB + 1023) / 1024 * 1024;
-  static constexpr int kRawStages = WQ ? (100 * 1024 - STAGES * kStage) / kRaw : 0;
-  static constexpr int kRawOff = STAGES * kStage;
-  static constexpr int kBars = (WQ ? 3 : 2) * STAGES + 2 * kRawStages + 1;
+  // bf16 experts: stages of {A weight tile, B activation tile}. Quantised
+  // experts: A stages (dequantised weight tiles) and a deeper ring of B
+  // activation tiles of their own, so an A stage's reuse waits for the
+  // dequantisation and the MMA only, not for a fresh activation load.
+  static constexpr int kStage = WQ ? kA : (kA + kB + 1023) / 1024 * 1024;
+  static constexpr int kBStages = WQ ? (BN <= 16 ? 8 : BN <= 32 ? 4 : STAGES) : 0;
+  static constexpr int kBOff = STAGES * kStage;
+  static constexpr int kRawOff = kBOff + kBStages * kB;
+  static constexpr int kRawStages = WQ ? (100 * 1024 - kRawOff) / kRaw : 0;
+  static constexpr int kBars = (WQ ? 3 : 2) * STAGES + 2 * kRawStages + 2 * kBStages + 1;
   static constexpr int kTotal = kRawOff + kRawStages * kRaw + kBars * 8 + 16 + 1024;
   static constexpr int kThreads = WQ ? 384 : 128;
   static constexpr int kMinBlocks = WQ ? 2 : 1;
@@ -231,6 +237,9 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
   const uint32_t bar_aready = bar_acc + 8;
   const uint32_t bar_rfull = bar_aready + 8 * STAGES;
   const uint32_t bar_rempty = bar_rfull + 8 * RS;
+  constexpr int BS = S::kBStages;
+  const uint32_t bar_bfull = bar_rempty + 8 * RS;  // quantised: B ring
+  const uint32_t bar_bempty = bar_bfull + 8 * BS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kRawOff + RS * S::kRaw + S::kBars * 8);
   __shared__ float xbuf[64][17];
   pdl_launch_dependents();
@@ -251,6 +260,10 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
       mbar_init(bar_rfull + 8 * s, 1);
       mbar_init(bar_rempty + 8 * s, 8);
     }
+    for (int b = 0; b < BS; ++b) {
+      mbar_init(bar_bfull + 8 * b, 1);
+      mbar_init(bar_bempty + 8 * b, 1);
+    }
     mbar_init(bar_acc, 1);
     fence_barrier_init();
   }
@@ -265,21 +278,33 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
   const int wrow = e * a.N + n0;
   const uint64_t pw = l2_policy_evict_first(), px = l2_policy_evict_last();
   if (warp == 0 && lane == 0) {
-    // operand producer: weight tile (bf16) + activation tile, or the
-    // activation tile alone (quantised: the dequantising warps write A)
-    const uint32_t tx_bytes = WQ ? (uint32_t)S::kB : (uint32_t)(S::kA + S::kB);
-    int issued = 0;
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % STAGES, r = i / STAGES;
-      if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
-      const uint32_t st = sbase + s * S::kStage;
-      mbar_arrive_expect_tx(bar_full + 8 * s, tx_bytes);
-      if constexpr (WQ == 0) tma_load_2d(st, &tmW, bar_full + 8 * s, i * 64, wrow, pw);
-      tma_load_2d(st + S::kA, &tmX, bar_full + 8 * s, i * 64, r0, px);
-      issued = i + 1;
+    if constexpr (WQ == 0) {
+      // operand producer: weight tile + activation tile per stage
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES, r = i / STAGES;
+        if (r > 0 && !mbar_wait(bar_empty + 8 * s, (r - 1) & 1, kErrGemmWait)) break;
+        const uint32_t st = sbase + s * S::kStage;
+        mbar_arrive_expect_tx(bar_full + 8 * s, (uint32_t)(S::kA + S::kB));
+        tma_load_2d(st, &tmW, bar_full + 8 * s, i * 64, wrow, pw);
+        tma_load_2d(st + S::kA, &tmX, bar_full + 8 * s, i * 64, r0, px);
+        issued = i + 1;
+      }
+      for (int i = max(0, issued - STAGES); i < issued; ++i)
+        mbar_wait(bar_full + 8 * (i % STAGES), (i / STAGES) & 1, kErrGemmWait);
+    } else {
+      // activation tiles into the B ring, BS blocks ahead of the MMA
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int b = i % BS, rb = i / BS;
+        if (rb > 0 && !mbar_wait(bar_bempty + 8 * b, (rb - 1) & 1, kErrGemmWait)) break;
+        mbar_arrive_expect_tx(bar_bfull + 8 * b, (uint32_t)S::kB);
+        tma_load_2d(sbase + S::kBOff + b * S::kB, &tmX, bar_bfull + 8 * b, i * 64, r0, px);
+        issued = i + 1;
+      }
+      for (int i = max(0, issued - BS); i < issued; ++i)
+        mbar_wait(bar_bfull + 8 * (i % BS), (i / BS) & 1, kErrGemmWait);
     }
-    for (int i = max(0, issued - STAGES); i < issued; ++i)
-      mbar_wait(bar_full + 8 * (i % STAGES), (i / STAGES) & 1, kErrGemmWait);
   } else if (warp == 2 && lane == 0) {
     if constexpr (WQ != 0) {
       // raw producer: codes + scales + biases, RS stages ahead
@@ -300,16 +325,23 @@ __global__ void __launch_bounds__(GSmem<BN, STAGES, WQ>::kThreads, GSmem<BN, STA
     constexpr uint32_t idesc = F16 ? umma_idesc_f16(128, BN) : umma_idesc_bf16(128, BN);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % STAGES, r = i / STAGES;
-      if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
-      if constexpr (WQ != 0) {
+      uint32_t baddr;
+      if constexpr (WQ == 0) {
+        if (!mbar_wait(bar_full + 8 * s, r & 1, kErrGemmWait)) break;
+        baddr = sbase + s * S::kStage + S::kA;
+      } else {
+        const int b = i % BS;
+        if (!mbar_wait(bar_bfull + 8 * b, (i / BS) & 1, kErrGemmWait)) break;
         if (!mbar_wait(bar_aready + 8 * s, r & 1, kErrGemmWait)) break;
+        baddr = sbase + S::kBOff + b * S::kB;
       }
       tc_fence_after();
       const uint64_t ad = umma_desc_k_sw128(sbase + s * S::kStage, 1024);
-      const uint64_t bd = umma_desc_k_sw128(sbase + s * S::kStage + S::kA, 1024);
+      const uint64_t bd = umma_desc_k_sw128(baddr, 1024);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) tc_mma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-      tc_commit(bar_empty + 8 * s);
+      tc_commit(bar_empty + 8 * s);  // A stage (and, bf16, its activation tile) free
+      if constexpr (WQ != 0) tc_commit(bar_bempty + 8 * (i % BS));
     }
     tc_commit(bar_acc);
   } else if (warp >= 4) {
