@@ -473,7 +473,7 @@ def load_model(path: str, device="cuda", dtype=torch.bfloat16, tp: TensorParalle
     if hadamard is not None:
         prism.validate(info, hadamard, tensors)
     model = build_from_tensors(cfg, tensors, device, dtype, tp, keep_quantized=keep_quantized, hadamard=hadamard)
-    if hf.get("vision_config") and hf.get("model_type") in ("qwen2_vl", "qwen2_5_vl"):
+    if hf.get("vision_config") and hf.get("model_type") in ("qwen2_vl", "qwen2_5_vl", "qwen3_vl"):
         model = _attach_vision(model, cfg, hf, tensors, device, dtype)
     elif hf.get("vision_config") and hf.get("model_type") in ("gemma3", "paligemma", "idefics3", "smolvlm"):
         model = _attach_siglip(model, cfg, hf, tensors, device, dtype, path)
@@ -490,11 +490,19 @@ def _attach_vision(lm, cfg, hf, tensors, device, dtype):
     from ..models.vision import QwenVisionTower, VisionConfig
     from ..models.vlm import Qwen2VLModel
 
-    rs = hf.get("rope_scaling") or (hf.get("text_config") or {}).get("rope_scaling") or {}
-    kind = "qwen2_5" if hf.get("model_type") == "qwen2_5_vl" else "qwen2"
+    tc = hf.get("text_config") or {}
+    rs = hf.get("rope_scaling") or tc.get("rope_scaling") or tc.get("rope_parameters") or {}
+    mt = hf.get("model_type")
+    kind = {"qwen2_5_vl": "qwen2_5", "qwen3_vl": "qwen3"}.get(mt, "qwen2")
     vcfg = VisionConfig.from_hf(hf["vision_config"], cfg.hidden_size, kind)
-    m = Qwen2VLModel(cfg, vcfg, device, dtype, hf.get("image_token_id", 151655), hf.get("video_token_id", 151656),
-                     rs.get("mrope_section", (16, 24, 24)))
+    if kind == "qwen3":
+        from ..models.vlm import Qwen3VLModel
+
+        m = Qwen3VLModel(cfg, vcfg, device, dtype, hf.get("image_token_id", 151655), hf.get("video_token_id", 151656),
+                         rs.get("mrope_section", (24, 20, 20)))
+    else:
+        m = Qwen2VLModel(cfg, vcfg, device, dtype, hf.get("image_token_id", 151655),
+                         hf.get("video_token_id", 151656), rs.get("mrope_section", (16, 24, 24)))
     m.embed, m.norm, m.lm_head, m.layers = lm.embed, lm.norm, lm.lm_head, lm.layers
     m.vision = QwenVisionTower.from_tensors(vcfg, tensors, device, dtype)
     return m

@@ -180,6 +180,8 @@ class DecoderLM:
         self.lora = None  # adapter whose update is currently added into the weights (adapters.lora)
         self.batched_lora = None  # adapters.batched.BatchedLoRA: per-row adapters, base weights untouched
         self._lora_slots = None  # per-token adapter slots of the forward in progress
+        # hook(li, x, delta) -> (x, delta) after layer li of a forward (Qwen3-VL deepstack rows)
+        self._after_layer = None
         self.tp_fused = None  # fused symmetric-memory TP decode path (parallel.tp_fused)
         # hybrid models: attention layers index the KV slab, linear layers the recurrent-state pool
         self.kv_index, self.rec_index = [], []
@@ -514,7 +516,10 @@ class DecoderLM:
         x = inputs_embeds if inputs_embeds is not None else ops.embedding(fb.input_ids, self.embed, cfg.embed_scale)
         delta = None
         attn = torch.empty((T, self.H, self.D), dtype=x.dtype, device=x.device)
+        hook = self._after_layer
         for li, L in enumerate(self.layers):
+            if hook is not None and li > 0:
+                x, delta = hook(li - 1, x, delta)
             h = self._norm(x, delta, L.ln1, L.ln1_b)
             if L.block == "ffn":  # FFN-only layer (NemotronH "-" / "E")
                 delta = self._mlp(L, h)

@@ -34,6 +34,8 @@ register("qwen2")  # q/k/v biases
 register("mimo")  # Xiaomi MiMo: the Qwen2 body (its MTP layers are not loaded)
 register("qwen2_vl", vlm="qwen2_vl")  # the language model of Qwen2-VL (q/k/v biases, M-RoPE)
 register("qwen2_5_vl", vlm="qwen2_vl")  # Qwen2.5-VL: the same language model; window-attention vision tower
+# Qwen3-VL: the Qwen3 language model (interleaved M-RoPE, deepstack rows in models/vlm.py)
+register("qwen3_vl", "qwen3_vl_text", qk_norm=True, vlm="qwen3_vl")
 register("qwen3", qk_norm=True)
 register("qwen3_moe", qk_norm=True, moe=True)
 register("qwen3_next", qk_norm=True, moe=True, hybrid=True)

@@ -1,4 +1,13 @@
-"""Qwen2-VL and Qwen2.5-VL vision towers on the decoder's kernels.
+"""Qwen2-VL, Qwen2.5-VL and Qwen3-VL vision towers on the decoder's kernels.
+
+Qwen3-VL (MLXVLM/Models/Qwen3VL.swift) keeps Qwen2-VL's LayerNorm blocks and
+2-D rotary embedding, adds a bias to the patch embedding and a learned
+position embedding on a fixed square grid that is bilinearly resampled to
+each image's patch grid, uses a GELU-tanh MLP (``linear_fc1`` / ``linear_fc2``),
+normalises before the 2x2 merge, and taps the hidden states after its
+``deepstack_visual_indexes`` blocks through extra mergers (normalising after
+the merge): those "deepstack" features are added to the language model's
+hidden states at the image positions after its first layers.
 
 Qwen2.5-VL (MLXVLM/Models/Qwen25VL.swift) changes the blocks to RMSNorm and a
 biased SwiGLU MLP, attends within windows of ``window_size`` pixels except in
@@ -44,10 +53,12 @@ class VisionConfig:
     in_chans: int = 3
     hidden_size: int = 3584  # language model hidden size (merger output)
     eps: float = 1e-6
-    kind: str = "qwen2"  # "qwen2" | "qwen2_5"
+    kind: str = "qwen2"  # "qwen2" | "qwen2_5" | "qwen3"
     intermediate_size: int = 0  # qwen2_5: SwiGLU width
     window_size: int = 112  # qwen2_5: attention window in pixels
     fullatt_blocks: tuple = ()  # qwen2_5: blocks attending whole frames
+    num_pos: int = 0  # qwen3: learned position embeddings (a square grid)
+    deepstack: tuple = ()  # qwen3: blocks whose outputs feed the deepstack mergers
 
     @property
     def head_dim(self) -> int:
@@ -63,6 +74,11 @@ class VisionConfig:
                       patch_size=vc.get("patch_size", 14), temporal_patch_size=vc.get("temporal_patch_size", 2),
                       spatial_merge_size=vc.get("spatial_merge_size", 2),
                       in_chans=vc.get("in_chans", vc.get("in_channels", 3)))
+        if kind == "qwen3":
+            return cls(embed_dim=vc.get("hidden_size", 1152), hidden_size=vc.get("out_hidden_size", text_hidden),
+                       intermediate_size=vc.get("intermediate_size", 4304), num_pos=vc.get("num_position_embeddings",
+                                                                                            2304),
+                       deepstack=tuple(vc.get("deepstack_visual_indexes", ())), kind="qwen3", **common)
         if kind == "qwen2_5":  # hidden_size is the tower width, out_hidden_size the language model's
             return cls(embed_dim=vc.get("hidden_size", 1280), hidden_size=vc.get("out_hidden_size", text_hidden),
                        intermediate_size=vc.get("intermediate_size", 3420), window_size=vc.get("window_size", 112),
@@ -103,7 +119,8 @@ class QwenVisionTower:
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
-        self.patch_w = None
+        self.patch_w = self.patch_b = self.pos_embed = None  # qwen3: patch bias, position grid
+        self.deep: list[dict] = []  # qwen3: deepstack mergers (post-merge LayerNorm + GELU MLP)
         self.blocks: list[VisionBlock] = []
         self.ln_q_w = self.ln_q_b = None
         self.m1_w = self.m1_b = self.m2_w = self.m2_b = None
@@ -123,6 +140,12 @@ class QwenVisionTower:
             return torch.ones(n, device=self.device, dtype=self.dtype)
 
         self.patch_w = rn(E, c.patch_dim)
+        q3 = c.kind == "qwen3"
+        if q3:
+            F = c.intermediate_size
+            self.patch_b, self.pos_embed = rn(E), rn(c.num_pos, E)
+            self.deep = [{"norm_w": ones(M), "norm_b": rn(M), "fc1_w": rn(M, M), "fc1_b": rn(M),
+                          "fc2_w": rn(c.hidden_size, M), "fc2_b": rn(c.hidden_size)} for _ in c.deepstack]
         self.blocks = []
         q25 = c.kind == "qwen2_5"
         for _ in range(c.depth):
@@ -143,11 +166,14 @@ class QwenVisionTower:
         return self
 
     def tensors(self):
-        for n in ("patch_w", "ln_q_w", "ln_q_b", "m1_w", "m1_b", "m2_w", "m2_b"):
+        for n in ("patch_w", "patch_b", "pos_embed", "ln_q_w", "ln_q_b", "m1_w", "m1_b", "m2_w", "m2_b"):
             yield n, getattr(self, n)
         for i, b in enumerate(self.blocks):
             for s in VisionBlock.__slots__:
                 yield f"blocks.{i}.{s}", getattr(b, s)
+        for j, d in enumerate(self.deep):
+            for k, v in d.items():
+                yield f"deep.{j}.{k}", v
 
     def to(self, device, dtype):
         self.device, self.dtype = torch.device(device), dtype
@@ -157,6 +183,9 @@ class QwenVisionTower:
             if n.startswith("blocks."):
                 _, i, s = n.split(".")
                 setattr(self.blocks[int(i)], s, v.to(self.device, dtype).contiguous())
+            elif n.startswith("deep."):
+                _, j, k = n.split(".")
+                self.deep[int(j)][k] = v.to(self.device, dtype).contiguous()
             else:
                 setattr(self, n, v.to(self.device, dtype).contiguous())
         return self
@@ -176,6 +205,28 @@ class QwenVisionTower:
         hp, wp = torch.cat(hs).double(), torch.cat(ws).double()
         ang = torch.cat([hp[:, None] * self.inv_freq[None], wp[:, None] * self.inv_freq[None]], -1)
         return torch.cat([ang.cos(), ang.sin()], -1).float().to(self.device)
+
+    def position_rows(self, grids: list[tuple[int, int, int]]) -> torch.Tensor:
+        """qwen3: learned position embedding of every patch [N, E] in patchify
+        order: the square grid of ``num_pos`` embeddings bilinearly resampled
+        to the frame's h x w patches (corner-aligned sample points), repeated
+        over frames, in merge-window order."""
+        c = self.cfg
+        n = int(round(c.num_pos ** 0.5))
+        m = c.spatial_merge_size
+        grid = self.pos_embed.float().view(n, n, -1)
+        out = []
+        for t, h, w in grids:
+            hy = torch.linspace(0, n - 1, h, dtype=torch.float32)
+            wx = torch.linspace(0, n - 1, w, dtype=torch.float32)
+            h0, w0 = hy.long(), wx.long()
+            h1, w1 = (h0 + 1).clamp(max=n - 1), (w0 + 1).clamp(max=n - 1)
+            dh, dw = (hy - h0)[:, None, None].to(grid.device), (wx - w0)[None, :, None].to(grid.device)
+            e = ((1 - dh) * (1 - dw) * grid[h0][:, w0] + (1 - dh) * dw * grid[h0][:, w1]
+                 + dh * (1 - dw) * grid[h1][:, w0] + dh * dw * grid[h1][:, w1])  # [h, w, E]
+            e = e.reshape(h // m, m, w // m, m, -1).permute(0, 2, 1, 3, 4).reshape(h * w, -1)
+            out.append(e.repeat(t, 1))
+        return torch.cat(out).to(self.dtype)
 
     def window_index(self, grids: list[tuple[int, int, int]]):
         """(order of the merged units window by window, window lengths in
@@ -206,9 +257,13 @@ class QwenVisionTower:
         c = self.cfg
         dev, E, NH, D = self.device, c.embed_dim, c.num_heads, c.head_dim
         q25 = c.kind == "qwen2_5"
+        q3 = c.kind == "qwen3"
         U = c.spatial_merge_size ** 2
-        x = ops.gemm(patches.to(dev, self.dtype).contiguous(), self.patch_w)
+        x = ops.gemm(patches.to(dev, self.dtype).contiguous(), self.patch_w, bias=self.patch_b)
         N = x.shape[0]
+        if q3:
+            x = (x.float() + self.position_rows(grids).float()).to(self.dtype)
+        deep = []
         table = self.rotary_table(grids)
         frames = [h * w for t, h, w in grids for _ in range(t)]  # attention within each frame
 
@@ -245,7 +300,14 @@ class QwenVisionTower:
                 delta = ops.gemm(ops.gemm(h, b.gu_w, epi="swiglu", bias=b.gu_b), b.dn_w, bias=b.dn_b)
             else:
                 h = ops.add_layernorm(x, d, b.norm2_w, b.norm2_b, c.eps)
-                delta = ops.gemm(ops.gemm(h, b.fc1_w, epi="quick_gelu", bias=b.fc1_b), b.fc2_w, bias=b.fc2_b)
+                act = "gelu_tanh" if q3 else "quick_gelu"
+                delta = ops.gemm(ops.gemm(h, b.fc1_w, epi=act, bias=b.fc1_b), b.fc2_w, bias=b.fc2_b)
+            if q3 and i in c.deepstack:  # the block's output through its deepstack merger
+                dm = self.deep[c.deepstack.index(i)]
+                y = (x.float() + delta.float()).to(self.dtype).reshape(N // U, -1).contiguous()
+                y = ops.add_layernorm(y, None, dm["norm_w"], dm["norm_b"], c.eps)
+                deep.append(ops.gemm(ops.gemm(y, dm["fc1_w"], epi="gelu", bias=dm["fc1_b"]), dm["fc2_w"],
+                                     bias=dm["fc2_b"]))
         if q25:
             hq = ops.add_rmsnorm(x, delta, self.ln_q_w, c.eps)
         else:
@@ -254,6 +316,8 @@ class QwenVisionTower:
         out = ops.gemm(ops.gemm(hq, self.m1_w, epi="gelu", bias=self.m1_b), self.m2_w, bias=self.m2_b)
         if q25:  # back to patchify order
             out = out.index_select(0, torch.argsort(order)).contiguous()
+        if q3:
+            return out, deep
         return out
 
     # ------------------------------------------------------------------ loading
@@ -273,6 +337,15 @@ class QwenVisionTower:
             w = w.permute(0, 4, 1, 2, 3)
         m.patch_w = w.reshape(w.shape[0], -1)
         q25 = cfg.kind == "qwen2_5"
+        q3 = cfg.kind == "qwen3"
+        if q3:
+            m.patch_b, m.pos_embed = g("patch_embed.proj.bias"), g("pos_embed.weight")
+            m.deep = [{"norm_w": g(f"deepstack_merger_list.{j}.norm.weight"),
+                       "norm_b": g(f"deepstack_merger_list.{j}.norm.bias"),
+                       "fc1_w": g(f"deepstack_merger_list.{j}.linear_fc1.weight"),
+                       "fc1_b": g(f"deepstack_merger_list.{j}.linear_fc1.bias"),
+                       "fc2_w": g(f"deepstack_merger_list.{j}.linear_fc2.weight"),
+                       "fc2_b": g(f"deepstack_merger_list.{j}.linear_fc2.bias")} for j in range(len(cfg.deepstack))]
         for i in range(cfg.depth):
             p = f"blocks.{i}."
             b = VisionBlock()
@@ -287,9 +360,15 @@ class QwenVisionTower:
             else:
                 b.norm1_w, b.norm1_b = g(p + "norm1.weight"), g(p + "norm1.bias")
                 b.norm2_w, b.norm2_b = g(p + "norm2.weight"), g(p + "norm2.bias")
-                b.fc1_w, b.fc1_b = g(p + "mlp.fc1.weight"), g(p + "mlp.fc1.bias")
-                b.fc2_w, b.fc2_b = g(p + "mlp.fc2.weight"), g(p + "mlp.fc2.bias")
+                fc = ("mlp.linear_fc1", "mlp.linear_fc2") if q3 else ("mlp.fc1", "mlp.fc2")
+                b.fc1_w, b.fc1_b = g(p + fc[0] + ".weight"), g(p + fc[0] + ".bias")
+                b.fc2_w, b.fc2_b = g(p + fc[1] + ".weight"), g(p + fc[1] + ".bias")
             m.blocks.append(b)
+        if q3:
+            m.ln_q_w, m.ln_q_b = g("merger.norm.weight"), g("merger.norm.bias")
+            m.m1_w, m.m1_b = g("merger.linear_fc1.weight"), g("merger.linear_fc1.bias")
+            m.m2_w, m.m2_b = g("merger.linear_fc2.weight"), g("merger.linear_fc2.bias")
+            return m.to(device, dtype)
         m.ln_q_w = g("merger.ln_q.weight")
         m.ln_q_b = None if q25 else g("merger.ln_q.bias")
         m.m1_w, m.m1_b = g("merger.mlp.0.weight"), g("merger.mlp.0.bias")

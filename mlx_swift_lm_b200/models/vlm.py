@@ -1,5 +1,11 @@
-"""Qwen2-VL vision-language model: the fused decoder plus a vision tower,
-multimodal rows and M-RoPE.
+"""Qwen2-VL / Qwen2.5-VL / Qwen3-VL vision-language models: the fused
+decoder plus a vision tower, multimodal rows and M-RoPE.
+
+Qwen3-VL (MLXVLM/Models/Qwen3VL.swift) interleaves the M-RoPE frequencies
+(frequency i follows the h position when i % 3 == 1 and the w position when
+i % 3 == 2, within 3 x section, else the t position) and adds the vision
+tower's deepstack features to the hidden states of the image tokens after
+the first decoder layers.
 
 Parity: MLXVLM/Models/Qwen2VL.swift - ``getRopeIndex`` (:345: text runs get
 equal (t, h, w) positions, an image of grid (t, h, w) / merge gets the 3-D
@@ -183,3 +189,85 @@ class Qwen2VLModel(DecoderLM):
             return super().forward(fb, kv, return_hidden, x, return_both, return_residual)
         finally:
             fb.rope_table = None
+
+
+class Qwen3VLModel(Qwen2VLModel):
+    """Qwen3-VL: interleaved M-RoPE and deepstack injection (see the module doc)."""
+
+    def __init__(self, cfg, vision_cfg: VisionConfig, device="cpu", dtype=torch.float32, image_token_id: int = 151655,
+                 video_token_id: int = 151656, mrope_section=(24, 20, 20)):
+        super().__init__(cfg, vision_cfg, device, dtype, image_token_id, video_token_id, mrope_section)
+        half = self.rot_dim // 2
+        sec = torch.zeros(half, dtype=torch.long)
+        for axis in (1, 2):
+            for i in range(axis, 3 * self.mrope_section[axis], 3):
+                sec[i] = axis
+        self._sec = sec
+
+    def clone_to(self, device, dtype):
+        m = super().clone_to(device, dtype)
+        out = Qwen3VLModel(self.cfg, self.vision.cfg, device, dtype, self.image_token_id, self.video_token_id,
+                           self.mrope_section)
+        out.embed, out.norm, out.lm_head, out.layers = m.embed, m.norm, m.lm_head, m.layers
+        out.vision = m.vision
+        out.vision.deep = [dict(d) for d in self.vision.deep]
+        out.vision.patch_b, out.vision.pos_embed = self.vision.patch_b, self.vision.pos_embed
+        out.vision.to(device, dtype)
+        return out
+
+    @torch.no_grad()
+    def prepare(self, prompt_tokens: list[int], media: MediaInput | None) -> tuple[list[int], dict | None]:
+        vis = self.vision
+        fwd = vis.forward
+        deep: list = []
+
+        def forward(patches, grids):  # keep the deepstack features next to the merged embeddings
+            out, d = fwd(patches, grids)
+            deep.extend(d)
+            return out
+
+        vis.forward = forward
+        try:
+            toks, mm = super().prepare(prompt_tokens, media)
+        finally:
+            del vis.forward
+        if mm is not None:
+            mm["deep"] = deep
+        return toks, mm
+
+    def forward(self, fb, kv, return_hidden: bool = False, inputs_embeds=None, return_both=False,
+                return_residual=False):
+        states = getattr(fb, "row_states", None)
+        rows = []
+        if inputs_embeds is None and states:
+            nd = fb.num_decode
+            pf = fb.pf_cu_q_host or [0]
+            for i, st in enumerate(states):
+                mm = st.req.mm if st is not None else None
+                if mm is None or i < nd or not mm.get("deep"):
+                    continue
+                a, n = nd + pf[i - nd], pf[i - nd + 1] - pf[i - nd]
+                p0 = int(fb.pf_pos0_host[i - nd])
+                ip = mm["image_pos"]
+                sel = ((ip >= p0) & (ip < p0 + n)).nonzero()[:, 0]
+                if len(sel):
+                    rows.append(((ip[sel] - p0 + a), sel, mm["deep"]))
+        if not rows:
+            return super().forward(fb, kv, return_hidden, inputs_embeds, return_both, return_residual)
+        n_deep = max(len(d) for _, _, d in rows)
+
+        def hook(li, x, delta):
+            if li >= n_deep:
+                return x, delta
+            x = (x.float() + delta.float()).to(x.dtype) if delta is not None else x
+            for r, sel, d in rows:
+                if li < len(d):
+                    rr = r.to(x.device)
+                    x[rr] = (x[rr].float() + d[li][sel.to(d[li].device)].float()).to(x.dtype)
+            return x, None
+
+        self._after_layer = hook
+        try:
+            return super().forward(fb, kv, return_hidden, inputs_embeds, return_both, return_residual)
+        finally:
+            self._after_layer = None
