@@ -56,6 +56,13 @@ struct CommCtx {
     float* r = reinterpret_cast<float*>(base[owner] + recv_off);
     return r + (((size_t)parity * world + src) * rows_per_rank + lrow) * hidden;
   }
+  // fp32 partial of row `row` (0 .. world*rpr-1) from `src`, in the buffer of
+  // `owner` (every rank receives every rank's partials of every row)
+  __device__ __forceinline__ float* recv_all(int owner, int parity, int src, int row) const {
+    float* r = reinterpret_cast<float*>(base[owner] + recv_off);
+    const size_t M = (size_t)world * rows_per_rank;
+    return r + (((size_t)parity * world + src) * M + row) * hidden;
+  }
   // normalised row `grow` (global row index 0..world*rpr-1) in the gathered
   // buffer [2][world*rpr][hidden] of `owner`; every rank pushes its rows into
   // every rank's buffer, so the all-gather GEMM reads local memory only

@@ -182,6 +182,7 @@ struct CollArgs {
   CommCtx comm;
   int phase;   // collective phase index within the step (epoch = step * kPhasesPerStep + phase + 1)
   int parity;  // buffer slot of this call
+  int rs_all;  // reduce-scatter epilogue: 1 = the partial rows go to every rank (each rank reduces all rows)
 };
 
 // Affine-quantised weights (WQ bits per code): w = scale[g] * q + bias[g] per
@@ -559,15 +560,21 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ, MT>::kThreads, 1)
           continue;
         }
         if constexpr (MODE == kModeRS) {
-          // fp32 partial row m -> inbox slot [parity][this rank][row] of its owner rank
           const int rpr = coll.comm.rows_per_rank;
-          float* dst = coll.comm.recv_row((int)m / rpr, coll.parity, coll.comm.rank, (int)m % rpr) + n;
-          if (n + 3 < args.N) {
-            *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-          } else {
+          const int W = coll.rs_all ? coll.comm.world : 1;
+          for (int jj = 0; jj < W; ++jj) {
+            // fp32 partial row m -> [parity][this rank][row] of its owner rank's inbox, or of
+            // every rank's (rs_all, starting with this rank's own buffer)
+            const int j = (coll.comm.rank + jj) % coll.comm.world;
+            float* dst = coll.rs_all ? coll.comm.recv_all(j, coll.parity, coll.comm.rank, (int)m) + n
+                                     : coll.comm.recv_row((int)m / rpr, coll.parity, coll.comm.rank, (int)m % rpr) + n;
+            if (n + 3 < args.N) {
+              *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (n + e < args.N) dst[e] = v[e];
+              for (int e = 0; e < 4; ++e)
+                if (n + e < args.N) dst[e] = v[e];
+            }
           }
         } else if (args.epi == kEpiStoreF32) {
           float* dst = reinterpret_cast<float*>(args.Y) + m * args.ldy + n;
@@ -999,13 +1006,14 @@ int b200_gemm_bf16_ag(const void* comm_ctx, int phase, int parity, int M_real, i
 // GEMM -> reduce-scatter: fp32 partial rows go to their owner rank's inbox
 // slot `parity`; the last CTA publishes phase `phase` on the RS pad.
 int b200_gemm_bf16_rs(const void* comm_ctx, int phase, int parity, const void* X, int M_real, int K, int ldx,
-                      const void* W, int N, int ldw, const void* bias, int num_sms, int force_splits,
+                      const void* W, int N, int ldw, const void* bias, int num_sms, int force_splits, int rs_all,
                       cudaStream_t stream) {
   CollArgs* coll = new CollArgs();
   std::unique_ptr<CollArgs> guard(coll);
   memcpy(&coll->comm, comm_ctx, sizeof(CommCtx));
   coll->phase = phase;
   coll->parity = parity;
+  coll->rs_all = rs_all;
   const CommCtx& c = coll->comm;
   const int M = c.world * c.rows_per_rank;
   if (M_real > M || c.hidden != N || (K % 8) || (ldx % 8) || (ldw % 8)) return -1;

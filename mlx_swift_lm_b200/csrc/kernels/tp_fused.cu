@@ -77,6 +77,65 @@ __global__ void __launch_bounds__(256) tp_combine_norm_kernel(CommCtx c, int pha
   if (threadIdx.x == 0) last_cta_signal(c, kPadAG, c.epoch(phase_ag));
 }
 
+// Every rank reduces every row (the RS GEMMs sent each rank all partials):
+// one CTA per row m < M. With `has_delta`: wait for every rank's partials,
+// sum them in rank order (the same order on every rank, so all ranks hold
+// identical rows), round to bf16 and add to the replicated residual x[m];
+// then h[m] = RMSNorm(x[m]) * w. No rows are pushed and nothing is signalled:
+// the next GEMM reads h from local memory.
+__global__ void __launch_bounds__(256) tp_combine_all_kernel(CommCtx c, int phase_rs, int parity_rs,
+                                                            __nv_bfloat16* x, const __nv_bfloat16* w, float eps,
+                                                            __nv_bfloat16* h, int has_delta) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float red[32];
+  extern __shared__ float rbuf[];
+  const int m = blockIdx.x;
+  const int H = c.hidden;
+  if (has_delta) wait_all_ranks(c, kPadRS, c.epoch(phase_rs));
+  __nv_bfloat16* xr = x + (size_t)m * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+    uint2 xv = *reinterpret_cast<const uint2*>(xr + i);
+    __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
+    float r[4];
+    if (has_delta) {
+      float4 acc = *reinterpret_cast<const float4*>(c.recv_all(c.rank, parity_rs, 0, m) + i);
+      for (int j = 1; j < c.world; ++j) {
+        const float4 p = *reinterpret_cast<const float4*>(c.recv_all(c.rank, parity_rs, j, m) + i);
+        acc.x += p.x;
+        acc.y += p.y;
+        acc.z += p.z;
+        acc.w += p.w;
+      }
+      const float d[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        xe[e] = f2bf(bf2f(xe[e]) + bf2f(f2bf(d[e])));
+        r[e] = bf2f(xe[e]);
+      }
+      *reinterpret_cast<uint2*>(xr + i) = xv;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) r[e] = bf2f(xe[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      rbuf[i + e] = r[e];
+      ss += r[e] * r[e];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / (float)H + eps);
+  __nv_bfloat16* hr = h + (size_t)m * H;
+  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+    __nv_bfloat16 o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = f2bf(rbuf[i + e] * inv * bf2f(w[i + e]));
+    *reinterpret_cast<uint2*>(hr + i) = *reinterpret_cast<const uint2*>(o);
+  }
+}
+
 // Embedding of this rank's rows into x_local (ids [T] of the whole step; rows
 // past T are zero), without publishing.
 __global__ void __launch_bounds__(256) tp_embed_kernel(CommCtx c, const int* ids, int T, const __nv_bfloat16* table,
@@ -181,6 +240,17 @@ int b200_tp_combine_norm(const void* ctx, int phase_rs, int parity_rs, int phase
   cudaError_t e = launch_k(tp_combine_norm_kernel, dim3(c.rows_per_rank), dim3(256), c.hidden * sizeof(float), st, 1,
                            c, phase_rs, parity_rs, phase_ag, parity_ag, reinterpret_cast<__nv_bfloat16*>(x_local),
                            reinterpret_cast<const __nv_bfloat16*>(w), eps, has_delta);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
+}
+
+int b200_tp_combine_all(const void* ctx, int phase_rs, int parity_rs, void* x, const void* w, float eps, void* h,
+                        int M, int has_delta, cudaStream_t st) {
+  CommCtx c;
+  memcpy(&c, ctx, sizeof(c));
+  if ((c.hidden % 4) || M > c.world * c.rows_per_rank || M <= 0) return -1;
+  cudaError_t e = launch_k(tp_combine_all_kernel, dim3(M), dim3(256), c.hidden * sizeof(float), st, 1, c, phase_rs,
+                           parity_rs, reinterpret_cast<__nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w),
+                           eps, reinterpret_cast<__nv_bfloat16*>(h), has_delta);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

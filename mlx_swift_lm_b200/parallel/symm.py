@@ -31,7 +31,10 @@ _lib.register_signatures({
                                      _lib.i32, C.c_void_p, _lib.i32, C.c_void_p, _lib.i32, _lib.i32, _lib.i32,
                                      C.c_void_p]),
     "b200_gemm_bf16_rs": (_lib.i32, [C.c_void_p, _lib.i32, _lib.i32, C.c_void_p, _lib.i32, _lib.i32, _lib.i32,
-                                     C.c_void_p, _lib.i32, _lib.i32, C.c_void_p, _lib.i32, _lib.i32, C.c_void_p]),
+                                     C.c_void_p, _lib.i32, _lib.i32, C.c_void_p, _lib.i32, _lib.i32, _lib.i32,
+                                     C.c_void_p]),
+    "b200_tp_combine_all": (_lib.i32, [C.c_void_p, _lib.i32, _lib.i32, C.c_void_p, C.c_void_p, _lib.f32, C.c_void_p,
+                                       _lib.i32, _lib.i32, C.c_void_p]),
     "b200_tp_combine_norm": (_lib.i32, [C.c_void_p, _lib.i32, _lib.i32, _lib.i32, _lib.i32, C.c_void_p, C.c_void_p,
                                         _lib.f32, _lib.i32, C.c_void_p]),
     "b200_tp_embed": (_lib.i32, [C.c_void_p, C.c_void_p, _lib.i32, C.c_void_p, _lib.i64, C.c_void_p, _lib.f32,
@@ -99,7 +102,9 @@ class SymmetricComm:
         L = _lib.lib()
         assert L.b200_comm_ctx_size() == C.sizeof(CommCtxStruct), "CommCtx layout mismatch"
         pads = NUM_PADS * MAX_RANKS * 4
-        recv = 2 * world * rows_per_rank * hidden * 4
+        # fp32 partial rows: [2][world (source)][world * rows_per_rank][hidden] (every rank's
+        # partials of every row; the owner-only layout uses the first rows_per_rank rows)
+        recv = 2 * world * world * rows_per_rank * hidden * 4
         hbuf = 2 * world * rows_per_rank * hidden * 2
         xarg = 2 * world * max_rows * 8
         self.pads_off = 0

@@ -1,15 +1,22 @@
 """Fused tensor-parallel decode forward over symmetric memory.
 
-Per layer, with rows sequence-parallel between the GEMMs (rank r owns rows
-[r*rpr, (r+1)*rpr) of the residual stream):
+Per layer (the residual stream x and the normed rows h are replicated on
+every rank; one cross-rank synchronisation per row-parallel projection):
 
-    qkv   = GEMM_AG(h, Wqkv_r)        all-gather fused into the GEMM prologue
-    attn  = paged attention on the rank's heads (all rows)
-    RS    = GEMM_RS(attn, Wo_r)       reduce-scatter fused into the epilogue
-    x, h  = combine_norm(RS, x, ln2)  rank-ordered sum + residual + RMSNorm, publish h
-    gu    = GEMM_AG(h, Wgu_r, SwiGLU)
-    RS    = GEMM_RS(gu, Wd_r)
-    x, h  = combine_norm(RS, x, ln1 of the next layer / final norm)
+    q, K/V = GEMM(h, Wqkv_r) + qk-norm + RoPE + paged K/V append (local)
+    attn   = paged attention on the rank's heads (all rows)
+    GEMM_RS(attn, Wo_r)        the epilogue writes its fp32 partial rows into
+                               every rank's inbox, the last CTA signals
+    x, h   = combine_all(ln2)  wait for every rank's partials, sum them in
+                               rank order (identical on every rank), add to x,
+                               RMSNorm into h (local, nothing pushed)
+    gu     = GEMM(h, Wgu_r, SwiGLU) (local)
+    GEMM_RS(gu, Wd_r); x, h = combine_all(ln1 of the next layer / final norm)
+
+Sending every rank all partials costs (world - 1) x rows x hidden x 4 bytes
+per projection per rank (0.5-3.5 MB at 64 rows of 4096 for 2-8 ranks), and
+saves the second exchange of a reduce-scatter + all-gather pair (a push of
+normed rows and its flag round trip) per projection.
 
 The head is vocabulary-parallel (rank r holds rows [r*V/N, (r+1)*V/N) of the
 LM head) and the token is a cross-rank split argmax, so every rank ends the
@@ -53,6 +60,9 @@ class FusedTP:
         self.V_local = V // self.world
         self.head = model.lm_head[self.rank * self.V_local:(self.rank + 1) * self.V_local]
         self.qkv = torch.empty(self.M_pad, (model.H + 2 * model.KVH) * model.D, dtype=dt, device=dev)
+        # replicated residual rows and their normed copy (the local GEMMs' input)
+        self.x = torch.zeros(self.M_pad, cfg.hidden_size, dtype=dt, device=dev)
+        self.h = torch.zeros(self.M_pad, cfg.hidden_size, dtype=dt, device=dev)
         self.gu = torch.empty(self.M_pad, model.F, dtype=dt, device=dev)
         self.logits = torch.empty(self.M_pad, self.V_local, dtype=torch.float32, device=dev)
         self.sms = num_sms(dev)
@@ -79,7 +89,7 @@ class FusedTP:
         _lib.count(1)
         return out
 
-    def _gemm_rs(self, X, T, W, bias=None):
+    def _gemm_rs(self, X, T, W, bias=None, rs_all=False):
         c = self.comm
         p = c.next_phase()
         par = c.rs_count & 1
@@ -87,9 +97,18 @@ class FusedTP:
         _lib.check(_lib.lib().b200_gemm_bf16_rs(c.ctx_ptr, p, par, X.data_ptr(), T, X.shape[1], X.stride(0),
                                                 W.data_ptr(), W.shape[0], W.stride(0),
                                                 _lib.ptr(bias) if self.rank == 0 else None, self.sms, 0,
-                                                _lib.stream_ptr(self.m.device)), "gemm_rs")
+                                                1 if rs_all else 0, _lib.stream_ptr(self.m.device)), "gemm_rs")
         _lib.count(1)
         return (p, par)
+
+    def _combine_all(self, rs, T, w):
+        """x += rank-ordered sum of every rank's partials (rs = None: no delta); h = RMSNorm(x) * w."""
+        c = self.comm
+        _lib.check(_lib.lib().b200_tp_combine_all(c.ctx_ptr, rs[0] if rs else 0, rs[1] if rs else 0,
+                                                  self.x.data_ptr(), w.data_ptr(), float(self.m.cfg.rms_norm_eps),
+                                                  self.h.data_ptr(), T, 1 if rs else 0,
+                                                  _lib.stream_ptr(self.m.device)), "tp_combine_all")
+        _lib.count(1)
 
     # ------------------------------------------------------------------ forward
     def decode_tokens(self, fb, kv, out, out2=None):
@@ -100,28 +119,30 @@ class FusedTP:
         c.phase = 0
         L = _lib.lib()
         st = _lib.stream_ptr(m.device)
-        _lib.check(L.b200_tp_embed(c.ctx_ptr, fb.input_ids.data_ptr(), T, m.embed.data_ptr(), m.embed.shape[0],
-                                   self.x_local.data_ptr(), float(cfg.embed_scale), st), "tp_embed")
-        _lib.count(1)
-        ag = self._publish(m.layers[0].ln1, False, None)
-        attn = None
+        ops.embedding(fb.input_ids, m.embed, cfg.embed_scale, out=self.x[:T])
+        self._combine_all(None, T, m.layers[0].ln1)
+        h = self.h[:T]
         for li, Lw in enumerate(m.layers):
-            qkv = self._gemm_ag(ag, T, Lw.wqkv, self.qkv, bias=Lw.bqkv)[:T]
             kc, vc = kv.layer(li)
             cs, rd = m.rope_for(li)
-            q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, cs, rd, cfg.rope_interleaved,
-                                    Lw.q_norm, Lw.k_norm, cfg.rms_norm_eps, kc, vc, m.H, m.KVH, m.D,
-                                    kv.k_scale(li), kv.v_scale(li))
+            if m._fused_qkv_rope(Lw, h, fb, rd):
+                q = ops.gemm_qkv_rope(h, Lw.wqkv, Lw.bqkv, fb.positions, fb.slots, cs, Lw.q_norm, Lw.k_norm,
+                                      cfg.rms_norm_eps, kc, vc, m.H, m.KVH, kv.k_scale(li), kv.v_scale(li))
+            else:
+                qkv = ops.gemm(h, Lw.wqkv, bias=Lw.bqkv, out=self.qkv[:T])
+                q = ops.qk_norm_rope_kv(qkv, fb.positions, fb.slots, cs, rd, cfg.rope_interleaved,
+                                        Lw.q_norm, Lw.k_norm, cfg.rms_norm_eps, kc, vc, m.H, m.KVH, m.D,
+                                        kv.k_scale(li), kv.v_scale(li))
             attn = ops.paged_decode(q, kc, vc, fb.dec_page_table, fb.dec_seq_lens, cfg.scale, cfg.window(li),
                                     Lw.sinks, cfg.attn_logit_softcap, kv.k_scale(li), kv.v_scale(li),
                                     fb.dec_max_parts)
-            rs = self._gemm_rs(attn.view(T, m.H * m.D), T, Lw.wo, Lw.bo)
-            ag = self._publish(Lw.ln2, True, rs)
-            self._gemm_ag(ag, T, Lw.wgu, self.gu, epi=cfg.glu_epi, bias=Lw.bgu)
-            rs = self._gemm_rs(self.gu[:T], T, Lw.wd, Lw.bd)
+            rs = self._gemm_rs(attn.view(T, m.H * m.D), T, Lw.wo, Lw.bo, rs_all=True)
+            self._combine_all(rs, T, Lw.ln2)
+            ops.gemm(h, Lw.wgu, epi=cfg.glu_epi, bias=Lw.bgu, out=self.gu[:T])
+            rs = self._gemm_rs(self.gu[:T], T, Lw.wd, Lw.bd, rs_all=True)
             nxt = m.layers[li + 1].ln1 if li + 1 < len(m.layers) else m.norm
-            ag = self._publish(nxt, True, rs)
-        self._gemm_ag(ag, T, self.head, self.logits, epi="f32")
+            self._combine_all(rs, T, nxt)
+        ops.gemm(h, self.head, epi="f32", out=self.logits[:T])
         p = c.next_phase()
         par = c.arg_count & 1
         c.arg_count += 1
