@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(256) tp_combine_norm_kernel(CommCtx c, int pha
 // identical rows), round to bf16 and add to the replicated residual x[m];
 // then h[m] = RMSNorm(x[m]) * w. No rows are pushed and nothing is signalled:
 // the next GEMM reads h from local memory.
-__global__ void __launch_bounds__(256) tp_combine_all_kernel(CommCtx c, int phase_rs, int parity_rs,
+__global__ void __launch_bounds__(1024) tp_combine_all_kernel(CommCtx c, int phase_rs, int parity_rs,
                                                             __nv_bfloat16* x, const __nv_bfloat16* w, float eps,
                                                             __nv_bfloat16* h, int has_delta) {
   pdl_launch_dependents();
@@ -248,7 +248,9 @@ int b200_tp_combine_all(const void* ctx, int phase_rs, int parity_rs, void* x, c
   CommCtx c;
   memcpy(&c, ctx, sizeof(c));
   if ((c.hidden % 4) || M > c.world * c.rows_per_rank || M <= 0) return -1;
-  cudaError_t e = launch_k(tp_combine_all_kernel, dim3(M), dim3(256), c.hidden * sizeof(float), st, 1, c, phase_rs,
+  // one pass per row: a thread per 4 elements (up to 1024 threads), so every load of the row is in flight at once
+  const int threads = min(1024, ((c.hidden / 4 + 31) / 32) * 32);
+  cudaError_t e = launch_k(tp_combine_all_kernel, dim3(M), dim3(threads), c.hidden * sizeof(float), st, 1, c, phase_rs,
                            parity_rs, reinterpret_cast<__nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w),
                            eps, reinterpret_cast<__nv_bfloat16*>(h), has_delta);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
