@@ -63,6 +63,12 @@ struct CommCtx {
     const size_t M = (size_t)world * rows_per_rank;
     return r + (((size_t)parity * world + src) * M + row) * hidden;
   }
+  // bf16 partials in the same region (half the bytes; used from 4 ranks up)
+  __device__ __forceinline__ __nv_bfloat16* recv_all_bf16(int owner, int parity, int src, int row) const {
+    __nv_bfloat16* r = reinterpret_cast<__nv_bfloat16*>(base[owner] + recv_off);
+    const size_t M = (size_t)world * rows_per_rank;
+    return r + (((size_t)parity * world + src) * M + row) * hidden;
+  }
   // normalised row `grow` (global row index 0..world*rpr-1) in the gathered
   // buffer [2][world*rpr][hidden] of `owner`; every rank pushes its rows into
   // every rank's buffer, so the all-gather GEMM reads local memory only

@@ -182,7 +182,8 @@ struct CollArgs {
   CommCtx comm;
   int phase;   // collective phase index within the step (epoch = step * kPhasesPerStep + phase + 1)
   int parity;  // buffer slot of this call
-  int rs_all;  // reduce-scatter epilogue: 1 = the partial rows go to every rank (each rank reduces all rows)
+  int rs_all;  // reduce-scatter epilogue: 1 = the partial rows go to every rank (each rank reduces all rows),
+              // 2 = the same with bf16 partials
 };
 
 // Affine-quantised weights (WQ bits per code): w = scale[g] * q + bias[g] per
@@ -566,6 +567,14 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ, MT>::kThreads, 1)
             // fp32 partial row m -> [parity][this rank][row] of its owner rank's inbox, or of
             // every rank's (rs_all, starting with this rank's own buffer)
             const int j = (coll.comm.rank + jj) % coll.comm.world;
+            if (coll.rs_all == 2) {  // N % 4 == 0 here (checked at launch)
+              __nv_bfloat16 o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) o[e] = f2bf(v[e]);
+              *reinterpret_cast<uint2*>(coll.comm.recv_all_bf16(j, coll.parity, coll.comm.rank, (int)m) + n) =
+                  *reinterpret_cast<const uint2*>(o);
+              continue;
+            }
             float* dst = coll.rs_all ? coll.comm.recv_all(j, coll.parity, coll.comm.rank, (int)m) + n
                                      : coll.comm.recv_row((int)m / rpr, coll.parity, coll.comm.rank, (int)m % rpr) + n;
             if (n + 3 < args.N) {
@@ -1014,6 +1023,7 @@ int b200_gemm_bf16_rs(const void* comm_ctx, int phase, int parity, const void* X
   coll->phase = phase;
   coll->parity = parity;
   coll->rs_all = rs_all;
+  if (rs_all == 2 && (N % 4)) return -1;
   const CommCtx& c = coll->comm;
   const int M = c.world * c.rows_per_rank;
   if (M_real > M || c.hidden != N || (K % 8) || (ldx % 8) || (ldw % 8)) return -1;

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(256) tp_combine_norm_kernel(CommCtx c, int pha
 // the next GEMM reads h from local memory.
 __global__ void __launch_bounds__(1024) tp_combine_all_kernel(CommCtx c, int phase_rs, int parity_rs,
                                                             __nv_bfloat16* x, const __nv_bfloat16* w, float eps,
-                                                            __nv_bfloat16* h, int has_delta) {
+                                                            __nv_bfloat16* h, int has_delta, int bf16_parts) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[32];
@@ -100,15 +100,21 @@ __global__ void __launch_bounds__(1024) tp_combine_all_kernel(CommCtx c, int pha
     __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
     float r[4];
     if (has_delta) {
-      float4 acc = *reinterpret_cast<const float4*>(c.recv_all(c.rank, parity_rs, 0, m) + i);
-      for (int j = 1; j < c.world; ++j) {
-        const float4 p = *reinterpret_cast<const float4*>(c.recv_all(c.rank, parity_rs, j, m) + i);
-        acc.x += p.x;
-        acc.y += p.y;
-        acc.z += p.z;
-        acc.w += p.w;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < c.world; ++j) {  // rank order
+        if (bf16_parts) {
+          const uint2 u = *reinterpret_cast<const uint2*>(c.recv_all_bf16(c.rank, parity_rs, j, m) + i);
+          const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d[e] += bf2f(b[e]);
+        } else {
+          const float4 p = *reinterpret_cast<const float4*>(c.recv_all(c.rank, parity_rs, j, m) + i);
+          d[0] += p.x;
+          d[1] += p.y;
+          d[2] += p.z;
+          d[3] += p.w;
+        }
       }
-      const float d[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         xe[e] = f2bf(bf2f(xe[e]) + bf2f(f2bf(d[e])));
@@ -244,7 +250,7 @@ int b200_tp_combine_norm(const void* ctx, int phase_rs, int parity_rs, int phase
 }
 
 int b200_tp_combine_all(const void* ctx, int phase_rs, int parity_rs, void* x, const void* w, float eps, void* h,
-                        int M, int has_delta, cudaStream_t st) {
+                        int M, int has_delta, int bf16_parts, cudaStream_t st) {
   CommCtx c;
   memcpy(&c, ctx, sizeof(c));
   if ((c.hidden % 4) || M > c.world * c.rows_per_rank || M <= 0) return -1;
@@ -252,7 +258,7 @@ int b200_tp_combine_all(const void* ctx, int phase_rs, int parity_rs, void* x, c
   const int threads = min(1024, ((c.hidden / 4 + 31) / 32) * 32);
   cudaError_t e = launch_k(tp_combine_all_kernel, dim3(M), dim3(threads), c.hidden * sizeof(float), st, 1, c, phase_rs,
                            parity_rs, reinterpret_cast<__nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w),
-                           eps, reinterpret_cast<__nv_bfloat16*>(h), has_delta);
+                           eps, reinterpret_cast<__nv_bfloat16*>(h), has_delta, bf16_parts);
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

@@ -66,6 +66,8 @@ class FusedTP:
         self.gu = torch.empty(self.M_pad, model.F, dtype=dt, device=dev)
         self.logits = torch.empty(self.M_pad, self.V_local, dtype=torch.float32, device=dev)
         self.sms = num_sms(dev)
+        # from 4 ranks up the partial rows cross NVLink as bf16 (half the bytes; summed in fp32)
+        self.rs_mode = 2 if self.world >= 4 else 1
 
     # ------------------------------------------------------------------ primitives
     def _publish(self, w, has_delta, rs):
@@ -97,7 +99,8 @@ class FusedTP:
         _lib.check(_lib.lib().b200_gemm_bf16_rs(c.ctx_ptr, p, par, X.data_ptr(), T, X.shape[1], X.stride(0),
                                                 W.data_ptr(), W.shape[0], W.stride(0),
                                                 _lib.ptr(bias) if self.rank == 0 else None, self.sms, 0,
-                                                1 if rs_all else 0, _lib.stream_ptr(self.m.device)), "gemm_rs")
+                                                self.rs_mode if rs_all else 0, _lib.stream_ptr(self.m.device)),
+                   "gemm_rs")
         _lib.count(1)
         return (p, par)
 
@@ -107,7 +110,8 @@ class FusedTP:
         _lib.check(_lib.lib().b200_tp_combine_all(c.ctx_ptr, rs[0] if rs else 0, rs[1] if rs else 0,
                                                   self.x.data_ptr(), w.data_ptr(), float(self.m.cfg.rms_norm_eps),
                                                   self.h.data_ptr(), T, 1 if rs else 0,
-                                                  _lib.stream_ptr(self.m.device)), "tp_combine_all")
+                                                  1 if self.rs_mode == 2 else 0, _lib.stream_ptr(self.m.device)),
+                   "tp_combine_all")
         _lib.count(1)
 
     # ------------------------------------------------------------------ forward
