@@ -30,6 +30,9 @@ from ..engine.types import Event, FinishReason
 K_ERR_PEER_WAIT = 4
 K_ERR_GEMM_WAIT = 1
 COLLECTIVE_ERRORS = ("DistBackendError", "DistNetworkError", "DistError", "TimeoutError")
+# message fragments of a failed collective: NCCL errors, a gloo transport
+# whose peer left (reset / closed pipe) and process-group timeouts
+_COLLECTIVE_TEXT = ("nccl", "gloo/transport", "timed out", "connection closed", "connection reset", "broken pipe")
 
 
 def _default_abort(group):
@@ -85,7 +88,7 @@ class CommGuard:
         """True if `exc` is a collective failure (the communicator is then aborted)."""
         name = type(exc).__name__
         text = str(exc).lower()
-        if name in COLLECTIVE_ERRORS or "nccl" in text or "timed out" in text or "connection closed" in text:
+        if name in COLLECTIVE_ERRORS or any(k in text for k in _COLLECTIVE_TEXT):
             self.abort(f"collective failed: {name}: {str(exc)[:200]}")
             return True
         return False

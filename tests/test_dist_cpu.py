@@ -2,6 +2,8 @@
 computes the same function as one rank; collectives and failure handling on
 the host."""
 import os
+import queue
+import time
 import socket
 
 import pytest
@@ -162,7 +164,15 @@ def test_comm_guard_aborts_on_dead_rank():
     ps = [ctx.Process(target=_guard_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in ps:
         p.start()
-    healthy, aborted, cause, finished = q.get(timeout=180)
+    res, t0 = None, time.monotonic()
+    while res is None and time.monotonic() - t0 < 180:
+        try:
+            res = q.get(timeout=2)
+        except queue.Empty:
+            if ps[0].exitcode not in (None, 0):  # the survivor raised instead of reporting
+                break
+    assert res is not None, f"survivor exit code {ps[0].exitcode}"
+    healthy, aborted, cause, finished = res
     for p in ps:
         p.join(30)
         if p.is_alive():
