@@ -183,7 +183,9 @@ struct CollArgs {
   int phase;   // collective phase index within the step (epoch = step * kPhasesPerStep + phase + 1)
   int parity;  // buffer slot of this call
   int rs_all;  // reduce-scatter epilogue: 1 = the partial rows go to every rank (each rank reduces all rows),
-              // 2 = the same with bf16 partials
+              // 2 = the same with bf16 partials, 3 = bf16 partials stored to this rank's own
+              // multicast-bound buffer `nvls_local` (the combine sums them in the NVSwitch)
+  __nv_bfloat16* nvls_local;  // [2][world*rows_per_rank][hidden] (rs_all == 3)
 };
 
 // Affine-quantised weights (WQ bits per code): w = scale[g] * q + bias[g] per
@@ -567,6 +569,15 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ, MT>::kThreads, 1)
             // fp32 partial row m -> [parity][this rank][row] of its owner rank's inbox, or of
             // every rank's (rs_all, starting with this rank's own buffer)
             const int j = (coll.comm.rank + jj) % coll.comm.world;
+            if (coll.rs_all == 3) {  // local store only; N % 4 == 0 here (checked at launch)
+              __nv_bfloat16 o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) o[e] = f2bf(v[e]);
+              const size_t M = (size_t)coll.comm.world * rpr;
+              *reinterpret_cast<uint2*>(coll.nvls_local + ((size_t)coll.parity * M + m) * args.N + n) =
+                  *reinterpret_cast<const uint2*>(o);
+              break;
+            }
             if (coll.rs_all == 2) {  // N % 4 == 0 here (checked at launch)
               __nv_bfloat16 o[4];
 #pragma unroll
@@ -619,6 +630,11 @@ __global__ void __launch_bounds__(GemmSmem<BN, STAGES, WQ, MT>::kThreads, 1)
         }
       }
     }
+  }
+  // stores made through the unicast address must be visible to peers that
+  // read them through the multicast alias
+  if constexpr (MODE == kModeRS) {
+    if (coll.rs_all == 3) asm volatile("fence.proxy.alias;" ::: "memory");
   }
   // no CTA may leave while a peer still reads its partial
   if (args.ksplit > 1) cluster_sync();
@@ -1016,14 +1032,16 @@ int b200_gemm_bf16_ag(const void* comm_ctx, int phase, int parity, int M_real, i
 // slot `parity`; the last CTA publishes phase `phase` on the RS pad.
 int b200_gemm_bf16_rs(const void* comm_ctx, int phase, int parity, const void* X, int M_real, int K, int ldx,
                       const void* W, int N, int ldw, const void* bias, int num_sms, int force_splits, int rs_all,
-                      cudaStream_t stream) {
+                      void* nvls_local, cudaStream_t stream) {
   CollArgs* coll = new CollArgs();
   std::unique_ptr<CollArgs> guard(coll);
   memcpy(&coll->comm, comm_ctx, sizeof(CommCtx));
   coll->phase = phase;
   coll->parity = parity;
   coll->rs_all = rs_all;
-  if (rs_all == 2 && (N % 4)) return -1;
+  if (rs_all >= 2 && (N % 4)) return -1;
+  if (rs_all == 3 && (!nvls_local || (reinterpret_cast<uintptr_t>(nvls_local) % 16))) return -1;
+  coll->nvls_local = reinterpret_cast<__nv_bfloat16*>(nvls_local);
   const CommCtx& c = coll->comm;
   const int M = c.world * c.rows_per_rank;
   if (M_real > M || c.hidden != N || (K % 8) || (ldx % 8) || (ldw % 8)) return -1;

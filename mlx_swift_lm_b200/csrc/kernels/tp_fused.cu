@@ -85,21 +85,42 @@ __global__ void __launch_bounds__(256) tp_combine_norm_kernel(CommCtx c, int pha
 // the next GEMM reads h from local memory.
 __global__ void __launch_bounds__(1024) tp_combine_all_kernel(CommCtx c, int phase_rs, int parity_rs,
                                                             __nv_bfloat16* x, const __nv_bfloat16* w, float eps,
-                                                            __nv_bfloat16* h, int has_delta, int bf16_parts) {
+                                                            __nv_bfloat16* h, int has_delta, int bf16_parts,
+                                                            const __nv_bfloat16* nvls_mc) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[32];
   extern __shared__ float rbuf[];
   const int m = blockIdx.x;
   const int H = c.hidden;
-  if (has_delta) wait_all_ranks(c, kPadRS, c.epoch(phase_rs));
+  if (has_delta) {
+    wait_all_ranks(c, kPadRS, c.epoch(phase_rs));
+    // the partials were stored through unicast addresses; read them through the multicast alias
+    if (nvls_mc) asm volatile("fence.proxy.alias;" ::: "memory");
+  }
   __nv_bfloat16* xr = x + (size_t)m * H;
   float ss = 0.f;
   for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
     uint2 xv = *reinterpret_cast<const uint2*>(xr + i);
     __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
     float r[4];
-    if (has_delta) {
+    if (has_delta && nvls_mc) {
+      // the NVSwitch returns the sum over ranks of the bf16 partials (fp32 accumulation)
+      const __nv_bfloat16* src = nvls_mc + ((size_t)parity_rs * c.world * c.rows_per_rank + m) * H + i;
+      uint32_t u0, u1;
+      asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v2.bf16x2 {%0, %1}, [%2];"
+                   : "=r"(u0), "=r"(u1)
+                   : "l"(src)
+                   : "memory");
+      const uint32_t uu[2] = {u0, u1};
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(uu);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        xe[e] = f2bf(bf2f(xe[e]) + bf2f(b[e]));
+        r[e] = bf2f(xe[e]);
+      }
+      *reinterpret_cast<uint2*>(xr + i) = xv;
+    } else if (has_delta) {
       float d[4] = {0.f, 0.f, 0.f, 0.f};
       for (int j = 0; j < c.world; ++j) {  // rank order
         if (bf16_parts) {
@@ -250,7 +271,7 @@ int b200_tp_combine_norm(const void* ctx, int phase_rs, int parity_rs, int phase
 }
 
 int b200_tp_combine_all(const void* ctx, int phase_rs, int parity_rs, void* x, const void* w, float eps, void* h,
-                        int M, int has_delta, int bf16_parts, cudaStream_t st) {
+                        int M, int has_delta, int bf16_parts, const void* nvls_mc, cudaStream_t st) {
   CommCtx c;
   memcpy(&c, ctx, sizeof(c));
   if ((c.hidden % 4) || M > c.world * c.rows_per_rank || M <= 0) return -1;
@@ -258,7 +279,8 @@ int b200_tp_combine_all(const void* ctx, int phase_rs, int parity_rs, void* x, c
   const int threads = min(1024, ((c.hidden / 4 + 31) / 32) * 32);
   cudaError_t e = launch_k(tp_combine_all_kernel, dim3(M), dim3(threads), c.hidden * sizeof(float), st, 1, c, phase_rs,
                            parity_rs, reinterpret_cast<__nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w),
-                           eps, reinterpret_cast<__nv_bfloat16*>(h), has_delta, bf16_parts);
+                           eps, reinterpret_cast<__nv_bfloat16*>(h), has_delta, bf16_parts,
+                           reinterpret_cast<const __nv_bfloat16*>(nvls_mc));
   return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 

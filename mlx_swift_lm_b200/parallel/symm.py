@@ -32,9 +32,9 @@ _lib.register_signatures({
                                      C.c_void_p]),
     "b200_gemm_bf16_rs": (_lib.i32, [C.c_void_p, _lib.i32, _lib.i32, C.c_void_p, _lib.i32, _lib.i32, _lib.i32,
                                      C.c_void_p, _lib.i32, _lib.i32, C.c_void_p, _lib.i32, _lib.i32, _lib.i32,
-                                     C.c_void_p]),
+                                     C.c_void_p, C.c_void_p]),
     "b200_tp_combine_all": (_lib.i32, [C.c_void_p, _lib.i32, _lib.i32, C.c_void_p, C.c_void_p, _lib.f32, C.c_void_p,
-                                       _lib.i32, _lib.i32, _lib.i32, C.c_void_p]),
+                                       _lib.i32, _lib.i32, _lib.i32, C.c_void_p, C.c_void_p]),
     "b200_tp_combine_norm": (_lib.i32, [C.c_void_p, _lib.i32, _lib.i32, _lib.i32, _lib.i32, C.c_void_p, C.c_void_p,
                                         _lib.f32, _lib.i32, C.c_void_p]),
     "b200_tp_embed": (_lib.i32, [C.c_void_p, C.c_void_p, _lib.i32, C.c_void_p, _lib.i64, C.c_void_p, _lib.f32,

@@ -27,6 +27,9 @@ collectives fused into the GEMMs instead of injected closures.
 """
 from __future__ import annotations
 
+import os
+import warnings
+
 import torch
 
 from .. import ops
@@ -35,6 +38,26 @@ from ..ops.linear import num_sms
 from .symm import SymmetricComm
 
 _EPI = {"none": 0, "swiglu": 1, "f32": 2, "geglu": 4, "swiglu_oai": 5}
+
+
+def nvls_buffer(group, shape, dev):
+    """A bf16 buffer bound to an NVLink multicast object over `group` (torch
+    symmetric memory): (tensor, multicast address of its first element), or
+    None where the system offers no multicast. Collective: every rank of the
+    group calls it."""
+    try:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        buf = symm_mem.empty(shape, dtype=torch.bfloat16, device=dev)
+        hdl = symm_mem.rendezvous(buf, group.group_name)
+        if not hdl.multicast_ptr:
+            return None
+        buf.zero_()
+        rank = torch.distributed.get_rank(group)
+        return buf, hdl, int(hdl.multicast_ptr) + (buf.data_ptr() - int(hdl.buffer_ptrs[rank]))
+    except Exception as e:  # no symmetric-memory backend or no NVLS
+        warnings.warn(f"NVLS multicast buffer unavailable: {e}")
+        return None
 
 
 def rows_per_rank(T: int, world: int) -> int:
@@ -68,6 +91,13 @@ class FusedTP:
         self.sms = num_sms(dev)
         # from 4 ranks up the partial rows cross NVLink as bf16 (half the bytes; summed in fp32)
         self.rs_mode = 2 if self.world >= 4 else 1
+        # B200LM_TP_NVLS=1: each rank stores its bf16 partials locally and the
+        # combine reads their sum through the NVSwitch (multimem.ld_reduce)
+        self.nvls = None
+        if os.environ.get("B200LM_TP_NVLS", "0") == "1":
+            self.nvls = nvls_buffer(tp.group, (2, self.M_pad, cfg.hidden_size), dev)
+            if self.nvls is not None:
+                self.rs_mode = 3
 
     # ------------------------------------------------------------------ primitives
     def _publish(self, w, has_delta, rs):
@@ -99,8 +129,9 @@ class FusedTP:
         _lib.check(_lib.lib().b200_gemm_bf16_rs(c.ctx_ptr, p, par, X.data_ptr(), T, X.shape[1], X.stride(0),
                                                 W.data_ptr(), W.shape[0], W.stride(0),
                                                 _lib.ptr(bias) if self.rank == 0 else None, self.sms, 0,
-                                                self.rs_mode if rs_all else 0, _lib.stream_ptr(self.m.device)),
-                   "gemm_rs")
+                                                self.rs_mode if rs_all else 0,
+                                                self.nvls[0].data_ptr() if self.rs_mode == 3 else None,
+                                                _lib.stream_ptr(self.m.device)), "gemm_rs")
         _lib.count(1)
         return (p, par)
 
@@ -110,8 +141,9 @@ class FusedTP:
         _lib.check(_lib.lib().b200_tp_combine_all(c.ctx_ptr, rs[0] if rs else 0, rs[1] if rs else 0,
                                                   self.x.data_ptr(), w.data_ptr(), float(self.m.cfg.rms_norm_eps),
                                                   self.h.data_ptr(), T, 1 if rs else 0,
-                                                  1 if self.rs_mode == 2 else 0, _lib.stream_ptr(self.m.device)),
-                   "tp_combine_all")
+                                                  1 if self.rs_mode == 2 else 0,
+                                                  self.nvls[2] if self.rs_mode == 3 else None,
+                                                  _lib.stream_ptr(self.m.device)), "tp_combine_all")
         _lib.count(1)
 
     # ------------------------------------------------------------------ forward
