@@ -200,3 +200,19 @@ def test_comm_guard_reads_kernel_status():
     g2 = CommGuard(e2, None, abort_fn=lambda grp: calls.append("w"))
     e2.on_step_wedge()  # the watchdog's wedge callback aborts too
     assert not e2.healthy and calls[-1] == "w"
+
+
+def test_nvls_buffer_falls_back_without_multicast():
+    """Where the system offers no NVLink multicast (here: a CPU gloo group),
+    the NVLS buffer request warns and returns None, so the fused TP keeps the
+    push-to-every-rank exchange."""
+    from mlx_swift_lm_b200.parallel.tp_fused import nvls_buffer
+
+    if dist.is_initialized():
+        pytest.skip("a default process group already exists in this process")
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{_free_port()}", rank=0, world_size=1)
+    try:
+        with pytest.warns(UserWarning, match="NVLS"):
+            assert nvls_buffer(dist.group.WORLD, (2, 8, 16), torch.device("cpu")) is None
+    finally:
+        dist.destroy_process_group()
